@@ -1,0 +1,306 @@
+// Conv helpers of the drop-in ABI: int8 im2col, the inference conv epilogue,
+// the fused backward gathers (fp32 wgrad/bias, fp32 and int8-weight dgrad)
+// and the 2x2 max-pools (src/backend.rs:28-60,105-110 of the reference's
+// later snapshot).
+//
+// The dgrad gathers sum taps in the reference's order ((kh, kw) outer, output
+// channel inner, one float accumulator), so their results are bit-identical
+// to the reference's CPU backend; they are the operator-level entry points.
+// The training step uses the tensor-core formulation in qat_model.cu.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+// One thread per byte of the padded [align16(rows), col_ld] matrix.
+__global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col, int C,
+                                  int H, int W, int kH, int kW, int sH, int sW, int pH, int pW,
+                                  int Ho, int Wo, int col_ld, i64 rows, i64 total) {
+    const int cols = C * kH * kW, khw = kH * kW;
+    GRID_LOOP(i, total) {
+        const i64 row = i / col_ld;
+        const int k = (int)(i - row * col_ld);
+        int8_t v = 0;
+        if (row < rows && k < cols) {
+            const i64 b = row / ((i64)Ho * Wo);
+            const int rem = (int)(row - b * Ho * Wo);
+            const int oh = rem / Wo, ow = rem - oh * Wo;
+            const int ci = k / khw, kk = k - ci * khw, kh = kk / kW, kw = kk - kh * kW;
+            const int ih = oh * sH + kh - pH, iw = ow * sW + kw - pW;
+            if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = in[((b * C + ci) * H + ih) * W + iw];
+        }
+        col[i] = v;
+    }
+}
+
+__global__ void im2col_f32_kernel(const int8_t *__restrict__ in, float *__restrict__ col, int C,
+                                  int H, int W, int kH, int kW, int sH, int sW, int pH, int pW,
+                                  int Ho, int Wo, i64 total) {
+    const int cols = C * kH * kW, khw = kH * kW;
+    GRID_LOOP(i, total) {
+        const i64 row = i / cols;
+        const int k = (int)(i - row * cols);
+        const i64 b = row / ((i64)Ho * Wo);
+        const int rem = (int)(row - b * Ho * Wo);
+        const int oh = rem / Wo, ow = rem - oh * Wo;
+        const int ci = k / khw, kk = k - ci * khw, kh = kk / kW, kw = kk - kh * kW;
+        const int ih = oh * sH + kh - pH, iw = ow * sW + kw - pW;
+        col[i] = (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                     ? (float)in[((b * C + ci) * H + ih) * W + iw]
+                     : 0.0f;
+    }
+}
+
+// int8 = rint_even(clamp(max(acc/div + bias, 0) * mul, -127, 127)), NCHW out.
+__global__ void conv_epilogue_kernel(const int32_t *__restrict__ acc, const float *__restrict__ bias,
+                                     int8_t *__restrict__ out, int ld, float div, float mul, int C,
+                                     i64 hw, i64 total) {
+    GRID_LOOP(i, total) {
+        const i64 b = i / ((i64)C * hw);
+        const int oc = (int)((i / hw) % C);
+        const i64 row = b * hw + (i % hw);
+        float v = fadd(fdiv((float)acc[row * ld + oc], div), bias[oc]);
+        v = fmul(fmaxf(v, 0.0f), mul);
+        v = fminf(fmaxf(v, -127.0f), 127.0f);
+        out[i] = (int8_t)rint_even(v);
+    }
+}
+
+// fp32 wgrad, one thread per weight element, direct sum in the reference's
+// (b, p) order (cpu_backend.cpp:261-293).
+__global__ void grad_weight_kernel(const int8_t *__restrict__ in, const float *__restrict__ go,
+                                   float *__restrict__ gw, int B, int Cin, int H, int W, int Cout,
+                                   int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo) {
+    const int cols = Cin * kH * kW, hwo = Ho * Wo, khw = kH * kW;
+    GRID_LOOP(i, (i64)Cout * cols) {
+        const int oc = (int)(i / cols), ci = (int)(i % cols);
+        const int c = ci / khw, kk = ci - c * khw, kh = kk / kW, kw = kk - kh * kW;
+        float acc = 0.0f;
+        for (int b = 0; b < B; ++b) {
+            const int8_t *in_b = in + ((i64)b * Cin + c) * H * W;
+            const float *go_b = go + ((i64)b * Cout + oc) * hwo;
+            for (int p = 0; p < hwo; ++p) {
+                const int oh = p / Wo, ow = p - oh * Wo;
+                const int ih = oh * sH + kh - pH, iw = ow * sW + kw - pW;
+                if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                    acc = fadd(acc, fmul(go_b[p], (float)in_b[ih * W + iw]));
+            }
+        }
+        gw[i] = acc;
+    }
+}
+
+// Per-channel sum of go: one CTA per channel, float accumulation in the
+// reference's order would serialise; a double tree sum rounds once instead.
+__global__ void grad_bias_kernel(const float *__restrict__ go, float *__restrict__ gb, int B,
+                                 int Cout, int hw) {
+    const int oc = blockIdx.x;
+    double s = 0.0;
+    for (int b = 0; b < B; ++b)
+        for (int j = threadIdx.x; j < hw; j += blockDim.x) s += (double)go[((i64)b * Cout + oc) * hw + j];
+    __shared__ double sm[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < (blockDim.x >> 5) ? sm[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (threadIdx.x == 0) gb[oc] = (float)s;
+    }
+}
+
+// dgrad gather, one thread per input element; W8 selects int8 weights
+// (times w_scale at the end) or fp32 weights.
+template <bool W8>
+__global__ void grad_input_kernel(const float *__restrict__ go, const float *__restrict__ wf,
+                                  const int8_t *__restrict__ wq, i64 w_ld, float w_scale,
+                                  float *__restrict__ gi, int B, int Cin, int H, int W, int Cout,
+                                  int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo) {
+    const int hwo = Ho * Wo, hwi = H * W;
+    GRID_LOOP(i, (i64)B * Cin * hwi) {
+        const i64 bc = i / hwi;
+        const int pix = (int)(i - bc * hwi);
+        const int b = (int)(bc / Cin), ci = (int)(bc - (i64)b * Cin);
+        const int ih = pix / W, iw = pix - ih * W;
+        const float *go_b = go + (i64)b * Cout * hwo;
+        float acc = 0.0f;
+        for (int kh = 0; kh < kH; ++kh) {
+            const int nh = ih + pH - kh;
+            if (nh < 0 || nh % sH) continue;
+            const int oh = nh / sH;
+            if (oh >= Ho) continue;
+            for (int kw = 0; kw < kW; ++kw) {
+                const int nw = iw + pW - kw;
+                if (nw < 0 || nw % sW) continue;
+                const int ow = nw / sW;
+                if (ow >= Wo) continue;
+                const i64 wc = (i64)(ci * kH + kh) * kW + kw;
+                const float *gp = go_b + oh * Wo + ow;
+                for (int oc = 0; oc < Cout; ++oc) {
+                    const float w = W8 ? (float)wq[(i64)oc * w_ld + wc] : wf[(i64)oc * w_ld + wc];
+                    acc = fadd(acc, fmul(gp[(i64)oc * hwo], w));
+                }
+            }
+        }
+        gi[i] = W8 ? fmul(acc, w_scale) : acc;
+    }
+}
+
+__global__ void maxpool_bwd_idx_kernel(const float *__restrict__ go, const i64 *__restrict__ idx,
+                                       float *__restrict__ gi, i64 n_out, i64 n_in) {
+    GRID_LOOP(i, n_out) {
+        const i64 t = idx[i];
+        if (t >= 0 && t < n_in) atomicAdd(gi + t, go[i]);
+    }
+}
+
+// 2x2 max over int8 NCHW; ties keep the first maximum in (0,0),(0,1),(1,0),(1,1).
+__global__ void maxpool_fwd_i8_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, int H,
+                                      int W, i64 total) {
+    const int Ho = H >> 1, Wo = W >> 1;
+    GRID_LOOP(i, total) {
+        const i64 bc = i / ((i64)Ho * Wo);
+        const int r = (int)(i - bc * Ho * Wo), oh = r / Wo, ow = r - oh * Wo;
+        const int8_t *w = x + bc * H * W + (i64)(2 * oh) * W + 2 * ow;
+        int8_t m = w[0];
+        if (w[1] > m) m = w[1];
+        if (w[W] > m) m = w[W];
+        if (w[W + 1] > m) m = w[W + 1];
+        y[i] = m;
+    }
+}
+
+// Backward recomputes the argmax from x; writes every element of dx.
+__global__ void maxpool_bwd_i8_kernel(const int8_t *__restrict__ x, const float *__restrict__ dy,
+                                      float *__restrict__ dx, int H, int W, i64 total) {
+    const int Ho = H >> 1, Wo = W >> 1;
+    GRID_LOOP(i, total) {
+        const i64 bc = i / ((i64)Ho * Wo);
+        const int r = (int)(i - bc * Ho * Wo), oh = r / Wo, ow = r - oh * Wo;
+        const i64 base = bc * H * W + (i64)(2 * oh) * W + 2 * ow;
+        const int8_t *w = x + base;
+        int win = 0;
+        int8_t m = w[0];
+        if (w[1] > m) { m = w[1]; win = 1; }
+        if (w[W] > m) { m = w[W]; win = 2; }
+        if (w[W + 1] > m) { m = w[W + 1]; win = 3; }
+        const float g = dy[i];
+        dx[base] = win == 0 ? g : 0.0f;
+        dx[base + 1] = win == 1 ? g : 0.0f;
+        dx[base + W] = win == 2 ? g : 0.0f;
+        dx[base + W + 1] = win == 3 ? g : 0.0f;
+    }
+}
+
+}  // namespace
+
+using namespace trba;
+
+extern "C" {
+
+void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H, int W, int kH,
+                       int kW, int sH, int sW, int pH, int pW, int Ho, int Wo, int col_ld, void *s) {
+    const int cols = C * kH * kW;
+    const i64 rows = (i64)batch * Ho * Wo;
+    if (col_ld < cols || (col_ld & 15) || rows <= 0) return;
+    const i64 total = ((rows + 15) / 16 * 16) * col_ld;
+    im2col_pad_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(
+        input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, total);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_im2col_gpu(const int8_t *input, float *col, int batch, int C, int H, int W, int kH,
+                       int kW, int sH, int sW, int pH, int pW, int Ho, int Wo, void *s) {
+    const i64 total = (i64)batch * Ho * Wo * C * kH * kW;
+    if (total <= 0) return;
+    im2col_f32_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(input, col, C, H, W, kH, kW,
+                                                                      sH, sW, pH, pW, Ho, Wo, total);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_conv_epilogue(const int32_t *acc, const float *bias, int8_t *out, int acc_ld,
+                          float acc_div, float out_mul, int B, int C, int Ho, int Wo, void *s) {
+    const i64 hw = (i64)Ho * Wo, total = (i64)B * C * hw;
+    if (total <= 0) return;
+    conv_epilogue_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(acc, bias, out, acc_ld,
+                                                                         acc_div, out_mul, C, hw,
+                                                                         total);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_conv_backward_grad_weight(const int8_t *input, const float *go, float *gw, int B,
+                                      int Cin, int H, int W, int Cout, int kH, int kW, int sH,
+                                      int sW, int pH, int pW, int Ho, int Wo, void *s) {
+    if (B <= 0 || Cout <= 0 || Cin <= 0) return;
+    const i64 n = (i64)Cout * Cin * kH * kW;
+    grad_weight_kernel<<<grid_for(n, 128), 128, 0, as_stream(s)>>>(input, go, gw, B, Cin, H, W, Cout,
+                                                                   kH, kW, sH, sW, pH, pW, Ho, Wo);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_conv_backward_grad_bias(const float *go, float *gb, int B, int Cout, int Ho, int Wo,
+                                    void *s) {
+    if (B <= 0 || Cout <= 0) return;
+    grad_bias_kernel<<<Cout, 256, 0, as_stream(s)>>>(go, gb, B, Cout, Ho * Wo);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_conv_backward_grad_input(const float *go, const float *Wt, float *gi, int B, int Cin,
+                                     int H, int W, int Cout, int kH, int kW, int sH, int sW, int pH,
+                                     int pW, int Ho, int Wo, void *s) {
+    if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0) return;
+    const i64 n = (i64)B * Cin * H * W;
+    grad_input_kernel<false><<<grid_for(n), kThreads, 0, as_stream(s)>>>(
+        go, Wt, nullptr, (i64)Cin * kH * kW, 1.0f, gi, B, Cin, H, W, Cout, kH, kW, sH, sW, pH, pW,
+        Ho, Wo);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_conv_backward_grad_input_i8(const float *go, const int8_t *Wq, int w_ld, float w_scale,
+                                        float *gi, int B, int Cin, int H, int W, int Cout, int kH,
+                                        int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
+                                        void *s) {
+    if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0) return;
+    const i64 n = (i64)B * Cin * H * W;
+    grad_input_kernel<true><<<grid_for(n), kThreads, 0, as_stream(s)>>>(
+        go, nullptr, Wq, w_ld, w_scale, gi, B, Cin, H, W, Cout, kH, kW, sH, sW, pH, pW, Ho, Wo);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_maxpool2x2_backward(const float *go, const i64 *idx, float *gi, i64 out_n, i64 in_n,
+                                void *s) {
+    if (in_n > 0) TRBA_CHECK(cudaMemsetAsync(gi, 0, (size_t)in_n * sizeof(float), as_stream(s)));
+    if (out_n <= 0) return;
+    maxpool_bwd_idx_kernel<<<grid_for(out_n), kThreads, 0, as_stream(s)>>>(go, idx, gi, out_n, in_n);
+    TRBA_LAUNCH_CHECK();
+}
+
+// Host pointers (the reference's one host-side entry, src/backend.rs:56).
+void maxpool2x2_backward_host(const float *go, const uint64_t *idx, float *gi, uint64_t out_n,
+                              uint64_t in_n) {
+    for (uint64_t i = 0; i < in_n; ++i) gi[i] = 0.0f;
+    for (uint64_t i = 0; i < out_n; ++i)
+        if (idx[i] < in_n) gi[idx[i]] += go[i];
+}
+
+void launch_maxpool2x2_forward_i8(const int8_t *x, int8_t *y, int B, int C, int H, int W, void *s) {
+    TRBA_REQUIRE(B > 0 && C > 0 && H >= 2 && W >= 2 && !(H & 1) && !(W & 1),
+                 "launch_maxpool2x2_forward_i8: bad shape");
+    const i64 total = (i64)B * C * (H / 2) * (W / 2);
+    maxpool_fwd_i8_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(x, y, H, W, total);
+    TRBA_LAUNCH_CHECK();
+}
+
+void launch_maxpool2x2_backward_i8(const int8_t *x, const float *dy, float *dx, int B, int C, int H,
+                                   int W, void *s) {
+    TRBA_REQUIRE(B > 0 && C > 0 && H >= 2 && W >= 2 && !(H & 1) && !(W & 1),
+                 "launch_maxpool2x2_backward_i8: bad shape");
+    const i64 total = (i64)B * C * (H / 2) * (W / 2);
+    maxpool_bwd_i8_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(x, dy, dx, H, W, total);
+    TRBA_LAUNCH_CHECK();
+}
+
+}  // extern "C"

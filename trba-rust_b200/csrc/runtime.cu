@@ -1,0 +1,247 @@
+// Runtime plumbing of the drop-in ABI: allocation, copies, streams, the
+// grow-only workspace pool, device properties, static weight blobs and the
+// error policy.  Mirrors the semantics the reference binds in
+// src/backend.rs:15-23,135-142 and src/gpu_memory.rs:13-20.
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace trba {
+
+static std::atomic<int> g_abort{1};
+static std::atomic<int> g_err{0};
+static char g_err_msg[512];
+static std::mutex g_err_mu;
+
+bool abort_on_error() { return g_abort.load() != 0; }
+
+void report_error(const char *file, int line, const char *what, int code) {
+    {
+        std::lock_guard<std::mutex> lk(g_err_mu);
+        if (g_err.load() == 0) {
+            snprintf(g_err_msg, sizeof g_err_msg, "%s:%d: %s (code %d)", file, line, what, code);
+            g_err.store(code == 0 ? -1 : code);
+        }
+    }
+    fprintf(stderr, "\n[CUDA FATAL] %s:%d: %s (code %d)\n", file, line, what, code);
+    if (abort_on_error()) abort();
+}
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+}  // namespace trba
+
+using namespace trba;
+
+extern "C" {
+
+void trba_set_abort_on_error(int on) { g_abort.store(on ? 1 : 0); }
+int trba_last_error(void) { return g_err.load(); }
+const char *trba_last_error_string(void) { return g_err.load() ? g_err_msg : ""; }
+void trba_clear_error(void) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_err.store(0);
+    g_err_msg[0] = 0;
+    cudaGetLastError();
+}
+
+void cuda_malloc(void **ptr, size_t size) {
+    *ptr = nullptr;
+    if (size == 0) return;
+    TRBA_CHECK(cudaMalloc(ptr, size));
+    // The reference's CPU mirror hands out zeroed memory; callers of the
+    // scratch pools rely on fresh buffers holding no NaN patterns.
+    if (*ptr) TRBA_CHECK(cudaMemset(*ptr, 0, size));
+}
+
+void cuda_free(void *ptr) {
+    if (ptr) TRBA_CHECK(cudaFree(ptr));
+}
+
+void cuda_memcpy_h2d(void *dst, const void *src, size_t size, void *stream) {
+    if (size == 0) return;
+    TRBA_CHECK(cudaMemcpyAsync(dst, src, size, cudaMemcpyHostToDevice, as_stream(stream)));
+}
+
+void cuda_memcpy_dtod(void *dst, const void *src, size_t size, void *stream) {
+    if (size == 0) return;
+    TRBA_CHECK(cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToDevice, as_stream(stream)));
+}
+
+void cuda_memcpy_d2h(void *dst, const void *src, size_t size, void *stream) {
+    if (size == 0) return;
+    TRBA_CHECK(cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToHost, as_stream(stream)));
+    // The reference consumes host results right after this call in several
+    // places before an explicit sync; keep the copy synchronous w.r.t. host.
+    TRBA_CHECK(cudaStreamSynchronize(as_stream(stream)));
+}
+
+void cuda_sync(void *stream) { TRBA_CHECK(cudaStreamSynchronize(as_stream(stream))); }
+
+void cuda_stream_create(void **stream) {
+    cudaStream_t s = nullptr;
+    TRBA_CHECK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    *stream = (void *)s;
+}
+
+void cuda_stream_destroy(void *stream) {
+    if (stream) TRBA_CHECK(cudaStreamDestroy(as_stream(stream)));
+}
+
+void cuda_get_memory_info(size_t *free_mem, size_t *total_mem) {
+    size_t f = 0, t = 0;
+    TRBA_CHECK(cudaMemGetInfo(&f, &t));
+    if (free_mem) *free_mem = f;
+    if (total_mem) *total_mem = t;
+}
+
+// ------------------------------------------------------------ workspace --
+// Block pool: a request takes the first free block that is large enough,
+// else a new block 12.5% larger than asked (the same growth rule the
+// reference uses), so two live workspaces never alias.
+namespace {
+struct Block {
+    void *ptr;
+    size_t size;
+    bool in_use;
+    int device;
+};
+std::vector<Block> g_pool;
+std::mutex g_pool_mu;
+}  // namespace
+
+void *trba_workspace_acquire(size_t bytes) {
+    if (bytes == 0) return nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    for (auto &b : g_pool)
+        if (!b.in_use && b.device == dev && b.size >= bytes) {
+            b.in_use = true;
+            return b.ptr;
+        }
+    size_t want = bytes + bytes / 8;
+    want = (want + 255) & ~(size_t)255;
+    void *p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) {
+        report_error(__FILE__, __LINE__, "trba_workspace_acquire: cudaMalloc failed", 2);
+        return nullptr;
+    }
+    g_pool.push_back(Block{p, want, true, dev});
+    return p;
+}
+
+size_t trba_workspace_size(void) {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    size_t t = 0;
+    for (auto &b : g_pool) t += b.size;
+    return t;
+}
+
+void trba_workspace_release(void *ptr) {
+    if (!ptr) return;
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    for (auto &b : g_pool)
+        if (b.ptr == ptr) {
+            b.in_use = false;
+            return;
+        }
+}
+
+void trba_workspace_release_all(void) {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    for (auto &b : g_pool) cudaFree(b.ptr);
+    g_pool.clear();
+}
+
+// ------------------------------------------------------ device identity --
+const char *trba_backend_name(void) { return "b200-sm100a"; }
+
+const char *trba_device_name(void) {
+    static char name[256] = {0};
+    if (!name[0]) {
+        cudaDeviceProp p;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaGetDeviceProperties(&p, dev) == cudaSuccess) {
+            strncpy(name, p.name, sizeof(name) - 1);
+        } else {
+            strncpy(name, "no CUDA device", sizeof(name) - 1);
+        }
+    }
+    return name;
+}
+
+int trba_device_cc_major(void) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+    return v;
+}
+
+int trba_device_cc_minor(void) {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return 0;
+    return v;
+}
+
+// --------------------------------------------------- static weight blobs --
+// src/gpu_memory.rs:13-20: four device blobs, allocated once, filled by
+// upload_*_weights, released together.
+static void *g_blob[4] = {nullptr, nullptr, nullptr, nullptr};
+static size_t g_blob_size[4] = {0, 0, 0, 0};
+
+static void blob_alloc(int i, size_t n) {
+    if (g_blob[i]) cudaFree(g_blob[i]);
+    g_blob[i] = nullptr;
+    g_blob_size[i] = 0;
+    if (n) {
+        TRBA_CHECK(cudaMalloc(&g_blob[i], n));
+        g_blob_size[i] = n;
+    }
+}
+
+static void blob_upload(int i, const void *data, size_t n) {
+    if (!g_blob[i] || !data || !n) return;
+    if (n > g_blob_size[i]) {
+        report_error(__FILE__, __LINE__, "upload_*_weights: size exceeds the allocated blob", -1);
+        return;
+    }
+    TRBA_CHECK(cudaMemcpy(g_blob[i], data, n, cudaMemcpyHostToDevice));
+}
+
+void allocate_model_weights(size_t cnn, size_t bilstm, size_t attn, size_t ctc) {
+    blob_alloc(0, cnn);
+    blob_alloc(1, bilstm);
+    blob_alloc(2, attn);
+    blob_alloc(3, ctc);
+}
+void upload_cnn_weights(const void *d, size_t n) { blob_upload(0, d, n); }
+void upload_bilstm_weights(const void *d, size_t n) { blob_upload(1, d, n); }
+void upload_attention_weights(const void *d, size_t n) { blob_upload(2, d, n); }
+void upload_ctc_weights(const void *d, size_t n) { blob_upload(3, d, n); }
+void *get_cnn_weights_ptr(void) { return g_blob[0]; }
+void *get_bilstm_weights_ptr(void) { return g_blob[1]; }
+void *get_attention_weights_ptr(void) { return g_blob[2]; }
+void *get_ctc_weights_ptr(void) { return g_blob[3]; }
+void free_model_weights(void) {
+    for (int i = 0; i < 4; ++i) blob_alloc(i, 0);
+}
+
+}  // extern "C"
