@@ -1,0 +1,265 @@
+#!/usr/bin/env python
+"""Benchmark of the TRBA INT8-QAT training step on B200.
+
+Metric: QAT train lines/s at 32x160 (TRBA-small: feat_dim 128, 2-layer BiLSTM
+hidden 64, max_len 20, 130 classes), one full forward + backward + clip +
+Muon/Adam + re-quantisation step per iteration, synthetic data.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
+    python bench.py --impl reference ...      # the reference's CPU path
+
+One process per GPU (torchrun for N > 1): each rank trains on its own batch
+of B lines (weak scaling) and the fp32 gradients are averaged with one NCCL
+all-reduce per step before the optimiser.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+METRIC = "QAT train lines/s (TRBA 32x160)"
+
+
+def load_package():
+    name = "trba_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = REPO / "trba-rust_b200"
+    spec = importlib.util.spec_from_file_location(name, pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=512, help="lines per GPU per step")
+    ap.add_argument("--img-w", type=int, default=160)
+    ap.add_argument("--max-len", type=int, default=20)
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ----------------------------------------------------------------- clocks --
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int):
+        self.dev, self.p = dev, None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.dev), "-lms", "200"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 6:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[2:6]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ reference --
+def cpu_step_sample(lines: int, steps: int, warmup: int, img_w: int, max_len: int, seed: int):
+    """Times the reference's CPU path (oracle/step_oracle.py driving the
+    reference's own CPU backend, oracle/_ref, OpenMP on every host core) on
+    `lines` lines per step; returns (lines/s, cores, backend name)."""
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    sys.path.insert(0, str(REPO / "oracle"))
+    import step_oracle as so
+    ref = REPO / "oracle" / "_ref" / "libtrba_ref_omp.so"
+    be = so.CpuBackend(ref if ref.exists() else REPO / "oracle" / "liboracle.so")
+    cfg = so.Config(img_w=img_w, max_len=max_len)
+    orc = so.OracleTrba(cfg, so.init_params(cfg, seed), be)
+    batches = [so.make_batch(cfg, lines, seed + i) for i in range(2)]
+    for i in range(warmup):
+        orc.train_step(*batches[i % 2])
+    t0 = time.perf_counter()
+    for i in range(steps):
+        orc.train_step(*batches[i % 2])
+    dt = time.perf_counter() - t0
+    kind = "reference" if be.path.name == "libtrba_ref_omp.so" else "port"
+    return lines * steps / dt, cores, kind, be.path.name
+
+
+def reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    # bounded sample: about 2 minutes of CPU work in total for the run
+    per_line = 0.12 * args.img_w / 160.0
+    lines = max(2, min(16, int(120.0 / max(1, args.steps + args.warmup) / per_line)))
+    v, cores, kind, lib = cpu_step_sample(lines, args.steps, args.warmup, args.img_w, args.max_len, args.seed)
+    sample = f"{lines} lines/step x {args.steps} timed steps (after {args.warmup} warm-up), {lib}, OMP {cores} threads"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "lines/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * lines / v, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMM / fp32", "data": "synthetic",
+        "config": {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}",
+                   "img": f"3x32x{args.img_w}", "feat_dim": 128, "hidden": 64, "classes": 130,
+                   "lines_per_step": lines},
+        "cpu_baseline": {"value": v, "unit": "lines/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": v, "unit": "lines/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------ ours --
+def our_arm(args):
+    import numpy as np
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    pkg = load_package()
+    from trba_b200 import data
+    from trba_b200.model import Config, QatModel
+    L = pkg.lib()
+    cfg = Config(img_w=args.img_w, max_len=args.max_len, batch=args.batch)
+    m = QatModel(cfg)
+    m.set_params(data.init_params(m.manifest(), cfg, args.seed))
+    if world > 1:
+        import torch.distributed as dist
+        obj = [QatModel.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        m.dp_init(obj[0], rank, world)
+    host = data.make_batch(cfg, args.batch, args.seed + 1000 * rank + 1)
+    pinned = [torch.from_numpy(a).pin_memory() for a in host]
+    devb = [p.to(dev) for p in pinned]
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        m.train_step(*devb, stream=sptr)
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    l0 = L.trba_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        m.train_step(*devb, stream=sptr)
+    e1.record(stream)
+    barrier()
+    ck = clocks.stop()
+    launches = (L.trba_launch_count() - l0) / args.steps
+    ms = e0.elapsed_time(e1) / args.steps
+    loss = m.loss()
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    value = args.batch * world / (ms / 1000.0)
+
+    # end to end through the host-buffer entry point: H2D inputs + D2H loss in every step
+    e2e = None
+    if not args.no_e2e:
+        np_in = [p.numpy() for p in pinned]
+        m.train_step_host(*np_in, stream=sptr)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.train_step_host(*np_in, stream=sptr)
+        e1.record(stream)
+        barrier()
+        ms2 = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(ms2, op=torch.distributed.ReduceOp.MAX)
+        h2d = sum(int(a.nbytes) for a in np_in)
+        e2e = {"value": args.batch * world / (float(ms2.item()) / 1000.0), "unit": "lines/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, kind, lib = cpu_step_sample(4, 2, 1, args.img_w, args.max_len, args.seed)
+        cpu = {"value": v, "unit": "lines/s", "cores": cores, "kind": kind,
+               "sample": f"4 lines/step x 2 steps of the same 32x{args.img_w} step, {lib}, OMP {cores} threads"}
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "lines/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 (s8xs8->s32 tcgen05) / fp32", "data": "synthetic",
+            "config": {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}",
+                       "img": f"3x32x{args.img_w}", "feat_dim": 128, "hidden": 64, "classes": 130,
+                       "global_batch": args.batch * world, "per_gpu_batch": args.batch,
+                       "parallelism": f"dp{world}", "l2": "working set > 126 MB L2 (activations of a step)",
+                       "loss_last": [float(x) for x in loss]},
+            "gpu_launches": launches,
+            "clocks": ck,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "roofline": None,
+        }
+        print(json.dumps(out), flush=True)
+    m.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        our_arm(args)
+
+
+if __name__ == "__main__":
+    main()

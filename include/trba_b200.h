@@ -17,6 +17,16 @@ extern "C" {
 void trba_gemm_int8_simt(const int8_t *a, const int8_t *b, int32_t *c, int m, int n, int k,
                          void *stream);
 
+/* Split-K variant of launch_gemm_int8 for long K: C (zeroed by the caller)
+ * += A . Bt^T, K split `splits` ways (0 = automatic), partial tiles combined
+ * with integer atomics (exact, order-independent). */
+void trba_gemm_int8_splitk(const int8_t *a, const int8_t *b, int32_t *c, int m, int n, int k, int splits,
+                           void *stream);
+
+/* Number of kernels this library has launched so far (every launch site
+ * counts itself), for reporting launches per step. */
+long long trba_launch_count(void);
+
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier
  * wait gave up.  Synchronises the device; clears the word if clear != 0. */
 int trba_tc_error_poll(int clear);

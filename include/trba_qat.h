@@ -1,0 +1,106 @@
+/*
+ * trba_qat.h — the fused, device-resident INT8-QAT training step of
+ * libtrba_b200.so (new entry points; no counterpart in the reference's C ABI).
+ *
+ * One call runs what the reference's return_main_step (later snapshot
+ * src/main.rs:2249-2413) runs across its Rust host and backend: SE-ResNet
+ * QAT forward/backward (src/qnet.rs), 2-layer BiLSTM (src/rnn.rs), attention
+ * decoder (src/attn.rs), CE + CTC losses (src/main.rs:2300-2336,
+ * src/ctc.rs), global-norm clip, Muon for matrices and Adam for vectors
+ * (src/opt.rs, device conv Muon src/qnet.rs:559-573) and the QAT weight
+ * re-quantisation — with every scale, statistic and gradient kept on the
+ * device (no host round trip inside the step).
+ *
+ * Parameters live in one flat fp32 buffer in the reference's manifest order
+ * (Model::params_filtered, src/main.rs:954-1030); gradients in a second
+ * buffer of the same layout, which is what data-parallel training
+ * all-reduces.  All pointers passed to *_dev functions are device pointers;
+ * *_host functions take host pointers (pinned for asynchronous copies).
+ * Functions return 0 on success, a negative value on invalid arguments and a
+ * positive CUDA error code otherwise.
+ */
+#ifndef TRBA_QAT_H
+#define TRBA_QAT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct trba_model trba_model;
+
+typedef struct {
+    int fd;           /* feature width (src/qnet.rs:1430: widths fd/8 .. fd)   */
+    int hidden;       /* BiLSTM / decoder hidden size                           */
+    int classes;      /* vocabulary incl. pad 0, sos 1, eos 2                   */
+    int img_h, img_w; /* input image (int8, NCHW, scale 1/127)                  */
+    int max_len;      /* decoder steps = max_len + 1                            */
+    int rnn_layers;
+    int batch;        /* largest batch a step may use (buffers are sized once)  */
+    int sos, eos, pad;
+    float lr, weight_decay, ctc_weight, muon_cap;
+    int clip_warmup;  /* steps with global-norm clipping at 5.0                 */
+    int wgrad_mode;   /* 0: reference-compatible operand order, 1: dW = dX^T col */
+} trba_model_config;
+
+/* TRBA-small defaults (fd 128, hidden 64, 130 classes, 32x160, max_len 20). */
+void trba_model_default_config(trba_model_config *cfg);
+
+trba_model *trba_model_create(const trba_model_config *cfg);
+void trba_model_destroy(trba_model *m);
+
+/* Parameter manifest: count of entries and of floats; entry i gives its name,
+ * offset (floats) in the flat buffer, matrix shape (cols = 0 for vectors) and
+ * kind (0 conv weight: device Muon, 1 matrix: Muon, 2 vector: Adam). */
+long long trba_model_param_count(const trba_model *m);
+int trba_model_param_entries(const trba_model *m);
+int trba_model_param_entry(const trba_model *m, int i, char *name, int name_cap, long long *offset, int *rows,
+                           int *cols, int *kind);
+
+/* Copy the whole parameter vector in / out (host fp32, manifest order).
+ * set_params also re-quantises the conv weights and resets optimiser state. */
+int trba_model_set_params(trba_model *m, const float *host, long long n);
+int trba_model_get_params(trba_model *m, float *host, long long n);
+/* Gradients of the last forward_backward (before clipping / averaging). */
+int trba_model_get_grads(trba_model *m, float *host, long long n);
+float *trba_model_grad_buffer(trba_model *m);
+
+/* Forward + backward on device inputs: img [B,3,H,W] int8; text_in, target
+ * [B, max_len+1] int32; ctc_tgt [B, max_len+1] int32 with lengths ctc_len
+ * [B] (tokens plus eos).  Leaves the loss in trba_model_loss_dev(). */
+int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                                const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream);
+/* Clip (first clip_warmup steps), Muon/Adam, re-quantise. */
+int trba_model_optimizer_step(trba_model *m, void *stream);
+/* forward_backward, gradient all-reduce (when data-parallel), optimizer_step. */
+int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                          const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream);
+/* The same step from host buffers: copies the inputs in, runs the step and
+ * copies the three losses (total, attention CE, CTC) back into loss_host. */
+int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                               const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, float *loss_host,
+                               void *stream);
+/* Device pointer to 4 floats: total loss, attention CE, CTC, CE grad scale. */
+const float *trba_model_loss_dev(const trba_model *m);
+/* Batch-norm running statistics (mean then var, conv manifest order). */
+int trba_model_get_running_stats(trba_model *m, float *host, long long n);
+long long trba_model_running_stats_count(const trba_model *m);
+/* Number of optimizer steps taken. */
+long long trba_model_step_count(const trba_model *m);
+/* Bytes of device memory the model holds. */
+long long trba_model_device_bytes(const trba_model *m);
+
+/* ---- data parallel (one process per GPU, NCCL over NVLink) ---- */
+/* 128-byte NCCL unique id from rank 0, broadcast by the caller. */
+int trba_dp_unique_id(void *id128);
+/* Join the NCCL communicator; afterwards train_step all-reduces (averages)
+ * the gradient buffer before the optimizer step. */
+int trba_dp_init(trba_model *m, const void *id128, int rank, int world);
+int trba_dp_finalize(trba_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -37,7 +37,16 @@ inline int grid_for(i64 n, int threads = 256) {
         if (e_ != cudaSuccess) trba::report_error(__FILE__, __LINE__, cudaGetErrorString(e_), (int)e_); \
     } while (0)
 
-#define TRBA_LAUNCH_CHECK() TRBA_CHECK(cudaGetLastError())
+// Every kernel launch of the library goes through this check, which also
+// counts it (trba_launch_count()).
+namespace trba {
+void count_launch();
+}
+#define TRBA_LAUNCH_CHECK()          \
+    do {                             \
+        trba::count_launch();        \
+        TRBA_CHECK(cudaGetLastError()); \
+    } while (0)
 
 // Shape contract violations (the reference's REQUIRE_SHAPE, cuda/kernels.cu
 // of the later snapshot, lines 89-96): same policy as CUDA errors.

@@ -1,16 +1,24 @@
-// launch_gemm_int8 on B200: C[M,N] s32 = A[M,K] . Bt[N,K]^T with tcgen05
-// kind::i8 tensor cores (reference contract: cuda/kernels.cu:227-250 of the
-// checked-out tree, operands row-major with leading dimension align16(K)).
+// int8 GEMM on B200 tensor cores: C[M,N] s32 = A[M,K] . Bt[N,K]^T with
+// tcgen05 kind::i8 (reference contract of launch_gemm_int8:
+// cuda/kernels.cu:227-250 of the checked-out tree — row-major operands,
+// leading dimension align16(K), compact C).
 //
 // Design (one persistent CTA per SM, 6 warps, warp-specialised):
-//   warp 0 lane 0 : TMA producer. For each 128 x BN output tile it streams
-//                   128-byte K slices of A (128 rows) and B (BN rows) into a
-//                   STAGES-deep ring of 128B-swizzled shared-memory stages.
+//   warp 0 lane 0 : TMA producer. For each 128 x BN output tile (and K
+//                   split) it streams 128-byte K slices of A (128 rows) and
+//                   B (BN rows) into a STAGES-deep ring of 128B-swizzled
+//                   shared-memory stages.
 //   warp 1 lane 0 : MMA issuer. Four tcgen05.mma (M=128, N=BN, K=32) per
 //                   stage into one of two TMEM accumulators, so the epilogue
 //                   of tile i overlaps the MMAs of tile i+1.
 //   warps 2..5    : epilogue. tcgen05.ld 32 columns at a time (each thread
-//                   owns one output row) and stores s32 to global memory.
+//                   owns one output row) and hands them to an epilogue policy:
+//                     EpiS32       s32 store (launch_gemm_int8)
+//                     EpiS32Atomic s32 atomicAdd, for split-K (exact: integer
+//                                  addition is associative)
+//                     EpiConvF32   conv forward: x = acc * (s_in * w_s) written
+//                                  NCHW, plus per-channel sum / sum of squares
+//                                  of x in f64 for the BatchNorm statistics.
 // Tensor maps cover exactly [M, K] and [N, K]: TMA zero-fills every
 // out-of-range row and column, so the kernel never reads the operands'
 // padding and needs no tail handling in the main loop.
@@ -37,6 +45,7 @@ constexpr int BM = 128;   // UMMA M (cta_group::1)
 constexpr int BK = 128;   // bytes of K per stage = one 128B swizzle row
 constexpr int UK = 32;    // K of one kind::i8 MMA
 constexpr int kThreads = 192;
+constexpr int kMaxN = 512;  // widest N an epilogue with per-column state supports
 
 template <int BN>
 struct Cfg {
@@ -45,7 +54,8 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two >= 64)
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512;
+    static constexpr int EPI_SMEM = 2 * kMaxN * 8;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512 + EPI_SMEM;
 };
 
 struct Ctl {  // lives after the stage ring in shared memory
@@ -60,20 +70,118 @@ struct Ctl {  // lives after the stage ring in shared memory
     uint32_t consumed;  // stage loads whose data the MMA warp waited for
 };
 
-template <int BN>
+// Sum of a[] over the 32 lanes for each of 32 columns: afterwards lane l
+// holds the total of column l (butterfly reduce-scatter, 31 shuffles).
+__device__ __forceinline__ double reduce_scatter32(double (&a)[32], int lane) {
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool upper = lane & s;
+#pragma unroll
+        for (int j = 0; j < s; ++j) {
+            const double send = upper ? a[j] : a[j + s];
+            const double keep = upper ? a[j + s] : a[j];
+            a[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+    return a[0];
+}
+
+// ------------------------------------------------------------ epilogues --
+struct EpiS32 {
+    int32_t *C;
+    int ldc;
+    bool vec4;  // C rows are 16-byte aligned and N % 4 == 0
+    __device__ void init(double *) {}
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
+        if (row >= M) return;
+        int32_t *crow = C + (i64)row * ldc;
+        if (vec4 && col + 32 <= N) {
+            int4 *dst = reinterpret_cast<int4 *>(crow + col);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                dst[j] = make_int4((int)v[4 * j], (int)v[4 * j + 1], (int)v[4 * j + 2], (int)v[4 * j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col + j < N) crow[col + j] = (int32_t)v[j];
+        }
+    }
+    __device__ void finish(double *, int) {}
+};
+
+struct EpiS32Atomic {
+    int32_t *C;
+    int ldc;
+    __device__ void init(double *) {}
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
+        if (row >= M) return;
+        int32_t *crow = C + (i64)row * ldc;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (col + j < N && v[j] != 0u) atomicAdd(crow + col + j, (int32_t)v[j]);
+    }
+    __device__ void finish(double *, int) {}
+};
+
+struct EpiConvF32 {
+    float *x;            // NCHW output, row r = b*HW + p, column = channel
+    const float *s_in;   // device scalar: activation scale of the conv input
+    const float *w_s;    // device scalar: per-tensor weight scale
+    double *bn_acc;      // [2*N]: per-channel sum, then sum of squares (f64)
+    int HW;
+    __device__ void init(double *sm) {
+        for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += 128) sm[i] = 0.0;
+    }
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
+        const float scale = fmul(*s_in, *w_s);
+        const bool rv = row < M;
+        const int b = rv ? row / HW : 0, p = rv ? row - b * HW : 0;
+        double s[32], q[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float val = fmul((float)(int32_t)v[j], scale);
+            const bool ok = rv && col + j < N;
+            if (ok) x[((i64)b * N + col + j) * HW + p] = val;
+            s[j] = ok ? (double)val : 0.0;
+            q[j] = ok ? (double)val * (double)val : 0.0;
+        }
+        const double cs = reduce_scatter32(s, lane);
+        const double cq = reduce_scatter32(q, lane);
+        if (col + lane < N) {
+            atomicAdd(sm + col + lane, cs);
+            atomicAdd(sm + kMaxN + col + lane, cq);
+        }
+    }
+    __device__ void finish(double *sm, int N) {
+        for (int i = threadIdx.x - 64; i < N; i += 128) {
+            if (sm[i] != 0.0) atomicAdd(bn_acc + i, sm[i]);
+            if (sm[kMaxN + i] != 0.0) atomicAdd(bn_acc + N + i, sm[kMaxN + i]);
+        }
+    }
+};
+
+struct Shape {
+    int M, N, K;
+    int splits;        // K splits (1 = none)
+    int kb_per_split;  // K blocks of 128 per split
+};
+
+template <int BN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  int M, int N, int K, int32_t *__restrict__ C) {
+gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
+                  Epi epi) {
     using G = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + G::STAGES * G::A_BYTES;
     Ctl *ctl = reinterpret_cast<Ctl *>(smem + G::STAGES * G::STAGE_BYTES);
+    double *epi_sm = reinterpret_cast<double *>(smem + G::STAGES * G::STAGE_BYTES + 512);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = sh.M, N = sh.N, K = sh.K;
     const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
-    const int tiles = m_tiles * n_tiles, kblocks = (K + BK - 1) / BK;
+    const int tiles = m_tiles * n_tiles * sh.splits, kblocks = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < G::STAGES; ++s) {
@@ -92,6 +200,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
+    if (warp >= 2) epi.init(epi_sm);
     if (warp == 1) {
         tmem_alloc(&ctl->tmem_base, G::TMEM_COLS);
         tmem_relinquish();
@@ -102,13 +211,25 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const uint32_t tbase = ctl->tmem_base;
     volatile int *abort = &ctl->abort;
 
+    // tile t -> (split, m block, n block); n fastest so CTAs working at the
+    // same time share the A block through L2.
+    auto tile_coords = [&](int t, int &m0, int &n0, int &kb0, int &kb1) {
+        const int per_split = m_tiles * n_tiles;
+        const int sp = t / per_split, r = t - sp * per_split;
+        m0 = (r / n_tiles) * BM;
+        n0 = (r % n_tiles) * BN;
+        kb0 = sp * sh.kb_per_split;
+        kb1 = min(kblocks, kb0 + sh.kb_per_split);
+    };
+
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             uint32_t it = 0;
             for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
-                const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                int m0, n0, kb0, kb1;
+                tile_coords(t, m0, n0, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % G::STAGES;
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort)) break;
@@ -126,10 +247,12 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             uint32_t it = 0, acc = 0, acc_ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                int m0, n0, kb0, kb1;
+                tile_coords(t, m0, n0, kb0, kb1);
                 if (!(ok = mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort))) break;
                 tc_fence_after();
                 const uint32_t d = tbase + acc * BN;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % G::STAGES;
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!(ok = mbar_wait(&ctl->full[s], ph, abort))) break;
@@ -139,7 +262,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 #pragma unroll
                     for (int k = 0; k < BK / UK; ++k)
                         mma_i8(d, desc_k_sw128(a0 + k * UK), desc_k_sw128(b0 + k * UK), idesc,
-                               (kb | k) != 0);
+                               (kb != kb0 || k != 0) ? 1u : 0u);
                     mma_commit(&ctl->empty[s]);
                 }
                 if (!ok) break;
@@ -147,9 +270,9 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                 acc ^= 1u;
                 if (acc == 0) acc_ph ^= 1u;
             }
-            // Every MMA this thread issued has retired once `drained` fires.
+            // Every MMA this thread issued has retired once `drained` fires
             // (waited on with a private flag: an abort raised elsewhere must
-            // not skip the drain before TMEM is released)
+            // not skip the drain before TMEM is released).
             mma_commit(&ctl->drained);
             volatile int never = 0;
             mbar_wait(&ctl->drained, 0, &never, 200000000ull);
@@ -159,31 +282,20 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         uint32_t acc = 0, acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            int m0, n0, kb0, kb1;
+            tile_coords(t, m0, n0, kb0, kb1);
             const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort);
             __syncwarp();  // reconverge before the warp-collective tcgen05.ld
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
             const int row = m0 + q * 32 + lane;
-            int32_t *crow = C + (i64)row * N;
+            const bool empty_split = kb0 >= kb1;  // nothing accumulated: skip
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += 32) {
+            for (int c0 = 0; c0 < BN && n0 + c0 < N && !empty_split; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
                 tmem_ld_wait();
-                if (row < M) {
-                    const int col = n0 + c0;
-                    if (col + 32 <= N && (N & 3) == 0) {
-                        int4 *dst = reinterpret_cast<int4 *>(crow + col);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            dst[j] = make_int4((int)v[4 * j], (int)v[4 * j + 1], (int)v[4 * j + 2], (int)v[4 * j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col + j < N) crow[col + j] = (int32_t)v[j];
-                    }
-                }
+                epi.store(row, n0 + c0, M, N, v, lane, epi_sm);
             }
             tc_fence_before();
             mbar_arrive(&ctl->tempty[acc]);
@@ -193,6 +305,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     }
 
     __syncthreads();
+    if (warp >= 2) epi.finish(epi_sm, N);
     if (threadIdx.x == 0 && *abort) {
         // Drain loads that were issued but never waited for, so no TMA write
         // lands in shared memory after the CTA is gone (bounded as well).
@@ -262,21 +375,43 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int BN>
-void launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K, int32_t *C,
-               cudaStream_t st) {
+template <int BN, class Epi>
+void launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const Epi &epi, cudaStream_t st) {
     using G = Cfg<BN>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        TRBA_CHECK(cudaFuncSetAttribute(gemm_i8_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+        TRBA_CHECK(cudaFuncSetAttribute(gemm_i8_tc_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        G::SMEM));
         attr_set[dev] = true;
     }
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int tiles = ((sh.M + BM - 1) / BM) * ((sh.N + BN - 1) / BN) * sh.splits;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_i8_tc_kernel<BN><<<grid, kThreads, G::SMEM, st>>>(ta, tb, M, N, K, C);
+    gemm_i8_tc_kernel<BN, Epi><<<grid, kThreads, G::SMEM, st>>>(ta, tb, sh, epi);
     TRBA_LAUNCH_CHECK();
+}
+
+template <class Epi>
+bool run_tc(const int8_t *A, int lda, const int8_t *B, int ldb, Shape sh, const Epi &epi, cudaStream_t st) {
+    const int bn = pick_bn(sh.N);
+    CUtensorMap ta, tb;
+    if (!make_tmap_i8(&ta, A, sh.M, sh.K, lda, BM) || !make_tmap_i8(&tb, B, sh.N, sh.K, ldb, bn)) return false;
+    switch (bn) {
+        case 32: launch_tc<32>(ta, tb, sh, epi, st); break;
+        case 64: launch_tc<64>(ta, tb, sh, epi, st); break;
+        case 128: launch_tc<128>(ta, tb, sh, epi, st); break;
+        default: launch_tc<256>(ta, tb, sh, epi, st); break;
+    }
+    return true;
+}
+
+Shape make_shape(int M, int N, int K, int splits) {
+    const int kblocks = (K + BK - 1) / BK;
+    if (splits < 1) splits = 1;
+    if (splits > kblocks) splits = kblocks;
+    const int per = (kblocks + splits - 1) / splits;
+    return Shape{M, N, K, (kblocks + per - 1) / per, per};
 }
 
 }  // namespace
@@ -299,24 +434,32 @@ bool make_tmap_i8(CUtensorMap *m, const void *ptr, int rows, int k, int ld, int 
 
 int pick_bn(int N) { return N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256; }
 
-// Returns false when the operands cannot be described by a tensor map (the
-// caller then uses the CUDA-core kernel).
-bool gemm_i8_tc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld,
-                cudaStream_t st) {
-    const int bn = pick_bn(N);
-    CUtensorMap ta, tb;
-    if (!make_tmap_i8(&ta, A, M, K, ld, BM) || !make_tmap_i8(&tb, B, N, K, ld, bn)) return false;
-    switch (bn) {
-        case 32: launch_tc<32>(ta, tb, M, N, K, C, st); break;
-        case 64: launch_tc<64>(ta, tb, M, N, K, C, st); break;
-        case 128: launch_tc<128>(ta, tb, M, N, K, C, st); break;
-        default: launch_tc<256>(ta, tb, M, N, K, C, st); break;
-    }
-    return true;
+bool gemm_i8_tc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st) {
+    EpiS32 e{C, N, ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && (N & 3) == 0};
+    return run_tc(A, ld, B, ld, make_shape(M, N, K, 1), e, st);
 }
 
-void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld,
-                  cudaStream_t st) {
+bool gemm_i8_splitk_atomic(const int8_t *A, int lda, const int8_t *B, int ldb, int32_t *C, int M, int N, int K,
+                           int splits, cudaStream_t st) {
+    return run_tc(A, lda, B, ldb, make_shape(M, N, K, splits), EpiS32Atomic{C, N}, st);
+}
+
+bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, float *x,
+                      const float *s_in, const float *w_s, double *bn_acc, int HW, cudaStream_t st) {
+    if (N > kMaxN) return false;
+    return run_tc(A, lda, B, ldb, make_shape(M, N, K, 1), EpiConvF32{x, s_in, w_s, bn_acc, HW}, st);
+}
+
+int splitk_for(int M, int N, int K) {
+    // Enough (m, n, split) tiles for two waves of SMs, at least 2 K blocks each.
+    const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
+    const int kblocks = (K + BK - 1) / BK;
+    int s = (2 * sm_count() + tiles - 1) / tiles;
+    if (s > kblocks / 2) s = kblocks / 2;
+    return s < 1 ? 1 : s;
+}
+
+void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st) {
     dim3 grid((M + 63) / 64, (N + 63) / 64);
     gemm_i8_simt_kernel<<<grid, 256, 0, st>>>(A, B, C, M, N, K, ld);
     TRBA_LAUNCH_CHECK();
@@ -336,6 +479,17 @@ void launch_gemm_int8(const int8_t *a, const int8_t *b, int32_t *c, int m, int n
 void trba_gemm_int8_simt(const int8_t *a, const int8_t *b, int32_t *c, int m, int n, int k, void *stream) {
     if (m <= 0 || n <= 0 || k <= 0) return;
     gemm_i8_simt(a, b, c, m, n, k, (k + 15) & ~15, as_stream(stream));
+}
+
+// Split-K variant: C (zeroed by the caller) += A . Bt^T, K split `splits`
+// ways (0 = automatic), partial tiles combined with integer atomics.
+void trba_gemm_int8_splitk(const int8_t *a, const int8_t *b, int32_t *c, int m, int n, int k, int splits,
+                           void *stream) {
+    if (m <= 0 || n <= 0 || k <= 0) return;
+    const int ld = (k + 15) & ~15;
+    if (splits <= 0) splits = splitk_for(m, n, k);
+    if (!gemm_i8_splitk_atomic(a, ld, b, ld, c, m, n, k, splits, as_stream(stream)))
+        report_error(__FILE__, __LINE__, "trba_gemm_int8_splitk: operands not 16-byte aligned", -1);
 }
 
 // Device-side error word of the tensor-core kernels (1 = a bounded wait

@@ -10,9 +10,17 @@ namespace trba {
 // 128 bytes of K by box_rows rows, 128-byte swizzle, zero fill outside.
 bool make_tmap_i8(CUtensorMap *m, const void *ptr, int rows, int k, int ld, int box_rows);
 int pick_bn(int N);
-bool gemm_i8_tc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld,
-                cudaStream_t st);
-void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld,
-                  cudaStream_t st);
+// C[M,N] s32 = A . Bt^T (compact C).  False if a tensor map cannot describe
+// the operands (caller falls back to gemm_i8_simt).
+bool gemm_i8_tc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st);
+// C (pre-zeroed) += A . Bt^T with K split `splits` ways, integer atomics.
+bool gemm_i8_splitk_atomic(const int8_t *A, int lda, const int8_t *B, int ldb, int32_t *C, int M, int N, int K,
+                           int splits, cudaStream_t st);
+// Conv forward: x[b, n, p] = (float)acc[r = b*HW + p, n] * (s_in * w_s), and
+// bn_acc[n] += sum x, bn_acc[N + n] += sum x^2 (f64).  N <= 512.
+bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, float *x,
+                      const float *s_in, const float *w_s, double *bn_acc, int HW, cudaStream_t st);
+int splitk_for(int M, int N, int K);
+void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st);
 
 }  // namespace trba

@@ -1,0 +1,559 @@
+// Fused element-wise / reduction kernels of the device-resident QAT step.
+// Each kernel restates one or more of the reference's host-orchestrated
+// launches (cited per kernel) with the same float expression order, written
+// with explicit round-to-nearest intrinsics so that nothing is contracted.
+#include "qat_kernels.cuh"
+
+namespace trba {
+namespace qat {
+namespace {
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block reductions (blockDim a multiple of 32, <= 1024).  Result in thread 0.
+__device__ double block_sum_d(double v, double *sm) {
+    v = warp_sum_d(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) sm[w] = v;
+    __syncthreads();
+    double r = 0.0;
+    if (w == 0) {
+        r = lane < nw ? sm[lane] : 0.0;
+        r = warp_sum_d(r);
+    }
+    return r;
+}
+__device__ float block_max_f(float v, float *sm) {
+    v = warp_max_f(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) sm[w] = v;
+    __syncthreads();
+    float r = 0.0f;
+    if (w == 0) {
+        r = lane < nw ? sm[lane] : 0.0f;
+        r = warp_max_f(r);
+    }
+    return r;
+}
+
+__device__ __forceinline__ void atomic_max_nonneg(float *p, float v) {
+    atomicMax(reinterpret_cast<int *>(p), __float_as_int(v));
+}
+
+// BatchNorm statistics from the f64 sums (cpu_backend.cpp of the later
+// snapshot, lines 762-767): mean = (float)s / cnt, var = max((float)q/cnt - m^2, 0).
+__device__ __forceinline__ void bn_mean_var(const double *acc, int C, int c, i64 count, float &m, float &v) {
+    const float cnt = (float)count;
+    m = fdiv((float)acc[c], cnt);
+    v = fsub(fdiv((float)acc[C + c], cnt), fmul(m, m));
+    v = v < 0.0f ? 0.0f : v;
+}
+__device__ __forceinline__ float bn_rstd(float var) { return fdiv(1.0f, __fsqrt_rn(fadd(var, kBnEps))); }
+
+// Per-plane view of a source: everything a thread needs for plane (b, c).
+struct PlaneSrc {
+    int kind;
+    const float *x;
+    float mean, r, gamma, beta, gate, res_s;
+    const float *res_f;
+    const int8_t *res_q;
+    __device__ __forceinline__ float at(i64 i) const {
+        switch (kind) {
+            case SRC_BN: return fadd(fmul(fmul(fsub(x[i], mean), r), gamma), beta);
+            case SRC_FLOAT: return x[i];
+            case SRC_SE_RES_F: return fadd(fmul(x[i], gate), res_f[i]);
+            default: return fadd(fmul(x[i], gate), fmul((float)res_q[i], res_s));
+        }
+    }
+};
+
+__device__ PlaneSrc plane_src(const Src &s, int b, int c, float *mean_out = nullptr, float *var_out = nullptr) {
+    PlaneSrc p;
+    p.kind = s.kind;
+    p.x = s.x;
+    p.mean = p.r = p.gamma = p.beta = p.gate = p.res_s = 0.0f;
+    p.res_f = s.res_f;
+    p.res_q = s.res_q;
+    if (s.kind == SRC_BN) {
+        float m, v;
+        bn_mean_var(s.bn_acc, s.C, c, s.count, m, v);
+        p.mean = m;
+        p.r = bn_rstd(v);
+        p.gamma = s.gamma[c];
+        p.beta = s.beta[c];
+        if (mean_out && b == 0 && threadIdx.x == 0) {
+            mean_out[c] = m;
+            var_out[c] = v;
+        }
+    } else if (s.kind == SRC_SE_RES_F || s.kind == SRC_SE_RES_Q) {
+        p.gate = s.gate[(i64)b * s.C + c];
+        if (s.kind == SRC_SE_RES_Q) p.res_s = *s.res_s;
+    }
+    return p;
+}
+
+// ------------------------------------------------------------- forward --
+// src/qnet.rs:877-895 (bn_apply), 1212-1214 (avgpool_hw of y2),
+// 1102-1106 (reduce_max_abs before relu_quant).
+__global__ void act_stats_kernel(Src s, float *y_out, float *mean_out, float *var_out, float *pool_out,
+                                 float *vmax) {
+    __shared__ double smd[32];
+    __shared__ float smf[32];
+    const int plane = blockIdx.x, b = plane / s.C, c = plane - b * s.C;
+    const PlaneSrc p = plane_src(s, b, c, mean_out, var_out);
+    const i64 base = (i64)plane * s.HW;
+    double sum = 0.0;
+    float mx = 0.0f;
+    for (int j = threadIdx.x; j < s.HW; j += blockDim.x) {
+        const float v = p.at(base + j);
+        if (y_out) y_out[base + j] = v;
+        sum += (double)v;
+        mx = fmaxf(mx, fabsf(v));
+    }
+    if (pool_out) {
+        const double t = block_sum_d(sum, smd);
+        if (threadIdx.x == 0) pool_out[plane] = (float)(t / (double)s.HW);
+    }
+    if (vmax) {
+        const float m = block_max_f(mx, smf);
+        if (threadIdx.x == 0) atomic_max_nonneg(vmax, m);
+    }
+}
+
+__global__ void act_quant_kernel(Src s, const float *vmax, float *s_out, int8_t *q, int relu) {
+    const int plane = blockIdx.x, b = plane / s.C, c = plane - b * s.C;
+    const PlaneSrc p = plane_src(s, b, c);
+    const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
+    const float inv = fdiv(1.0f, sc);
+    if (plane == 0 && threadIdx.x == 0 && s_out) *s_out = sc;
+    const i64 base = (i64)plane * s.HW;
+    for (int j = threadIdx.x; j < s.HW; j += blockDim.x) {
+        const float v = p.at(base + j);
+        const float t = relu ? fminf(fmul(fmaxf(v, 0.0f), inv), 127.0f) : fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f);
+        q[base + j] = (int8_t)rint_even(t);
+    }
+}
+
+int plane_threads(int HW) { return HW >= 256 ? 256 : HW > 64 ? 128 : HW > 32 ? 64 : 32; }
+
+// src/qnet.rs:1219-1222: pre1 = fc1 pool, h1 = relu, pre2 = fc2 h1, gate = sigmoid.
+__global__ void se_forward_kernel(const float *pool, const float *w1, const float *w2, int C, int R, float *h1,
+                                  float *gate) {
+    extern __shared__ float sm[];
+    float *sp = sm, *sh = sm + C;
+    const int b = blockIdx.x;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) sp[i] = pool[(i64)b * C + i];
+    __syncthreads();
+    for (int j = threadIdx.x; j < R; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int i = 0; i < C; ++i) acc = fadd(acc, fmul(sp[i], w1[(i64)j * C + i]));
+        const float h = fmaxf(acc, 0.0f);
+        sh[j] = h;
+        h1[(i64)b * R + j] = h;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < R; ++j) acc = fadd(acc, fmul(sh[j], w2[(i64)c * R + j]));
+        gate[(i64)b * C + c] = fdiv(1.0f, fadd(1.0f, expf(-acc)));
+    }
+}
+
+// ------------------------------------------------------------ backward --
+__global__ void grad_quant_max_kernel(const float *gv, const float *s_out, i64 n, float *vmax) {
+    __shared__ float smf[32];
+    const float s = *s_out;
+    float mx = 0.0f;
+    GRID_LOOP(i, n) mx = fmaxf(mx, fabsf(fmul(gv[i], s)));
+    const float m = block_max_f(mx, smf);
+    if (threadIdx.x == 0) atomic_max_nonneg(vmax, m);
+}
+
+__global__ void grad_quant_mask_kernel(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out,
+                                       i64 n, float *s_dq_out, float *dz) {
+    const float s = *s_out;
+    const float sdq = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
+    const float inv = fdiv(1.0f, sdq);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && s_dq_out) *s_dq_out = sdq;
+    GRID_LOOP(i, n) {
+        const float v = fmul(gv[i], s);
+        const int qd = rint_even(fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f));
+        dz[i] = q_out[i] > 0 ? fmul((float)qd, sdq) : 0.0f;
+    }
+}
+
+// One CTA per sample: SE squeeze of dz*y2, the excitation MLP backward and
+// dy2_full = dz*gate + dpooled/HW over the sample's planes.
+__global__ void se_backward_kernel(const float *dz, const float *y2, const float *gate, const float *h1,
+                                   const float *w1, const float *w2, int C, int HW, int R, float *dpre1,
+                                   float *dpre2, float *dpooled, float *dy2_full) {
+    extern __shared__ float sm[];
+    float *s_dp2 = sm, *s_dp1 = sm + C, *s_dpool = sm + C + R;
+    const int b = blockIdx.x;
+    const i64 base = (i64)b * C * HW;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float *pz = dz + base + (i64)c * HW, *py = y2 + base + (i64)c * HW;
+        double s = 0.0;
+        for (int j = 0; j < HW; ++j) s += (double)fmul(pz[j], py[j]);
+        const float pm = (float)(s / (double)HW);
+        const float dgate = fmul(pm, (float)HW);
+        const float g = gate[(i64)b * C + c];
+        const float d2 = fmul(fmul(dgate, g), fsub(1.0f, g));
+        s_dp2[c] = d2;
+        dpre2[(i64)b * C + c] = d2;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < R; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int c = 0; c < C; ++c) acc = fadd(acc, fmul(s_dp2[c], w2[(i64)c * R + j]));
+        const float d1 = h1[(i64)b * R + j] > 0.0f ? acc : 0.0f;
+        s_dp1[j] = d1;
+        dpre1[(i64)b * R + j] = d1;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < R; ++j) acc = fadd(acc, fmul(s_dp1[j], w1[(i64)j * C + i]));
+        s_dpool[i] = acc;
+        dpooled[(i64)b * C + i] = acc;
+    }
+    __syncthreads();
+    for (i64 e = threadIdx.x; e < (i64)C * HW; e += blockDim.x) {
+        const int c = (int)(e / HW);
+        dy2_full[base + e] = fadd(fmul(dz[base + e], gate[(i64)b * C + c]), fdiv(s_dpool[c], (float)HW));
+    }
+}
+
+// g_w2[c, j] += sum_b dpre2[b,c] h1[b,j];  g_w1[j, i] += sum_b dpre1[b,j] pool[b,i]
+__global__ void se_wgrad_kernel(const float *dpre1, const float *dpre2, const float *h1, const float *pool, int B,
+                                int C, int R, float *g_w1, float *g_w2) {
+    const int n2 = C * R;
+    GRID_LOOP(e, (i64)2 * n2) {
+        float acc = 0.0f;
+        if (e < n2) {
+            const int c = (int)(e / R), j = (int)(e - (i64)c * R);
+            for (int b = 0; b < B; ++b) acc = fadd(acc, fmul(dpre2[(i64)b * C + c], h1[(i64)b * R + j]));
+            g_w2[e] = fadd(g_w2[e], acc);
+        } else {
+            const i64 f = e - n2;
+            const int j = (int)(f / C), i = (int)(f - (i64)j * C);
+            for (int b = 0; b < B; ++b) acc = fadd(acc, fmul(dpre1[(i64)b * R + j], pool[(i64)b * C + i]));
+            g_w1[f] = fadd(g_w1[f], acc);
+        }
+    }
+}
+
+// later snapshot cpu_backend.cpp:782-802, one CTA per (b, c) plane, f64
+// partials added into acc[c] (sum dy) and acc[C + c] (sum dy*xhat).
+__global__ void bn_bwd_sums_kernel(const float *dy, const float *x, const float *mean, const float *var, int C,
+                                   int HW, double *acc) {
+    __shared__ double smd[32];
+    const int plane = blockIdx.x, c = plane % C;
+    const float m = mean[c], r = bn_rstd(var[c]);
+    const i64 base = (i64)plane * HW;
+    double s = 0.0, sx = 0.0;
+    for (int j = threadIdx.x; j < HW; j += blockDim.x) {
+        const float d = dy[base + j];
+        const float xh = fmul(fsub(x[base + j], m), r);
+        s += (double)d;
+        sx += (double)fmul(d, xh);
+    }
+    const double ts = block_sum_d(s, smd);
+    const double tx = block_sum_d(sx, smd);
+    if (threadIdx.x == 0) {
+        atomicAdd(acc + c, ts);
+        atomicAdd(acc + C + c, tx);
+    }
+}
+
+struct DxPlane {
+    float m, r, a, sdy, sdxh, cnt;
+};
+__device__ DxPlane dx_plane(const float *mean, const float *var, const float *gamma, const double *acc, int C, int c,
+                            i64 count) {
+    DxPlane p;
+    p.m = mean[c];
+    p.r = bn_rstd(var[c]);
+    p.cnt = (float)count;
+    p.a = fdiv(fmul(gamma[c], p.r), p.cnt);
+    p.sdy = (float)acc[c];
+    p.sdxh = (float)acc[C + c];
+    return p;
+}
+// later snapshot cpu_backend.cpp:804-817
+__device__ __forceinline__ float dx_at(const DxPlane &p, float dy, float x) {
+    const float xh = fmul(fsub(x, p.m), p.r);
+    return fmul(p.a, fsub(fsub(fmul(p.cnt, dy), p.sdy), fmul(xh, p.sdxh)));
+}
+
+__global__ void bn_dx_max_kernel(const float *dy, const float *x, const float *mean, const float *var,
+                                 const float *gamma, const double *acc, int B, int C, int HW, float *g_gamma,
+                                 float *g_beta, float *vmax) {
+    __shared__ float smf[32];
+    const int plane = blockIdx.x, b = plane / C, c = plane - b * C;
+    const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, (i64)B * HW);
+    if (b == 0 && threadIdx.x == 0) {  // src/qnet.rs:974-982: g_beta += sum dy, g_gamma += sum dy xhat
+        g_beta[c] = fadd(g_beta[c], p.sdy);
+        g_gamma[c] = fadd(g_gamma[c], p.sdxh);
+    }
+    const i64 base = (i64)plane * HW;
+    float mx = 0.0f;
+    for (int j = threadIdx.x; j < HW; j += blockDim.x) mx = fmaxf(mx, fabsf(dx_at(p, dy[base + j], x[base + j])));
+    const float t = block_max_f(mx, smf);
+    if (threadIdx.x == 0) atomic_max_nonneg(vmax, t);
+}
+
+__global__ void bn_dx_quant_kernel(const float *dy, const float *x, const float *mean, const float *var,
+                                   const float *gamma, const double *acc, int B, int C, int HW, const float *vmax,
+                                   float *s_dx, int8_t *A, int ld, int compat) {
+    const int plane = blockIdx.x, b = plane / C, c = plane - b * C;
+    const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, (i64)B * HW);
+    const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
+    const float inv = fdiv(1.0f, sc);
+    if (plane == 0 && threadIdx.x == 0) *s_dx = sc;
+    const i64 base = (i64)plane * HW;
+    for (int j = threadIdx.x; j < HW; j += blockDim.x) {
+        const float d = dx_at(p, dy[base + j], x[base + j]);
+        const int8_t qv = (int8_t)rint_even(fminf(fmaxf(fmul(d, inv), -127.0f), 127.0f));
+        const i64 i = base + j;
+        if (compat) {
+            const i64 r = i / C, o = i - r * C;  // the NCHW buffer viewed as [rows, C]
+            A[o * ld + r] = qv;
+        } else {
+            A[(i64)c * ld + (i64)b * HW + j] = qv;
+        }
+    }
+}
+
+__global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const float *s_in, i64 n, float *g) {
+    const float deq = fmul(*s_dx, *s_in);
+    GRID_LOOP(i, n) g[i] = fadd(g[i], fmul((float)acc[i], deq));
+}
+
+__global__ void dgrad_kernel(const float *go, const int8_t *wq, i64 w_ld, const float *w_s, int B, int Cin, int H,
+                             int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
+                             const int8_t *mask_q, const float *add, float *gi) {
+    const int hwo = Ho * Wo, hwi = H * W;
+    const float ws = *w_s;
+    GRID_LOOP(i, (i64)B * Cin * hwi) {
+        const i64 bc = i / hwi;
+        const int pix = (int)(i - bc * hwi);
+        const int b = (int)(bc / Cin), ci = (int)(bc - (i64)b * Cin);
+        const int ih = pix / W, iw = pix - ih * W;
+        const float *go_b = go + (i64)b * Cout * hwo;
+        float acc = 0.0f;
+        for (int kh = 0; kh < kH; ++kh) {
+            const int nh = ih + pH - kh;
+            if (nh < 0 || nh % sH) continue;
+            const int oh = nh / sH;
+            if (oh >= Ho) continue;
+            for (int kw = 0; kw < kW; ++kw) {
+                const int nw = iw + pW - kw;
+                if (nw < 0 || nw % sW) continue;
+                const int ow = nw / sW;
+                if (ow >= Wo) continue;
+                const i64 wc = (i64)(ci * kH + kh) * kW + kw;
+                const float *gp = go_b + oh * Wo + ow;
+                for (int oc = 0; oc < Cout; ++oc)
+                    acc = fadd(acc, fmul(gp[(i64)oc * hwo], (float)wq[(i64)oc * w_ld + wc]));
+            }
+        }
+        float v = fmul(acc, ws);
+        if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
+        if (add) v = fadd(v, add[i]);
+        gi[i] = v;
+    }
+}
+
+__global__ void im2col_t_kernel(const int8_t *in, int8_t *colT, int C, int H, int W, int kH, int kW, int sH, int sW,
+                                int pH, int pW, int Ho, int Wo, i64 rows, int ld) {
+    const int cols = C * kH * kW, khw = kH * kW;
+    GRID_LOOP(e, (i64)cols * rows) {
+        const int n = (int)(e / rows);
+        const i64 r = e - (i64)n * rows;
+        const i64 b = r / ((i64)Ho * Wo);
+        const int rem = (int)(r - b * Ho * Wo), oh = rem / Wo, ow = rem - oh * Wo;
+        const int ci = n / khw, kk = n - ci * khw, kh = kk / kW, kw = kk - kh * kW;
+        const int ih = oh * sH + kh - pH, iw = ow * sW + kw - pW;
+        int8_t v = 0;
+        if (ih >= 0 && ih < H && iw >= 0 && iw < W) v = in[((b * C + ci) * H + ih) * W + iw];
+        colT[(i64)n * ld + r] = v;
+    }
+}
+
+__global__ void pool_bwd_mask_kernel(const int8_t *q1, const float *gv, const float *s_pool, int H, int W, i64 n,
+                                     float *dy) {
+    const float sp = *s_pool;
+    const int Ho = H >> 1, Wo = W >> 1;
+    GRID_LOOP(i, n) {
+        const i64 bc = i / ((i64)H * W);
+        const int pix = (int)(i - bc * H * W), ih = pix / W, iw = pix - ih * W;
+        const int oh = ih >> 1, ow = iw >> 1;
+        const i64 wb = bc * H * W + (i64)(2 * oh) * W + 2 * ow;
+        const int8_t *w = q1 + wb;
+        int win = 0;
+        int8_t m = w[0];
+        if (w[1] > m) { m = w[1]; win = 1; }
+        if (w[W] > m) { m = w[W]; win = W; }
+        if (w[W + 1] > m) { m = w[W + 1]; win = W + 1; }
+        float v = 0.0f;
+        if (wb + win == i) v = fmul(gv[bc * Ho * Wo + (i64)oh * Wo + ow], sp);
+        dy[i] = q1[i] > 0 ? v : 0.0f;
+    }
+}
+
+__global__ void features_kernel(const int8_t *q, const float *s, int C, int H, int W, i64 total, float *feat) {
+    const float sc = *s;
+    GRID_LOOP(i, total) {
+        const int c = (int)(i % C), w = (int)((i / C) % W);
+        const i64 b = i / ((i64)C * W);
+        const int8_t *p = q + ((b * C + c) * H) * W + w;
+        float acc = 0.0f;
+        for (int h = 0; h < H; ++h) acc = fadd(acc, fmul((float)p[(i64)h * W], sc));
+        feat[i] = fdiv(acc, (float)H);
+    }
+}
+
+__global__ void features_bwd_kernel(const float *dfeat, const int8_t *q, const float *s, int C, int H, int W,
+                                    i64 n, float *dy) {
+    const float sc = *s;
+    GRID_LOOP(i, n) {
+        const i64 bc = i / ((i64)H * W);
+        const int pix = (int)(i - bc * H * W), w = pix % W;
+        const i64 b = bc / C;
+        const int c = (int)(bc - b * C);
+        const float v = fmul(fdiv(dfeat[(b * W + w) * C + c], (float)H), sc);
+        dy[i] = q[i] > 0 ? v : 0.0f;
+    }
+}
+
+__global__ void mask_by_q_kernel(const int8_t *q, const float *g, i64 n, float *dy) {
+    GRID_LOOP(i, n) dy[i] = q[i] > 0 ? g[i] : 0.0f;
+}
+
+}  // namespace
+
+void act_stats(const Src &s, int B, float *y_out, float *mean_out, float *var_out, float *pool_out, float *vmax,
+               cudaStream_t st) {
+    act_stats_kernel<<<B * s.C, plane_threads(s.HW), 0, st>>>(s, y_out, mean_out, var_out, pool_out, vmax);
+    TRBA_LAUNCH_CHECK();
+}
+
+void act_quant(const Src &s, int B, const float *vmax, float *s_out, int8_t *q, bool relu, cudaStream_t st) {
+    act_quant_kernel<<<B * s.C, plane_threads(s.HW), 0, st>>>(s, vmax, s_out, q, relu ? 1 : 0);
+    TRBA_LAUNCH_CHECK();
+}
+
+void se_forward(const float *pool, const float *w1, const float *w2, int B, int C, int R, float *h1, float *gate,
+                cudaStream_t st) {
+    se_forward_kernel<<<B, 128, (C + R) * sizeof(float), st>>>(pool, w1, w2, C, R, h1, gate);
+    TRBA_LAUNCH_CHECK();
+}
+
+void grad_quant_max(const float *gv, const float *s_out, i64 n, float *vmax, cudaStream_t st) {
+    grad_quant_max_kernel<<<grid_for(n), 256, 0, st>>>(gv, s_out, n, vmax);
+    TRBA_LAUNCH_CHECK();
+}
+
+void grad_quant_mask(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out, i64 n,
+                     float *s_dq_out, float *dz, cudaStream_t st) {
+    grad_quant_mask_kernel<<<grid_for(n), 256, 0, st>>>(gv, s_out, vmax, q_out, n, s_dq_out, dz);
+    TRBA_LAUNCH_CHECK();
+}
+
+void se_backward(const float *dz, const float *y2, const float *gate, const float *h1, const float *pool,
+                 const float *w1, const float *w2, int B, int C, int HW, int R, float *dpre1, float *dpre2,
+                 float *dpooled, float *dy2_full, cudaStream_t st) {
+    (void)pool;
+    se_backward_kernel<<<B, 128, (2 * C + R) * sizeof(float), st>>>(dz, y2, gate, h1, w1, w2, C, HW, R, dpre1, dpre2,
+                                                                   dpooled, dy2_full);
+    TRBA_LAUNCH_CHECK();
+}
+
+void se_weight_grads(const float *dpre1, const float *dpre2, const float *h1, const float *pool, int B, int C, int R,
+                     float *g_w1, float *g_w2, cudaStream_t st) {
+    se_wgrad_kernel<<<grid_for(2 * C * R, 128), 128, 0, st>>>(dpre1, dpre2, h1, pool, B, C, R, g_w1, g_w2);
+    TRBA_LAUNCH_CHECK();
+}
+
+void bn_bwd_sums(const float *dy, const float *x, const float *mean, const float *var, int B, int C, int HW,
+                 double *acc, cudaStream_t st) {
+    bn_bwd_sums_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, C, HW, acc);
+    TRBA_LAUNCH_CHECK();
+}
+
+void bn_dx_max(const float *dy, const float *x, const float *mean, const float *var, const float *gamma,
+               const double *acc, int B, int C, int HW, float *g_gamma, float *g_beta, float *vmax, cudaStream_t st) {
+    bn_dx_max_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, g_gamma, g_beta,
+                                                          vmax);
+    TRBA_LAUNCH_CHECK();
+}
+
+void bn_dx_quant(const float *dy, const float *x, const float *mean, const float *var, const float *gamma,
+                 const double *acc, int B, int C, int HW, const float *vmax, float *s_dx, int8_t *A, int ld,
+                 bool compat, cudaStream_t st) {
+    bn_dx_quant_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, vmax, s_dx, A,
+                                                            ld, compat ? 1 : 0);
+    TRBA_LAUNCH_CHECK();
+}
+
+void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n, float *g, cudaStream_t st) {
+    grad_accum_kernel<<<grid_for(n), 256, 0, st>>>(acc, s_dx, s_in, n, g);
+    TRBA_LAUNCH_CHECK();
+}
+
+void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B, int Cin, int H, int W, int Cout,
+           int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, const int8_t *mask_q, const float *add,
+           float *gi, cudaStream_t st) {
+    const i64 n = (i64)B * Cin * H * W;
+    dgrad_kernel<<<grid_for(n), 256, 0, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
+                                              mask_q, add, gi);
+    TRBA_LAUNCH_CHECK();
+}
+
+void im2col_t(const int8_t *in, int8_t *colT, int B, int C, int H, int W, int kh, int kw, int sh, int sw, int ph,
+              int pw, int Ho, int Wo, int ld, cudaStream_t st) {
+    const i64 rows = (i64)B * Ho * Wo;
+    im2col_t_kernel<<<grid_for((i64)C * kh * kw * rows), 256, 0, st>>>(in, colT, C, H, W, kh, kw, sh, sw, ph, pw, Ho,
+                                                                       Wo, rows, ld);
+    TRBA_LAUNCH_CHECK();
+}
+
+void pool_bwd_mask(const int8_t *q1, const float *gv, const float *s_pool, int B, int C, int H, int W, float *dy,
+                   cudaStream_t st) {
+    const i64 n = (i64)B * C * H * W;
+    pool_bwd_mask_kernel<<<grid_for(n), 256, 0, st>>>(q1, gv, s_pool, H, W, n, dy);
+    TRBA_LAUNCH_CHECK();
+}
+
+void features(const int8_t *q, const float *s, int B, int C, int H, int W, float *feat, cudaStream_t st) {
+    const i64 total = (i64)B * W * C;
+    features_kernel<<<grid_for(total), 256, 0, st>>>(q, s, C, H, W, total, feat);
+    TRBA_LAUNCH_CHECK();
+}
+
+void features_bwd(const float *dfeat, const int8_t *q, const float *s, int B, int C, int H, int W, float *dy,
+                  cudaStream_t st) {
+    const i64 n = (i64)B * C * H * W;
+    features_bwd_kernel<<<grid_for(n), 256, 0, st>>>(dfeat, q, s, C, H, W, n, dy);
+    TRBA_LAUNCH_CHECK();
+}
+
+void mask_by_q(const int8_t *q, const float *g, i64 n, float *dy, cudaStream_t st) {
+    mask_by_q_kernel<<<grid_for(n), 256, 0, st>>>(q, g, n, dy);
+    TRBA_LAUNCH_CHECK();
+}
+
+}  // namespace qat
+}  // namespace trba

@@ -1,0 +1,1186 @@
+// Device-resident TRBA INT8-QAT training step (include/trba_qat.h).
+//
+// Model: SE-ResNet QAT backbone (src/qnet.rs:1425-1758), BiLSTM stack
+// (src/rnn.rs), attention decoder (src/attn.rs), CTC head (LinearF), losses
+// and optimiser of return_main_step (later snapshot src/main.rs:2249-2413).
+// Every buffer is allocated once at creation for the largest batch; a step
+// launches kernels only (no allocation, no host synchronisation), so the
+// whole step can be enqueued back to back and, in data-parallel mode, the
+// gradient buffer is all-reduced with one NCCL call.
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm_i8.cuh"
+#include "qat_kernels.cuh"
+#include "seq_kernels.cuh"
+#include "trba_backend.h"
+#include "trba_qat.h"
+
+using namespace trba;
+
+namespace {
+
+__host__ __device__ inline int a16(int x) { return (x + 15) & ~15; }
+inline i64 a16l(i64 x) { return (x + 15) & ~15LL; }
+
+// ----------------------------------------------------------- allocation --
+struct Arena {
+    char *base = nullptr;
+    size_t cap = 0, used = 0;
+    std::vector<std::pair<size_t, size_t>> plan;  // (offset, bytes) while planning
+    bool planning = true;
+    size_t take(size_t bytes) {
+        size_t off = (used + 255) & ~size_t(255);
+        used = off + bytes;
+        return off;
+    }
+};
+
+template <typename T>
+struct Ref {  // arena-relative pointer, resolved after the single cudaMalloc
+    size_t off = 0;
+    Arena *a = nullptr;
+    T *get() const { return reinterpret_cast<T *>(a->base + off); }
+};
+
+enum Kind { K_CONV = 0, K_MAT = 1, K_VEC = 2 };
+
+struct Entry {
+    std::string name;
+    i64 off;
+    int rows, cols, kind;
+    i64 size() const { return cols ? (i64)rows * cols : rows; }
+};
+
+struct Seg {  // a parameter segment for the multi-tensor optimiser kernels
+    i64 off;
+    int n;
+    int rows, cols;
+    int aux;  // conv: index into conv tables
+};
+
+struct ConvL {
+    std::string name;
+    int cin, cout, kh, kw, sh, sw, ph, pw;
+    int H, W, Ho, Wo;
+    int K, kp;
+    i64 w_off, gamma_off, beta_off;
+    // persistent
+    Ref<int8_t> wq;          // [a16(cout), kp]
+    Ref<float> ws, wmax;     // device scalars
+    Ref<float> run_mean, run_var;
+    // forward traces
+    Ref<int8_t> col, colT;   // [a16(rows), kp] / [a16(K), a16(rows)]
+    Ref<float> x, mean, var, y;
+    Ref<int8_t> q;           // quantised output (when the conv is followed by relu_quant)
+    Ref<float> s_q;          // its scale
+    const int8_t *q_in = nullptr;  // resolved per step
+    const float *s_in = nullptr;
+    // per-step zeroed
+    Ref<double> bn_acc, bwd_acc;
+    Ref<float> ymax, dxmax, s_dx;
+    Ref<int32_t> gw;
+    // backward
+    Ref<int8_t> A;           // [a16(cout), a16(rows)]
+    bool need_y = false, need_q = false;
+    i64 rows(int B) const { return (i64)B * Ho * Wo; }
+};
+
+struct BlockL {
+    int c1, c2, ds;  // conv indices (ds = -1 if none)
+    int C, Cin, H, W, Ho, Wo, R;
+    i64 w1_off, w2_off;
+    Ref<float> pool, h1, gate, s_out, zmax, gvmax, s_dq;
+    Ref<int8_t> q_out;
+    Ref<float> dz, dy2, dy1, gin, dpre1, dpre2, dpooled;
+};
+
+struct RnnL {
+    int D, H;
+    i64 wih[2], bih[2], whh[2], bhh[2], pw, pb;
+    Ref<float> xg[2], gates[2], c[2], hprev[2], dg[2];
+    Ref<float> cat, y, dcat, dx;
+};
+
+}  // namespace
+
+struct trba_model {
+    trba_model_config cfg;
+    int B = 0;  // max batch
+    int T = 0, steps = 0, Hf = 0;
+    std::vector<Entry> manifest;
+    i64 n_params = 0;
+    std::vector<ConvL> convs;
+    std::vector<BlockL> blocks;
+    std::vector<RnnL> rnn;
+    Arena arena, zarena;  // persistent / zeroed every step
+    // parameters, gradients, Adam moments
+    Ref<float> P, G, Mm, Vv;
+    // stem
+    Ref<int8_t> qpool;
+    Ref<float> s_img;
+    Ref<float> dy_c1, dy_c0, gv_last, dy_o1, dy_o0;
+    // features and sequence head
+    Ref<float> feat, dfeat;
+    Ref<float> proj_h, tanh_tr, alpha, cell_in, agates, hs, cs, logits, dlogits, row_loss, ctc_logits, dctc;
+    Ref<float> d_out_hid, adg, ade, adprojhh, d_proj_h, d_bh;
+    Ref<double> ctc_sample_loss;
+    Ref<float> loss;  // 4 floats
+    // optimiser scratch (zeroed per step)
+    Ref<double> gsq_total;
+    Ref<double> conv_gsq;  // per conv
+    Ref<float> clip_f, mat_step, conv_step;
+    // inputs staged for the host-buffer entry point
+    Ref<int8_t> in_img;
+    Ref<int32_t> in_text, in_target, in_ctc, in_ctc_len;
+    // segment tables
+    std::vector<Seg> vec_segs, mat_segs, conv_segs;
+    Seg *d_vec = nullptr, *d_mat = nullptr, *d_conv = nullptr;
+    // conv tables for multi-conv kernels
+    struct ConvTab {
+        int8_t *wq;
+        float *ws, *wmax;
+        float *mean, *var, *run_mean, *run_var;
+        int cout, K, kp;
+    };
+    ConvTab *d_convtab = nullptr;
+    long long t = 0;
+    int last_B = 0;
+    ncclComm_t comm = nullptr;
+    int world = 1;
+    cudaEvent_t ev = nullptr;
+};
+
+namespace {
+
+// ------------------------------------------------- optimiser kernels --
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void sumsq_kernel(const float *g, i64 n, double *out) {
+    __shared__ double sm[32];
+    double s = 0.0;
+    GRID_LOOP(i, n) s += (double)g[i] * (double)g[i];
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < (blockDim.x >> 5) ? sm[threadIdx.x] : 0.0;
+        s = warp_sum_d(s);
+        if (threadIdx.x == 0) atomicAdd(out, s);
+    }
+}
+
+// src/main.rs:2382-2390: f = 5 / (norm + 1e-6) when norm > 5, else 1.
+__global__ void clip_factor_kernel(const double *gsq, int active, float *f) {
+    if (threadIdx.x == 0) {
+        float v = 1.0f;
+        if (active) {
+            const double norm = sqrt(*gsq);
+            if (norm > 5.0) v = (float)(5.0 / (norm + 1e-6));
+        }
+        *f = v;
+    }
+}
+
+// Adam on vector parameters (src/opt.rs adam_vec with the grads scaled by f:
+// the same arithmetic as launch_adam_f32 with clip = f).
+__global__ void adam_segs_kernel(const Seg *segs, float *P, const float *G, float *M, float *V, const float *f,
+                                 double lr, double wd, double b1, double b2, double eps, double bc1, double bc2) {
+    const Seg s = segs[blockIdx.y];
+    const double clip = (double)*f;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x) {
+        const i64 i = s.off + j;
+        const double gi = __dadd_rn((double)(float)__dmul_rn((double)G[i], clip), __dmul_rn(wd, (double)P[i]));
+        const float mf = (float)__dadd_rn(__dmul_rn(b1, (double)M[i]), __dmul_rn(1.0 - b1, gi));
+        const float vf = (float)__dadd_rn(__dmul_rn(b2, (double)V[i]), __dmul_rn(__dmul_rn(1.0 - b2, gi), gi));
+        M[i] = mf;
+        V[i] = vf;
+        const double mh = __ddiv_rn((double)mf, bc1), vh = __ddiv_rn((double)vf, bc2);
+        P[i] = fsub(P[i], (float)__ddiv_rn(__dmul_rn(lr, mh), __dadd_rn(__dsqrt_rn(vh), eps)));
+    }
+}
+
+// Host Muon (src/opt.rs muon_step_f32) on grads scaled by f: one CTA per
+// matrix computes ||g||^2 in f32 and the step lr*sqrt(max)*min(sqrt(min)/frob, cap).
+__global__ void muon_mat_norm_kernel(const Seg *segs, const float *G, const float *f, float lr, float cap,
+                                     float *step) {
+    __shared__ float sm[32];
+    const Seg s = segs[blockIdx.x];
+    const float fv = *f;
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < s.n; j += blockDim.x) {
+        const float g = fmul(G[s.off + j], fv);
+        acc = fadd(acc, fmul(g, g));
+    }
+    acc = warp_sum_f(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fadd(t, sm[w]);
+        const float frob = fmaxf(__fsqrt_rn(t), 1e-8f);
+        const float mn = (float)min(s.rows, s.cols), mx = (float)max(s.rows, s.cols);
+        const float scale = fminf(fdiv(__fsqrt_rn(mn), frob), cap);
+        step[blockIdx.x] = fmul(fmul(lr, __fsqrt_rn(mx)), scale);
+    }
+}
+
+__global__ void muon_mat_apply_kernel(const Seg *segs, float *P, const float *G, const float *f, const float *step,
+                                      float dec) {
+    const Seg s = segs[blockIdx.y];
+    const float fv = *f, st = step[blockIdx.y];
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x) {
+        const i64 i = s.off + j;
+        const float u = fsub(fmul(P[i], dec), fmul(st, fmul(G[i], fv)));
+        P[i] = isfinite(u) ? u : 0.0f;
+    }
+}
+
+// Device conv Muon (later snapshot cpu_backend.cpp:1197-1213 /
+// src/qnet.rs:559-573): per conv gsq = sum g^2 (f64, unscaled grads), step =
+// (float)(clip * lr sqrt(max) * min(sqrt(min)/||g||, cap)).
+__global__ void conv_gsq_kernel(const Seg *segs, const float *G, double *gsq) {
+    __shared__ double sm[32];
+    const Seg s = segs[blockIdx.y];
+    double acc = 0.0;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x) {
+        const double v = (double)G[s.off + j];
+        acc += v * v;
+    }
+    acc = warp_sum_d(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        acc = threadIdx.x < (blockDim.x >> 5) ? sm[threadIdx.x] : 0.0;
+        acc = warp_sum_d(acc);
+        if (threadIdx.x == 0) atomicAdd(gsq + blockIdx.y, acc);
+    }
+}
+
+__global__ void conv_muon_apply_kernel(const Seg *segs, float *P, const float *G, const double *gsq, const float *f,
+                                       double lr, double wd, double cap) {
+    const Seg s = segs[blockIdx.y];
+    const double frob = __dsqrt_rn(fmax(gsq[blockIdx.y], 1e-30));
+    const double mn = (double)min(s.rows, s.cols), mx = (double)max(s.rows, s.cols);
+    const double scale = fmin(__ddiv_rn(__dsqrt_rn(mn), fmax(frob, 1e-8)), cap);
+    const double lre = __dmul_rn(lr, __dsqrt_rn(mx));
+    const float step = (float)__dmul_rn(__dmul_rn((double)*f, lre), scale);
+    const float dec = (float)(1.0 - __dmul_rn(lr, wd));
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x) {
+        const i64 i = s.off + j;
+        const float u = fsub(fmul(P[i], dec), fmul(step, G[i]));
+        P[i] = isfinite(u) ? u : 0.0f;
+    }
+}
+
+// Re-quantisation of every conv (src/qnet.rs:601-624): max|w| per conv, then
+// the padded int8 operand with s = max/127 (f64; 1 if 0).
+__global__ void conv_wmax_kernel(const Seg *segs, const float *P, trba_model::ConvTab *tab) {
+    __shared__ float sm[32];
+    const Seg s = segs[blockIdx.x];
+    float m = 0.0f;
+    for (int j = threadIdx.x; j < s.n; j += blockDim.x) m = fmaxf(m, fabsf(P[s.off + j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, sm[w]);
+        *tab[s.aux].wmax = t;
+        const double mx = (double)t;
+        *tab[s.aux].ws = (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
+    }
+}
+
+__global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_model::ConvTab *tab) {
+    const Seg s = segs[blockIdx.y];
+    const trba_model::ConvTab t = tab[s.aux];
+    const double mx = (double)*t.wmax;
+    const float sc = (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
+    const i64 total = (i64)a16(t.cout) * t.kp;
+    for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (i64)gridDim.x * blockDim.x) {
+        const int r = (int)(e / t.kp), c = (int)(e - (i64)r * t.kp);
+        float v = 0.0f;
+        if (r < t.cout && c < t.K) {
+            v = (float)__ddiv_rn((double)P[s.off + (i64)r * t.K + c], (double)sc);
+            v = fminf(fmaxf(v, -127.0f), 127.0f);
+        }
+        t.wq[e] = (int8_t)roundf(v);
+    }
+}
+
+// BatchNorm running statistics (src/qnet.rs:63-68): r = 0.9 r + 0.1 batch.
+__global__ void bn_running_kernel(const trba_model::ConvTab *tab, int nconv) {
+    const trba_model::ConvTab t = tab[blockIdx.x];
+    for (int c = threadIdx.x; c < t.cout; c += blockDim.x) {
+        t.run_mean[c] = fadd(fmul(0.9f, t.run_mean[c]), fmul(0.1f, t.mean[c]));
+        t.run_var[c] = fadd(fmul(0.9f, t.run_var[c]), fmul(0.1f, t.var[c]));
+    }
+    (void)nconv;
+}
+
+__global__ void fill_f32_kernel(float *p, i64 n, float v) { GRID_LOOP(i, n) p[i] = v; }
+
+// f32 powi of Rust / LLVM (__powisf2): square and multiply.
+float powi_f32(float a, long long n) {
+    float r = 1.0f;
+    while (true) {
+        if (n & 1) r *= a;
+        n >>= 1;
+        if (!n) return r;
+        a *= a;
+    }
+}
+
+// ----------------------------------------------------------- building --
+struct Builder {
+    trba_model *m;
+    Arena *A, *Z;
+    template <typename T>
+    Ref<T> take(Arena *ar, i64 count) {
+        Ref<T> r;
+        r.a = ar;
+        r.off = ar->take((size_t)count * sizeof(T));
+        return r;
+    }
+    template <typename T>
+    Ref<T> p(i64 n) { return take<T>(A, n); }
+    template <typename T>
+    Ref<T> z(i64 n) { return take<T>(Z, n); }
+};
+
+void add_entry(trba_model *m, const std::string &name, int rows, int cols, int kind) {
+    Entry e{name, m->n_params, rows, cols, kind};
+    m->n_params += e.size();
+    m->manifest.push_back(e);
+}
+
+i64 entry_off(const trba_model *m, const std::string &name) {
+    for (auto &e : m->manifest)
+        if (e.name == name) return e.off;
+    return -1;
+}
+
+void plan(trba_model *m) {
+    const auto &c = m->cfg;
+    const int fd = c.fd;
+    const int w[6] = {fd / 8, fd / 4, fd / 2, fd / 2, fd, fd};
+    struct BS {
+        std::string name;
+        int ic, oc, s, li, bi;
+    };
+    std::vector<BS> bs = {{"layer1.0", w[1], w[2], 2, 0, 0}, {"layer2.0", w[2], w[3], 1, 1, 0},
+                          {"layer2.1", w[3], w[3], 1, 1, 1}, {"layer3.0", w[3], w[4], 2, 2, 0}};
+    for (int i = 1; i < 5; ++i) bs.push_back({"layer3." + std::to_string(i), w[4], w[4], 1, 2, i});
+    for (int i = 0; i < 3; ++i) bs.push_back({"layer4." + std::to_string(i), w[5], w[5], 1, 3, i});
+
+    auto add_conv = [&](const std::string &name, int cin, int cout, int k1, int k2, int s1, int s2, int p1, int p2,
+                        int H, int W) -> int {
+        ConvL L;
+        L.name = name;
+        L.cin = cin, L.cout = cout, L.kh = k1, L.kw = k2, L.sh = s1, L.sw = s2, L.ph = p1, L.pw = p2;
+        L.H = H, L.W = W;
+        L.Ho = (H + 2 * p1 - k1) / s1 + 1;
+        L.Wo = (W + 2 * p2 - k2) / s2 + 1;
+        L.K = cin * k1 * k2;
+        L.kp = a16(L.K);
+        m->convs.push_back(L);
+        return (int)m->convs.size() - 1;
+    };
+    int H = c.img_h, W = c.img_w;
+    add_conv("stem.0", 3, w[0], 3, 3, 1, 1, 1, 1, H, W);
+    add_conv("stem.3", w[0], w[1], 3, 3, 1, 1, 1, 1, H, W);
+    H /= 2;
+    W /= 2;
+    for (auto &b : bs) {
+        BlockL bl;
+        bl.ds = -1;
+        if (b.s != 1 || b.ic != b.oc) bl.ds = add_conv(b.name + ".downsample.0", b.ic, b.oc, 1, 1, b.s, b.s, 0, 0, H, W);
+        bl.c1 = add_conv(b.name + ".conv1", b.ic, b.oc, 3, 3, b.s, b.s, 1, 1, H, W);
+        const ConvL &c1 = m->convs[bl.c1];
+        bl.c2 = add_conv(b.name + ".conv2", b.oc, b.oc, 3, 3, 1, 1, 1, 1, c1.Ho, c1.Wo);
+        bl.C = b.oc, bl.Cin = b.ic, bl.H = H, bl.W = W, bl.Ho = c1.Ho, bl.Wo = c1.Wo, bl.R = b.oc / 16;
+        m->blocks.push_back(bl);
+        H = bl.Ho;
+        W = bl.Wo;
+    }
+    add_conv("conv_out.0", w[5], w[5], 2, 2, 2, 1, 0, 1, H, W);
+    const ConvL &o0 = m->convs.back();
+    add_conv("conv_out.3", w[5], w[5], 2, 2, 1, 1, 0, 0, o0.Ho, o0.Wo);
+    m->Hf = m->convs.back().Ho;
+    m->T = m->convs.back().Wo;
+    m->steps = c.max_len + 1;
+
+    // manifest (src/main.rs:954-1030 order)
+    for (auto &L : m->convs) {
+        add_entry(m, L.name + ".w", L.cout, L.K, K_CONV);
+        add_entry(m, L.name + ".gamma", L.cout, 0, K_VEC);
+        add_entry(m, L.name + ".beta", L.cout, 0, K_VEC);
+    }
+    for (size_t i = 0; i < bs.size(); ++i) {
+        const std::string pre = "l" + std::to_string(bs[i].li) + "b" + std::to_string(bs[i].bi) + ".se.";
+        add_entry(m, pre + "fc1.w", bs[i].oc / 16, bs[i].oc, K_MAT);
+        add_entry(m, pre + "fc2.w", bs[i].oc, bs[i].oc / 16, K_MAT);
+    }
+    const int Hh = c.hidden, V = c.classes;
+    for (int li = 0; li < c.rnn_layers; ++li) {
+        const int D = li == 0 ? fd : Hh;
+        const std::string pre = "rnn" + std::to_string(li) + ".";
+        for (const char *dn : {"f", "b"}) {
+            add_entry(m, pre + dn + ".w_ih", 4 * Hh, D, K_MAT);
+            add_entry(m, pre + dn + ".b_ih", 4 * Hh, 0, K_VEC);
+            add_entry(m, pre + dn + ".w_hh", 4 * Hh, Hh, K_MAT);
+            add_entry(m, pre + dn + ".b_hh", 4 * Hh, 0, K_VEC);
+        }
+        add_entry(m, pre + "proj.w", Hh, 2 * Hh, K_MAT);
+        add_entry(m, pre + "proj.b", Hh, 0, K_VEC);
+    }
+    add_entry(m, "attn.i2h.w", Hh, Hh, K_MAT);
+    add_entry(m, "attn.h2h.w", Hh, Hh, K_MAT);
+    add_entry(m, "attn.h2h.b", Hh, 0, K_VEC);
+    add_entry(m, "attn.score.w", 1, Hh, K_MAT);
+    add_entry(m, "attn.w_ih", 4 * Hh, Hh + V, K_MAT);
+    add_entry(m, "attn.b_ih", 4 * Hh, 0, K_VEC);
+    add_entry(m, "attn.w_hh", 4 * Hh, Hh, K_MAT);
+    add_entry(m, "attn.b_hh", 4 * Hh, 0, K_VEC);
+    add_entry(m, "attn.gen.w", V, Hh, K_MAT);
+    add_entry(m, "attn.gen.b", V, 0, K_VEC);
+    add_entry(m, "ctc.w", V, Hh, K_MAT);
+    add_entry(m, "ctc.b", V, 0, K_VEC);
+
+    for (auto &L : m->convs) {
+        L.w_off = entry_off(m, L.name + ".w");
+        L.gamma_off = entry_off(m, L.name + ".gamma");
+        L.beta_off = entry_off(m, L.name + ".beta");
+    }
+    for (size_t i = 0; i < bs.size(); ++i) {
+        const std::string pre = "l" + std::to_string(bs[i].li) + "b" + std::to_string(bs[i].bi) + ".se.";
+        m->blocks[i].w1_off = entry_off(m, pre + "fc1.w");
+        m->blocks[i].w2_off = entry_off(m, pre + "fc2.w");
+    }
+    for (int li = 0; li < c.rnn_layers; ++li) {
+        RnnL r;
+        r.D = li == 0 ? fd : Hh;
+        r.H = Hh;
+        const std::string pre = "rnn" + std::to_string(li) + ".";
+        const char *dn[2] = {"f", "b"};
+        for (int d = 0; d < 2; ++d) {
+            r.wih[d] = entry_off(m, pre + dn[d] + ".w_ih");
+            r.bih[d] = entry_off(m, pre + dn[d] + ".b_ih");
+            r.whh[d] = entry_off(m, pre + dn[d] + ".w_hh");
+            r.bhh[d] = entry_off(m, pre + dn[d] + ".b_hh");
+        }
+        r.pw = entry_off(m, pre + "proj.w");
+        r.pb = entry_off(m, pre + "proj.b");
+        m->rnn.push_back(r);
+    }
+    for (auto &e : m->manifest) {
+        Seg s{e.off, (int)e.size(), e.rows, e.cols, 0};
+        if (e.kind == K_VEC) m->vec_segs.push_back(s);
+        else if (e.kind == K_MAT) m->mat_segs.push_back(s);
+    }
+    for (size_t i = 0; i < m->convs.size(); ++i) {
+        const ConvL &L = m->convs[i];
+        m->conv_segs.push_back(Seg{L.w_off, L.cout * L.K, L.cout, L.K, (int)i});
+    }
+}
+
+void allocate(trba_model *m) {
+    const auto &c = m->cfg;
+    const int B = m->B;
+    Builder b{m, &m->arena, &m->zarena};
+    m->P = b.p<float>(m->n_params);
+    m->G = b.p<float>(m->n_params);
+    m->Mm = b.p<float>(m->n_params);
+    m->Vv = b.p<float>(m->n_params);
+    m->s_img = b.p<float>(1);
+    const bool correct = c.wgrad_mode == 1;
+    for (size_t i = 0; i < m->convs.size(); ++i) {
+        ConvL &L = m->convs[i];
+        const i64 rows = L.rows(B), rp = a16l(rows), n = (i64)B * L.cout * L.Ho * L.Wo;
+        L.wq = b.p<int8_t>((i64)a16(L.cout) * L.kp);
+        L.ws = b.p<float>(1);
+        L.wmax = b.p<float>(1);
+        L.run_mean = b.p<float>(L.cout);
+        L.run_var = b.p<float>(L.cout);
+        L.col = b.p<int8_t>(rp * L.kp);
+        if (correct) L.colT = b.p<int8_t>((i64)a16(L.K) * rp);
+        L.x = b.p<float>(n);
+        L.mean = b.p<float>(L.cout);
+        L.var = b.p<float>(L.cout);
+        L.A = b.p<int8_t>((i64)a16(L.cout) * rp);
+        L.bn_acc = b.z<double>(2 * L.cout);
+        L.bwd_acc = b.z<double>(2 * L.cout);
+        L.ymax = b.z<float>(1);
+        L.dxmax = b.z<float>(1);
+        L.s_dx = b.z<float>(1);
+        L.gw = b.z<int32_t>((i64)L.cout * L.K);
+    }
+    // which convs store y / produce a quantised output
+    for (auto &bl : m->blocks) {
+        m->convs[bl.c2].need_y = true;
+        if (bl.ds >= 0) m->convs[bl.ds].need_y = true;
+        m->convs[bl.c1].need_q = true;
+    }
+    const int nc = (int)m->convs.size();
+    for (int i : {0, 1, nc - 2, nc - 1}) m->convs[i].need_q = true;
+    for (auto &L : m->convs) {
+        const i64 n = (i64)B * L.cout * L.Ho * L.Wo;
+        if (L.need_y) L.y = b.p<float>(n);
+        if (L.need_q) {
+            L.q = b.p<int8_t>(n);
+            L.s_q = b.p<float>(1);
+        }
+    }
+    const ConvL &s1 = m->convs[1];
+    m->qpool = b.p<int8_t>((i64)B * s1.cout * (s1.Ho / 2) * (s1.Wo / 2));
+    for (auto &bl : m->blocks) {
+        const i64 n = (i64)B * bl.C * bl.Ho * bl.Wo, nin = (i64)B * bl.Cin * bl.H * bl.W;
+        bl.pool = b.p<float>((i64)B * bl.C);
+        bl.h1 = b.p<float>((i64)B * bl.R);
+        bl.gate = b.p<float>((i64)B * bl.C);
+        bl.s_out = b.p<float>(1);
+        bl.s_dq = b.p<float>(1);
+        bl.q_out = b.p<int8_t>(n);
+        bl.zmax = b.z<float>(1);
+        bl.gvmax = b.z<float>(1);
+        bl.dz = b.p<float>(n);
+        bl.dy2 = b.p<float>(n);
+        bl.dy1 = b.p<float>(n);
+        bl.gin = b.p<float>(nin);
+        bl.dpre1 = b.p<float>((i64)B * bl.R);
+        bl.dpre2 = b.p<float>((i64)B * bl.C);
+        bl.dpooled = b.p<float>((i64)B * bl.C);
+    }
+    const ConvL &o0 = m->convs[nc - 2], &o1 = m->convs[nc - 1];
+    m->dy_o1 = b.p<float>((i64)B * o1.cout * o1.Ho * o1.Wo);
+    m->dy_o0 = b.p<float>((i64)B * o0.cout * o0.Ho * o0.Wo);
+    m->gv_last = b.p<float>((i64)B * o0.cin * o0.H * o0.W);
+    m->dy_c1 = b.p<float>((i64)B * s1.cout * s1.Ho * s1.Wo);
+    m->dy_c0 = b.p<float>((i64)B * m->convs[0].cout * m->convs[0].Ho * m->convs[0].Wo);
+    const int T = m->T, Hh = c.hidden, V = c.classes, S = m->steps, fd = c.fd;
+    m->feat = b.p<float>((i64)B * T * fd);
+    m->dfeat = b.p<float>((i64)B * T * fd);
+    for (auto &r : m->rnn) {
+        for (int d = 0; d < 2; ++d) {
+            r.xg[d] = b.p<float>((i64)B * T * 4 * Hh);
+            r.gates[d] = b.p<float>((i64)B * T * 4 * Hh);
+            r.c[d] = b.p<float>((i64)B * T * Hh);
+            r.hprev[d] = b.p<float>((i64)B * T * Hh);
+            r.dg[d] = b.p<float>((i64)B * T * 4 * Hh);
+        }
+        r.cat = b.p<float>((i64)B * T * 2 * Hh);
+        r.dcat = b.p<float>((i64)B * T * 2 * Hh);
+        r.y = b.p<float>((i64)B * T * Hh);
+        r.dx = b.p<float>((i64)B * T * r.D);
+    }
+    m->proj_h = b.p<float>((i64)B * T * Hh);
+    m->tanh_tr = b.p<float>((i64)S * B * T * Hh);
+    m->alpha = b.p<float>((i64)S * B * T);
+    m->cell_in = b.p<float>((i64)S * B * (Hh + V));
+    m->agates = b.p<float>((i64)S * B * 4 * Hh);
+    m->hs = b.p<float>((i64)S * B * Hh);
+    m->cs = b.p<float>((i64)S * B * Hh);
+    m->logits = b.p<float>((i64)S * B * V);
+    m->dlogits = b.p<float>((i64)S * B * V);
+    m->row_loss = b.p<float>((i64)S * B);
+    m->ctc_logits = b.p<float>((i64)B * T * V);
+    m->dctc = b.p<float>((i64)B * T * V);
+    m->d_out_hid = b.p<float>((i64)S * B * Hh);
+    m->adg = b.p<float>((i64)S * B * 4 * Hh);
+    m->ade = b.p<float>((i64)S * B * T);
+    m->adprojhh = b.p<float>((i64)S * B * Hh);
+    m->d_proj_h = b.p<float>((i64)B * T * Hh);
+    m->d_bh = b.p<float>((i64)B * T * Hh);
+    m->ctc_sample_loss = b.p<double>(B);
+    m->loss = b.p<float>(4);
+    m->gsq_total = b.z<double>(1);
+    m->conv_gsq = b.z<double>((i64)m->convs.size());
+    m->clip_f = b.p<float>(1);
+    m->mat_step = b.p<float>((i64)m->mat_segs.size());
+    m->conv_step = b.p<float>((i64)m->convs.size());
+    m->in_img = b.p<int8_t>((i64)B * 3 * c.img_h * c.img_w);
+    m->in_text = b.p<int32_t>((i64)B * S);
+    m->in_target = b.p<int32_t>((i64)B * S);
+    m->in_ctc = b.p<int32_t>((i64)B * S);
+    m->in_ctc_len = b.p<int32_t>(B);
+}
+
+// ------------------------------------------------------------ the step --
+struct Ctx {
+    trba_model *m;
+    cudaStream_t st;
+    int B;
+    float *P, *G;
+};
+
+void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
+    const int B = c.B;
+    const i64 rows = L.rows(B);
+    L.q_in = q_in;
+    L.s_in = s_in;
+    launch_im2col_pad(q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo, L.kp,
+                      c.st);
+    if (!gemm_i8_conv_f32(L.col.get(), L.kp, L.wq.get(), L.kp, (int)rows, L.cout, L.K, L.x.get(), s_in, L.ws.get(),
+                          L.bn_acc.get(), L.Ho * L.Wo, c.st))
+        report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
+    if (c.m->cfg.wgrad_mode == 1)
+        qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
+                      (int)a16l(rows), c.st);
+}
+
+qat::Src bn_src(Ctx &c, ConvL &L) {
+    qat::Src s{};
+    s.kind = qat::SRC_BN;
+    s.x = L.x.get();
+    s.bn_acc = L.bn_acc.get();
+    s.gamma = c.P + L.gamma_off;
+    s.beta = c.P + L.beta_off;
+    s.C = L.cout;
+    s.HW = L.Ho * L.Wo;
+    s.count = (i64)c.B * L.Ho * L.Wo;
+    return s;
+}
+
+// conv + BN + (ReLU-)quantise: the reference's ConvQat::forward followed by
+// relu_quant_owned (src/qnet.rs:788-916, 1102-1112).
+void conv_bn_quant(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
+    conv_fwd(c, L, q_in, s_in);
+    qat::Src s = bn_src(c, L);
+    qat::act_stats(s, c.B, nullptr, L.mean.get(), L.var.get(), nullptr, L.ymax.get(), c.st);
+    qat::act_quant(s, c.B, L.ymax.get(), L.s_q.get(), L.q.get(), true, c.st);
+}
+
+// ConvQat::backward (src/qnet.rs:918-1083).  gi: input gradient (or null).
+void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const float *add, float *gi) {
+    const int B = c.B, HW = L.Ho * L.Wo;
+    const i64 rows = L.rows(B), rp = a16l(rows);
+    const bool compat = c.m->cfg.wgrad_mode == 0;
+    qat::bn_bwd_sums(dy, L.x.get(), L.mean.get(), L.var.get(), B, L.cout, HW, L.bwd_acc.get(), c.st);
+    qat::bn_dx_max(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
+                   c.G + L.gamma_off, c.G + L.beta_off, L.dxmax.get(), c.st);
+    if (compat && (rows & 15)) TRBA_CHECK(cudaMemsetAsync(L.A.get(), 0, (size_t)a16(L.cout) * rp, c.st));
+    qat::bn_dx_quant(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
+                     L.dxmax.get(), L.s_dx.get(), L.A.get(), compat ? (int)rows : (int)rp, compat, c.st);
+    const int splits = splitk_for(L.cout, L.K, (int)rows);
+    const int8_t *Bop = compat ? L.col.get() : L.colT.get();
+    if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits, c.st))
+        report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
+    qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, c.st);
+    if (gi)
+        qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
+                   L.Ho, L.Wo, mask_q, add, gi, c.st);
+}
+
+void cnn_forward(Ctx &c, const int8_t *img) {
+    trba_model *m = c.m;
+    auto &cv = m->convs;
+    conv_bn_quant(c, cv[0], img, m->s_img.get());
+    conv_bn_quant(c, cv[1], cv[0].q.get(), cv[0].s_q.get());
+    launch_maxpool2x2_forward_i8(cv[1].q.get(), m->qpool.get(), c.B, cv[1].cout, cv[1].Ho, cv[1].Wo, c.st);
+    const int8_t *q = m->qpool.get();
+    const float *s = cv[1].s_q.get();
+    for (auto &bl : m->blocks) {
+        ConvL &c1 = cv[bl.c1], &c2 = cv[bl.c2];
+        if (bl.ds >= 0) {
+            ConvL &ds = cv[bl.ds];
+            conv_fwd(c, ds, q, s);
+            qat::act_stats(bn_src(c, ds), c.B, ds.y.get(), ds.mean.get(), ds.var.get(), nullptr, nullptr, c.st);
+        }
+        conv_bn_quant(c, c1, q, s);
+        conv_fwd(c, c2, c1.q.get(), c1.s_q.get());
+        qat::act_stats(bn_src(c, c2), c.B, c2.y.get(), c2.mean.get(), c2.var.get(), bl.pool.get(), nullptr, c.st);
+        qat::se_forward(bl.pool.get(), c.P + bl.w1_off, c.P + bl.w2_off, c.B, bl.C, bl.R, bl.h1.get(), bl.gate.get(),
+                        c.st);
+        qat::Src z{};
+        z.kind = bl.ds >= 0 ? qat::SRC_SE_RES_F : qat::SRC_SE_RES_Q;
+        z.x = c2.y.get();
+        z.gate = bl.gate.get();
+        z.res_f = bl.ds >= 0 ? cv[bl.ds].y.get() : nullptr;
+        z.res_q = q;
+        z.res_s = s;
+        z.C = bl.C;
+        z.HW = bl.Ho * bl.Wo;
+        qat::act_stats(z, c.B, nullptr, nullptr, nullptr, nullptr, bl.zmax.get(), c.st);
+        qat::act_quant(z, c.B, bl.zmax.get(), bl.s_out.get(), bl.q_out.get(), true, c.st);
+        q = bl.q_out.get();
+        s = bl.s_out.get();
+    }
+    const int nc = (int)cv.size();
+    conv_bn_quant(c, cv[nc - 2], q, s);
+    conv_bn_quant(c, cv[nc - 1], cv[nc - 2].q.get(), cv[nc - 2].s_q.get());
+    const ConvL &o1 = cv[nc - 1];
+    qat::features(o1.q.get(), o1.s_q.get(), c.B, o1.cout, o1.Ho, o1.Wo, m->feat.get(), c.st);
+    bn_running_kernel<<<nc, 128, 0, c.st>>>(m->d_convtab, nc);
+    TRBA_LAUNCH_CHECK();
+}
+
+void cnn_backward(Ctx &c) {
+    trba_model *m = c.m;
+    auto &cv = m->convs;
+    const int nc = (int)cv.size();
+    ConvL &o0 = cv[nc - 2], &o1 = cv[nc - 1];
+    qat::features_bwd(m->dfeat.get(), o1.q.get(), o1.s_q.get(), c.B, o1.cout, o1.Ho, o1.Wo, m->dy_o1.get(), c.st);
+    conv_bwd(c, o1, m->dy_o1.get(), o0.q.get(), nullptr, m->dy_o0.get());
+    conv_bwd(c, o0, m->dy_o0.get(), nullptr, nullptr, m->gv_last.get());
+    const float *gv = m->gv_last.get();
+    for (int bi = (int)m->blocks.size() - 1; bi >= 0; --bi) {
+        BlockL &bl = m->blocks[bi];
+        ConvL &c1 = cv[bl.c1], &c2 = cv[bl.c2];
+        const i64 n = (i64)c.B * bl.C * bl.Ho * bl.Wo;
+        qat::grad_quant_max(gv, bl.s_out.get(), n, bl.gvmax.get(), c.st);
+        qat::grad_quant_mask(gv, bl.s_out.get(), bl.gvmax.get(), bl.q_out.get(), n, bl.s_dq.get(), bl.dz.get(), c.st);
+        qat::se_backward(bl.dz.get(), c2.y.get(), bl.gate.get(), bl.h1.get(), bl.pool.get(), c.P + bl.w1_off,
+                         c.P + bl.w2_off, c.B, bl.C, bl.Ho * bl.Wo, bl.R, bl.dpre1.get(), bl.dpre2.get(),
+                         bl.dpooled.get(), bl.dy2.get(), c.st);
+        qat::se_weight_grads(bl.dpre1.get(), bl.dpre2.get(), bl.h1.get(), bl.pool.get(), c.B, bl.C, bl.R,
+                             c.G + bl.w1_off, c.G + bl.w2_off, c.st);
+        conv_bwd(c, c2, bl.dy2.get(), c1.q.get(), nullptr, bl.dy1.get());
+        if (bl.ds >= 0) {
+            conv_bwd(c, c1, bl.dy1.get(), nullptr, nullptr, bl.gin.get());
+            // total = gi_in + dx_ds (src/qnet.rs:1345-1349)
+            conv_bwd(c, cv[bl.ds], bl.dz.get(), nullptr, bl.gin.get(), bl.gin.get());
+        } else {
+            conv_bwd(c, c1, bl.dy1.get(), nullptr, bl.dz.get(), bl.gin.get());
+        }
+        gv = bl.gin.get();
+    }
+    qat::pool_bwd_mask(cv[1].q.get(), gv, cv[1].s_q.get(), c.B, cv[1].cout, cv[1].Ho, cv[1].Wo, m->dy_c1.get(), c.st);
+    conv_bwd(c, cv[1], m->dy_c1.get(), cv[0].q.get(), nullptr, m->dy_c0.get());
+    conv_bwd(c, cv[0], m->dy_c0.get(), nullptr, nullptr, nullptr);
+}
+
+seq::Gemm gemm(int M, int N, int K, const float *A, i64 sam, i64 sak, const float *Bm, i64 sbk, i64 sbn, float *C,
+               i64 ldc, float beta = 0.0f, const float *bias = nullptr) {
+    seq::Gemm g;
+    g.M = M, g.N = N, g.K = K;
+    g.A = A, g.sam = sam, g.sak = sak;
+    g.B = Bm, g.sbk = sbk, g.sbn = sbn;
+    g.C = C, g.ldc = ldc;
+    g.beta = beta;
+    g.bias = bias;
+    return g;
+}
+
+void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const int32_t *ctc_tgt,
+                  const int32_t *ctc_len) {
+    trba_model *m = c.m;
+    const auto &cf = m->cfg;
+    const int B = c.B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps;
+    const float *x = m->feat.get();
+    for (auto &r : m->rnn) {  // BiLstmLayer::forward (src/rnn.rs:167-174)
+        for (int d = 0; d < 2; ++d) {
+            seq::sgemm(gemm(B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
+            seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
+                          r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
+        }
+        seq::sgemm(gemm(B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, 0.0f, c.P + r.pb),
+                   c.st);
+        x = r.y.get();
+    }
+    const float *enc = x;  // [B, T, H]
+    const i64 oi2h = entry_off(m, "attn.i2h.w");
+    seq::sgemm(gemm(B * T, H, H, enc, H, 1, c.P + oi2h, 1, H, m->proj_h.get(), H), c.st);
+    seq::AttnFwd a{};
+    a.bh = enc;
+    a.proj_h = m->proj_h.get();
+    a.text_in = text_in;
+    a.h2h_w = c.P + entry_off(m, "attn.h2h.w");
+    a.h2h_b = c.P + entry_off(m, "attn.h2h.b");
+    a.score_w = c.P + entry_off(m, "attn.score.w");
+    a.w_ih = c.P + entry_off(m, "attn.w_ih");
+    a.b_ih = c.P + entry_off(m, "attn.b_ih");
+    a.w_hh = c.P + entry_off(m, "attn.w_hh");
+    a.b_hh = c.P + entry_off(m, "attn.b_hh");
+    a.B = B, a.T = T, a.H = H, a.V = V, a.steps = S;
+    a.tanh_tr = m->tanh_tr.get();
+    a.alpha = m->alpha.get();
+    a.cell_in = m->cell_in.get();
+    a.gates = m->agates.get();
+    a.hs = m->hs.get();
+    a.cs = m->cs.get();
+    seq::attn_fwd(a, c.st);
+    seq::sgemm(gemm(S * B, V, H, m->hs.get(), H, 1, c.P + entry_off(m, "attn.gen.w"), 1, H, m->logits.get(), V, 0.0f,
+                    c.P + entry_off(m, "attn.gen.b")),
+               c.st);
+    seq::sgemm(gemm(B * T, V, H, enc, H, 1, c.P + entry_off(m, "ctc.w"), 1, H, m->ctc_logits.get(), V, 0.0f,
+                    c.P + entry_off(m, "ctc.b")),
+               c.st);
+    seq::ce_rows(m->logits.get(), target, B, S, V, cf.pad, m->dlogits.get(), m->row_loss.get(), c.st);
+    seq::ctc(m->ctc_logits.get(), ctc_tgt, ctc_len, S, B, T, V, cf.ctc_weight, m->dctc.get(),
+             m->ctc_sample_loss.get(), c.st);
+    seq::loss_finalize(m->row_loss.get(), target, B, S, cf.pad, m->ctc_sample_loss.get(), ctc_len, T, cf.ctc_weight,
+                       m->dlogits.get(), V, m->loss.get(), c.st);
+}
+
+void head_backward(Ctx &c) {
+    trba_model *m = c.m;
+    const auto &cf = m->cfg;
+    const int B = c.B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps, R = S * B;
+    const float *enc = m->rnn.back().y.get();
+    const i64 ogw = entry_off(m, "attn.gen.w"), ogb = entry_off(m, "attn.gen.b");
+    // generator (src/attn.rs:274-284)
+    seq::sgemm(gemm(V, H, R, m->dlogits.get(), 1, V, m->hs.get(), H, 1, c.G + ogw, H, 1.0f), c.st);
+    seq::col_sums(m->dlogits.get(), R, V, V, c.G + ogb, true, c.st);
+    seq::sgemm(gemm(R, H, V, m->dlogits.get(), V, 1, c.P + ogw, H, 1, m->d_out_hid.get(), H), c.st);
+    seq::AttnBwd a{};
+    a.d_out_hid = m->d_out_hid.get();
+    a.bh = enc;
+    a.tanh_tr = m->tanh_tr.get();
+    a.alpha = m->alpha.get();
+    a.gates = m->agates.get();
+    a.cs = m->cs.get();
+    a.score_w = c.P + entry_off(m, "attn.score.w");
+    a.w_ih = c.P + entry_off(m, "attn.w_ih");
+    a.w_hh = c.P + entry_off(m, "attn.w_hh");
+    a.h2h_w = c.P + entry_off(m, "attn.h2h.w");
+    a.B = B, a.T = T, a.H = H, a.V = V, a.steps = S;
+    a.dgates = m->adg.get();
+    a.de = m->ade.get();
+    a.dprojhh = m->adprojhh.get();
+    a.d_proj_h = m->d_proj_h.get();
+    a.d_bh = m->d_bh.get();
+    seq::attn_bwd(a, c.st);
+    const int CV = H + V;
+    float *dg = m->adg.get();
+    seq::sgemm(gemm(4 * H, CV, R, dg, 1, 4 * H, m->cell_in.get(), CV, 1, c.G + entry_off(m, "attn.w_ih"), CV, 1.0f),
+               c.st);
+    seq::col_sums(dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_ih"), true, c.st);
+    seq::col_sums(dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_hh"), true, c.st);
+    // w_hh and h2h: h_prev of step st is hs of st-1 (zero at st = 0)
+    seq::sgemm(gemm(4 * H, H, R - B, dg + (i64)B * 4 * H, 1, 4 * H, m->hs.get(), H, 1,
+                    c.G + entry_off(m, "attn.w_hh"), H, 1.0f),
+               c.st);
+    seq::sgemm(gemm(H, H, R - B, m->adprojhh.get() + (i64)B * H, 1, H, m->hs.get(), H, 1,
+                    c.G + entry_off(m, "attn.h2h.w"), H, 1.0f),
+               c.st);
+    seq::col_sums(m->adprojhh.get(), R, H, H, c.G + entry_off(m, "attn.h2h.b"), true, c.st);
+    seq::sgemm(gemm(1, H, R * T, m->ade.get(), 0, 1, m->tanh_tr.get(), H, 1, c.G + entry_off(m, "attn.score.w"), H,
+                    1.0f),
+               c.st);
+    const i64 oi2h = entry_off(m, "attn.i2h.w");
+    seq::sgemm(gemm(H, H, B * T, m->d_proj_h.get(), 1, H, enc, H, 1, c.G + oi2h, H, 1.0f), c.st);
+    seq::sgemm(gemm(B * T, H, H, m->d_proj_h.get(), H, 1, c.P + oi2h, H, 1, m->d_bh.get(), H, 1.0f), c.st);
+    // CTC head (src/main.rs:2344): LinearF backward
+    const i64 ocw = entry_off(m, "ctc.w"), ocb = entry_off(m, "ctc.b");
+    seq::sgemm(gemm(V, H, B * T, m->dctc.get(), 1, V, enc, H, 1, c.G + ocw, H, 1.0f), c.st);
+    seq::col_sums(m->dctc.get(), B * T, V, V, c.G + ocb, true, c.st);
+    seq::sgemm(gemm(B * T, H, V, m->dctc.get(), V, 1, c.P + ocw, H, 1, m->d_bh.get(), H, 1.0f), c.st);
+    // BiLSTM backward, top layer first (src/rnn.rs:176-198)
+    const float *dy = m->d_bh.get();
+    for (int li = (int)m->rnn.size() - 1; li >= 0; --li) {
+        RnnL &r = m->rnn[li];
+        const float *xin = li == 0 ? m->feat.get() : m->rnn[li - 1].y.get();
+        seq::sgemm(gemm(H, 2 * H, B * T, dy, 1, H, r.cat.get(), 2 * H, 1, c.G + r.pw, 2 * H, 1.0f), c.st);
+        seq::col_sums(dy, B * T, H, H, c.G + r.pb, true, c.st);
+        seq::sgemm(gemm(B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
+        float *dxout = li == 0 ? m->dfeat.get() : r.dx.get();
+        for (int d = 0; d < 2; ++d) {
+            seq::lstm_bwd(r.dcat.get(), r.gates[d].get(), r.c[d].get(), c.P + r.whh[d], B, T, H, d, d, r.dg[d].get(),
+                          c.st);
+            const float *g = r.dg[d].get();
+            seq::sgemm(gemm(4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, 1.0f), c.st);
+            seq::sgemm(gemm(4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, 1.0f), c.st);
+            seq::col_sums(g, B * T, 4 * H, 4 * H, c.G + r.bih[d], true, c.st);
+            seq::col_sums(g, B * T, 4 * H, 4 * H, c.G + r.bhh[d], true, c.st);
+            seq::sgemm(gemm(B * T, r.D, 4 * H, g, 4 * H, 1, c.P + r.wih[d], r.D, 1, dxout, r.D, d ? 1.0f : 0.0f),
+                       c.st);
+        }
+        dy = dxout;
+    }
+}
+
+void optimizer(trba_model *m, cudaStream_t st) {
+    const auto &cf = m->cfg;
+    float *P = m->P.get(), *G = m->G.get();
+    sumsq_kernel<<<grid_for(m->n_params), 256, 0, st>>>(G, m->n_params, m->gsq_total.get());
+    clip_factor_kernel<<<1, 32, 0, st>>>(m->gsq_total.get(), m->t < cf.clip_warmup ? 1 : 0, m->clip_f.get());
+    m->t += 1;
+    const double bc1 = 1.0 - (double)powi_f32(0.9f, m->t), bc2 = 1.0 - (double)powi_f32(0.999f, m->t);
+    const double lr = (double)cf.lr, wd = (double)cf.weight_decay;
+    const int nv = (int)m->vec_segs.size(), nm = (int)m->mat_segs.size(), ncv = (int)m->conv_segs.size();
+    adam_segs_kernel<<<dim3(4, nv), 256, 0, st>>>(m->d_vec, P, G, m->Mm.get(), m->Vv.get(), m->clip_f.get(), lr, wd,
+                                                  (double)0.9f, (double)0.999f, (double)1e-8f, bc1, bc2);
+    muon_mat_norm_kernel<<<nm, 256, 0, st>>>(m->d_mat, G, m->clip_f.get(), cf.lr, cf.muon_cap, m->mat_step.get());
+    muon_mat_apply_kernel<<<dim3(8, nm), 256, 0, st>>>(m->d_mat, P, G, m->clip_f.get(), m->mat_step.get(),
+                                                       1.0f - cf.lr * cf.weight_decay);
+    conv_gsq_kernel<<<dim3(8, ncv), 256, 0, st>>>(m->d_conv, G, m->conv_gsq.get());
+    conv_muon_apply_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, G, m->conv_gsq.get(), m->clip_f.get(), lr, wd,
+                                                          (double)cf.muon_cap);
+    conv_wmax_kernel<<<ncv, 256, 0, st>>>(m->d_conv, P, m->d_convtab);
+    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->d_convtab);
+    TRBA_LAUNCH_CHECK();
+}
+
+void requantize(trba_model *m, cudaStream_t st) {
+    const int ncv = (int)m->conv_segs.size();
+    conv_wmax_kernel<<<ncv, 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab);
+    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab);
+    TRBA_LAUNCH_CHECK();
+}
+
+template <typename T>
+T *upload_table(const std::vector<T> &v) {
+    T *d = nullptr;
+    if (v.empty()) return nullptr;
+    TRBA_CHECK(cudaMalloc(&d, sizeof(T) * v.size()));
+    TRBA_CHECK(cudaMemcpy(d, v.data(), sizeof(T) * v.size(), cudaMemcpyHostToDevice));
+    return d;
+}
+
+int cuda_status() {
+    const int e = trba_last_error();
+    return e > 0 ? e : (e < 0 ? -e : 0);
+}
+
+}  // namespace
+
+extern "C" {
+
+void trba_model_default_config(trba_model_config *c) {
+    std::memset(c, 0, sizeof(*c));
+    c->fd = 128;
+    c->hidden = 64;
+    c->classes = 130;
+    c->img_h = 32;
+    c->img_w = 160;
+    c->max_len = 20;
+    c->rnn_layers = 2;
+    c->batch = 48;
+    c->sos = 1;
+    c->eos = 2;
+    c->pad = 0;
+    c->lr = 5.107e-4f;
+    c->weight_decay = 1.9548e-5f;
+    c->ctc_weight = 0.03f;
+    c->muon_cap = 10.0f;
+    c->clip_warmup = 500;
+    c->wgrad_mode = 0;
+}
+
+trba_model *trba_model_create(const trba_model_config *cfg) {
+    if (!cfg || cfg->fd < 16 || cfg->fd % 16 || cfg->fd > 512 || cfg->batch <= 0 || cfg->hidden <= 0 ||
+        cfg->hidden > 128 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
+        (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0) {
+        report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
+        return nullptr;
+    }
+    trba_model *m = new trba_model();
+    m->cfg = *cfg;
+    m->B = cfg->batch;
+    plan(m);
+    if (m->T <= 0 || m->Hf <= 0) {
+        report_error(__FILE__, __LINE__, "trba_model_create: image too small for the backbone", -1);
+        delete m;
+        return nullptr;
+    }
+    allocate(m);
+    TRBA_CHECK(cudaMalloc(&m->arena.base, m->arena.used));
+    TRBA_CHECK(cudaMalloc(&m->zarena.base, m->zarena.used));
+    TRBA_CHECK(cudaMemset(m->arena.base, 0, m->arena.used));
+    TRBA_CHECK(cudaMemset(m->zarena.base, 0, m->zarena.used));
+    const float s_img = 1.0f / 127.0f;  // src/main.rs:1997
+    TRBA_CHECK(cudaMemcpy(m->s_img.get(), &s_img, 4, cudaMemcpyHostToDevice));
+    std::vector<trba_model::ConvTab> tab;
+    for (auto &L : m->convs) {
+        tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
+                       L.run_var.get(), L.cout, L.K, L.kp});
+        fill_f32_kernel<<<1, 128>>>(L.run_var.get(), L.cout, 1.0f);
+    }
+    m->d_convtab = upload_table(tab);
+    m->d_vec = upload_table(m->vec_segs);
+    m->d_mat = upload_table(m->mat_segs);
+    m->d_conv = upload_table(m->conv_segs);
+    TRBA_CHECK(cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming));
+    TRBA_CHECK(cudaDeviceSynchronize());
+    return m;
+}
+
+void trba_model_destroy(trba_model *m) {
+    if (!m) return;
+    if (m->comm) ncclCommDestroy(m->comm);
+    cudaFree(m->arena.base);
+    cudaFree(m->zarena.base);
+    cudaFree(m->d_convtab);
+    cudaFree(m->d_vec);
+    cudaFree(m->d_mat);
+    cudaFree(m->d_conv);
+    if (m->ev) cudaEventDestroy(m->ev);
+    delete m;
+}
+
+long long trba_model_param_count(const trba_model *m) { return m ? m->n_params : -1; }
+int trba_model_param_entries(const trba_model *m) { return m ? (int)m->manifest.size() : -1; }
+
+int trba_model_param_entry(const trba_model *m, int i, char *name, int name_cap, long long *offset, int *rows,
+                           int *cols, int *kind) {
+    if (!m || i < 0 || i >= (int)m->manifest.size()) return -1;
+    const Entry &e = m->manifest[i];
+    if (name && name_cap > 0) {
+        std::strncpy(name, e.name.c_str(), name_cap - 1);
+        name[name_cap - 1] = 0;
+    }
+    if (offset) *offset = e.off;
+    if (rows) *rows = e.rows;
+    if (cols) *cols = e.cols;
+    if (kind) *kind = e.kind;
+    return 0;
+}
+
+int trba_model_set_params(trba_model *m, const float *host, long long n) {
+    if (!m || !host || n != m->n_params) return -1;
+    TRBA_CHECK(cudaMemcpy(m->P.get(), host, n * 4, cudaMemcpyHostToDevice));
+    TRBA_CHECK(cudaMemset(m->Mm.get(), 0, n * 4));
+    TRBA_CHECK(cudaMemset(m->Vv.get(), 0, n * 4));
+    m->t = 0;
+    requantize(m, 0);
+    TRBA_CHECK(cudaDeviceSynchronize());
+    return cuda_status();
+}
+
+int trba_model_get_params(trba_model *m, float *host, long long n) {
+    if (!m || !host || n != m->n_params) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    TRBA_CHECK(cudaMemcpy(host, m->P.get(), n * 4, cudaMemcpyDeviceToHost));
+    return cuda_status();
+}
+
+int trba_model_get_grads(trba_model *m, float *host, long long n) {
+    if (!m || !host || n != m->n_params) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    TRBA_CHECK(cudaMemcpy(host, m->G.get(), n * 4, cudaMemcpyDeviceToHost));
+    return cuda_status();
+}
+
+float *trba_model_grad_buffer(trba_model *m) { return m ? m->G.get() : nullptr; }
+const float *trba_model_loss_dev(const trba_model *m) { return m ? m->loss.get() : nullptr; }
+long long trba_model_step_count(const trba_model *m) { return m ? m->t : -1; }
+long long trba_model_device_bytes(const trba_model *m) {
+    return m ? (long long)(m->arena.used + m->zarena.used) : -1;
+}
+
+long long trba_model_running_stats_count(const trba_model *m) {
+    if (!m) return -1;
+    long long n = 0;
+    for (auto &L : m->convs) n += 2 * L.cout;
+    return n;
+}
+
+int trba_model_get_running_stats(trba_model *m, float *host, long long n) {
+    if (!m || !host || n != trba_model_running_stats_count(m)) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    long long o = 0;
+    for (auto &L : m->convs) {
+        TRBA_CHECK(cudaMemcpy(host + o, L.run_mean.get(), L.cout * 4, cudaMemcpyDeviceToHost));
+        TRBA_CHECK(cudaMemcpy(host + o + L.cout, L.run_var.get(), L.cout * 4, cudaMemcpyDeviceToHost));
+        o += 2 * L.cout;
+    }
+    return cuda_status();
+}
+
+int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                                const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
+    if (!m || !img || !text_in || !target || !ctc_tgt || !ctc_len || batch <= 0 || batch > m->B) return -1;
+    cudaStream_t st = as_stream(stream);
+    Ctx c{m, st, batch, m->P.get(), m->G.get()};
+    m->last_B = batch;
+    TRBA_CHECK(cudaMemsetAsync(m->zarena.base, 0, m->zarena.used, st));
+    TRBA_CHECK(cudaMemsetAsync(m->G.get(), 0, (size_t)m->n_params * 4, st));
+    cnn_forward(c, img);
+    head_forward(c, text_in, target, ctc_tgt, ctc_len);
+    head_backward(c);
+    cnn_backward(c);
+    return cuda_status();
+}
+
+int trba_model_optimizer_step(trba_model *m, void *stream) {
+    if (!m) return -1;
+    optimizer(m, as_stream(stream));
+    return cuda_status();
+}
+
+int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                          const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
+    int rc = trba_model_forward_backward(m, img, text_in, target, ctc_tgt, ctc_len, batch, stream);
+    if (rc) return rc;
+    if (m->comm) {
+        const ncclResult_t r = ncclAllReduce(m->G.get(), m->G.get(), (size_t)m->n_params, ncclFloat, ncclAvg, m->comm,
+                                             as_stream(stream));
+        if (r != ncclSuccess) {
+            report_error(__FILE__, __LINE__, ncclGetErrorString(r), (int)r);
+            return (int)r;
+        }
+    }
+    return trba_model_optimizer_step(m, stream);
+}
+
+int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                               const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, float *loss_host,
+                               void *stream) {
+    if (!m || batch <= 0 || batch > m->B || !loss_host) return -1;
+    cudaStream_t st = as_stream(stream);
+    const auto &cf = m->cfg;
+    const size_t S = (size_t)m->steps;
+    TRBA_CHECK(cudaMemcpyAsync(m->in_img.get(), img, (size_t)batch * 3 * cf.img_h * cf.img_w, cudaMemcpyHostToDevice, st));
+    TRBA_CHECK(cudaMemcpyAsync(m->in_text.get(), text_in, batch * S * 4, cudaMemcpyHostToDevice, st));
+    TRBA_CHECK(cudaMemcpyAsync(m->in_target.get(), target, batch * S * 4, cudaMemcpyHostToDevice, st));
+    TRBA_CHECK(cudaMemcpyAsync(m->in_ctc.get(), ctc_tgt, batch * S * 4, cudaMemcpyHostToDevice, st));
+    TRBA_CHECK(cudaMemcpyAsync(m->in_ctc_len.get(), ctc_len, batch * 4, cudaMemcpyHostToDevice, st));
+    int rc = trba_model_train_step(m, m->in_img.get(), m->in_text.get(), m->in_target.get(), m->in_ctc.get(),
+                                   m->in_ctc_len.get(), batch, stream);
+    if (rc) return rc;
+    TRBA_CHECK(cudaMemcpyAsync(loss_host, m->loss.get(), 3 * sizeof(float), cudaMemcpyDeviceToHost, st));
+    TRBA_CHECK(cudaStreamSynchronize(st));
+    return cuda_status();
+}
+
+int trba_dp_unique_id(void *id128) {
+    if (!id128) return -1;
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return (int)r;
+    std::memcpy(id128, &id, sizeof(id));
+    return 0;
+}
+
+int trba_dp_init(trba_model *m, const void *id128, int rank, int world) {
+    if (!m || !id128 || world < 1 || rank < 0 || rank >= world) return -1;
+    if (world == 1) return 0;
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof(id));
+    const ncclResult_t r = ncclCommInitRank(&m->comm, world, id, rank);
+    if (r != ncclSuccess) {
+        report_error(__FILE__, __LINE__, ncclGetErrorString(r), (int)r);
+        m->comm = nullptr;
+        return (int)r;
+    }
+    m->world = world;
+    return 0;
+}
+
+int trba_dp_finalize(trba_model *m) {
+    if (!m) return -1;
+    if (m->comm) {
+        ncclCommDestroy(m->comm);
+        m->comm = nullptr;
+    }
+    m->world = 1;
+    return 0;
+}
+
+}  // extern "C"

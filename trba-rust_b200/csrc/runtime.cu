@@ -19,6 +19,9 @@ static std::mutex g_err_mu;
 
 bool abort_on_error() { return g_abort.load() != 0; }
 
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 void report_error(const char *file, int line, const char *what, int code) {
     {
         std::lock_guard<std::mutex> lk(g_err_mu);
@@ -51,6 +54,7 @@ using namespace trba;
 extern "C" {
 
 void trba_set_abort_on_error(int on) { g_abort.store(on ? 1 : 0); }
+long long trba_launch_count(void) { return g_launches.load(); }
 int trba_last_error(void) { return g_err.load(); }
 const char *trba_last_error_string(void) { return g_err.load() ? g_err_msg : ""; }
 void trba_clear_error(void) {

@@ -1,0 +1,586 @@
+// Sequence head of the device-resident QAT step: fp32 GEMM, BiLSTM time
+// loops, attention decoder, CE and CTC.  The recurrences are latency-bound
+// (T <= 64 dependent steps over tiny matrices), so each runs as ONE
+// persistent launch per direction / decoder with the recurrent weights in
+// shared memory and one CTA per group of samples (samples never interact
+// inside a recurrence); the big batched products (input projections, weight
+// gradients, logits) run as ordinary GEMMs outside the time loop.
+#include "seq_kernels.cuh"
+
+namespace trba {
+namespace seq {
+namespace {
+
+__device__ __forceinline__ float sigm(float v) { return fdiv(1.0f, fadd(1.0f, expf(-v))); }
+
+// ------------------------------------------------------------- sgemm --
+constexpr int TM = 64, TN = 64, TK = 16;
+
+__global__ void __launch_bounds__(256) sgemm_kernel(Gemm g) {
+    __shared__ float sa[TK][TM + 1], sb[TK][TN + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < g.K; k0 += TK) {
+        for (int e = threadIdx.x; e < TM * TK; e += 256) {
+            const int kk = e / TM, mm = e - kk * TM;  // consecutive threads walk m
+            const int m = m0 + mm, k = k0 + kk;
+            sa[kk][mm] = (m < g.M && k < g.K) ? g.A[(i64)m * g.sam + (i64)k * g.sak] : 0.0f;
+            const int nn = mm, n = n0 + nn;
+            sb[kk][nn] = (n < g.N && k < g.K) ? g.B[(i64)k * g.sbk + (i64)n * g.sbn] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < TK; ++kk)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(sa[kk][ty * 4 + i], sb[kk][tx * 4 + j], acc[i][j]);
+        __syncthreads();
+    }
+    for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 4; ++j) {
+            const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+            if (m >= g.M || n >= g.N) continue;
+            float v = g.alpha * acc[i][j];
+            float *c = g.C + (i64)m * g.ldc + n;
+            if (g.beta != 0.0f) v = fadd(v, g.beta * *c);
+            if (g.bias) v = fadd(v, g.bias[n]);
+            *c = v;
+        }
+}
+
+__global__ void col_sums_kernel(const float *X, int rows, int cols, i64 ld, float *out, int accumulate) {
+    GRID_LOOP(n, cols) {
+        float s = 0.0f;
+        for (int r = 0; r < rows; ++r) s = fadd(s, X[(i64)r * ld + n]);
+        out[n] = accumulate ? fadd(out[n], s) : s;
+    }
+}
+
+// -------------------------------------------------------------- LSTM --
+constexpr int BG = 4;  // samples per CTA in the recurrences
+
+__global__ void lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B,
+                                int T, int H, int rev, float *gates, float *c_tr, float *h_prev_tr, float *cat,
+                                int dir) {
+    extern __shared__ float sm[];
+    const int G4 = 4 * H;
+    float *wT = sm;                  // [H][4H]: wT[k*4H + o] = w_hh[o*H + k]
+    float *hb = wT + H * G4;         // [BG][H]
+    float *cb = hb + BG * H;         // [BG][H]
+    float *gb = cb + BG * H;         // [BG][4H]
+    const int b0 = blockIdx.x * BG;
+    for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) {
+        const int o = e / H, k = e - o * H;
+        wT[k * G4 + o] = w_hh[e];
+    }
+    for (int e = threadIdx.x; e < BG * H; e += blockDim.x) hb[e] = cb[e] = 0.0f;
+    __syncthreads();
+    for (int s = 0; s < T; ++s) {
+        const int tt = rev ? T - 1 - s : s;
+        for (int e = threadIdx.x; e < BG * G4; e += blockDim.x) {
+            const int g = e / G4, o = e - g * G4, b = b0 + g;
+            if (b >= B) continue;
+            float acc = 0.0f;
+            for (int k = 0; k < H; ++k) acc = fmaf(hb[g * H + k], wT[k * G4 + o], acc);
+            gb[e] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[((i64)b * T + tt) * G4 + o]), acc);
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
+            const int g = e / H, i = e - g * H, b = b0 + g;
+            if (b >= B) continue;
+            const float *pg = gb + g * G4;
+            const float ig = sigm(pg[i]), fg = sigm(pg[H + i]), cg = tanhf(pg[2 * H + i]), og = sigm(pg[3 * H + i]);
+            const float cn = fadd(fmul(fg, cb[e]), fmul(ig, cg));
+            const float hn = fmul(og, tanhf(cn));
+            const i64 r = (i64)b * T + tt;
+            gates[r * G4 + i] = ig;
+            gates[r * G4 + H + i] = fg;
+            gates[r * G4 + 2 * H + i] = cg;
+            gates[r * G4 + 3 * H + i] = og;
+            c_tr[r * H + i] = cn;
+            h_prev_tr[r * H + i] = hb[e];
+            cat[r * 2 * H + dir * H + i] = hn;
+            cb[e] = cn;
+            hb[e] = hn;  // only this thread touches hb[e] in this phase
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void lstm_bwd_kernel(const float *dcat, const float *gates, const float *c_tr, const float *w_hh, int B,
+                                int T, int H, int rev, int dir, float *dgates) {
+    extern __shared__ float sm[];
+    const int G4 = 4 * H;
+    float *w = sm;                   // [4H][H] natural layout
+    float *dhn = w + G4 * H;         // [BG][H]
+    float *dcn = dhn + BG * H;       // [BG][H]
+    float *dg = dcn + BG * H;        // [BG][4H]
+    const int b0 = blockIdx.x * BG;
+    for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) w[e] = w_hh[e];
+    for (int e = threadIdx.x; e < BG * H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
+    __syncthreads();
+    for (int s = T - 1; s >= 0; --s) {
+        const int tt = rev ? T - 1 - s : s;
+        const int tp = rev ? tt + 1 : tt - 1;  // time position of the previous slot
+        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
+            const int g = e / H, i = e - g * H, b = b0 + g;
+            if (b >= B) continue;
+            const i64 r = (i64)b * T + tt;
+            const float ig = gates[r * G4 + i], fg = gates[r * G4 + H + i], cg = gates[r * G4 + 2 * H + i],
+                        og = gates[r * G4 + 3 * H + i];
+            const float tc = tanhf(c_tr[r * H + i]);
+            const float cp = s > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
+            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[e]);
+            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[e], fg));
+            float *d = dg + g * G4;
+            d[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            d[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            d[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            d[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            dcn[e] = dc;
+            for (int q = 0; q < 4; ++q) dgates[r * G4 + q * H + i] = d[q * H + i];
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
+            const int g = e / H, k = e - g * H;
+            if (b0 + g >= B) continue;
+            float acc = 0.0f;
+            for (int o = 0; o < G4; ++o) acc = fmaf(dg[g * G4 + o], w[o * H + k], acc);
+            dhn[e] = acc;
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------ attention dec --
+__global__ void attn_fwd_kernel(AttnFwd a) {
+    extern __shared__ float sm[];
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    float *wihT = sm;             // [H][4H], context columns of w_ih, transposed
+    float *whhT = wihT + H * G4;  // [H][4H]
+    float *h2hT = whhT + H * G4;  // [H][H]:  h2hT[j*H + k] = h2h_w[k*H + j]
+    float *h = h2hT + H * H, *c = h + H, *phh = c + H, *ctx = phh + H, *pre = ctx + H;  // pre: 4H
+    float *tn = pre + G4, *e = tn + T * H, *al = e + T;
+    const int b = blockIdx.x;
+    for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
+        const int o = i / H, k = i - o * H;
+        wihT[k * G4 + o] = a.w_ih[(i64)o * CV + k];
+        whhT[k * G4 + o] = a.w_hh[i];
+    }
+    for (int i = threadIdx.x; i < H * H; i += blockDim.x) {
+        const int k = i / H, j = i - k * H;
+        h2hT[j * H + k] = a.h2h_w[i];
+    }
+    for (int i = threadIdx.x; i < H; i += blockDim.x) h[i] = c[i] = 0.0f;
+    __syncthreads();
+    const float *bh = a.bh + (i64)b * T * H, *ph = a.proj_h + (i64)b * T * H;
+    for (int st = 0; st < a.steps; ++st) {
+        const i64 sb = (i64)st * a.B + b;
+        for (int k = threadIdx.x; k < H; k += blockDim.x) {  // proj_hh = h2h(h), bias first
+            float acc = a.h2h_b[k];
+            for (int j = 0; j < H; ++j) acc = fadd(acc, fmul(h[j], h2hT[j * H + k]));
+            phh[k] = acc;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
+            const int k = i % H;
+            const float v = tanhf(fadd(ph[i], phh[k]));
+            tn[i] = v;
+            a.tanh_tr[sb * T * H + i] = v;
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            float acc = 0.0f;
+            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(tn[t * H + k], a.score_w[k]));
+            e[t] = acc;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {  // softmax over T
+            float mx = -INFINITY;
+            for (int t = 0; t < T; ++t) mx = fmaxf(mx, e[t]);
+            float s = 0.0f;
+            for (int t = 0; t < T; ++t) {
+                al[t] = expf(fsub(e[t], mx));
+                s = fadd(s, al[t]);
+            }
+            for (int t = 0; t < T; ++t) al[t] = fdiv(al[t], s);
+        }
+        __syncthreads();
+        const int tok = a.text_in[(i64)b * a.steps + st];
+        for (int k = threadIdx.x; k < H; k += blockDim.x) {
+            float acc = 0.0f;
+            for (int t = 0; t < T; ++t)
+                if (al[t] != 0.0f) acc = fadd(acc, fmul(al[t], bh[t * H + k]));
+            ctx[k] = acc;
+        }
+        for (int t = threadIdx.x; t < T; t += blockDim.x) a.alpha[sb * T + t] = al[t];
+        __syncthreads();
+        for (int i = threadIdx.x; i < CV; i += blockDim.x)
+            a.cell_in[sb * CV + i] = i < H ? ctx[i] : (i - H == tok ? 1.0f : 0.0f);
+        for (int o = threadIdx.x; o < G4; o += blockDim.x) {
+            float acc = fadd(a.b_ih[o], a.b_hh[o]);
+            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(ctx[k], wihT[k * G4 + o]));
+            acc = fadd(acc, a.w_ih[(i64)o * CV + H + tok]);
+            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(h[k], whhT[k * G4 + o]));
+            pre[o] = acc;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float ig = sigm(pre[i]), fg = sigm(pre[H + i]), cg = tanhf(pre[2 * H + i]), og = sigm(pre[3 * H + i]);
+            const float cn = fadd(fmul(fg, c[i]), fmul(ig, cg));
+            const float hn = fmul(og, tanhf(cn));
+            a.gates[sb * G4 + i] = ig;
+            a.gates[sb * G4 + H + i] = fg;
+            a.gates[sb * G4 + 2 * H + i] = cg;
+            a.gates[sb * G4 + 3 * H + i] = og;
+            a.cs[sb * H + i] = cn;
+            a.hs[sb * H + i] = hn;
+            c[i] = cn;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < H; i += blockDim.x) h[i] = a.hs[sb * H + i];
+        __syncthreads();
+    }
+}
+
+__global__ void attn_bwd_kernel(AttnBwd a) {
+    extern __shared__ float sm[];
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    float *wc = sm;                 // [4H][H] context columns of w_ih
+    float *whh = wc + G4 * H;       // [4H][H]
+    float *h2h = whh + G4 * H;      // [H][H]
+    float *dhn = h2h + H * H, *dcn = dhn + H, *dg = dcn + H, *dctx = dg + G4, *dhp = dctx + H, *dphh = dhp + H;
+    float *da = dphh + H, *de = da + T, *dot = de + T;  // dot: 1
+    float *acc_bh = dot + 1, *acc_ph = acc_bh + T * H;
+    const int b = blockIdx.x;
+    for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
+        const int o = i / H, k = i - o * H;
+        wc[i] = a.w_ih[(i64)o * CV + k];
+        whh[i] = a.w_hh[i];
+    }
+    for (int i = threadIdx.x; i < H * H; i += blockDim.x) h2h[i] = a.h2h_w[i];
+    for (int i = threadIdx.x; i < H; i += blockDim.x) dhn[i] = dcn[i] = 0.0f;
+    for (int i = threadIdx.x; i < T * H; i += blockDim.x) acc_bh[i] = acc_ph[i] = 0.0f;
+    __syncthreads();
+    const float *bh = a.bh + (i64)b * T * H;
+    for (int st = a.steps - 1; st >= 0; --st) {
+        const i64 sb = (i64)st * a.B + b;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float *g = a.gates + sb * G4;
+            const float ig = g[i], fg = g[H + i], cg = g[2 * H + i], og = g[3 * H + i];
+            const float tc = tanhf(a.cs[sb * H + i]);
+            const float cp = st > 0 ? a.cs[(sb - a.B) * H + i] : 0.0f;
+            const float dh = fadd(a.d_out_hid[sb * H + i], dhn[i]);
+            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
+            dg[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            dg[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            dg[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            dg[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            dcn[i] = dc;
+        }
+        __syncthreads();
+        for (int o = threadIdx.x; o < G4; o += blockDim.x) a.dgates[sb * G4 + o] = dg[o];
+        for (int k = threadIdx.x; k < H; k += blockDim.x) {
+            float s1 = 0.0f, s2 = 0.0f;
+            for (int o = 0; o < G4; ++o) {
+                const float dv = dg[o];
+                if (dv == 0.0f) continue;
+                s1 = fadd(s1, fmul(dv, wc[o * H + k]));
+                s2 = fadd(s2, fmul(dv, whh[o * H + k]));
+            }
+            dctx[k] = s1;
+            dhp[k] = s2;
+        }
+        __syncthreads();
+        const float *al = a.alpha + sb * T;
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            float s = 0.0f;
+            for (int k = 0; k < H; ++k) s = fadd(s, fmul(dctx[k], bh[t * H + k]));
+            da[t] = s;
+            const float at = al[t];
+            for (int k = 0; k < H; ++k) acc_bh[t * H + k] = fadd(acc_bh[t * H + k], fmul(at, dctx[k]));
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float s = 0.0f;
+            for (int t = 0; t < T; ++t) s = fadd(s, fmul(al[t], da[t]));
+            *dot = s;
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            const float v = fmul(al[t], fsub(da[t], *dot));
+            de[t] = v;
+            a.de[sb * T + t] = v;
+        }
+        __syncthreads();
+        const float *tn = a.tanh_tr + sb * T * H;
+        for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
+            const int t = i / H, k = i - t * H;
+            if (de[t] == 0.0f) continue;
+            acc_ph[i] = fadd(acc_ph[i], fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(tn[i], tn[i]))));
+        }
+        for (int k = threadIdx.x; k < H; k += blockDim.x) {
+            float s = 0.0f;
+            for (int t = 0; t < T; ++t) {
+                if (de[t] == 0.0f) continue;
+                const float v = tn[t * H + k];
+                s = fadd(s, fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(v, v))));
+            }
+            dphh[k] = s;
+            a.dprojhh[sb * H + k] = s;
+        }
+        __syncthreads();
+        for (int j = threadIdx.x; j < H; j += blockDim.x) {
+            float s = 0.0f;
+            for (int k = 0; k < H; ++k) s = fadd(s, fmul(dphh[k], h2h[k * H + j]));
+            dhn[j] = fadd(dhp[j], s);
+        }
+        __syncthreads();
+    }
+    for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
+        a.d_proj_h[(i64)b * T * H + i] = acc_ph[i];
+        a.d_bh[(i64)b * T * H + i] = acc_bh[i];
+    }
+}
+
+// ------------------------------------------------------------ losses --
+__global__ void ce_rows_kernel(const float *logits, const int32_t *target, int B, int steps, int V, int pad,
+                               float *d, float *row_loss) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= B * steps) return;
+    const int st = warp / B, b = warp - st * B;
+    const float *x = logits + (i64)warp * V;
+    float *dr = d + (i64)warp * V;
+    const int tgt = target[(i64)b * steps + st];
+    if (tgt == pad) {
+        for (int k = lane; k < V; k += 32) dr[k] = 0.0f;
+        if (lane == 0) row_loss[warp] = 0.0f;
+        return;
+    }
+    float mx = -INFINITY;
+    for (int k = lane; k < V; k += 32) mx = fmaxf(mx, x[k]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float s = 0.0f;
+    for (int k = lane; k < V; k += 32) s += expf(fsub(x[k], mx));
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    for (int k = lane; k < V; k += 32) {
+        const float p = fdiv(expf(fsub(x[k], mx)), s);
+        dr[k] = k == tgt ? fsub(p, 1.0f) : p;
+    }
+    if (lane == 0) row_loss[warp] = -logf(fdiv(expf(fsub(x[tgt], mx)), s));
+}
+
+__device__ __forceinline__ double logadd(double a, double b) {
+    if (a == -INFINITY) return b;
+    if (b == -INFINITY) return a;
+    return a > b ? a + log(1.0 + exp(b - a)) : b + log(1.0 + exp(a - b));
+}
+
+__device__ bool ctc_valid(const int32_t *len, int b, int T) { return len[b] > 0 && T >= len[b] + 1; }
+
+__global__ void ctc_kernel(const float *logits, const int32_t *tgt, const int32_t *len, int Lmax, int B, int T, int V,
+                           float cw, float *grad, double *sample_loss) {
+    extern __shared__ double smd[];
+    const int b = blockIdx.x;
+    const int L = len[b];
+    const int S = 2 * L + 1;
+    double *al = smd, *be = al + (i64)T * (2 * Lmax + 1);
+    float *lp = reinterpret_cast<float *>(be + (i64)T * (2 * Lmax + 1));  // [T][V]
+    int *ext = reinterpret_cast<int *>(lp + T * V);
+    __shared__ double loss_s;
+    __shared__ int n_valid;
+    float *g = grad + (i64)b * T * V;
+    if (!ctc_valid(len, b, T)) {  // zero_infinity: no loss, zero gradient
+        for (int i = threadIdx.x; i < T * V; i += blockDim.x) g[i] = 0.0f;
+        if (threadIdx.x == 0) sample_loss[b] = 0.0;
+        return;
+    }
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int i = 0; i < B; ++i) n += ctc_valid(len, i, T) ? 1 : 0;
+        n_valid = n > 0 ? n : 1;
+    }
+    for (int s = threadIdx.x; s < S; s += blockDim.x) ext[s] = (s & 1) ? tgt[(i64)b * Lmax + (s >> 1)] : 0;
+    // log-softmax rows (src/ctc.rs:1-19): f32 max, f64 sum of exp, f32 result
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float *x = logits + ((i64)b * T + t) * V;
+        float mx = -INFINITY;
+        for (int k = 0; k < V; ++k) mx = fmaxf(mx, x[k]);
+        double se = 0.0;
+        for (int k = 0; k < V; ++k) se += exp((double)fsub(x[k], mx));
+        const double ls = log(se);
+        for (int k = 0; k < V; ++k) lp[t * V + k] = (float)((double)x[k] - (double)mx - ls);
+    }
+    __syncthreads();
+    const int SS = 2 * Lmax + 1;
+    for (int s = threadIdx.x; s < S; s += blockDim.x) {
+        al[s] = s < 2 ? (double)lp[ext[s]] : -INFINITY;
+        be[(T - 1) * SS + s] = s >= S - 2 ? 0.0 : -INFINITY;
+    }
+    __syncthreads();
+    for (int t = 1; t < T; ++t) {  // src/ctc.rs:49-73
+        for (int s = threadIdx.x; s < S; s += blockDim.x) {
+            double best = al[(t - 1) * SS + s];
+            if (s > 0) best = logadd(best, al[(t - 1) * SS + s - 1]);
+            if (s >= 2 && ext[s - 2] != ext[s]) best = logadd(best, al[(t - 1) * SS + s - 2]);
+            al[t * SS + s] = best + (double)lp[t * V + ext[s]];
+        }
+        __syncthreads();
+    }
+    for (int t = T - 2; t >= 0; --t) {  // src/ctc.rs:75-100
+        for (int s = threadIdx.x; s < S; s += blockDim.x) {
+            const float *row = lp + (t + 1) * V;
+            double best = be[(t + 1) * SS + s] + (double)row[ext[s]];
+            if (s + 1 < S) best = logadd(best, be[(t + 1) * SS + s + 1] + (double)row[ext[s + 1]]);
+            if (s + 2 < S && ext[s + 2] != ext[s]) best = logadd(best, be[(t + 1) * SS + s + 2] + (double)row[ext[s + 2]]);
+            be[t * SS + s] = best;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) loss_s = -logadd(al[(T - 1) * SS + S - 1], al[(T - 1) * SS + S - 2]);
+    __syncthreads();
+    const double loss = loss_s;
+    if (!isfinite(loss)) {
+        for (int i = threadIdx.x; i < T * V; i += blockDim.x) g[i] = 0.0f;
+        if (threadIdx.x == 0) sample_loss[b] = 0.0;
+        return;
+    }
+    const double scale = 1.0 / ((double)L * (double)n_valid);
+    for (int i = threadIdx.x; i < T * V; i += blockDim.x) {
+        const int t = i / V, k = i - t * V;
+        double gam = 0.0;
+        for (int s = 0; s < S; ++s)
+            if (ext[s] == k) gam += exp(al[t * SS + s] + be[t * SS + s] + loss);
+        const double p = (double)expf(lp[i]);
+        g[i] = fmul((float)((p - gam) * scale), cw);
+    }
+    if (threadIdx.x == 0) sample_loss[b] = loss / (double)L;
+}
+
+__global__ void loss_finalize_kernel(const float *row_loss, const int32_t *target, int B, int steps, int pad,
+                                     const double *sample_loss, const int32_t *ctc_len, int T, float cw, float *out,
+                                     float *scale_out) {
+    __shared__ double sa[32], sc[32];
+    __shared__ int cnt[32], nv[32];
+    double a = 0.0, c = 0.0;
+    int k = 0, n = 0;
+    for (int i = threadIdx.x; i < B * steps; i += blockDim.x) {
+        const int st = i / B, b = i - st * B;
+        if (target[(i64)b * steps + st] != pad) {
+            ++k;
+            a += (double)row_loss[i];
+        }
+    }
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        c += sample_loss[b];
+        n += ctc_valid(ctc_len, b, T) ? 1 : 0;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        c += __shfl_xor_sync(0xffffffffu, c, o);
+        k += __shfl_xor_sync(0xffffffffu, k, o);
+        n += __shfl_xor_sync(0xffffffffu, n, o);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sa[w] = a; sc[w] = c; cnt[w] = k; nv[w] = n; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double A = 0.0, Cc = 0.0;
+        int K = 0, N = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { A += sa[i]; Cc += sc[i]; K += cnt[i]; N += nv[i]; }
+        K = K > 0 ? K : 1;
+        N = N > 0 ? N : 1;
+        const double attn = A / K, ctc = Cc / N;
+        out[0] = (float)((double)fsub(1.0f, cw) * attn + (double)cw * ctc);
+        out[1] = (float)attn;
+        out[2] = (float)ctc;
+        *scale_out = fdiv(fsub(1.0f, cw), (float)K);
+    }
+}
+
+__global__ void scale_by_kernel(float *x, const float *s, i64 n) {
+    const float v = *s;
+    GRID_LOOP(i, n) x[i] = fmul(x[i], v);
+}
+
+}  // namespace
+
+void sgemm(const Gemm &g, cudaStream_t st) {
+    if (g.M <= 0 || g.N <= 0) return;
+    dim3 grid((g.M + TM - 1) / TM, (g.N + TN - 1) / TN);
+    sgemm_kernel<<<grid, 256, 0, st>>>(g);
+    TRBA_LAUNCH_CHECK();
+}
+
+void col_sums(const float *X, int rows, int cols, i64 ld, float *out, bool accumulate, cudaStream_t st) {
+    col_sums_kernel<<<grid_for(cols, 128), 128, 0, st>>>(X, rows, cols, ld, out, accumulate ? 1 : 0);
+    TRBA_LAUNCH_CHECK();
+}
+
+static void set_smem(const void *fn, size_t bytes) {
+    if (bytes > 48 * 1024) TRBA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H, int rev,
+              float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st) {
+    const size_t smem = sizeof(float) * ((size_t)4 * H * H + BG * H * 2 + BG * 4 * H);
+    set_smem((const void *)lstm_fwd_kernel, smem);
+    lstm_fwd_kernel<<<(B + BG - 1) / BG, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev, cat,
+                                                          dir);
+    TRBA_LAUNCH_CHECK();
+}
+
+void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H, int rev,
+              int dir, float *dgates, cudaStream_t st) {
+    const size_t smem = sizeof(float) * ((size_t)4 * H * H + BG * H * 2 + BG * 4 * H);
+    set_smem((const void *)lstm_bwd_kernel, smem);
+    lstm_bwd_kernel<<<(B + BG - 1) / BG, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
+    TRBA_LAUNCH_CHECK();
+}
+
+void attn_fwd(const AttnFwd &a, cudaStream_t st) {
+    const int H = a.H, T = a.T;
+    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + 4 * H + 4 * H + T * H + 2 * T);
+    set_smem((const void *)attn_fwd_kernel, smem);
+    attn_fwd_kernel<<<a.B, 256, smem, st>>>(a);
+    TRBA_LAUNCH_CHECK();
+}
+
+void attn_bwd(const AttnBwd &a, cudaStream_t st) {
+    const int H = a.H, T = a.T;
+    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + 5 * H + 4 * H + 2 * T + 1 + 2 * T * H);
+    set_smem((const void *)attn_bwd_kernel, smem);
+    attn_bwd_kernel<<<a.B, 256, smem, st>>>(a);
+    TRBA_LAUNCH_CHECK();
+}
+
+void ce_rows(const float *logits, const int32_t *target, int B, int steps, int V, int pad, float *d_logits,
+             float *row_loss, cudaStream_t st) {
+    const int rows = B * steps;
+    ce_rows_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(logits, target, B, steps, V, pad, d_logits, row_loss);
+    TRBA_LAUNCH_CHECK();
+}
+
+void ctc(const float *logits, const int32_t *ctc_tgt, const int32_t *ctc_len, int Lmax, int B, int T, int V, float cw,
+         float *grad, double *sample_loss, cudaStream_t st) {
+    const size_t smem = sizeof(double) * 2 * (size_t)T * (2 * Lmax + 1) + sizeof(float) * (size_t)T * V +
+                        sizeof(int) * (2 * Lmax + 1);
+    set_smem((const void *)ctc_kernel, smem);
+    ctc_kernel<<<B, 128, smem, st>>>(logits, ctc_tgt, ctc_len, Lmax, B, T, V, cw, grad, sample_loss);
+    TRBA_LAUNCH_CHECK();
+}
+
+void loss_finalize(const float *row_loss, const int32_t *target, int B, int steps, int pad, const double *sample_loss,
+                   const int32_t *ctc_len, int T, float cw, float *d_logits, int V, float *out, cudaStream_t st) {
+    loss_finalize_kernel<<<1, 1024, 0, st>>>(row_loss, target, B, steps, pad, sample_loss, ctc_len, T, cw, out,
+                                             out + 3);
+    TRBA_LAUNCH_CHECK();
+    const i64 n = (i64)B * steps * V;
+    scale_by_kernel<<<grid_for(n), 256, 0, st>>>(d_logits, out + 3, n);
+    TRBA_LAUNCH_CHECK();
+}
+
+}  // namespace seq
+}  // namespace trba

@@ -1,0 +1,80 @@
+// Kernels of the sequence head of the device-resident QAT step: fp32 GEMM,
+// BiLSTM recurrences, the attention decoder, CE and CTC losses.  All traces
+// of the recurrences are kept per sample in time-position order [B, T, .].
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace trba {
+namespace seq {
+
+// C[m, n] = alpha * sum_k A(m, k) B(k, n) + beta * C[m, n] + bias[n], with
+// A(m, k) = A[m*sam + k*sak], B(k, n) = B[k*sbk + n*sbn], C[m*ldc + n].
+// Summation over k in order (deterministic).  alpha_dev, if set, multiplies alpha.
+struct Gemm {
+    int M, N, K;
+    const float *A;
+    i64 sam, sak;
+    const float *B;
+    i64 sbk, sbn;
+    float *C;
+    i64 ldc;
+    float alpha = 1.0f, beta = 0.0f;
+    const float *bias = nullptr;
+};
+void sgemm(const Gemm &g, cudaStream_t st);
+// out[n] (+)= sum over rows of X[r*ld + n] (column sums, rows in order).
+void col_sums(const float *X, int rows, int cols, i64 ld, float *out, bool accumulate, cudaStream_t st);
+
+// One LSTM direction over all T slots (src/rnn.rs:107-166).  xg = x W_ih^T
+// [B, T, 4H]; writes gates (post-activation) and c [B, T, .], h into
+// cat[b, tt, dir*H + i] (row stride 2H) and h_prev [B, T, H].
+void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H,
+              int rev, float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st);
+// Backward through time of one direction (src/rnn.rs:200-288): dh_out from
+// dcat[b, tt, dir*H + i]; writes dgates [B, T, 4H].
+void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H,
+              int rev, int dir, float *dgates, cudaStream_t st);
+
+// Attention decoder, teacher forced (src/attn.rs:119-261).  bh/proj_h [B,T,H];
+// text_in [B, steps]; traces laid out [steps, B, .].
+struct AttnFwd {
+    const float *bh, *proj_h;
+    const int32_t *text_in;
+    const float *h2h_w, *h2h_b, *score_w, *w_ih, *b_ih, *w_hh, *b_hh;
+    int B, T, H, V, steps;
+    float *tanh_tr;  // [steps, B, T, H]
+    float *alpha;    // [steps, B, T]
+    float *cell_in;  // [steps, B, H+V]  (context, then the one-hot token)
+    float *gates;    // [steps, B, 4H]
+    float *hs, *cs;  // [steps, B, H]
+};
+void attn_fwd(const AttnFwd &a, cudaStream_t st);
+
+// Backward (src/attn.rs:263-500): d_out_hid [steps, B, H]; writes dgates
+// [steps, B, 4H], de [steps, B, T], dprojhh [steps, B, H], d_proj_h [B, T, H]
+// and d_bh [B, T, H] (the context part only; the i2h path is added later).
+struct AttnBwd {
+    const float *d_out_hid, *bh, *tanh_tr, *alpha, *gates, *cs, *score_w, *w_ih, *w_hh, *h2h_w;
+    int B, T, H, V, steps;
+    float *dgates, *de, *dprojhh, *d_proj_h, *d_bh;
+};
+void attn_bwd(const AttnBwd &a, cudaStream_t st);
+
+// CE with ignore-pad over logits [steps, B, V] (src/main.rs:2300-2328):
+// d_logits = (p - onehot), row loss -ln p_tgt; rows whose target is pad get 0.
+void ce_rows(const float *logits, const int32_t *target, int B, int steps, int V, int pad, float *d_logits,
+             float *row_loss, cudaStream_t st);
+// CTC (src/ctc.rs:103-193) over logits [B*T, V]; ctc_tgt [B, Lmax] with
+// lengths ctc_len [B]; grad already multiplied by cw.
+void ctc(const float *logits, const int32_t *ctc_tgt, const int32_t *ctc_len, int Lmax, int B, int T, int V,
+         float cw, float *grad, double *sample_loss, cudaStream_t st);
+// Totals: attn = sum(row_loss)/count, ctc = sum(sample_loss)/n, loss =
+// (1-cw) attn + cw ctc into out[0..2]; scales d_logits by (1-cw)/count.
+void loss_finalize(const float *row_loss, const int32_t *target, int B, int steps, int pad, const double *sample_loss,
+                   const int32_t *ctc_len, int T, float cw, float *d_logits, int V, float *out, cudaStream_t st);
+
+}  // namespace seq
+}  // namespace trba
