@@ -92,6 +92,11 @@ long long trba_model_step_count(const trba_model *m);
 /* Bytes of device memory the model holds. */
 long long trba_model_device_bytes(const trba_model *m);
 
+/* Diagnostics: copy an internal fp32 buffer of the last step to the host
+ * (feat, dfeat, enc, d_enc, logits, dlogits, ctc_logits, dctc, <conv>.x,
+ * <conv>.mean, <conv>.var); n must equal the buffer's element count. */
+int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long long n);
+
 /* ---- data parallel (one process per GPU, NCCL over NVLink) ---- */
 /* 128-byte NCCL unique id from rank 0, broadcast by the caller. */
 int trba_dp_unique_id(void *id128);

@@ -289,15 +289,47 @@ def make_batch(cfg: Config, b: int, seed: int, fixed_len: int | None = None):
 
 
 # ------------------------------------------------------------- host math --
+# Host arithmetic.  Every dot product accumulates in f64 and is rounded once
+# to f32, and exp / tanh / log are evaluated in f64 and rounded once: the
+# results are then the correctly rounded values (ties aside), which the GPU
+# build computes the same way, so both produce identical f32 numbers.  The
+# reference's sequential f32 loops and f32 libm calls differ from these by a
+# few ulps (rayon / OpenMP already make the reference non-reproducible at
+# that level).
+F64 = np.float64
+
+
+def dot64(a, b):
+    """(a @ b) accumulated in f64, rounded to f32."""
+    return (np.asarray(a, F64) @ np.asarray(b, F64)).astype(F32)
+
+
+def sum64(x, axis=None):
+    return np.asarray(x, F64).sum(axis=axis).astype(F32)
+
+
+def exp32(x):
+    return np.exp(np.asarray(x, F32).astype(F64)).astype(F32)
+
+
+def tanh32(x):
+    return np.tanh(np.asarray(x, F32).astype(F64)).astype(F32)
+
+
+def log32(x):
+    return np.log(np.asarray(x, F32).astype(F64)).astype(F32)
+
+
 def sigmoid(x):
-    return (F32(1.0) / (F32(1.0) + np.exp(-x))).astype(F32)
+    return (F32(1.0) / (F32(1.0) + exp32(-np.asarray(x, F32)))).astype(F32)
 
 
 def linear_fwd(x, w, b=None):
-    y = x @ w.T
+    """LinearF::forward (src/qnet.rs:120-138): x w^T (+ b)."""
+    y = dot64(x, w.T)
     if b is not None:
-        y = y + b
-    return y.astype(F32)
+        y = (y + b).astype(F32)
+    return y
 
 
 # ---------------------------------------------------------------- oracle --
@@ -475,11 +507,11 @@ class OracleTrba:
         gate = tr["gate"]
         dpre2 = (dgate * gate * (F32(1.0) - gate)).astype(F32).reshape(b, c)
         w2, w1 = self.p[f"{se_name(bname)}.fc2.w"], self.p[f"{se_name(bname)}.fc1.w"]
-        self.g[f"{se_name(bname)}.fc2.w"] += (dpre2.T @ tr["h1"]).astype(F32)
-        dh1 = (dpre2 @ w2).astype(F32)
+        self.g[f"{se_name(bname)}.fc2.w"] += dot64(dpre2.T, tr["h1"])
+        dh1 = dot64(dpre2, w2)
         dpre1 = np.where(tr["h1"] > 0, dh1, F32(0)).astype(F32)
-        self.g[f"{se_name(bname)}.fc1.w"] += (dpre1.T @ tr["pooled"].reshape(b, c)).astype(F32)
-        dpooled = (dpre1 @ w1).astype(F32).reshape(-1)
+        self.g[f"{se_name(bname)}.fc1.w"] += dot64(dpre1.T, tr["pooled"].reshape(b, c))
+        dpooled = dot64(dpre1, w1).reshape(-1)
         apb = np.zeros(n_out, F32)
         self.be("launch_avgpool_hw_backward", dpooled, c, hw, b, apb)
         dy2f = np.zeros(n_out, F32)
@@ -573,23 +605,25 @@ class OracleTrba:
     def lstm_dir(self, pre, x, b, t, rev):
         w_ih, b_ih, w_hh, b_hh = (self.p[pre + s] for s in (".w_ih", ".b_ih", ".w_hh", ".b_hh"))
         H = w_hh.shape[1]
-        xg = (x.reshape(b, t, -1) @ w_ih.T).astype(F32)  # [B, T, 4H]
+        xg = dot64(x.reshape(b * t, -1), w_ih.T).reshape(b, t, 4 * H)  # [B, T, 4H]
         gates = np.zeros((t, b, 4 * H), F32)
         cs = np.zeros((t, b, H), F32)
         hs = np.zeros((t, b, H), F32)
+        hprev = np.zeros((t, b, H), F32)
         c_prev = np.zeros((b, H), F32)
         h_prev = np.zeros((b, H), F32)
+        bsum = (b_ih + b_hh).astype(F32)
         for step in range(t):
             tt = t - 1 - step if rev else step
-            g = ((b_ih + b_hh) + xg[:, tt, :] + h_prev @ w_hh.T).astype(F32)
+            g = ((bsum + xg[:, tt, :]) + dot64(h_prev, w_hh.T)).astype(F32)
             ig, fg = sigmoid(g[:, :H]), sigmoid(g[:, H:2 * H])
-            cg, og = np.tanh(g[:, 2 * H:3 * H]).astype(F32), sigmoid(g[:, 3 * H:])
+            cg, og = tanh32(g[:, 2 * H:3 * H]), sigmoid(g[:, 3 * H:])
             c = (fg * c_prev + ig * cg).astype(F32)
-            hh = (og * np.tanh(c)).astype(F32)
+            hh = (og * tanh32(c)).astype(F32)
             gates[step] = np.concatenate([ig, fg, cg, og], axis=1)
-            cs[step], hs[step] = c, hh
+            cs[step], hs[step], hprev[step] = c, hh, h_prev
             c_prev, h_prev = c, hh
-        return dict(gates=gates, c=cs, h=hs)
+        return dict(gates=gates, c=cs, h=hs, hprev=hprev)
 
     def bilstm_layer_fwd(self, li, x, b, t):
         f = self.lstm_dir(f"rnn{li}.f", x, b, t, False)
@@ -606,41 +640,39 @@ class OracleTrba:
         w_ih, w_hh = self.p[pre + ".w_ih"], self.p[pre + ".w_hh"]
         H, D = w_hh.shape[1], w_ih.shape[1]
         x = tr["x"].reshape(b, t, D)
-        dx = np.zeros((b, t, D), F32)
+        dg_all = np.zeros((b, t, 4 * H), F32)    # by time position
+        hp_all = np.zeros((b, t, H), F32)
         dc_next = np.zeros((b, H), F32)
         dh_next = np.zeros((b, H), F32)
-        g_wih, g_whh = np.zeros_like(w_ih), np.zeros_like(w_hh)
-        g_b = np.zeros(4 * H, F32)
         for step in range(t - 1, -1, -1):
             tt = t - 1 - step if rev else step
             gr, c = trc["gates"][step], trc["c"][step]
-            h_prev = trc["h"][step - 1] if step else np.zeros((b, H), F32)
             c_prev = trc["c"][step - 1] if step else np.zeros((b, H), F32)
             ig, fg, cg, og = gr[:, :H], gr[:, H:2 * H], gr[:, 2 * H:3 * H], gr[:, 3 * H:]
-            tc = np.tanh(c).astype(F32)
+            tc = tanh32(c)
             dh = (dh_out[step] + dh_next).astype(F32)
             dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
             dg = np.concatenate([dc * cg * ig * (F32(1) - ig), dc * c_prev * fg * (F32(1) - fg),
                                  dc * ig * (F32(1) - cg * cg), dh * tc * og * (F32(1) - og)], axis=1).astype(F32)
             dc_next = dc
-            g_b += dg.sum(axis=0, dtype=np.float64).astype(F32)
-            g_wih += (dg.T @ x[:, tt, :]).astype(F32)
-            g_whh += (dg.T @ h_prev).astype(F32)
-            dx[:, tt, :] = dg @ w_ih
-            dh_next = (dg @ w_hh).astype(F32)
-        self.g[pre + ".w_ih"] += g_wih
-        self.g[pre + ".w_hh"] += g_whh
-        self.g[pre + ".b_ih"] += g_b
-        self.g[pre + ".b_hh"] += g_b
-        return dx.reshape(-1)
+            dg_all[:, tt] = dg
+            hp_all[:, tt] = trc["hprev"][step]
+            dh_next = dot64(dg, w_hh)
+        dg2 = dg_all.reshape(b * t, 4 * H)
+        gb = sum64(dg2, axis=0)
+        self.g[pre + ".w_ih"] += dot64(dg2.T, x.reshape(b * t, D))
+        self.g[pre + ".w_hh"] += dot64(dg2.T, hp_all.reshape(b * t, H))
+        self.g[pre + ".b_ih"] += gb
+        self.g[pre + ".b_hh"] += gb
+        return dot64(dg2, w_ih).reshape(-1)
 
     def bilstm_layer_bwd(self, li, dy, tr):
         b, t, H = tr["b"], tr["t"], self.cfg.hidden
         dy = dy.reshape(b * t, H)
         pw = self.p[f"rnn{li}.proj.w"]
-        dcat = (dy @ pw).astype(F32).reshape(b, t, 2 * H)
-        self.g[f"rnn{li}.proj.w"] += (dy.T @ tr["cat"].reshape(b * t, 2 * H)).astype(F32)
-        self.g[f"rnn{li}.proj.b"] += dy.sum(axis=0, dtype=np.float64).astype(F32)
+        dcat = dot64(dy, pw).reshape(b, t, 2 * H)
+        self.g[f"rnn{li}.proj.w"] += dot64(dy.T, tr["cat"].reshape(b * t, 2 * H))
+        self.g[f"rnn{li}.proj.b"] += sum64(dy, axis=0)
         dh_f = dcat[:, :, :H].transpose(1, 0, 2)
         dh_b = dcat[:, ::-1, H:].transpose(1, 0, 2)
         dx1 = self.lstm_dir_bwd(f"rnn{li}.f", np.ascontiguousarray(dh_f), tr, tr["f"], False)
@@ -653,28 +685,31 @@ class OracleTrba:
         H, V, steps = cfg.hidden, cfg.classes, text_in.shape[1]
         P = self.p
         bh = enc.reshape(b, t, H)
-        proj_h = linear_fwd(bh.reshape(b * t, H), P["attn.i2h.w"]).reshape(b, t, H)
+        proj_h = dot64(bh.reshape(b * t, H), P["attn.i2h.w"].T).reshape(b, t, H)
         h = np.zeros((b, H), F32)
         cc = np.zeros((b, H), F32)
         tr = dict(tanh=np.zeros((steps, b, t, H), F32), alpha=np.zeros((steps, b, t), F32),
                   cell_in=np.zeros((steps, b, H + V), F32), gates=np.zeros((steps, b, 4 * H), F32),
                   hs=np.zeros((steps, b, H), F32), cs=np.zeros((steps, b, H), F32))
         scw = P["attn.score.w"].reshape(H)
+        wc, wtok = P["attn.w_ih"][:, :H], P["attn.w_ih"][:, H:]
+        bsum = (P["attn.b_ih"] + P["attn.b_hh"]).astype(F32)
         for st in range(steps):
             phh = linear_fwd(h, P["attn.h2h.w"], P["attn.h2h.b"])
-            tn = np.tanh(proj_h + phh[:, None, :]).astype(F32)
-            e = (tn @ scw).astype(F32)
-            ex = np.exp(e - e.max(axis=1, keepdims=True)).astype(F32)
-            alpha = (ex / ex.sum(axis=1, keepdims=True)).astype(F32)
-            ctx = np.einsum("bt,btk->bk", alpha, bh).astype(F32)
+            tn = tanh32(proj_h + phh[:, None, :])
+            e = dot64(tn, scw)
+            ex = exp32(e - e.max(axis=1, keepdims=True))
+            alpha = (ex / sum64(ex, axis=1)[:, None]).astype(F32)
+            ctx = np.einsum("bt,btk->bk", alpha.astype(F64), bh.astype(F64)).astype(F32)
+            tok = text_in[:, st]
             ci = np.zeros((b, H + V), F32)
             ci[:, :H] = ctx
-            ci[np.arange(b), H + text_in[:, st]] = F32(1.0)
-            pre = ((P["attn.b_ih"] + P["attn.b_hh"]) + ci @ P["attn.w_ih"].T + h @ P["attn.w_hh"].T).astype(F32)
+            ci[np.arange(b), H + tok] = F32(1.0)
+            pre = (((bsum + dot64(ctx, wc.T)) + wtok[:, tok].T) + dot64(h, P["attn.w_hh"].T)).astype(F32)
             ig, fg = sigmoid(pre[:, :H]), sigmoid(pre[:, H:2 * H])
-            cg, og = np.tanh(pre[:, 2 * H:3 * H]).astype(F32), sigmoid(pre[:, 3 * H:])
+            cg, og = tanh32(pre[:, 2 * H:3 * H]), sigmoid(pre[:, 3 * H:])
             cc = (fg * cc + ig * cg).astype(F32)
-            h = (og * np.tanh(cc)).astype(F32)
+            h = (og * tanh32(cc)).astype(F32)
             tr["tanh"][st], tr["alpha"][st], tr["cell_in"][st] = tn, alpha, ci
             tr["gates"][st] = np.concatenate([ig, fg, cg, og], axis=1)
             tr["hs"][st], tr["cs"][st] = h, cc
@@ -689,52 +724,59 @@ class OracleTrba:
         H, V = cfg.hidden, cfg.classes
         dyg = d_logits.reshape(b, steps, V).transpose(1, 0, 2).reshape(steps * b, V)
         hs = tr["hs"].reshape(steps * b, H)
-        G["attn.gen.w"] += (dyg.T @ hs).astype(F32)
-        G["attn.gen.b"] += dyg.sum(axis=0, dtype=np.float64).astype(F32)
-        d_out_hid = (dyg @ P["attn.gen.w"]).astype(F32).reshape(steps, b, H)
+        G["attn.gen.w"] += dot64(dyg.T, hs)
+        G["attn.gen.b"] += sum64(dyg, axis=0)
+        d_out_hid = dot64(dyg, P["attn.gen.w"]).reshape(steps, b, H)
         dh_next = np.zeros((b, H), F32)
         dc_next = np.zeros((b, H), F32)
         d_proj_h = np.zeros((b, t, H), F32)
         d_bh = np.zeros((b, t, H), F32)
         scw = P["attn.score.w"].reshape(H)
+        wc = P["attn.w_ih"][:, :H]
         zeros = np.zeros((b, H), F32)
+        dg_all = np.zeros((steps, b, 4 * H), F32)
+        de_all = np.zeros((steps, b, t), F32)
+        dphh_all = np.zeros((steps, b, H), F32)
         for st in range(steps - 1, -1, -1):
             g = tr["gates"][st]
-            ci = tr["cell_in"][st]
             c_prev = tr["cs"][st - 1] if st else zeros
-            h_prev = tr["hs"][st - 1] if st else zeros
             ig, fg, cg, og = g[:, :H], g[:, H:2 * H], g[:, 2 * H:3 * H], g[:, 3 * H:]
-            tc = np.tanh(tr["cs"][st]).astype(F32)
+            tc = tanh32(tr["cs"][st])
             dh = (d_out_hid[st] + dh_next).astype(F32)
             dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
             dg = np.concatenate([dc * cg * ig * (F32(1) - ig), dc * c_prev * fg * (F32(1) - fg),
                                  dc * ig * (F32(1) - cg * cg), dh * tc * og * (F32(1) - og)], axis=1).astype(F32)
             dc_next = dc
-            sdg = dg.sum(axis=0, dtype=np.float64).astype(F32)
-            G["attn.b_ih"] += sdg
-            G["attn.b_hh"] += sdg
-            G["attn.w_ih"] += (dg.T @ ci).astype(F32)
-            G["attn.w_hh"] += (dg.T @ h_prev).astype(F32)
-            d_cellin = (dg @ P["attn.w_ih"]).astype(F32)
-            dh_prev = (dg @ P["attn.w_hh"]).astype(F32)
-            dctx = d_cellin[:, :H]
+            dg_all[st] = dg
+            dctx = dot64(dg, wc)
+            dh_prev = dot64(dg, P["attn.w_hh"])
             alpha = tr["alpha"][st]
-            da = np.einsum("bk,btk->bt", dctx, tr["bh"]).astype(F32)
+            da = np.einsum("bk,btk->bt", dctx.astype(F64), tr["bh"].astype(F64)).astype(F32)
             d_bh += (alpha[:, :, None] * dctx[:, None, :]).astype(F32)
-            dot = (alpha * da).sum(axis=1).astype(F32)
+            dot = np.einsum("bt,bt->b", alpha.astype(F64), da.astype(F64)).astype(F32)
             de = (alpha * (da - dot[:, None])).astype(F32)  # [B, T]
+            de_all[st] = de
             tn = tr["tanh"][st]
             dtn = (de[:, :, None] * scw[None, None, :] * (F32(1) - tn * tn)).astype(F32)
             d_proj_h += dtn
-            G["attn.score.w"] += np.einsum("bt,btk->k", de, tn).astype(F32).reshape(1, H)
-            dprojhh = dtn.sum(axis=1).astype(F32)
-            G["attn.h2h.w"] += (dprojhh.T @ h_prev).astype(F32)
-            G["attn.h2h.b"] += dprojhh.sum(axis=0, dtype=np.float64).astype(F32)
-            dh_prev = (dh_prev + dprojhh @ P["attn.h2h.w"]).astype(F32)
-            dh_next = dh_prev
+            dprojhh = sum64(dtn, axis=1)
+            dphh_all[st] = dprojhh
+            dh_next = (dh_prev + dot64(dprojhh, P["attn.h2h.w"])).astype(F32)
+        R = steps * b
+        dg2 = dg_all.reshape(R, 4 * H)
+        sdg = sum64(dg2, axis=0)
+        G["attn.b_ih"] += sdg
+        G["attn.b_hh"] += sdg
+        G["attn.w_ih"] += dot64(dg2.T, tr["cell_in"].reshape(R, H + V))
+        hs_prev = tr["hs"].reshape(R, H)[:R - b]  # h_prev of steps 1.. (zero at step 0)
+        G["attn.w_hh"] += dot64(dg2[b:].T, hs_prev)
+        dp2 = dphh_all.reshape(R, H)
+        G["attn.h2h.w"] += dot64(dp2[b:].T, hs_prev)
+        G["attn.h2h.b"] += sum64(dp2, axis=0)
+        G["attn.score.w"] += dot64(de_all.reshape(1, R * t), tr["tanh"].reshape(R * t, H))
         dph = d_proj_h.reshape(b * t, H)
-        G["attn.i2h.w"] += (dph.T @ tr["bh"].reshape(b * t, H)).astype(F32)
-        d_bh = (d_bh.reshape(b * t, H) + dph @ P["attn.i2h.w"]).astype(F32)
+        G["attn.i2h.w"] += dot64(dph.T, tr["bh"].reshape(b * t, H))
+        d_bh = (dot64(dph, P["attn.i2h.w"]) + d_bh.reshape(b * t, H)).astype(F32)
         return d_bh.reshape(-1)
 
     # -- CTC, src/ctc.rs:1-193 ----------------------------------------------
@@ -803,7 +845,7 @@ class OracleTrba:
                 for si in range(S):
                     gamma[tt, ext[si]] += math.exp(al[tt, si] + be[tt, si] + loss)
             scale = 1.0 / (L * n)
-            p = np.exp(lp32[bi * t:(bi + 1) * t]).astype(np.float64)
+            p = exp32(lp32[bi * t:(bi + 1) * t]).astype(np.float64)
             grad[bi * t:(bi + 1) * t] = ((p - gamma) * scale).astype(F32)
         return total / n, grad.reshape(-1)
 
@@ -831,10 +873,10 @@ class OracleTrba:
         keep = tgt != cfg.pad
         count = int(keep.sum())
         mx = lg.max(axis=1, keepdims=True)
-        ex = np.exp(lg - mx).astype(F32)
-        s = ex.sum(axis=1, keepdims=True).astype(F32)
+        ex = exp32(lg - mx)
+        s = sum64(ex, axis=1)[:, None]
         pr = (ex / s).astype(F32)
-        attn_loss = float(-np.log(pr[keep, tgt[keep]]).astype(np.float64).sum())
+        attn_loss = float(-log32(pr[keep, tgt[keep]]).astype(np.float64).sum())
         d_logits = pr.copy()
         d_logits[np.arange(b * steps), tgt] -= F32(1.0)
         d_logits[~keep] = 0
@@ -843,16 +885,21 @@ class OracleTrba:
         d_logits = (d_logits * F32((F32(1.0) - cw) / F32(count))).astype(F32)
         ctc_loss, d_ctc = self.ctc_loss_backward(ctc_logits, b, t, V, ctc_targets, 0)
         d_ctc = (d_ctc * cw).astype(F32)
-        total = float((1.0 - float(cw)) * attn_loss + float(cw) * ctc_loss)
+        total = float(float(F32(1.0) - cw) * attn_loss + float(cw) * ctc_loss)
+        self.debug = dict(feat=feat, enc=enc.reshape(-1), logits=logits.transpose(1, 0, 2).reshape(-1),
+                          dlogits=d_logits.reshape(b, steps, V).transpose(1, 0, 2).reshape(-1), dctc=d_ctc,
+                          ctc_logits=ctc_logits.reshape(-1))
         # backward
         d_enc = self.attn_bwd(d_logits, atr)
         dct = d_ctc.reshape(b * t, V)
-        self.g["ctc.w"] += (dct.T @ enc.reshape(b * t, H)).astype(F32)
-        self.g["ctc.b"] += dct.sum(axis=0, dtype=np.float64).astype(F32)
-        d_enc = (d_enc + (dct @ self.p["ctc.w"]).reshape(-1)).astype(F32)
+        self.g["ctc.w"] += dot64(dct.T, enc.reshape(b * t, H))
+        self.g["ctc.b"] += sum64(dct, axis=0)
+        d_enc = (d_enc + dot64(dct, self.p["ctc.w"]).reshape(-1)).astype(F32)
         d = d_enc
+        self.debug["d_enc"] = d_enc
         for li in range(cfg.rnn_layers - 1, -1, -1):
             d = self.bilstm_layer_bwd(li, d, rtr[li])
+        self.debug["dfeat"] = d
         self.cnn_bwd(np.ascontiguousarray(d.astype(F32)), ctr)
         self.optimizer_step()
         return dict(loss=total, attn=attn_loss, ctc=ctc_loss)
@@ -886,7 +933,7 @@ class OracleTrba:
                 p -= (float(lr) * mh / (np.sqrt(vh) + eps)).astype(F32)
             else:  # host Muon, src/opt.rs muon_step_f32
                 rows, cols = p.shape
-                sq = F32((g.astype(F32) * g.astype(F32)).sum(dtype=np.float32))
+                sq = F32((g.astype(F32) * g.astype(F32)).astype(np.float64).sum())
                 frob = max(F32(np.sqrt(sq)), F32(1e-8))
                 scale = min(F32(np.sqrt(F32(min(rows, cols)))) / frob, F32(cfg.muon_cap))
                 lr_eff = lr * F32(np.sqrt(F32(max(rows, cols))))

@@ -12,6 +12,11 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+try:  # load PyTorch (and its CUDA / NCCL libraries) before libtrba_b200
+    import torch  # noqa: F401
+except Exception:  # pragma: no cover
+    torch = None
+
 REPO = Path(__file__).resolve().parent.parent
 GOLDEN = REPO / "tests" / "golden"
 sys.path.insert(0, str(REPO))

@@ -36,15 +36,15 @@ def _nvcc() -> str:
 
 
 def _nccl_dirs() -> tuple[list[str], list[str]]:
-    """Include and link flags for NCCL (system copy, else the wheel's)."""
-    inc, lib = [], []
+    """NCCL header location (system copy, else the wheel's).  The library is
+    not linked against NCCL: it is dlopen'ed at run time."""
+    inc, lib = [], ["-ldl"]
     if Path("/usr/include/nccl.h").exists():
-        return inc, ["-lnccl"]
+        return inc, lib
     try:
         import nvidia.nccl as nn  # type: ignore
         root = Path(list(nn.__path__)[0])
         inc = [f"-I{root / 'include'}"]
-        lib = [f"-L{root / 'lib'}", "-l:libnccl.so.2", f"-Xlinker=-rpath={root / 'lib'}"]
     except Exception:
         pass
     return inc, lib

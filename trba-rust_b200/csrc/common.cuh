@@ -73,3 +73,12 @@ __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b)
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ int rint_even(float v) { return __float2int_rn(v); }
+
+// Transcendentals of the training step, evaluated in f64 and rounded once to
+// f32 (correctly rounded except in vanishingly rare ties).  The CPU oracle
+// evaluates the same way, so both sides produce identical f32 results; the
+// reference's f32 libm calls differ from these by at most an ulp.
+__device__ __forceinline__ float cr_expf(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float cr_tanhf(float x) { return (float)tanh((double)x); }
+__device__ __forceinline__ float cr_logf(float x) { return (float)log((double)x); }
+__device__ __forceinline__ float cr_sigmoid(float x) { return fdiv(1.0f, fadd(1.0f, cr_expf(-x))); }

@@ -156,17 +156,17 @@ __global__ void se_forward_kernel(const float *pool, const float *w1, const floa
     for (int i = threadIdx.x; i < C; i += blockDim.x) sp[i] = pool[(i64)b * C + i];
     __syncthreads();
     for (int j = threadIdx.x; j < R; j += blockDim.x) {
-        float acc = 0.0f;
-        for (int i = 0; i < C; ++i) acc = fadd(acc, fmul(sp[i], w1[(i64)j * C + i]));
-        const float h = fmaxf(acc, 0.0f);
+        double acc = 0.0;
+        for (int i = 0; i < C; ++i) acc = fma((double)sp[i], (double)w1[(i64)j * C + i], acc);
+        const float h = fmaxf((float)acc, 0.0f);
         sh[j] = h;
         h1[(i64)b * R + j] = h;
     }
     __syncthreads();
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j < R; ++j) acc = fadd(acc, fmul(sh[j], w2[(i64)c * R + j]));
-        gate[(i64)b * C + c] = fdiv(1.0f, fadd(1.0f, expf(-acc)));
+        double acc = 0.0;
+        for (int j = 0; j < R; ++j) acc = fma((double)sh[j], (double)w2[(i64)c * R + j], acc);
+        gate[(i64)b * C + c] = cr_sigmoid((float)acc);
     }
 }
 
@@ -215,18 +215,18 @@ __global__ void se_backward_kernel(const float *dz, const float *y2, const float
     }
     __syncthreads();
     for (int j = threadIdx.x; j < R; j += blockDim.x) {
-        float acc = 0.0f;
-        for (int c = 0; c < C; ++c) acc = fadd(acc, fmul(s_dp2[c], w2[(i64)c * R + j]));
-        const float d1 = h1[(i64)b * R + j] > 0.0f ? acc : 0.0f;
+        double acc = 0.0;
+        for (int c = 0; c < C; ++c) acc = fma((double)s_dp2[c], (double)w2[(i64)c * R + j], acc);
+        const float d1 = h1[(i64)b * R + j] > 0.0f ? (float)acc : 0.0f;
         s_dp1[j] = d1;
         dpre1[(i64)b * R + j] = d1;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < C; i += blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j < R; ++j) acc = fadd(acc, fmul(s_dp1[j], w1[(i64)j * C + i]));
-        s_dpool[i] = acc;
-        dpooled[(i64)b * C + i] = acc;
+        double acc = 0.0;
+        for (int j = 0; j < R; ++j) acc = fma((double)s_dp1[j], (double)w1[(i64)j * C + i], acc);
+        s_dpool[i] = (float)acc;
+        dpooled[(i64)b * C + i] = (float)acc;
     }
     __syncthreads();
     for (i64 e = threadIdx.x; e < (i64)C * HW; e += blockDim.x) {
@@ -240,16 +240,16 @@ __global__ void se_wgrad_kernel(const float *dpre1, const float *dpre2, const fl
                                 int C, int R, float *g_w1, float *g_w2) {
     const int n2 = C * R;
     GRID_LOOP(e, (i64)2 * n2) {
-        float acc = 0.0f;
+        double acc = 0.0;
         if (e < n2) {
             const int c = (int)(e / R), j = (int)(e - (i64)c * R);
-            for (int b = 0; b < B; ++b) acc = fadd(acc, fmul(dpre2[(i64)b * C + c], h1[(i64)b * R + j]));
-            g_w2[e] = fadd(g_w2[e], acc);
+            for (int b = 0; b < B; ++b) acc = fma((double)dpre2[(i64)b * C + c], (double)h1[(i64)b * R + j], acc);
+            g_w2[e] = fadd(g_w2[e], (float)acc);
         } else {
             const i64 f = e - n2;
             const int j = (int)(f / C), i = (int)(f - (i64)j * C);
-            for (int b = 0; b < B; ++b) acc = fadd(acc, fmul(dpre1[(i64)b * R + j], pool[(i64)b * C + i]));
-            g_w1[f] = fadd(g_w1[f], acc);
+            for (int b = 0; b < B; ++b) acc = fma((double)dpre1[(i64)b * R + j], (double)pool[(i64)b * C + i], acc);
+            g_w1[f] = fadd(g_w1[f], (float)acc);
         }
     }
 }

@@ -7,6 +7,7 @@
 // launches kernels only (no allocation, no host synchronisation), so the
 // whole step can be enqueued back to back and, in data-parallel mode, the
 // gradient buffer is all-reduced with one NCCL call.
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <cmath>
@@ -24,6 +25,37 @@
 using namespace trba;
 
 namespace {
+
+// NCCL is resolved at run time (dlopen) rather than linked: a process that
+// already holds a libnccl.so.2 (PyTorch bundles one) keeps using that copy,
+// and a process that never goes data-parallel never loads NCCL at all.
+struct Nccl {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+const Nccl &nccl() {
+    static Nccl n;
+    static bool tried = false;
+    if (tried) return n;
+    tried = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return n;
+    n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+    n.CommInitRank = (decltype(n.CommInitRank))dlsym(h, "ncclCommInitRank");
+    n.AllReduce = (decltype(n.AllReduce))dlsym(h, "ncclAllReduce");
+    n.CommDestroy = (decltype(n.CommDestroy))dlsym(h, "ncclCommDestroy");
+    n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
+    n.ok = n.GetUniqueId && n.CommInitRank && n.AllReduce && n.CommDestroy && n.GetErrorString;
+    return n;
+}
 
 __host__ __device__ inline int a16(int x) { return (x + 15) & ~15; }
 inline i64 a16l(i64 x) { return (x + 15) & ~15LL; }
@@ -130,6 +162,9 @@ struct trba_model {
     Ref<float> proj_h, tanh_tr, alpha, cell_in, agates, hs, cs, logits, dlogits, row_loss, ctc_logits, dctc;
     Ref<float> d_out_hid, adg, ade, adprojhh, d_proj_h, d_bh;
     Ref<double> ctc_sample_loss;
+    Ref<double> gemm_ws;   // split-K partial sums of the fp32 GEMMs
+    i64 gemm_ws_elems = 0;
+    Ref<float> ones;       // column-sum helper
     Ref<float> loss;  // 4 floats
     // optimiser scratch (zeroed per step)
     Ref<double> gsq_total;
@@ -218,20 +253,21 @@ __global__ void adam_segs_kernel(const Seg *segs, float *P, const float *G, floa
 // matrix computes ||g||^2 in f32 and the step lr*sqrt(max)*min(sqrt(min)/frob, cap).
 __global__ void muon_mat_norm_kernel(const Seg *segs, const float *G, const float *f, float lr, float cap,
                                      float *step) {
-    __shared__ float sm[32];
+    __shared__ double sm[32];
     const Seg s = segs[blockIdx.x];
     const float fv = *f;
-    float acc = 0.0f;
+    double acc = 0.0;  // ||f g||^2 accumulated in f64, rounded once
     for (int j = threadIdx.x; j < s.n; j += blockDim.x) {
         const float g = fmul(G[s.off + j], fv);
-        acc = fadd(acc, fmul(g, g));
+        acc += (double)fmul(g, g);
     }
-    acc = warp_sum_f(acc);
+    acc = warp_sum_d(acc);
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
     __syncthreads();
     if (threadIdx.x == 0) {
-        float t = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fadd(t, sm[w]);
+        double td = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) td += sm[w];
+        const float t = (float)td;
         const float frob = fmaxf(__fsqrt_rn(t), 1e-8f);
         const float mn = (float)min(s.rows, s.cols), mx = (float)max(s.rows, s.cols);
         const float scale = fminf(fdiv(__fsqrt_rn(mn), frob), cap);
@@ -608,6 +644,9 @@ void allocate(trba_model *m) {
     m->d_proj_h = b.p<float>((i64)B * T * Hh);
     m->d_bh = b.p<float>((i64)B * T * Hh);
     m->ctc_sample_loss = b.p<double>(B);
+    m->gemm_ws_elems = (i64)8 << 20;
+    m->gemm_ws = b.p<double>(m->gemm_ws_elems);
+    m->ones = b.p<float>((i64)B * (S > T ? S : T) * 1);
     m->loss = b.p<float>(4);
     m->gsq_total = b.z<double>(1);
     m->conv_gsq = b.z<double>((i64)m->convs.size());
@@ -765,16 +804,22 @@ void cnn_backward(Ctx &c) {
     conv_bwd(c, cv[0], m->dy_c0.get(), nullptr, nullptr, nullptr);
 }
 
-seq::Gemm gemm(int M, int N, int K, const float *A, i64 sam, i64 sak, const float *Bm, i64 sbk, i64 sbn, float *C,
-               i64 ldc, float beta = 0.0f, const float *bias = nullptr) {
+seq::Gemm gemm(trba_model *m, int M, int N, int K, const float *A, i64 sam, i64 sak, const float *Bm, i64 sbk,
+               i64 sbn, float *C, i64 ldc, bool accumulate = false, const float *bias = nullptr) {
     seq::Gemm g;
     g.M = M, g.N = N, g.K = K;
     g.A = A, g.sam = sam, g.sak = sak;
     g.B = Bm, g.sbk = sbk, g.sbn = sbn;
     g.C = C, g.ldc = ldc;
-    g.beta = beta;
+    g.accumulate = accumulate;
     g.bias = bias;
+    g.ws = m->gemm_ws.get();
+    g.ws_elems = m->gemm_ws_elems;
     return g;
+}
+
+void colsum(trba_model *m, const float *X, int rows, int cols, i64 ld, float *out, cudaStream_t st) {
+    seq::col_sums(X, rows, cols, ld, m->ones.get(), out, true, m->gemm_ws.get(), m->gemm_ws_elems, st);
 }
 
 void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const int32_t *ctc_tgt,
@@ -785,17 +830,17 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
     const float *x = m->feat.get();
     for (auto &r : m->rnn) {  // BiLstmLayer::forward (src/rnn.rs:167-174)
         for (int d = 0; d < 2; ++d) {
-            seq::sgemm(gemm(B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
+            seq::sgemm(gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
             seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
                           r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
         }
-        seq::sgemm(gemm(B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, 0.0f, c.P + r.pb),
+        seq::sgemm(gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
                    c.st);
         x = r.y.get();
     }
     const float *enc = x;  // [B, T, H]
     const i64 oi2h = entry_off(m, "attn.i2h.w");
-    seq::sgemm(gemm(B * T, H, H, enc, H, 1, c.P + oi2h, 1, H, m->proj_h.get(), H), c.st);
+    seq::sgemm(gemm(m, B * T, H, H, enc, H, 1, c.P + oi2h, 1, H, m->proj_h.get(), H), c.st);
     seq::AttnFwd a{};
     a.bh = enc;
     a.proj_h = m->proj_h.get();
@@ -815,10 +860,10 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
     a.hs = m->hs.get();
     a.cs = m->cs.get();
     seq::attn_fwd(a, c.st);
-    seq::sgemm(gemm(S * B, V, H, m->hs.get(), H, 1, c.P + entry_off(m, "attn.gen.w"), 1, H, m->logits.get(), V, 0.0f,
+    seq::sgemm(gemm(m, S * B, V, H, m->hs.get(), H, 1, c.P + entry_off(m, "attn.gen.w"), 1, H, m->logits.get(), V, 0.0f,
                     c.P + entry_off(m, "attn.gen.b")),
                c.st);
-    seq::sgemm(gemm(B * T, V, H, enc, H, 1, c.P + entry_off(m, "ctc.w"), 1, H, m->ctc_logits.get(), V, 0.0f,
+    seq::sgemm(gemm(m, B * T, V, H, enc, H, 1, c.P + entry_off(m, "ctc.w"), 1, H, m->ctc_logits.get(), V, 0.0f,
                     c.P + entry_off(m, "ctc.b")),
                c.st);
     seq::ce_rows(m->logits.get(), target, B, S, V, cf.pad, m->dlogits.get(), m->row_loss.get(), c.st);
@@ -835,9 +880,9 @@ void head_backward(Ctx &c) {
     const float *enc = m->rnn.back().y.get();
     const i64 ogw = entry_off(m, "attn.gen.w"), ogb = entry_off(m, "attn.gen.b");
     // generator (src/attn.rs:274-284)
-    seq::sgemm(gemm(V, H, R, m->dlogits.get(), 1, V, m->hs.get(), H, 1, c.G + ogw, H, 1.0f), c.st);
-    seq::col_sums(m->dlogits.get(), R, V, V, c.G + ogb, true, c.st);
-    seq::sgemm(gemm(R, H, V, m->dlogits.get(), V, 1, c.P + ogw, H, 1, m->d_out_hid.get(), H), c.st);
+    seq::sgemm(gemm(m, V, H, R, m->dlogits.get(), 1, V, m->hs.get(), H, 1, c.G + ogw, H, true), c.st);
+    colsum(m, m->dlogits.get(), R, V, V, c.G + ogb, c.st);
+    seq::sgemm(gemm(m, R, H, V, m->dlogits.get(), V, 1, c.P + ogw, H, 1, m->d_out_hid.get(), H), c.st);
     seq::AttnBwd a{};
     a.d_out_hid = m->d_out_hid.get();
     a.bh = enc;
@@ -858,47 +903,47 @@ void head_backward(Ctx &c) {
     seq::attn_bwd(a, c.st);
     const int CV = H + V;
     float *dg = m->adg.get();
-    seq::sgemm(gemm(4 * H, CV, R, dg, 1, 4 * H, m->cell_in.get(), CV, 1, c.G + entry_off(m, "attn.w_ih"), CV, 1.0f),
+    seq::sgemm(gemm(m, 4 * H, CV, R, dg, 1, 4 * H, m->cell_in.get(), CV, 1, c.G + entry_off(m, "attn.w_ih"), CV, true),
                c.st);
-    seq::col_sums(dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_ih"), true, c.st);
-    seq::col_sums(dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_hh"), true, c.st);
+    colsum(m, dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_ih"), c.st);
+    colsum(m, dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_hh"), c.st);
     // w_hh and h2h: h_prev of step st is hs of st-1 (zero at st = 0)
-    seq::sgemm(gemm(4 * H, H, R - B, dg + (i64)B * 4 * H, 1, 4 * H, m->hs.get(), H, 1,
-                    c.G + entry_off(m, "attn.w_hh"), H, 1.0f),
+    seq::sgemm(gemm(m, 4 * H, H, R - B, dg + (i64)B * 4 * H, 1, 4 * H, m->hs.get(), H, 1,
+                    c.G + entry_off(m, "attn.w_hh"), H, true),
                c.st);
-    seq::sgemm(gemm(H, H, R - B, m->adprojhh.get() + (i64)B * H, 1, H, m->hs.get(), H, 1,
-                    c.G + entry_off(m, "attn.h2h.w"), H, 1.0f),
+    seq::sgemm(gemm(m, H, H, R - B, m->adprojhh.get() + (i64)B * H, 1, H, m->hs.get(), H, 1,
+                    c.G + entry_off(m, "attn.h2h.w"), H, true),
                c.st);
-    seq::col_sums(m->adprojhh.get(), R, H, H, c.G + entry_off(m, "attn.h2h.b"), true, c.st);
-    seq::sgemm(gemm(1, H, R * T, m->ade.get(), 0, 1, m->tanh_tr.get(), H, 1, c.G + entry_off(m, "attn.score.w"), H,
-                    1.0f),
+    colsum(m, m->adprojhh.get(), R, H, H, c.G + entry_off(m, "attn.h2h.b"), c.st);
+    seq::sgemm(gemm(m, 1, H, R * T, m->ade.get(), 0, 1, m->tanh_tr.get(), H, 1, c.G + entry_off(m, "attn.score.w"), H,
+                    true),
                c.st);
     const i64 oi2h = entry_off(m, "attn.i2h.w");
-    seq::sgemm(gemm(H, H, B * T, m->d_proj_h.get(), 1, H, enc, H, 1, c.G + oi2h, H, 1.0f), c.st);
-    seq::sgemm(gemm(B * T, H, H, m->d_proj_h.get(), H, 1, c.P + oi2h, H, 1, m->d_bh.get(), H, 1.0f), c.st);
+    seq::sgemm(gemm(m, H, H, B * T, m->d_proj_h.get(), 1, H, enc, H, 1, c.G + oi2h, H, true), c.st);
+    seq::sgemm(gemm(m, B * T, H, H, m->d_proj_h.get(), H, 1, c.P + oi2h, H, 1, m->d_bh.get(), H, true), c.st);
     // CTC head (src/main.rs:2344): LinearF backward
     const i64 ocw = entry_off(m, "ctc.w"), ocb = entry_off(m, "ctc.b");
-    seq::sgemm(gemm(V, H, B * T, m->dctc.get(), 1, V, enc, H, 1, c.G + ocw, H, 1.0f), c.st);
-    seq::col_sums(m->dctc.get(), B * T, V, V, c.G + ocb, true, c.st);
-    seq::sgemm(gemm(B * T, H, V, m->dctc.get(), V, 1, c.P + ocw, H, 1, m->d_bh.get(), H, 1.0f), c.st);
+    seq::sgemm(gemm(m, V, H, B * T, m->dctc.get(), 1, V, enc, H, 1, c.G + ocw, H, true), c.st);
+    colsum(m, m->dctc.get(), B * T, V, V, c.G + ocb, c.st);
+    seq::sgemm(gemm(m, B * T, H, V, m->dctc.get(), V, 1, c.P + ocw, H, 1, m->d_bh.get(), H, true), c.st);
     // BiLSTM backward, top layer first (src/rnn.rs:176-198)
     const float *dy = m->d_bh.get();
     for (int li = (int)m->rnn.size() - 1; li >= 0; --li) {
         RnnL &r = m->rnn[li];
         const float *xin = li == 0 ? m->feat.get() : m->rnn[li - 1].y.get();
-        seq::sgemm(gemm(H, 2 * H, B * T, dy, 1, H, r.cat.get(), 2 * H, 1, c.G + r.pw, 2 * H, 1.0f), c.st);
-        seq::col_sums(dy, B * T, H, H, c.G + r.pb, true, c.st);
-        seq::sgemm(gemm(B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
+        seq::sgemm(gemm(m, H, 2 * H, B * T, dy, 1, H, r.cat.get(), 2 * H, 1, c.G + r.pw, 2 * H, true), c.st);
+        colsum(m, dy, B * T, H, H, c.G + r.pb, c.st);
+        seq::sgemm(gemm(m, B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
         float *dxout = li == 0 ? m->dfeat.get() : r.dx.get();
         for (int d = 0; d < 2; ++d) {
             seq::lstm_bwd(r.dcat.get(), r.gates[d].get(), r.c[d].get(), c.P + r.whh[d], B, T, H, d, d, r.dg[d].get(),
                           c.st);
             const float *g = r.dg[d].get();
-            seq::sgemm(gemm(4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, 1.0f), c.st);
-            seq::sgemm(gemm(4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, 1.0f), c.st);
-            seq::col_sums(g, B * T, 4 * H, 4 * H, c.G + r.bih[d], true, c.st);
-            seq::col_sums(g, B * T, 4 * H, 4 * H, c.G + r.bhh[d], true, c.st);
-            seq::sgemm(gemm(B * T, r.D, 4 * H, g, 4 * H, 1, c.P + r.wih[d], r.D, 1, dxout, r.D, d ? 1.0f : 0.0f),
+            seq::sgemm(gemm(m, 4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, true), c.st);
+            seq::sgemm(gemm(m, 4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, true), c.st);
+            colsum(m, g, B * T, 4 * H, 4 * H, c.G + r.bih[d], c.st);
+            colsum(m, g, B * T, 4 * H, 4 * H, c.G + r.bhh[d], c.st);
+            seq::sgemm(gemm(m, B * T, r.D, 4 * H, g, 4 * H, 1, c.P + r.wih[d], r.D, 1, dxout, r.D, d != 0),
                        c.st);
         }
         dy = dxout;
@@ -1000,12 +1045,16 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
                        L.run_var.get(), L.cout, L.K, L.kp});
-        fill_f32_kernel<<<1, 128>>>(L.run_var.get(), L.cout, 1.0f);
+        fill_f32_kernel<<<1, 128>>>(L.run_var.get(), L.cout, true);
     }
     m->d_convtab = upload_table(tab);
     m->d_vec = upload_table(m->vec_segs);
     m->d_mat = upload_table(m->mat_segs);
     m->d_conv = upload_table(m->conv_segs);
+    {
+        const i64 n1 = (i64)m->B * (m->steps > m->T ? m->steps : m->T);
+        fill_f32_kernel<<<grid_for(n1), 256>>>(m->ones.get(), n1, 1.0f);
+    }
     TRBA_CHECK(cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming));
     TRBA_CHECK(cudaDeviceSynchronize());
     return m;
@@ -1013,7 +1062,7 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
 
 void trba_model_destroy(trba_model *m) {
     if (!m) return;
-    if (m->comm) ncclCommDestroy(m->comm);
+    if (m->comm) nccl().CommDestroy(m->comm);
     cudaFree(m->arena.base);
     cudaFree(m->zarena.base);
     cudaFree(m->d_convtab);
@@ -1119,10 +1168,10 @@ int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_
     int rc = trba_model_forward_backward(m, img, text_in, target, ctc_tgt, ctc_len, batch, stream);
     if (rc) return rc;
     if (m->comm) {
-        const ncclResult_t r = ncclAllReduce(m->G.get(), m->G.get(), (size_t)m->n_params, ncclFloat, ncclAvg, m->comm,
-                                             as_stream(stream));
+        const ncclResult_t r = nccl().AllReduce(m->G.get(), m->G.get(), (size_t)m->n_params, ncclFloat, ncclAvg,
+                                                m->comm, as_stream(stream));
         if (r != ncclSuccess) {
-            report_error(__FILE__, __LINE__, ncclGetErrorString(r), (int)r);
+            report_error(__FILE__, __LINE__, nccl().GetErrorString(r), (int)r);
             return (int)r;
         }
     }
@@ -1149,10 +1198,46 @@ int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *
     return cuda_status();
 }
 
+// Diagnostics: copy an internal fp32 buffer of the last step to the host.
+// Names: feat, dfeat, enc, d_enc, logits, dlogits, ctc_logits, dctc,
+// <conv>.x, <conv>.mean, <conv>.var; n must be the buffer's element count.
+int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long long n) {
+    if (!m || !name || !host || n <= 0) return -1;
+    const auto &cf = m->cfg;
+    const i64 B = m->last_B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps;
+    const std::string nm(name);
+    const float *src = nullptr;
+    i64 cnt = 0;
+    if (nm == "feat") src = m->feat.get(), cnt = B * T * cf.fd;
+    else if (nm == "dfeat") src = m->dfeat.get(), cnt = B * T * cf.fd;
+    else if (nm == "enc") src = m->rnn.back().y.get(), cnt = B * T * H;
+    else if (nm == "d_enc") src = m->d_bh.get(), cnt = B * T * H;
+    else if (nm == "logits") src = m->logits.get(), cnt = S * B * V;
+    else if (nm == "dlogits") src = m->dlogits.get(), cnt = S * B * V;
+    else if (nm == "ctc_logits") src = m->ctc_logits.get(), cnt = B * T * V;
+    else if (nm == "dctc") src = m->dctc.get(), cnt = B * T * V;
+    else {
+        for (auto &L : m->convs) {
+            const i64 nx = B * L.cout * L.Ho * L.Wo;
+            if (nm == L.name + ".x") src = L.x.get(), cnt = nx;
+            else if (nm == L.name + ".mean") src = L.mean.get(), cnt = L.cout;
+            else if (nm == L.name + ".var") src = L.var.get(), cnt = L.cout;
+        }
+    }
+    if (!src || cnt != n) return -2;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    TRBA_CHECK(cudaMemcpy(host, src, n * 4, cudaMemcpyDeviceToHost));
+    return cuda_status();
+}
+
 int trba_dp_unique_id(void *id128) {
     if (!id128) return -1;
+    if (!nccl().ok) {
+        report_error(__FILE__, __LINE__, "libnccl.so.2 not found", -1);
+        return -2;
+    }
     ncclUniqueId id;
-    const ncclResult_t r = ncclGetUniqueId(&id);
+    const ncclResult_t r = nccl().GetUniqueId(&id);
     if (r != ncclSuccess) return (int)r;
     std::memcpy(id128, &id, sizeof(id));
     return 0;
@@ -1161,11 +1246,15 @@ int trba_dp_unique_id(void *id128) {
 int trba_dp_init(trba_model *m, const void *id128, int rank, int world) {
     if (!m || !id128 || world < 1 || rank < 0 || rank >= world) return -1;
     if (world == 1) return 0;
+    if (!nccl().ok) {
+        report_error(__FILE__, __LINE__, "libnccl.so.2 not found", -1);
+        return -2;
+    }
     ncclUniqueId id;
     std::memcpy(&id, id128, sizeof(id));
-    const ncclResult_t r = ncclCommInitRank(&m->comm, world, id, rank);
+    const ncclResult_t r = nccl().CommInitRank(&m->comm, world, id, rank);
     if (r != ncclSuccess) {
-        report_error(__FILE__, __LINE__, ncclGetErrorString(r), (int)r);
+        report_error(__FILE__, __LINE__, nccl().GetErrorString(r), (int)r);
         m->comm = nullptr;
         return (int)r;
     }
@@ -1176,7 +1265,7 @@ int trba_dp_init(trba_model *m, const void *id128, int rank, int world) {
 int trba_dp_finalize(trba_model *m) {
     if (!m) return -1;
     if (m->comm) {
-        ncclCommDestroy(m->comm);
+        nccl().CommDestroy(m->comm);
         m->comm = nullptr;
     }
     m->world = 1;

@@ -11,50 +11,64 @@ namespace trba {
 namespace seq {
 namespace {
 
-__device__ __forceinline__ float sigm(float v) { return fdiv(1.0f, fadd(1.0f, expf(-v))); }
+__device__ __forceinline__ float sigm(float v) { return cr_sigmoid(v); }
 
 // ------------------------------------------------------------- sgemm --
 constexpr int TM = 64, TN = 64, TK = 16;
 
-__global__ void __launch_bounds__(256) sgemm_kernel(Gemm g) {
+__device__ __forceinline__ void gemm_store(const Gemm &g, int m, int n, double acc) {
+    float v = (float)acc;
+    float *c = g.C + (i64)m * g.ldc + n;
+    if (g.accumulate) v = fadd(v, *c);
+    if (g.bias) v = fadd(v, g.bias[n]);
+    *c = v;
+}
+
+// One 64x64 output tile over the K range of split blockIdx.z (f64 accumulation).
+__global__ void __launch_bounds__(256) sgemm_kernel(Gemm g, int kchunk) {
     __shared__ float sa[TK][TM + 1], sb[TK][TN + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < g.K; k0 += TK) {
+    const int kb = blockIdx.z * kchunk, ke = min(g.K, kb + kchunk);
+    double acc[4][4] = {};
+    for (int k0 = kb; k0 < ke; k0 += TK) {
         for (int e = threadIdx.x; e < TM * TK; e += 256) {
-            const int kk = e / TM, mm = e - kk * TM;  // consecutive threads walk m
-            const int m = m0 + mm, k = k0 + kk;
-            sa[kk][mm] = (m < g.M && k < g.K) ? g.A[(i64)m * g.sam + (i64)k * g.sak] : 0.0f;
-            const int nn = mm, n = n0 + nn;
-            sb[kk][nn] = (n < g.N && k < g.K) ? g.B[(i64)k * g.sbk + (i64)n * g.sbn] : 0.0f;
+            const int kk = e / TM, mm = e - kk * TM;  // consecutive threads walk m / n
+            const int m = m0 + mm, k = k0 + kk, n = n0 + mm;
+            sa[kk][mm] = (m < g.M && k < ke) ? g.A[(i64)m * g.sam + (i64)k * g.sak] : 0.0f;
+            sb[kk][mm] = (n < g.N && k < ke) ? g.B[(i64)k * g.sbk + (i64)n * g.sbn] : 0.0f;
         }
         __syncthreads();
 #pragma unroll
-        for (int kk = 0; kk < TK; ++kk)
+        for (int kk = 0; kk < TK; ++kk) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = (double)sa[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = (double)sb[kk][tx * 4 + j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(sa[kk][ty * 4 + i], sb[kk][tx * 4 + j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+        }
         __syncthreads();
     }
     for (int i = 0; i < 4; ++i)
         for (int j = 0; j < 4; ++j) {
             const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
             if (m >= g.M || n >= g.N) continue;
-            float v = g.alpha * acc[i][j];
-            float *c = g.C + (i64)m * g.ldc + n;
-            if (g.beta != 0.0f) v = fadd(v, g.beta * *c);
-            if (g.bias) v = fadd(v, g.bias[n]);
-            *c = v;
+            if (gridDim.z == 1) gemm_store(g, m, n, acc[i][j]);
+            else g.ws[((i64)blockIdx.z * g.M + m) * g.N + n] = acc[i][j];
         }
 }
 
-__global__ void col_sums_kernel(const float *X, int rows, int cols, i64 ld, float *out, int accumulate) {
-    GRID_LOOP(n, cols) {
-        float s = 0.0f;
-        for (int r = 0; r < rows; ++r) s = fadd(s, X[(i64)r * ld + n]);
-        out[n] = accumulate ? fadd(out[n], s) : s;
+// Sums the split partials in split order and stores.
+__global__ void sgemm_finish_kernel(Gemm g, int splits) {
+    GRID_LOOP(e, (i64)g.M * g.N) {
+        double acc = 0.0;
+        for (int s = 0; s < splits; ++s) acc += g.ws[(i64)s * g.M * g.N + e];
+        const int m = (int)(e / g.N), n = (int)(e - (i64)m * g.N);
+        gemm_store(g, m, n, acc);
     }
 }
 
@@ -82,18 +96,18 @@ __global__ void lstm_fwd_kernel(const float *xg, const float *b_ih, const float 
         for (int e = threadIdx.x; e < BG * G4; e += blockDim.x) {
             const int g = e / G4, o = e - g * G4, b = b0 + g;
             if (b >= B) continue;
-            float acc = 0.0f;
-            for (int k = 0; k < H; ++k) acc = fmaf(hb[g * H + k], wT[k * G4 + o], acc);
-            gb[e] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[((i64)b * T + tt) * G4 + o]), acc);
+            double acc = 0.0;
+            for (int k = 0; k < H; ++k) acc = fma((double)hb[g * H + k], (double)wT[k * G4 + o], acc);
+            gb[e] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[((i64)b * T + tt) * G4 + o]), (float)acc);
         }
         __syncthreads();
         for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
             const int g = e / H, i = e - g * H, b = b0 + g;
             if (b >= B) continue;
             const float *pg = gb + g * G4;
-            const float ig = sigm(pg[i]), fg = sigm(pg[H + i]), cg = tanhf(pg[2 * H + i]), og = sigm(pg[3 * H + i]);
+            const float ig = sigm(pg[i]), fg = sigm(pg[H + i]), cg = cr_tanhf(pg[2 * H + i]), og = sigm(pg[3 * H + i]);
             const float cn = fadd(fmul(fg, cb[e]), fmul(ig, cg));
-            const float hn = fmul(og, tanhf(cn));
+            const float hn = fmul(og, cr_tanhf(cn));
             const i64 r = (i64)b * T + tt;
             gates[r * G4 + i] = ig;
             gates[r * G4 + H + i] = fg;
@@ -130,7 +144,7 @@ __global__ void lstm_bwd_kernel(const float *dcat, const float *gates, const flo
             const i64 r = (i64)b * T + tt;
             const float ig = gates[r * G4 + i], fg = gates[r * G4 + H + i], cg = gates[r * G4 + 2 * H + i],
                         og = gates[r * G4 + 3 * H + i];
-            const float tc = tanhf(c_tr[r * H + i]);
+            const float tc = cr_tanhf(c_tr[r * H + i]);
             const float cp = s > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
             const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[e]);
             const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[e], fg));
@@ -146,9 +160,9 @@ __global__ void lstm_bwd_kernel(const float *dcat, const float *gates, const flo
         for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
             const int g = e / H, k = e - g * H;
             if (b0 + g >= B) continue;
-            float acc = 0.0f;
-            for (int o = 0; o < G4; ++o) acc = fmaf(dg[g * G4 + o], w[o * H + k], acc);
-            dhn[e] = acc;
+            double acc = 0.0;
+            for (int o = 0; o < G4; ++o) acc = fma((double)dg[g * G4 + o], (double)w[o * H + k], acc);
+            dhn[e] = (float)acc;
         }
         __syncthreads();
     }
@@ -179,58 +193,58 @@ __global__ void attn_fwd_kernel(AttnFwd a) {
     for (int st = 0; st < a.steps; ++st) {
         const i64 sb = (i64)st * a.B + b;
         for (int k = threadIdx.x; k < H; k += blockDim.x) {  // proj_hh = h2h(h), bias first
-            float acc = a.h2h_b[k];
-            for (int j = 0; j < H; ++j) acc = fadd(acc, fmul(h[j], h2hT[j * H + k]));
-            phh[k] = acc;
+            double acc = 0.0;
+            for (int j = 0; j < H; ++j) acc = fma((double)h[j], (double)h2hT[j * H + k], acc);
+            phh[k] = fadd((float)acc, a.h2h_b[k]);
         }
         __syncthreads();
         for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
             const int k = i % H;
-            const float v = tanhf(fadd(ph[i], phh[k]));
+            const float v = cr_tanhf(fadd(ph[i], phh[k]));
             tn[i] = v;
             a.tanh_tr[sb * T * H + i] = v;
         }
         __syncthreads();
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            float acc = 0.0f;
-            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(tn[t * H + k], a.score_w[k]));
-            e[t] = acc;
+            double acc = 0.0;
+            for (int k = 0; k < H; ++k) acc = fma((double)tn[t * H + k], (double)a.score_w[k], acc);
+            e[t] = (float)acc;
         }
         __syncthreads();
         if (threadIdx.x == 0) {  // softmax over T
             float mx = -INFINITY;
             for (int t = 0; t < T; ++t) mx = fmaxf(mx, e[t]);
-            float s = 0.0f;
+            double s = 0.0;
             for (int t = 0; t < T; ++t) {
-                al[t] = expf(fsub(e[t], mx));
-                s = fadd(s, al[t]);
+                al[t] = cr_expf(fsub(e[t], mx));
+                s += (double)al[t];
             }
-            for (int t = 0; t < T; ++t) al[t] = fdiv(al[t], s);
+            const float sf = (float)s;
+            for (int t = 0; t < T; ++t) al[t] = fdiv(al[t], sf);
         }
         __syncthreads();
         const int tok = a.text_in[(i64)b * a.steps + st];
         for (int k = threadIdx.x; k < H; k += blockDim.x) {
-            float acc = 0.0f;
-            for (int t = 0; t < T; ++t)
-                if (al[t] != 0.0f) acc = fadd(acc, fmul(al[t], bh[t * H + k]));
-            ctx[k] = acc;
+            double acc = 0.0;
+            for (int t = 0; t < T; ++t) acc = fma((double)al[t], (double)bh[t * H + k], acc);
+            ctx[k] = (float)acc;
         }
         for (int t = threadIdx.x; t < T; t += blockDim.x) a.alpha[sb * T + t] = al[t];
         __syncthreads();
         for (int i = threadIdx.x; i < CV; i += blockDim.x)
             a.cell_in[sb * CV + i] = i < H ? ctx[i] : (i - H == tok ? 1.0f : 0.0f);
         for (int o = threadIdx.x; o < G4; o += blockDim.x) {
-            float acc = fadd(a.b_ih[o], a.b_hh[o]);
-            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(ctx[k], wihT[k * G4 + o]));
-            acc = fadd(acc, a.w_ih[(i64)o * CV + H + tok]);
-            for (int k = 0; k < H; ++k) acc = fadd(acc, fmul(h[k], whhT[k * G4 + o]));
-            pre[o] = acc;
+            double dc = 0.0, dh = 0.0;
+            for (int k = 0; k < H; ++k) dc = fma((double)ctx[k], (double)wihT[k * G4 + o], dc);
+            for (int k = 0; k < H; ++k) dh = fma((double)h[k], (double)whhT[k * G4 + o], dh);
+            // (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h
+            pre[o] = fadd(fadd(fadd(fadd(a.b_ih[o], a.b_hh[o]), (float)dc), a.w_ih[(i64)o * CV + H + tok]), (float)dh);
         }
         __syncthreads();
         for (int i = threadIdx.x; i < H; i += blockDim.x) {
-            const float ig = sigm(pre[i]), fg = sigm(pre[H + i]), cg = tanhf(pre[2 * H + i]), og = sigm(pre[3 * H + i]);
+            const float ig = sigm(pre[i]), fg = sigm(pre[H + i]), cg = cr_tanhf(pre[2 * H + i]), og = sigm(pre[3 * H + i]);
             const float cn = fadd(fmul(fg, c[i]), fmul(ig, cg));
-            const float hn = fmul(og, tanhf(cn));
+            const float hn = fmul(og, cr_tanhf(cn));
             a.gates[sb * G4 + i] = ig;
             a.gates[sb * G4 + H + i] = fg;
             a.gates[sb * G4 + 2 * H + i] = cg;
@@ -270,7 +284,7 @@ __global__ void attn_bwd_kernel(AttnBwd a) {
         for (int i = threadIdx.x; i < H; i += blockDim.x) {
             const float *g = a.gates + sb * G4;
             const float ig = g[i], fg = g[H + i], cg = g[2 * H + i], og = g[3 * H + i];
-            const float tc = tanhf(a.cs[sb * H + i]);
+            const float tc = cr_tanhf(a.cs[sb * H + i]);
             const float cp = st > 0 ? a.cs[(sb - a.B) * H + i] : 0.0f;
             const float dh = fadd(a.d_out_hid[sb * H + i], dhn[i]);
             const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
@@ -283,30 +297,29 @@ __global__ void attn_bwd_kernel(AttnBwd a) {
         __syncthreads();
         for (int o = threadIdx.x; o < G4; o += blockDim.x) a.dgates[sb * G4 + o] = dg[o];
         for (int k = threadIdx.x; k < H; k += blockDim.x) {
-            float s1 = 0.0f, s2 = 0.0f;
+            double s1 = 0.0, s2 = 0.0;
             for (int o = 0; o < G4; ++o) {
-                const float dv = dg[o];
-                if (dv == 0.0f) continue;
-                s1 = fadd(s1, fmul(dv, wc[o * H + k]));
-                s2 = fadd(s2, fmul(dv, whh[o * H + k]));
+                const double dv = (double)dg[o];
+                s1 = fma(dv, (double)wc[o * H + k], s1);
+                s2 = fma(dv, (double)whh[o * H + k], s2);
             }
-            dctx[k] = s1;
-            dhp[k] = s2;
+            dctx[k] = (float)s1;
+            dhp[k] = (float)s2;
         }
         __syncthreads();
         const float *al = a.alpha + sb * T;
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            float s = 0.0f;
-            for (int k = 0; k < H; ++k) s = fadd(s, fmul(dctx[k], bh[t * H + k]));
-            da[t] = s;
+            double s = 0.0;
+            for (int k = 0; k < H; ++k) s = fma((double)dctx[k], (double)bh[t * H + k], s);
+            da[t] = (float)s;
             const float at = al[t];
             for (int k = 0; k < H; ++k) acc_bh[t * H + k] = fadd(acc_bh[t * H + k], fmul(at, dctx[k]));
         }
         __syncthreads();
         if (threadIdx.x == 0) {
-            float s = 0.0f;
-            for (int t = 0; t < T; ++t) s = fadd(s, fmul(al[t], da[t]));
-            *dot = s;
+            double s = 0.0;
+            for (int t = 0; t < T; ++t) s = fma((double)al[t], (double)da[t], s);
+            *dot = (float)s;
         }
         __syncthreads();
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
@@ -322,20 +335,19 @@ __global__ void attn_bwd_kernel(AttnBwd a) {
             acc_ph[i] = fadd(acc_ph[i], fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(tn[i], tn[i]))));
         }
         for (int k = threadIdx.x; k < H; k += blockDim.x) {
-            float s = 0.0f;
+            double s = 0.0;
             for (int t = 0; t < T; ++t) {
-                if (de[t] == 0.0f) continue;
                 const float v = tn[t * H + k];
-                s = fadd(s, fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(v, v))));
+                s += (double)fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(v, v)));
             }
-            dphh[k] = s;
+            dphh[k] = (float)s;
             a.dprojhh[sb * H + k] = s;
         }
         __syncthreads();
         for (int j = threadIdx.x; j < H; j += blockDim.x) {
-            float s = 0.0f;
-            for (int k = 0; k < H; ++k) s = fadd(s, fmul(dphh[k], h2h[k * H + j]));
-            dhn[j] = fadd(dhp[j], s);
+            double s = 0.0;
+            for (int k = 0; k < H; ++k) s = fma((double)dphh[k], (double)h2h[k * H + j], s);
+            dhn[j] = fadd(dhp[j], (float)s);
         }
         __syncthreads();
     }
@@ -362,14 +374,15 @@ __global__ void ce_rows_kernel(const float *logits, const int32_t *target, int B
     float mx = -INFINITY;
     for (int k = lane; k < V; k += 32) mx = fmaxf(mx, x[k]);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float s = 0.0f;
-    for (int k = lane; k < V; k += 32) s += expf(fsub(x[k], mx));
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    double sd = 0.0;
+    for (int k = lane; k < V; k += 32) sd += (double)cr_expf(fsub(x[k], mx));
+    for (int o = 16; o > 0; o >>= 1) sd += __shfl_xor_sync(0xffffffffu, sd, o);
+    const float s = (float)sd;
     for (int k = lane; k < V; k += 32) {
-        const float p = fdiv(expf(fsub(x[k], mx)), s);
+        const float p = fdiv(cr_expf(fsub(x[k], mx)), s);
         dr[k] = k == tgt ? fsub(p, 1.0f) : p;
     }
-    if (lane == 0) row_loss[warp] = -logf(fdiv(expf(fsub(x[tgt], mx)), s));
+    if (lane == 0) row_loss[warp] = -cr_logf(fdiv(cr_expf(fsub(x[tgt], mx)), s));
 }
 
 __device__ __forceinline__ double logadd(double a, double b) {
@@ -453,7 +466,7 @@ __global__ void ctc_kernel(const float *logits, const int32_t *tgt, const int32_
         double gam = 0.0;
         for (int s = 0; s < S; ++s)
             if (ext[s] == k) gam += exp(al[t * SS + s] + be[t * SS + s] + loss);
-        const double p = (double)expf(lp[i]);
+        const double p = (double)cr_expf(lp[i]);
         g[i] = fmul((float)((p - gam) * scale), cw);
     }
     if (threadIdx.x == 0) sample_loss[b] = loss / (double)L;
@@ -509,14 +522,38 @@ __global__ void scale_by_kernel(float *x, const float *s, i64 n) {
 
 void sgemm(const Gemm &g, cudaStream_t st) {
     if (g.M <= 0 || g.N <= 0) return;
-    dim3 grid((g.M + TM - 1) / TM, (g.N + TN - 1) / TN);
-    sgemm_kernel<<<grid, 256, 0, st>>>(g);
+    const int mt = (g.M + TM - 1) / TM, nt = (g.N + TN - 1) / TN;
+    // Split K until the grid covers two waves of SMs (chunks of >= 64).
+    int splits = 1;
+    if (g.ws && g.K > 128) {
+        const int want = (2 * sm_count() + mt * nt - 1) / (mt * nt);
+        const int maxs = (g.K + 63) / 64;
+        splits = want < maxs ? want : maxs;
+        if ((i64)splits * g.M * g.N > g.ws_elems) splits = (int)(g.ws_elems / ((i64)g.M * g.N));
+        if (splits < 1) splits = 1;
+    }
+    int kchunk = (g.K + splits - 1) / splits;
+    kchunk = (kchunk + TK - 1) / TK * TK;
+    splits = (g.K + kchunk - 1) / kchunk;
+    if (splits < 1) splits = 1;
+    sgemm_kernel<<<dim3(mt, nt, splits), 256, 0, st>>>(g, kchunk > 0 ? kchunk : TK);
     TRBA_LAUNCH_CHECK();
+    if (splits > 1) {
+        sgemm_finish_kernel<<<grid_for((i64)g.M * g.N), 256, 0, st>>>(g, splits);
+        TRBA_LAUNCH_CHECK();
+    }
 }
 
-void col_sums(const float *X, int rows, int cols, i64 ld, float *out, bool accumulate, cudaStream_t st) {
-    col_sums_kernel<<<grid_for(cols, 128), 128, 0, st>>>(X, rows, cols, ld, out, accumulate ? 1 : 0);
-    TRBA_LAUNCH_CHECK();
+void col_sums(const float *X, int rows, int cols, i64 ld, const float *ones, float *out, bool accumulate, double *ws,
+              i64 ws_elems, cudaStream_t st) {
+    Gemm g;
+    g.M = 1, g.N = cols, g.K = rows;
+    g.A = ones, g.sam = 0, g.sak = 1;
+    g.B = X, g.sbk = ld, g.sbn = 1;
+    g.C = out, g.ldc = cols;
+    g.accumulate = accumulate;
+    g.ws = ws, g.ws_elems = ws_elems;
+    sgemm(g, st);
 }
 
 static void set_smem(const void *fn, size_t bytes) {

@@ -10,9 +10,12 @@
 namespace trba {
 namespace seq {
 
-// C[m, n] = alpha * sum_k A(m, k) B(k, n) + beta * C[m, n] + bias[n], with
+// C[m, n] = (float)(sum_k A(m, k) B(k, n)) [+ C[m, n] if accumulate] [+ bias[n]],
 // A(m, k) = A[m*sam + k*sak], B(k, n) = B[k*sbk + n*sbn], C[m*ldc + n].
-// Summation over k in order (deterministic).  alpha_dev, if set, multiplies alpha.
+// The sum is accumulated in f64 and rounded once (the correctly rounded dot
+// product in practice), so the result does not depend on the summation
+// order; long K is split over CTAs through the f64 workspace `ws` and the
+// partial sums are combined in a fixed order (deterministic).
 struct Gemm {
     int M, N, K;
     const float *A;
@@ -21,12 +24,12 @@ struct Gemm {
     i64 sbk, sbn;
     float *C;
     i64 ldc;
-    float alpha = 1.0f, beta = 0.0f;
+    bool accumulate = false;
     const float *bias = nullptr;
+    double *ws = nullptr;   // split-K workspace (may be null: no split)
+    i64 ws_elems = 0;
 };
 void sgemm(const Gemm &g, cudaStream_t st);
-// out[n] (+)= sum over rows of X[r*ld + n] (column sums, rows in order).
-void col_sums(const float *X, int rows, int cols, i64 ld, float *out, bool accumulate, cudaStream_t st);
 
 // One LSTM direction over all T slots (src/rnn.rs:107-166).  xg = x W_ih^T
 // [B, T, 4H]; writes gates (post-activation) and c [B, T, .], h into
@@ -71,6 +74,10 @@ void ce_rows(const float *logits, const int32_t *target, int B, int steps, int V
 // lengths ctc_len [B]; grad already multiplied by cw.
 void ctc(const float *logits, const int32_t *ctc_tgt, const int32_t *ctc_len, int Lmax, int B, int T, int V,
          float cw, float *grad, double *sample_loss, cudaStream_t st);
+// Column sums of X [rows, cols] (row stride ld) through sgemm with a ones
+// vector `ones` (length >= rows): out[n] (+)= sum_r X[r*ld + n].
+void col_sums(const float *X, int rows, int cols, i64 ld, const float *ones, float *out, bool accumulate,
+              double *ws, i64 ws_elems, cudaStream_t st);
 // Totals: attn = sum(row_loss)/count, ctc = sum(sample_loss)/n, loss =
 // (1-cw) attn + cw ctc into out[0..2]; scales d_logits by (1-cw)/count.
 void loss_finalize(const float *row_loss, const int32_t *target, int B, int steps, int pad, const double *sample_loss,

@@ -116,6 +116,11 @@ class QatModel:
         self._check(self.L.trba_model_get_running_stats(self.h, _ptr(out), n), "running_stats")
         return out
 
+    def debug_tensor(self, name: str, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self._check(self.L.trba_model_debug_tensor(self.h, name.encode(), _ptr(out), n), f"debug_tensor({name})")
+        return out
+
     def forward_backward(self, img, text_in, target, ctc_tgt, ctc_len, stream=None):
         b = int(img.shape[0])
         self._check(self.L.trba_model_forward_backward(self.h, _ptr(img), _ptr(text_in), _ptr(target), _ptr(ctc_tgt),
