@@ -23,6 +23,17 @@ void trba_gemm_int8_simt(const int8_t *a, const int8_t *b, int32_t *c, int m, in
 void trba_gemm_int8_splitk(const int8_t *a, const int8_t *b, int32_t *c, int m, int n, int k, int splits,
                            void *stream);
 
+/* C[M,N] = A[M,K] . B[K,N] (fp32, row-major, compact C; the contract of
+ * launch_gemm_fp32) with f64 accumulation and split-K, allocating nothing:
+ * its split-K scratch is a static 8 MiB device array.  For callers that may
+ * not allocate device memory (plugins whose host owns every allocation,
+ * loops where cudaMalloc would synchronise the device).  At most 131072
+ * outputs (M*N) per call, larger calls return -1 with an error.  The first
+ * call on a device looks up the array's address: make it before any stream
+ * capture.  All calls share the array, so calls overlapping on the GPU race.
+ * No counterpart in the reference's ABI.  Returns 0 or an error code. */
+int trba_sgemm_exact_noalloc(const float *a, const float *b, float *c, int m, int n, int k, void *stream);
+
 /* Number of kernels this library has launched so far (every launch site
  * counts itself), for reporting launches per step. */
 long long trba_launch_count(void);

@@ -621,3 +621,72 @@ void loss_finalize(const float *row_loss, const int32_t *target, int B, int step
 
 }  // namespace seq
 }  // namespace trba
+
+// ---------------------------------------------------------------------------
+// GEMM entry point that allocates nothing.
+//
+// Some callers cannot call cudaMalloc: plugins whose host framework owns every
+// device allocation, or latency-critical loops in which cudaMalloc / cudaFree
+// would synchronise the device.  trba_sgemm_exact_noalloc gives them the
+// f64-accumulated, split-K fp32 GEMM of the training step without any
+// allocation: the split-K partial sums live in the file-scope array below.
+//
+// Limits and behaviour:
+//   * the scratch array holds kNoAllocScratch doubles (8 MiB); every GPU that
+//     loads this library keeps it for the life of the process;
+//   * at most kNoAllocMaxOut = M*N outputs per call; larger calls are
+//     rejected with an error (nothing is launched);
+//   * the first call on a device looks up the array's device address
+//     (cudaGetSymbolAddress, with that device current) — make that first call
+//     before any stream capture;
+//   * every call shares the one array and finds the previous call's partial
+//     sums in it; each call overwrites every element it later reads, so no
+//     clearing is needed, but calls that overlap on the GPU (different
+//     streams, different host threads) race on the array and must be
+//     serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr long long kNoAllocScratch = 1LL << 20;  // doubles
+constexpr long long kNoAllocMaxOut = 1LL << 17;   // M * N
+
+__device__ __align__(256) double g_noalloc_scratch[kNoAllocScratch];
+
+double *g_noalloc_ptr[64] = {};
+
+}  // namespace
+
+extern "C" int trba_sgemm_exact_noalloc(const float *a, const float *b, float *c, int m, int n, int k, void *stream) {
+    using namespace trba;
+    if (m <= 0 || n <= 0 || k <= 0) return 0;
+    if ((long long)m * n > kNoAllocMaxOut) {
+        report_error(__FILE__, __LINE__,
+                     "trba_sgemm_exact_noalloc: M*N exceeds the 131072 outputs its static scratch supports", -1);
+        return -1;
+    }
+    int dev = 0;
+    const cudaError_t de = cudaGetDevice(&dev);
+    if (de != cudaSuccess || dev < 0 || dev >= 64) {
+        report_error(__FILE__, __LINE__, "trba_sgemm_exact_noalloc: no current device", (int)de);
+        return de != cudaSuccess ? (int)de : -1;
+    }
+    if (!g_noalloc_ptr[dev]) {  // once per device, with that device current
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            report_error(__FILE__, __LINE__, "trba_sgemm_exact_noalloc: cudaGetSymbolAddress failed", (int)e);
+            return e != cudaSuccess ? (int)e : -1;
+        }
+        g_noalloc_ptr[dev] = static_cast<double *>(p);
+    }
+    seq::Gemm g;
+    g.M = m, g.N = n, g.K = k;
+    g.A = a, g.sam = k, g.sak = 1;  // A [M, K] row-major
+    g.B = b, g.sbk = n, g.sbn = 1;  // B [K, N] row-major
+    g.C = c, g.ldc = n;             // C [M, N] compact
+    g.ws = g_noalloc_ptr[dev];
+    g.ws_elems = kNoAllocScratch;
+    seq::sgemm(g, as_stream(stream));
+    const cudaError_t le = cudaGetLastError();
+    return le == cudaSuccess ? 0 : (int)le;
+}
