@@ -34,6 +34,52 @@ __global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restr
     }
 }
 
+// The same operand, 16 bytes per thread: thread u covers row u / G and the
+// bytes [16 g, 16 g + 16) of it (G = col_ld / 16), written with one 16-byte
+// store, so a warp writes 512 contiguous bytes.  A table in shared memory
+// gives every column k = (c, kh, kw) its input offset c*H*W + kh*W + kw and
+// its (kh, kw), so the gather itself does no divisions.
+constexpr int kIm2colMaxLd = 6144;  // table of col_ld int2 entries: 48 KB
+
+__global__ void __launch_bounds__(256) im2col16_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
+                                                       int C, int H, int W, int kH, int kW, int sH, int sW, int pH,
+                                                       int pW, int Ho, int Wo, int col_ld, i64 rows, i64 units) {
+    extern __shared__ int2 ktab[];
+    const int cols = C * kH * kW, khw = kH * kW;
+    for (int k = threadIdx.x; k < col_ld; k += blockDim.x) {
+        if (k < cols) {
+            const int c = k / khw, kk = k - c * khw, kh = kk / kW, kw = kk - kh * kW;
+            ktab[k] = make_int2(c * H * W + kh * W + kw, (kh << 16) | kw);
+        } else {
+            ktab[k] = make_int2(-1, 0);
+        }
+    }
+    __syncthreads();
+    const int G = col_ld >> 4;
+    const i64 hwo = (i64)Ho * Wo, chw = (i64)C * H * W;
+    for (i64 u = (i64)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (i64)gridDim.x * blockDim.x) {
+        const i64 r = u / G;
+        const int g = (int)(u - r * G);
+        uint32_t w4[4] = {0u, 0u, 0u, 0u};
+        if (r < rows) {
+            const i64 b = r / hwo;
+            const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
+            const int ih0 = oh * sH - pH, iw0 = ow * sW - pW;
+            const i64 base = b * chw + (i64)ih0 * W + iw0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int2 t = ktab[g * 16 + j];
+                const int ih = ih0 + (t.y >> 16), iw = iw0 + (t.y & 0xffff);
+                uint32_t v = 0;
+                if (t.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
+                    v = (uint8_t)in[base + t.x];
+                w4[j >> 2] |= v << (8 * (j & 3));
+            }
+        }
+        *reinterpret_cast<uint4 *>(col + r * col_ld + g * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+}
+
 __global__ void im2col_f32_kernel(const int8_t *__restrict__ in, float *__restrict__ col, int C,
                                   int H, int W, int kH, int kW, int sH, int sW, int pH, int pW,
                                   int Ho, int Wo, i64 total) {
@@ -207,8 +253,14 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
     const i64 rows = (i64)batch * Ho * Wo;
     if (col_ld < cols || (col_ld & 15) || rows <= 0) return;
     const i64 total = ((rows + 15) / 16 * 16) * col_ld;
-    im2col_pad_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(
-        input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, total);
+    if (col_ld <= kIm2colMaxLd && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {
+        const i64 units = total / 16;
+        im2col16_kernel<<<grid_for(units), kThreads, sizeof(int2) * col_ld, as_stream(s)>>>(
+            input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, units);
+    } else {
+        im2col_pad_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(
+            input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, total);
+    }
     TRBA_LAUNCH_CHECK();
 }
 

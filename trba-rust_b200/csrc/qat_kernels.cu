@@ -341,35 +341,72 @@ __global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const f
     GRID_LOOP(i, n) g[i] = fadd(g[i], fmul((float)acc[i], deq));
 }
 
-__global__ void dgrad_kernel(const float *go, const int8_t *wq, i64 w_ld, const float *w_s, int B, int Cin, int H,
-                             int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
-                             const int8_t *mask_q, const float *add, float *gi) {
+// Input gradient (src/qnet.rs:1068-1080 -> launch_conv_backward_grad_input_i8),
+// 8 input channels per thread: the 8 outputs of one input pixel share every
+// dy load, and their int8 weights (as f32) sit in shared memory as
+// [tap][oc][8], read as two broadcast float4 per (tap, oc).  Each output is
+// still accumulated in the reference's order — taps (kh, kw) outer, output
+// channels inner, one f32 multiply and one f32 add per term — then scaled by
+// w_s, so the result is bit-identical to the reference's gather.
+constexpr int kDgradCi = 8;
+
+__global__ void __launch_bounds__(256) dgrad_ci8_kernel(const float *__restrict__ go, const int8_t *__restrict__ wq,
+                                                        i64 w_ld, const float *__restrict__ w_s, int B, int Cin, int H,
+                                                        int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW,
+                                                        int Ho, int Wo, const int8_t *__restrict__ mask_q,
+                                                        const float *__restrict__ add, float *__restrict__ gi) {
+    extern __shared__ float4 wsm4[];  // [taps][Cout][2] float4
+    const int khw = kH * kW, ci0 = blockIdx.y * kDgradCi;
+    for (int e = threadIdx.x; e < khw * Cout * kDgradCi; e += blockDim.x) {
+        const int j = e % kDgradCi, oc = (e / kDgradCi) % Cout, t = e / (kDgradCi * Cout);
+        const int ci = ci0 + j;
+        reinterpret_cast<float *>(wsm4)[e] = ci < Cin ? (float)wq[(i64)oc * w_ld + (i64)ci * khw + t] : 0.0f;
+    }
+    __syncthreads();
     const int hwo = Ho * Wo, hwi = H * W;
-    const float ws = *w_s;
-    GRID_LOOP(i, (i64)B * Cin * hwi) {
-        const i64 bc = i / hwi;
-        const int pix = (int)(i - bc * hwi);
-        const int b = (int)(bc / Cin), ci = (int)(bc - (i64)b * Cin);
-        const int ih = pix / W, iw = pix - ih * W;
-        const float *go_b = go + (i64)b * Cout * hwo;
-        float acc = 0.0f;
-        for (int kh = 0; kh < kH; ++kh) {
-            const int nh = ih + pH - kh;
-            if (nh < 0 || nh % sH) continue;
-            const int oh = nh / sH;
-            if (oh >= Ho) continue;
-            for (int kw = 0; kw < kW; ++kw) {
-                const int nw = iw + pW - kw;
-                if (nw < 0 || nw % sW) continue;
-                const int ow = nw / sW;
-                if (ow >= Wo) continue;
-                const i64 wc = (i64)(ci * kH + kh) * kW + kw;
-                const float *gp = go_b + oh * Wo + ow;
-                for (int oc = 0; oc < Cout; ++oc)
-                    acc = fadd(acc, fmul(gp[(i64)oc * hwo], (float)wq[(i64)oc * w_ld + wc]));
+    const i64 npix = (i64)B * hwi;
+    const i64 pix = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+    if (pix >= npix) return;
+    const int b = (int)(pix / hwi), rem = (int)(pix - (i64)b * hwi);
+    const int ih = rem / W, iw = rem - ih * W;
+    const float *go_b = go + (i64)b * Cout * hwo;
+    float acc[kDgradCi];
+#pragma unroll
+    for (int j = 0; j < kDgradCi; ++j) acc[j] = 0.0f;
+    for (int kh = 0; kh < kH; ++kh) {
+        const int nh = ih + pH - kh;
+        if (nh < 0 || nh % sH) continue;
+        const int oh = nh / sH;
+        if (oh >= Ho) continue;
+        for (int kw = 0; kw < kW; ++kw) {
+            const int nw = iw + pW - kw;
+            if (nw < 0 || nw % sW) continue;
+            const int ow = nw / sW;
+            if (ow >= Wo) continue;
+            const float *gp = go_b + oh * Wo + ow;
+            const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * 2;
+#pragma unroll 4
+            for (int oc = 0; oc < Cout; ++oc) {
+                const float d = gp[(i64)oc * hwo];
+                const float4 w0 = wt[2 * oc], w1 = wt[2 * oc + 1];
+                acc[0] = fadd(acc[0], fmul(d, w0.x));
+                acc[1] = fadd(acc[1], fmul(d, w0.y));
+                acc[2] = fadd(acc[2], fmul(d, w0.z));
+                acc[3] = fadd(acc[3], fmul(d, w0.w));
+                acc[4] = fadd(acc[4], fmul(d, w1.x));
+                acc[5] = fadd(acc[5], fmul(d, w1.y));
+                acc[6] = fadd(acc[6], fmul(d, w1.z));
+                acc[7] = fadd(acc[7], fmul(d, w1.w));
             }
         }
-        float v = fmul(acc, ws);
+    }
+    const float ws = *w_s;
+#pragma unroll
+    for (int j = 0; j < kDgradCi; ++j) {
+        const int ci = ci0 + j;
+        if (ci >= Cin) break;
+        const i64 i = ((i64)b * Cin + ci) * hwi + rem;
+        float v = fmul(acc[j], ws);
         if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
         if (add) v = fadd(v, add[i]);
         gi[i] = v;
@@ -516,8 +553,18 @@ void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n,
 void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B, int Cin, int H, int W, int Cout,
            int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, const int8_t *mask_q, const float *add,
            float *gi, cudaStream_t st) {
-    const i64 n = (i64)B * Cin * H * W;
-    dgrad_kernel<<<grid_for(n), 256, 0, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
+    const i64 npix = (i64)B * H * W;
+    const size_t smem = sizeof(float) * (size_t)kh * kw * Cout * kDgradCi;
+    TRBA_REQUIRE(smem <= 200 * 1024, "dgrad: kernel taps x output channels too large for shared memory");
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
+        TRBA_CHECK(cudaFuncSetAttribute(dgrad_ci8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr[dev] = true;
+    }
+    dim3 grid((unsigned)((npix + 255) / 256), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
+    dgrad_ci8_kernel<<<grid, 256, smem, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
                                               mask_q, add, gi);
     TRBA_LAUNCH_CHECK();
 }

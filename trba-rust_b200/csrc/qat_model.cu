@@ -139,6 +139,17 @@ struct RnnL {
     Ref<float> cat, y, dcat, dx;
 };
 
+// Kernel probe: CUDA events around every launch of one kernel family, on
+// the stream the step runs on, so that a timed loop can report that family's
+// device time per launch live (trba_model_probe / trba_model_probe_read).
+struct Probe {
+    int kind = -1;
+    std::vector<cudaEvent_t> ev;  // start/stop pairs
+    size_t used = 0;
+    double work = 0.0;  // algorithmic ops (GEMMs) or bytes (gathers) of the timed launches
+    long long launches = 0;
+};
+
 }  // namespace
 
 struct trba_model {
@@ -189,6 +200,7 @@ struct trba_model {
     ncclComm_t comm = nullptr;
     int world = 1;
     cudaEvent_t ev = nullptr;
+    Probe probe;
 };
 
 namespace {
@@ -668,6 +680,33 @@ struct Ctx {
     float *P, *G;
 };
 
+struct ProbeScope {
+    Probe *p = nullptr;
+    cudaStream_t st;
+    ProbeScope(trba_model *m, int kind, double work, cudaStream_t s) : st(s) {
+        if (m->probe.kind != kind) return;
+        p = &m->probe;
+        while (p->ev.size() < p->used + 2) {
+            cudaEvent_t e;
+            TRBA_CHECK(cudaEventCreate(&e));
+            p->ev.push_back(e);
+        }
+        TRBA_CHECK(cudaEventRecord(p->ev[p->used], st));
+        p->work += work;
+        p->launches += 1;
+    }
+    ~ProbeScope() {
+        if (!p) return;
+        TRBA_CHECK(cudaEventRecord(p->ev[p->used + 1], st));
+        p->used += 2;
+    }
+};
+
+void sgemm(Ctx &c, const seq::Gemm &g, cudaStream_t st) {
+    ProbeScope ps(c.m, TRBA_PROBE_SGEMM, 2.0 * g.M * g.N * g.K, st);
+    seq::sgemm(g, st);
+}
+
 void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     const int B = c.B;
     const i64 rows = L.rows(B);
@@ -675,9 +714,12 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     L.s_in = s_in;
     launch_im2col_pad(q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo, L.kp,
                       c.st);
-    if (!gemm_i8_conv_f32(L.col.get(), L.kp, L.wq.get(), L.kp, (int)rows, L.cout, L.K, L.x.get(), s_in, L.ws.get(),
-                          L.bn_acc.get(), L.Ho * L.Wo, c.st))
-        report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
+    {
+        ProbeScope ps(c.m, TRBA_PROBE_CONV_GEMM, 2.0 * rows * L.cout * L.K, c.st);
+        if (!gemm_i8_conv_f32(L.col.get(), L.kp, L.wq.get(), L.kp, (int)rows, L.cout, L.K, L.x.get(), s_in,
+                              L.ws.get(), L.bn_acc.get(), L.Ho * L.Wo, c.st))
+            report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
+    }
     if (c.m->cfg.wgrad_mode == 1)
         qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
                       (int)a16l(rows), c.st);
@@ -718,12 +760,21 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
                      L.dxmax.get(), L.s_dx.get(), L.A.get(), compat ? (int)rows : (int)rp, compat, c.st);
     const int splits = splitk_for(L.cout, L.K, (int)rows);
     const int8_t *Bop = compat ? L.col.get() : L.colT.get();
-    if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits, c.st))
-        report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
+    {
+        ProbeScope ps(c.m, TRBA_PROBE_WGRAD_GEMM, 2.0 * rows * L.cout * L.K, c.st);
+        if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits,
+                                   c.st))
+            report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
+    }
     qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, c.st);
-    if (gi)
+    if (gi) {
+        const double in_n = (double)B * L.cin * L.H * L.W;
+        const double bytes = 4.0 * B * L.cout * HW + 4.0 * in_n + (mask_q ? in_n : 0.0) + (add ? 4.0 * in_n : 0.0) +
+                             (double)L.cout * L.K;
+        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, bytes, c.st);
         qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
                    L.Ho, L.Wo, mask_q, add, gi, c.st);
+    }
 }
 
 void cnn_forward(Ctx &c, const int8_t *img) {
@@ -830,17 +881,17 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
     const float *x = m->feat.get();
     for (auto &r : m->rnn) {  // BiLstmLayer::forward (src/rnn.rs:167-174)
         for (int d = 0; d < 2; ++d) {
-            seq::sgemm(gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
+            sgemm(c, gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
             seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
                           r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
         }
-        seq::sgemm(gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
+        sgemm(c, gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
                    c.st);
         x = r.y.get();
     }
     const float *enc = x;  // [B, T, H]
     const i64 oi2h = entry_off(m, "attn.i2h.w");
-    seq::sgemm(gemm(m, B * T, H, H, enc, H, 1, c.P + oi2h, 1, H, m->proj_h.get(), H), c.st);
+    sgemm(c, gemm(m, B * T, H, H, enc, H, 1, c.P + oi2h, 1, H, m->proj_h.get(), H), c.st);
     seq::AttnFwd a{};
     a.bh = enc;
     a.proj_h = m->proj_h.get();
@@ -860,10 +911,10 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
     a.hs = m->hs.get();
     a.cs = m->cs.get();
     seq::attn_fwd(a, c.st);
-    seq::sgemm(gemm(m, S * B, V, H, m->hs.get(), H, 1, c.P + entry_off(m, "attn.gen.w"), 1, H, m->logits.get(), V, 0.0f,
+    sgemm(c, gemm(m, S * B, V, H, m->hs.get(), H, 1, c.P + entry_off(m, "attn.gen.w"), 1, H, m->logits.get(), V, 0.0f,
                     c.P + entry_off(m, "attn.gen.b")),
                c.st);
-    seq::sgemm(gemm(m, B * T, V, H, enc, H, 1, c.P + entry_off(m, "ctc.w"), 1, H, m->ctc_logits.get(), V, 0.0f,
+    sgemm(c, gemm(m, B * T, V, H, enc, H, 1, c.P + entry_off(m, "ctc.w"), 1, H, m->ctc_logits.get(), V, 0.0f,
                     c.P + entry_off(m, "ctc.b")),
                c.st);
     seq::ce_rows(m->logits.get(), target, B, S, V, cf.pad, m->dlogits.get(), m->row_loss.get(), c.st);
@@ -880,9 +931,9 @@ void head_backward(Ctx &c) {
     const float *enc = m->rnn.back().y.get();
     const i64 ogw = entry_off(m, "attn.gen.w"), ogb = entry_off(m, "attn.gen.b");
     // generator (src/attn.rs:274-284)
-    seq::sgemm(gemm(m, V, H, R, m->dlogits.get(), 1, V, m->hs.get(), H, 1, c.G + ogw, H, true), c.st);
+    sgemm(c, gemm(m, V, H, R, m->dlogits.get(), 1, V, m->hs.get(), H, 1, c.G + ogw, H, true), c.st);
     colsum(m, m->dlogits.get(), R, V, V, c.G + ogb, c.st);
-    seq::sgemm(gemm(m, R, H, V, m->dlogits.get(), V, 1, c.P + ogw, H, 1, m->d_out_hid.get(), H), c.st);
+    sgemm(c, gemm(m, R, H, V, m->dlogits.get(), V, 1, c.P + ogw, H, 1, m->d_out_hid.get(), H), c.st);
     seq::AttnBwd a{};
     a.d_out_hid = m->d_out_hid.get();
     a.bh = enc;
@@ -903,47 +954,47 @@ void head_backward(Ctx &c) {
     seq::attn_bwd(a, c.st);
     const int CV = H + V;
     float *dg = m->adg.get();
-    seq::sgemm(gemm(m, 4 * H, CV, R, dg, 1, 4 * H, m->cell_in.get(), CV, 1, c.G + entry_off(m, "attn.w_ih"), CV, true),
+    sgemm(c, gemm(m, 4 * H, CV, R, dg, 1, 4 * H, m->cell_in.get(), CV, 1, c.G + entry_off(m, "attn.w_ih"), CV, true),
                c.st);
     colsum(m, dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_ih"), c.st);
     colsum(m, dg, R, 4 * H, 4 * H, c.G + entry_off(m, "attn.b_hh"), c.st);
     // w_hh and h2h: h_prev of step st is hs of st-1 (zero at st = 0)
-    seq::sgemm(gemm(m, 4 * H, H, R - B, dg + (i64)B * 4 * H, 1, 4 * H, m->hs.get(), H, 1,
+    sgemm(c, gemm(m, 4 * H, H, R - B, dg + (i64)B * 4 * H, 1, 4 * H, m->hs.get(), H, 1,
                     c.G + entry_off(m, "attn.w_hh"), H, true),
                c.st);
-    seq::sgemm(gemm(m, H, H, R - B, m->adprojhh.get() + (i64)B * H, 1, H, m->hs.get(), H, 1,
+    sgemm(c, gemm(m, H, H, R - B, m->adprojhh.get() + (i64)B * H, 1, H, m->hs.get(), H, 1,
                     c.G + entry_off(m, "attn.h2h.w"), H, true),
                c.st);
     colsum(m, m->adprojhh.get(), R, H, H, c.G + entry_off(m, "attn.h2h.b"), c.st);
-    seq::sgemm(gemm(m, 1, H, R * T, m->ade.get(), 0, 1, m->tanh_tr.get(), H, 1, c.G + entry_off(m, "attn.score.w"), H,
+    sgemm(c, gemm(m, 1, H, R * T, m->ade.get(), 0, 1, m->tanh_tr.get(), H, 1, c.G + entry_off(m, "attn.score.w"), H,
                     true),
                c.st);
     const i64 oi2h = entry_off(m, "attn.i2h.w");
-    seq::sgemm(gemm(m, H, H, B * T, m->d_proj_h.get(), 1, H, enc, H, 1, c.G + oi2h, H, true), c.st);
-    seq::sgemm(gemm(m, B * T, H, H, m->d_proj_h.get(), H, 1, c.P + oi2h, H, 1, m->d_bh.get(), H, true), c.st);
+    sgemm(c, gemm(m, H, H, B * T, m->d_proj_h.get(), 1, H, enc, H, 1, c.G + oi2h, H, true), c.st);
+    sgemm(c, gemm(m, B * T, H, H, m->d_proj_h.get(), H, 1, c.P + oi2h, H, 1, m->d_bh.get(), H, true), c.st);
     // CTC head (src/main.rs:2344): LinearF backward
     const i64 ocw = entry_off(m, "ctc.w"), ocb = entry_off(m, "ctc.b");
-    seq::sgemm(gemm(m, V, H, B * T, m->dctc.get(), 1, V, enc, H, 1, c.G + ocw, H, true), c.st);
+    sgemm(c, gemm(m, V, H, B * T, m->dctc.get(), 1, V, enc, H, 1, c.G + ocw, H, true), c.st);
     colsum(m, m->dctc.get(), B * T, V, V, c.G + ocb, c.st);
-    seq::sgemm(gemm(m, B * T, H, V, m->dctc.get(), V, 1, c.P + ocw, H, 1, m->d_bh.get(), H, true), c.st);
+    sgemm(c, gemm(m, B * T, H, V, m->dctc.get(), V, 1, c.P + ocw, H, 1, m->d_bh.get(), H, true), c.st);
     // BiLSTM backward, top layer first (src/rnn.rs:176-198)
     const float *dy = m->d_bh.get();
     for (int li = (int)m->rnn.size() - 1; li >= 0; --li) {
         RnnL &r = m->rnn[li];
         const float *xin = li == 0 ? m->feat.get() : m->rnn[li - 1].y.get();
-        seq::sgemm(gemm(m, H, 2 * H, B * T, dy, 1, H, r.cat.get(), 2 * H, 1, c.G + r.pw, 2 * H, true), c.st);
+        sgemm(c, gemm(m, H, 2 * H, B * T, dy, 1, H, r.cat.get(), 2 * H, 1, c.G + r.pw, 2 * H, true), c.st);
         colsum(m, dy, B * T, H, H, c.G + r.pb, c.st);
-        seq::sgemm(gemm(m, B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
+        sgemm(c, gemm(m, B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
         float *dxout = li == 0 ? m->dfeat.get() : r.dx.get();
         for (int d = 0; d < 2; ++d) {
             seq::lstm_bwd(r.dcat.get(), r.gates[d].get(), r.c[d].get(), c.P + r.whh[d], B, T, H, d, d, r.dg[d].get(),
                           c.st);
             const float *g = r.dg[d].get();
-            seq::sgemm(gemm(m, 4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, true), c.st);
-            seq::sgemm(gemm(m, 4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, true), c.st);
+            sgemm(c, gemm(m, 4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, true), c.st);
+            sgemm(c, gemm(m, 4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, true), c.st);
             colsum(m, g, B * T, 4 * H, 4 * H, c.G + r.bih[d], c.st);
             colsum(m, g, B * T, 4 * H, 4 * H, c.G + r.bhh[d], c.st);
-            seq::sgemm(gemm(m, B * T, r.D, 4 * H, g, 4 * H, 1, c.P + r.wih[d], r.D, 1, dxout, r.D, d != 0),
+            sgemm(c, gemm(m, B * T, r.D, 4 * H, g, 4 * H, 1, c.P + r.wih[d], r.D, 1, dxout, r.D, d != 0),
                        c.st);
         }
         dy = dxout;
@@ -1070,6 +1121,7 @@ void trba_model_destroy(trba_model *m) {
     cudaFree(m->d_mat);
     cudaFree(m->d_conv);
     if (m->ev) cudaEventDestroy(m->ev);
+    for (cudaEvent_t e : m->probe.ev) cudaEventDestroy(e);
     delete m;
 }
 
@@ -1227,6 +1279,31 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
     if (!src || cnt != n) return -2;
     TRBA_CHECK(cudaDeviceSynchronize());
     TRBA_CHECK(cudaMemcpy(host, src, n * 4, cudaMemcpyDeviceToHost));
+    return cuda_status();
+}
+
+int trba_model_probe(trba_model *m, int kind) {
+    if (!m || kind < -1 || kind > TRBA_PROBE_SGEMM) return -1;
+    m->probe.kind = kind;
+    m->probe.used = 0;
+    m->probe.work = 0.0;
+    m->probe.launches = 0;
+    return 0;
+}
+
+int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *work) {
+    if (!m || !ms_total || !launches || !work) return -1;
+    auto &p = m->probe;
+    double ms = 0.0;
+    if (p.used) TRBA_CHECK(cudaEventSynchronize(p.ev[p.used - 1]));
+    for (size_t i = 0; i + 1 < p.used; i += 2) {
+        float t = 0.0f;
+        TRBA_CHECK(cudaEventElapsedTime(&t, p.ev[i], p.ev[i + 1]));
+        ms += t;
+    }
+    *ms_total = ms;
+    *launches = p.launches;
+    *work = p.work;
     return cuda_status();
 }
 

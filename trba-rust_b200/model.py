@@ -153,6 +153,18 @@ class QatModel:
     def loss_dev_ptr(self) -> int:
         return C.cast(self.L.trba_model_loss_dev(self.h), C.c_void_p).value
 
+    PROBE_CONV_GEMM, PROBE_WGRAD_GEMM, PROBE_DGRAD, PROBE_SGEMM = 0, 1, 2, 3
+
+    def probe(self, kind: int):
+        """Bracket every launch of one kernel family with CUDA events (-1 = off)."""
+        self._check(self.L.trba_model_probe(self.h, kind), "probe")
+
+    def probe_read(self):
+        """(device ms summed over the probed launches, launches, algorithmic work)."""
+        ms, n, work = C.c_double(), C.c_longlong(), C.c_double()
+        self._check(self.L.trba_model_probe_read(self.h, C.byref(ms), C.byref(n), C.byref(work)), "probe_read")
+        return ms.value, n.value, work.value
+
     def dp_init(self, id128: bytes, rank: int, world: int):
         buf = C.create_string_buffer(id128, 128)
         self._check(self.L.trba_dp_init(self.h, buf, rank, world), "dp_init")
