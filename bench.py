@@ -153,6 +153,51 @@ def reference_arm(args):
 
 
 # ------------------------------------------------------------------ ours --
+def measured_peaks() -> dict:
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def int8_gemm_peak(dev) -> float:
+    """cuBLAS int8 GEMM throughput (TOP/s) at 8192^3 on this GPU: the
+    measured denominator of the int8 tensor-core roofline."""
+    import torch
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    torch.cuda.empty_cache()
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def profiled_traffic(kernel: str, batch: int):
+    """DRAM bytes per launch of `kernel` at this batch, from the committed ncu
+    summary profiles/<kernel>_traffic.txt (line 'bytes_per_launch_per_line:
+    X', DRAM read + write per launch divided by the batch the capture ran
+    at; traffic grows with the batch).  None when no capture is committed."""
+    f = REPO / "profiles" / f"{kernel}_traffic.txt"
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("bytes_per_launch_per_line:"):
+                return float(line.split(":", 1)[1]) * batch
+    except OSError:
+        pass
+    return None
+
+
+
 def our_arm(args):
     import numpy as np
     import torch
@@ -163,18 +208,15 @@ def our_arm(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     pkg = load_package()
-    from trba_b200 import data
+    from trba_b200 import data, dp
     from trba_b200.model import Config, QatModel
     L = pkg.lib()
     cfg = Config(img_w=args.img_w, max_len=args.max_len, batch=args.batch)
     m = QatModel(cfg)
     m.set_params(data.init_params(m.manifest(), cfg, args.seed))
     if world > 1:
-        import torch.distributed as dist
-        obj = [QatModel.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        m.dp_init(obj[0], rank, world)
-    host = data.make_batch(cfg, args.batch, args.seed + 1000 * rank + 1)
+        dp.join(m)
+    host = data.make_batch(cfg, args.batch, dp.rank_seed(args.seed, rank))
     pinned = [torch.from_numpy(a).pin_memory() for a in host]
     devb = [p.to(dev) for p in pinned]
     stream = torch.cuda.current_stream(dev)
@@ -186,12 +228,21 @@ def our_arm(args):
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
+    # measured ceilings for the roofline, taken before the timed region
+    f32_peak = C.c_double()
+    if L.trba_measure_f32_muladd_peak(C.byref(f32_peak), sptr) != 0:
+        raise RuntimeError(L.trba_last_error_string().decode())
+    int8_peak = int8_gemm_peak(dev) if rank == 0 else None
+
     for _ in range(max(3, args.warmup)):
         m.train_step(*devb, stream=sptr)
     barrier()
     clocks = Clocks(local)
     clocks.start()
     l0 = L.trba_launch_count()
+    # the dominant kernel (the conv input-gradient gather) is bracketed by
+    # CUDA events on the step's stream throughout the timed region
+    m.probe(m.PROBE_DGRAD)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -200,12 +251,10 @@ def our_arm(args):
     barrier()
     ck = clocks.stop()
     launches = (L.trba_launch_count() - l0) / args.steps
-    ms = e0.elapsed_time(e1) / args.steps
+    dg_ms, dg_n, dg_ops, dg_bytes = m.probe_read()
+    m.probe(-1)
+    ms = dp.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     loss = m.loss()
-    ms_t = torch.tensor([ms], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(ms_t.item())
     value = args.batch * world / (ms / 1000.0)
 
     # end to end through the host-buffer entry point: H2D inputs + D2H loss in every step
@@ -219,18 +268,59 @@ def our_arm(args):
             m.train_step_host(*np_in, stream=sptr)
         e1.record(stream)
         barrier()
-        ms2 = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
-        if world > 1:
-            torch.distributed.all_reduce(ms2, op=torch.distributed.ReduceOp.MAX)
+        ms2 = dp.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
         h2d = sum(int(a.nbytes) for a in np_in)
-        e2e = {"value": args.batch * world / (float(ms2.item()) / 1000.0), "unit": "lines/s",
+        e2e = {"value": args.batch * world / (ms2 / 1000.0), "unit": "lines/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12}
+
+    # int8 tensor-core GEMMs of the step (forward conv + weight gradient),
+    # probed over a few extra steps after the timed region
+    gemm = {}
+    for name, kind in (("conv_fwd", m.PROBE_CONV_GEMM), ("conv_wgrad", m.PROBE_WGRAD_GEMM)):
+        m.probe(kind)
+        for _ in range(3):
+            m.train_step(*devb, stream=sptr)
+        g_ms, g_n, g_ops, g_bytes = m.probe_read()
+        m.probe(-1)
+        gemm[name] = {"launches_per_step": g_n // 3, "ms_per_step": g_ms / 3,
+                      "tops": g_ops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None}
+    barrier()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, lib = cpu_step_sample(4, 2, 1, args.img_w, args.max_len, args.seed)
+        v, cores, kind, lib = cpu_step_sample(32, 2, 1, args.img_w, args.max_len, args.seed)
         cpu = {"value": v, "unit": "lines/s", "cores": cores, "kind": kind,
-               "sample": f"4 lines/step x 2 steps of the same 32x{args.img_w} step, {lib}, OMP {cores} threads"}
+               "sample": f"32 lines/step x 2 timed steps (1 warm-up) of the same 32x{args.img_w} step, {lib}, "
+                         f"OMP {cores} threads"}
+
+    roofline = None
+    if dg_n > 0 and dg_ms > 0:
+        per_launch_s = dg_ms * 1e-3 / dg_n
+        achieved = dg_ops / dg_n / per_launch_s / 1e12
+        traffic = profiled_traffic("dgrad_kernel", args.batch)
+        roofline = {
+            "kernel": "dgrad_kernel: conv input gradient, f32 in the reference's summation order",
+            "bound": "fp32",
+            "achieved": achieved, "peak": f32_peak.value, "unit": "TFLOP/s",
+            "frac": achieved / f32_peak.value,
+            "peak_source": "measured in this run: trba_measure_f32_muladd_peak (separately rounded f32x2 "
+                           "multiply + add chains on every SM)",
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": dg_bytes / dg_n,
+            "hbm_gbs_at_algorithmic_bytes": dg_bytes / dg_n / per_launch_s / 1e9,
+            "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
+            "launches_per_step": dg_n / args.steps,
+            "ms_per_step": dg_ms / args.steps,
+            "share_of_step": dg_ms / args.steps / ms,
+        }
+    gemm_line = None
+    if int8_peak:
+        tot_ms = sum(g["ms_per_step"] for g in gemm.values())
+        tot_tops = sum((g["tops"] or 0) * g["ms_per_step"] for g in gemm.values()) / tot_ms if tot_ms else None
+        gemm_line = {"bound": "tensor", "achieved": tot_tops, "peak": int8_peak, "unit": "TOP/s",
+                     "frac": tot_tops / int8_peak if tot_tops else None,
+                     "peak_source": "measured in this run: torch._int_mm (cuBLAS) int8 8192^3, best of 10",
+                     "by_gemm": gemm}
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "lines/s", "n_gpus": world, "steps": args.steps,
@@ -245,7 +335,8 @@ def our_arm(args):
             "clocks": ck,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "roofline": None,
+            "roofline": roofline,
+            "roofline_int8_gemm": gemm_line,
         }
         print(json.dumps(out), flush=True)
     m.close()

@@ -36,6 +36,12 @@ int trba_sgemm_exact_noalloc(const float *a, const float *b, float *c, int m, in
 
 /* Number of kernels this library has launched so far (every launch site
  * counts itself), for reporting launches per step. */
+/* Measured ceiling (no counterpart in the reference) of separately rounded
+ * f32 multiply + add pairs issued as packed f32x2 instructions — the
+ * arithmetic of the exact input-gradient gather: a kernel of independent
+ * chains on every SM, timed with CUDA events; *tflops counts the multiply
+ * and the add as one flop each.  Synchronises the stream. */
+int trba_measure_f32_muladd_peak(double *tflops, void *stream);
 long long trba_launch_count(void);
 
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier

@@ -99,17 +99,18 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
 
 /* Kernel probe (no counterpart in the reference): while a kind is set, every
  * launch of that kernel family in the step is bracketed by CUDA events on the
- * step's stream, and its algorithmic work is summed — 2*M*N*K ops for the
- * GEMM kinds, bytes read + written for the input-gradient gather.
- * trba_model_probe(m, kind) selects a kind (-1 = off) and clears the record;
- * trba_model_probe_read waits for the last event and returns the summed
- * device milliseconds, the number of launches and the summed work. */
+ * step's stream, and its algorithmic work is summed: arithmetic operations
+ * (2*M*N*K for the GEMMs; one multiply and one add per gather term for the
+ * input gradient) and bytes (one read of every input, one write of every
+ * output).  trba_model_probe(m, kind) selects a kind (-1 = off) and clears
+ * the record; trba_model_probe_read waits for the last event and returns the
+ * summed device milliseconds, launches, operations and bytes. */
 #define TRBA_PROBE_CONV_GEMM 0  /* conv forward int8 tcgen05 GEMM (+BN sums epilogue) */
 #define TRBA_PROBE_WGRAD_GEMM 1 /* conv weight-gradient int8 tcgen05 split-K GEMM */
-#define TRBA_PROBE_DGRAD 2      /* conv input-gradient gather (fp32) */
+#define TRBA_PROBE_DGRAD 2      /* conv input-gradient gather (fp32, reference summation order) */
 #define TRBA_PROBE_SGEMM 3      /* sequence-head fp32 GEMMs (f64 accumulation) */
 int trba_model_probe(trba_model *m, int kind);
-int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *work);
+int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes);
 
 /* ---- data parallel (one process per GPU, NCCL over NVLink) ---- */
 /* 128-byte NCCL unique id from rank 0, broadcast by the caller. */

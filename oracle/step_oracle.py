@@ -850,7 +850,10 @@ class OracleTrba:
         return total / n, grad.reshape(-1)
 
     # -- the step: src/main.rs:2249-2413 ------------------------------------
-    def train_step(self, img, text_in, target, ctc_targets):
+    def train_step(self, img, text_in, target, ctc_targets, optimize: bool = True):
+        """One step (src/main.rs:2249-2413): forward, losses, backward into
+        self.g and, unless optimize is False (data-parallel callers average
+        self.g across ranks first), the optimiser step."""
         cfg = self.cfg
         b = img.shape[0]
         H, V, steps = cfg.hidden, cfg.classes, cfg.steps
@@ -901,7 +904,8 @@ class OracleTrba:
             d = self.bilstm_layer_bwd(li, d, rtr[li])
         self.debug["dfeat"] = d
         self.cnn_bwd(np.ascontiguousarray(d.astype(F32)), ctr)
-        self.optimizer_step()
+        if optimize:
+            self.optimizer_step()
         return dict(loss=total, attn=attn_loss, ctc=ctc_loss)
 
     # -- clip + Muon/Adam + requantize: src/main.rs:2373-2410, src/opt.rs ----

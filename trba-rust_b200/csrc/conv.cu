@@ -34,17 +34,27 @@ __global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restr
     }
 }
 
-// The same operand, 16 bytes per thread: thread u covers row u / G and the
-// bytes [16 g, 16 g + 16) of it (G = col_ld / 16), written with one 16-byte
-// store, so a warp writes 512 contiguous bytes.  A table in shared memory
-// gives every column k = (c, kh, kw) its input offset c*H*W + kh*W + kw and
-// its (kh, kw), so the gather itself does no divisions.
-constexpr int kIm2colMaxLd = 6144;  // table of col_ld int2 entries: 48 KB
+// The same operand, staged through shared memory in tiles of kTileRows rows.
+// Gather: consecutive threads take consecutive rows (output pixels) for one
+// column k = (c, kh, kw), so a warp's byte loads fall on neighbouring input
+// pixels; a table in shared memory gives every column its input offset
+// c*H*W + kh*W + kw and its (kh, kw), and every row of the tile its base
+// offset and window origin, so the gather does no divisions.  Store: the
+// tile is contiguous in col (ld = col_ld), written with 16-byte stores.
+// Shared memory: col_ld int2 (table) + kTileRows * (col_ld + 4) bytes (tile;
+// the 4-byte pad puts the rows of one column in distinct banks).
+constexpr int kIm2colMaxLd = 4096;
+constexpr int kTileRows = 32;
 
-__global__ void __launch_bounds__(256) im2col16_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
-                                                       int C, int H, int W, int kH, int kW, int sH, int sW, int pH,
-                                                       int pW, int Ho, int Wo, int col_ld, i64 rows, i64 units) {
+__global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
+                                                          int C, int H, int W, int kH, int kW, int sH, int sW,
+                                                          int pH, int pW, int Ho, int Wo, int col_ld, i64 rows,
+                                                          i64 rows_pad) {
     extern __shared__ int2 ktab[];
+    __shared__ long long row_base[kTileRows];
+    __shared__ int row_ih[kTileRows], row_iw[kTileRows];
+    uint8_t *tile = reinterpret_cast<uint8_t *>(ktab + col_ld);
+    const int pitch = col_ld + 4;
     const int cols = C * kH * kW, khw = kH * kW;
     for (int k = threadIdx.x; k < col_ld; k += blockDim.x) {
         if (k < cols) {
@@ -54,29 +64,43 @@ __global__ void __launch_bounds__(256) im2col16_kernel(const int8_t *__restrict_
             ktab[k] = make_int2(-1, 0);
         }
     }
-    __syncthreads();
-    const int G = col_ld >> 4;
     const i64 hwo = (i64)Ho * Wo, chw = (i64)C * H * W;
-    for (i64 u = (i64)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (i64)gridDim.x * blockDim.x) {
-        const i64 r = u / G;
-        const int g = (int)(u - r * G);
-        uint32_t w4[4] = {0u, 0u, 0u, 0u};
-        if (r < rows) {
-            const i64 b = r / hwo;
-            const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
-            const int ih0 = oh * sH - pH, iw0 = ow * sW - pW;
-            const i64 base = b * chw + (i64)ih0 * W + iw0;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int2 t = ktab[g * 16 + j];
-                const int ih = ih0 + (t.y >> 16), iw = iw0 + (t.y & 0xffff);
-                uint32_t v = 0;
-                if (t.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
-                    v = (uint8_t)in[base + t.x];
-                w4[j >> 2] |= v << (8 * (j & 3));
+    const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
+    const int chunks_per_row = col_ld >> 4;
+    for (i64 t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const i64 r0 = t * kTileRows;
+        if (threadIdx.x < kTileRows) {
+            const i64 r = r0 + threadIdx.x;
+            if (r < rows) {
+                const i64 b = r / hwo;
+                const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
+                row_ih[threadIdx.x] = oh * sH - pH;
+                row_iw[threadIdx.x] = ow * sW - pW;
+                row_base[threadIdx.x] = b * chw + (i64)row_ih[threadIdx.x] * W + row_iw[threadIdx.x];
+            } else {
+                row_ih[threadIdx.x] = -(1 << 30);  // fails every bounds check: zero row
+                row_iw[threadIdx.x] = 0;
+                row_base[threadIdx.x] = 0;
             }
         }
-        *reinterpret_cast<uint4 *>(col + r * col_ld + g * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        __syncthreads();
+        for (int e = threadIdx.x; e < kTileRows * col_ld; e += blockDim.x) {
+            const int r = e & (kTileRows - 1), k = e / kTileRows;
+            const int2 tk = ktab[k];
+            const int ih = row_ih[r] + (tk.y >> 16), iw = row_iw[r] + (tk.y & 0xffff);
+            uint8_t v = 0;
+            if (tk.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
+                v = (uint8_t)in[row_base[r] + tk.x];
+            tile[r * pitch + k] = v;
+        }
+        __syncthreads();
+        const int live_rows = (int)min((i64)kTileRows, rows_pad - r0);
+        for (int c = threadIdx.x; c < live_rows * chunks_per_row; c += blockDim.x) {
+            const int r = c / chunks_per_row, cc = c - r * chunks_per_row;
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(tile + r * pitch + cc * 16);
+            *reinterpret_cast<uint4 *>(col + (r0 + r) * col_ld + cc * 16) = make_uint4(src[0], src[1], src[2], src[3]);
+        }
+        __syncthreads();
     }
 }
 
@@ -254,9 +278,20 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
     if (col_ld < cols || (col_ld & 15) || rows <= 0) return;
     const i64 total = ((rows + 15) / 16 * 16) * col_ld;
     if (col_ld <= kIm2colMaxLd && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {
-        const i64 units = total / 16;
-        im2col16_kernel<<<grid_for(units), kThreads, sizeof(int2) * col_ld, as_stream(s)>>>(
-            input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, units);
+        const i64 rows_pad = (rows + 15) / 16 * 16;
+        const size_t smem = sizeof(int2) * col_ld + (size_t)kTileRows * (col_ld + 4);
+        static bool attr[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
+            TRBA_CHECK(cudaFuncSetAttribute(im2col_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)(sizeof(int2) * kIm2colMaxLd + kTileRows * (kIm2colMaxLd + 4))));
+            attr[dev] = true;
+        }
+        const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
+        const i64 cap = (i64)sm_count() * 4;
+        im2col_tile_kernel<<<(unsigned)(ntiles < cap ? ntiles : cap), kThreads, smem, as_stream(s)>>>(
+            input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, rows_pad);
     } else {
         im2col_pad_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(
             input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, total);

@@ -3,6 +3,7 @@
 // launches (cited per kernel) with the same float expression order, written
 // with explicit round-to-nearest intrinsics so that nothing is contracted.
 #include "qat_kernels.cuh"
+#include "f32x2.cuh"
 
 namespace trba {
 namespace qat {
@@ -341,75 +342,115 @@ __global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const f
     GRID_LOOP(i, n) g[i] = fadd(g[i], fmul((float)acc[i], deq));
 }
 
-// Input gradient (src/qnet.rs:1068-1080 -> launch_conv_backward_grad_input_i8),
-// 8 input channels per thread: the 8 outputs of one input pixel share every
-// dy load, and their int8 weights (as f32) sit in shared memory as
-// [tap][oc][8], read as two broadcast float4 per (tap, oc).  Each output is
-// still accumulated in the reference's order — taps (kh, kw) outer, output
-// channels inner, one f32 multiply and one f32 add per term — then scaled by
-// w_s, so the result is bit-identical to the reference's gather.
-constexpr int kDgradCi = 8;
+// Input gradient (src/qnet.rs:1068-1080 -> launch_conv_backward_grad_input_i8).
+//
+// Every output gi[b, ci, ih, iw] is accumulated in the reference's order —
+// taps (kh, kw) outer, output channels inner, one f32 multiply and one f32
+// add per term, both rounded — then scaled by w_s, so the result is
+// bit-identical to the reference's per-element gather.
+//
+// Blocking: a thread owns 2 input pixels x 16 input channels (32
+// accumulators).  The int8 weights of the CTA's 16 channels sit in shared
+// memory as f32, [tap][oc][16], read as four broadcast float4 per (tap, oc);
+// each dy value loaded feeds 16 accumulators.  The arithmetic runs on the
+// packed f32x2 pipe: the product of a pair is fma.rn.f32x2(d, w, z) with
+// z = -0.0 passed at run time (d*w + -0 is the correctly rounded product),
+// then add.rn.f32x2 into the accumulators.  A plain mul.rn.f32x2 followed by
+// add.rn.f32x2 is contracted into one fused multiply-add by the code
+// generator, which would change the rounding; the run-time addend keeps the
+// two roundings apart.  A tap outside the output plane contributes d = 0:
+// the accumulator starts at +0 and can never be -0, so adding +-0 leaves it
+// unchanged, exactly as skipping the tap does.
+constexpr int kDgradCi = 16, kDgradPx = 2;
 
-__global__ void __launch_bounds__(256) dgrad_ci8_kernel(const float *__restrict__ go, const int8_t *__restrict__ wq,
-                                                        i64 w_ld, const float *__restrict__ w_s, int B, int Cin, int H,
-                                                        int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW,
-                                                        int Ho, int Wo, const int8_t *__restrict__ mask_q,
-                                                        const float *__restrict__ add, float *__restrict__ gi) {
-    extern __shared__ float4 wsm4[];  // [taps][Cout][2] float4
-    const int khw = kH * kW, ci0 = blockIdx.y * kDgradCi;
-    for (int e = threadIdx.x; e < khw * Cout * kDgradCi; e += blockDim.x) {
-        const int j = e % kDgradCi, oc = (e / kDgradCi) % Cout, t = e / (kDgradCi * Cout);
+__device__ float g_dgrad_zero[1];  // target of the masked (outside-plane) dy loads
+
+__global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go, const int8_t *__restrict__ wq,
+                                                    i64 w_ld, const float *__restrict__ w_s, int B, int Cin, int H,
+                                                    int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW,
+                                                    int Ho, int Wo, const int8_t *__restrict__ mask_q,
+                                                    const float *__restrict__ add, float *__restrict__ gi,
+                                                    float neg_zero) {
+    constexpr int P = kDgradPx, CI = kDgradCi, NP = CI / 2;
+    extern __shared__ float4 wsm4[];  // [taps][Cout][CI / 4] float4
+    const int khw = kH * kW, ci0 = blockIdx.y * CI;
+    for (int e = threadIdx.x; e < khw * Cout * CI; e += blockDim.x) {
+        const int j = e % CI, oc = (e / CI) % Cout, t = e / (CI * Cout);
         const int ci = ci0 + j;
         reinterpret_cast<float *>(wsm4)[e] = ci < Cin ? (float)wq[(i64)oc * w_ld + (i64)ci * khw + t] : 0.0f;
     }
     __syncthreads();
     const int hwo = Ho * Wo, hwi = H * W;
     const i64 npix = (i64)B * hwi;
-    const i64 pix = (i64)blockIdx.x * blockDim.x + threadIdx.x;
-    if (pix >= npix) return;
-    const int b = (int)(pix / hwi), rem = (int)(pix - (i64)b * hwi);
-    const int ih = rem / W, iw = rem - ih * W;
-    const float *go_b = go + (i64)b * Cout * hwo;
-    float acc[kDgradCi];
+    const i64 pix0 = ((i64)blockIdx.x * blockDim.x + threadIdx.x) * P;
+    if (pix0 >= npix) return;
+    int pb[P], prem[P], pih[P], piw[P];
+    bool live[P];
 #pragma unroll
-    for (int j = 0; j < kDgradCi; ++j) acc[j] = 0.0f;
+    for (int p = 0; p < P; ++p) {
+        const i64 px = pix0 + p;
+        live[p] = px < npix;
+        const i64 q = live[p] ? px : pix0;
+        pb[p] = (int)(q / hwi);
+        prem[p] = (int)(q - (i64)pb[p] * hwi);
+        pih[p] = prem[p] / W;
+        piw[p] = prem[p] - pih[p] * W;
+    }
+    F2 acc[P][NP];
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int j = 0; j < NP; ++j) acc[p][j] = F2{0.0f, 0.0f};
     for (int kh = 0; kh < kH; ++kh) {
-        const int nh = ih + pH - kh;
-        if (nh < 0 || nh % sH) continue;
-        const int oh = nh / sH;
-        if (oh >= Ho) continue;
         for (int kw = 0; kw < kW; ++kw) {
-            const int nw = iw + pW - kw;
-            if (nw < 0 || nw % sW) continue;
-            const int ow = nw / sW;
-            if (ow >= Wo) continue;
-            const float *gp = go_b + oh * Wo + ow;
-            const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * 2;
-#pragma unroll 4
+            const float *gp[P];
+            i64 gst[P];
+            bool any = false;
+#pragma unroll
+            for (int p = 0; p < P; ++p) {
+                const int nh = pih[p] + pH - kh, nw = piw[p] + pW - kw;
+                const bool ok = live[p] && nh >= 0 && nw >= 0 && nh % sH == 0 && nw % sW == 0 && nh / sH < Ho &&
+                                nw / sW < Wo;
+                gp[p] = ok ? go + (i64)pb[p] * Cout * hwo + (nh / sH) * Wo + nw / sW : g_dgrad_zero;
+                gst[p] = ok ? hwo : 0;
+                any |= ok;
+            }
+            if (!any) continue;
+            const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * (CI / 4);
+#pragma unroll 2
             for (int oc = 0; oc < Cout; ++oc) {
-                const float d = gp[(i64)oc * hwo];
-                const float4 w0 = wt[2 * oc], w1 = wt[2 * oc + 1];
-                acc[0] = fadd(acc[0], fmul(d, w0.x));
-                acc[1] = fadd(acc[1], fmul(d, w0.y));
-                acc[2] = fadd(acc[2], fmul(d, w0.z));
-                acc[3] = fadd(acc[3], fmul(d, w0.w));
-                acc[4] = fadd(acc[4], fmul(d, w1.x));
-                acc[5] = fadd(acc[5], fmul(d, w1.y));
-                acc[6] = fadd(acc[6], fmul(d, w1.z));
-                acc[7] = fadd(acc[7], fmul(d, w1.w));
+                F2 wv[NP];
+#pragma unroll
+                for (int q = 0; q < CI / 4; ++q) {
+                    const float4 w4 = wt[(CI / 4) * oc + q];
+                    wv[2 * q] = F2{w4.x, w4.y};
+                    wv[2 * q + 1] = F2{w4.z, w4.w};
+                }
+#pragma unroll
+                for (int p = 0; p < P; ++p) {
+                    const float d = gp[p][oc * gst[p]];
+                    const F2 dd{d, d};
+#pragma unroll
+                    for (int j = 0; j < NP; ++j) acc[p][j] = add2_rn(acc[p][j], prod2_rn(dd, wv[j], neg_zero));
+                }
             }
         }
     }
     const float ws = *w_s;
 #pragma unroll
-    for (int j = 0; j < kDgradCi; ++j) {
-        const int ci = ci0 + j;
-        if (ci >= Cin) break;
-        const i64 i = ((i64)b * Cin + ci) * hwi + rem;
-        float v = fmul(acc[j], ws);
-        if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
-        if (add) v = fadd(v, add[i]);
-        gi[i] = v;
+    for (int p = 0; p < P; ++p) {
+        if (!live[p]) continue;
+        const float *a = &acc[p][0].x;
+#pragma unroll
+        for (int j = 0; j < CI; ++j) {
+            const int ci = ci0 + j;
+            if (ci >= Cin) break;
+            const i64 i = ((i64)pb[p] * Cin + ci) * hwi + prem[p];
+            float v = fmul(a[j], ws);
+            if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
+            if (add) v = fadd(v, add[i]);
+            gi[i] = v;
+        }
     }
 }
 
@@ -560,12 +601,13 @@ void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B,
     int dev = 0;
     cudaGetDevice(&dev);
     if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
-        TRBA_CHECK(cudaFuncSetAttribute(dgrad_ci8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        TRBA_CHECK(cudaFuncSetAttribute(dgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr[dev] = true;
     }
-    dim3 grid((unsigned)((npix + 255) / 256), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
-    dgrad_ci8_kernel<<<grid, 256, smem, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
-                                              mask_q, add, gi);
+    const i64 per_cta = 256 * kDgradPx;
+    dim3 grid((unsigned)((npix + per_cta - 1) / per_cta), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
+    dgrad_kernel<<<grid, 256, smem, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
+                                          mask_q, add, gi, -0.0f);
     TRBA_LAUNCH_CHECK();
 }
 

@@ -146,7 +146,8 @@ struct Probe {
     int kind = -1;
     std::vector<cudaEvent_t> ev;  // start/stop pairs
     size_t used = 0;
-    double work = 0.0;  // algorithmic ops (GEMMs) or bytes (gathers) of the timed launches
+    double ops = 0.0;    // algorithmic arithmetic operations of the timed launches
+    double bytes = 0.0;  // algorithmic bytes (one read of every input, one write of every output)
     long long launches = 0;
 };
 
@@ -683,7 +684,7 @@ struct Ctx {
 struct ProbeScope {
     Probe *p = nullptr;
     cudaStream_t st;
-    ProbeScope(trba_model *m, int kind, double work, cudaStream_t s) : st(s) {
+    ProbeScope(trba_model *m, int kind, double ops, double bytes, cudaStream_t s) : st(s) {
         if (m->probe.kind != kind) return;
         p = &m->probe;
         while (p->ev.size() < p->used + 2) {
@@ -692,7 +693,8 @@ struct ProbeScope {
             p->ev.push_back(e);
         }
         TRBA_CHECK(cudaEventRecord(p->ev[p->used], st));
-        p->work += work;
+        p->ops += ops;
+        p->bytes += bytes;
         p->launches += 1;
     }
     ~ProbeScope() {
@@ -703,7 +705,8 @@ struct ProbeScope {
 };
 
 void sgemm(Ctx &c, const seq::Gemm &g, cudaStream_t st) {
-    ProbeScope ps(c.m, TRBA_PROBE_SGEMM, 2.0 * g.M * g.N * g.K, st);
+    ProbeScope ps(c.m, TRBA_PROBE_SGEMM, 2.0 * g.M * g.N * g.K, 4.0 * ((double)g.M * g.K + (double)g.K * g.N + (double)g.M * g.N),
+                  st);
     seq::sgemm(g, st);
 }
 
@@ -715,7 +718,9 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     launch_im2col_pad(q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo, L.kp,
                       c.st);
     {
-        ProbeScope ps(c.m, TRBA_PROBE_CONV_GEMM, 2.0 * rows * L.cout * L.K, c.st);
+        // bytes: im2col operand + weights read, x (f32) written
+        ProbeScope ps(c.m, TRBA_PROBE_CONV_GEMM, 2.0 * rows * L.cout * L.K,
+                      (double)rows * L.kp + (double)L.cout * L.kp + 4.0 * rows * L.cout, c.st);
         if (!gemm_i8_conv_f32(L.col.get(), L.kp, L.wq.get(), L.kp, (int)rows, L.cout, L.K, L.x.get(), s_in,
                               L.ws.get(), L.bn_acc.get(), L.Ho * L.Wo, c.st))
             report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
@@ -747,6 +752,18 @@ void conv_bn_quant(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     qat::act_quant(s, c.B, L.ymax.get(), L.s_q.get(), L.q.get(), true, c.st);
 }
 
+// Number of (input position, kernel tap) pairs along one axis whose output
+// position lies on the output grid: the gather terms of the input gradient.
+double valid_taps(int n_in, int k, int s, int pad, int n_out) {
+    double v = 0.0;
+    for (int i = 0; i < n_in; ++i)
+        for (int t = 0; t < k; ++t) {
+            const int q = i + pad - t;
+            if (q >= 0 && q % s == 0 && q / s < n_out) v += 1.0;
+        }
+    return v;
+}
+
 // ConvQat::backward (src/qnet.rs:918-1083).  gi: input gradient (or null).
 void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const float *add, float *gi) {
     const int B = c.B, HW = L.Ho * L.Wo;
@@ -761,17 +778,22 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
     const int splits = splitk_for(L.cout, L.K, (int)rows);
     const int8_t *Bop = compat ? L.col.get() : L.colT.get();
     {
-        ProbeScope ps(c.m, TRBA_PROBE_WGRAD_GEMM, 2.0 * rows * L.cout * L.K, c.st);
+        // bytes: quantised dx + im2col operand read, s32 dW accumulated
+        ProbeScope ps(c.m, TRBA_PROBE_WGRAD_GEMM, 2.0 * rows * L.cout * L.K,
+                      (double)rows * L.cout + (double)rows * L.kp + 4.0 * L.cout * L.K, c.st);
         if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits,
                                    c.st))
             report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
     }
     qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, c.st);
     if (gi) {
+        // ops: one multiply and one add per (input element, valid tap, output channel)
         const double in_n = (double)B * L.cin * L.H * L.W;
         const double bytes = 4.0 * B * L.cout * HW + 4.0 * in_n + (mask_q ? in_n : 0.0) + (add ? 4.0 * in_n : 0.0) +
                              (double)L.cout * L.K;
-        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, bytes, c.st);
+        const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
+                             valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
+        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.st);
         qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
                    L.Ho, L.Wo, mask_q, add, gi, c.st);
     }
@@ -1286,13 +1308,14 @@ int trba_model_probe(trba_model *m, int kind) {
     if (!m || kind < -1 || kind > TRBA_PROBE_SGEMM) return -1;
     m->probe.kind = kind;
     m->probe.used = 0;
-    m->probe.work = 0.0;
+    m->probe.ops = 0.0;
+    m->probe.bytes = 0.0;
     m->probe.launches = 0;
     return 0;
 }
 
-int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *work) {
-    if (!m || !ms_total || !launches || !work) return -1;
+int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes) {
+    if (!m || !ms_total || !launches || !ops || !bytes) return -1;
     auto &p = m->probe;
     double ms = 0.0;
     if (p.used) TRBA_CHECK(cudaEventSynchronize(p.ev[p.used - 1]));
@@ -1303,7 +1326,8 @@ int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, 
     }
     *ms_total = ms;
     *launches = p.launches;
-    *work = p.work;
+    *ops = p.ops;
+    *bytes = p.bytes;
     return cuda_status();
 }
 

@@ -160,10 +160,11 @@ class QatModel:
         self._check(self.L.trba_model_probe(self.h, kind), "probe")
 
     def probe_read(self):
-        """(device ms summed over the probed launches, launches, algorithmic work)."""
-        ms, n, work = C.c_double(), C.c_longlong(), C.c_double()
-        self._check(self.L.trba_model_probe_read(self.h, C.byref(ms), C.byref(n), C.byref(work)), "probe_read")
-        return ms.value, n.value, work.value
+        """(device ms summed over the probed launches, launches, algorithmic ops, algorithmic bytes)."""
+        ms, n, ops, nbytes = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+        self._check(self.L.trba_model_probe_read(self.h, C.byref(ms), C.byref(n), C.byref(ops), C.byref(nbytes)),
+                    "probe_read")
+        return ms.value, n.value, ops.value, nbytes.value
 
     def dp_init(self, id128: bytes, rank: int, world: int):
         buf = C.create_string_buffer(id128, 128)
