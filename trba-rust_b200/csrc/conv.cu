@@ -45,6 +45,7 @@ __global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restr
 // the 4-byte pad puts the rows of one column in distinct banks).
 constexpr int kIm2colMaxLd = 4096;
 constexpr int kTileRows = 32;
+constexpr int kGatherBatch = 16;
 
 __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
                                                           int C, int H, int W, int kH, int kW, int sH, int sW,
@@ -84,14 +85,28 @@ __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restri
             }
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < kTileRows * col_ld; e += blockDim.x) {
-            const int r = e & (kTileRows - 1), k = e / kTileRows;
-            const int2 tk = ktab[k];
-            const int ih = row_ih[r] + (tk.y >> 16), iw = row_iw[r] + (tk.y & 0xffff);
-            uint8_t v = 0;
-            if (tk.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
-                v = (uint8_t)in[row_base[r] + tk.x];
-            tile[r * pitch + k] = v;
+        // kGatherBatch independent byte loads per thread are issued before
+        // any of them is stored, so enough loads are in flight per SM.
+        const int tile_elems = kTileRows * col_ld;
+        for (int e0 = threadIdx.x; e0 < tile_elems; e0 += blockDim.x * kGatherBatch) {
+            uint8_t v[kGatherBatch];
+#pragma unroll
+            for (int j = 0; j < kGatherBatch; ++j) {
+                const int e = e0 + j * blockDim.x;
+                v[j] = 0;
+                if (e < tile_elems) {
+                    const int r = e & (kTileRows - 1), k = e / kTileRows;
+                    const int2 tk = ktab[k];
+                    const int ih = row_ih[r] + (tk.y >> 16), iw = row_iw[r] + (tk.y & 0xffff);
+                    if (tk.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
+                        v[j] = (uint8_t)in[row_base[r] + tk.x];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kGatherBatch; ++j) {
+                const int e = e0 + j * blockDim.x;
+                if (e < tile_elems) tile[(e & (kTileRows - 1)) * pitch + e / kTileRows] = v[j];
+            }
         }
         __syncthreads();
         const int live_rows = (int)min((i64)kTileRows, rows_pad - r0);

@@ -79,7 +79,41 @@ struct PlaneSrc {
     }
 };
 
-__device__ PlaneSrc plane_src(const Src &s, int b, int c, float *mean_out = nullptr, float *var_out = nullptr) {
+// Planes of HW elements are processed one per warp when small (8 planes per
+// 256-thread CTA) and one per CTA otherwise; PlaneIdx says which plane a
+// thread works on, its index inside the plane's thread group and the group's
+// width.  Reductions over a plane are warp shuffles or a block reduction.
+constexpr int kWarpPlaneMaxHW = 1024;
+
+struct PlaneIdx {
+    int plane, lane, width;
+    bool live, leader;
+};
+
+__device__ __forceinline__ PlaneIdx plane_idx(int nplanes, int warp_mode) {
+    PlaneIdx q;
+    if (warp_mode) {
+        q.plane = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        q.lane = threadIdx.x & 31;
+        q.width = 32;
+    } else {
+        q.plane = blockIdx.x;
+        q.lane = threadIdx.x;
+        q.width = blockDim.x;
+    }
+    q.live = q.plane < nplanes;
+    if (!q.live) q.plane = nplanes - 1;  // valid reads; no writes
+    q.leader = q.live && q.lane == 0;
+    return q;
+}
+
+// Sum over a plane's thread group; valid in the group's lane 0.
+__device__ __forceinline__ double plane_sum_d(double v, int warp_mode, double *sm) {
+    return warp_mode ? warp_sum_d(v) : block_sum_d(v, sm);
+}
+
+__device__ PlaneSrc plane_src(const Src &s, int b, int c, bool leader, float *mean_out = nullptr,
+                              float *var_out = nullptr) {
     PlaneSrc p;
     p.kind = s.kind;
     p.x = s.x;
@@ -93,7 +127,7 @@ __device__ PlaneSrc plane_src(const Src &s, int b, int c, float *mean_out = null
         p.r = bn_rstd(v);
         p.gamma = s.gamma[c];
         p.beta = s.beta[c];
-        if (mean_out && b == 0 && threadIdx.x == 0) {
+        if (mean_out && b == 0 && leader) {
             mean_out[c] = m;
             var_out[c] = v;
         }
@@ -107,24 +141,27 @@ __device__ PlaneSrc plane_src(const Src &s, int b, int c, float *mean_out = null
 // ------------------------------------------------------------- forward --
 // src/qnet.rs:877-895 (bn_apply), 1212-1214 (avgpool_hw of y2),
 // 1102-1106 (reduce_max_abs before relu_quant).
-__global__ void act_stats_kernel(Src s, float *y_out, float *mean_out, float *var_out, float *pool_out,
-                                 float *vmax) {
+__global__ void act_stats_kernel(Src s, int nplanes, int warp_mode, float *y_out, float *mean_out, float *var_out,
+                                 float *pool_out, float *vmax) {
     __shared__ double smd[32];
     __shared__ float smf[32];
-    const int plane = blockIdx.x, b = plane / s.C, c = plane - b * s.C;
-    const PlaneSrc p = plane_src(s, b, c, mean_out, var_out);
-    const i64 base = (i64)plane * s.HW;
+    const PlaneIdx q = plane_idx(nplanes, warp_mode);
+    const int b = q.plane / s.C, c = q.plane - b * s.C;
+    const PlaneSrc p = plane_src(s, b, c, q.leader, mean_out, var_out);
+    const i64 base = (i64)q.plane * s.HW;
     double sum = 0.0;
     float mx = 0.0f;
-    for (int j = threadIdx.x; j < s.HW; j += blockDim.x) {
-        const float v = p.at(base + j);
-        if (y_out) y_out[base + j] = v;
-        sum += (double)v;
-        mx = fmaxf(mx, fabsf(v));
+    if (q.live) {
+        for (int j = q.lane; j < s.HW; j += q.width) {
+            const float v = p.at(base + j);
+            if (y_out) y_out[base + j] = v;
+            sum += (double)v;
+            mx = fmaxf(mx, fabsf(v));
+        }
     }
     if (pool_out) {
-        const double t = block_sum_d(sum, smd);
-        if (threadIdx.x == 0) pool_out[plane] = (float)(t / (double)s.HW);
+        const double t = plane_sum_d(sum, warp_mode, smd);
+        if (q.leader) pool_out[q.plane] = (float)(t / (double)s.HW);
     }
     if (vmax) {
         const float m = block_max_f(mx, smf);
@@ -132,17 +169,20 @@ __global__ void act_stats_kernel(Src s, float *y_out, float *mean_out, float *va
     }
 }
 
-__global__ void act_quant_kernel(Src s, const float *vmax, float *s_out, int8_t *q, int relu) {
-    const int plane = blockIdx.x, b = plane / s.C, c = plane - b * s.C;
-    const PlaneSrc p = plane_src(s, b, c);
+__global__ void act_quant_kernel(Src s, int nplanes, int warp_mode, const float *vmax, float *s_out, int8_t *qo,
+                                 int relu) {
+    const PlaneIdx q = plane_idx(nplanes, warp_mode);
+    if (!q.live) return;
+    const int b = q.plane / s.C, c = q.plane - b * s.C;
+    const PlaneSrc p = plane_src(s, b, c, q.leader);
     const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
     const float inv = fdiv(1.0f, sc);
-    if (plane == 0 && threadIdx.x == 0 && s_out) *s_out = sc;
-    const i64 base = (i64)plane * s.HW;
-    for (int j = threadIdx.x; j < s.HW; j += blockDim.x) {
+    if (q.plane == 0 && q.leader && s_out) *s_out = sc;
+    const i64 base = (i64)q.plane * s.HW;
+    for (int j = q.lane; j < s.HW; j += q.width) {
         const float v = p.at(base + j);
         const float t = relu ? fminf(fmul(fmaxf(v, 0.0f), inv), 127.0f) : fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f);
-        q[base + j] = (int8_t)rint_even(t);
+        qo[base + j] = (int8_t)rint_even(t);
     }
 }
 
@@ -203,16 +243,21 @@ __global__ void se_backward_kernel(const float *dz, const float *y2, const float
     float *s_dp2 = sm, *s_dp1 = sm + C, *s_dpool = sm + C + R;
     const int b = blockIdx.x;
     const i64 base = (i64)b * C * HW;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    // one warp per plane: lane-strided (coalesced) products, f64 warp sum
+    const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (int c = threadIdx.x >> 5; c < C; c += nwarps) {
         const float *pz = dz + base + (i64)c * HW, *py = y2 + base + (i64)c * HW;
         double s = 0.0;
-        for (int j = 0; j < HW; ++j) s += (double)fmul(pz[j], py[j]);
-        const float pm = (float)(s / (double)HW);
-        const float dgate = fmul(pm, (float)HW);
-        const float g = gate[(i64)b * C + c];
-        const float d2 = fmul(fmul(dgate, g), fsub(1.0f, g));
-        s_dp2[c] = d2;
-        dpre2[(i64)b * C + c] = d2;
+        for (int j = lane; j < HW; j += 32) s += (double)fmul(pz[j], py[j]);
+        s = warp_sum_d(s);
+        if (lane == 0) {
+            const float pm = (float)(s / (double)HW);
+            const float dgate = fmul(pm, (float)HW);
+            const float g = gate[(i64)b * C + c];
+            const float d2 = fmul(fmul(dgate, g), fsub(1.0f, g));
+            s_dp2[c] = d2;
+            dpre2[(i64)b * C + c] = d2;
+        }
     }
     __syncthreads();
     for (int j = threadIdx.x; j < R; j += blockDim.x) {
@@ -258,21 +303,24 @@ __global__ void se_wgrad_kernel(const float *dpre1, const float *dpre2, const fl
 // later snapshot cpu_backend.cpp:782-802, one CTA per (b, c) plane, f64
 // partials added into acc[c] (sum dy) and acc[C + c] (sum dy*xhat).
 __global__ void bn_bwd_sums_kernel(const float *dy, const float *x, const float *mean, const float *var, int C,
-                                   int HW, double *acc) {
+                                   int HW, int nplanes, int warp_mode, double *acc) {
     __shared__ double smd[32];
-    const int plane = blockIdx.x, c = plane % C;
+    const PlaneIdx q = plane_idx(nplanes, warp_mode);
+    const int c = q.plane % C;
     const float m = mean[c], r = bn_rstd(var[c]);
-    const i64 base = (i64)plane * HW;
+    const i64 base = (i64)q.plane * HW;
     double s = 0.0, sx = 0.0;
-    for (int j = threadIdx.x; j < HW; j += blockDim.x) {
-        const float d = dy[base + j];
-        const float xh = fmul(fsub(x[base + j], m), r);
-        s += (double)d;
-        sx += (double)fmul(d, xh);
+    if (q.live) {
+        for (int j = q.lane; j < HW; j += q.width) {
+            const float d = dy[base + j];
+            const float xh = fmul(fsub(x[base + j], m), r);
+            s += (double)d;
+            sx += (double)fmul(d, xh);
+        }
     }
-    const double ts = block_sum_d(s, smd);
-    const double tx = block_sum_d(sx, smd);
-    if (threadIdx.x == 0) {
+    const double ts = plane_sum_d(s, warp_mode, smd);
+    const double tx = plane_sum_d(sx, warp_mode, smd);
+    if (q.leader) {
         atomicAdd(acc + c, ts);
         atomicAdd(acc + C + c, tx);
     }
@@ -299,41 +347,99 @@ __device__ __forceinline__ float dx_at(const DxPlane &p, float dy, float x) {
 }
 
 __global__ void bn_dx_max_kernel(const float *dy, const float *x, const float *mean, const float *var,
-                                 const float *gamma, const double *acc, int B, int C, int HW, float *g_gamma,
-                                 float *g_beta, float *vmax) {
+                                 const float *gamma, const double *acc, int B, int C, int HW, int nplanes,
+                                 int warp_mode, float *g_gamma, float *g_beta, float *vmax) {
     __shared__ float smf[32];
-    const int plane = blockIdx.x, b = plane / C, c = plane - b * C;
+    const PlaneIdx q = plane_idx(nplanes, warp_mode);
+    const int b = q.plane / C, c = q.plane - b * C;
     const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, (i64)B * HW);
-    if (b == 0 && threadIdx.x == 0) {  // src/qnet.rs:974-982: g_beta += sum dy, g_gamma += sum dy xhat
+    if (b == 0 && q.leader) {  // src/qnet.rs:974-982: g_beta += sum dy, g_gamma += sum dy xhat
         g_beta[c] = fadd(g_beta[c], p.sdy);
         g_gamma[c] = fadd(g_gamma[c], p.sdxh);
     }
-    const i64 base = (i64)plane * HW;
+    const i64 base = (i64)q.plane * HW;
     float mx = 0.0f;
-    for (int j = threadIdx.x; j < HW; j += blockDim.x) mx = fmaxf(mx, fabsf(dx_at(p, dy[base + j], x[base + j])));
+    if (q.live)
+        for (int j = q.lane; j < HW; j += q.width) mx = fmaxf(mx, fabsf(dx_at(p, dy[base + j], x[base + j])));
     const float t = block_max_f(mx, smf);
     if (threadIdx.x == 0) atomic_max_nonneg(vmax, t);
 }
 
+__device__ __forceinline__ int8_t quant_dx(float d, float inv) {
+    return (int8_t)rint_even(fminf(fmaxf(fmul(d, inv), -127.0f), 127.0f));
+}
+
+// dx quantised into the wgrad operand laid out [C, rows] (dW = dX^T col):
+// A[c * ld + b*HW + j].
 __global__ void bn_dx_quant_kernel(const float *dy, const float *x, const float *mean, const float *var,
-                                   const float *gamma, const double *acc, int B, int C, int HW, const float *vmax,
-                                   float *s_dx, int8_t *A, int ld, int compat) {
-    const int plane = blockIdx.x, b = plane / C, c = plane - b * C;
+                                   const float *gamma, const double *acc, int B, int C, int HW, int nplanes,
+                                   int warp_mode, const float *vmax, float *s_dx, int8_t *A, int ld) {
+    const PlaneIdx q = plane_idx(nplanes, warp_mode);
+    if (!q.live) return;
+    const int b = q.plane / C, c = q.plane - b * C;
     const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, (i64)B * HW);
     const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
     const float inv = fdiv(1.0f, sc);
-    if (plane == 0 && threadIdx.x == 0) *s_dx = sc;
-    const i64 base = (i64)plane * HW;
-    for (int j = threadIdx.x; j < HW; j += blockDim.x) {
-        const float d = dx_at(p, dy[base + j], x[base + j]);
-        const int8_t qv = (int8_t)rint_even(fminf(fmaxf(fmul(d, inv), -127.0f), 127.0f));
-        const i64 i = base + j;
-        if (compat) {
-            const i64 r = i / C, o = i - r * C;  // the NCHW buffer viewed as [rows, C]
-            A[o * ld + r] = qv;
-        } else {
-            A[(i64)c * ld + (i64)b * HW + j] = qv;
+    if (q.plane == 0 && q.leader) *s_dx = sc;
+    const i64 base = (i64)q.plane * HW;
+    for (int j = q.lane; j < HW; j += q.width)
+        A[(i64)c * ld + (i64)b * HW + j] = quant_dx(dx_at(p, dy[base + j], x[base + j]), inv);
+}
+
+// The reference-compatible operand (src/qnet.rs:984-1001: transpose_i8 of the
+// NCHW dx buffer viewed as [rows, C]): A[o * ld + r] = q(dx_flat[r * C + o]).
+// 32 x 32 tiles through shared memory: the reads walk dx_flat contiguously,
+// the writes walk A's rows contiguously.  Per-channel BN terms for all C
+// channels sit in shared memory.
+constexpr int kQtTile = 32;
+
+__global__ void __launch_bounds__(256) bn_dx_quant_t_kernel(const float *dy, const float *x, const float *mean,
+                                                            const float *var, const float *gamma,
+                                                            const double *acc, int B, int C, int HW,
+                                                            const float *vmax, float *s_dx, int8_t *A, int ld,
+                                                            i64 rows) {
+    extern __shared__ float chs[];  // [5][C]: m, r, a, sdy, sdxh
+    __shared__ int8_t tile[kQtTile][kQtTile + 4];
+    const i64 count = (i64)B * HW;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, count);
+        chs[c] = p.m;
+        chs[C + c] = p.r;
+        chs[2 * C + c] = p.a;
+        chs[3 * C + c] = p.sdy;
+        chs[4 * C + c] = p.sdxh;
+    }
+    __syncthreads();
+    const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
+    const float inv = fdiv(1.0f, sc);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *s_dx = sc;
+    const float cnt = (float)count;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const i64 r0 = (i64)blockIdx.x * kQtTile;
+    const int o0 = blockIdx.y * kQtTile;
+    for (int k = ty; k < kQtTile; k += blockDim.x >> 5) {
+        const i64 r = r0 + k;
+        const int o = o0 + tx;
+        int8_t v = 0;
+        if (r < rows && o < C) {
+            const i64 i = r * C + o;
+            const int c = (int)((i / HW) % C);
+            DxPlane p;
+            p.m = chs[c];
+            p.r = chs[C + c];
+            p.a = chs[2 * C + c];
+            p.sdy = chs[3 * C + c];
+            p.sdxh = chs[4 * C + c];
+            p.cnt = cnt;
+            v = quant_dx(dx_at(p, dy[i], x[i]), inv);
         }
+        tile[tx][k] = v;
+    }
+    __syncthreads();
+    for (int k = ty; k < kQtTile; k += blockDim.x >> 5) {
+        const int o = o0 + k;
+        const i64 r = r0 + tx;
+        if (o < C && r < rows) A[(i64)o * ld + r] = tile[k][tx];
     }
 }
 
@@ -417,7 +523,7 @@ __global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go
             }
             if (!any) continue;
             const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * (CI / 4);
-#pragma unroll 2
+#pragma unroll 4
             for (int oc = 0; oc < Cout; ++oc) {
                 F2 wv[NP];
 #pragma unroll
@@ -522,14 +628,26 @@ __global__ void mask_by_q_kernel(const int8_t *q, const float *g, i64 n, float *
 
 }  // namespace
 
+struct PlaneLaunch {
+    int grid, threads, warp_mode;
+};
+PlaneLaunch plane_launch(i64 nplanes, int HW) {
+    if (HW <= kWarpPlaneMaxHW) return {(int)((nplanes + 7) / 8), 256, 1};
+    return {(int)nplanes, plane_threads(HW), 0};
+}
+
 void act_stats(const Src &s, int B, float *y_out, float *mean_out, float *var_out, float *pool_out, float *vmax,
                cudaStream_t st) {
-    act_stats_kernel<<<B * s.C, plane_threads(s.HW), 0, st>>>(s, y_out, mean_out, var_out, pool_out, vmax);
+    const int np = B * s.C;
+    const PlaneLaunch L = plane_launch(np, s.HW);
+    act_stats_kernel<<<L.grid, L.threads, 0, st>>>(s, np, L.warp_mode, y_out, mean_out, var_out, pool_out, vmax);
     TRBA_LAUNCH_CHECK();
 }
 
 void act_quant(const Src &s, int B, const float *vmax, float *s_out, int8_t *q, bool relu, cudaStream_t st) {
-    act_quant_kernel<<<B * s.C, plane_threads(s.HW), 0, st>>>(s, vmax, s_out, q, relu ? 1 : 0);
+    const int np = B * s.C;
+    const PlaneLaunch L = plane_launch(np, s.HW);
+    act_quant_kernel<<<L.grid, L.threads, 0, st>>>(s, np, L.warp_mode, vmax, s_out, q, relu ? 1 : 0);
     TRBA_LAUNCH_CHECK();
 }
 
@@ -554,7 +672,7 @@ void se_backward(const float *dz, const float *y2, const float *gate, const floa
                  const float *w1, const float *w2, int B, int C, int HW, int R, float *dpre1, float *dpre2,
                  float *dpooled, float *dy2_full, cudaStream_t st) {
     (void)pool;
-    se_backward_kernel<<<B, 128, (2 * C + R) * sizeof(float), st>>>(dz, y2, gate, h1, w1, w2, C, HW, R, dpre1, dpre2,
+    se_backward_kernel<<<B, 256, (2 * C + R) * sizeof(float), st>>>(dz, y2, gate, h1, w1, w2, C, HW, R, dpre1, dpre2,
                                                                    dpooled, dy2_full);
     TRBA_LAUNCH_CHECK();
 }
@@ -567,22 +685,35 @@ void se_weight_grads(const float *dpre1, const float *dpre2, const float *h1, co
 
 void bn_bwd_sums(const float *dy, const float *x, const float *mean, const float *var, int B, int C, int HW,
                  double *acc, cudaStream_t st) {
-    bn_bwd_sums_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, C, HW, acc);
+    const int np = B * C;
+    const PlaneLaunch L = plane_launch(np, HW);
+    bn_bwd_sums_kernel<<<L.grid, L.threads, 0, st>>>(dy, x, mean, var, C, HW, np, L.warp_mode, acc);
     TRBA_LAUNCH_CHECK();
 }
 
 void bn_dx_max(const float *dy, const float *x, const float *mean, const float *var, const float *gamma,
                const double *acc, int B, int C, int HW, float *g_gamma, float *g_beta, float *vmax, cudaStream_t st) {
-    bn_dx_max_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, g_gamma, g_beta,
-                                                          vmax);
+    const int np = B * C;
+    const PlaneLaunch L = plane_launch(np, HW);
+    bn_dx_max_kernel<<<L.grid, L.threads, 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, np, L.warp_mode, g_gamma,
+                                                   g_beta, vmax);
     TRBA_LAUNCH_CHECK();
 }
 
 void bn_dx_quant(const float *dy, const float *x, const float *mean, const float *var, const float *gamma,
                  const double *acc, int B, int C, int HW, const float *vmax, float *s_dx, int8_t *A, int ld,
                  bool compat, cudaStream_t st) {
-    bn_dx_quant_kernel<<<B * C, plane_threads(HW), 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, vmax, s_dx, A,
-                                                            ld, compat ? 1 : 0);
+    if (compat) {
+        const i64 rows = (i64)B * HW;
+        dim3 grid((unsigned)((rows + kQtTile - 1) / kQtTile), (unsigned)((C + kQtTile - 1) / kQtTile));
+        bn_dx_quant_t_kernel<<<grid, 256, 5 * C * sizeof(float), st>>>(dy, x, mean, var, gamma, acc, B, C, HW, vmax,
+                                                                        s_dx, A, ld, rows);
+    } else {
+        const int np = B * C;
+        const PlaneLaunch L = plane_launch(np, HW);
+        bn_dx_quant_kernel<<<L.grid, L.threads, 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, np, L.warp_mode,
+                                                         vmax, s_dx, A, ld);
+    }
     TRBA_LAUNCH_CHECK();
 }
 
