@@ -34,86 +34,81 @@ __global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restr
     }
 }
 
-// The same operand, staged through shared memory in tiles of kTileRows rows.
-// Gather: consecutive threads take consecutive rows (output pixels) for one
-// column k = (c, kh, kw), so a warp's byte loads fall on neighbouring input
-// pixels; a table in shared memory gives every column its input offset
-// c*H*W + kh*W + kw and its (kh, kw), and every row of the tile its base
-// offset and window origin, so the gather does no divisions.  Store: the
-// tile is contiguous in col (ld = col_ld), written with 16-byte stores.
-// Shared memory: col_ld int2 (table) + kTileRows * (col_ld + 4) bytes (tile;
-// the 4-byte pad puts the rows of one column in distinct banks).
+// The same operand, staged through shared memory in tiles of kTileRows = 32
+// rows (output pixels).  Lane r of every warp owns row r of the tile (its
+// window origin and base offset live in registers); warp w gathers input
+// channels w, w + 8, ...: for a channel the kH x kW window bytes of the 32
+// rows are loaded together (neighbouring lanes read neighbouring input
+// pixels) and stored to the tile at column k = (c, kh, kw).  The tile is
+// contiguous in col (ld = col_ld) and leaves with 16-byte stores.  KH / KW
+// are compile-time for the 3x3, 2x2 and 1x1 convolutions (window bounds
+// checks hoisted out of the channel loop); 0 selects run-time loops.
+// Shared memory: kTileRows * (col_ld + 4) bytes (the 4-byte pad puts the 32
+// rows of one column in distinct banks).
 constexpr int kIm2colMaxLd = 4096;
 constexpr int kTileRows = 32;
-constexpr int kGatherBatch = 16;
 
+template <int KH, int KW>
 __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
-                                                          int C, int H, int W, int kH, int kW, int sH, int sW,
+                                                          int C, int H, int W, int kH_, int kW_, int sH, int sW,
                                                           int pH, int pW, int Ho, int Wo, int col_ld, i64 rows,
                                                           i64 rows_pad) {
-    extern __shared__ int2 ktab[];
-    __shared__ long long row_base[kTileRows];
-    __shared__ int row_ih[kTileRows], row_iw[kTileRows];
-    uint8_t *tile = reinterpret_cast<uint8_t *>(ktab + col_ld);
+    extern __shared__ uint8_t tile[];
+    const int kH = KH ? KH : kH_, kW = KW ? KW : kW_;
     const int pitch = col_ld + 4;
-    const int cols = C * kH * kW, khw = kH * kW;
-    for (int k = threadIdx.x; k < col_ld; k += blockDim.x) {
-        if (k < cols) {
-            const int c = k / khw, kk = k - c * khw, kh = kk / kW, kw = kk - kh * kW;
-            ktab[k] = make_int2(c * H * W + kh * W + kw, (kh << 16) | kw);
-        } else {
-            ktab[k] = make_int2(-1, 0);
-        }
-    }
-    const i64 hwo = (i64)Ho * Wo, chw = (i64)C * H * W;
+    const int khw = kH * kW, cols = C * khw;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const i64 hwo = (i64)Ho * Wo, chw = (i64)C * H * W, hw = (i64)H * W;
     const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
     const int chunks_per_row = col_ld >> 4;
+    uint8_t *trow = tile + lane * pitch;
     for (i64 t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const i64 r0 = t * kTileRows;
-        if (threadIdx.x < kTileRows) {
-            const i64 r = r0 + threadIdx.x;
-            if (r < rows) {
-                const i64 b = r / hwo;
-                const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
-                row_ih[threadIdx.x] = oh * sH - pH;
-                row_iw[threadIdx.x] = ow * sW - pW;
-                row_base[threadIdx.x] = b * chw + (i64)row_ih[threadIdx.x] * W + row_iw[threadIdx.x];
-            } else {
-                row_ih[threadIdx.x] = -(1 << 30);  // fails every bounds check: zero row
-                row_iw[threadIdx.x] = 0;
-                row_base[threadIdx.x] = 0;
-            }
+        const i64 r0 = t * kTileRows, r = r0 + lane;
+        int ih0 = -(1 << 28), iw0 = 0;  // rows past the end fail every bounds check
+        i64 base = 0;
+        if (r < rows) {
+            const i64 b = r / hwo;
+            const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
+            ih0 = oh * sH - pH;
+            iw0 = ow * sW - pW;
+            base = b * chw + (i64)ih0 * W + iw0;
         }
-        __syncthreads();
-        // kGatherBatch independent byte loads per thread are issued before
-        // any of them is stored, so enough loads are in flight per SM.
-        const int tile_elems = kTileRows * col_ld;
-        for (int e0 = threadIdx.x; e0 < tile_elems; e0 += blockDim.x * kGatherBatch) {
-            uint8_t v[kGatherBatch];
+        if constexpr (KH > 0 && KW > 0) {
+            bool okh[KH], okw[KW];
 #pragma unroll
-            for (int j = 0; j < kGatherBatch; ++j) {
-                const int e = e0 + j * blockDim.x;
-                v[j] = 0;
-                if (e < tile_elems) {
-                    const int r = e & (kTileRows - 1), k = e / kTileRows;
-                    const int2 tk = ktab[k];
-                    const int ih = row_ih[r] + (tk.y >> 16), iw = row_iw[r] + (tk.y & 0xffff);
-                    if (tk.x >= 0 && (unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
-                        v[j] = (uint8_t)in[row_base[r] + tk.x];
+            for (int i = 0; i < KH; ++i) okh[i] = (unsigned)(ih0 + i) < (unsigned)H;
+#pragma unroll
+            for (int j = 0; j < KW; ++j) okw[j] = (unsigned)(iw0 + j) < (unsigned)W;
+            for (int c = warp; c < C; c += nwarps) {
+                const int8_t *src = in + base + c * hw;
+                uint8_t v[KH * KW];
+#pragma unroll
+                for (int i = 0; i < KH; ++i)
+#pragma unroll
+                    for (int j = 0; j < KW; ++j) v[i * KW + j] = (okh[i] && okw[j]) ? (uint8_t)src[i * W + j] : 0;
+#pragma unroll
+                for (int e = 0; e < KH * KW; ++e) trow[c * KH * KW + e] = v[e];
+            }
+        } else {
+            for (int c = warp; c < C; c += nwarps) {
+                const int8_t *src = in + base + c * hw;
+                for (int i = 0; i < kH; ++i) {
+                    const bool oh = (unsigned)(ih0 + i) < (unsigned)H;
+                    for (int j = 0; j < kW; ++j) {
+                        const bool ok = oh && (unsigned)(iw0 + j) < (unsigned)W;
+                        trow[c * khw + i * kW + j] = ok ? (uint8_t)src[i * W + j] : 0;
+                    }
                 }
             }
-#pragma unroll
-            for (int j = 0; j < kGatherBatch; ++j) {
-                const int e = e0 + j * blockDim.x;
-                if (e < tile_elems) tile[(e & (kTileRows - 1)) * pitch + e / kTileRows] = v[j];
-            }
         }
+        for (int k = cols + warp; k < col_ld; k += nwarps) trow[k] = 0;  // K padding
         __syncthreads();
         const int live_rows = (int)min((i64)kTileRows, rows_pad - r0);
-        for (int c = threadIdx.x; c < live_rows * chunks_per_row; c += blockDim.x) {
-            const int r = c / chunks_per_row, cc = c - r * chunks_per_row;
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(tile + r * pitch + cc * 16);
-            *reinterpret_cast<uint4 *>(col + (r0 + r) * col_ld + cc * 16) = make_uint4(src[0], src[1], src[2], src[3]);
+        for (int cidx = threadIdx.x; cidx < live_rows * chunks_per_row; cidx += blockDim.x) {
+            const int rr = cidx / chunks_per_row, cc = cidx - rr * chunks_per_row;
+            const uint32_t *srcw = reinterpret_cast<const uint32_t *>(tile + rr * pitch + cc * 16);
+            *reinterpret_cast<uint4 *>(col + (r0 + rr) * col_ld + cc * 16) =
+                make_uint4(srcw[0], srcw[1], srcw[2], srcw[3]);
         }
         __syncthreads();
     }
@@ -294,19 +289,30 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
     const i64 total = ((rows + 15) / 16 * 16) * col_ld;
     if (col_ld <= kIm2colMaxLd && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {
         const i64 rows_pad = (rows + 15) / 16 * 16;
-        const size_t smem = sizeof(int2) * col_ld + (size_t)kTileRows * (col_ld + 4);
-        static bool attr[64] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
-            TRBA_CHECK(cudaFuncSetAttribute(im2col_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)(sizeof(int2) * kIm2colMaxLd + kTileRows * (kIm2colMaxLd + 4))));
-            attr[dev] = true;
-        }
+        const size_t smem = (size_t)kTileRows * (col_ld + 4);
         const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
         const i64 cap = (i64)sm_count() * 4;
-        im2col_tile_kernel<<<(unsigned)(ntiles < cap ? ntiles : cap), kThreads, smem, as_stream(s)>>>(
-            input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, rows_pad);
+        const unsigned grid = (unsigned)(ntiles < cap ? ntiles : cap);
+        auto go = [&](auto kern) {
+            static bool attr[64] = {};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr[dev]) {
+                TRBA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kTileRows * (kIm2colMaxLd + 4)));
+                attr[dev] = true;
+            }
+            kern<<<grid, kThreads, smem, as_stream(s)>>>(input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo,
+                                                         col_ld, rows, rows_pad);
+        };
+        if (kH == 3 && kW == 3)
+            go(im2col_tile_kernel<3, 3>);
+        else if (kH == 2 && kW == 2)
+            go(im2col_tile_kernel<2, 2>);
+        else if (kH == 1 && kW == 1)
+            go(im2col_tile_kernel<1, 1>);
+        else
+            go(im2col_tile_kernel<0, 0>);
     } else {
         im2col_pad_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(
             input, col, C, H, W, kH, kW, sH, sW, pH, pW, Ho, Wo, col_ld, rows, total);

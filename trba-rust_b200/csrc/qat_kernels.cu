@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go
                                                     int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW,
                                                     int Ho, int Wo, const int8_t *__restrict__ mask_q,
                                                     const float *__restrict__ add, float *__restrict__ gi,
-                                                    float neg_zero) {
+                                                    float neg_zero, int pair_mode) {
     constexpr int P = kDgradPx, CI = kDgradCi, NP = CI / 2;
     extern __shared__ float4 wsm4[];  // [taps][Cout][CI / 4] float4
     const int khw = kH * kW, ci0 = blockIdx.y * CI;
@@ -488,13 +488,26 @@ __global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go
     __syncthreads();
     const int hwo = Ho * Wo, hwi = H * W;
     const i64 npix = (i64)B * hwi;
-    const i64 pix0 = ((i64)blockIdx.x * blockDim.x + threadIdx.x) * P;
+    const i64 pair = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+    // pair_mode 0: pixels 2*pair and 2*pair + 1.  pair_mode 1 (stride 2 along
+    // W, W % 4 == 0): pixels iw and iw + 2 of one row, so both have the same
+    // valid taps.
+    i64 pix0;
+    if (pair_mode) {
+        const int half = W >> 1;
+        const i64 row = pair / half;
+        const int k = (int)(pair - row * half);
+        pix0 = row * W + 4 * (k >> 1) + (k & 1);
+    } else {
+        pix0 = pair * P;
+    }
     if (pix0 >= npix) return;
+    const int pstep = pair_mode ? 2 : 1;
     int pb[P], prem[P], pih[P], piw[P];
     bool live[P];
 #pragma unroll
     for (int p = 0; p < P; ++p) {
-        const i64 px = pix0 + p;
+        const i64 px = pix0 + (i64)p * pstep;
         live[p] = px < npix;
         const i64 q = live[p] ? px : pix0;
         pb[p] = (int)(q / hwi);
@@ -523,7 +536,7 @@ __global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go
             }
             if (!any) continue;
             const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * (CI / 4);
-#pragma unroll 4
+#pragma unroll 8
             for (int oc = 0; oc < Cout; ++oc) {
                 F2 wv[NP];
 #pragma unroll
@@ -735,10 +748,11 @@ void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B,
         TRBA_CHECK(cudaFuncSetAttribute(dgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr[dev] = true;
     }
+    const int pair_mode = (sw == 2 && (W & 3) == 0) ? 1 : 0;
     const i64 per_cta = 256 * kDgradPx;
     dim3 grid((unsigned)((npix + per_cta - 1) / per_cta), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
     dgrad_kernel<<<grid, 256, smem, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
-                                          mask_q, add, gi, -0.0f);
+                                          mask_q, add, gi, -0.0f, pair_mode);
     TRBA_LAUNCH_CHECK();
 }
 
