@@ -69,15 +69,51 @@ struct PlaneSrc {
     float mean, r, gamma, beta, gate, res_s;
     const float *res_f;
     const int8_t *res_q;
-    __device__ __forceinline__ float at(i64 i) const {
+    __device__ __forceinline__ float one(float xv, i64 i) const {
         switch (kind) {
-            case SRC_BN: return fadd(fmul(fmul(fsub(x[i], mean), r), gamma), beta);
-            case SRC_FLOAT: return x[i];
-            case SRC_SE_RES_F: return fadd(fmul(x[i], gate), res_f[i]);
-            default: return fadd(fmul(x[i], gate), fmul((float)res_q[i], res_s));
+            case SRC_BN: return fadd(fmul(fmul(fsub(xv, mean), r), gamma), beta);
+            case SRC_FLOAT: return xv;
+            case SRC_SE_RES_F: return fadd(fmul(xv, gate), res_f[i]);
+            default: return fadd(fmul(xv, gate), fmul((float)res_q[i], res_s));
+        }
+    }
+    __device__ __forceinline__ float at(i64 i) const { return one(x[i], i); }
+    // Four consecutive elements from a 16-byte aligned index i.
+    __device__ __forceinline__ float4 at4(i64 i) const {
+        const float4 xv = *reinterpret_cast<const float4 *>(x + i);
+        float4 v;
+        switch (kind) {
+            case SRC_BN:
+                v.x = fadd(fmul(fmul(fsub(xv.x, mean), r), gamma), beta);
+                v.y = fadd(fmul(fmul(fsub(xv.y, mean), r), gamma), beta);
+                v.z = fadd(fmul(fmul(fsub(xv.z, mean), r), gamma), beta);
+                v.w = fadd(fmul(fmul(fsub(xv.w, mean), r), gamma), beta);
+                return v;
+            case SRC_FLOAT: return xv;
+            case SRC_SE_RES_F: {
+                const float4 rf = *reinterpret_cast<const float4 *>(res_f + i);
+                v.x = fadd(fmul(xv.x, gate), rf.x);
+                v.y = fadd(fmul(xv.y, gate), rf.y);
+                v.z = fadd(fmul(xv.z, gate), rf.z);
+                v.w = fadd(fmul(xv.w, gate), rf.w);
+                return v;
+            }
+            default: {
+                const char4 rq = *reinterpret_cast<const char4 *>(res_q + i);
+                v.x = fadd(fmul(xv.x, gate), fmul((float)rq.x, res_s));
+                v.y = fadd(fmul(xv.y, gate), fmul((float)rq.y, res_s));
+                v.z = fadd(fmul(xv.z, gate), fmul((float)rq.z, res_s));
+                v.w = fadd(fmul(xv.w, gate), fmul((float)rq.w, res_s));
+                return v;
+            }
         }
     }
 };
+
+// Planes whose length is a multiple of 4 are read as float4 (all buffers
+// are 256-byte aligned, so a plane starting at a multiple of 4 elements is
+// 16-byte aligned).
+__device__ __forceinline__ bool vec4_ok(int HW) { return (HW & 3) == 0; }
 
 // Planes of HW elements are processed one per warp when small (8 planes per
 // 256-thread CTA) and one per CTA otherwise; PlaneIdx says which plane a
@@ -152,11 +188,20 @@ __global__ void act_stats_kernel(Src s, int nplanes, int warp_mode, float *y_out
     double sum = 0.0;
     float mx = 0.0f;
     if (q.live) {
-        for (int j = q.lane; j < s.HW; j += q.width) {
-            const float v = p.at(base + j);
-            if (y_out) y_out[base + j] = v;
-            sum += (double)v;
-            mx = fmaxf(mx, fabsf(v));
+        if (vec4_ok(s.HW)) {
+            for (int j = 4 * q.lane; j < s.HW; j += 4 * q.width) {
+                const float4 v = p.at4(base + j);
+                if (y_out) *reinterpret_cast<float4 *>(y_out + base + j) = v;
+                sum += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+        } else {
+            for (int j = q.lane; j < s.HW; j += q.width) {
+                const float v = p.at(base + j);
+                if (y_out) y_out[base + j] = v;
+                sum += (double)v;
+                mx = fmaxf(mx, fabsf(v));
+            }
         }
     }
     if (pool_out) {
@@ -179,10 +224,17 @@ __global__ void act_quant_kernel(Src s, int nplanes, int warp_mode, const float 
     const float inv = fdiv(1.0f, sc);
     if (q.plane == 0 && q.leader && s_out) *s_out = sc;
     const i64 base = (i64)q.plane * s.HW;
-    for (int j = q.lane; j < s.HW; j += q.width) {
-        const float v = p.at(base + j);
+    auto quant = [&](float v) -> int8_t {
         const float t = relu ? fminf(fmul(fmaxf(v, 0.0f), inv), 127.0f) : fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f);
-        qo[base + j] = (int8_t)rint_even(t);
+        return (int8_t)rint_even(t);
+    };
+    if (vec4_ok(s.HW)) {
+        for (int j = 4 * q.lane; j < s.HW; j += 4 * q.width) {
+            const float4 v = p.at4(base + j);
+            *reinterpret_cast<char4 *>(qo + base + j) = make_char4(quant(v.x), quant(v.y), quant(v.z), quant(v.w));
+        }
+    } else {
+        for (int j = q.lane; j < s.HW; j += q.width) qo[base + j] = quant(p.at(base + j));
     }
 }
 
@@ -282,21 +334,27 @@ __global__ void se_backward_kernel(const float *dz, const float *y2, const float
 }
 
 // g_w2[c, j] += sum_b dpre2[b,c] h1[b,j];  g_w1[j, i] += sum_b dpre1[b,j] pool[b,i]
+// One warp per weight: lanes stride over the batch, f64 products summed
+// with a warp reduction and rounded once.
 __global__ void se_wgrad_kernel(const float *dpre1, const float *dpre2, const float *h1, const float *pool, int B,
                                 int C, int R, float *g_w1, float *g_w2) {
     const int n2 = C * R;
-    GRID_LOOP(e, (i64)2 * n2) {
-        double acc = 0.0;
-        if (e < n2) {
-            const int c = (int)(e / R), j = (int)(e - (i64)c * R);
-            for (int b = 0; b < B; ++b) acc = fma((double)dpre2[(i64)b * C + c], (double)h1[(i64)b * R + j], acc);
-            g_w2[e] = fadd(g_w2[e], (float)acc);
-        } else {
-            const i64 f = e - n2;
-            const int j = (int)(f / C), i = (int)(f - (i64)j * C);
-            for (int b = 0; b < B; ++b) acc = fma((double)dpre1[(i64)b * R + j], (double)pool[(i64)b * C + i], acc);
-            g_w1[f] = fadd(g_w1[f], (float)acc);
-        }
+    const i64 e = (i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (e >= 2 * (i64)n2) return;
+    double acc = 0.0;
+    if (e < n2) {
+        const int c = (int)(e / R), j = (int)(e - (i64)c * R);
+        for (int b = lane; b < B; b += 32) acc = fma((double)dpre2[(i64)b * C + c], (double)h1[(i64)b * R + j], acc);
+        acc = warp_sum_d(acc);
+        if (lane == 0) g_w2[e] = fadd(g_w2[e], (float)acc);
+    } else {
+        const i64 f = e - n2;
+        const int j = (int)(f / C), i = (int)(f - (i64)j * C);
+        for (int b = lane; b < B; b += 32)
+            acc = fma((double)dpre1[(i64)b * R + j], (double)pool[(i64)b * C + i], acc);
+        acc = warp_sum_d(acc);
+        if (lane == 0) g_w1[f] = fadd(g_w1[f], (float)acc);
     }
 }
 
@@ -311,11 +369,21 @@ __global__ void bn_bwd_sums_kernel(const float *dy, const float *x, const float 
     const i64 base = (i64)q.plane * HW;
     double s = 0.0, sx = 0.0;
     if (q.live) {
-        for (int j = q.lane; j < HW; j += q.width) {
-            const float d = dy[base + j];
-            const float xh = fmul(fsub(x[base + j], m), r);
-            s += (double)d;
-            sx += (double)fmul(d, xh);
+        if (vec4_ok(HW)) {
+            for (int j = 4 * q.lane; j < HW; j += 4 * q.width) {
+                const float4 d = *reinterpret_cast<const float4 *>(dy + base + j);
+                const float4 xv = *reinterpret_cast<const float4 *>(x + base + j);
+                s += (double)d.x + (double)d.y + (double)d.z + (double)d.w;
+                sx += (double)fmul(d.x, fmul(fsub(xv.x, m), r)) + (double)fmul(d.y, fmul(fsub(xv.y, m), r)) +
+                      (double)fmul(d.z, fmul(fsub(xv.z, m), r)) + (double)fmul(d.w, fmul(fsub(xv.w, m), r));
+            }
+        } else {
+            for (int j = q.lane; j < HW; j += q.width) {
+                const float d = dy[base + j];
+                const float xh = fmul(fsub(x[base + j], m), r);
+                s += (double)d;
+                sx += (double)fmul(d, xh);
+            }
         }
     }
     const double ts = plane_sum_d(s, warp_mode, smd);
@@ -359,8 +427,18 @@ __global__ void bn_dx_max_kernel(const float *dy, const float *x, const float *m
     }
     const i64 base = (i64)q.plane * HW;
     float mx = 0.0f;
-    if (q.live)
-        for (int j = q.lane; j < HW; j += q.width) mx = fmaxf(mx, fabsf(dx_at(p, dy[base + j], x[base + j])));
+    if (q.live) {
+        if (vec4_ok(HW)) {
+            for (int j = 4 * q.lane; j < HW; j += 4 * q.width) {
+                const float4 d = *reinterpret_cast<const float4 *>(dy + base + j);
+                const float4 xv = *reinterpret_cast<const float4 *>(x + base + j);
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(dx_at(p, d.x, xv.x)), fabsf(dx_at(p, d.y, xv.y))),
+                                     fmaxf(fabsf(dx_at(p, d.z, xv.z)), fabsf(dx_at(p, d.w, xv.w)))));
+            }
+        } else {
+            for (int j = q.lane; j < HW; j += q.width) mx = fmaxf(mx, fabsf(dx_at(p, dy[base + j], x[base + j])));
+        }
+    }
     const float t = block_max_f(mx, smf);
     if (threadIdx.x == 0) atomic_max_nonneg(vmax, t);
 }
@@ -382,8 +460,18 @@ __global__ void bn_dx_quant_kernel(const float *dy, const float *x, const float 
     const float inv = fdiv(1.0f, sc);
     if (q.plane == 0 && q.leader) *s_dx = sc;
     const i64 base = (i64)q.plane * HW;
-    for (int j = q.lane; j < HW; j += q.width)
-        A[(i64)c * ld + (i64)b * HW + j] = quant_dx(dx_at(p, dy[base + j], x[base + j]), inv);
+    int8_t *arow = A + (i64)c * ld + (i64)b * HW;
+    if (vec4_ok(HW)) {
+        for (int j = 4 * q.lane; j < HW; j += 4 * q.width) {
+            const float4 d = *reinterpret_cast<const float4 *>(dy + base + j);
+            const float4 xv = *reinterpret_cast<const float4 *>(x + base + j);
+            *reinterpret_cast<char4 *>(arow + j) =
+                make_char4(quant_dx(dx_at(p, d.x, xv.x), inv), quant_dx(dx_at(p, d.y, xv.y), inv),
+                           quant_dx(dx_at(p, d.z, xv.z), inv), quant_dx(dx_at(p, d.w, xv.w), inv));
+        }
+    } else {
+        for (int j = q.lane; j < HW; j += q.width) arow[j] = quant_dx(dx_at(p, dy[base + j], x[base + j]), inv);
+    }
 }
 
 // The reference-compatible operand (src/qnet.rs:984-1001: transpose_i8 of the
@@ -393,11 +481,32 @@ __global__ void bn_dx_quant_kernel(const float *dy, const float *x, const float 
 // channels sit in shared memory.
 constexpr int kQtTile = 32;
 
+// Division of 32-bit unsigned numerators by a run-time constant d >= 1:
+// n / d = umulhi(n, m) >> s with m, s chosen on the host (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994;
+// the round-up method with a 33-bit multiplier, split as 2^32 + m).
+struct FastDiv {
+    uint32_t d, m, s;
+    __host__ static FastDiv make(uint32_t d) {
+        FastDiv f;
+        f.d = d;
+        uint32_t l = 0;
+        while ((1ull << l) < d) ++l;  // l = ceil(log2 d)
+        f.m = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+        f.s = l;
+        return f;
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        const uint32_t t = __umulhi(n, m);
+        return s == 0 ? n : (t + ((n - t) >> 1)) >> (s - 1);
+    }
+};
+
 __global__ void __launch_bounds__(256) bn_dx_quant_t_kernel(const float *dy, const float *x, const float *mean,
                                                             const float *var, const float *gamma,
                                                             const double *acc, int B, int C, int HW,
                                                             const float *vmax, float *s_dx, int8_t *A, int ld,
-                                                            i64 rows) {
+                                                            i64 rows, FastDiv div_hw, FastDiv div_c) {
     extern __shared__ float chs[];  // [5][C]: m, r, a, sdy, sdxh
     __shared__ int8_t tile[kQtTile][kQtTile + 4];
     const i64 count = (i64)B * HW;
@@ -423,7 +532,8 @@ __global__ void __launch_bounds__(256) bn_dx_quant_t_kernel(const float *dy, con
         int8_t v = 0;
         if (r < rows && o < C) {
             const i64 i = r * C + o;
-            const int c = (int)((i / HW) % C);
+            const uint32_t plane = div_hw.div((uint32_t)i);
+            const int c = (int)(plane - div_c.div(plane) * (uint32_t)C);
             DxPlane p;
             p.m = chs[c];
             p.r = chs[C + c];
@@ -692,7 +802,8 @@ void se_backward(const float *dz, const float *y2, const float *gate, const floa
 
 void se_weight_grads(const float *dpre1, const float *dpre2, const float *h1, const float *pool, int B, int C, int R,
                      float *g_w1, float *g_w2, cudaStream_t st) {
-    se_wgrad_kernel<<<grid_for(2 * C * R, 128), 128, 0, st>>>(dpre1, dpre2, h1, pool, B, C, R, g_w1, g_w2);
+    const i64 warps = 2LL * C * R;
+    se_wgrad_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(dpre1, dpre2, h1, pool, B, C, R, g_w1, g_w2);
     TRBA_LAUNCH_CHECK();
 }
 
@@ -719,8 +830,10 @@ void bn_dx_quant(const float *dy, const float *x, const float *mean, const float
     if (compat) {
         const i64 rows = (i64)B * HW;
         dim3 grid((unsigned)((rows + kQtTile - 1) / kQtTile), (unsigned)((C + kQtTile - 1) / kQtTile));
+        TRBA_REQUIRE(rows * C < (1ll << 32), "bn_dx_quant: tensor too large for 32-bit indexing");
         bn_dx_quant_t_kernel<<<grid, 256, 5 * C * sizeof(float), st>>>(dy, x, mean, var, gamma, acc, B, C, HW, vmax,
-                                                                        s_dx, A, ld, rows);
+                                                                        s_dx, A, ld, rows, FastDiv::make(HW),
+                                                                        FastDiv::make(C));
     } else {
         const int np = B * C;
         const PlaneLaunch L = plane_launch(np, HW);
