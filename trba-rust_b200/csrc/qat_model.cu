@@ -1093,7 +1093,7 @@ void trba_model_default_config(trba_model_config *c) {
 
 trba_model *trba_model_create(const trba_model_config *cfg) {
     if (!cfg || cfg->fd < 16 || cfg->fd % 16 || cfg->fd > 512 || cfg->batch <= 0 || cfg->hidden <= 0 ||
-        cfg->hidden > 128 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
+        cfg->hidden > 128 || cfg->hidden % 8 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
         (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0) {
         report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
         return nullptr;

@@ -73,111 +73,154 @@ __global__ void sgemm_finish_kernel(Gemm g, int splits) {
 }
 
 // -------------------------------------------------------------- LSTM --
-constexpr int BG = 4;  // samples per CTA in the recurrences
+// One CTA per sample: the recurrent weights (4H x H) sit in shared memory,
+// the 4H gate outputs of a step are spread over the threads, and the H-long
+// (forward) or 4H-long (backward) dot products run as independent partial
+// sums (two per thread forward; four lanes per output backward) so the f64
+// multiply-add chains stay short.
 
-__global__ void lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B,
-                                int T, int H, int rev, float *gates, float *c_tr, float *h_prev_tr, float *cat,
-                                int dir) {
+__global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh,
+                                                       const float *w_hh, int B, int T, int H, int rev,
+                                                       float *gates, float *c_tr, float *h_prev_tr, float *cat,
+                                                       int dir) {
     extern __shared__ float sm[];
     const int G4 = 4 * H;
-    float *wT = sm;                  // [H][4H]: wT[k*4H + o] = w_hh[o*H + k]
-    float *hb = wT + H * G4;         // [BG][H]
-    float *cb = hb + BG * H;         // [BG][H]
-    float *gb = cb + BG * H;         // [BG][4H]
-    const int b0 = blockIdx.x * BG;
+    float *wT = sm;           // [H][4H]: wT[k*4H + o] = w_hh[o*H + k]
+    float *hb = wT + H * G4;  // [H]
+    float *cb = hb + H;       // [H]
+    float *gb = cb + H;       // [4H]
+    const int b = blockIdx.x;
     for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) {
         const int o = e / H, k = e - o * H;
         wT[k * G4 + o] = w_hh[e];
     }
-    for (int e = threadIdx.x; e < BG * H; e += blockDim.x) hb[e] = cb[e] = 0.0f;
+    for (int e = threadIdx.x; e < H; e += blockDim.x) hb[e] = cb[e] = 0.0f;
     __syncthreads();
     for (int s = 0; s < T; ++s) {
         const int tt = rev ? T - 1 - s : s;
-        for (int e = threadIdx.x; e < BG * G4; e += blockDim.x) {
-            const int g = e / G4, o = e - g * G4, b = b0 + g;
-            if (b >= B) continue;
-            double acc = 0.0;
-            for (int k = 0; k < H; ++k) acc = fma((double)hb[g * H + k], (double)wT[k * G4 + o], acc);
-            gb[e] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[((i64)b * T + tt) * G4 + o]), (float)acc);
+        const i64 r = (i64)b * T + tt;
+        for (int o = threadIdx.x; o < G4; o += blockDim.x) {
+            double a0 = 0.0, a1 = 0.0;
+            int k = 0;
+            for (; k + 1 < H; k += 2) {
+                a0 = fma((double)hb[k], (double)wT[k * G4 + o], a0);
+                a1 = fma((double)hb[k + 1], (double)wT[(k + 1) * G4 + o], a1);
+            }
+            if (k < H) a0 = fma((double)hb[k], (double)wT[k * G4 + o], a0);
+            gb[o] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[r * G4 + o]), (float)(a0 + a1));
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
-            const int g = e / H, i = e - g * H, b = b0 + g;
-            if (b >= B) continue;
-            const float *pg = gb + g * G4;
-            const float ig = sigm(pg[i]), fg = sigm(pg[H + i]), cg = cr_tanhf(pg[2 * H + i]), og = sigm(pg[3 * H + i]);
-            const float cn = fadd(fmul(fg, cb[e]), fmul(ig, cg));
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float ig = sigm(gb[i]), fg = sigm(gb[H + i]), cg = cr_tanhf(gb[2 * H + i]), og = sigm(gb[3 * H + i]);
+            const float cn = fadd(fmul(fg, cb[i]), fmul(ig, cg));
             const float hn = fmul(og, cr_tanhf(cn));
-            const i64 r = (i64)b * T + tt;
             gates[r * G4 + i] = ig;
             gates[r * G4 + H + i] = fg;
             gates[r * G4 + 2 * H + i] = cg;
             gates[r * G4 + 3 * H + i] = og;
             c_tr[r * H + i] = cn;
-            h_prev_tr[r * H + i] = hb[e];
+            h_prev_tr[r * H + i] = hb[i];
             cat[r * 2 * H + dir * H + i] = hn;
-            cb[e] = cn;
-            hb[e] = hn;  // only this thread touches hb[e] in this phase
+            cb[i] = cn;
+            hb[i] = hn;  // only this thread touches hb[i] in this phase
         }
         __syncthreads();
     }
 }
 
-__global__ void lstm_bwd_kernel(const float *dcat, const float *gates, const float *c_tr, const float *w_hh, int B,
-                                int T, int H, int rev, int dir, float *dgates) {
+__global__ void __launch_bounds__(256) lstm_bwd_kernel(const float *dcat, const float *gates, const float *c_tr,
+                                                       const float *w_hh, int B, int T, int H, int rev, int dir,
+                                                       float *dgates) {
     extern __shared__ float sm[];
     const int G4 = 4 * H;
-    float *w = sm;                   // [4H][H] natural layout
-    float *dhn = w + G4 * H;         // [BG][H]
-    float *dcn = dhn + BG * H;       // [BG][H]
-    float *dg = dcn + BG * H;        // [BG][4H]
-    const int b0 = blockIdx.x * BG;
+    float *w = sm;            // [4H][H] natural layout
+    float *dhn = w + G4 * H;  // [H]
+    float *dcn = dhn + H;     // [H]
+    float *dg = dcn + H;      // [4H]
+    const int b = blockIdx.x;
     for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) w[e] = w_hh[e];
-    for (int e = threadIdx.x; e < BG * H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
+    for (int e = threadIdx.x; e < H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
     __syncthreads();
     for (int s = T - 1; s >= 0; --s) {
         const int tt = rev ? T - 1 - s : s;
         const int tp = rev ? tt + 1 : tt - 1;  // time position of the previous slot
-        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
-            const int g = e / H, i = e - g * H, b = b0 + g;
-            if (b >= B) continue;
-            const i64 r = (i64)b * T + tt;
+        const i64 r = (i64)b * T + tt;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
             const float ig = gates[r * G4 + i], fg = gates[r * G4 + H + i], cg = gates[r * G4 + 2 * H + i],
                         og = gates[r * G4 + 3 * H + i];
             const float tc = cr_tanhf(c_tr[r * H + i]);
             const float cp = s > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
-            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[e]);
-            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[e], fg));
-            float *d = dg + g * G4;
-            d[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
-            d[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
-            d[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
-            d[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
-            dcn[e] = dc;
-            for (int q = 0; q < 4; ++q) dgates[r * G4 + q * H + i] = d[q * H + i];
+            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[i]);
+            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
+            dg[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            dg[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            dg[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            dg[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            dcn[i] = dc;
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < BG * H; e += blockDim.x) {
-            const int g = e / H, k = e - g * H;
-            if (b0 + g >= B) continue;
+        for (int o = threadIdx.x; o < G4; o += blockDim.x) dgates[r * G4 + o] = dg[o];
+        // dh_prev[k] = sum_o dg[o] w[o, k]: four consecutive lanes per k, each
+        // over o = q, q + 4, ..., combined with two shuffles
+        for (int e = threadIdx.x; e < 4 * H; e += blockDim.x) {
+            const int k = e >> 2, q = e & 3;
             double acc = 0.0;
-            for (int o = 0; o < G4; ++o) acc = fma((double)dg[g * G4 + o], (double)w[o * H + k], acc);
-            dhn[e] = (float)acc;
+            for (int o = q; o < G4; o += 4) acc = fma((double)dg[o], (double)w[o * H + k], acc);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (q == 0) dhn[k] = (float)acc;
         }
         __syncthreads();
     }
 }
 
 // ------------------------------------------------------ attention dec --
-__global__ void attn_fwd_kernel(AttnFwd a) {
+// Attention decoder.  A CTA runs kAttnS samples through all decoder steps
+// with every thread busy: the recurrent weights sit in shared memory once per
+// CTA, each phase of a step spreads its (sample, output) pairs over all
+// threads, and the T- or H-long reductions that feed a single value run
+// across a warp.  Dot products accumulate in f64 and round once; the
+// element-wise expressions keep the reference's f32 order.
+constexpr int kAttnS = 4;
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// sum_k x[k] * w[k * stride] over k < n, f64, two interleaved partial sums.
+__device__ __forceinline__ double dot2_d(const float *x, const float *w, int stride, int n) {
+    double a0 = 0.0, a1 = 0.0;
+    int k = 0;
+    for (; k + 1 < n; k += 2) {
+        a0 = fma((double)x[k], (double)w[(i64)k * stride], a0);
+        a1 = fma((double)x[k + 1], (double)w[(i64)(k + 1) * stride], a1);
+    }
+    if (k < n) a0 = fma((double)x[k], (double)w[(i64)k * stride], a0);
+    return a0 + a1;
+}
+
+__global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
     extern __shared__ float sm[];
-    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
     float *wihT = sm;             // [H][4H], context columns of w_ih, transposed
     float *whhT = wihT + H * G4;  // [H][4H]
     float *h2hT = whhT + H * G4;  // [H][H]:  h2hT[j*H + k] = h2h_w[k*H + j]
-    float *h = h2hT + H * H, *c = h + H, *phh = c + H, *ctx = phh + H, *pre = ctx + H;  // pre: 4H
-    float *tn = pre + G4, *e = tn + T * H, *al = e + T;
-    const int b = blockIdx.x;
+    float *h = h2hT + H * H;      // [S][H]
+    float *c = h + S * H, *phh = c + S * H, *ctx = phh + S * H;  // [S][H]
+    float *pre = ctx + S * H;     // [S][4H]
+    float *tn = pre + S * G4;     // [S][T][H]
+    float *e = tn + S * T * H;    // [S][T]
+    float *al = e + S * T;        // [S][T]
+    int *tok = reinterpret_cast<int *>(al + S * T);  // [S]
+    const int b0 = blockIdx.x * S;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
         const int o = i / H, k = i - o * H;
         wihT[k * G4 + o] = a.w_ih[(i64)o * CV + k];
@@ -187,173 +230,225 @@ __global__ void attn_fwd_kernel(AttnFwd a) {
         const int k = i / H, j = i - k * H;
         h2hT[j * H + k] = a.h2h_w[i];
     }
-    for (int i = threadIdx.x; i < H; i += blockDim.x) h[i] = c[i] = 0.0f;
+    for (int i = threadIdx.x; i < S * H; i += blockDim.x) h[i] = c[i] = 0.0f;
     __syncthreads();
-    const float *bh = a.bh + (i64)b * T * H, *ph = a.proj_h + (i64)b * T * H;
     for (int st = 0; st < a.steps; ++st) {
-        const i64 sb = (i64)st * a.B + b;
-        for (int k = threadIdx.x; k < H; k += blockDim.x) {  // proj_hh = h2h(h), bias first
-            double acc = 0.0;
-            for (int j = 0; j < H; ++j) acc = fma((double)h[j], (double)h2hT[j * H + k], acc);
-            phh[k] = fadd((float)acc, a.h2h_b[k]);
+        // proj_hh = h2h(h) + bias
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H;
+            phh[i] = fadd((float)dot2_d(h + sl * H, h2hT + k, H, H), a.h2h_b[k]);
+        }
+        if (threadIdx.x < S) {
+            const int b = min(b0 + (int)threadIdx.x, a.B - 1);
+            tok[threadIdx.x] = a.text_in[(i64)b * a.steps + st];
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
-            const int k = i % H;
-            const float v = cr_tanhf(fadd(ph[i], phh[k]));
+        // tanh(proj_H + proj_hh)
+        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+            const int sl = i / (T * H), r = i - sl * T * H, k = r % H;
+            const int b = b0 + sl;
+            const float v = cr_tanhf(fadd(a.proj_h[((i64)min(b, a.B - 1) * T) * H + r], phh[sl * H + k]));
             tn[i] = v;
-            a.tanh_tr[sb * T * H + i] = v;
+            if (b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T) * H + r] = v;
         }
         __syncthreads();
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        // scores e = tanh(.) . score_w, one warp per (sample, t)
+        for (int p = warp; p < S * T; p += nwarps) {
             double acc = 0.0;
-            for (int k = 0; k < H; ++k) acc = fma((double)tn[t * H + k], (double)a.score_w[k], acc);
-            e[t] = (float)acc;
+            for (int k = lane; k < H; k += 32) acc = fma((double)tn[p * H + k], (double)a.score_w[k], acc);
+            acc = warp_sum_d(acc);
+            if (lane == 0) e[p] = (float)acc;
         }
         __syncthreads();
-        if (threadIdx.x == 0) {  // softmax over T
+        // softmax over T, one warp per sample
+        for (int sl = warp; sl < S; sl += nwarps) {
             float mx = -INFINITY;
-            for (int t = 0; t < T; ++t) mx = fmaxf(mx, e[t]);
-            double s = 0.0;
-            for (int t = 0; t < T; ++t) {
-                al[t] = cr_expf(fsub(e[t], mx));
-                s += (double)al[t];
+            for (int t = lane; t < T; t += 32) mx = fmaxf(mx, e[sl * T + t]);
+            mx = warp_max_f(mx);
+            double sum = 0.0;
+            for (int t = lane; t < T; t += 32) {
+                const float v = cr_expf(fsub(e[sl * T + t], mx));
+                al[sl * T + t] = v;
+                sum += (double)v;
             }
-            const float sf = (float)s;
-            for (int t = 0; t < T; ++t) al[t] = fdiv(al[t], sf);
+            const float sf = (float)warp_sum_d(sum);
+            const int b = b0 + sl;
+            for (int t = lane; t < T; t += 32) {
+                const float v = fdiv(al[sl * T + t], sf);
+                al[sl * T + t] = v;
+                if (b < a.B) a.alpha[((i64)st * a.B + b) * T + t] = v;
+            }
         }
         __syncthreads();
-        const int tok = a.text_in[(i64)b * a.steps + st];
-        for (int k = threadIdx.x; k < H; k += blockDim.x) {
+        // context and the decoder cell input [ctx, one-hot token]
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H;
+            const int b = min(b0 + sl, a.B - 1);
             double acc = 0.0;
-            for (int t = 0; t < T; ++t) acc = fma((double)al[t], (double)bh[t * H + k], acc);
-            ctx[k] = (float)acc;
-        }
-        for (int t = threadIdx.x; t < T; t += blockDim.x) a.alpha[sb * T + t] = al[t];
-        __syncthreads();
-        for (int i = threadIdx.x; i < CV; i += blockDim.x)
-            a.cell_in[sb * CV + i] = i < H ? ctx[i] : (i - H == tok ? 1.0f : 0.0f);
-        for (int o = threadIdx.x; o < G4; o += blockDim.x) {
-            double dc = 0.0, dh = 0.0;
-            for (int k = 0; k < H; ++k) dc = fma((double)ctx[k], (double)wihT[k * G4 + o], dc);
-            for (int k = 0; k < H; ++k) dh = fma((double)h[k], (double)whhT[k * G4 + o], dh);
-            // (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h
-            pre[o] = fadd(fadd(fadd(fadd(a.b_ih[o], a.b_hh[o]), (float)dc), a.w_ih[(i64)o * CV + H + tok]), (float)dh);
+            for (int t = 0; t < T; ++t) acc = fma((double)al[sl * T + t], (double)a.bh[((i64)b * T + t) * H + k], acc);
+            ctx[i] = (float)acc;
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
-            const float ig = sigm(pre[i]), fg = sigm(pre[H + i]), cg = cr_tanhf(pre[2 * H + i]), og = sigm(pre[3 * H + i]);
+        for (int i = threadIdx.x; i < S * CV; i += blockDim.x) {
+            const int sl = i / CV, j = i - sl * CV, b = b0 + sl;
+            if (b < a.B)
+                a.cell_in[((i64)st * a.B + b) * CV + j] = j < H ? ctx[sl * H + j] : (j - H == tok[sl] ? 1.0f : 0.0f);
+        }
+        // gate pre-activations: (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h
+        for (int i = threadIdx.x; i < S * G4; i += blockDim.x) {
+            const int sl = i / G4, o = i - sl * G4;
+            const double dc = dot2_d(ctx + sl * H, wihT + o, G4, H);
+            const double dh = dot2_d(h + sl * H, whhT + o, G4, H);
+            pre[i] = fadd(fadd(fadd(fadd(a.b_ih[o], a.b_hh[o]), (float)dc), a.w_ih[(i64)o * CV + H + tok[sl]]),
+                          (float)dh);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H, b = b0 + sl;
+            const float *pg = pre + sl * G4;
+            const float ig = sigm(pg[k]), fg = sigm(pg[H + k]), cg = cr_tanhf(pg[2 * H + k]), og = sigm(pg[3 * H + k]);
             const float cn = fadd(fmul(fg, c[i]), fmul(ig, cg));
             const float hn = fmul(og, cr_tanhf(cn));
-            a.gates[sb * G4 + i] = ig;
-            a.gates[sb * G4 + H + i] = fg;
-            a.gates[sb * G4 + 2 * H + i] = cg;
-            a.gates[sb * G4 + 3 * H + i] = og;
-            a.cs[sb * H + i] = cn;
-            a.hs[sb * H + i] = hn;
+            if (b < a.B) {
+                const i64 sb = (i64)st * a.B + b;
+                a.gates[sb * G4 + k] = ig;
+                a.gates[sb * G4 + H + k] = fg;
+                a.gates[sb * G4 + 2 * H + k] = cg;
+                a.gates[sb * G4 + 3 * H + k] = og;
+                a.cs[sb * H + k] = cn;
+                a.hs[sb * H + k] = hn;
+            }
             c[i] = cn;
+            h[i] = hn;
         }
-        __syncthreads();
-        for (int i = threadIdx.x; i < H; i += blockDim.x) h[i] = a.hs[sb * H + i];
         __syncthreads();
     }
 }
 
-__global__ void attn_bwd_kernel(AttnBwd a) {
+__global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
     extern __shared__ float sm[];
-    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
     float *wc = sm;                 // [4H][H] context columns of w_ih
     float *whh = wc + G4 * H;       // [4H][H]
     float *h2h = whh + G4 * H;      // [H][H]
-    float *dhn = h2h + H * H, *dcn = dhn + H, *dg = dcn + H, *dctx = dg + G4, *dhp = dctx + H, *dphh = dhp + H;
-    float *da = dphh + H, *de = da + T, *dot = de + T;  // dot: 1
-    float *acc_bh = dot + 1, *acc_ph = acc_bh + T * H;
-    const int b = blockIdx.x;
+    float *dhn = h2h + H * H;       // [S][H]
+    float *dcn = dhn + S * H, *dctx = dcn + S * H, *dhp = dctx + S * H, *dphh = dhp + S * H;  // [S][H]
+    float *dg = dphh + S * H;       // [S][4H]
+    float *da = dg + S * G4, *de = da + S * T, *dot = de + S * T;  // [S][T], [S][T], [S]
+    float *acc_bh = dot + S, *acc_ph = acc_bh + S * T * H;        // [S][T][H]
+    const int b0 = blockIdx.x * S;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
         const int o = i / H, k = i - o * H;
         wc[i] = a.w_ih[(i64)o * CV + k];
         whh[i] = a.w_hh[i];
     }
     for (int i = threadIdx.x; i < H * H; i += blockDim.x) h2h[i] = a.h2h_w[i];
-    for (int i = threadIdx.x; i < H; i += blockDim.x) dhn[i] = dcn[i] = 0.0f;
-    for (int i = threadIdx.x; i < T * H; i += blockDim.x) acc_bh[i] = acc_ph[i] = 0.0f;
+    for (int i = threadIdx.x; i < S * H; i += blockDim.x) dhn[i] = dcn[i] = 0.0f;
+    for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) acc_bh[i] = acc_ph[i] = 0.0f;
     __syncthreads();
-    const float *bh = a.bh + (i64)b * T * H;
     for (int st = a.steps - 1; st >= 0; --st) {
-        const i64 sb = (i64)st * a.B + b;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        // LSTM cell backward
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H, b = min(b0 + sl, a.B - 1);
+            const i64 sb = (i64)st * a.B + b;
             const float *g = a.gates + sb * G4;
-            const float ig = g[i], fg = g[H + i], cg = g[2 * H + i], og = g[3 * H + i];
-            const float tc = cr_tanhf(a.cs[sb * H + i]);
-            const float cp = st > 0 ? a.cs[(sb - a.B) * H + i] : 0.0f;
-            const float dh = fadd(a.d_out_hid[sb * H + i], dhn[i]);
+            const float ig = g[k], fg = g[H + k], cg = g[2 * H + k], og = g[3 * H + k];
+            const float tc = cr_tanhf(a.cs[sb * H + k]);
+            const float cp = st > 0 ? a.cs[(sb - a.B) * H + k] : 0.0f;
+            const float dh = fadd(a.d_out_hid[sb * H + k], dhn[i]);
             const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
-            dg[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
-            dg[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
-            dg[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
-            dg[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            float *d = dg + sl * G4;
+            d[k] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            d[H + k] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            d[2 * H + k] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            d[3 * H + k] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
             dcn[i] = dc;
         }
         __syncthreads();
-        for (int o = threadIdx.x; o < G4; o += blockDim.x) a.dgates[sb * G4 + o] = dg[o];
-        for (int k = threadIdx.x; k < H; k += blockDim.x) {
-            double s1 = 0.0, s2 = 0.0;
-            for (int o = 0; o < G4; ++o) {
-                const double dv = (double)dg[o];
-                s1 = fma(dv, (double)wc[o * H + k], s1);
-                s2 = fma(dv, (double)whh[o * H + k], s2);
+        for (int i = threadIdx.x; i < S * G4; i += blockDim.x) {
+            const int sl = i / G4, o = i - sl * G4, b = b0 + sl;
+            if (b < a.B) a.dgates[((i64)st * a.B + b) * G4 + o] = dg[i];
+        }
+        // d ctx = w_ih[:, :H]^T dg, d h_prev (direct) = w_hh^T dg
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H;
+            const float *d = dg + sl * G4;
+            double s1a = 0.0, s1b = 0.0, s2a = 0.0, s2b = 0.0;
+            for (int o = 0; o < G4; o += 2) {
+                const double d0 = (double)d[o], d1 = (double)d[o + 1];
+                s1a = fma(d0, (double)wc[o * H + k], s1a);
+                s1b = fma(d1, (double)wc[(o + 1) * H + k], s1b);
+                s2a = fma(d0, (double)whh[o * H + k], s2a);
+                s2b = fma(d1, (double)whh[(o + 1) * H + k], s2b);
             }
-            dctx[k] = (float)s1;
-            dhp[k] = (float)s2;
+            dctx[i] = (float)(s1a + s1b);
+            dhp[i] = (float)(s2a + s2b);
         }
         __syncthreads();
-        const float *al = a.alpha + sb * T;
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            double s = 0.0;
-            for (int k = 0; k < H; ++k) s = fma((double)dctx[k], (double)bh[t * H + k], s);
-            da[t] = (float)s;
-            const float at = al[t];
-            for (int k = 0; k < H; ++k) acc_bh[t * H + k] = fadd(acc_bh[t * H + k], fmul(at, dctx[k]));
+        // d alpha = d ctx . bh[t], one warp per (sample, t); acc_bh += alpha * d ctx
+        for (int p = warp; p < S * T; p += nwarps) {
+            const int sl = p / T, t = p - sl * T, b = min(b0 + sl, a.B - 1);
+            double acc = 0.0;
+            for (int k = lane; k < H; k += 32)
+                acc = fma((double)dctx[sl * H + k], (double)a.bh[((i64)b * T + t) * H + k], acc);
+            acc = warp_sum_d(acc);
+            if (lane == 0) da[p] = (float)acc;
+        }
+        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+            const int sl = i / (T * H), r = i - sl * T * H, t = r / H, k = r - t * H;
+            const int b = min(b0 + sl, a.B - 1);
+            const float at = a.alpha[((i64)st * a.B + b) * T + t];
+            acc_bh[i] = fadd(acc_bh[i], fmul(at, dctx[sl * H + k]));
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            double s = 0.0;
-            for (int t = 0; t < T; ++t) s = fma((double)al[t], (double)da[t], s);
-            *dot = (float)s;
+        // softmax backward, one warp per sample: de = alpha (d alpha - alpha . d alpha)
+        for (int sl = warp; sl < S; sl += nwarps) {
+            const int b = min(b0 + sl, a.B - 1);
+            const float *al = a.alpha + ((i64)st * a.B + b) * T;
+            double acc = 0.0;
+            for (int t = lane; t < T; t += 32) acc = fma((double)al[t], (double)da[sl * T + t], acc);
+            const float dt = (float)warp_sum_d(acc);
+            for (int t = lane; t < T; t += 32) {
+                const float v = fmul(al[t], fsub(da[sl * T + t], dt));
+                de[sl * T + t] = v;
+                if (b0 + sl < a.B) a.de[((i64)st * a.B + b) * T + t] = v;
+            }
         }
         __syncthreads();
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            const float v = fmul(al[t], fsub(da[t], *dot));
-            de[t] = v;
-            a.de[sb * T + t] = v;
+        // through tanh: acc_ph += de * score_w * (1 - tn^2); d proj_hh = sum over t
+        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+            const int sl = i / (T * H), r = i - sl * T * H, t = r / H, k = r - t * H;
+            const float d = de[sl * T + t];
+            if (d == 0.0f) continue;
+            const int b = min(b0 + sl, a.B - 1);
+            const float v = a.tanh_tr[(((i64)st * a.B + b) * T) * H + r];
+            acc_ph[i] = fadd(acc_ph[i], fmul(fmul(d, a.score_w[k]), fsub(1.0f, fmul(v, v))));
         }
-        __syncthreads();
-        const float *tn = a.tanh_tr + sb * T * H;
-        for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
-            const int t = i / H, k = i - t * H;
-            if (de[t] == 0.0f) continue;
-            acc_ph[i] = fadd(acc_ph[i], fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(tn[i], tn[i]))));
-        }
-        for (int k = threadIdx.x; k < H; k += blockDim.x) {
-            double s = 0.0;
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, k = i - sl * H, b = min(b0 + sl, a.B - 1);
+            const float *tn = a.tanh_tr + (((i64)st * a.B + b) * T) * H;
+            double sum = 0.0;
             for (int t = 0; t < T; ++t) {
                 const float v = tn[t * H + k];
-                s += (double)fmul(fmul(de[t], a.score_w[k]), fsub(1.0f, fmul(v, v)));
+                sum += (double)fmul(fmul(de[sl * T + t], a.score_w[k]), fsub(1.0f, fmul(v, v)));
             }
-            dphh[k] = (float)s;
-            a.dprojhh[sb * H + k] = s;
+            dphh[i] = (float)sum;
+            if (b0 + sl < a.B) a.dprojhh[((i64)st * a.B + b) * H + k] = (float)sum;
         }
         __syncthreads();
-        for (int j = threadIdx.x; j < H; j += blockDim.x) {
-            double s = 0.0;
-            for (int k = 0; k < H; ++k) s = fma((double)dphh[k], (double)h2h[k * H + j], s);
-            dhn[j] = fadd(dhp[j], (float)s);
+        // d h_prev += h2h^T d proj_hh
+        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+            const int sl = i / H, j = i - sl * H;
+            dhn[i] = fadd(dhp[i], (float)dot2_d(dphh + sl * H, h2h + j, H, H));
         }
         __syncthreads();
     }
-    for (int i = threadIdx.x; i < T * H; i += blockDim.x) {
-        a.d_proj_h[(i64)b * T * H + i] = acc_ph[i];
-        a.d_bh[(i64)b * T * H + i] = acc_bh[i];
+    for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+        const int sl = i / (T * H), r = i - sl * T * H, b = b0 + sl;
+        if (b >= a.B) continue;
+        a.d_proj_h[(i64)b * T * H + r] = acc_ph[i];
+        a.d_bh[(i64)b * T * H + r] = acc_bh[i];
     }
 }
 
@@ -562,34 +657,35 @@ static void set_smem(const void *fn, size_t bytes) {
 
 void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H, int rev,
               float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st) {
-    const size_t smem = sizeof(float) * ((size_t)4 * H * H + BG * H * 2 + BG * 4 * H);
+    const size_t smem = sizeof(float) * ((size_t)4 * H * H + 2 * H + 4 * H);
     set_smem((const void *)lstm_fwd_kernel, smem);
-    lstm_fwd_kernel<<<(B + BG - 1) / BG, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev, cat,
-                                                          dir);
+    lstm_fwd_kernel<<<B, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev, cat, dir);
     TRBA_LAUNCH_CHECK();
 }
 
 void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H, int rev,
               int dir, float *dgates, cudaStream_t st) {
-    const size_t smem = sizeof(float) * ((size_t)4 * H * H + BG * H * 2 + BG * 4 * H);
+    TRBA_REQUIRE(H % 8 == 0, "lstm_bwd: hidden size must be a multiple of 8 (4*hidden fills whole warps)");
+    const size_t smem = sizeof(float) * ((size_t)4 * H * H + 2 * H + 4 * H);
     set_smem((const void *)lstm_bwd_kernel, smem);
-    lstm_bwd_kernel<<<(B + BG - 1) / BG, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
+    lstm_bwd_kernel<<<B, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
     TRBA_LAUNCH_CHECK();
 }
 
 void attn_fwd(const AttnFwd &a, cudaStream_t st) {
-    const int H = a.H, T = a.T;
-    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + 4 * H + 4 * H + T * H + 2 * T);
+    const int H = a.H, T = a.T, S = kAttnS;
+    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S);
     set_smem((const void *)attn_fwd_kernel, smem);
-    attn_fwd_kernel<<<a.B, 256, smem, st>>>(a);
+    attn_fwd_kernel<<<(a.B + S - 1) / S, 256, smem, st>>>(a);
     TRBA_LAUNCH_CHECK();
 }
 
 void attn_bwd(const AttnBwd &a, cudaStream_t st) {
-    const int H = a.H, T = a.T;
-    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + 5 * H + 4 * H + 2 * T + 1 + 2 * T * H);
+    const int H = a.H, T = a.T, S = kAttnS;
+    const size_t smem =
+        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (5 * H + 4 * H + 2 * T + 1 + 2 * T * H));
     set_smem((const void *)attn_bwd_kernel, smem);
-    attn_bwd_kernel<<<a.B, 256, smem, st>>>(a);
+    attn_bwd_kernel<<<(a.B + S - 1) / S, 256, smem, st>>>(a);
     TRBA_LAUNCH_CHECK();
 }
 
