@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm-sweep", action="store_true")
+    ap.add_argument("--gemm-shape", default=None,
+                    help="M,N,K: time only the int8 GEMM (s32 and fused int8 epilogue) at this shape")
     return ap.parse_args()
 
 
@@ -182,6 +185,69 @@ def int8_gemm_peak(dev) -> float:
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
+GEMM_SWEEP = [(m, n, k) for m in (6144, 24576, 98304) for n in (64, 128, 256, 512) for k in (64, 576, 1152, 2304)]
+
+
+def gemm_sweep(L, dev, int8_peak: float, hbm_gbs: float | None, reps: int = 5) -> dict:
+    """The standalone int8 GEMM sweep (48 im2col / gate GEMM shapes): every
+    shape through launch_gemm_int8 (s32 out) and trba_gemm_int8_requant
+    (fused int8 out), each launch timed alone with CUDA events after an L2
+    flush (a 256 MB memset), best of `reps`.  Reported per shape: TOP/s,
+    fraction of the cuBLAS int8 peak and of max(ops/peak, bytes/HBM) — the
+    roofline time of that shape's algorithmic bytes."""
+    import torch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g = torch.Generator(device=dev).manual_seed(3)
+    rows = []
+    mmax, nmax, kmax = 98304, 512, 2304
+    A = torch.randint(-127, 128, (mmax, kmax), dtype=torch.int8, device=dev, generator=g)
+    B = torch.randint(-127, 128, (nmax, kmax), dtype=torch.int8, device=dev, generator=g)
+    C32 = torch.empty(mmax * nmax, dtype=torch.int32, device=dev)
+    C8 = torch.empty(mmax * nmax, dtype=torch.int8, device=dev)
+    bias = torch.zeros(nmax, dtype=torch.float32, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    for (m, n, k) in GEMM_SWEEP:
+        a = A[:m, :k].contiguous()
+        b = B[:n, :k].contiguous()
+        res = {}
+        for name in ("s32", "requant_i8"):
+            best = float("inf")
+            for _ in range(reps + 1):
+                flush.zero_()
+                e0.record()
+                if name == "s32":
+                    L.launch_gemm_int8(p(a), p(b), p(C32), m, n, k, None)
+                else:
+                    L.trba_gemm_int8_requant(p(a), p(b), p(bias), p(C8), m, n, k, 127.0 * 64.0, 50.0, None)
+                e1.record()
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            ops = 2.0 * m * n * k
+            nbytes = m * k + n * k + (4 if name == "s32" else 1) * m * n
+            t_roof = max(ops / (int8_peak * 1e12), nbytes / (hbm_gbs * 1e9)) if hbm_gbs else ops / (int8_peak * 1e12)
+            res[name] = {"us": best * 1e3, "tops": ops / (best * 1e-3) / 1e12,
+                         "frac_peak": ops / (best * 1e-3) / 1e12 / int8_peak,
+                         "frac_roofline": t_roof / (best * 1e-3),
+                         "compute_bound": ops / (int8_peak * 1e12) >= (nbytes / (hbm_gbs * 1e9) if hbm_gbs else 0)}
+        rows.append({"m": m, "n": n, "k": k, **res})
+    del A, B, C32, C8, flush
+    torch.cuda.empty_cache()
+    if L.trba_tc_error_poll(1) != 0:
+        raise RuntimeError("tensor-core GEMM reported a timed-out wait during the sweep")
+    cb = [r for r in rows if r["requant_i8"]["compute_bound"]]
+    return {
+        "shapes": len(rows), "peak_tops": int8_peak, "unit": "TOP/s",
+        "best_tops_s32": max(r["s32"]["tops"] for r in rows),
+        "best_tops_requant_i8": max(r["requant_i8"]["tops"] for r in rows),
+        "compute_bound_requant_i8": [{"shape": [r["m"], r["n"], r["k"]], "tops": r["requant_i8"]["tops"],
+                                      "frac_peak": r["requant_i8"]["frac_peak"]} for r in cb],
+        "median_frac_roofline_s32": statistics.median(r["s32"]["frac_roofline"] for r in rows),
+        "median_frac_roofline_requant_i8": statistics.median(r["requant_i8"]["frac_roofline"] for r in rows),
+        "per_shape": rows,
+    }
+
+
 def profiled_traffic(kernel: str, batch: int):
     """DRAM bytes per launch of `kernel` at this batch, from the committed ncu
     summary profiles/<kernel>_traffic.txt (line 'bytes_per_launch_per_line:
@@ -286,6 +352,10 @@ def our_arm(args):
                       "tops": g_ops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None}
     barrier()
 
+    sweep = None
+    if rank == 0 and world == 1 and not args.no_gemm_sweep and int8_peak:
+        sweep = gemm_sweep(L, dev, int8_peak, measured_peaks().get("hbm_gbs"))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, kind, lib = cpu_step_sample(32, 2, 1, args.img_w, args.max_len, args.seed)
@@ -337,6 +407,7 @@ def our_arm(args):
             "cpu_baseline": cpu,
             "roofline": roofline,
             "roofline_int8_gemm": gemm_line,
+            "int8_gemm_sweep": sweep,
         }
         print(json.dumps(out), flush=True)
     m.close()
@@ -344,8 +415,45 @@ def our_arm(args):
         torch.distributed.destroy_process_group()
 
 
+def gemm_only(args):
+    """One GEMM shape, s32 and fused-int8 outputs (for profiling one launch)."""
+    import torch
+    m, n, k = (int(x) for x in args.gemm_shape.split(","))
+    pkg = load_package()
+    L = pkg.lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    kp = (k + 15) & ~15
+    a = torch.randint(-127, 128, (m, kp), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (n, kp), dtype=torch.int8, device=dev, generator=g)
+    c32 = torch.empty((m, n), dtype=torch.int32, device=dev)
+    c8 = torch.empty((m, n), dtype=torch.int8, device=dev)
+    bias = torch.zeros(n, dtype=torch.float32, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    out = {"gemm": [m, n, k]}
+    for name in ("s32", "requant_i8"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = float("inf")
+        for _ in range(max(3, args.steps)):
+            e0.record()
+            if name == "s32":
+                L.launch_gemm_int8(p(a), p(b), p(c32), m, n, k, None)
+            else:
+                L.trba_gemm_int8_requant(p(a), p(b), p(bias), p(c8), m, n, k, 127.0 * 64.0, 50.0, None)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        out[name] = {"us": best * 1e3, "tops": 2.0 * m * n * k / (best * 1e-3) / 1e12}
+    if L.trba_tc_error_poll(1) != 0:
+        raise RuntimeError("tensor-core GEMM reported a timed-out wait")
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
+    if args.gemm_shape:
+        gemm_only(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
     else:

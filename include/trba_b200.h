@@ -42,6 +42,18 @@ int trba_sgemm_exact_noalloc(const float *a, const float *b, float *c, int m, in
  * chains on every SM, timed with CUDA events; *tflops counts the multiply
  * and the add as one flop each.  Synchronises the stream. */
 int trba_measure_f32_muladd_peak(double *tflops, void *stream);
+/* GEMM with the conv inference epilogue fused (no counterpart in the
+ * reference; equal to launch_gemm_int8 followed by launch_conv_epilogue(acc,
+ * bias, out, n, acc_div, out_mul, m, n, 1, 1)): out int8 [m, n] =
+ * rint(clamp(max(acc/acc_div + bias[n], 0) * out_mul, +-127)).  Operands as
+ * launch_gemm_int8. */
+void trba_gemm_int8_requant(const int8_t *a, const int8_t *b, const float *bias, int8_t *out, int m, int n, int k,
+                            float acc_div, float out_mul, void *stream);
+/* GEMM with per-output-channel dequantisation fused (no counterpart in the
+ * reference): out f32 [m, n] = act((float)acc * (a_scale * w_scale[n])
+ * [+ bias[n]]), act = ReLU when relu != 0.  bias may be NULL. */
+void trba_gemm_int8_dequant_f32(const int8_t *a, const int8_t *b, const float *w_scale, float a_scale,
+                                const float *bias, int relu, float *out, int m, int n, int k, void *stream);
 long long trba_launch_count(void);
 
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier

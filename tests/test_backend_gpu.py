@@ -104,3 +104,65 @@ def test_gemm_unaligned_operand_takes_the_fallback(lib, cuda):
     want = (a.to(torch.float64) @ b.to(torch.float64).t()).to(torch.int32)
     torch.cuda.synchronize()
     assert torch.equal(c, want)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (17, 5, 3), (129, 33, 129), (1000, 260, 300), (6144, 512, 2304),
+                                   (3840, 128, 1152), (200, 48, 64)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_fused_requant_epilogue_equals_gemm_then_conv_epilogue(shape, lib, cuda, oracle):
+    """trba_gemm_int8_requant = launch_gemm_int8 + launch_conv_epilogue
+    (cuda/kernels.cu:434-466) fused: int8 outputs bit-identical to the
+    two-launch composition here and to the oracle's composition."""
+    import torch
+    m, n, k = shape
+    a, b = _gemm_inputs(torch, m, n, k, seed=5 + m + n + k)
+    g = torch.Generator(device="cpu").manual_seed(m + n)
+    bias = (torch.rand(n, generator=g) * 2 - 1).float().cuda()
+    div, mul = 127.0 * 64.0, 50.0
+    fused = torch.full((m, n), 99, dtype=torch.int8, device="cuda")
+    lib.trba_gemm_int8_requant(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(bias.data_ptr()),
+                               C.c_void_p(fused.data_ptr()), m, n, k, div, mul, None)
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    lib.launch_gemm_int8(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(acc.data_ptr()), m, n, k,
+                         None)
+    two = torch.full((m, n), 99, dtype=torch.int8, device="cuda")
+    lib.launch_conv_epilogue(C.c_void_p(acc.data_ptr()), C.c_void_p(bias.data_ptr()), C.c_void_p(two.data_ptr()), n,
+                             div, mul, m, n, 1, 1, None)
+    torch.cuda.synchronize()
+    assert lib.trba_tc_error_poll(1) == 0
+    assert torch.equal(fused, two)
+    acc_h, bias_h = acc.cpu().numpy(), bias.cpu().numpy()
+    want = np.zeros((m, n), np.int8)
+    oracle.launch_conv_epilogue(C.c_void_p(acc_h.ctypes.data), C.c_void_p(bias_h.ctypes.data),
+                                C.c_void_p(want.ctypes.data), n, div, mul, m, n, 1, 1, None)
+    assert np.array_equal(fused.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (129, 33, 129), (1000, 260, 300), (6144, 512, 2304)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("bias,relu", [(False, 0), (True, 1)], ids=["plain", "bias_relu"])
+def test_fused_dequant_epilogue(shape, bias, relu, lib, cuda):
+    """out = act((float)acc * (a_scale * w_scale[n]) + bias[n]), every
+    operation an IEEE f32 multiply / add: bit-identical to numpy float32."""
+    import torch
+    m, n, k = shape
+    a, b = _gemm_inputs(torch, m, n, k, seed=9 + m + n + k)
+    g = np.random.default_rng(m * 3 + n)
+    w_scale = np.exp(g.uniform(np.log(1e-4), np.log(1e-1), n)).astype(np.float32)
+    bvec = g.uniform(-1, 1, n).astype(np.float32)
+    a_scale = np.float32(1.0 / 127.0)
+    ws_d = torch.from_numpy(w_scale).cuda()
+    b_d = torch.from_numpy(bvec).cuda()
+    out = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    lib.trba_gemm_int8_dequant_f32(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(ws_d.data_ptr()),
+                                   float(a_scale), C.c_void_p(b_d.data_ptr()) if bias else None, relu,
+                                   C.c_void_p(out.data_ptr()), m, n, k, None)
+    acc = (a[:, :k].to(torch.float64) @ b[:, :k].to(torch.float64).t()).to(torch.int32).cpu().numpy()
+    torch.cuda.synchronize()
+    assert lib.trba_tc_error_poll(1) == 0
+    want = acc.astype(np.float32) * (a_scale * w_scale)[None, :]
+    if bias:
+        want = (want + bvec[None, :]).astype(np.float32)
+    if relu:
+        want = np.maximum(want, np.float32(0))
+    assert np.array_equal(out.cpu().numpy(), want.astype(np.float32))

@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "gemm_i8.cuh"
+#include "trba_backend.h"
 #include "tc_primitives.cuh"
 
 using namespace trba;
@@ -158,6 +159,79 @@ struct EpiConvF32 {
             if (sm[kMaxN + i] != 0.0) atomicAdd(bn_acc + N + i, sm[kMaxN + i]);
         }
     }
+};
+
+// Fused inference epilogue of the conv path (cuda/kernels.cu:434-466,
+// launch_conv_epilogue): out[r, n] = rint(clamp(max(acc/div + bias[n], 0) *
+// mul, +-127)) as int8, row-major [M, ldo].
+struct EpiRequantI8 {
+    int8_t *out;
+    int ldo;
+    const float *bias;
+    float div, mul;
+    bool vec;  // out rows 16-byte aligned and N % 16 == 0
+    __device__ void init(double *) {}
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
+        if (row >= M) return;
+        int8_t *orow = out + (i64)row * ldo;
+        uint32_t packed[8];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = col + j < N ? col + j : N - 1;
+            float t = fadd(fdiv((float)(int32_t)v[j], div), bias[n]);
+            t = fmul(fmaxf(t, 0.0f), mul);
+            t = fminf(fmaxf(t, -127.0f), 127.0f);
+            const uint32_t q = (uint32_t)(uint8_t)(int8_t)rint_even(t);
+            if ((j & 3) == 0) packed[j >> 2] = 0u;
+            packed[j >> 2] |= q << (8 * (j & 3));
+        }
+        if (vec && col + 32 <= N) {
+            uint4 *dst = reinterpret_cast<uint4 *>(orow + col);
+            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col + j < N) orow[col + j] = (int8_t)((packed[j >> 2] >> (8 * (j & 3))) & 0xffu);
+        }
+    }
+    __device__ void finish(double *, int) {}
+};
+
+// Dequantising epilogue with per-output-channel weight scales:
+// out[r, n] = act((float)acc * (a_scale * w_scale[n]) [+ bias[n]]), f32
+// row-major [M, ldo]; act = ReLU when relu, identity otherwise.
+struct EpiDequantF32 {
+    float *out;
+    int ldo;
+    const float *w_scale;
+    const float *bias;  // may be null
+    float a_scale;
+    int relu;
+    bool vec;  // out rows 16-byte aligned and N % 4 == 0
+    __device__ void init(double *) {}
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
+        if (row >= M) return;
+        float *orow = out + (i64)row * ldo;
+        float r[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = col + j < N ? col + j : N - 1;
+            float t = fmul((float)(int32_t)v[j], fmul(a_scale, w_scale[n]));
+            if (bias) t = fadd(t, bias[n]);
+            r[j] = relu ? fmaxf(t, 0.0f) : t;
+        }
+        if (vec && col + 32 <= N) {
+            float4 *dst = reinterpret_cast<float4 *>(orow + col);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col + j < N) orow[col + j] = r[j];
+        }
+    }
+    __device__ void finish(double *, int) {}
 };
 
 struct Shape {
@@ -450,6 +524,19 @@ bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M,
     return run_tc(A, lda, B, ldb, make_shape(M, N, K, 1), EpiConvF32{x, s_in, w_s, bn_acc, HW}, st);
 }
 
+bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float *bias, int M, int N, int K, int ld,
+                     float div, float mul, cudaStream_t st) {
+    EpiRequantI8 e{out, N, bias, div, mul, ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (N & 15) == 0};
+    return run_tc(A, ld, B, ld, make_shape(M, N, K, 1), e, st);
+}
+
+bool gemm_i8_dequant(const int8_t *A, const int8_t *B, float *out, const float *w_scale, float a_scale,
+                     const float *bias, int relu, int M, int N, int K, int ld, cudaStream_t st) {
+    EpiDequantF32 e{out, N, w_scale, bias, a_scale, relu,
+                    ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (N & 3) == 0};
+    return run_tc(A, ld, B, ld, make_shape(M, N, K, 1), e, st);
+}
+
 int splitk_for(int M, int N, int K) {
     // Enough (m, n, split) tiles for two waves of SMs, at least 2 K blocks each.
     const int tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
@@ -490,6 +577,33 @@ void trba_gemm_int8_splitk(const int8_t *a, const int8_t *b, int32_t *c, int m, 
     if (splits <= 0) splits = splitk_for(m, n, k);
     if (!gemm_i8_splitk_atomic(a, ld, b, ld, c, m, n, k, splits, as_stream(stream)))
         report_error(__FILE__, __LINE__, "trba_gemm_int8_splitk: operands not 16-byte aligned", -1);
+}
+
+// GEMM + the conv inference epilogue in one kernel: out int8 [m, n] =
+// launch_gemm_int8 followed by launch_conv_epilogue(acc, bias, out, n, div,
+// mul, m, n, 1, 1).  Operands as launch_gemm_int8 (padded, 16-byte aligned).
+void trba_gemm_int8_requant(const int8_t *a, const int8_t *b, const float *bias, int8_t *out, int m, int n, int k,
+                            float acc_div, float out_mul, void *stream) {
+    if (m <= 0 || n <= 0 || k <= 0) return;
+    const int ld = (k + 15) & ~15;
+    if (gemm_i8_requant(a, b, out, bias, m, n, k, ld, acc_div, out_mul, as_stream(stream))) return;
+    int32_t *acc = nullptr;
+    TRBA_CHECK(cudaMallocAsync((void **)&acc, (size_t)m * n * sizeof(int32_t), as_stream(stream)));
+    if (!acc) return;
+    gemm_i8_simt(a, b, acc, m, n, k, ld, as_stream(stream));
+    launch_conv_epilogue(acc, bias, out, n, acc_div, out_mul, m, n, 1, 1, stream);
+    TRBA_CHECK(cudaFreeAsync(acc, as_stream(stream)));
+}
+
+// GEMM + per-channel dequantisation (+ bias, + ReLU) in one kernel:
+// out f32 [m, n] = act((float)acc * (a_scale * w_scale[n]) [+ bias[n]]).
+void trba_gemm_int8_dequant_f32(const int8_t *a, const int8_t *b, const float *w_scale, float a_scale,
+                                const float *bias, int relu, float *out, int m, int n, int k, void *stream) {
+    if (m <= 0 || n <= 0 || k <= 0) return;
+    TRBA_REQUIRE(w_scale != nullptr, "trba_gemm_int8_dequant_f32: w_scale is required");
+    const int ld = (k + 15) & ~15;
+    if (gemm_i8_dequant(a, b, out, w_scale, a_scale, bias, relu, m, n, k, ld, as_stream(stream))) return;
+    report_error(__FILE__, __LINE__, "trba_gemm_int8_dequant_f32: operands not 16-byte aligned", -1);
 }
 
 // Device-side error word of the tensor-core kernels (1 = a bounded wait

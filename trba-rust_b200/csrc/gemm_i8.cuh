@@ -20,6 +20,12 @@ bool gemm_i8_splitk_atomic(const int8_t *A, int lda, const int8_t *B, int ldb, i
 // bn_acc[n] += sum x, bn_acc[N + n] += sum x^2 (f64).  N <= 512.
 bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, float *x,
                       const float *s_in, const float *w_s, double *bn_acc, int HW, cudaStream_t st);
+// Fused epilogues on row-major outputs [M, N]: the conv inference requant
+// (int8) and per-channel dequantisation (f32, optional bias and ReLU).
+bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float *bias, int M, int N, int K, int ld,
+                     float div, float mul, cudaStream_t st);
+bool gemm_i8_dequant(const int8_t *A, const int8_t *B, float *out, const float *w_scale, float a_scale,
+                     const float *bias, int relu, int M, int N, int K, int ld, cudaStream_t st);
 int splitk_for(int M, int N, int K);
 void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st);
 
