@@ -45,7 +45,8 @@ namespace {
 constexpr int BM = 128;   // UMMA M (cta_group::1)
 constexpr int BK = 128;   // bytes of K per stage = one 128B swizzle row
 constexpr int UK = 32;    // K of one kind::i8 MMA
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, splitting the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxN = 512;  // widest N an epilogue with per-column state supports
 
 template <int BN>
@@ -131,7 +132,7 @@ struct EpiConvF32 {
     double *bn_acc;      // [2*N]: per-channel sum, then sum of squares (f64)
     int HW;
     __device__ void init(double *sm) {
-        for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += 128) sm[i] = 0.0;
+        for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += kThreads - 64) sm[i] = 0.0;
     }
     __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
         const float scale = fmul(*s_in, *w_s);
@@ -154,7 +155,7 @@ struct EpiConvF32 {
         }
     }
     __device__ void finish(double *sm, int N) {
-        for (int i = threadIdx.x - 64; i < N; i += 128) {
+        for (int i = threadIdx.x - 64; i < N; i += kThreads - 64) {
             if (sm[i] != 0.0) atomicAdd(bn_acc + i, sm[i]);
             if (sm[kMaxN + i] != 0.0) atomicAdd(bn_acc + N + i, sm[kMaxN + i]);
         }
@@ -264,7 +265,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&ctl->tfull[a], 1);
-            mbar_init(&ctl->tempty[a], 4 * 32);
+            mbar_init(&ctl->tempty[a], kEpiWarps * 32);
         }
         mbar_init(&ctl->drained, 1);
         ctl->abort = 0;
@@ -352,8 +353,9 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             mbar_wait(&ctl->drained, 0, &never, 200000000ull);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        // ---------------- epilogue (warps 2..9) ----------------
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;       // which 32-column blocks of the tile it takes
         uint32_t acc = 0, acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int m0, n0, kb0, kb1;
@@ -365,7 +367,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const int row = m0 + q * 32 + lane;
             const bool empty_split = kb0 >= kb1;  // nothing accumulated: skip
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN && n0 + c0 < N && !empty_split; c0 += 32) {
+            for (int c0 = 32 * half; c0 < BN && n0 + c0 < N && !empty_split; c0 += 64) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
                 tmem_ld_wait();
