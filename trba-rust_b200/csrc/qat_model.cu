@@ -201,6 +201,11 @@ struct trba_model {
     ncclComm_t comm = nullptr;
     int world = 1;
     cudaEvent_t ev = nullptr;
+    // Side stream of the conv backward: the input-gradient gather (which reads
+    // only dy) runs there while the BN backward chain and the weight-gradient
+    // GEMM of the same conv run on the step's stream.
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     Probe probe;
 };
 
@@ -769,6 +774,23 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
     const int B = c.B, HW = L.Ho * L.Wo;
     const i64 rows = L.rows(B), rp = a16l(rows);
     const bool compat = c.m->cfg.wgrad_mode == 0;
+    // The input gradient reads only dy (and the int8 weights, the ReLU mask
+    // and the residual gradient), so it runs on the side stream while the
+    // BN backward chain and the weight gradient run here; the caller sees gi
+    // after the join at the end.
+    if (gi) {
+        TRBA_CHECK(cudaEventRecord(c.m->fork_ev, c.st));
+        TRBA_CHECK(cudaStreamWaitEvent(c.m->side, c.m->fork_ev, 0));
+        // ops: one multiply and one add per (input element, valid tap, output channel)
+        const double in_n = (double)B * L.cin * L.H * L.W;
+        const double bytes = 4.0 * B * L.cout * HW + 4.0 * in_n + (mask_q ? in_n : 0.0) + (add ? 4.0 * in_n : 0.0) +
+                             (double)L.cout * L.K;
+        const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
+                             valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
+        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.m->side);
+        qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
+                   L.Ho, L.Wo, mask_q, add, gi, c.m->side);
+    }
     qat::bn_bwd_sums(dy, L.x.get(), L.mean.get(), L.var.get(), B, L.cout, HW, L.bwd_acc.get(), c.st);
     qat::bn_dx_max(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
                    c.G + L.gamma_off, c.G + L.beta_off, L.dxmax.get(), c.st);
@@ -787,15 +809,8 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
     }
     qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, c.st);
     if (gi) {
-        // ops: one multiply and one add per (input element, valid tap, output channel)
-        const double in_n = (double)B * L.cin * L.H * L.W;
-        const double bytes = 4.0 * B * L.cout * HW + 4.0 * in_n + (mask_q ? in_n : 0.0) + (add ? 4.0 * in_n : 0.0) +
-                             (double)L.cout * L.K;
-        const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
-                             valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
-        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.st);
-        qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
-                   L.Ho, L.Wo, mask_q, add, gi, c.st);
+        TRBA_CHECK(cudaEventRecord(c.m->join_ev, c.m->side));
+        TRBA_CHECK(cudaStreamWaitEvent(c.st, c.m->join_ev, 0));
     }
 }
 
@@ -1129,6 +1144,9 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
         fill_f32_kernel<<<grid_for(n1), 256>>>(m->ones.get(), n1, 1.0f);
     }
     TRBA_CHECK(cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming));
+    TRBA_CHECK(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking));
+    TRBA_CHECK(cudaEventCreateWithFlags(&m->fork_ev, cudaEventDisableTiming));
+    TRBA_CHECK(cudaEventCreateWithFlags(&m->join_ev, cudaEventDisableTiming));
     TRBA_CHECK(cudaDeviceSynchronize());
     return m;
 }
@@ -1143,6 +1161,9 @@ void trba_model_destroy(trba_model *m) {
     cudaFree(m->d_mat);
     cudaFree(m->d_conv);
     if (m->ev) cudaEventDestroy(m->ev);
+    if (m->fork_ev) cudaEventDestroy(m->fork_ev);
+    if (m->join_ev) cudaEventDestroy(m->join_ev);
+    if (m->side) cudaStreamDestroy(m->side);
     for (cudaEvent_t e : m->probe.ev) cudaEventDestroy(e);
     delete m;
 }
