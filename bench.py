@@ -342,7 +342,8 @@ def our_arm(args):
     # int8 tensor-core GEMMs of the step (forward conv + weight gradient),
     # probed over a few extra steps after the timed region
     gemm = {}
-    for name, kind in (("conv_fwd", m.PROBE_CONV_GEMM), ("conv_wgrad", m.PROBE_WGRAD_GEMM)):
+    for name, kind in (("conv_fwd", m.PROBE_CONV_GEMM), ("conv_wgrad", m.PROBE_WGRAD_GEMM),
+                       ("head_sgemm_f64acc", m.PROBE_SGEMM)):
         m.probe(kind)
         for _ in range(3):
             m.train_step(*devb, stream=sptr)
@@ -384,6 +385,7 @@ def our_arm(args):
             "share_of_step": dg_ms / args.steps / ms,
         }
     gemm_line = None
+    head = gemm.pop("head_sgemm_f64acc")
     if int8_peak:
         tot_ms = sum(g["ms_per_step"] for g in gemm.values())
         tot_tops = sum((g["tops"] or 0) * g["ms_per_step"] for g in gemm.values()) / tot_ms if tot_ms else None
@@ -408,6 +410,8 @@ def our_arm(args):
             "roofline": roofline,
             "roofline_int8_gemm": gemm_line,
             "int8_gemm_sweep": sweep,
+            "head_sgemm": {"launches_per_step": head["launches_per_step"], "ms_per_step": head["ms_per_step"],
+                           "tflops": head["tops"]},
         }
         print(json.dumps(out), flush=True)
     m.close()
