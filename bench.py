@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm-sweep", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch the step kernel by kernel (no CUDA graph)")
     ap.add_argument("--gemm-shape", default=None,
                     help="M,N,K: time only the int8 GEMM (s32 and fused int8 epilogue) at this shape")
     return ap.parse_args()
@@ -300,15 +301,24 @@ def our_arm(args):
         raise RuntimeError(L.trba_last_error_string().decode())
     int8_peak = int8_gemm_peak(dev) if rank == 0 else None
 
+    # The dominant kernel (the conv input-gradient gather) is timed on the
+    # stream it runs on.  Eager steps (--eager): CUDA events around every
+    # launch of the timed region.  Graph replays (default): the probe is
+    # recorded into the step graph (set before the warm-up, which records the
+    # graph); each launch is bracketed by device %globaltimer stamps (events
+    # recorded inside a graph cannot be timed), read for the last timed step.
+    graphs = not args.eager
+    m.use_graphs(graphs)
+    if graphs:
+        m.probe(m.PROBE_DGRAD)
     for _ in range(max(3, args.warmup)):
         m.train_step(*devb, stream=sptr)
     barrier()
     clocks = Clocks(local)
     clocks.start()
     l0 = L.trba_launch_count()
-    # the dominant kernel (the conv input-gradient gather) is bracketed by
-    # CUDA events on the step's stream throughout the timed region
-    m.probe(m.PROBE_DGRAD)
+    if not graphs:
+        m.probe(m.PROBE_DGRAD)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -317,8 +327,7 @@ def our_arm(args):
     barrier()
     ck = clocks.stop()
     launches = (L.trba_launch_count() - l0) / args.steps
-    dg_ms, dg_n, dg_ops, dg_bytes = m.probe_read()
-    m.probe(-1)
+    dg_ms, dg_n, dg_ops, dg_bytes, dg_steps = m.probe_read()
     ms = dp.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     loss = m.loss()
     value = args.batch * world / (ms / 1000.0)
@@ -339,15 +348,17 @@ def our_arm(args):
         e2e = {"value": args.batch * world / (ms2 / 1000.0), "unit": "lines/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12}
 
+    m.probe(-1)
     # int8 tensor-core GEMMs of the step (forward conv + weight gradient),
-    # probed over a few extra steps after the timed region
+    # probed over a few eager steps after the timed region
+    m.use_graphs(False)
     gemm = {}
     for name, kind in (("conv_fwd", m.PROBE_CONV_GEMM), ("conv_wgrad", m.PROBE_WGRAD_GEMM),
                        ("head_sgemm_f64acc", m.PROBE_SGEMM)):
         m.probe(kind)
         for _ in range(3):
             m.train_step(*devb, stream=sptr)
-        g_ms, g_n, g_ops, g_bytes = m.probe_read()
+        g_ms, g_n, g_ops, g_bytes, _ = m.probe_read()
         m.probe(-1)
         gemm[name] = {"launches_per_step": g_n // 3, "ms_per_step": g_ms / 3,
                       "tops": g_ops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None}
@@ -380,9 +391,11 @@ def our_arm(args):
             "algorithmic_bytes_per_launch": dg_bytes / dg_n,
             "hbm_gbs_at_algorithmic_bytes": dg_bytes / dg_n / per_launch_s / 1e9,
             "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
-            "launches_per_step": dg_n / args.steps,
-            "ms_per_step": dg_ms / args.steps,
-            "share_of_step": dg_ms / args.steps / ms,
+            "launches_per_step": dg_n / dg_steps,
+            "ms_per_step": dg_ms / dg_steps,
+            "share_of_step": dg_ms / dg_steps / ms,
+            "timed_launches": "CUDA events around every launch of the timed region" if not graphs
+            else "device globaltimer stamps around the launches of the last timed step (replayed CUDA graph)",
         }
     gemm_line = None
     head = gemm.pop("head_sgemm_f64acc")

@@ -110,7 +110,24 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
 #define TRBA_PROBE_DGRAD 2      /* conv input-gradient gather (fp32, reference summation order) */
 #define TRBA_PROBE_SGEMM 3      /* sequence-head fp32 GEMMs (f64 accumulation) */
 int trba_model_probe(trba_model *m, int kind);
-int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes);
+int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes,
+                          long long *steps);
+
+/* CUDA-graph execution of the step (no counterpart in the reference).  With
+ * enable != 0, trba_model_train_step records the whole step (forward,
+ * backward, gradient all-reduce, optimiser) into a CUDA graph the first time
+ * it sees a set of input pointers, batch and probe kind — recording runs
+ * nothing — and replays that graph on later calls with the same pointers:
+ * callers refresh the input buffers in place.  Every step-dependent scalar
+ * (the optimiser's step count, clip switch and bias corrections) lives on the
+ * device, so replays compute exactly what eager steps compute.
+ * trba_model_train_step_host stages into the model's own input buffers and so
+ * always replays one graph.  A probe selected before the recording is
+ * recorded with it: each probed launch is bracketed by two one-thread
+ * kernels that write the device's %globaltimer (an event recorded inside a
+ * graph cannot be timed), and trba_model_probe_read then reports the
+ * launches of the latest replay (steps = 1). */
+int trba_model_use_graphs(trba_model *m, int enable);
 
 /* ---- data parallel (one process per GPU, NCCL over NVLink) ---- */
 /* 128-byte NCCL unique id from rank 0, broadcast by the caller. */

@@ -141,3 +141,38 @@ def test_loss_curve_200_steps_matches_oracle(lib, cuda):
     rel = np.abs(lg - lo) / np.abs(lo)
     assert rel.max() < 0.01, f"max relative loss gap {rel.max():.3g} at step {int(rel.argmax())}"
     assert np.mean(lo[-20:]) < np.mean(lo[:20]), "the oracle's loss did not decrease"
+
+
+def test_graph_replay_equals_eager_steps(lib, cuda):
+    """trba_model_use_graphs: the step recorded once as a CUDA graph and
+    replayed (inputs refreshed in place) gives bit-identical losses and
+    parameters to eager steps, through both entry points."""
+    import torch
+    import trba_b200.model as tm
+    geom = dict(img_w=64, max_len=4)
+    ocfg, params, eager, man = _setup(geom, 8, seed=41)
+    _, _, graph, _ = _setup(geom, 8, seed=41)
+    graph.use_graphs(True)
+    bufs = None
+    for i in range(6):
+        img, ti, tg, ct = so.make_batch(ocfg, 8, seed=300 + i)
+        dev = _to_dev(img, ti, tg, ct, ocfg.steps)
+        eager.train_step(*dev)
+        if bufs is None:
+            bufs = [d.clone() for d in dev]
+        else:
+            for b, d in zip(bufs, dev):
+                b.copy_(d)
+        graph.train_step(*bufs)
+        assert np.array_equal(eager.loss(), graph.loss()), f"step {i}"
+    assert np.array_equal(eager.get_params(), graph.get_params())
+    assert lib.trba_model_step_count(graph.h) == 6
+    for i in range(3):  # host-buffer entry point: one graph over the model's staging buffers
+        img, ti, tg, ct = so.make_batch(ocfg, 8, seed=400 + i)
+        host = (np.ascontiguousarray(img), *tm.pack_labels(ti, tg, ct, ocfg.steps))
+        l1 = eager.train_step_host(*host)
+        l2 = graph.train_step_host(*host)
+        assert np.array_equal(l1, l2)
+    assert np.array_equal(eager.get_params(), graph.get_params())
+    torch.cuda.synchronize()
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()

@@ -41,6 +41,8 @@ inline int grid_for(i64 n, int threads = 256) {
 // counts it (trba_launch_count()).
 namespace trba {
 void count_launch();
+void count_launches(long long n);  // kernels replayed inside a CUDA graph
+long long launches_so_far();
 }
 #define TRBA_LAUNCH_CHECK()          \
     do {                             \

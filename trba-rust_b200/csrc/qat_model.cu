@@ -142,6 +142,14 @@ struct RnnL {
 // Kernel probe: CUDA events around every launch of one kernel family, on
 // the stream the step runs on, so that a timed loop can report that family's
 // device time per launch live (trba_model_probe / trba_model_probe_read).
+constexpr size_t kProbeStamps = 256;
+
+__global__ void stamp_kernel(unsigned long long *dst) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    *dst = t;
+}
+
 struct Probe {
     int kind = -1;
     std::vector<cudaEvent_t> ev;  // start/stop pairs
@@ -149,6 +157,13 @@ struct Probe {
     double ops = 0.0;    // algorithmic arithmetic operations of the timed launches
     double bytes = 0.0;  // algorithmic bytes (one read of every input, one write of every output)
     long long launches = 0;
+    long long steps = 0;  // steps recorded while probing (a step graph records one)
+    // Inside a step graph the launches are bracketed by device timestamps
+    // (%globaltimer, written by a one-thread kernel on the same stream)
+    // instead of events: a graph-recorded event cannot be timed.
+    unsigned long long *stamps = nullptr;  // [2 * kProbeStamps] device
+    size_t nstamp = 0;
+    bool stamped = false;
 };
 
 }  // namespace
@@ -182,6 +197,7 @@ struct trba_model {
     Ref<double> gsq_total;
     Ref<double> conv_gsq;  // per conv
     Ref<float> clip_f, mat_step, conv_step;
+    Ref<double> step_state;  // [t, clip active, bc1, bc2]: advanced on the device every step
     // inputs staged for the host-buffer entry point
     Ref<int8_t> in_img;
     Ref<int32_t> in_text, in_target, in_ctc, in_ctc_len;
@@ -206,6 +222,15 @@ struct trba_model {
     // GEMM of the same conv run on the step's stream.
     cudaStream_t side = nullptr;
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+    // CUDA-graph execution of the whole step (trba_model_use_graphs): the
+    // graph is recorded on gstream for one set of input pointers and batch.
+    bool use_graphs = false;
+    cudaStream_t gstream = nullptr;
+    cudaEvent_t gfork = nullptr, gjoin = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    const void *gkey[5] = {};
+    int gkey_batch = 0, gkey_probe = -1;
+    long long graph_kernels = 0;  // kernel launches recorded in the step graph
     Probe probe;
 };
 
@@ -238,10 +263,35 @@ __global__ void sumsq_kernel(const float *g, i64 n, double *out) {
 }
 
 // src/main.rs:2382-2390: f = 5 / (norm + 1e-6) when norm > 5, else 1.
-__global__ void clip_factor_kernel(const double *gsq, int active, float *f) {
+// Rust f32::powi (LLVM __powisf2): square-and-multiply in f32.
+__device__ float powi_dev(float a, long long n) {
+    float r = 1.0f;
+    while (true) {
+        if (n & 1) r = fmul(r, a);
+        n >>= 1;
+        if (n == 0) return r;
+        a = fmul(a, a);
+    }
+}
+
+// Advances the optimiser's step state on the device: clip is active while the
+// step count before this step is below clip_warmup; the Adam bias corrections
+// (src/opt.rs) use the count after it.  st = [t, clip active, bc1, bc2].
+__global__ void step_state_kernel(double *st, int clip_warmup) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const long long t0 = (long long)st[0];
+        st[1] = t0 < clip_warmup ? 1.0 : 0.0;
+        const long long t = t0 + 1;
+        st[0] = (double)t;
+        st[2] = 1.0 - (double)powi_dev(0.9f, t);
+        st[3] = 1.0 - (double)powi_dev(0.999f, t);
+    }
+}
+
+__global__ void clip_factor_kernel(const double *gsq, const double *st, float *f) {
     if (threadIdx.x == 0) {
         float v = 1.0f;
-        if (active) {
+        if (st[1] != 0.0) {
             const double norm = sqrt(*gsq);
             if (norm > 5.0) v = (float)(5.0 / (norm + 1e-6));
         }
@@ -252,9 +302,10 @@ __global__ void clip_factor_kernel(const double *gsq, int active, float *f) {
 // Adam on vector parameters (src/opt.rs adam_vec with the grads scaled by f:
 // the same arithmetic as launch_adam_f32 with clip = f).
 __global__ void adam_segs_kernel(const Seg *segs, float *P, const float *G, float *M, float *V, const float *f,
-                                 double lr, double wd, double b1, double b2, double eps, double bc1, double bc2) {
+                                 double lr, double wd, double b1, double b2, double eps, const double *st) {
     const Seg s = segs[blockIdx.y];
     const double clip = (double)*f;
+    const double bc1 = st[2], bc2 = st[3];
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x) {
         const i64 i = s.off + j;
         const double gi = __dadd_rn((double)(float)__dmul_rn((double)G[i], clip), __dmul_rn(wd, (double)P[i]));
@@ -389,17 +440,6 @@ __global__ void bn_running_kernel(const trba_model::ConvTab *tab, int nconv) {
 }
 
 __global__ void fill_f32_kernel(float *p, i64 n, float v) { GRID_LOOP(i, n) p[i] = v; }
-
-// f32 powi of Rust / LLVM (__powisf2): square and multiply.
-float powi_f32(float a, long long n) {
-    float r = 1.0f;
-    while (true) {
-        if (n & 1) r *= a;
-        n >>= 1;
-        if (!n) return r;
-        a *= a;
-    }
-}
 
 // ----------------------------------------------------------- building --
 struct Builder {
@@ -669,6 +709,7 @@ void allocate(trba_model *m) {
     m->gsq_total = b.z<double>(1);
     m->conv_gsq = b.z<double>((i64)m->convs.size());
     m->clip_f = b.p<float>(1);
+    m->step_state = b.p<double>(4);
     m->mat_step = b.p<float>((i64)m->mat_segs.size());
     m->conv_step = b.p<float>((i64)m->convs.size());
     m->in_img = b.p<int8_t>((i64)B * 3 * c.img_h * c.img_w);
@@ -689,23 +730,43 @@ struct Ctx {
 struct ProbeScope {
     Probe *p = nullptr;
     cudaStream_t st;
+    bool stamp = false;
     ProbeScope(trba_model *m, int kind, double ops, double bytes, cudaStream_t s) : st(s) {
         if (m->probe.kind != kind) return;
         p = &m->probe;
-        while (p->ev.size() < p->used + 2) {
-            cudaEvent_t e;
-            TRBA_CHECK(cudaEventCreate(&e));
-            p->ev.push_back(e);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        TRBA_CHECK(cudaStreamIsCapturing(st, &cs));
+        stamp = cs == cudaStreamCaptureStatusActive;
+        if (stamp) {
+            if (p->nstamp + 2 > 2 * kProbeStamps) {
+                p = nullptr;
+                return;
+            }
+            stamp_kernel<<<1, 1, 0, st>>>(p->stamps + p->nstamp);
+            TRBA_LAUNCH_CHECK();
+            p->stamped = true;
+        } else {
+            while (p->ev.size() < p->used + 2) {
+                cudaEvent_t e;
+                TRBA_CHECK(cudaEventCreate(&e));
+                p->ev.push_back(e);
+            }
+            TRBA_CHECK(cudaEventRecord(p->ev[p->used], st));
         }
-        TRBA_CHECK(cudaEventRecord(p->ev[p->used], st));
         p->ops += ops;
         p->bytes += bytes;
         p->launches += 1;
     }
     ~ProbeScope() {
         if (!p) return;
-        TRBA_CHECK(cudaEventRecord(p->ev[p->used + 1], st));
-        p->used += 2;
+        if (stamp) {
+            stamp_kernel<<<1, 1, 0, st>>>(p->stamps + p->nstamp + 1);
+            TRBA_LAUNCH_CHECK();
+            p->nstamp += 2;
+        } else {
+            TRBA_CHECK(cudaEventRecord(p->ev[p->used + 1], st));
+            p->used += 2;
+        }
     }
 };
 
@@ -1042,13 +1103,14 @@ void optimizer(trba_model *m, cudaStream_t st) {
     const auto &cf = m->cfg;
     float *P = m->P.get(), *G = m->G.get();
     sumsq_kernel<<<grid_for(m->n_params), 256, 0, st>>>(G, m->n_params, m->gsq_total.get());
-    clip_factor_kernel<<<1, 32, 0, st>>>(m->gsq_total.get(), m->t < cf.clip_warmup ? 1 : 0, m->clip_f.get());
-    m->t += 1;
-    const double bc1 = 1.0 - (double)powi_f32(0.9f, m->t), bc2 = 1.0 - (double)powi_f32(0.999f, m->t);
+    step_state_kernel<<<1, 32, 0, st>>>(m->step_state.get(), cf.clip_warmup);
+    clip_factor_kernel<<<1, 32, 0, st>>>(m->gsq_total.get(), m->step_state.get(), m->clip_f.get());
+    m->t += 1;  // host mirror of step_state[0]
     const double lr = (double)cf.lr, wd = (double)cf.weight_decay;
     const int nv = (int)m->vec_segs.size(), nm = (int)m->mat_segs.size(), ncv = (int)m->conv_segs.size();
     adam_segs_kernel<<<dim3(4, nv), 256, 0, st>>>(m->d_vec, P, G, m->Mm.get(), m->Vv.get(), m->clip_f.get(), lr, wd,
-                                                  (double)0.9f, (double)0.999f, (double)1e-8f, bc1, bc2);
+                                                  (double)0.9f, (double)0.999f, (double)1e-8f,
+                                                  m->step_state.get());
     muon_mat_norm_kernel<<<nm, 256, 0, st>>>(m->d_mat, G, m->clip_f.get(), cf.lr, cf.muon_cap, m->mat_step.get());
     muon_mat_apply_kernel<<<dim3(8, nm), 256, 0, st>>>(m->d_mat, P, G, m->clip_f.get(), m->mat_step.get(),
                                                        1.0f - cf.lr * cf.weight_decay);
@@ -1145,6 +1207,10 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     }
     TRBA_CHECK(cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming));
     TRBA_CHECK(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking));
+    TRBA_CHECK(cudaStreamCreateWithFlags(&m->gstream, cudaStreamNonBlocking));
+    TRBA_CHECK(cudaMalloc(&m->probe.stamps, 2 * kProbeStamps * sizeof(unsigned long long)));
+    TRBA_CHECK(cudaEventCreateWithFlags(&m->gfork, cudaEventDisableTiming));
+    TRBA_CHECK(cudaEventCreateWithFlags(&m->gjoin, cudaEventDisableTiming));
     TRBA_CHECK(cudaEventCreateWithFlags(&m->fork_ev, cudaEventDisableTiming));
     TRBA_CHECK(cudaEventCreateWithFlags(&m->join_ev, cudaEventDisableTiming));
     TRBA_CHECK(cudaDeviceSynchronize());
@@ -1164,7 +1230,12 @@ void trba_model_destroy(trba_model *m) {
     if (m->fork_ev) cudaEventDestroy(m->fork_ev);
     if (m->join_ev) cudaEventDestroy(m->join_ev);
     if (m->side) cudaStreamDestroy(m->side);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->gfork) cudaEventDestroy(m->gfork);
+    if (m->gjoin) cudaEventDestroy(m->gjoin);
+    if (m->gstream) cudaStreamDestroy(m->gstream);
     for (cudaEvent_t e : m->probe.ev) cudaEventDestroy(e);
+    if (m->probe.stamps) cudaFree(m->probe.stamps);
     delete m;
 }
 
@@ -1192,6 +1263,7 @@ int trba_model_set_params(trba_model *m, const float *host, long long n) {
     TRBA_CHECK(cudaMemset(m->Mm.get(), 0, n * 4));
     TRBA_CHECK(cudaMemset(m->Vv.get(), 0, n * 4));
     m->t = 0;
+    TRBA_CHECK(cudaMemset(m->step_state.get(), 0, 4 * sizeof(double)));
     requantize(m, 0);
     TRBA_CHECK(cudaDeviceSynchronize());
     return cuda_status();
@@ -1243,6 +1315,7 @@ int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t 
     cudaStream_t st = as_stream(stream);
     Ctx c{m, st, batch, m->P.get(), m->G.get()};
     m->last_B = batch;
+    if (m->probe.kind >= 0) m->probe.steps += 1;
     TRBA_CHECK(cudaMemsetAsync(m->zarena.base, 0, m->zarena.used, st));
     TRBA_CHECK(cudaMemsetAsync(m->G.get(), 0, (size_t)m->n_params * 4, st));
     cnn_forward(c, img);
@@ -1258,19 +1331,95 @@ int trba_model_optimizer_step(trba_model *m, void *stream) {
     return cuda_status();
 }
 
-int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
-                          const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
-    int rc = trba_model_forward_backward(m, img, text_in, target, ctc_tgt, ctc_len, batch, stream);
+}  // extern "C"
+
+namespace {
+
+// forward_backward, the data-parallel gradient all-reduce, optimizer_step.
+int step_body(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+              const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, cudaStream_t st) {
+    int rc = trba_model_forward_backward(m, img, text_in, target, ctc_tgt, ctc_len, batch, st);
     if (rc) return rc;
     if (m->comm) {
         const ncclResult_t r = nccl().AllReduce(m->G.get(), m->G.get(), (size_t)m->n_params, ncclFloat, ncclAvg,
-                                                m->comm, as_stream(stream));
+                                                m->comm, st);
         if (r != ncclSuccess) {
             report_error(__FILE__, __LINE__, nccl().GetErrorString(r), (int)r);
             return (int)r;
         }
     }
-    return trba_model_optimizer_step(m, stream);
+    return trba_model_optimizer_step(m, st);
+}
+
+// The step as one CUDA graph: recorded on the model's own stream the first
+// time these input pointers and batch are seen (recording executes nothing),
+// then replayed; the caller's stream is joined in and out with events.
+int graph_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+               const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, cudaStream_t user) {
+    const void *key[5] = {img, text_in, target, ctc_tgt, ctc_len};
+    bool same = m->gexec && m->gkey_batch == batch && m->gkey_probe == m->probe.kind;
+    for (int i = 0; i < 5 && same; ++i) same = m->gkey[i] == key[i];
+    if (!same) {
+        if (m->gexec) {
+            TRBA_CHECK(cudaGraphExecDestroy(m->gexec));
+            m->gexec = nullptr;
+        }
+        const long long t_host = m->t, l0 = launches_so_far();
+        cudaGraph_t g = nullptr;
+        TRBA_CHECK(cudaStreamBeginCapture(m->gstream, cudaStreamCaptureModeRelaxed));
+        const int rc = step_body(m, img, text_in, target, ctc_tgt, ctc_len, batch, m->gstream);
+        const cudaError_t e = cudaStreamEndCapture(m->gstream, &g);
+        m->t = t_host;  // recording ran nothing
+        m->graph_kernels = launches_so_far() - l0;
+        count_launches(-m->graph_kernels);  // counted when replayed
+        if (rc || e != cudaSuccess || !g) {
+            if (g) cudaGraphDestroy(g);
+            report_error(__FILE__, __LINE__, "trba_model_train_step: recording the step graph failed",
+                         e != cudaSuccess ? (int)e : -1);
+            return rc ? rc : -1;
+        }
+        const cudaError_t ei = cudaGraphInstantiate(&m->gexec, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) {
+            m->gexec = nullptr;
+            report_error(__FILE__, __LINE__, "trba_model_train_step: instantiating the step graph failed", (int)ei);
+            return (int)ei;
+        }
+        for (int i = 0; i < 5; ++i) m->gkey[i] = key[i];
+        m->gkey_batch = batch;
+        m->gkey_probe = m->probe.kind;
+        m->last_B = batch;
+    }
+    TRBA_CHECK(cudaEventRecord(m->gfork, user));
+    TRBA_CHECK(cudaStreamWaitEvent(m->gstream, m->gfork, 0));
+    TRBA_CHECK(cudaGraphLaunch(m->gexec, m->gstream));
+    count_launches(m->graph_kernels);
+    TRBA_CHECK(cudaEventRecord(m->gjoin, m->gstream));
+    TRBA_CHECK(cudaStreamWaitEvent(user, m->gjoin, 0));
+    m->t += 1;
+    return cuda_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
+                          const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
+    if (!m || !img || !text_in || !target || !ctc_tgt || !ctc_len || batch <= 0 || batch > m->B) return -1;
+    if (m->use_graphs)
+        return graph_step(m, img, text_in, target, ctc_tgt, ctc_len, batch, as_stream(stream));
+    return step_body(m, img, text_in, target, ctc_tgt, ctc_len, batch, as_stream(stream));
+}
+
+int trba_model_use_graphs(trba_model *m, int enable) {
+    if (!m) return -1;
+    m->use_graphs = enable != 0;
+    if (!m->use_graphs && m->gexec) {
+        TRBA_CHECK(cudaGraphExecDestroy(m->gexec));
+        m->gexec = nullptr;
+    }
+    return cuda_status();
 }
 
 int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
@@ -1327,28 +1476,45 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
 
 int trba_model_probe(trba_model *m, int kind) {
     if (!m || kind < -1 || kind > TRBA_PROBE_SGEMM) return -1;
+    if (m->gexec) {  // a recorded step graph may hold this probe's events
+        TRBA_CHECK(cudaStreamSynchronize(m->gstream));
+        TRBA_CHECK(cudaGraphExecDestroy(m->gexec));
+        m->gexec = nullptr;
+    }
     m->probe.kind = kind;
     m->probe.used = 0;
     m->probe.ops = 0.0;
     m->probe.bytes = 0.0;
+    m->probe.steps = 0;
     m->probe.launches = 0;
+    m->probe.nstamp = 0;
+    m->probe.stamped = false;
     return 0;
 }
 
-int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes) {
-    if (!m || !ms_total || !launches || !ops || !bytes) return -1;
+int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes,
+                          long long *steps) {
+    if (!m || !ms_total || !launches || !ops || !bytes || !steps) return -1;
     auto &p = m->probe;
     double ms = 0.0;
-    if (p.used) TRBA_CHECK(cudaEventSynchronize(p.ev[p.used - 1]));
-    for (size_t i = 0; i + 1 < p.used; i += 2) {
-        float t = 0.0f;
-        TRBA_CHECK(cudaEventElapsedTime(&t, p.ev[i], p.ev[i + 1]));
-        ms += t;
+    if (p.stamped) {  // launches of the latest replay of the step graph
+        TRBA_CHECK(cudaStreamSynchronize(m->gstream));
+        std::vector<unsigned long long> h(p.nstamp);
+        TRBA_CHECK(cudaMemcpy(h.data(), p.stamps, p.nstamp * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i + 1 < p.nstamp; i += 2) ms += (double)(h[i + 1] - h[i]) * 1e-6;
+    } else {
+        if (p.used) TRBA_CHECK(cudaEventSynchronize(p.ev[p.used - 1]));
+        for (size_t i = 0; i + 1 < p.used; i += 2) {
+            float t = 0.0f;
+            TRBA_CHECK(cudaEventElapsedTime(&t, p.ev[i], p.ev[i + 1]));
+            ms += t;
+        }
     }
     *ms_total = ms;
     *launches = p.launches;
     *ops = p.ops;
     *bytes = p.bytes;
+    *steps = p.steps;
     return cuda_status();
 }
 

@@ -21,6 +21,8 @@ bool abort_on_error() { return g_abort.load() != 0; }
 
 static std::atomic<long long> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
 
 void report_error(const char *file, int line, const char *what, int code) {
     {

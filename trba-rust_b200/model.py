@@ -160,11 +160,16 @@ class QatModel:
         self._check(self.L.trba_model_probe(self.h, kind), "probe")
 
     def probe_read(self):
-        """(device ms summed over the probed launches, launches, algorithmic ops, algorithmic bytes)."""
-        ms, n, ops, nbytes = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
-        self._check(self.L.trba_model_probe_read(self.h, C.byref(ms), C.byref(n), C.byref(ops), C.byref(nbytes)),
-                    "probe_read")
-        return ms.value, n.value, ops.value, nbytes.value
+        """(device ms summed over the probed launches, launches, algorithmic ops,
+        algorithmic bytes, steps covered)."""
+        ms, n, ops, nbytes, steps = C.c_double(), C.c_longlong(), C.c_double(), C.c_double(), C.c_longlong()
+        self._check(self.L.trba_model_probe_read(self.h, C.byref(ms), C.byref(n), C.byref(ops), C.byref(nbytes),
+                                                 C.byref(steps)), "probe_read")
+        return ms.value, n.value, ops.value, nbytes.value, steps.value
+
+    def use_graphs(self, enable: bool = True):
+        """Record the step as a CUDA graph and replay it (inputs refreshed in place)."""
+        self._check(self.L.trba_model_use_graphs(self.h, 1 if enable else 0), "use_graphs")
 
     def dp_init(self, id128: bytes, rank: int, world: int):
         buf = C.create_string_buffer(id128, 128)
