@@ -72,6 +72,18 @@ float *trba_model_grad_buffer(trba_model *m);
  * [B] (tokens plus eos).  Leaves the loss in trba_model_loss_dev(). */
 int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
                                 const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream);
+/* Inference (run_inference, later snapshot src/main.rs:2690; greedy
+ * decoding src/attn.rs:368-447): the CNN with BN running statistics, the
+ * BiLSTM stack, greedy attention decoding from sos.  step_tokens (device,
+ * [max_len+1, batch] int32, or NULL for the model's own buffer) receives the
+ * argmax token of every decoding step. */
+int trba_model_infer(trba_model *m, const int8_t *img, int batch, int32_t *step_tokens, void *stream);
+/* The same from a host image batch, with the reference's output rule: eos is
+ * not emitted and decoding stops after the first step at which every sample
+ * produced eos.  tokens (host, [batch, max_len+1]) gets each sample's tokens
+ * followed by -1, lengths (host, [batch]) their counts.  Synchronises. */
+int trba_model_infer_host(trba_model *m, const int8_t *img, int batch, int32_t *tokens, int32_t *lengths,
+                          void *stream);
 /* Clip (first clip_warmup steps), Muon/Adam, re-quantise. */
 int trba_model_optimizer_step(trba_model *m, void *stream);
 /* forward_backward, gradient all-reduce (when data-parallel), optimizer_step. */
@@ -84,6 +96,8 @@ int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *
                                void *stream);
 /* Device pointer to 4 floats: total loss, attention CE, CTC, CE grad scale. */
 const float *trba_model_loss_dev(const trba_model *m);
+/* Device pointer to the model's [max_len+1, batch] greedy-decoding tokens. */
+const int32_t *trba_model_step_tokens_dev(const trba_model *m);
 /* Batch-norm running statistics (mean then var, conv manifest order). */
 int trba_model_get_running_stats(trba_model *m, float *host, long long n);
 long long trba_model_running_stats_count(const trba_model *m);

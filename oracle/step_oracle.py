@@ -399,7 +399,7 @@ class OracleTrba:
         return out
 
     # -- ConvQat::forward, src/qnet.rs:788-916 -----------------------------
-    def conv_fwd(self, name, q_in, s_in, b, h, w):
+    def conv_fwd(self, name, q_in, s_in, b, h, w, train=True):
         cs = self.convs[name]
         c = cs.spec
         ho, wo = c.out_hw(h, w)
@@ -413,7 +413,10 @@ class OracleTrba:
         x = np.zeros(n, F32)
         self.be("launch_epilogue_f32", acc, c.cout, float(F32(s_in) * cs.w_s), x, c.cout, ho, wo, n)
         mean, var = np.zeros(c.cout, F32), np.zeros(c.cout, F32)
-        self.be("launch_bn_stats", x, b, c.cout, ho * wo, mean, var)
+        if train:
+            self.be("launch_bn_stats", x, b, c.cout, ho * wo, mean, var)
+        else:  # inference: running statistics (src/qnet.rs:871-876)
+            mean[:], var[:] = self.run_mean[name], self.run_var[name]
         y = np.zeros(n, F32)
         self.be("launch_bn_apply", x, mean, var, self.p[f"{name}.gamma"], self.p[f"{name}.beta"], BN_EPS, y,
                 c.cout, ho * wo, n)
@@ -463,12 +466,12 @@ class OracleTrba:
         return gi
 
     # -- BasicBlock::forward, src/qnet.rs:1182-1271 ------------------------
-    def block_fwd(self, bname, has_ds, q_in, s_in, b, h, w):
+    def block_fwd(self, bname, has_ds, q_in, s_in, b, h, w, train=True):
         cout = self.convs[f"{bname}.conv2"].spec.cout
-        ds = self.conv_fwd(f"{bname}.downsample.0", q_in, s_in, b, h, w) if has_ds else None
-        f1 = self.conv_fwd(f"{bname}.conv1", q_in, s_in, b, h, w)
+        ds = self.conv_fwd(f"{bname}.downsample.0", q_in, s_in, b, h, w, train) if has_ds else None
+        f1 = self.conv_fwd(f"{bname}.conv1", q_in, s_in, b, h, w, train)
         q1, s1 = self.relu_quant(f1["y"])
-        f2 = self.conv_fwd(f"{bname}.conv2", q1, s1, b, f1["ho"], f1["wo"])
+        f2 = self.conv_fwd(f"{bname}.conv2", q1, s1, b, f1["ho"], f1["wo"], train)
         hw = f2["ho"] * f2["wo"]
         n_out = b * cout * hw
         pooled = np.zeros(b * cout, F32)
@@ -528,14 +531,14 @@ class OracleTrba:
         return total
 
     # -- SEResNetQ::forward / backward, src/qnet.rs:1533-1737 ---------------
-    def cnn_fwd(self, img, b):
+    def cnn_fwd(self, img, b, train=True):
         cfg = self.cfg
         h, w = cfg.img_h, cfg.img_w
         s_img = F32(1.0) / F32(127.0)
         chain = []
-        f0 = self.conv_fwd("stem.0", img, s_img, b, h, w)
+        f0 = self.conv_fwd("stem.0", img, s_img, b, h, w, train)
         q0, s0 = self.relu_quant(f0["y"])
-        f1 = self.conv_fwd("stem.3", q0, s0, b, h, w)
+        f1 = self.conv_fwd("stem.3", q0, s0, b, h, w, train)
         q1, s1 = self.relu_quant(f1["y"])
         c1 = self.convs["stem.3"].spec.cout
         qp = np.zeros(b * c1 * (h // 2) * (w // 2), np.int8)
@@ -544,13 +547,13 @@ class OracleTrba:
         q, s = qp, s1
         blocks = []
         for (name, ic, oc, st) in block_specs(cfg):
-            q, s, tr = self.block_fwd(name, st != 1 or ic != oc, q, s, b, h, w)
+            q, s, tr = self.block_fwd(name, st != 1 or ic != oc, q, s, b, h, w, train)
             h, w = tr["ho"], tr["wo"]
             blocks.append(tr)
             chain.append((q, s))
-        fo0 = self.conv_fwd("conv_out.0", q, s, b, h, w)
+        fo0 = self.conv_fwd("conv_out.0", q, s, b, h, w, train)
         qo0, so0 = self.relu_quant(fo0["y"])
-        fo1 = self.conv_fwd("conv_out.3", qo0, so0, b, fo0["ho"], fo0["wo"])
+        fo1 = self.conv_fwd("conv_out.3", qo0, so0, b, fo0["ho"], fo0["wo"], train)
         qo1, so1 = self.relu_quant(fo1["y"])
         hf, wf = fo1["ho"], fo1["wo"]
         fv = self.dequant(qo1, so1)
@@ -717,6 +720,63 @@ class OracleTrba:
         logits = logits_sb.reshape(steps, b, V).transpose(1, 0, 2).copy()  # [B, steps, V]
         tr.update(bh=bh, proj_h=proj_h, b=b, t=t, steps=steps)
         return logits, tr
+
+    # -- AttentionDecoder::greedy_decode, src/attn.rs:368-447 --------------
+    def greedy_decode(self, enc, b, t):
+        """Greedy decoding from sos: the argmax token (first maximum) is fed
+        back; decoding stops after the first step at which every sample of the
+        batch produced eos; eos tokens are not emitted, tokens after a
+        sample's eos are (as in the reference).  Returns (per-sample token
+        lists, per-step argmax tokens [steps, b])."""
+        cfg = self.cfg
+        H, V, steps = cfg.hidden, cfg.classes, cfg.steps
+        P = self.p
+        bh = enc.reshape(b, t, H)
+        proj_h = dot64(bh.reshape(b * t, H), P["attn.i2h.w"].T).reshape(b, t, H)
+        h = np.zeros((b, H), F32)
+        cc = np.zeros((b, H), F32)
+        scw = P["attn.score.w"].reshape(H)
+        wc, wtok = P["attn.w_ih"][:, :H], P["attn.w_ih"][:, H:]
+        bsum = (P["attn.b_ih"] + P["attn.b_hh"]).astype(F32)
+        tok = np.full(b, cfg.sos, np.int64)
+        out = [[] for _ in range(b)]
+        step_tok = np.full((steps, b), -1, np.int32)
+        for st in range(steps):
+            phh = linear_fwd(h, P["attn.h2h.w"], P["attn.h2h.b"])
+            tn = tanh32(proj_h + phh[:, None, :])
+            e = dot64(tn, scw)
+            ex = exp32(e - e.max(axis=1, keepdims=True))
+            alpha = (ex / sum64(ex, axis=1)[:, None]).astype(F32)
+            ctx = np.einsum("bt,btk->bk", alpha.astype(F64), bh.astype(F64)).astype(F32)
+            pre = (((bsum + dot64(ctx, wc.T)) + wtok[:, tok].T) + dot64(h, P["attn.w_hh"].T)).astype(F32)
+            ig, fg = sigmoid(pre[:, :H]), sigmoid(pre[:, H:2 * H])
+            cg, og = tanh32(pre[:, 2 * H:3 * H]), sigmoid(pre[:, 3 * H:])
+            cc = (fg * cc + ig * cg).astype(F32)
+            h = (og * tanh32(cc)).astype(F32)
+            logits = linear_fwd(h, P["attn.gen.w"], P["attn.gen.b"])
+            best = np.argmax(logits, axis=1)
+            step_tok[st] = best
+            all_eos = True
+            for bi in range(b):
+                if best[bi] == cfg.eos:
+                    continue
+                all_eos = False
+                out[bi].append(int(best[bi]))
+            tok = best
+            if all_eos:
+                break
+        return out, step_tok
+
+    def infer(self, img):
+        """run_inference (later snapshot src/main.rs:2690): the CNN with BN
+        running statistics, the BiLSTM stack, greedy attention decoding."""
+        b = img.shape[0]
+        feat, ctr = self.cnn_fwd(np.ascontiguousarray(img.reshape(-1)), b, train=False)
+        t = ctr["wf"]
+        x = feat
+        for li in range(self.cfg.rnn_layers):
+            x, _ = self.bilstm_layer_fwd(li, x, b, t)
+        return self.greedy_decode(x.reshape(b, t, self.cfg.hidden), b, t)
 
     def attn_bwd(self, d_logits, tr):
         cfg, P, G = self.cfg, self.p, self.g

@@ -156,7 +156,13 @@ __device__ PlaneSrc plane_src(const Src &s, int b, int c, bool leader, float *me
     p.mean = p.r = p.gamma = p.beta = p.gate = p.res_s = 0.0f;
     p.res_f = s.res_f;
     p.res_q = s.res_q;
-    if (s.kind == SRC_BN) {
+    if (s.kind == SRC_BN_EVAL) {  // src/qnet.rs:871-876: mean / var are the running statistics
+        p.kind = SRC_BN;
+        p.mean = s.run_mean[c];
+        p.r = bn_rstd(s.run_var[c]);
+        p.gamma = s.gamma[c];
+        p.beta = s.beta[c];
+    } else if (s.kind == SRC_BN) {
         float m, v;
         bn_mean_var(s.bn_acc, s.C, c, s.count, m, v);
         p.mean = m;

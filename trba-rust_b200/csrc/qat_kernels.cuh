@@ -19,12 +19,14 @@ enum SrcKind {
     SRC_FLOAT = 1,     // a stored fp32 tensor
     SRC_SE_RES_F = 2,  // z = y2 * gate[b,c] + res_f[i]          (downsample branch)
     SRC_SE_RES_Q = 3,  // z = y2 * gate[b,c] + q_in[i] * s_in    (identity branch)
+    SRC_BN_EVAL = 4,   // y = BN(x) with the running statistics (inference)
 };
 
 struct Src {
     int kind;
     const float *x;       // SRC_BN: x; SRC_FLOAT / SRC_SE_*: y / y2
     const double *bn_acc; // SRC_BN: [2C] sum / sum of squares of x
+    const float *run_mean, *run_var;  // SRC_BN_EVAL
     const float *gamma, *beta;
     const float *gate;    // SRC_SE_*: [B*C]
     const float *res_f;   // SRC_SE_RES_F

@@ -193,6 +193,7 @@ struct trba_model {
     i64 gemm_ws_elems = 0;
     Ref<float> ones;       // column-sum helper
     Ref<float> loss;  // 4 floats
+    Ref<int32_t> step_tokens;  // [steps, B]: greedy-decoding argmax of every step (inference)
     // optimiser scratch (zeroed per step)
     Ref<double> gsq_total;
     Ref<double> conv_gsq;  // per conv
@@ -706,6 +707,7 @@ void allocate(trba_model *m) {
     m->gemm_ws = b.p<double>(m->gemm_ws_elems);
     m->ones = b.p<float>((i64)B * (S > T ? S : T) * 1);
     m->loss = b.p<float>(4);
+    m->step_tokens = b.p<int32_t>((i64)S * B);
     m->gsq_total = b.z<double>(1);
     m->conv_gsq = b.z<double>((i64)m->convs.size());
     m->clip_f = b.p<float>(1);
@@ -725,6 +727,7 @@ struct Ctx {
     cudaStream_t st;
     int B;
     float *P, *G;
+    bool eval = false;  // inference: BN with the running statistics, no running-stat update
 };
 
 struct ProbeScope {
@@ -798,9 +801,11 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
 
 qat::Src bn_src(Ctx &c, ConvL &L) {
     qat::Src s{};
-    s.kind = qat::SRC_BN;
+    s.kind = c.eval ? qat::SRC_BN_EVAL : qat::SRC_BN;
     s.x = L.x.get();
     s.bn_acc = L.bn_acc.get();
+    s.run_mean = L.run_mean.get();
+    s.run_var = L.run_var.get();
     s.gamma = c.P + L.gamma_off;
     s.beta = c.P + L.beta_off;
     s.C = L.cout;
@@ -914,8 +919,10 @@ void cnn_forward(Ctx &c, const int8_t *img) {
     conv_bn_quant(c, cv[nc - 1], cv[nc - 2].q.get(), cv[nc - 2].s_q.get());
     const ConvL &o1 = cv[nc - 1];
     qat::features(o1.q.get(), o1.s_q.get(), c.B, o1.cout, o1.Ho, o1.Wo, m->feat.get(), c.st);
-    bn_running_kernel<<<nc, 128, 0, c.st>>>(m->d_convtab, nc);
-    TRBA_LAUNCH_CHECK();
+    if (!c.eval) {
+        bn_running_kernel<<<nc, 128, 0, c.st>>>(m->d_convtab, nc);
+        TRBA_LAUNCH_CHECK();
+    }
 }
 
 void cnn_backward(Ctx &c) {
@@ -1020,6 +1027,43 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
              m->ctc_sample_loss.get(), c.st);
     seq::loss_finalize(m->row_loss.get(), target, B, S, cf.pad, m->ctc_sample_loss.get(), ctc_len, T, cf.ctc_weight,
                        m->dlogits.get(), V, m->loss.get(), c.st);
+}
+
+// Inference head (run_inference, later snapshot src/main.rs:2690): the
+// BiLSTM stack as in training, then greedy attention decoding.
+void head_infer(Ctx &c, int32_t *step_tokens) {
+    trba_model *m = c.m;
+    const auto &cf = m->cfg;
+    const int B = c.B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps;
+    const float *x = m->feat.get();
+    for (auto &r : m->rnn) {
+        for (int d = 0; d < 2; ++d) {
+            sgemm(c, gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
+            seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
+                          r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
+        }
+        sgemm(c, gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
+              c.st);
+        x = r.y.get();
+    }
+    const float *enc = x;
+    sgemm(c, gemm(m, B * T, H, H, enc, H, 1, c.P + entry_off(m, "attn.i2h.w"), 1, H, m->proj_h.get(), H), c.st);
+    seq::AttnFwd a{};
+    a.bh = enc;
+    a.proj_h = m->proj_h.get();
+    a.h2h_w = c.P + entry_off(m, "attn.h2h.w");
+    a.h2h_b = c.P + entry_off(m, "attn.h2h.b");
+    a.score_w = c.P + entry_off(m, "attn.score.w");
+    a.w_ih = c.P + entry_off(m, "attn.w_ih");
+    a.b_ih = c.P + entry_off(m, "attn.b_ih");
+    a.w_hh = c.P + entry_off(m, "attn.w_hh");
+    a.b_hh = c.P + entry_off(m, "attn.b_hh");
+    a.gen_w = c.P + entry_off(m, "attn.gen.w");
+    a.gen_b = c.P + entry_off(m, "attn.gen.b");
+    a.sos = cf.sos;
+    a.B = B, a.T = T, a.H = H, a.V = V, a.steps = S;
+    a.step_tokens = step_tokens;
+    seq::attn_decode(a, c.st);
 }
 
 void head_backward(Ctx &c) {
@@ -1285,6 +1329,7 @@ int trba_model_get_grads(trba_model *m, float *host, long long n) {
 
 float *trba_model_grad_buffer(trba_model *m) { return m ? m->G.get() : nullptr; }
 const float *trba_model_loss_dev(const trba_model *m) { return m ? m->loss.get() : nullptr; }
+const int32_t *trba_model_step_tokens_dev(const trba_model *m) { return m ? m->step_tokens.get() : nullptr; }
 long long trba_model_step_count(const trba_model *m) { return m ? m->t : -1; }
 long long trba_model_device_bytes(const trba_model *m) {
     return m ? (long long)(m->arena.used + m->zarena.used) : -1;
@@ -1322,6 +1367,54 @@ int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t 
     head_forward(c, text_in, target, ctc_tgt, ctc_len);
     head_backward(c);
     cnn_backward(c);
+    return cuda_status();
+}
+
+int trba_model_infer(trba_model *m, const int8_t *img, int batch, int32_t *step_tokens, void *stream) {
+    if (!m || !img || batch <= 0 || batch > m->B) return -1;
+    cudaStream_t st = as_stream(stream);
+    Ctx c{m, st, batch, m->P.get(), m->G.get()};
+    c.eval = true;
+    m->last_B = batch;
+    cnn_forward(c, img);
+    head_infer(c, step_tokens ? step_tokens : m->step_tokens.get());
+    return cuda_status();
+}
+
+int trba_model_infer_host(trba_model *m, const int8_t *img, int batch, int32_t *tokens, int32_t *lengths,
+                          void *stream) {
+    if (!m || !img || !tokens || !lengths || batch <= 0 || batch > m->B) return -1;
+    cudaStream_t st = as_stream(stream);
+    const auto &cf = m->cfg;
+    const int S = m->steps;
+    TRBA_CHECK(cudaMemcpyAsync(m->in_img.get(), img, (size_t)batch * 3 * cf.img_h * cf.img_w, cudaMemcpyHostToDevice,
+                               st));
+    int rc = trba_model_infer(m, m->in_img.get(), batch, nullptr, stream);
+    if (rc) return rc;
+    std::vector<int32_t> stok((size_t)S * batch);
+    TRBA_CHECK(cudaMemcpyAsync(stok.data(), m->step_tokens.get(), stok.size() * sizeof(int32_t),
+                               cudaMemcpyDeviceToHost, st));
+    TRBA_CHECK(cudaStreamSynchronize(st));
+    // src/attn.rs:423-443: eos is not emitted; decoding stops after the first
+    // step at which every sample of the batch produced eos.
+    int last = S - 1;
+    for (int s = 0; s < S; ++s) {
+        bool all_eos = true;
+        for (int b = 0; b < batch && all_eos; ++b) all_eos = stok[(size_t)s * batch + b] == cf.eos;
+        if (all_eos) {
+            last = s;
+            break;
+        }
+    }
+    for (int b = 0; b < batch; ++b) {
+        int n = 0;
+        for (int s = 0; s <= last; ++s) {
+            const int t = stok[(size_t)s * batch + b];
+            if (t != cf.eos) tokens[(size_t)b * S + n++] = t;
+        }
+        lengths[b] = n;
+        for (int j = n; j < S; ++j) tokens[(size_t)b * S + j] = -1;
+    }
     return cuda_status();
 }
 

@@ -206,6 +206,12 @@ __device__ __forceinline__ double dot2_d(const float *x, const float *w, int str
     return a0 + a1;
 }
 
+// DECODE = false: teacher-forced forward of the training step (tokens from
+// text_in, every trace stored).  DECODE = true: greedy decoding
+// (src/attn.rs:368-447): the token fed at step s is the argmax (first
+// maximum) of the generator logits of step s-1, sos at step 0; only the
+// per-step argmax tokens are stored.
+template <bool DECODE>
 __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
     extern __shared__ float sm[];
     const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
@@ -230,7 +236,9 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
         const int k = i / H, j = i - k * H;
         h2hT[j * H + k] = a.h2h_w[i];
     }
+    float *logit = reinterpret_cast<float *>(tok + S);  // [S][V] (DECODE)
     for (int i = threadIdx.x; i < S * H; i += blockDim.x) h[i] = c[i] = 0.0f;
+    if (DECODE && threadIdx.x < S) tok[threadIdx.x] = a.sos;
     __syncthreads();
     for (int st = 0; st < a.steps; ++st) {
         // proj_hh = h2h(h) + bias
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             const int sl = i / H, k = i - sl * H;
             phh[i] = fadd((float)dot2_d(h + sl * H, h2hT + k, H, H), a.h2h_b[k]);
         }
-        if (threadIdx.x < S) {
+        if (!DECODE && threadIdx.x < S) {
             const int b = min(b0 + (int)threadIdx.x, a.B - 1);
             tok[threadIdx.x] = a.text_in[(i64)b * a.steps + st];
         }
@@ -249,7 +257,7 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             const int b = b0 + sl;
             const float v = cr_tanhf(fadd(a.proj_h[((i64)min(b, a.B - 1) * T) * H + r], phh[sl * H + k]));
             tn[i] = v;
-            if (b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T) * H + r] = v;
+            if (!DECODE && b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T) * H + r] = v;
         }
         __syncthreads();
         // scores e = tanh(.) . score_w, one warp per (sample, t)
@@ -276,7 +284,7 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             for (int t = lane; t < T; t += 32) {
                 const float v = fdiv(al[sl * T + t], sf);
                 al[sl * T + t] = v;
-                if (b < a.B) a.alpha[((i64)st * a.B + b) * T + t] = v;
+                if (!DECODE && b < a.B) a.alpha[((i64)st * a.B + b) * T + t] = v;
             }
         }
         __syncthreads();
@@ -289,10 +297,13 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             ctx[i] = (float)acc;
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < S * CV; i += blockDim.x) {
-            const int sl = i / CV, j = i - sl * CV, b = b0 + sl;
-            if (b < a.B)
-                a.cell_in[((i64)st * a.B + b) * CV + j] = j < H ? ctx[sl * H + j] : (j - H == tok[sl] ? 1.0f : 0.0f);
+        if (!DECODE) {
+            for (int i = threadIdx.x; i < S * CV; i += blockDim.x) {
+                const int sl = i / CV, j = i - sl * CV, b = b0 + sl;
+                if (b < a.B)
+                    a.cell_in[((i64)st * a.B + b) * CV + j] =
+                        j < H ? ctx[sl * H + j] : (j - H == tok[sl] ? 1.0f : 0.0f);
+            }
         }
         // gate pre-activations: (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h
         for (int i = threadIdx.x; i < S * G4; i += blockDim.x) {
@@ -309,7 +320,7 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             const float ig = sigm(pg[k]), fg = sigm(pg[H + k]), cg = cr_tanhf(pg[2 * H + k]), og = sigm(pg[3 * H + k]);
             const float cn = fadd(fmul(fg, c[i]), fmul(ig, cg));
             const float hn = fmul(og, cr_tanhf(cn));
-            if (b < a.B) {
+            if (!DECODE && b < a.B) {
                 const i64 sb = (i64)st * a.B + b;
                 a.gates[sb * G4 + k] = ig;
                 a.gates[sb * G4 + H + k] = fg;
@@ -322,6 +333,42 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             h[i] = hn;
         }
         __syncthreads();
+        if (DECODE) {
+            // generator logits = gen_w h + gen_b (the training path's GEMM
+            // expression: f64 dot rounded once, then the bias)
+            for (int i = threadIdx.x; i < S * V; i += blockDim.x) {
+                const int sl = i / V, v = i - sl * V;
+                logit[i] = fadd((float)dot2_d(h + sl * H, a.gen_w + (i64)v * H, 1, H), a.gen_b[v]);
+            }
+            __syncthreads();
+            // argmax, first maximum, one warp per sample
+            for (int sl = warp; sl < S; sl += nwarps) {
+                float bv = -INFINITY;
+                int bi = V;
+                for (int v = lane; v < V; v += 32) {
+                    const float x = logit[sl * V + v];
+                    if (x > bv) {
+                        bv = x;
+                        bi = v;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    const int best = bi < V ? bi : 0;  // nothing above -inf: the reference keeps 0
+                    tok[sl] = best;
+                    if (b0 + sl < a.B) a.step_tokens[(i64)st * a.B + b0 + sl] = best;
+                }
+            }
+            __syncthreads();
+        }
     }
 }
 
@@ -675,8 +722,17 @@ void lstm_bwd(const float *dcat, const float *gates, const float *c, const float
 void attn_fwd(const AttnFwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, S = kAttnS;
     const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S);
-    set_smem((const void *)attn_fwd_kernel, smem);
-    attn_fwd_kernel<<<(a.B + S - 1) / S, 256, smem, st>>>(a);
+    set_smem((const void *)attn_fwd_kernel<false>, smem);
+    attn_fwd_kernel<false><<<(a.B + S - 1) / S, 256, smem, st>>>(a);
+    TRBA_LAUNCH_CHECK();
+}
+
+void attn_decode(const AttnFwd &a, cudaStream_t st) {
+    const int H = a.H, T = a.T, V = a.V, S = kAttnS;
+    const size_t smem =
+        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S + (size_t)S * V);
+    set_smem((const void *)attn_fwd_kernel<true>, smem);
+    attn_fwd_kernel<true><<<(a.B + S - 1) / S, 256, smem, st>>>(a);
     TRBA_LAUNCH_CHECK();
 }
 

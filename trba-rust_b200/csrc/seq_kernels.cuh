@@ -53,8 +53,15 @@ struct AttnFwd {
     float *cell_in;  // [steps, B, H+V]  (context, then the one-hot token)
     float *gates;    // [steps, B, 4H]
     float *hs, *cs;  // [steps, B, H]
+    // greedy decoding only (attn_decode): generator, start token, output
+    const float *gen_w = nullptr, *gen_b = nullptr;  // [V, H], [V]
+    int sos = 1;
+    int32_t *step_tokens = nullptr;  // [steps, B]: argmax token of every step
 };
 void attn_fwd(const AttnFwd &a, cudaStream_t st);
+// Greedy decoding (src/attn.rs:368-447) over every step; the caller applies
+// the reference's stop rule (all samples at eos) to step_tokens.
+void attn_decode(const AttnFwd &a, cudaStream_t st);
 
 // Backward (src/attn.rs:263-500): d_out_hid [steps, B, H]; writes dgates
 // [steps, B, 4H], de [steps, B, T], dprojhh [steps, B, H], d_proj_h [B, T, H]

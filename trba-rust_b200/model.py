@@ -143,6 +143,29 @@ class QatModel:
                                                       _ptr(ctc_len), b, _ptr(loss), stream), "train_step_host")
         return loss
 
+    def infer(self, img, stream=None):
+        """Greedy decoding of device images [B, 3, H, W] int8; returns the
+        argmax token of every step, [max_len+1, B] int32 (synchronises)."""
+        b = int(img.shape[0])
+        self._check(self.L.trba_model_infer(self.h, _ptr(img), b, None, stream), "infer")
+        out = np.empty((self.cfg.steps, b), np.int32)
+        self.L.cuda_sync(None)
+        self.L.cuda_memcpy_d2h(_ptr(out), self._step_tokens_ptr(), out.nbytes, None)
+        return out
+
+    def _step_tokens_ptr(self):
+        return C.c_void_p(self.L.trba_model_step_tokens_dev(self.h))
+
+    def infer_host(self, img, stream=None) -> list:
+        """Greedy decoding of host images; the reference's output: one token
+        list per line (eos not emitted, batch-level stop)."""
+        img = np.ascontiguousarray(img, np.int8)
+        b = int(img.shape[0])
+        tok = np.empty((b, self.cfg.steps), np.int32)
+        lens = np.empty(b, np.int32)
+        self._check(self.L.trba_model_infer_host(self.h, _ptr(img), b, _ptr(tok), _ptr(lens), stream), "infer_host")
+        return [tok[i, :lens[i]].tolist() for i in range(b)]
+
     def loss(self) -> np.ndarray:
         """[total, attention CE, CTC] of the last step (synchronises)."""
         out = np.zeros(3, np.float32)
