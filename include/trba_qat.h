@@ -106,6 +106,17 @@ long long trba_model_step_count(const trba_model *m);
 /* Bytes of device memory the model holds. */
 long long trba_model_device_bytes(const trba_model *m);
 
+/* Optimiser state and BN running statistics in and out, for checkpoints
+ * (src/main.rs:1099-1193 of the later snapshot saves them): the Adam first /
+ * second moments of every parameter (manifest order, zero where Adam is not
+ * used), the running statistics in trba_model_get_running_stats' order, and
+ * the optimiser step count.  set_params resets all three, so restore them
+ * after it. */
+int trba_model_get_moments(trba_model *m, float *m_host, float *v_host, long long n);
+int trba_model_set_moments(trba_model *m, const float *m_host, const float *v_host, long long n);
+int trba_model_set_running_stats(trba_model *m, const float *host, long long n);
+int trba_model_set_step_count(trba_model *m, long long t);
+
 /* Diagnostics: copy an internal fp32 buffer of the last step to the host
  * (feat, dfeat, enc, d_enc, logits, dlogits, ctc_logits, dctc, <conv>.x,
  * <conv>.mean, <conv>.var); n must equal the buffer's element count. */

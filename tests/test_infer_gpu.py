@@ -45,6 +45,9 @@ def test_greedy_decoding_matches_oracle(geom, B, steps, lib, cuda):
     ran = want_steps[:, 0] >= 0  # the oracle stops at the first all-eos step
     assert np.array_equal(got_steps[ran], want_steps[ran])
     assert gm.infer_host(img) == want_lists
+    other, _, _, _ = so.make_batch(ocfg, B, seed=4321)
+    gm.infer_host(other)  # an unrelated call in between leaves no trace
+    assert gm.infer_host(img) == want_lists
     assert lib.trba_last_error() == 0, lib.trba_last_error_string()
 
 

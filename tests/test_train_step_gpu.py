@@ -176,3 +176,47 @@ def test_graph_replay_equals_eager_steps(lib, cuda):
     assert np.array_equal(eager.get_params(), graph.get_params())
     torch.cuda.synchronize()
     assert lib.trba_last_error() == 0, lib.trba_last_error_string()
+
+
+@pytest.mark.parametrize("version", [6, 5, 4])
+def test_checkpoint_resume_equals_uninterrupted_training(version, lib, cuda, tmp_path):
+    """TRBA_V6 written (and V5 / V4 derived from it as the reference lays them
+    out) and read back into a fresh model: training continues exactly as the
+    uninterrupted model (V4 carries no Adam moments, so only V6 / V5 resume
+    bit-identically; V4 restores weights, BN statistics and the step)."""
+    import struct
+    import trba_b200.checkpoint as ck
+    geom = dict(img_w=64, max_len=4)
+    ocfg, params, a, man = _setup(geom, 8, seed=61)
+    batches = [so.make_batch(ocfg, 8, seed=500 + i) for i in range(4)]
+    for bt in batches[:2]:
+        a.train_step(*_to_dev(*bt, ocfg.steps))
+    path = tmp_path / "model.ckpt"
+    ck.save(a, path, epoch_done=3, batch_in_epoch=17)
+    if version < 6:  # rewrite into the older layouts
+        full = ck.read(path)
+        with open(path, "wb") as f:
+            f.write(ck.MAGIC_V5 if version == 5 else ck.MAGIC_V4)
+            f.write(struct.pack("<Q", full["epoch_done"]))
+            if version == 5:
+                f.write(struct.pack("<Q", full["batch_in_epoch"]))
+            f.write(struct.pack("<Q", full["opt_t"]))
+            f.write(struct.pack("<Q", len(full["params"])))
+            for _, val, m, v in full["params"]:
+                for arr in ((val, m, v) if version == 5 else (val,)):
+                    f.write(struct.pack("<Q", arr.size) + arr.astype("<f4").tobytes())
+            for rm, rv, cm, cv in full["convs"]:
+                for arr in ((rm, rv, cm, cv) if version == 5 else (rm, rv)):
+                    f.write(struct.pack("<Q", arr.size) + arr.astype("<f4").tobytes())
+    _, _, b, _ = _setup(geom, 8, seed=999)  # different weights: everything must come from the file
+    meta = ck.load(b, path)
+    assert meta["version"] == version and meta["opt_t"] == 2 and meta["epoch_done"] == 3
+    assert np.array_equal(a.get_params(), b.get_params())
+    assert np.array_equal(a.running_stats(), b.running_stats())
+    assert b.step_count() == 2
+    for bt in batches[2:]:
+        a.train_step(*_to_dev(*bt, ocfg.steps))
+        b.train_step(*_to_dev(*bt, ocfg.steps))
+    if version >= 5:
+        assert np.array_equal(a.get_params(), b.get_params())
+        assert np.array_equal(a.loss(), b.loss())

@@ -1376,6 +1376,8 @@ int trba_model_infer(trba_model *m, const int8_t *img, int batch, int32_t *step_
     Ctx c{m, st, batch, m->P.get(), m->G.get()};
     c.eval = true;
     m->last_B = batch;
+    // the per-tensor max-abs scalars (and BN sums) accumulate into the zeroed arena
+    TRBA_CHECK(cudaMemsetAsync(m->zarena.base, 0, m->zarena.used, st));
     cnn_forward(c, img);
     head_infer(c, step_tokens ? step_tokens : m->step_tokens.get());
     return cuda_status();
@@ -1538,6 +1540,44 @@ int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *
 // Diagnostics: copy an internal fp32 buffer of the last step to the host.
 // Names: feat, dfeat, enc, d_enc, logits, dlogits, ctc_logits, dctc,
 // <conv>.x, <conv>.mean, <conv>.var; n must be the buffer's element count.
+// Optimiser state and running statistics in and out (checkpoints).
+int trba_model_get_moments(trba_model *m, float *m_host, float *v_host, long long n) {
+    if (!m || n != m->n_params) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    if (m_host) TRBA_CHECK(cudaMemcpy(m_host, m->Mm.get(), n * 4, cudaMemcpyDeviceToHost));
+    if (v_host) TRBA_CHECK(cudaMemcpy(v_host, m->Vv.get(), n * 4, cudaMemcpyDeviceToHost));
+    return cuda_status();
+}
+
+int trba_model_set_moments(trba_model *m, const float *m_host, const float *v_host, long long n) {
+    if (!m || n != m->n_params) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    if (m_host) TRBA_CHECK(cudaMemcpy(m->Mm.get(), m_host, n * 4, cudaMemcpyHostToDevice));
+    if (v_host) TRBA_CHECK(cudaMemcpy(m->Vv.get(), v_host, n * 4, cudaMemcpyHostToDevice));
+    return cuda_status();
+}
+
+int trba_model_set_running_stats(trba_model *m, const float *host, long long n) {
+    if (!m || !host || n != trba_model_running_stats_count(m)) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    long long o = 0;
+    for (auto &L : m->convs) {
+        TRBA_CHECK(cudaMemcpy(L.run_mean.get(), host + o, L.cout * 4, cudaMemcpyHostToDevice));
+        TRBA_CHECK(cudaMemcpy(L.run_var.get(), host + o + L.cout, L.cout * 4, cudaMemcpyHostToDevice));
+        o += 2 * L.cout;
+    }
+    return cuda_status();
+}
+
+int trba_model_set_step_count(trba_model *m, long long t) {
+    if (!m || t < 0) return -1;
+    TRBA_CHECK(cudaDeviceSynchronize());
+    const double st[4] = {(double)t, 0.0, 0.0, 0.0};
+    TRBA_CHECK(cudaMemcpy(m->step_state.get(), st, sizeof(st), cudaMemcpyHostToDevice));
+    m->t = t;
+    return cuda_status();
+}
+
 int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long long n) {
     if (!m || !name || !host || n <= 0) return -1;
     const auto &cf = m->cfg;

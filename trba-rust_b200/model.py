@@ -116,6 +116,29 @@ class QatModel:
         self._check(self.L.trba_model_get_running_stats(self.h, _ptr(out), n), "running_stats")
         return out
 
+    def get_moments(self, m_out: np.ndarray, v_out: np.ndarray):
+        """Adam first / second moments of every parameter (manifest order)."""
+        self._check(self.L.trba_model_get_moments(self.h, _ptr(m_out), _ptr(v_out), self.n_params), "get_moments")
+
+    def set_moments(self, m_in: np.ndarray, v_in: np.ndarray):
+        m_in = np.ascontiguousarray(m_in, np.float32)
+        v_in = np.ascontiguousarray(v_in, np.float32)
+        self._check(self.L.trba_model_set_moments(self.h, _ptr(m_in), _ptr(v_in), self.n_params), "set_moments")
+
+    def set_running_stats(self, rs: np.ndarray):
+        rs = np.ascontiguousarray(rs, np.float32)
+        self._check(self.L.trba_model_set_running_stats(self.h, _ptr(rs), rs.size), "set_running_stats")
+
+    def step_count(self) -> int:
+        return int(self.L.trba_model_step_count(self.h))
+
+    def set_step_count(self, t: int):
+        self._check(self.L.trba_model_set_step_count(self.h, int(t)), "set_step_count")
+
+    def conv_channels(self) -> list:
+        """Output channels of every convolution, in the running-statistics order."""
+        return [rows for name, _, rows, cols, kind in self.manifest() if name.endswith(".gamma")]
+
     def debug_tensor(self, name: str, n: int) -> np.ndarray:
         out = np.empty(n, np.float32)
         self._check(self.L.trba_model_debug_tensor(self.h, name.encode(), _ptr(out), n), f"debug_tensor({name})")
