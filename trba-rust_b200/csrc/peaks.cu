@@ -17,22 +17,27 @@ __device__ float g_peak_sink;
 // previous iteration's accumulators, so nothing is loop-invariant and the
 // chains stay independent within an iteration.  No memory traffic.
 __global__ void __launch_bounds__(kPeakThreads) f32_muladd_peak_kernel(float d0, float w0, float neg_zero) {
-    F2 acc[kPeakChains], w[kPeakChains];
+    const f32x2 z = pack2(neg_zero, neg_zero);
+    f32x2 acc[kPeakChains], w[kPeakChains];
 #pragma unroll
     for (int j = 0; j < kPeakChains; ++j) {
-        acc[j] = F2{d0 + (float)threadIdx.x, d0 - (float)(blockIdx.x + j)};
-        w[j] = F2{w0 * (float)(j + 1), -w0 * (float)(j + 1)};
+        acc[j] = pack2(d0 + (float)threadIdx.x, d0 - (float)(blockIdx.x + j));
+        w[j] = pack2(w0 * (float)(j + 1), -w0 * (float)(j + 1));
     }
     for (int it = 0; it < kPeakIters; ++it) {
-        F2 p[kPeakChains];
+        f32x2 p[kPeakChains];
 #pragma unroll
-        for (int j = 0; j < kPeakChains; ++j) p[j] = prod2_rn(acc[(j + kPeakChains - 1) % kPeakChains], w[j], neg_zero);
+        for (int j = 0; j < kPeakChains; ++j) p[j] = prod2_rn(acc[(j + kPeakChains - 1) % kPeakChains], w[j], z);
 #pragma unroll
         for (int j = 0; j < kPeakChains; ++j) acc[j] = add2_rn(acc[j], p[j]);
     }
     float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kPeakChains; ++j) s += acc[j].x + acc[j].y;
+    for (int j = 0; j < kPeakChains; ++j) {
+        float lo, hi;
+        unpack2(acc[j], lo, hi);
+        s += lo + hi;
+    }
     if (s == 1.2345f) g_peak_sink = s;  // keeps the chains live
 }
 

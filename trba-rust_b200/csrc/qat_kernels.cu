@@ -2,6 +2,8 @@
 // Each kernel restates one or more of the reference's host-orchestrated
 // launches (cited per kernel) with the same float expression order, written
 // with explicit round-to-nearest intrinsics so that nothing is contracted.
+#include <algorithm>
+
 #include "qat_kernels.cuh"
 #include "f32x2.cuh"
 
@@ -571,121 +573,94 @@ __global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const f
 // add per term, both rounded — then scaled by w_s, so the result is
 // bit-identical to the reference's per-element gather.
 //
-// Blocking: a thread owns 2 input pixels x 16 input channels (32
-// accumulators).  The int8 weights of the CTA's 16 channels sit in shared
-// memory as f32, [tap][oc][16], read as four broadcast float4 per (tap, oc);
-// each dy value loaded feeds 16 accumulators.  The arithmetic runs on the
-// packed f32x2 pipe: the product of a pair is fma.rn.f32x2(d, w, z) with
-// z = -0.0 passed at run time (d*w + -0 is the correctly rounded product),
-// then add.rn.f32x2 into the accumulators.  A plain mul.rn.f32x2 followed by
-// add.rn.f32x2 is contracted into one fused multiply-add by the code
-// generator, which would change the rounding; the run-time addend keeps the
-// two roundings apart.  A tap outside the output plane contributes d = 0:
-// the accumulator starts at +0 and can never be -0, so adding +-0 leaves it
-// unchanged, exactly as skipping the tap does.
-constexpr int kDgradCi = 16, kDgradPx = 2;
+// A thread owns one input pixel x 16 input channels (8 packed accumulator
+// pairs).  The CTA's weights, (float) of the int8 weights laid out
+// [tap][oc][16 channels] by the re-quantisation (dgrad_weights_index), are
+// copied into shared memory once and read as 64-bit pairs broadcast to the
+// whole warp; each dy value loaded feeds 16 accumulators.  The arithmetic runs
+// on the packed f32x2 pipe (prod2_rn / add2_rn: separately rounded multiply
+// and add).  A tap outside the output plane is skipped, exactly as the
+// reference skips it.
+//
+// Pixel order: with `perm` null thread t takes pixel t (row-major over
+// images).  Otherwise pixels are grouped by the set of taps that are valid
+// for them (`perm` lists the image-local pixels class by class, `cstart` the
+// class offsets), class-major over the batch, so the lanes of a warp share
+// their taps and no lane idles on a tap that only its neighbours need — for
+// stride 2 half of the natural order's lanes would.
+constexpr int kDgradCi = 16, kDgradThreads = 256;
 
-__device__ float g_dgrad_zero[1];  // target of the masked (outside-plane) dy loads
-
-__global__ void __launch_bounds__(256) dgrad_kernel(const float *__restrict__ go, const int8_t *__restrict__ wq,
-                                                    i64 w_ld, const float *__restrict__ w_s, int B, int Cin, int H,
-                                                    int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW,
-                                                    int Ho, int Wo, const int8_t *__restrict__ mask_q,
-                                                    const float *__restrict__ add, float *__restrict__ gi,
-                                                    float neg_zero, int pair_mode) {
-    constexpr int P = kDgradPx, CI = kDgradCi, NP = CI / 2;
-    extern __shared__ float4 wsm4[];  // [taps][Cout][CI / 4] float4
+__global__ void __launch_bounds__(kDgradThreads, 3) dgrad_kernel(
+    const float *__restrict__ go, const float *__restrict__ wT, const float *__restrict__ w_s, int B, int Cin, int H,
+    int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo, const int *__restrict__ perm,
+    const int *__restrict__ cstart, int ncls, const int8_t *__restrict__ mask_q, const float *__restrict__ add,
+    float *__restrict__ gi, float neg_zero) {
+    constexpr int CI = kDgradCi, NP = CI / 2;
+    extern __shared__ float4 wsm4[];  // [taps][Cout][CI / 4]
     const int khw = kH * kW, ci0 = blockIdx.y * CI;
-    for (int e = threadIdx.x; e < khw * Cout * CI; e += blockDim.x) {
-        const int j = e % CI, oc = (e / CI) % Cout, t = e / (CI * Cout);
-        const int ci = ci0 + j;
-        reinterpret_cast<float *>(wsm4)[e] = ci < Cin ? (float)wq[(i64)oc * w_ld + (i64)ci * khw + t] : 0.0f;
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(wT) + (i64)blockIdx.y * khw * Cout * (CI / 4);
+        for (int e = threadIdx.x; e < khw * Cout * (CI / 4); e += kDgradThreads) wsm4[e] = src[e];
     }
     __syncthreads();
     const int hwo = Ho * Wo, hwi = H * W;
-    const i64 npix = (i64)B * hwi;
-    const i64 pair = (i64)blockIdx.x * blockDim.x + threadIdx.x;
-    // pair_mode 0: pixels 2*pair and 2*pair + 1.  pair_mode 1 (stride 2 along
-    // W, W % 4 == 0): pixels iw and iw + 2 of one row, so both have the same
-    // valid taps.
-    i64 pix0;
-    if (pair_mode) {
-        const int half = W >> 1;
-        const i64 row = pair / half;
-        const int k = (int)(pair - row * half);
-        pix0 = row * W + 4 * (k >> 1) + (k & 1);
+    const i64 t = (i64)blockIdx.x * kDgradThreads + threadIdx.x;
+    if (t >= (i64)B * hwi) return;
+    int b, pix;
+    if (perm) {
+        int c = 0;
+        while (c + 1 < ncls && t >= (i64)B * cstart[c + 1]) ++c;
+        const int c0 = cstart[c], csz = cstart[c + 1] - c0;
+        const i64 local = t - (i64)B * c0;
+        b = (int)(local / csz);
+        pix = perm[c0 + (int)(local - (i64)b * csz)];
     } else {
-        pix0 = pair * P;
+        b = (int)(t / hwi);
+        pix = (int)(t - (i64)b * hwi);
     }
-    if (pix0 >= npix) return;
-    const int pstep = pair_mode ? 2 : 1;
-    int pb[P], prem[P], pih[P], piw[P];
-    bool live[P];
+    const int ih = pix / W, iw = pix - ih * W;
+    const f32x2 z = pack2(neg_zero, neg_zero);
+    f32x2 acc[NP];
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-        const i64 px = pix0 + (i64)p * pstep;
-        live[p] = px < npix;
-        const i64 q = live[p] ? px : pix0;
-        pb[p] = (int)(q / hwi);
-        prem[p] = (int)(q - (i64)pb[p] * hwi);
-        pih[p] = prem[p] / W;
-        piw[p] = prem[p] - pih[p] * W;
-    }
-    F2 acc[P][NP];
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-#pragma unroll
-        for (int j = 0; j < NP; ++j) acc[p][j] = F2{0.0f, 0.0f};
+    for (int j = 0; j < NP; ++j) acc[j] = 0ull;  // (+0, +0)
+    const float *gob = go + (i64)b * Cout * hwo;
     for (int kh = 0; kh < kH; ++kh) {
+        const int nh = ih + pH - kh;
+        if (nh < 0 || nh % sH != 0 || nh / sH >= Ho) continue;
         for (int kw = 0; kw < kW; ++kw) {
-            const float *gp[P];
-            i64 gst[P];
-            bool any = false;
-#pragma unroll
-            for (int p = 0; p < P; ++p) {
-                const int nh = pih[p] + pH - kh, nw = piw[p] + pW - kw;
-                const bool ok = live[p] && nh >= 0 && nw >= 0 && nh % sH == 0 && nw % sW == 0 && nh / sH < Ho &&
-                                nw / sW < Wo;
-                gp[p] = ok ? go + (i64)pb[p] * Cout * hwo + (nh / sH) * Wo + nw / sW : g_dgrad_zero;
-                gst[p] = ok ? hwo : 0;
-                any |= ok;
-            }
-            if (!any) continue;
-            const float4 *wt = wsm4 + (i64)(kh * kW + kw) * Cout * (CI / 4);
+            const int nw = iw + pW - kw;
+            if (nw < 0 || nw % sW != 0 || nw / sW >= Wo) continue;
+            const float *gp = gob + (nh / sH) * Wo + nw / sW;
+            const ulonglong2 *wt = reinterpret_cast<const ulonglong2 *>(wsm4) + (i64)(kh * kW + kw) * Cout * (CI / 4);
 #pragma unroll 8
             for (int oc = 0; oc < Cout; ++oc) {
-                F2 wv[NP];
+                f32x2 wv[NP];
 #pragma unroll
                 for (int q = 0; q < CI / 4; ++q) {
-                    const float4 w4 = wt[(CI / 4) * oc + q];
-                    wv[2 * q] = F2{w4.x, w4.y};
-                    wv[2 * q + 1] = F2{w4.z, w4.w};
+                    const ulonglong2 w2 = wt[(CI / 4) * oc + q];
+                    wv[2 * q] = w2.x;
+                    wv[2 * q + 1] = w2.y;
                 }
+                const float d = gp[(i64)oc * hwo];
+                const f32x2 dd = pack2(d, d);
 #pragma unroll
-                for (int p = 0; p < P; ++p) {
-                    const float d = gp[p][oc * gst[p]];
-                    const F2 dd{d, d};
-#pragma unroll
-                    for (int j = 0; j < NP; ++j) acc[p][j] = add2_rn(acc[p][j], prod2_rn(dd, wv[j], neg_zero));
-                }
+                for (int j = 0; j < NP; ++j) acc[j] = add2_rn(acc[j], prod2_rn(dd, wv[j], z));
             }
         }
     }
     const float ws = *w_s;
+    float a[CI];
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-        if (!live[p]) continue;
-        const float *a = &acc[p][0].x;
+    for (int j = 0; j < NP; ++j) unpack2(acc[j], a[2 * j], a[2 * j + 1]);
 #pragma unroll
-        for (int j = 0; j < CI; ++j) {
-            const int ci = ci0 + j;
-            if (ci >= Cin) break;
-            const i64 i = ((i64)pb[p] * Cin + ci) * hwi + prem[p];
-            float v = fmul(a[j], ws);
-            if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
-            if (add) v = fadd(v, add[i]);
-            gi[i] = v;
-        }
+    for (int j = 0; j < CI; ++j) {
+        const int ci = ci0 + j;
+        if (ci >= Cin) break;
+        const i64 i = ((i64)b * Cin + ci) * hwi + pix;
+        float v = fmul(a[j], ws);
+        if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
+        if (add) v = fadd(v, add[i]);
+        gi[i] = v;
     }
 }
 
@@ -854,12 +829,42 @@ void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n,
     TRBA_LAUNCH_CHECK();
 }
 
-void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B, int Cin, int H, int W, int Cout,
-           int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, const int8_t *mask_q, const float *add,
-           float *gi, cudaStream_t st) {
+i64 dgrad_weights_size(int Cin, int Cout, int khw) { return (i64)((Cin + kDgradCi - 1) / kDgradCi) * khw * Cout * kDgradCi; }
+
+void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, std::vector<int> &perm,
+                   std::vector<int> &cstart) {
+    std::vector<std::pair<unsigned long long, int>> key;
+    key.reserve((size_t)H * W);
+    for (int ih = 0; ih < H; ++ih)
+        for (int iw = 0; iw < W; ++iw) {
+            unsigned long long m = 0;
+            for (int a = 0; a < kh; ++a)
+                for (int c = 0; c < kw; ++c) {
+                    const int nh = ih + ph - a, nw = iw + pw - c;
+                    if (nh >= 0 && nw >= 0 && nh % sh == 0 && nw % sw == 0 && nh / sh < Ho && nw / sw < Wo)
+                        m |= 1ull << ((a * kw + c) & 63);
+                }
+            key.push_back({m, ih * W + iw});
+        }
+    std::stable_sort(key.begin(), key.end(), [](const std::pair<unsigned long long, int> &x,
+                                                const std::pair<unsigned long long, int> &y) { return x.first > y.first; });
+    perm.clear();
+    cstart.clear();
+    for (size_t i = 0; i < key.size(); ++i) {
+        if (i == 0 || key[i].first != key[i - 1].first) cstart.push_back((int)i);
+        perm.push_back(key[i].second);
+    }
+    cstart.push_back((int)key.size());
+}
+
+void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, int H, int W, int Cout, int kh, int kw,
+           int sh, int sw, int ph, int pw, int Ho, int Wo, const int *perm, const int *cstart, int ncls,
+           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st) {
     const i64 npix = (i64)B * H * W;
+    if (npix <= 0 || Cin <= 0) return;
     const size_t smem = sizeof(float) * (size_t)kh * kw * Cout * kDgradCi;
     TRBA_REQUIRE(smem <= 200 * 1024, "dgrad: kernel taps x output channels too large for shared memory");
+    TRBA_REQUIRE(kh * kw <= 64, "dgrad: at most 64 kernel taps");
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -867,11 +872,9 @@ void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B,
         TRBA_CHECK(cudaFuncSetAttribute(dgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr[dev] = true;
     }
-    const int pair_mode = (sw == 2 && (W & 3) == 0) ? 1 : 0;
-    const i64 per_cta = 256 * kDgradPx;
-    dim3 grid((unsigned)((npix + per_cta - 1) / per_cta), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
-    dgrad_kernel<<<grid, 256, smem, st>>>(dy, wq, w_ld, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
-                                          mask_q, add, gi, -0.0f, pair_mode);
+    dim3 grid((unsigned)((npix + kDgradThreads - 1) / kDgradThreads), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
+    dgrad_kernel<<<grid, kDgradThreads, smem, st>>>(dy, wT, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
+                                                    perm, cstart, perm ? ncls : 0, mask_q, add, gi, -0.0f);
     TRBA_LAUNCH_CHECK();
 }
 

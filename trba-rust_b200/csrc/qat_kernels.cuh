@@ -3,6 +3,7 @@
 // the device (no host round trip per conv, unlike the reference, which
 // synchronises for every max-abs scale and BN statistic).
 #pragma once
+#include <vector>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -77,9 +78,22 @@ void bn_dx_quant(const float *dy, const float *x, const float *mean, const float
 void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n, float *g, cudaStream_t st);
 // Input gradient (gather over taps and output channels in the reference
 // order) times w_s, then: mask_q ? (mask_q > 0 ? v : 0) : v, then + add.
-void dgrad(const float *dy, const int8_t *wq, int w_ld, const float *w_s, int B, int Cin, int H, int W, int Cout,
-           int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, const int8_t *mask_q, const float *add,
-           float *gi, cudaStream_t st);
+// wT: (float) of the int8 weights at dgrad_weights_index; perm / cstart:
+// the tap-class pixel order of dgrad_classes (device copies), or null for
+// the natural order.
+void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, int H, int W, int Cout, int kh, int kw,
+           int sh, int sw, int ph, int pw, int Ho, int Wo, const int *perm, const int *cstart, int ncls,
+           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st);
+// Floats of the input-gradient weight layout [Cin / 16 blocks][taps][Cout][16].
+i64 dgrad_weights_size(int Cin, int Cout, int khw);
+// Index in that layout of weight (oc, ci, tap).
+__host__ __device__ inline i64 dgrad_weights_index(int oc, int ci, int tap, int Cout, int khw) {
+    return (((i64)(ci >> 4) * khw + tap) * Cout + oc) * 16 + (ci & 15);
+}
+// Pixels of one image grouped by the set of taps valid for them (classes in
+// a fixed order): perm[H*W] image-local pixel indices, cstart[classes + 1].
+void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, std::vector<int> &perm,
+                   std::vector<int> &cstart);
 // Transposed im2col for the correct-mode weight gradient: colT[n*ld + r].
 void im2col_t(const int8_t *in, int8_t *colT, int B, int C, int H, int W, int kh, int kw, int sh, int sw, int ph,
               int pw, int Ho, int Wo, int ld, cudaStream_t st);

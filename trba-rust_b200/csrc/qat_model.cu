@@ -104,6 +104,9 @@ struct ConvL {
     i64 w_off, gamma_off, beta_off;
     // persistent
     Ref<int8_t> wq;          // [a16(cout), kp]
+    Ref<float> wT;           // (float) wq in the input-gradient layout (dgrad_weights_index)
+    std::vector<int> cls_perm, cls_start;  // tap-class pixel order of the input gradient (empty: natural)
+    Ref<int32_t> d_perm, d_cstart;
     Ref<float> ws, wmax;     // device scalars
     Ref<float> run_mean, run_var;
     // forward traces
@@ -211,6 +214,8 @@ struct trba_model {
         float *ws, *wmax;
         float *mean, *var, *run_mean, *run_var;
         int cout, K, kp;
+        float *wT;
+        int khw;
     };
     ConvTab *d_convtab = nullptr;
     long long t = 0;
@@ -413,6 +418,13 @@ __global__ void conv_wmax_kernel(const Seg *segs, const float *P, trba_model::Co
     }
 }
 
+__device__ __forceinline__ int8_t quant_w(float w, float sc) {
+    const float v = (float)__ddiv_rn((double)w, (double)sc);
+    return (int8_t)roundf(fminf(fmaxf(v, -127.0f), 127.0f));
+}
+
+// Writes the padded int8 GEMM operand and, for the input gradient, the same
+// values as f32 in the [Cin / 16][tap][Cout][16] layout.
 __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_model::ConvTab *tab) {
     const Seg s = segs[blockIdx.y];
     const trba_model::ConvTab t = tab[s.aux];
@@ -421,12 +433,17 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
     const i64 total = (i64)a16(t.cout) * t.kp;
     for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (i64)gridDim.x * blockDim.x) {
         const int r = (int)(e / t.kp), c = (int)(e - (i64)r * t.kp);
-        float v = 0.0f;
-        if (r < t.cout && c < t.K) {
-            v = (float)__ddiv_rn((double)P[s.off + (i64)r * t.K + c], (double)sc);
-            v = fminf(fmaxf(v, -127.0f), 127.0f);
-        }
-        t.wq[e] = (int8_t)roundf(v);
+        t.wq[e] = (r < t.cout && c < t.K) ? quant_w(P[s.off + (i64)r * t.K + c], sc) : (int8_t)0;
+    }
+    const int cin = t.K / t.khw;
+    const i64 nT = (i64)((cin + 15) >> 4) * t.khw * t.cout * 16;
+    for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < nT; e += (i64)gridDim.x * blockDim.x) {
+        const int j = (int)(e & 15);
+        const i64 r = e >> 4;
+        const int oc = (int)(r % t.cout);
+        const i64 r2 = r / t.cout;
+        const int tap = (int)(r2 % t.khw), ci = (int)(r2 / t.khw) * 16 + j;
+        t.wT[e] = ci < cin ? (float)quant_w(P[s.off + (i64)oc * t.K + (i64)ci * t.khw + tap], sc) : 0.0f;
     }
 }
 
@@ -494,6 +511,10 @@ void plan(trba_model *m) {
         L.Wo = (W + 2 * p2 - k2) / s2 + 1;
         L.K = cin * k1 * k2;
         L.kp = a16(L.K);
+        // Strided convs: half or more of the natural order's lanes would idle
+        // on every tap of the input gradient; group pixels by their taps.
+        if (s1 > 1 || s2 > 1)
+            qat::dgrad_classes(H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, L.cls_perm, L.cls_start);
         m->convs.push_back(L);
         return (int)m->convs.size() - 1;
     };
@@ -609,6 +630,11 @@ void allocate(trba_model *m) {
         ConvL &L = m->convs[i];
         const i64 rows = L.rows(B), rp = a16l(rows), n = (i64)B * L.cout * L.Ho * L.Wo;
         L.wq = b.p<int8_t>((i64)a16(L.cout) * L.kp);
+        L.wT = b.p<float>(qat::dgrad_weights_size(L.cin, L.cout, L.kh * L.kw));
+        if (!L.cls_perm.empty()) {
+            L.d_perm = b.p<int32_t>((i64)L.cls_perm.size());
+            L.d_cstart = b.p<int32_t>((i64)L.cls_start.size());
+        }
         L.ws = b.p<float>(1);
         L.wmax = b.p<float>(1);
         L.run_mean = b.p<float>(L.cout);
@@ -854,8 +880,10 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
         const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
                              valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
         ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.m->side);
-        qat::dgrad(dy, L.wq.get(), L.kp, L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw,
-                   L.Ho, L.Wo, mask_q, add, gi, c.m->side);
+        qat::dgrad(dy, L.wT.get(), L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
+                   L.Wo, L.cls_perm.empty() ? nullptr : L.d_perm.get(),
+                   L.cls_perm.empty() ? nullptr : L.d_cstart.get(), (int)L.cls_start.size() - 1, mask_q, add, gi,
+                   c.m->side);
     }
     qat::bn_bwd_sums(dy, L.x.get(), L.mean.get(), L.var.get(), B, L.cout, HW, L.bwd_acc.get(), c.st);
     qat::bn_dx_max(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
@@ -1238,7 +1266,13 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     std::vector<trba_model::ConvTab> tab;
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
-                       L.run_var.get(), L.cout, L.K, L.kp});
+                       L.run_var.get(), L.cout, L.K, L.kp, L.wT.get(), L.kh * L.kw});
+        if (!L.cls_perm.empty()) {
+            TRBA_CHECK(cudaMemcpy(L.d_perm.get(), L.cls_perm.data(), sizeof(int) * L.cls_perm.size(),
+                                  cudaMemcpyHostToDevice));
+            TRBA_CHECK(cudaMemcpy(L.d_cstart.get(), L.cls_start.data(), sizeof(int) * L.cls_start.size(),
+                                  cudaMemcpyHostToDevice));
+        }
         fill_f32_kernel<<<1, 128>>>(L.run_var.get(), L.cout, true);
     }
     m->d_convtab = upload_table(tab);
