@@ -583,11 +583,14 @@ __global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const f
 // reference skips it.
 //
 // Pixel order: with `perm` null thread t takes pixel t (row-major over
-// images).  Otherwise pixels are grouped by the set of taps that are valid
-// for them (`perm` lists the image-local pixels class by class, `cstart` the
-// class offsets), class-major over the batch, so the lanes of a warp share
-// their taps and no lane idles on a tap that only its neighbours need — for
-// stride 2 half of the natural order's lanes would.
+// images).  Otherwise pixels are grouped into classes (`perm` lists the
+// image-local pixels class by class, `cstart` the class offsets), class-major
+// over the batch, so the lanes of a warp share their taps and no lane idles
+// on a tap that only its neighbours need.  Strided convs group by the full set
+// of valid taps (in the natural order half or more of the lanes would idle);
+// stride-1 convs group by the valid kernel rows only, which keeps each warp
+// on contiguous row segments of dy (grouping by columns as well breaks rows
+// into short runs and measured slower on 4 x 20 planes).
 constexpr int kDgradCi = 16, kDgradThreads = 256;
 
 __global__ void __launch_bounds__(kDgradThreads, 3) dgrad_kernel(
@@ -831,8 +834,8 @@ void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n,
 
 i64 dgrad_weights_size(int Cin, int Cout, int khw) { return (i64)((Cin + kDgradCi - 1) / kDgradCi) * khw * Cout * kDgradCi; }
 
-void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, std::vector<int> &perm,
-                   std::vector<int> &cstart) {
+void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, bool rows_only,
+                   std::vector<int> &perm, std::vector<int> &cstart) {
     std::vector<std::pair<unsigned long long, int>> key;
     key.reserve((size_t)H * W);
     for (int ih = 0; ih < H; ++ih)
@@ -841,7 +844,8 @@ void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw,
             for (int a = 0; a < kh; ++a)
                 for (int c = 0; c < kw; ++c) {
                     const int nh = ih + ph - a, nw = iw + pw - c;
-                    if (nh >= 0 && nw >= 0 && nh % sh == 0 && nw % sw == 0 && nh / sh < Ho && nw / sw < Wo)
+                    const bool row_ok = nh >= 0 && nh % sh == 0 && nh / sh < Ho;
+                    if (rows_only ? row_ok : row_ok && nw >= 0 && nw % sw == 0 && nw / sw < Wo)
                         m |= 1ull << ((a * kw + c) & 63);
                 }
             key.push_back({m, ih * W + iw});
@@ -855,6 +859,10 @@ void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw,
         perm.push_back(key[i].second);
     }
     cstart.push_back((int)key.size());
+    if (cstart.size() <= 2) {  // one class: the natural order
+        perm.clear();
+        cstart.clear();
+    }
 }
 
 void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, int H, int W, int Cout, int kh, int kw,

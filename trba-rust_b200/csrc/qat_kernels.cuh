@@ -90,10 +90,11 @@ i64 dgrad_weights_size(int Cin, int Cout, int khw);
 __host__ __device__ inline i64 dgrad_weights_index(int oc, int ci, int tap, int Cout, int khw) {
     return (((i64)(ci >> 4) * khw + tap) * Cout + oc) * 16 + (ci & 15);
 }
-// Pixels of one image grouped by the set of taps valid for them (classes in
-// a fixed order): perm[H*W] image-local pixel indices, cstart[classes + 1].
-void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, std::vector<int> &perm,
-                   std::vector<int> &cstart);
+// Pixels of one image grouped by the set of taps valid for them (rows_only:
+// by the valid kernel rows), classes in a fixed order: perm[H*W] image-local
+// pixel indices, cstart[classes + 1]; both empty when there is one class.
+void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int Ho, int Wo, bool rows_only,
+                   std::vector<int> &perm, std::vector<int> &cstart);
 // Transposed im2col for the correct-mode weight gradient: colT[n*ld + r].
 void im2col_t(const int8_t *in, int8_t *colT, int B, int C, int H, int W, int kh, int kw, int sh, int sw, int ph,
               int pw, int Ho, int Wo, int ld, cudaStream_t st);

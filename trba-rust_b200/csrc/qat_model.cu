@@ -511,10 +511,9 @@ void plan(trba_model *m) {
         L.Wo = (W + 2 * p2 - k2) / s2 + 1;
         L.K = cin * k1 * k2;
         L.kp = a16(L.K);
-        // Strided convs: half or more of the natural order's lanes would idle
-        // on every tap of the input gradient; group pixels by their taps.
-        if (s1 > 1 || s2 > 1)
-            qat::dgrad_classes(H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, L.cls_perm, L.cls_start);
+        // Input-gradient pixel order: grouped by valid taps (strided convs) or
+        // by valid kernel rows (stride 1).
+        qat::dgrad_classes(H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, s1 == 1 && s2 == 1, L.cls_perm, L.cls_start);
         m->convs.push_back(L);
         return (int)m->convs.size() - 1;
     };
