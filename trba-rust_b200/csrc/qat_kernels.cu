@@ -704,6 +704,45 @@ __global__ void pool_bwd_mask_kernel(const int8_t *q1, const float *gv, const fl
     }
 }
 
+// Fast path of pool_bwd_mask for H even and W % 4 == 0: one thread per two
+// horizontally adjacent 2x2 windows (4-byte q1 loads, 16-byte dy stores,
+// 32-bit index arithmetic within a plane).  Same first-maximum rule.
+__device__ __forceinline__ void pool_win_bwd(int8_t a, int8_t b, int8_t c, int8_t d, float g, float &oa, float &ob,
+                                             float &oc, float &od) {
+    int win = 0;
+    int8_t m = a;
+    if (b > m) { m = b; win = 1; }
+    if (c > m) { m = c; win = 2; }
+    if (d > m) win = 3;
+    oa = (win == 0 && a > 0) ? g : 0.0f;
+    ob = (win == 1 && b > 0) ? g : 0.0f;
+    oc = (win == 2 && c > 0) ? g : 0.0f;
+    od = (win == 3 && d > 0) ? g : 0.0f;
+}
+
+__global__ void pool_bwd_mask4_kernel(const int8_t *__restrict__ q1, const float *__restrict__ gv,
+                                      const float *__restrict__ s_pool, int H, int W, int BC, float *__restrict__ dy) {
+    const float sp = *s_pool;
+    const int Ho = H >> 1, Wo = W >> 1, W4 = W >> 2, per = Ho * W4;
+    for (int bc = blockIdx.y; bc < BC; bc += gridDim.y) {
+        const int8_t *qp = q1 + (i64)bc * H * W;
+        const float *gp = gv + (i64)bc * Ho * Wo;
+        float *dp = dy + (i64)bc * H * W;
+        for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < per; k += gridDim.x * blockDim.x) {
+            const int oh = k / W4, q = k - oh * W4;
+            const int o = 2 * oh * W + 4 * q;
+            const char4 r0 = *reinterpret_cast<const char4 *>(qp + o);
+            const char4 r1 = *reinterpret_cast<const char4 *>(qp + o + W);
+            const float2 g = *reinterpret_cast<const float2 *>(gp + oh * Wo + 2 * q);
+            float4 t, u;
+            pool_win_bwd(r0.x, r0.y, r1.x, r1.y, fmul(g.x, sp), t.x, t.y, u.x, u.y);
+            pool_win_bwd(r0.z, r0.w, r1.z, r1.w, fmul(g.y, sp), t.z, t.w, u.z, u.w);
+            *reinterpret_cast<float4 *>(dp + o) = t;
+            *reinterpret_cast<float4 *>(dp + o + W) = u;
+        }
+    }
+}
+
 __global__ void features_kernel(const int8_t *q, const float *s, int C, int H, int W, i64 total, float *feat) {
     const float sc = *s;
     GRID_LOOP(i, total) {
@@ -897,7 +936,13 @@ void im2col_t(const int8_t *in, int8_t *colT, int B, int C, int H, int W, int kh
 void pool_bwd_mask(const int8_t *q1, const float *gv, const float *s_pool, int B, int C, int H, int W, float *dy,
                    cudaStream_t st) {
     const i64 n = (i64)B * C * H * W;
-    pool_bwd_mask_kernel<<<grid_for(n), 256, 0, st>>>(q1, gv, s_pool, H, W, n, dy);
+    if ((H & 1) == 0 && (W & 3) == 0 && (i64)H * W < (1ll << 30)) {
+        const int BC = B * C, per = (H >> 1) * (W >> 2);
+        dim3 grid((unsigned)((per + 255) / 256), (unsigned)(BC < 65535 ? BC : 65535));
+        pool_bwd_mask4_kernel<<<grid, 256, 0, st>>>(q1, gv, s_pool, H, W, BC, dy);
+    } else {
+        pool_bwd_mask_kernel<<<grid_for(n), 256, 0, st>>>(q1, gv, s_pool, H, W, n, dy);
+    }
     TRBA_LAUNCH_CHECK();
 }
 

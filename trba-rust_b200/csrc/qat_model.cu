@@ -200,6 +200,7 @@ struct trba_model {
     // optimiser scratch (zeroed per step)
     Ref<double> gsq_total;
     Ref<double> conv_gsq;  // per conv
+    Ref<unsigned> wmax_bits;  // per conv: max |w| as f32 bits (atomicMax), cleared before each re-quantisation
     Ref<float> clip_f, mat_step, conv_step;
     Ref<double> step_state;  // [t, clip active, bc1, bc2]: advanced on the device every step
     // inputs staged for the host-buffer entry point
@@ -399,12 +400,16 @@ __global__ void conv_muon_apply_kernel(const Seg *segs, float *P, const float *G
 }
 
 // Re-quantisation of every conv (src/qnet.rs:601-624): max|w| per conv, then
-// the padded int8 operand with s = max/127 (f64; 1 if 0).
-__global__ void conv_wmax_kernel(const Seg *segs, const float *P, trba_model::ConvTab *tab) {
+// the padded int8 operand with s = max/127 (f64; 1 if 0).  The maximum is
+// reduced by gridDim.x blocks per conv: each block's max (fmaxf, so NaN is
+// ignored as in a sequential fmaxf scan) is merged with an integer atomicMax
+// on the f32 bits, which orders non-negative floats exactly.
+__global__ void conv_wmax_kernel(const Seg *segs, const float *P, unsigned *wmax_bits) {
     __shared__ float sm[32];
-    const Seg s = segs[blockIdx.x];
+    const Seg s = segs[blockIdx.y];
     float m = 0.0f;
-    for (int j = threadIdx.x; j < s.n; j += blockDim.x) m = fmaxf(m, fabsf(P[s.off + j]));
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < s.n; j += gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(P[s.off + j]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
@@ -412,9 +417,7 @@ __global__ void conv_wmax_kernel(const Seg *segs, const float *P, trba_model::Co
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, sm[w]);
-        *tab[s.aux].wmax = t;
-        const double mx = (double)t;
-        *tab[s.aux].ws = (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
+        atomicMax(wmax_bits + blockIdx.y, __float_as_uint(t));
     }
 }
 
@@ -425,11 +428,17 @@ __device__ __forceinline__ int8_t quant_w(float w, float sc) {
 
 // Writes the padded int8 GEMM operand and, for the input gradient, the same
 // values as f32 in the [Cin / 16][tap][Cout][16] layout.
-__global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_model::ConvTab *tab) {
+__global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_model::ConvTab *tab,
+                                  const unsigned *wmax_bits) {
     const Seg s = segs[blockIdx.y];
     const trba_model::ConvTab t = tab[s.aux];
-    const double mx = (double)*t.wmax;
+    const float wmax = __uint_as_float(wmax_bits[blockIdx.y]);
+    const double mx = (double)wmax;
     const float sc = (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        *t.wmax = wmax;
+        *t.ws = sc;
+    }
     const i64 total = (i64)a16(t.cout) * t.kp;
     for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (i64)gridDim.x * blockDim.x) {
         const int r = (int)(e / t.kp), c = (int)(e - (i64)r * t.kp);
@@ -735,6 +744,7 @@ void allocate(trba_model *m) {
     m->step_tokens = b.p<int32_t>((i64)S * B);
     m->gsq_total = b.z<double>(1);
     m->conv_gsq = b.z<double>((i64)m->convs.size());
+    m->wmax_bits = b.p<unsigned>((i64)m->convs.size());
     m->clip_f = b.p<float>(1);
     m->step_state = b.p<double>(4);
     m->mat_step = b.p<float>((i64)m->mat_segs.size());
@@ -1188,15 +1198,17 @@ void optimizer(trba_model *m, cudaStream_t st) {
     conv_gsq_kernel<<<dim3(8, ncv), 256, 0, st>>>(m->d_conv, G, m->conv_gsq.get());
     conv_muon_apply_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, G, m->conv_gsq.get(), m->clip_f.get(), lr, wd,
                                                           (double)cf.muon_cap);
-    conv_wmax_kernel<<<ncv, 256, 0, st>>>(m->d_conv, P, m->d_convtab);
-    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->d_convtab);
+    TRBA_CHECK(cudaMemsetAsync(m->wmax_bits.get(), 0, sizeof(unsigned) * ncv, st));
+    conv_wmax_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->wmax_bits.get());
+    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->d_convtab, m->wmax_bits.get());
     TRBA_LAUNCH_CHECK();
 }
 
 void requantize(trba_model *m, cudaStream_t st) {
     const int ncv = (int)m->conv_segs.size();
-    conv_wmax_kernel<<<ncv, 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab);
-    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab);
+    TRBA_CHECK(cudaMemsetAsync(m->wmax_bits.get(), 0, sizeof(unsigned) * ncv, st));
+    conv_wmax_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->wmax_bits.get());
+    conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab, m->wmax_bits.get());
     TRBA_LAUNCH_CHECK();
 }
 
