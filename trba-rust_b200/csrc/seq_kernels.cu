@@ -24,28 +24,73 @@ __device__ __forceinline__ void gemm_store(const Gemm &g, int m, int n, double a
     *c = v;
 }
 
-// One 64x64 output tile over the K range of split blockIdx.z (f64 accumulation).
+// One 64x64 output tile over the K range of split blockIdx.z (f64
+// accumulation, products of f32 operands are exact in f64).  The operand
+// tiles are converted to f64 once, when staged in shared memory; the loader
+// walks the operand's unit-stride dimension with consecutive threads so the
+// global reads coalesce whichever way the operand is laid out, and the next
+// K tile is read into registers while the current one is multiplied.  Thread
+// (tx, ty) owns rows ty + 16 i and columns tx + 16 j (i, j < 4), so a warp's
+// shared-memory reads are broadcasts (A) or 16 consecutive doubles (B).
+constexpr int kStageElems = TM * TK / 256;
+
+struct TileLoad {
+    float v[kStageElems];
+    __device__ __forceinline__ void load(const float *src, i64 s_row, i64 s_k, int r0, int rows, int k0, int ke) {
+#pragma unroll
+        for (int q = 0; q < kStageElems; ++q) {
+            const int e = threadIdx.x + 256 * q;
+            int rr, kk;
+            if (s_k == 1) {
+                rr = e / TK, kk = e - rr * TK;
+            } else {
+                kk = e / TM, rr = e - kk * TM;
+            }
+            const int r = r0 + rr, k = k0 + kk;
+            v[q] = (r < rows && k < ke) ? src[(i64)r * s_row + (i64)k * s_k] : 0.0f;
+        }
+    }
+    __device__ __forceinline__ void store(double (*dst)[TM + 1], i64 s_k) const {
+#pragma unroll
+        for (int q = 0; q < kStageElems; ++q) {
+            const int e = threadIdx.x + 256 * q;
+            int rr, kk;
+            if (s_k == 1) {
+                rr = e / TK, kk = e - rr * TK;
+            } else {
+                kk = e / TM, rr = e - kk * TM;
+            }
+            dst[kk][rr] = (double)v[q];
+        }
+    }
+};
+
 __global__ void __launch_bounds__(256) sgemm_kernel(Gemm g, int kchunk) {
-    __shared__ float sa[TK][TM + 1], sb[TK][TN + 1];
+    __shared__ double sa[TK][TM + 1], sb[TK][TN + 1];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
     const int kb = blockIdx.z * kchunk, ke = min(g.K, kb + kchunk);
     double acc[4][4] = {};
+    TileLoad la, lb;
+    if (kb < ke) {
+        la.load(g.A, g.sam, g.sak, m0, g.M, kb, ke);
+        lb.load(g.B, g.sbn, g.sbk, n0, g.N, kb, ke);
+    }
     for (int k0 = kb; k0 < ke; k0 += TK) {
-        for (int e = threadIdx.x; e < TM * TK; e += 256) {
-            const int kk = e / TM, mm = e - kk * TM;  // consecutive threads walk m / n
-            const int m = m0 + mm, k = k0 + kk, n = n0 + mm;
-            sa[kk][mm] = (m < g.M && k < ke) ? g.A[(i64)m * g.sam + (i64)k * g.sak] : 0.0f;
-            sb[kk][mm] = (n < g.N && k < ke) ? g.B[(i64)k * g.sbk + (i64)n * g.sbn] : 0.0f;
-        }
+        la.store(sa, g.sak);
+        lb.store(sb, g.sbk);
         __syncthreads();
+        if (k0 + TK < ke) {
+            la.load(g.A, g.sam, g.sak, m0, g.M, k0 + TK, ke);
+            lb.load(g.B, g.sbn, g.sbk, n0, g.N, k0 + TK, ke);
+        }
 #pragma unroll
         for (int kk = 0; kk < TK; ++kk) {
             double a[4], b[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = (double)sa[kk][ty * 4 + i];
+            for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty + 16 * i];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = (double)sb[kk][tx * 4 + j];
+            for (int j = 0; j < 4; ++j) b[j] = sb[kk][tx + 16 * j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -55,11 +100,42 @@ __global__ void __launch_bounds__(256) sgemm_kernel(Gemm g, int kchunk) {
     }
     for (int i = 0; i < 4; ++i)
         for (int j = 0; j < 4; ++j) {
-            const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+            const int m = m0 + ty + 16 * i, n = n0 + tx + 16 * j;
             if (m >= g.M || n >= g.N) continue;
             if (gridDim.z == 1) gemm_store(g, m, n, acc[i][j]);
             else g.ws[((i64)blockIdx.z * g.M + m) * g.N + n] = acc[i][j];
         }
+}
+
+// Single-row products (M == 1: column sums, the score-vector gradient):
+// lane = output column, the CTA's 8 warps interleave the K range of the
+// split with 4 independent f64 partial sums each, combined in a fixed order.
+__global__ void __launch_bounds__(256) gemv_kernel(Gemm g, int kchunk) {
+    __shared__ double red[8][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int n = blockIdx.x * 32 + lane;
+    const int kb = blockIdx.y * kchunk, ke = min(g.K, kb + kchunk);
+    double p0 = 0.0, p1 = 0.0, p2 = 0.0, p3 = 0.0;
+    if (n < g.N) {
+        const float *bcol = g.B + (i64)n * g.sbn;
+        int k = kb + w;
+        for (; k + 24 < ke; k += 32) {
+            p0 = fma((double)g.A[(i64)k * g.sak], (double)bcol[(i64)k * g.sbk], p0);
+            p1 = fma((double)g.A[(i64)(k + 8) * g.sak], (double)bcol[(i64)(k + 8) * g.sbk], p1);
+            p2 = fma((double)g.A[(i64)(k + 16) * g.sak], (double)bcol[(i64)(k + 16) * g.sbk], p2);
+            p3 = fma((double)g.A[(i64)(k + 24) * g.sak], (double)bcol[(i64)(k + 24) * g.sbk], p3);
+        }
+        for (; k < ke; k += 8) p0 = fma((double)g.A[(i64)k * g.sak], (double)bcol[(i64)k * g.sbk], p0);
+    }
+    red[w][lane] = (p0 + p1) + (p2 + p3);
+    __syncthreads();
+    if (w == 0 && n < g.N) {
+        double t = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t += red[i][lane];
+        if (gridDim.y == 1) gemm_store(g, 0, n, t);
+        else g.ws[(i64)blockIdx.y * g.N + n] = t;
+    }
 }
 
 // Sums the split partials in split order and stores.
@@ -664,11 +740,32 @@ __global__ void scale_by_kernel(float *x, const float *s, i64 n) {
 
 void sgemm(const Gemm &g, cudaStream_t st) {
     if (g.M <= 0 || g.N <= 0) return;
+    if (g.M == 1) {
+        const int nb = (g.N + 31) / 32;
+        int splits = 1;
+        if (g.ws && g.K > 256) {
+            const int want = (4 * sm_count() + nb - 1) / nb;
+            const int maxs = (g.K + 255) / 256;
+            splits = want < maxs ? want : maxs;
+            if ((i64)splits * g.N > g.ws_elems) splits = (int)(g.ws_elems / g.N);
+            if (splits < 1) splits = 1;
+        }
+        const int kchunk = (g.K + splits - 1) / splits;
+        splits = (g.K + kchunk - 1) / kchunk;
+        if (splits < 1) splits = 1;
+        gemv_kernel<<<dim3(nb, splits), 256, 0, st>>>(g, kchunk > 0 ? kchunk : 1);
+        TRBA_LAUNCH_CHECK();
+        if (splits > 1) {
+            sgemm_finish_kernel<<<grid_for((i64)g.N), 256, 0, st>>>(g, splits);
+            TRBA_LAUNCH_CHECK();
+        }
+        return;
+    }
     const int mt = (g.M + TM - 1) / TM, nt = (g.N + TN - 1) / TN;
-    // Split K until the grid covers two waves of SMs (chunks of >= 64).
+    // Split K until the grid covers four CTAs per SM (chunks of >= 64).
     int splits = 1;
     if (g.ws && g.K > 128) {
-        const int want = (2 * sm_count() + mt * nt - 1) / (mt * nt);
+        const int want = (4 * sm_count() + mt * nt - 1) / (mt * nt);
         const int maxs = (g.K + 63) / 64;
         splits = want < maxs ? want : maxs;
         if ((i64)splits * g.M * g.N > g.ws_elems) splits = (int)(g.ws_elems / ((i64)g.M * g.N));
