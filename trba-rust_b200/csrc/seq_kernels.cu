@@ -149,56 +149,82 @@ __global__ void sgemm_finish_kernel(Gemm g, int splits) {
 }
 
 // -------------------------------------------------------------- LSTM --
-// One CTA per sample: the recurrent weights (4H x H) sit in shared memory,
-// the 4H gate outputs of a step are spread over the threads, and the H-long
-// (forward) or 4H-long (backward) dot products run as independent partial
-// sums (two per thread forward; four lanes per output backward) so the f64
-// multiply-add chains stay short.
+// kLstmS samples per CTA share the recurrent weights (4H x H, f32) in shared
+// memory; the recurrent state of every sample is kept there as f64, so each
+// f64 multiply-add converts only the weight, once for all kLstmS samples.
+// The H-long (forward) or 4H-long (backward) dot products run as independent
+// partial sums (even / odd k forward; four lanes per output backward) so the
+// f64 chains stay short, and the samples give each thread kLstmS
+// independent chains.  Samples never interact inside a recurrence.
+constexpr int kLstmS = 4;
 
 __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh,
                                                        const float *w_hh, int B, int T, int H, int rev,
                                                        float *gates, float *c_tr, float *h_prev_tr, float *cat,
                                                        int dir) {
-    extern __shared__ float sm[];
+    constexpr int S = kLstmS;
+    extern __shared__ double smd[];
     const int G4 = 4 * H;
-    float *wT = sm;           // [H][4H]: wT[k*4H + o] = w_hh[o*H + k]
-    float *hb = wT + H * G4;  // [H]
-    float *cb = hb + H;       // [H]
-    float *gb = cb + H;       // [4H]
-    const int b = blockIdx.x;
+    double *hb = smd;                                    // [S][H] h of the previous step
+    float *wT = reinterpret_cast<float *>(hb + S * H);   // [H][4H]: wT[k*4H + o] = w_hh[o*H + k]
+    float *cb = wT + H * G4;                             // [S][H]
+    float *gb = cb + S * H;                              // [S][4H]
+    const int b0 = blockIdx.x * S;
+    const int ns = min(S, B - b0);
     for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) {
         const int o = e / H, k = e - o * H;
         wT[k * G4 + o] = w_hh[e];
     }
-    for (int e = threadIdx.x; e < H; e += blockDim.x) hb[e] = cb[e] = 0.0f;
+    for (int e = threadIdx.x; e < S * H; e += blockDim.x) {
+        hb[e] = 0.0;
+        cb[e] = 0.0f;
+    }
     __syncthreads();
-    for (int s = 0; s < T; ++s) {
-        const int tt = rev ? T - 1 - s : s;
-        const i64 r = (i64)b * T + tt;
+    for (int st = 0; st < T; ++st) {
+        const int tt = rev ? T - 1 - st : st;
         for (int o = threadIdx.x; o < G4; o += blockDim.x) {
-            double a0 = 0.0, a1 = 0.0;
+            double a0[S], a1[S];
+#pragma unroll
+            for (int q = 0; q < S; ++q) a0[q] = a1[q] = 0.0;
             int k = 0;
             for (; k + 1 < H; k += 2) {
-                a0 = fma((double)hb[k], (double)wT[k * G4 + o], a0);
-                a1 = fma((double)hb[k + 1], (double)wT[(k + 1) * G4 + o], a1);
+                const double w0 = (double)wT[k * G4 + o], w1 = (double)wT[(k + 1) * G4 + o];
+#pragma unroll
+                for (int q = 0; q < S; ++q) {
+                    a0[q] = fma(hb[q * H + k], w0, a0[q]);
+                    a1[q] = fma(hb[q * H + k + 1], w1, a1[q]);
+                }
             }
-            if (k < H) a0 = fma((double)hb[k], (double)wT[k * G4 + o], a0);
-            gb[o] = fadd(fadd(fadd(b_ih[o], b_hh[o]), xg[r * G4 + o]), (float)(a0 + a1));
+            if (k < H) {
+                const double w0 = (double)wT[k * G4 + o];
+#pragma unroll
+                for (int q = 0; q < S; ++q) a0[q] = fma(hb[q * H + k], w0, a0[q]);
+            }
+            const float bias = fadd(b_ih[o], b_hh[o]);
+#pragma unroll
+            for (int q = 0; q < S; ++q) {
+                if (q >= ns) break;
+                const i64 r = (i64)(b0 + q) * T + tt;
+                gb[q * G4 + o] = fadd(fadd(bias, xg[r * G4 + o]), (float)(a0[q] + a1[q]));
+            }
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
-            const float ig = sigm(gb[i]), fg = sigm(gb[H + i]), cg = cr_tanhf(gb[2 * H + i]), og = sigm(gb[3 * H + i]);
-            const float cn = fadd(fmul(fg, cb[i]), fmul(ig, cg));
+        for (int e = threadIdx.x; e < ns * H; e += blockDim.x) {
+            const int q = e / H, i = e - q * H;
+            const i64 r = (i64)(b0 + q) * T + tt;
+            const float *g = gb + q * G4;
+            const float ig = sigm(g[i]), fg = sigm(g[H + i]), cg = cr_tanhf(g[2 * H + i]), og = sigm(g[3 * H + i]);
+            const float cn = fadd(fmul(fg, cb[e]), fmul(ig, cg));
             const float hn = fmul(og, cr_tanhf(cn));
             gates[r * G4 + i] = ig;
             gates[r * G4 + H + i] = fg;
             gates[r * G4 + 2 * H + i] = cg;
             gates[r * G4 + 3 * H + i] = og;
             c_tr[r * H + i] = cn;
-            h_prev_tr[r * H + i] = hb[i];
+            h_prev_tr[r * H + i] = (float)hb[e];
             cat[r * 2 * H + dir * H + i] = hn;
-            cb[i] = cn;
-            hb[i] = hn;  // only this thread touches hb[i] in this phase
+            cb[e] = cn;
+            hb[e] = (double)hn;  // only this thread touches hb[e] in this phase
         }
         __syncthreads();
     }
@@ -207,44 +233,67 @@ __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const fl
 __global__ void __launch_bounds__(256) lstm_bwd_kernel(const float *dcat, const float *gates, const float *c_tr,
                                                        const float *w_hh, int B, int T, int H, int rev, int dir,
                                                        float *dgates) {
-    extern __shared__ float sm[];
+    constexpr int S = kLstmS;
+    extern __shared__ double smd[];
     const int G4 = 4 * H;
-    float *w = sm;            // [4H][H] natural layout
-    float *dhn = w + G4 * H;  // [H]
-    float *dcn = dhn + H;     // [H]
-    float *dg = dcn + H;      // [4H]
-    const int b = blockIdx.x;
+    double *dgd = smd;                                  // [S][4H] gate gradients of the step, f64
+    float *w = reinterpret_cast<float *>(dgd + S * G4);  // [4H][H] natural layout
+    float *dhn = w + G4 * H;                            // [S][H]
+    float *dcn = dhn + S * H;                           // [S][H]
+    const int b0 = blockIdx.x * S;
+    const int ns = min(S, B - b0);
     for (int e = threadIdx.x; e < G4 * H; e += blockDim.x) w[e] = w_hh[e];
-    for (int e = threadIdx.x; e < H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
+    for (int e = threadIdx.x; e < S * H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
+    for (int e = threadIdx.x; e < S * G4; e += blockDim.x) dgd[e] = 0.0;
     __syncthreads();
-    for (int s = T - 1; s >= 0; --s) {
-        const int tt = rev ? T - 1 - s : s;
+    for (int st = T - 1; st >= 0; --st) {
+        const int tt = rev ? T - 1 - st : st;
         const int tp = rev ? tt + 1 : tt - 1;  // time position of the previous slot
-        const i64 r = (i64)b * T + tt;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        for (int e = threadIdx.x; e < ns * H; e += blockDim.x) {
+            const int q = e / H, i = e - q * H;
+            const int b = b0 + q;
+            const i64 r = (i64)b * T + tt;
             const float ig = gates[r * G4 + i], fg = gates[r * G4 + H + i], cg = gates[r * G4 + 2 * H + i],
                         og = gates[r * G4 + 3 * H + i];
             const float tc = cr_tanhf(c_tr[r * H + i]);
-            const float cp = s > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
-            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[i]);
-            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
-            dg[i] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
-            dg[H + i] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
-            dg[2 * H + i] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
-            dg[3 * H + i] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
-            dcn[i] = dc;
+            const float cp = st > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
+            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[e]);
+            const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[e], fg));
+            const float d0 = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            const float d1 = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            const float d2 = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            const float d3 = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            dgates[r * G4 + i] = d0;
+            dgates[r * G4 + H + i] = d1;
+            dgates[r * G4 + 2 * H + i] = d2;
+            dgates[r * G4 + 3 * H + i] = d3;
+            double *dq = dgd + q * G4;
+            dq[i] = (double)d0;
+            dq[H + i] = (double)d1;
+            dq[2 * H + i] = (double)d2;
+            dq[3 * H + i] = (double)d3;
+            dcn[e] = dc;
         }
         __syncthreads();
-        for (int o = threadIdx.x; o < G4; o += blockDim.x) dgates[r * G4 + o] = dg[o];
         // dh_prev[k] = sum_o dg[o] w[o, k]: four consecutive lanes per k, each
         // over o = q, q + 4, ..., combined with two shuffles
         for (int e = threadIdx.x; e < 4 * H; e += blockDim.x) {
-            const int k = e >> 2, q = e & 3;
-            double acc = 0.0;
-            for (int o = q; o < G4; o += 4) acc = fma((double)dg[o], (double)w[o * H + k], acc);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (q == 0) dhn[k] = (float)acc;
+            const int k = e >> 2, l = e & 3;
+            double acc[S];
+#pragma unroll
+            for (int q = 0; q < S; ++q) acc[q] = 0.0;
+            for (int o = l; o < G4; o += 4) {
+                const double wv = (double)w[o * H + k];
+#pragma unroll
+                for (int q = 0; q < S; ++q) acc[q] = fma(dgd[q * G4 + o], wv, acc[q]);
+            }
+#pragma unroll
+            for (int q = 0; q < S; ++q) {
+                double v = acc[q];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if (l == 0 && q < ns) dhn[q * H + k] = (float)v;
+            }
         }
         __syncthreads();
     }
@@ -801,18 +850,21 @@ static void set_smem(const void *fn, size_t bytes) {
 
 void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H, int rev,
               float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st) {
-    const size_t smem = sizeof(float) * ((size_t)4 * H * H + 2 * H + 4 * H);
+    const size_t smem = sizeof(double) * kLstmS * H + sizeof(float) * ((size_t)4 * H * H + kLstmS * H + kLstmS * 4 * H);
+    TRBA_REQUIRE(smem <= 200 * 1024, "lstm_fwd: hidden size too large for the shared-memory recurrence");
     set_smem((const void *)lstm_fwd_kernel, smem);
-    lstm_fwd_kernel<<<B, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev, cat, dir);
+    lstm_fwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev,
+                                                                  cat, dir);
     TRBA_LAUNCH_CHECK();
 }
 
 void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H, int rev,
               int dir, float *dgates, cudaStream_t st) {
     TRBA_REQUIRE(H % 8 == 0, "lstm_bwd: hidden size must be a multiple of 8 (4*hidden fills whole warps)");
-    const size_t smem = sizeof(float) * ((size_t)4 * H * H + 2 * H + 4 * H);
+    const size_t smem = sizeof(double) * kLstmS * 4 * H + sizeof(float) * ((size_t)4 * H * H + 2 * kLstmS * H);
+    TRBA_REQUIRE(smem <= 200 * 1024, "lstm_bwd: hidden size too large for the shared-memory recurrence");
     set_smem((const void *)lstm_bwd_kernel, smem);
-    lstm_bwd_kernel<<<B, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
+    lstm_bwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
     TRBA_LAUNCH_CHECK();
 }
 
