@@ -156,7 +156,7 @@ __global__ void sgemm_finish_kernel(Gemm g, int splits) {
 // partial sums (even / odd k forward; four lanes per output backward) so the
 // f64 chains stay short, and the samples give each thread kLstmS
 // independent chains.  Samples never interact inside a recurrence.
-constexpr int kLstmS = 4;
+constexpr int kLstmS = 4, kLstmRows = 2;
 
 __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh,
                                                        const float *w_hh, int B, int T, int H, int rev,
@@ -180,9 +180,34 @@ __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const fl
         cb[e] = 0.0f;
     }
     __syncthreads();
+    // The input projections of step st + 1 are read while step st runs (they
+    // do not depend on the recurrence), so the global-memory latency stays
+    // off the per-step critical path.  Threads own gate rows o = threadIdx.x
+    // + k * blockDim.x; kLstmRows bounds k (4H <= kLstmRows * blockDim).
+    float xn[kLstmRows][S];
+    auto load_xg = [&](int step) {
+        const int tq = rev ? T - 1 - step : step;
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j) {
+            const int o = threadIdx.x + j * blockDim.x;
+#pragma unroll
+            for (int q = 0; q < S; ++q)
+                xn[j][q] = (o < G4 && q < ns) ? xg[((i64)(b0 + q) * T + tq) * G4 + o] : 0.0f;
+        }
+    };
+    load_xg(0);
     for (int st = 0; st < T; ++st) {
         const int tt = rev ? T - 1 - st : st;
-        for (int o = threadIdx.x; o < G4; o += blockDim.x) {
+        float xc[kLstmRows][S];
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j)
+#pragma unroll
+            for (int q = 0; q < S; ++q) xc[j][q] = xn[j][q];
+        if (st + 1 < T) load_xg(st + 1);
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j) {
+            const int o = threadIdx.x + j * blockDim.x;
+            if (o >= G4) break;
             double a0[S], a1[S];
 #pragma unroll
             for (int q = 0; q < S; ++q) a0[q] = a1[q] = 0.0;
@@ -204,8 +229,7 @@ __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const fl
 #pragma unroll
             for (int q = 0; q < S; ++q) {
                 if (q >= ns) break;
-                const i64 r = (i64)(b0 + q) * T + tt;
-                gb[q * G4 + o] = fadd(fadd(bias, xg[r * G4 + o]), (float)(a0[q] + a1[q]));
+                gb[q * G4 + o] = fadd(fadd(bias, xc[j][q]), (float)(a0[q] + a1[q]));
             }
         }
         __syncthreads();
@@ -246,18 +270,47 @@ __global__ void __launch_bounds__(256) lstm_bwd_kernel(const float *dcat, const 
     for (int e = threadIdx.x; e < S * H; e += blockDim.x) dhn[e] = dcn[e] = 0.0f;
     for (int e = threadIdx.x; e < S * G4; e += blockDim.x) dgd[e] = 0.0;
     __syncthreads();
+    // The step's saved gates, cell states and output gradient do not depend
+    // on the recurrence: those of step st - 1 are read while step st runs.
+    float pf[kLstmRows][7];
+    auto load_step = [&](int step) {
+        const int tq = rev ? T - 1 - step : step;
+        const int tpq = rev ? tq + 1 : tq - 1;
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j) {
+            const int e = threadIdx.x + j * blockDim.x;
+            if (e >= ns * H) break;
+            const int q = e / H, i = e - q * H;
+            const i64 r = (i64)(b0 + q) * T + tq;
+            pf[j][0] = gates[r * G4 + i];
+            pf[j][1] = gates[r * G4 + H + i];
+            pf[j][2] = gates[r * G4 + 2 * H + i];
+            pf[j][3] = gates[r * G4 + 3 * H + i];
+            pf[j][4] = c_tr[r * H + i];
+            pf[j][5] = step > 0 ? c_tr[((i64)(b0 + q) * T + tpq) * H + i] : 0.0f;
+            pf[j][6] = dcat[r * 2 * H + dir * H + i];
+        }
+    };
+    load_step(T - 1);
     for (int st = T - 1; st >= 0; --st) {
         const int tt = rev ? T - 1 - st : st;
-        const int tp = rev ? tt + 1 : tt - 1;  // time position of the previous slot
-        for (int e = threadIdx.x; e < ns * H; e += blockDim.x) {
+        float cur[kLstmRows][7];
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j)
+#pragma unroll
+            for (int u = 0; u < 7; ++u) cur[j][u] = pf[j][u];
+        if (st > 0) load_step(st - 1);
+#pragma unroll
+        for (int j = 0; j < kLstmRows; ++j) {
+            const int e = threadIdx.x + j * blockDim.x;
+            if (e >= ns * H) break;
             const int q = e / H, i = e - q * H;
             const int b = b0 + q;
             const i64 r = (i64)b * T + tt;
-            const float ig = gates[r * G4 + i], fg = gates[r * G4 + H + i], cg = gates[r * G4 + 2 * H + i],
-                        og = gates[r * G4 + 3 * H + i];
-            const float tc = cr_tanhf(c_tr[r * H + i]);
-            const float cp = st > 0 ? c_tr[((i64)b * T + tp) * H + i] : 0.0f;
-            const float dh = fadd(dcat[r * 2 * H + dir * H + i], dhn[e]);
+            const float ig = cur[j][0], fg = cur[j][1], cg = cur[j][2], og = cur[j][3];
+            const float tc = cr_tanhf(cur[j][4]);
+            const float cp = cur[j][5];
+            const float dh = fadd(cur[j][6], dhn[e]);
             const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[e], fg));
             const float d0 = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
             const float d1 = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
@@ -306,7 +359,8 @@ __global__ void __launch_bounds__(256) lstm_bwd_kernel(const float *dcat, const 
 // threads, and the T- or H-long reductions that feed a single value run
 // across a warp.  Dot products accumulate in f64 and round once; the
 // element-wise expressions keep the reference's f32 order.
-constexpr int kAttnS = 4;
+constexpr int kAttnS = 4, kAttnThreads = 512;
+constexpr size_t kAttnMaxSmem = 227 * 1024;
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -337,7 +391,7 @@ __device__ __forceinline__ double dot2_d(const float *x, const float *w, int str
 // maximum) of the generator logits of step s-1, sos at step 0; only the
 // per-step argmax tokens are stored.
 template <bool DECODE>
-__global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
+__global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int stage) {
     extern __shared__ float sm[];
     const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
     float *wihT = sm;             // [H][4H], context columns of w_ih, transposed
@@ -350,6 +404,10 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
     float *e = tn + S * T * H;    // [S][T]
     float *al = e + S * T;        // [S][T]
     int *tok = reinterpret_cast<int *>(al + S * T);  // [S]
+    float *logit = reinterpret_cast<float *>(tok + S);  // [S][V] (DECODE)
+    // stage != 0: the CTA's encoder projections and features [S][T][H] are
+    // copied into shared memory once (they are read at every step).
+    float *sph = logit + (DECODE ? S * V : 0), *sbh = sph + S * T * H;
     const int b0 = blockIdx.x * S;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
@@ -361,7 +419,14 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
         const int k = i / H, j = i - k * H;
         h2hT[j * H + k] = a.h2h_w[i];
     }
-    float *logit = reinterpret_cast<float *>(tok + S);  // [S][V] (DECODE)
+    if (stage) {
+        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+            const int sl = i / (T * H), r = i - sl * T * H;
+            const i64 g = (i64)min(b0 + sl, a.B - 1) * T * H + r;
+            sph[i] = a.proj_h[g];
+            sbh[i] = a.bh[g];
+        }
+    }
     for (int i = threadIdx.x; i < S * H; i += blockDim.x) h[i] = c[i] = 0.0f;
     if (DECODE && threadIdx.x < S) tok[threadIdx.x] = a.sos;
     __syncthreads();
@@ -380,7 +445,8 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
         for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
             const int sl = i / (T * H), r = i - sl * T * H, k = r % H;
             const int b = b0 + sl;
-            const float v = cr_tanhf(fadd(a.proj_h[((i64)min(b, a.B - 1) * T) * H + r], phh[sl * H + k]));
+            const float ph = stage ? sph[i] : a.proj_h[((i64)min(b, a.B - 1) * T) * H + r];
+            const float v = cr_tanhf(fadd(ph, phh[sl * H + k]));
             tn[i] = v;
             if (!DECODE && b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T) * H + r] = v;
         }
@@ -418,7 +484,12 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
             const int sl = i / H, k = i - sl * H;
             const int b = min(b0 + sl, a.B - 1);
             double acc = 0.0;
-            for (int t = 0; t < T; ++t) acc = fma((double)al[sl * T + t], (double)a.bh[((i64)b * T + t) * H + k], acc);
+            if (stage) {
+                for (int t = 0; t < T; ++t) acc = fma((double)al[sl * T + t], (double)sbh[(sl * T + t) * H + k], acc);
+            } else {
+                for (int t = 0; t < T; ++t)
+                    acc = fma((double)al[sl * T + t], (double)a.bh[((i64)b * T + t) * H + k], acc);
+            }
             ctx[i] = (float)acc;
         }
         __syncthreads();
@@ -497,7 +568,7 @@ __global__ void __launch_bounds__(256) attn_fwd_kernel(AttnFwd a) {
     }
 }
 
-__global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
+__global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwd a, int stage) {
     extern __shared__ float sm[];
     const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
     float *wc = sm;                 // [4H][H] context columns of w_ih
@@ -508,6 +579,8 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
     float *dg = dphh + S * H;       // [S][4H]
     float *da = dg + S * G4, *de = da + S * T, *dot = de + S * T;  // [S][T], [S][T], [S]
     float *acc_bh = dot + S, *acc_ph = acc_bh + S * T * H;        // [S][T][H]
+    float *als = acc_ph + S * T * H;                              // [S][T] alpha of the step
+    float *sbh = als + S * T;                                     // [S][T][H] when stage != 0
     const int b0 = blockIdx.x * S;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
@@ -517,9 +590,19 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
     }
     for (int i = threadIdx.x; i < H * H; i += blockDim.x) h2h[i] = a.h2h_w[i];
     for (int i = threadIdx.x; i < S * H; i += blockDim.x) dhn[i] = dcn[i] = 0.0f;
-    for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) acc_bh[i] = acc_ph[i] = 0.0f;
+    for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+        acc_bh[i] = acc_ph[i] = 0.0f;
+        if (stage) {
+            const int sl = i / (T * H), r = i - sl * T * H;
+            sbh[i] = a.bh[(i64)min(b0 + sl, a.B - 1) * T * H + r];
+        }
+    }
     __syncthreads();
     for (int st = a.steps - 1; st >= 0; --st) {
+        for (int i = threadIdx.x; i < S * T; i += blockDim.x) {
+            const int sl = i / T, t = i - sl * T;
+            als[i] = a.alpha[((i64)st * a.B + min(b0 + sl, a.B - 1)) * T + t];
+        }
         // LSTM cell backward
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
             const int sl = i / H, k = i - sl * H, b = min(b0 + sl, a.B - 1);
@@ -562,22 +645,20 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
         for (int p = warp; p < S * T; p += nwarps) {
             const int sl = p / T, t = p - sl * T, b = min(b0 + sl, a.B - 1);
             double acc = 0.0;
-            for (int k = lane; k < H; k += 32)
-                acc = fma((double)dctx[sl * H + k], (double)a.bh[((i64)b * T + t) * H + k], acc);
+            const float *bht = stage ? sbh + (sl * T + t) * H : a.bh + ((i64)b * T + t) * H;
+            for (int k = lane; k < H; k += 32) acc = fma((double)dctx[sl * H + k], (double)bht[k], acc);
             acc = warp_sum_d(acc);
             if (lane == 0) da[p] = (float)acc;
         }
         for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
             const int sl = i / (T * H), r = i - sl * T * H, t = r / H, k = r - t * H;
-            const int b = min(b0 + sl, a.B - 1);
-            const float at = a.alpha[((i64)st * a.B + b) * T + t];
-            acc_bh[i] = fadd(acc_bh[i], fmul(at, dctx[sl * H + k]));
+            acc_bh[i] = fadd(acc_bh[i], fmul(als[sl * T + t], dctx[sl * H + k]));
         }
         __syncthreads();
         // softmax backward, one warp per sample: de = alpha (d alpha - alpha . d alpha)
         for (int sl = warp; sl < S; sl += nwarps) {
             const int b = min(b0 + sl, a.B - 1);
-            const float *al = a.alpha + ((i64)st * a.B + b) * T;
+            const float *al = als + sl * T;
             double acc = 0.0;
             for (int t = lane; t < T; t += 32) acc = fma((double)al[t], (double)da[sl * T + t], acc);
             const float dt = (float)warp_sum_d(acc);
@@ -588,22 +669,20 @@ __global__ void __launch_bounds__(256) attn_bwd_kernel(AttnBwd a) {
             }
         }
         __syncthreads();
-        // through tanh: acc_ph += de * score_w * (1 - tn^2); d proj_hh = sum over t
-        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
-            const int sl = i / (T * H), r = i - sl * T * H, t = r / H, k = r - t * H;
-            const float d = de[sl * T + t];
-            if (d == 0.0f) continue;
-            const int b = min(b0 + sl, a.B - 1);
-            const float v = a.tanh_tr[(((i64)st * a.B + b) * T) * H + r];
-            acc_ph[i] = fadd(acc_ph[i], fmul(fmul(d, a.score_w[k]), fsub(1.0f, fmul(v, v))));
-        }
+        // through tanh, one (sample, k) per thread over t: acc_ph += de *
+        // score_w * (1 - tn^2) (a zero de leaves acc_ph as it is), d proj_hh
+        // = the f64 sum of the same terms over t
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
             const int sl = i / H, k = i - sl * H, b = min(b0 + sl, a.B - 1);
             const float *tn = a.tanh_tr + (((i64)st * a.B + b) * T) * H;
+            const float sw = a.score_w[k];
             double sum = 0.0;
             for (int t = 0; t < T; ++t) {
                 const float v = tn[t * H + k];
-                sum += (double)fmul(fmul(de[sl * T + t], a.score_w[k]), fsub(1.0f, fmul(v, v)));
+                const float d = de[sl * T + t];
+                const float term = fmul(fmul(d, sw), fsub(1.0f, fmul(v, v)));
+                if (d != 0.0f) acc_ph[(sl * T + t) * H + k] = fadd(acc_ph[(sl * T + t) * H + k], term);
+                sum += (double)term;
             }
             dphh[i] = (float)sum;
             if (b0 + sl < a.B) a.dprojhh[((i64)st * a.B + b) * H + k] = (float)sum;
@@ -852,6 +931,7 @@ void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float
               float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st) {
     const size_t smem = sizeof(double) * kLstmS * H + sizeof(float) * ((size_t)4 * H * H + kLstmS * H + kLstmS * 4 * H);
     TRBA_REQUIRE(smem <= 200 * 1024, "lstm_fwd: hidden size too large for the shared-memory recurrence");
+    TRBA_REQUIRE(4 * H <= kLstmRows * 256, "lstm_fwd: at most 2 gate rows per thread (hidden <= 128)");
     set_smem((const void *)lstm_fwd_kernel, smem);
     lstm_fwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev,
                                                                   cat, dir);
@@ -863,6 +943,7 @@ void lstm_bwd(const float *dcat, const float *gates, const float *c, const float
     TRBA_REQUIRE(H % 8 == 0, "lstm_bwd: hidden size must be a multiple of 8 (4*hidden fills whole warps)");
     const size_t smem = sizeof(double) * kLstmS * 4 * H + sizeof(float) * ((size_t)4 * H * H + 2 * kLstmS * H);
     TRBA_REQUIRE(smem <= 200 * 1024, "lstm_bwd: hidden size too large for the shared-memory recurrence");
+    TRBA_REQUIRE(kLstmS * H <= kLstmRows * 256, "lstm_bwd: at most 2 state rows per thread (hidden <= 128)");
     set_smem((const void *)lstm_bwd_kernel, smem);
     lstm_bwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
     TRBA_LAUNCH_CHECK();
@@ -871,8 +952,12 @@ void lstm_bwd(const float *dcat, const float *gates, const float *c, const float
 void attn_fwd(const AttnFwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, S = kAttnS;
     const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S);
-    set_smem((const void *)attn_fwd_kernel<false>, smem);
-    attn_fwd_kernel<false><<<(a.B + S - 1) / S, 256, smem, st>>>(a);
+    const size_t stage_bytes = sizeof(float) * 2 * (size_t)S * T * H;
+    const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
+    const size_t total = smem + (stage ? stage_bytes : 0);
+    TRBA_REQUIRE(total <= kAttnMaxSmem, "attn_fwd: hidden / encoder length too large for shared memory");
+    set_smem((const void *)attn_fwd_kernel<false>, total);
+    attn_fwd_kernel<false><<<(a.B + S - 1) / S, kAttnThreads, total, st>>>(a, stage);
     TRBA_LAUNCH_CHECK();
 }
 
@@ -880,17 +965,25 @@ void attn_decode(const AttnFwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, V = a.V, S = kAttnS;
     const size_t smem =
         sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S + (size_t)S * V);
-    set_smem((const void *)attn_fwd_kernel<true>, smem);
-    attn_fwd_kernel<true><<<(a.B + S - 1) / S, 256, smem, st>>>(a);
+    const size_t stage_bytes = sizeof(float) * 2 * (size_t)S * T * H;
+    const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
+    const size_t total = smem + (stage ? stage_bytes : 0);
+    TRBA_REQUIRE(total <= kAttnMaxSmem, "attn_decode: hidden / encoder length too large for shared memory");
+    set_smem((const void *)attn_fwd_kernel<true>, total);
+    attn_fwd_kernel<true><<<(a.B + S - 1) / S, kAttnThreads, total, st>>>(a, stage);
     TRBA_LAUNCH_CHECK();
 }
 
 void attn_bwd(const AttnBwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, S = kAttnS;
     const size_t smem =
-        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (5 * H + 4 * H + 2 * T + 1 + 2 * T * H));
-    set_smem((const void *)attn_bwd_kernel, smem);
-    attn_bwd_kernel<<<(a.B + S - 1) / S, 256, smem, st>>>(a);
+        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (5 * H + 4 * H + 3 * T + 1 + 2 * T * H));
+    const size_t stage_bytes = sizeof(float) * (size_t)S * T * H;
+    const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
+    const size_t total = smem + (stage ? stage_bytes : 0);
+    TRBA_REQUIRE(total <= kAttnMaxSmem, "attn_bwd: hidden / encoder length too large for shared memory");
+    set_smem((const void *)attn_bwd_kernel, total);
+    attn_bwd_kernel<<<(a.B + S - 1) / S, kAttnThreads, total, st>>>(a, stage);
     TRBA_LAUNCH_CHECK();
 }
 
