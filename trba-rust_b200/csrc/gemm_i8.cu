@@ -356,6 +356,9 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int half = (warp - 2) >> 2;       // which 32-column blocks of the tile it takes
+        // With BN = 32 a tile has one column block: the two halves take
+        // alternate tiles instead (the tiles of accumulator 0, of 1), so two
+        // tiles drain at once; the other half only releases the accumulator.
         uint32_t acc = 0, acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int m0, n0, kb0, kb1;
@@ -366,8 +369,10 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             tc_fence_after();
             const int row = m0 + q * 32 + lane;
             const bool empty_split = kb0 >= kb1;  // nothing accumulated: skip
+            const bool mine = BN > 32 || (int)acc == half;
 #pragma unroll 1
-            for (int c0 = 32 * half; c0 < BN && n0 + c0 < N && !empty_split; c0 += 64) {
+            for (int c0 = BN > 32 ? 32 * half : 0; mine && c0 < BN && n0 + c0 < N && !empty_split;
+                 c0 += (BN > 32 ? 64 : 32)) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
                 tmem_ld_wait();
