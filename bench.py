@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--mope", action="store_true",
                     help="MoPE inference serving: 9 length-bucket experts, greedy decoding (not the training metric)")
     ap.add_argument("--mope-lines", type=int, default=65536)
+    ap.add_argument("--preproc", action="store_true",
+                    help="line-image preprocessing (load_image_q) throughput instead of the training step")
+    ap.add_argument("--preproc-lines", type=int, default=512)
     ap.add_argument("--mope-batch", type=int, default=512)
     ap.add_argument("--gemm-shape", default=None,
                     help="M,N,K: time only the int8 GEMM (s32 and fused int8 epilogue) at this shape")
@@ -533,8 +536,93 @@ def mope_arm(args):
         torch.distributed.destroy_process_group()
 
 
+def synthetic_line_images(n: int, seed: int):
+    """Decoded RGB8 line images: height 48..160 px, width 4..16x the height,
+    light paper with dark strokes (seeded)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        h = int(rng.integers(48, 161))
+        w = int(h * rng.uniform(4.0, 16.0))
+        im = np.full((h, w, 3), 235, np.uint8)
+        strokes = rng.random((h, w)) < 0.08
+        im[strokes] = rng.integers(0, 80, (int(strokes.sum()), 1), dtype=np.uint8)
+        out.append(im)
+    return out
+
+
+def preproc_arm(args):
+    """load_image_q on the device for a batch of decoded line images.  value:
+    device-timed lines/s with the pixels resident (CUDA events around the
+    kernel, L2 flushed before each step); e2e: the same through
+    preprocess_lines' path with the H2D copy of the packed pixels from pinned
+    memory inside the timed region (the int8 batch stays on the device for
+    the model); cpu_baseline: the CPU restatement (oracle/preproc_oracle.py,
+    numpy, one thread) on a sample of the same images."""
+    import numpy as np
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    load_package()
+    from trba_b200 import preproc as pp
+    imgs = synthetic_line_images(args.preproc_lines, args.seed + rank)
+    packed = pp.PackedImages(imgs)
+    batch = pp.DeviceBatch(packed, dev)
+    out = torch.empty((len(imgs), 32 * 160 * 3), dtype=torch.int8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        pp.preprocess_device(batch, 32, 160, out)
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record()
+        pp.preprocess_device(batch, 32, 160, out)
+        b.record()
+    torch.cuda.synchronize(dev)
+    ms = sorted(a.elapsed_time(b) for a, b in ev)[len(ev) // 2]
+    e2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in e2:
+        flush.zero_()
+        a.record()
+        bt = pp.DeviceBatch(packed, dev)
+        pp.preprocess_device(bt, 32, 160, out)
+        b.record()
+    torch.cuda.synchronize(dev)
+    ms_e2e = sorted(a.elapsed_time(b) for a, b in e2)[len(e2) // 2]
+    src_px = int(sum(im.shape[0] * im.shape[1] for im in imgs))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(REPO / "oracle"))
+        import preproc_oracle as po
+        k = min(len(imgs), 16)
+        t0 = time.perf_counter()
+        for im in imgs[:k]:
+            po.load_image_q(im, 32, 160)
+        dt = time.perf_counter() - t0
+        cpu = {"value": k / dt, "unit": "lines/s", "cores": 1, "kind": "port",
+               "sample": f"{k} of the same images through the numpy restatement"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "line-image preprocessing lines/s (decoded RGB8 -> 32x160 int8 model input)",
+            "value": len(imgs) / (ms / 1000.0), "unit": "lines/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+            "dtype": "u8 -> f32 -> int8", "data": "synthetic",
+            "config": {"workload": f"{len(imgs)} line images, height 48..160, width 4..16x height",
+                       "source_megapixels": src_px / 1e6, "l2": "256 MB flush before each step"},
+            "e2e": {"value": len(imgs) / (ms_e2e / 1000.0), "unit": "lines/s",
+                    "h2d_bytes_per_step": packed.nbytes + 16 * len(imgs), "d2h_bytes_per_step": 0},
+            "gpu_launches": 1, "cpu_baseline": cpu,
+        }), flush=True)
+
+
 def main():
     args = parse()
+    if args.preproc:
+        preproc_arm(args)
+        return
     if args.mope:
         mope_arm(args)
         return
