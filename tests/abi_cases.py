@@ -45,6 +45,8 @@ def conv_geoms():
         (2, 5, 7, 7, 9, 1, 1, 2, 2, 0, 0),
         (2, 8, 4, 9, 8, 2, 2, 2, 1, 0, 1),   # conv_out.0 geometry
         (1, 8, 2, 10, 8, 2, 2, 1, 1, 0, 0),  # conv_out.3 geometry
+        (2, 16, 6, 13, 4, 3, 3, 1, 1, 1, 1),  # stem.3 channel count (row-per-thread im2col)
+        (2, 3, 7, 9, 4, 3, 3, 2, 2, 1, 1),    # 3 channels, strided
     ]
 
 

@@ -48,6 +48,51 @@ __global__ void im2col_pad_kernel(const int8_t *__restrict__ in, int8_t *__restr
 constexpr int kIm2colMaxLd = 4096;
 constexpr int kTileRows = 32;
 
+// Narrow operands (the stem convolutions: C = 3 or 16 channels, 3x3, so
+// col_ld = 32 or 144 bytes): one thread per row.  The thread gathers its
+// row's C * 9 window bytes (neighbouring lanes read neighbouring input
+// pixels), packs them into 32-bit words in registers in K order (c, kh, kw)
+// and writes the row with 16-byte stores; a warp covers 32 consecutive rows,
+// i.e. one contiguous span of col.  Rows in [rows, rows_pad) are written as
+// zeros.  All index arithmetic is 32-bit within an image plane.
+template <int C, int KH, int KW>
+__global__ void __launch_bounds__(256) im2col_rows_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
+                                                          int H, int W, int sH, int sW, int pH, int pW, int Ho,
+                                                          int Wo, i64 rows, i64 rows_pad) {
+    constexpr int K = C * KH * KW, LD = (K + 15) / 16 * 16, NW = LD / 4;
+    const int hwo = Ho * Wo, hw = H * W;
+    for (i64 r = (i64)blockIdx.x * blockDim.x + threadIdx.x; r < rows_pad; r += (i64)gridDim.x * blockDim.x) {
+        uint32_t w[NW];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) w[i] = 0u;
+        if (r < rows) {
+            const i64 b = r / hwo;
+            const int rem = (int)(r - b * hwo), oh = rem / Wo, ow = rem - oh * Wo;
+            const int ih0 = oh * sH - pH, iw0 = ow * sW - pW;
+            const int8_t *src = in + b * C * hw;
+            bool okh[KH], okw[KW];
+#pragma unroll
+            for (int i = 0; i < KH; ++i) okh[i] = (unsigned)(ih0 + i) < (unsigned)H;
+#pragma unroll
+            for (int j = 0; j < KW; ++j) okw[j] = (unsigned)(iw0 + j) < (unsigned)W;
+#pragma unroll
+            for (int c = 0; c < C; ++c)
+#pragma unroll
+                for (int i = 0; i < KH; ++i)
+#pragma unroll
+                    for (int j = 0; j < KW; ++j) {
+                        const int k = (c * KH + i) * KW + j;
+                        const uint32_t v =
+                            (okh[i] && okw[j]) ? (uint32_t)(uint8_t)src[c * hw + (ih0 + i) * W + iw0 + j] : 0u;
+                        w[k >> 2] |= v << (8 * (k & 3));
+                    }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(col + r * LD);
+#pragma unroll
+        for (int q = 0; q < NW / 4; ++q) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+}
+
 template <int KH, int KW>
 __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
                                                           int C, int H, int W, int kH_, int kW_, int sH, int sW,
@@ -287,7 +332,21 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
     const i64 rows = (i64)batch * Ho * Wo;
     if (col_ld < cols || (col_ld & 15) || rows <= 0) return;
     const i64 total = ((rows + 15) / 16 * 16) * col_ld;
-    if (col_ld <= kIm2colMaxLd && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {
+    const bool aligned = (reinterpret_cast<uintptr_t>(col) & 15) == 0;
+    if (aligned && kH == 3 && kW == 3 && (C == 3 || C == 16) && col_ld == (C * 9 + 15) / 16 * 16) {
+        const i64 rows_pad = (rows + 15) / 16 * 16;
+        const i64 want = (rows_pad + 255) / 256, cap = (i64)sm_count() * 16;
+        const unsigned grid = (unsigned)(want < cap ? want : cap);
+        if (C == 3)
+            im2col_rows_kernel<3, 3, 3><<<grid, 256, 0, as_stream(s)>>>(input, col, H, W, sH, sW, pH, pW, Ho, Wo,
+                                                                       rows, rows_pad);
+        else
+            im2col_rows_kernel<16, 3, 3><<<grid, 256, 0, as_stream(s)>>>(input, col, H, W, sH, sW, pH, pW, Ho, Wo,
+                                                                        rows, rows_pad);
+        TRBA_LAUNCH_CHECK();
+        return;
+    }
+    if (col_ld <= kIm2colMaxLd && aligned) {
         const i64 rows_pad = (rows + 15) / 16 * 16;
         const size_t smem = (size_t)kTileRows * (col_ld + 4);
         const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
