@@ -468,6 +468,31 @@ def gemm_only(args):
             e1.synchronize()
             best = min(best, e0.elapsed_time(e1))
         out[name] = {"us": best * 1e3, "tops": 2.0 * m * n * k / (best * 1e-3) / 1e12}
+    # the same s32 GEMM on one CTA per tile (pair kernel off) and through cuBLAS, for context
+    prev = L.trba_gemm_pair_enable(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for _ in range(max(3, args.steps)):
+        e0.record()
+        L.launch_gemm_int8(p(a), p(b), p(c32), m, n, k, None)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    L.trba_gemm_pair_enable(prev)
+    out["s32_single_cta"] = {"us": best * 1e3, "tops": 2.0 * m * n * k / (best * 1e-3) / 1e12}
+    try:
+        bt = b[:, :k].t()
+        a_k = a[:, :k].contiguous()
+        best = float("inf")
+        for _ in range(max(3, args.steps)):
+            e0.record()
+            torch._int_mm(a_k, bt)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        out["cublas_s32"] = {"us": best * 1e3, "tops": 2.0 * m * n * k / (best * 1e-3) / 1e12}
+    except Exception as exc:  # pragma: no cover - shape constraints of the library call
+        out["cublas_s32"] = {"unavailable": str(exc)[:120]}
     if L.trba_tc_error_poll(1) != 0:
         raise RuntimeError("tensor-core GEMM reported a timed-out wait")
     print(json.dumps(out), flush=True)

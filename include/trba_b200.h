@@ -55,6 +55,12 @@ void trba_gemm_int8_requant(const int8_t *a, const int8_t *b, const float *bias,
 void trba_gemm_int8_dequant_f32(const int8_t *a, const int8_t *b, const float *w_scale, float a_scale,
                                 const float *bias, int relu, float *out, int m, int n, int k, void *stream);
 long long trba_launch_count(void);
+/* Large int8 GEMMs (unsplit, N a multiple of 256, at least one wave of
+ * 256 x 256 tiles) run on CTA pairs (tcgen05 cta_group::2); enable = 0 routes
+ * them to the single-CTA kernel instead (same results bit for bit; used by
+ * the tests to compare the two).  Returns the previous setting.  No
+ * counterpart in the reference. */
+int trba_gemm_pair_enable(int enable);
 
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier
  * wait gave up.  Synchronises the device; clears the word if clear != 0. */

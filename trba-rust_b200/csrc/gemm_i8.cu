@@ -404,6 +404,189 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     }
 }
 
+// ------------------------------------------------- CTA-pair (2-SM) variant
+// For large M x N (at least one wave of 256 x 256 tiles): a cluster of two
+// CTAs computes one 256 x 256 tile with tcgen05.mma.cta_group::2.  CTA r
+// loads rows [m0 + 128 r, +128) of A and rows [n0 + 128 r, +128) of B (its
+// half of the tile's B) into its own shared memory; CTA 0 issues M = 256 MMAs
+// that read both halves and write 128 accumulator rows into each CTA's TMEM.
+// Per SM a 128-byte K slice costs 32 KB of operand traffic instead of the
+// single-CTA 48 KB for the same multiply-adds, and six stages fit.
+//   full[s]   (CTA 0): armed by CTA 0 with both CTAs' bytes, completed by
+//             the TMA loads of both CTAs.
+//   empty[s]  (each CTA): released by CTA 0's MMA commit (one commit per CTA).
+//   tfull[a]  (each CTA): accumulator a is ready (commits as above).
+//   tempty[a] (CTA 0): released by the epilogue threads of both CTAs.
+// All waits are bounded as in the single-CTA kernel; the CTAs meet at a
+// cluster barrier before TMEM is freed.
+constexpr int kPairBN = 256;   // N of one pair MMA; each CTA holds 128 rows of B
+constexpr int kPairStages = 6;
+
+struct PairCfg {
+    static constexpr int A_BYTES = BM * BK;               // 16 KB
+    static constexpr int B_BYTES = (kPairBN / 2) * BK;    // 16 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * kPairBN;         // two accumulators: the whole TMEM
+    static constexpr int EPI_SMEM = 2 * kMaxN * 8;
+    static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + 512 + EPI_SMEM;
+};
+
+template <class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
+                    Epi epi) {
+    using G = PairCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + kPairStages * G::A_BYTES;
+    Ctl *ctl = reinterpret_cast<Ctl *>(smem + kPairStages * G::STAGE_BYTES);
+    double *epi_sm = reinterpret_cast<double *>(smem + kPairStages * G::STAGE_BYTES + 512);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int M = sh.M, N = sh.N, K = sh.K;
+    const int m_tiles = (M + 2 * BM - 1) / (2 * BM), n_tiles = (N + kPairBN - 1) / kPairBN;
+    const int tiles = m_tiles * n_tiles, kblocks = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&ctl->tfull[a], 1);
+            mbar_init(&ctl->tempty[a], 2 * kEpiWarps * 32);
+        }
+        mbar_init(&ctl->drained, 1);
+        ctl->abort = 0;
+        ctl->issued = 0;
+        ctl->consumed = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp >= 2) epi.init(epi_sm);
+    if (warp == 1) {
+        tmem_alloc_pair(&ctl->tmem_base, G::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised before any remote use
+    tc_fence_after();
+    const uint32_t tbase = ctl->tmem_base;
+    volatile int *abort = &ctl->abort;
+
+    auto tile_coords = [&](int t, int &m0, int &n0) {
+        m0 = (t / n_tiles) * (2 * BM);
+        n0 = (t % n_tiles) * kPairBN;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            uint32_t it = 0;
+            for (int t = pair; t < tiles && !*abort; t += npairs) {
+                int m0, n0;
+                tile_coords(t, m0, n0);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    const uint32_t ph = (it / kPairStages) & 1u;
+                    if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort)) break;
+                    if (rank == 0) mbar_expect_tx(&ctl->full[s], 2 * G::STAGE_BYTES);
+                    const uint32_t full0 = mapa_shared(smem_u32(&ctl->full[s]), 0);
+                    tma_load_2d_pair(sA + s * G::A_BYTES, &tmA, full0, kb * BK, m0 + (int)rank * BM);
+                    tma_load_2d_pair(sB + s * G::B_BYTES, &tmB, full0, kb * BK, n0 + (int)rank * (kPairBN / 2));
+                    ctl->issued = it + 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (CTA 0) ----------------
+            constexpr uint32_t idesc = idesc_i8(2 * BM, kPairBN);
+            uint32_t it = 0, acc = 0, acc_ph = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                if (!(ok = mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort))) break;
+                tc_fence_after();
+                const uint32_t d = tbase + acc * kPairBN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    const uint32_t ph = (it / kPairStages) & 1u;
+                    if (!(ok = mbar_wait(&ctl->full[s], ph, abort))) break;
+                    ctl->consumed = it + 1;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * G::A_BYTES), b0 = smem_u32(sB + s * G::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / UK; ++k)
+                        mma_i8_pair(d, desc_k_sw128(a0 + k * UK), desc_k_sw128(b0 + k * UK), idesc,
+                                    (kb != 0 || k != 0) ? 1u : 0u);
+                    const uint32_t e_loc = smem_u32(&ctl->empty[s]);
+                    mma_commit_pair(e_loc);
+                    mma_commit_pair(mapa_shared(e_loc, 1));
+                }
+                if (!ok) break;
+                const uint32_t f_loc = smem_u32(&ctl->tfull[acc]);
+                mma_commit_pair(f_loc);
+                mma_commit_pair(mapa_shared(f_loc, 1));
+                acc ^= 1u;
+                if (acc == 0) acc_ph ^= 1u;
+            }
+            mma_commit_pair(smem_u32(&ctl->drained));
+            volatile int never = 0;
+            mbar_wait(&ctl->drained, 0, &never, 200000000ull);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        uint32_t acc = 0, acc_ph = 0;
+        for (int t = pair; t < tiles; t += npairs) {
+            int m0, n0;
+            tile_coords(t, m0, n0);
+            const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort);
+            __syncwarp();
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const int row = m0 + (int)rank * BM + q * 32 + lane;
+#pragma unroll 1
+            for (int c0 = 32 * half; c0 < kPairBN && n0 + c0 < N; c0 += 64) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * kPairBN + c0, v);
+                tmem_ld_wait();
+                epi.store(row, n0 + c0, M, N, v, lane, epi_sm);
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
+            acc ^= 1u;
+            if (acc == 0) acc_ph ^= 1u;
+        }
+    }
+
+    __syncthreads();
+    if (warp >= 2) epi.finish(epi_sm, N);
+    if (threadIdx.x == 0 && *abort) {
+        if (rank == 0) {
+            for (uint32_t i = ctl->consumed; i < ctl->issued; ++i) {
+                volatile int never = 0;
+                mbar_wait(&ctl->full[i % kPairStages], (i / kPairStages) & 1u, &never, 200000000ull);
+            }
+        }
+        atomicExch(&g_tc_error, 1);
+    }
+    __syncthreads();
+    cluster_sync();  // the peer has finished with this CTA's barriers and TMEM
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tbase, G::TMEM_COLS);
+    }
+}
+
+
 // CUDA-core fallback for operands TMA cannot describe (base address not
 // 16-byte aligned): 64x64 tile per CTA, K in 32-byte slices, dp4a.
 __global__ void gemm_i8_simt_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B,
@@ -473,8 +656,54 @@ void launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const Epi
     TRBA_LAUNCH_CHECK();
 }
 
+int g_pair_enabled = 1;  // host-side switch (trba_gemm_pair_enable)
+bool pair_enabled() { return g_pair_enabled != 0; }
+
+// The pair kernel serves unsplit problems with N a multiple of 256 and at
+// least one wave of pair tiles; everything else takes the single-CTA kernel.
+bool use_pair(const Shape &sh) {
+    if (sh.splits != 1 || sh.N < kPairBN || (sh.N % kPairBN) != 0) return false;
+    const int tiles = ((sh.M + 2 * BM - 1) / (2 * BM)) * (sh.N / kPairBN);
+    return tiles >= sm_count() / 2;
+}
+
+template <class Epi>
+void launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const Epi &epi, cudaStream_t st) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        TRBA_CHECK(cudaFuncSetAttribute(gemm_i8_pair_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        PairCfg::SMEM));
+        attr_set[dev] = true;
+    }
+    const int tiles = ((sh.M + 2 * BM - 1) / (2 * BM)) * (sh.N / kPairBN);
+    const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = PairCfg::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TRBA_CHECK(cudaLaunchKernelEx(&cfg, gemm_i8_pair_kernel<Epi>, ta, tb, sh, epi));
+    TRBA_LAUNCH_CHECK();
+}
+
 template <class Epi>
 bool run_tc(const int8_t *A, int lda, const int8_t *B, int ldb, Shape sh, const Epi &epi, cudaStream_t st) {
+    if (use_pair(sh) && pair_enabled()) {
+        CUtensorMap ta, tb;
+        if (make_tmap_i8(&ta, A, sh.M, sh.K, lda, BM) && make_tmap_i8(&tb, B, sh.N, sh.K, ldb, kPairBN / 2)) {
+            launch_pair(ta, tb, sh, epi, st);
+            return true;
+        }
+    }
     const int bn = pick_bn(sh.N);
     CUtensorMap ta, tb;
     if (!make_tmap_i8(&ta, A, sh.M, sh.K, lda, BM) || !make_tmap_i8(&tb, B, sh.N, sh.K, ldb, bn)) return false;
@@ -627,3 +856,9 @@ int trba_tc_error_poll(int clear) {
 }
 
 }  // extern "C"
+
+extern "C" int trba_gemm_pair_enable(int enable) {
+    const int prev = g_pair_enabled;
+    g_pair_enabled = enable ? 1 : 0;
+    return prev;
+}
