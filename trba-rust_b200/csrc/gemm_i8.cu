@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gemm_i8.cuh"
@@ -132,7 +133,7 @@ struct EpiConvF32 {
     double *bn_acc;      // [2*N]: per-channel sum, then sum of squares (f64)
     int HW;
     __device__ void init(double *sm) {
-        for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += kThreads - 64) sm[i] = 0.0;
+        for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += blockDim.x - 64) sm[i] = 0.0;
     }
     __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
         const float scale = fmul(*s_in, *w_s);
@@ -155,7 +156,7 @@ struct EpiConvF32 {
         }
     }
     __device__ void finish(double *sm, int N) {
-        for (int i = threadIdx.x - 64; i < N; i += kThreads - 64) {
+        for (int i = threadIdx.x - 64; i < N; i += blockDim.x - 64) {
             if (sm[i] != 0.0) atomicAdd(bn_acc + i, sm[i]);
             if (sm[kMaxN + i] != 0.0) atomicAdd(bn_acc + N + i, sm[kMaxN + i]);
         }
@@ -421,6 +422,13 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 // cluster barrier before TMEM is freed.
 constexpr int kPairBN = 256;   // N of one pair MMA; each CTA holds 128 rows of B
 constexpr int kPairStages = 6;
+// Epilogue warps of the pair kernel: 16 (four per TMEM lane quarter) for the
+// arithmetic epilogues, 8 for the plain s32 store, which is bound by its
+// stores (more warps measured slower there).
+template <class Epi>
+constexpr int pair_epi_warps() {
+    return std::is_same<Epi, EpiS32>::value ? 8 : 16;
+}
 
 struct PairCfg {
     static constexpr int A_BYTES = BM * BK;               // 16 KB
@@ -431,8 +439,8 @@ struct PairCfg {
     static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + 512 + EPI_SMEM;
 };
 
-template <class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+template <class Epi, int EW = pair_epi_warps<Epi>()>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
                     Epi epi) {
     using G = PairCfg;
@@ -457,7 +465,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&ctl->tfull[a], 1);
-            mbar_init(&ctl->tempty[a], 2 * kEpiWarps * 32);
+            mbar_init(&ctl->tempty[a], 2 * EW * 32);
         }
         mbar_init(&ctl->drained, 1);
         ctl->abort = 0;
@@ -540,9 +548,9 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             mbar_wait(&ctl->drained, 0, &never, 200000000ull);
         }
     } else {
-        // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+        // ---------------- epilogue (warps 2..EW+1, both CTAs) ----------------
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int grp = (warp - 2) >> 2;  // column group: blocks 32 * grp, 32 * grp + 8 * EW, ...
         uint32_t acc = 0, acc_ph = 0;
         for (int t = pair; t < tiles; t += npairs) {
             int m0, n0;
@@ -553,7 +561,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tc_fence_after();
             const int row = m0 + (int)rank * BM + q * 32 + lane;
 #pragma unroll 1
-            for (int c0 = 32 * half; c0 < kPairBN && n0 + c0 < N; c0 += 64) {
+            for (int c0 = 32 * grp; c0 < kPairBN && n0 + c0 < N; c0 += 8 * EW) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * kPairBN + c0, v);
                 tmem_ld_wait();
@@ -681,7 +689,7 @@ void launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const E
     const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * pairs));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(64 + 32 * pair_epi_warps<Epi>());
     cfg.dynamicSmemBytes = PairCfg::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
