@@ -369,6 +369,15 @@ def our_arm(args):
         m.probe(-1)
         gemm[name] = {"launches_per_step": g_n // 3, "ms_per_step": g_ms / 3,
                       "tops": g_ops / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None}
+    # where the step's time goes: each phase spanned on the step's stream
+    phases = {}
+    for name, kind in m.PROBE_PHASES.items():
+        m.probe(kind)
+        for _ in range(3):
+            m.train_step(*devb, stream=sptr)
+        p_ms, _, _, _, _ = m.probe_read()
+        m.probe(-1)
+        phases[name] = p_ms / 3
     barrier()
 
     sweep = None
@@ -432,6 +441,7 @@ def our_arm(args):
             "int8_gemm_sweep": sweep,
             "head_sgemm": {"launches_per_step": head["launches_per_step"], "ms_per_step": head["ms_per_step"],
                            "tflops": head["tops"]},
+            "step_phases_ms": {**phases, "note": "eager steps, each phase spanned on the step's stream"},
         }
         print(json.dumps(out), flush=True)
     m.close()

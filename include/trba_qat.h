@@ -134,6 +134,15 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
 #define TRBA_PROBE_WGRAD_GEMM 1 /* conv weight-gradient int8 tcgen05 split-K GEMM */
 #define TRBA_PROBE_DGRAD 2      /* conv input-gradient gather (fp32, reference summation order) */
 #define TRBA_PROBE_SGEMM 3      /* sequence-head fp32 GEMMs (f64 accumulation) */
+/* Whole phases of the step on the step's stream (one span per step each):
+ * SE-ResNet forward, sequence head forward with the losses, sequence head
+ * backward, SE-ResNet backward (until the input-gradient side stream has
+ * joined), gradient all-reduce + clip + optimiser + re-quantisation. */
+#define TRBA_PROBE_PHASE_CNN_FWD 4
+#define TRBA_PROBE_PHASE_HEAD_FWD 5
+#define TRBA_PROBE_PHASE_HEAD_BWD 6
+#define TRBA_PROBE_PHASE_CNN_BWD 7
+#define TRBA_PROBE_PHASE_OPTIMIZER 8
 int trba_model_probe(trba_model *m, int kind);
 int trba_model_probe_read(trba_model *m, double *ms_total, long long *launches, double *ops, double *bytes,
                           long long *steps);

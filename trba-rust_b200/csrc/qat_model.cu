@@ -224,9 +224,10 @@ struct trba_model {
     ncclComm_t comm = nullptr;
     int world = 1;
     cudaEvent_t ev = nullptr;
-    // Side stream of the conv backward: the input-gradient gather (which reads
-    // only dy) runs there while the BN backward chain and the weight-gradient
-    // GEMM of the same conv run on the step's stream.
+    // Weight-gradient stream of the conv backward: every conv's BN backward
+    // chain and weight-gradient GEMM run there (forked when the conv's dy is
+    // ready, joined once after the last conv), while the chain of input
+    // gradients runs on the step's stream.
     cudaStream_t side = nullptr;
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     // CUDA-graph execution of the whole step (trba_model_use_graphs): the
@@ -875,46 +876,49 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
     const int B = c.B, HW = L.Ho * L.Wo;
     const i64 rows = L.rows(B), rp = a16l(rows);
     const bool compat = c.m->cfg.wgrad_mode == 0;
-    // The input gradient reads only dy (and the int8 weights, the ReLU mask
-    // and the residual gradient), so it runs on the side stream while the
-    // BN backward chain and the weight gradient run here; the caller sees gi
-    // after the join at the end.
+    cudaStream_t ws = c.m->side;
+    // The input gradient of the reference reads the BN-output gradient dy
+    // (not the BN-input gradient), so the BN backward chain and the weight
+    // gradient feed nothing but the parameter gradients: they run on the
+    // weight-gradient stream, joined once at the end of the backward pass,
+    // while the chain of input gradients (the critical path) stays here.
+    TRBA_CHECK(cudaEventRecord(c.m->fork_ev, c.st));
+    TRBA_CHECK(cudaStreamWaitEvent(ws, c.m->fork_ev, 0));
+    qat::bn_bwd_sums(dy, L.x.get(), L.mean.get(), L.var.get(), B, L.cout, HW, L.bwd_acc.get(), ws);
+    qat::bn_dx_max(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
+                   c.G + L.gamma_off, c.G + L.beta_off, L.dxmax.get(), ws);
+    if (compat && (rows & 15)) TRBA_CHECK(cudaMemsetAsync(L.A.get(), 0, (size_t)a16(L.cout) * rp, ws));
+    qat::bn_dx_quant(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
+                     L.dxmax.get(), L.s_dx.get(), L.A.get(), compat ? (int)rows : (int)rp, compat, ws);
+    const int splits = splitk_for(L.cout, L.K, (int)rows);
+    const int8_t *Bop = compat ? L.col.get() : L.colT.get();
+    {
+        // bytes: quantised dx + im2col operand read, s32 dW accumulated
+        ProbeScope ps(c.m, TRBA_PROBE_WGRAD_GEMM, 2.0 * rows * L.cout * L.K,
+                      (double)rows * L.cout + (double)rows * L.kp + 4.0 * L.cout * L.K, ws);
+        if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits, ws))
+            report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
+    }
+    qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, ws);
     if (gi) {
-        TRBA_CHECK(cudaEventRecord(c.m->fork_ev, c.st));
-        TRBA_CHECK(cudaStreamWaitEvent(c.m->side, c.m->fork_ev, 0));
         // ops: one multiply and one add per (input element, valid tap, output channel)
         const double in_n = (double)B * L.cin * L.H * L.W;
         const double bytes = 4.0 * B * L.cout * HW + 4.0 * in_n + (mask_q ? in_n : 0.0) + (add ? 4.0 * in_n : 0.0) +
                              (double)L.cout * L.K;
         const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
                              valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
-        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.m->side);
+        ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.st);
         qat::dgrad(dy, L.wT.get(), L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
                    L.Wo, L.cls_perm.empty() ? nullptr : L.d_perm.get(),
                    L.cls_perm.empty() ? nullptr : L.d_cstart.get(), (int)L.cls_start.size() - 1, mask_q, add, gi,
-                   c.m->side);
+                   c.st);
     }
-    qat::bn_bwd_sums(dy, L.x.get(), L.mean.get(), L.var.get(), B, L.cout, HW, L.bwd_acc.get(), c.st);
-    qat::bn_dx_max(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
-                   c.G + L.gamma_off, c.G + L.beta_off, L.dxmax.get(), c.st);
-    if (compat && (rows & 15)) TRBA_CHECK(cudaMemsetAsync(L.A.get(), 0, (size_t)a16(L.cout) * rp, c.st));
-    qat::bn_dx_quant(dy, L.x.get(), L.mean.get(), L.var.get(), c.P + L.gamma_off, L.bwd_acc.get(), B, L.cout, HW,
-                     L.dxmax.get(), L.s_dx.get(), L.A.get(), compat ? (int)rows : (int)rp, compat, c.st);
-    const int splits = splitk_for(L.cout, L.K, (int)rows);
-    const int8_t *Bop = compat ? L.col.get() : L.colT.get();
-    {
-        // bytes: quantised dx + im2col operand read, s32 dW accumulated
-        ProbeScope ps(c.m, TRBA_PROBE_WGRAD_GEMM, 2.0 * rows * L.cout * L.K,
-                      (double)rows * L.cout + (double)rows * L.kp + 4.0 * L.cout * L.K, c.st);
-        if (!gemm_i8_splitk_atomic(L.A.get(), (int)rp, Bop, (int)rp, L.gw.get(), L.cout, L.K, (int)rows, splits,
-                                   c.st))
-            report_error(__FILE__, __LINE__, "conv wgrad GEMM: operands not TMA-describable", -1);
-    }
-    qat::grad_accum(L.gw.get(), L.s_dx.get(), L.s_in, (i64)L.cout * L.K, c.G + L.w_off, c.st);
-    if (gi) {
-        TRBA_CHECK(cudaEventRecord(c.m->join_ev, c.m->side));
-        TRBA_CHECK(cudaStreamWaitEvent(c.st, c.m->join_ev, 0));
-    }
+}
+
+// Joins the weight-gradient stream back into the step's stream.
+void join_weight_grads(Ctx &c) {
+    TRBA_CHECK(cudaEventRecord(c.m->join_ev, c.m->side));
+    TRBA_CHECK(cudaStreamWaitEvent(c.st, c.m->join_ev, 0));
 }
 
 void cnn_forward(Ctx &c, const int8_t *img) {
@@ -995,6 +999,7 @@ void cnn_backward(Ctx &c) {
     qat::pool_bwd_mask(cv[1].q.get(), gv, cv[1].s_q.get(), c.B, cv[1].cout, cv[1].Ho, cv[1].Wo, m->dy_c1.get(), c.st);
     conv_bwd(c, cv[1], m->dy_c1.get(), cv[0].q.get(), nullptr, m->dy_c0.get());
     conv_bwd(c, cv[0], m->dy_c0.get(), nullptr, nullptr, nullptr);
+    join_weight_grads(c);
 }
 
 seq::Gemm gemm(trba_model *m, int M, int N, int K, const float *A, i64 sam, i64 sak, const float *Bm, i64 sbk,
@@ -1408,10 +1413,22 @@ int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t 
     if (m->probe.kind >= 0) m->probe.steps += 1;
     TRBA_CHECK(cudaMemsetAsync(m->zarena.base, 0, m->zarena.used, st));
     TRBA_CHECK(cudaMemsetAsync(m->G.get(), 0, (size_t)m->n_params * 4, st));
-    cnn_forward(c, img);
-    head_forward(c, text_in, target, ctc_tgt, ctc_len);
-    head_backward(c);
-    cnn_backward(c);
+    {
+        ProbeScope ps(m, TRBA_PROBE_PHASE_CNN_FWD, 0.0, 0.0, st);
+        cnn_forward(c, img);
+    }
+    {
+        ProbeScope ps(m, TRBA_PROBE_PHASE_HEAD_FWD, 0.0, 0.0, st);
+        head_forward(c, text_in, target, ctc_tgt, ctc_len);
+    }
+    {
+        ProbeScope ps(m, TRBA_PROBE_PHASE_HEAD_BWD, 0.0, 0.0, st);
+        head_backward(c);
+    }
+    {
+        ProbeScope ps(m, TRBA_PROBE_PHASE_CNN_BWD, 0.0, 0.0, st);
+        cnn_backward(c);
+    }
     return cuda_status();
 }
 
@@ -1480,6 +1497,7 @@ int step_body(trba_model *m, const int8_t *img, const int32_t *text_in, const in
               const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, cudaStream_t st) {
     int rc = trba_model_forward_backward(m, img, text_in, target, ctc_tgt, ctc_len, batch, st);
     if (rc) return rc;
+    ProbeScope ps(m, TRBA_PROBE_PHASE_OPTIMIZER, 0.0, 0.0, st);
     if (m->comm) {
         const ncclResult_t r = nccl().AllReduce(m->G.get(), m->G.get(), (size_t)m->n_params, ncclFloat, ncclAvg,
                                                 m->comm, st);
@@ -1653,7 +1671,7 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
 }
 
 int trba_model_probe(trba_model *m, int kind) {
-    if (!m || kind < -1 || kind > TRBA_PROBE_SGEMM) return -1;
+    if (!m || kind < -1 || kind > TRBA_PROBE_PHASE_OPTIMIZER) return -1;
     if (m->gexec) {  // a recorded step graph may hold this probe's events
         TRBA_CHECK(cudaStreamSynchronize(m->gstream));
         TRBA_CHECK(cudaGraphExecDestroy(m->gexec));

@@ -200,6 +200,8 @@ class QatModel:
         return C.cast(self.L.trba_model_loss_dev(self.h), C.c_void_p).value
 
     PROBE_CONV_GEMM, PROBE_WGRAD_GEMM, PROBE_DGRAD, PROBE_SGEMM = 0, 1, 2, 3
+    PROBE_PHASES = {"cnn_forward": 4, "head_forward": 5, "head_backward": 6, "cnn_backward": 7,
+                    "allreduce_optimizer": 8}
 
     def probe(self, kind: int):
         """Bracket every launch of one kernel family with CUDA events (-1 = off)."""
