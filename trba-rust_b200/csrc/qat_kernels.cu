@@ -597,7 +597,7 @@ __global__ void __launch_bounds__(kDgradThreads, 3) dgrad_kernel(
     const float *__restrict__ go, const float *__restrict__ wT, const float *__restrict__ w_s, int B, int Cin, int H,
     int W, int Cout, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo, const int *__restrict__ perm,
     const int *__restrict__ cstart, int ncls, const int8_t *__restrict__ mask_q, const float *__restrict__ add,
-    float *__restrict__ gi, float neg_zero) {
+    float *__restrict__ gi, float neg_zero, const float *__restrict__ gmax_scale, float *__restrict__ gmax_out) {
     constexpr int CI = kDgradCi, NP = CI / 2;
     extern __shared__ float4 wsm4[];  // [taps][Cout][CI / 4]
     const int khw = kH * kW, ci0 = blockIdx.y * CI;
@@ -608,62 +608,74 @@ __global__ void __launch_bounds__(kDgradThreads, 3) dgrad_kernel(
     __syncthreads();
     const int hwo = Ho * Wo, hwi = H * W;
     const i64 t = (i64)blockIdx.x * kDgradThreads + threadIdx.x;
-    if (t >= (i64)B * hwi) return;
-    int b, pix;
-    if (perm) {
-        int c = 0;
-        while (c + 1 < ncls && t >= (i64)B * cstart[c + 1]) ++c;
-        const int c0 = cstart[c], csz = cstart[c + 1] - c0;
-        const i64 local = t - (i64)B * c0;
-        b = (int)(local / csz);
-        pix = perm[c0 + (int)(local - (i64)b * csz)];
-    } else {
-        b = (int)(t / hwi);
-        pix = (int)(t - (i64)b * hwi);
-    }
-    const int ih = pix / W, iw = pix - ih * W;
-    const f32x2 z = pack2(neg_zero, neg_zero);
-    f32x2 acc[NP];
+    // threads past the end take part in the optional max reduction only
+    const bool live = t < (i64)B * hwi;
+    float gmax = 0.0f;
+    if (live) {
+        int b, pix;
+        if (perm) {
+            int c = 0;
+            while (c + 1 < ncls && t >= (i64)B * cstart[c + 1]) ++c;
+            const int c0 = cstart[c], csz = cstart[c + 1] - c0;
+            const i64 local = t - (i64)B * c0;
+            b = (int)(local / csz);
+            pix = perm[c0 + (int)(local - (i64)b * csz)];
+        } else {
+            b = (int)(t / hwi);
+            pix = (int)(t - (i64)b * hwi);
+        }
+        const int ih = pix / W, iw = pix - ih * W;
+        const f32x2 z = pack2(neg_zero, neg_zero);
+        f32x2 acc[NP];
 #pragma unroll
-    for (int j = 0; j < NP; ++j) acc[j] = 0ull;  // (+0, +0)
-    const float *gob = go + (i64)b * Cout * hwo;
-    for (int kh = 0; kh < kH; ++kh) {
-        const int nh = ih + pH - kh;
-        if (nh < 0 || nh % sH != 0 || nh / sH >= Ho) continue;
-        for (int kw = 0; kw < kW; ++kw) {
-            const int nw = iw + pW - kw;
-            if (nw < 0 || nw % sW != 0 || nw / sW >= Wo) continue;
-            const float *gp = gob + (nh / sH) * Wo + nw / sW;
-            const ulonglong2 *wt = reinterpret_cast<const ulonglong2 *>(wsm4) + (i64)(kh * kW + kw) * Cout * (CI / 4);
+        for (int j = 0; j < NP; ++j) acc[j] = 0ull;  // (+0, +0)
+        const float *gob = go + (i64)b * Cout * hwo;
+        for (int kh = 0; kh < kH; ++kh) {
+            const int nh = ih + pH - kh;
+            if (nh < 0 || nh % sH != 0 || nh / sH >= Ho) continue;
+            for (int kw = 0; kw < kW; ++kw) {
+                const int nw = iw + pW - kw;
+                if (nw < 0 || nw % sW != 0 || nw / sW >= Wo) continue;
+                const float *gp = gob + (nh / sH) * Wo + nw / sW;
+                const ulonglong2 *wt = reinterpret_cast<const ulonglong2 *>(wsm4) + (i64)(kh * kW + kw) * Cout * (CI / 4);
 #pragma unroll 8
-            for (int oc = 0; oc < Cout; ++oc) {
-                f32x2 wv[NP];
+                for (int oc = 0; oc < Cout; ++oc) {
+                    f32x2 wv[NP];
 #pragma unroll
-                for (int q = 0; q < CI / 4; ++q) {
-                    const ulonglong2 w2 = wt[(CI / 4) * oc + q];
-                    wv[2 * q] = w2.x;
-                    wv[2 * q + 1] = w2.y;
+                    for (int q = 0; q < CI / 4; ++q) {
+                        const ulonglong2 w2 = wt[(CI / 4) * oc + q];
+                        wv[2 * q] = w2.x;
+                        wv[2 * q + 1] = w2.y;
+                    }
+                    const float d = gp[(i64)oc * hwo];
+                    const f32x2 dd = pack2(d, d);
+#pragma unroll
+                    for (int j = 0; j < NP; ++j) acc[j] = add2_rn(acc[j], prod2_rn(dd, wv[j], z));
                 }
-                const float d = gp[(i64)oc * hwo];
-                const f32x2 dd = pack2(d, d);
-#pragma unroll
-                for (int j = 0; j < NP; ++j) acc[j] = add2_rn(acc[j], prod2_rn(dd, wv[j], z));
             }
         }
+        const float ws = *w_s;
+        float a[CI];
+#pragma unroll
+        for (int j = 0; j < NP; ++j) unpack2(acc[j], a[2 * j], a[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < CI; ++j) {
+            const int ci = ci0 + j;
+            if (ci >= Cin) break;
+            const i64 i = ((i64)b * Cin + ci) * hwi + pix;
+            float v = fmul(a[j], ws);
+            if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
+            if (add) v = fadd(v, add[i]);
+            gi[i] = v;
+            if (gmax_out) gmax = fmaxf(gmax, fabsf(fmul(v, *gmax_scale)));
+        }
     }
-    const float ws = *w_s;
-    float a[CI];
-#pragma unroll
-    for (int j = 0; j < NP; ++j) unpack2(acc[j], a[2 * j], a[2 * j + 1]);
-#pragma unroll
-    for (int j = 0; j < CI; ++j) {
-        const int ci = ci0 + j;
-        if (ci >= Cin) break;
-        const i64 i = ((i64)b * Cin + ci) * hwi + pix;
-        float v = fmul(a[j], ws);
-        if (mask_q) v = mask_q[i] > 0 ? v : 0.0f;
-        if (add) v = fadd(v, add[i]);
-        gi[i] = v;
+    if (gmax_out) {
+        // max |gi * gmax_scale| over the launch (the next block's
+        // re-quantisation scale): one atomic per CTA
+        __shared__ float wmax[kDgradThreads / 32];
+        const float m = block_max_f(gmax, wmax);
+        if (threadIdx.x == 0) atomic_max_nonneg(gmax_out, m);
     }
 }
 
@@ -906,7 +918,8 @@ void dgrad_classes(int H, int W, int kh, int kw, int sh, int sw, int ph, int pw,
 
 void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, int H, int W, int Cout, int kh, int kw,
            int sh, int sw, int ph, int pw, int Ho, int Wo, const int *perm, const int *cstart, int ncls,
-           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st) {
+           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st, const float *gmax_scale,
+           float *gmax_out) {
     const i64 npix = (i64)B * H * W;
     if (npix <= 0 || Cin <= 0) return;
     const size_t smem = sizeof(float) * (size_t)kh * kw * Cout * kDgradCi;
@@ -921,7 +934,8 @@ void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, i
     }
     dim3 grid((unsigned)((npix + kDgradThreads - 1) / kDgradThreads), (unsigned)((Cin + kDgradCi - 1) / kDgradCi));
     dgrad_kernel<<<grid, kDgradThreads, smem, st>>>(dy, wT, w_s, B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw, Ho, Wo,
-                                                    perm, cstart, perm ? ncls : 0, mask_q, add, gi, -0.0f);
+                                                    perm, cstart, perm ? ncls : 0, mask_q, add, gi, -0.0f,
+                                                    gmax_out ? gmax_scale : nullptr, gmax_scale ? gmax_out : nullptr);
     TRBA_LAUNCH_CHECK();
 }
 

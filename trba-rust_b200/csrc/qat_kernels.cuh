@@ -80,10 +80,13 @@ void grad_accum(const int32_t *acc, const float *s_dx, const float *s_in, i64 n,
 // order) times w_s, then: mask_q ? (mask_q > 0 ? v : 0) : v, then + add.
 // wT: (float) of the int8 weights at dgrad_weights_index; perm / cstart:
 // the tap-class pixel order of dgrad_classes (device copies), or null for
-// the natural order.
+// the natural order.  With gmax_out, atomically maxes max |gi * *gmax_scale|
+// into *gmax_out (a non-negative f32, zeroed by the caller) — the
+// re-quantisation scale of the block that consumes gi.
 void dgrad(const float *dy, const float *wT, const float *w_s, int B, int Cin, int H, int W, int Cout, int kh, int kw,
            int sh, int sw, int ph, int pw, int Ho, int Wo, const int *perm, const int *cstart, int ncls,
-           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st);
+           const int8_t *mask_q, const float *add, float *gi, cudaStream_t st, const float *gmax_scale = nullptr,
+           float *gmax_out = nullptr);
 // Floats of the input-gradient weight layout [Cin / 16 blocks][taps][Cout][16].
 i64 dgrad_weights_size(int Cin, int Cout, int khw);
 // Index in that layout of weight (oc, ci, tap).

@@ -872,7 +872,11 @@ double valid_taps(int n_in, int k, int s, int pad, int n_out) {
 }
 
 // ConvQat::backward (src/qnet.rs:918-1083).  gi: input gradient (or null).
-void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const float *add, float *gi) {
+// gi: input gradient (or null).  gmax_scale / gmax_out (optional): the input
+// gradient's max |gi * scale| for the block that consumes it, accumulated by
+// the gather's epilogue instead of a separate pass.
+void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const float *add, float *gi,
+              const float *gmax_scale = nullptr, float *gmax_out = nullptr) {
     const int B = c.B, HW = L.Ho * L.Wo;
     const i64 rows = L.rows(B), rp = a16l(rows);
     const bool compat = c.m->cfg.wgrad_mode == 0;
@@ -911,7 +915,7 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
         qat::dgrad(dy, L.wT.get(), L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
                    L.Wo, L.cls_perm.empty() ? nullptr : L.d_perm.get(),
                    L.cls_perm.empty() ? nullptr : L.d_cstart.get(), (int)L.cls_start.size() - 1, mask_q, add, gi,
-                   c.st);
+                   c.st, gmax_scale, gmax_out);
     }
 }
 
@@ -973,13 +977,18 @@ void cnn_backward(Ctx &c) {
     ConvL &o0 = cv[nc - 2], &o1 = cv[nc - 1];
     qat::features_bwd(m->dfeat.get(), o1.q.get(), o1.s_q.get(), c.B, o1.cout, o1.Ho, o1.Wo, m->dy_o1.get(), c.st);
     conv_bwd(c, o1, m->dy_o1.get(), o0.q.get(), nullptr, m->dy_o0.get());
-    conv_bwd(c, o0, m->dy_o0.get(), nullptr, nullptr, m->gv_last.get());
+    // Each block's output gradient is re-quantised with max |gv * s_out|; the
+    // gather that writes gv last accumulates that max in its epilogue.
+    const int nb = (int)m->blocks.size();
+    conv_bwd(c, o0, m->dy_o0.get(), nullptr, nullptr, m->gv_last.get(), nb ? m->blocks[nb - 1].s_out.get() : nullptr,
+             nb ? m->blocks[nb - 1].gvmax.get() : nullptr);
     const float *gv = m->gv_last.get();
-    for (int bi = (int)m->blocks.size() - 1; bi >= 0; --bi) {
+    for (int bi = nb - 1; bi >= 0; --bi) {
         BlockL &bl = m->blocks[bi];
         ConvL &c1 = cv[bl.c1], &c2 = cv[bl.c2];
         const i64 n = (i64)c.B * bl.C * bl.Ho * bl.Wo;
-        qat::grad_quant_max(gv, bl.s_out.get(), n, bl.gvmax.get(), c.st);
+        const float *next_scale = bi > 0 ? m->blocks[bi - 1].s_out.get() : nullptr;
+        float *next_max = bi > 0 ? m->blocks[bi - 1].gvmax.get() : nullptr;
         qat::grad_quant_mask(gv, bl.s_out.get(), bl.gvmax.get(), bl.q_out.get(), n, bl.s_dq.get(), bl.dz.get(), c.st);
         qat::se_backward(bl.dz.get(), c2.y.get(), bl.gate.get(), bl.h1.get(), bl.pool.get(), c.P + bl.w1_off,
                          c.P + bl.w2_off, c.B, bl.C, bl.Ho * bl.Wo, bl.R, bl.dpre1.get(), bl.dpre2.get(),
@@ -990,9 +999,9 @@ void cnn_backward(Ctx &c) {
         if (bl.ds >= 0) {
             conv_bwd(c, c1, bl.dy1.get(), nullptr, nullptr, bl.gin.get());
             // total = gi_in + dx_ds (src/qnet.rs:1345-1349)
-            conv_bwd(c, cv[bl.ds], bl.dz.get(), nullptr, bl.gin.get(), bl.gin.get());
+            conv_bwd(c, cv[bl.ds], bl.dz.get(), nullptr, bl.gin.get(), bl.gin.get(), next_scale, next_max);
         } else {
-            conv_bwd(c, c1, bl.dy1.get(), nullptr, bl.dz.get(), bl.gin.get());
+            conv_bwd(c, c1, bl.dy1.get(), nullptr, bl.dz.get(), bl.gin.get(), next_scale, next_max);
         }
         gv = bl.gin.get();
     }
