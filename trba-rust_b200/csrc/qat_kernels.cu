@@ -561,6 +561,81 @@ __global__ void __launch_bounds__(256) bn_dx_quant_t_kernel(const float *dy, con
     }
 }
 
+// Small-C form of the same operand (C % 4 == 0, HW % 4 == 0, C <= 512): a
+// CTA takes R whole rows of the [rows, C] view, R = (8192 / C) rounded down
+// to 16.  Thread (o, rows 4j..4j+3) quantises four elements of column o (a
+// coalesced read across the warp's consecutive columns) into one 32-bit word
+// of a [C][R + 4] byte tile; each of the C operand rows then receives its R
+// bytes as 16-byte stores.  With C = 16 or 32 the 32 x 32 tiles above leave
+// half their threads idle and write 32-byte row pieces.
+constexpr int kQtElems = 8192;
+__host__ __device__ inline int qt_rows(int C) { return (kQtElems / C) & ~15; }
+
+__global__ void __launch_bounds__(256) bn_dx_quant_tr_kernel(const float *dy, const float *x, const float *mean,
+                                                             const float *var, const float *gamma,
+                                                             const double *acc, int B, int C, int HW,
+                                                             const float *vmax, float *s_dx, int8_t *A, int ld,
+                                                             i64 rows, FastDiv div_hw, FastDiv div_c) {
+    extern __shared__ float chs[];  // [5][C]: m, r, a, sdy, sdxh
+    __shared__ __align__(16) uint32_t tile[(kQtElems + 4 * 512) / 4];  // [C][R + 4] bytes
+    const i64 count = (i64)B * HW;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, count);
+        chs[c] = p.m;
+        chs[C + c] = p.r;
+        chs[2 * C + c] = p.a;
+        chs[3 * C + c] = p.sdy;
+        chs[4 * C + c] = p.sdxh;
+    }
+    __syncthreads();
+    const float sc = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
+    const float inv = fdiv(1.0f, sc);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *s_dx = sc;
+    const float cnt = (float)count;
+    const int R = qt_rows(C), RW = R / 4 + 1;  // tile row stride in words
+    const i64 r0 = (i64)blockIdx.x * R;
+    const int nrows = (int)min((i64)R, rows - r0);
+    const int quads = (nrows + 3) >> 2;
+    for (int k = threadIdx.x; k < C * quads; k += blockDim.x) {
+        const int q4 = k / C, o = k - q4 * C;
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int r = 4 * q4 + j;
+            if (r < nrows) {
+                const uint32_t i = (uint32_t)((r0 + r) * C + o);
+                const uint32_t plane = div_hw.div(i);
+                const int c = (int)(plane - div_c.div(plane) * (uint32_t)C);
+                DxPlane p;
+                p.m = chs[c];
+                p.r = chs[C + c];
+                p.a = chs[2 * C + c];
+                p.sdy = chs[3 * C + c];
+                p.sdxh = chs[4 * C + c];
+                p.cnt = cnt;
+                word |= (uint32_t)(uint8_t)quant_dx(dx_at(p, dy[i], x[i]), inv) << (8 * j);
+            }
+        }
+        tile[o * RW + q4] = word;
+    }
+    __syncthreads();
+    if (nrows == R) {
+        const int cpr = R / 16;  // 16-byte pieces per operand row
+        for (int k = threadIdx.x; k < C * cpr; k += blockDim.x) {
+            const int o = k / cpr, j = k - o * cpr;
+            const uint32_t *t = tile + o * RW + 4 * j;
+            *reinterpret_cast<int4 *>(A + (i64)o * ld + r0 + 16 * j) =
+                make_int4((int)t[0], (int)t[1], (int)t[2], (int)t[3]);
+        }
+    } else {
+        const int8_t *tb = reinterpret_cast<const int8_t *>(tile);
+        for (int k = threadIdx.x; k < C * nrows; k += blockDim.x) {
+            const int o = k / nrows, j = k - o * nrows;
+            A[(i64)o * ld + r0 + j] = tb[4 * o * RW + j];
+        }
+    }
+}
+
 __global__ void grad_accum_kernel(const int32_t *acc, const float *s_dx, const float *s_in, i64 n, float *g) {
     const float deq = fmul(*s_dx, *s_in);
     GRID_LOOP(i, n) g[i] = fadd(g[i], fmul((float)acc[i], deq));
@@ -864,8 +939,15 @@ void bn_dx_quant(const float *dy, const float *x, const float *mean, const float
                  bool compat, cudaStream_t st) {
     if (compat) {
         const i64 rows = (i64)B * HW;
-        dim3 grid((unsigned)((rows + kQtTile - 1) / kQtTile), (unsigned)((C + kQtTile - 1) / kQtTile));
         TRBA_REQUIRE(rows * C < (1ll << 32), "bn_dx_quant: tensor too large for 32-bit indexing");
+        if (C % 4 == 0 && C <= 512 && HW % 4 == 0 && ld % 16 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0) {
+            const int R = qt_rows(C);
+            bn_dx_quant_tr_kernel<<<(unsigned)((rows + R - 1) / R), 256, 5 * C * sizeof(float), st>>>(
+                dy, x, mean, var, gamma, acc, B, C, HW, vmax, s_dx, A, ld, rows, FastDiv::make(HW), FastDiv::make(C));
+            TRBA_LAUNCH_CHECK();
+            return;
+        }
+        dim3 grid((unsigned)((rows + kQtTile - 1) / kQtTile), (unsigned)((C + kQtTile - 1) / kQtTile));
         bn_dx_quant_t_kernel<<<grid, 256, 5 * C * sizeof(float), st>>>(dy, x, mean, var, gamma, acc, B, C, HW, vmax,
                                                                         s_dx, A, ld, rows, FastDiv::make(HW),
                                                                         FastDiv::make(C));

@@ -385,29 +385,48 @@ __device__ __forceinline__ double dot2_d(const float *x, const float *w, int str
     return a0 + a1;
 }
 
+// Shared-memory layout of the decoder kernels.  The per-step vectors that
+// feed dot products (h, context, gate gradients, ...) are kept as f64 copies
+// laid out [k][sample], so that a dot product converts only its weight (an
+// f32 -> f64 conversion runs on the SM's narrow conversion pipe, which bounds
+// these kernels), and a thread that owns one weight column serves every
+// sample of the CTA with one conversion per weight.
 // DECODE = false: teacher-forced forward of the training step (tokens from
 // text_in, every trace stored).  DECODE = true: greedy decoding
 // (src/attn.rs:368-447): the token fed at step s is the argmax (first
 // maximum) of the generator logits of step s-1, sos at step 0; only the
 // per-step argmax tokens are stored.
+// stage bit 0: the CTA's encoder projections [S][T][H] are copied into
+// shared memory once (read at every step); bit 1: the encoder features too.
+constexpr int kAttnRows = 4;  // (sample, t) rows whose warp reductions overlap
+
+__host__ __device__ inline size_t attn_fwd_smem_base(int H, int T, int V, bool decode) {
+    const int S = kAttnS, G4 = 4 * H;
+    return sizeof(double) * ((size_t)2 * H * S + S * T + H) +
+           sizeof(float) * ((size_t)9 * H * H + 16 + 4 * S * H + S * G4 + 2 * S * T + S + (decode ? S * V : 0));
+}
+
 template <bool DECODE>
 __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int stage) {
-    extern __shared__ float sm[];
-    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
-    float *wihT = sm;             // [H][4H], context columns of w_ih, transposed
-    float *whhT = wihT + H * G4;  // [H][4H]
-    float *h2hT = whhT + H * G4;  // [H][H]:  h2hT[j*H + k] = h2h_w[k*H + j]
-    float *h = h2hT + H * H;      // [S][H]
+    extern __shared__ __align__(16) double attn_smd[];
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    constexpr int S = kAttnS;
+    double *hd = attn_smd;        // [H][S] h as f64
+    double *ctxd = hd + H * S;    // [H][S] context as f64
+    double *ald = ctxd + H * S;   // [S][T] alpha as f64
+    double *swd = ald + S * T;    // [H] score weights as f64
+    float *wihT = reinterpret_cast<float *>(swd + H);  // [H][4H], context columns of w_ih, transposed
+    float *whhT = wihT + H * G4 + 16;  // [H][4H] (16 floats apart: the two arrays fall in different banks)
+    float *h2hT = whhT + H * G4;       // [H][H]:  h2hT[j*H + k] = h2h_w[k*H + j]
+    float *h = h2hT + H * H;           // [S][H]
     float *c = h + S * H, *phh = c + S * H, *ctx = phh + S * H;  // [S][H]
     float *pre = ctx + S * H;     // [S][4H]
-    float *tn = pre + S * G4;     // [S][T][H]
-    float *e = tn + S * T * H;    // [S][T]
+    float *e = pre + S * G4;      // [S][T]
     float *al = e + S * T;        // [S][T]
     int *tok = reinterpret_cast<int *>(al + S * T);  // [S]
     float *logit = reinterpret_cast<float *>(tok + S);  // [S][V] (DECODE)
-    // stage != 0: the CTA's encoder projections and features [S][T][H] are
-    // copied into shared memory once (they are read at every step).
-    float *sph = logit + (DECODE ? S * V : 0), *sbh = sph + S * T * H;
+    float *sph = logit + (DECODE ? S * V : 0);
+    float *sbh = sph + ((stage & 1) ? S * T * H : 0);
     const int b0 = blockIdx.x * S;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
@@ -419,44 +438,64 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
         const int k = i / H, j = i - k * H;
         h2hT[j * H + k] = a.h2h_w[i];
     }
-    if (stage) {
-        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
-            const int sl = i / (T * H), r = i - sl * T * H;
-            const i64 g = (i64)min(b0 + sl, a.B - 1) * T * H + r;
-            sph[i] = a.proj_h[g];
-            sbh[i] = a.bh[g];
-        }
+    for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
+        const int sl = i / (T * H), r = i - sl * T * H;
+        const i64 g = (i64)min(b0 + sl, a.B - 1) * T * H + r;
+        if (stage & 1) sph[i] = a.proj_h[g];
+        if (stage & 2) sbh[i] = a.bh[g];
     }
-    for (int i = threadIdx.x; i < S * H; i += blockDim.x) h[i] = c[i] = 0.0f;
+    for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
+        h[i] = c[i] = 0.0f;
+        hd[i] = 0.0;
+    }
+    for (int k = threadIdx.x; k < H; k += blockDim.x) swd[k] = (double)a.score_w[k];
     if (DECODE && threadIdx.x < S) tok[threadIdx.x] = a.sos;
     __syncthreads();
     for (int st = 0; st < a.steps; ++st) {
         // proj_hh = h2h(h) + bias
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
             const int sl = i / H, k = i - sl * H;
-            phh[i] = fadd((float)dot2_d(h + sl * H, h2hT + k, H, H), a.h2h_b[k]);
+            double a0 = 0.0, a1 = 0.0;
+            int j = 0;
+            for (; j + 1 < H; j += 2) {
+                a0 = fma(hd[j * S + sl], (double)h2hT[j * H + k], a0);
+                a1 = fma(hd[(j + 1) * S + sl], (double)h2hT[(j + 1) * H + k], a1);
+            }
+            if (j < H) a0 = fma(hd[j * S + sl], (double)h2hT[j * H + k], a0);
+            phh[i] = fadd((float)(a0 + a1), a.h2h_b[k]);
         }
         if (!DECODE && threadIdx.x < S) {
             const int b = min(b0 + (int)threadIdx.x, a.B - 1);
             tok[threadIdx.x] = a.text_in[(i64)b * a.steps + st];
         }
         __syncthreads();
-        // tanh(proj_H + proj_hh)
-        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
-            const int sl = i / (T * H), r = i - sl * T * H, k = r % H;
-            const int b = b0 + sl;
-            const float ph = stage ? sph[i] : a.proj_h[((i64)min(b, a.B - 1) * T) * H + r];
-            const float v = cr_tanhf(fadd(ph, phh[sl * H + k]));
-            tn[i] = v;
-            if (!DECODE && b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T) * H + r] = v;
-        }
-        __syncthreads();
-        // scores e = tanh(.) . score_w, one warp per (sample, t)
-        for (int p = warp; p < S * T; p += nwarps) {
-            double acc = 0.0;
-            for (int k = lane; k < H; k += 32) acc = fma((double)tn[p * H + k], (double)a.score_w[k], acc);
-            acc = warp_sum_d(acc);
-            if (lane == 0) e[p] = (float)acc;
+        // tanh(proj_H + proj_hh) and the scores e = tanh(.) . score_w, one
+        // warp per (sample, t) row, kAttnRows rows' reductions overlapped
+        for (int p0 = warp; p0 < S * T; p0 += nwarps * kAttnRows) {
+            double acc[kAttnRows];
+#pragma unroll
+            for (int u = 0; u < kAttnRows; ++u) {
+                acc[u] = 0.0;
+                const int p = p0 + u * nwarps;
+                if (p < S * T) {
+                    const int sl = p / T, t = p - sl * T, b = b0 + sl;
+                    const float *php = (stage & 1) ? sph + p * H : a.proj_h + ((i64)min(b, a.B - 1) * T + t) * H;
+                    for (int k = lane; k < H; k += 32) {
+                        const float v = cr_tanhf(fadd(php[k], phh[sl * H + k]));
+                        if (!DECODE && b < a.B) a.tanh_tr[(((i64)st * a.B + b) * T + t) * H + k] = v;
+                        acc[u] = fma((double)v, swd[k], acc[u]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < kAttnRows; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < kAttnRows; ++u)
+                    if (p0 + u * nwarps < S * T) e[p0 + u * nwarps] = (float)acc[u];
+            }
         }
         __syncthreads();
         // softmax over T, one warp per sample
@@ -475,6 +514,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
             for (int t = lane; t < T; t += 32) {
                 const float v = fdiv(al[sl * T + t], sf);
                 al[sl * T + t] = v;
+                ald[sl * T + t] = (double)v;
                 if (!DECODE && b < a.B) a.alpha[((i64)st * a.B + b) * T + t] = v;
             }
         }
@@ -483,14 +523,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
             const int sl = i / H, k = i - sl * H;
             const int b = min(b0 + sl, a.B - 1);
+            const float *bp = (stage & 2) ? sbh + sl * T * H + k : a.bh + (i64)b * T * H + k;
             double acc = 0.0;
-            if (stage) {
-                for (int t = 0; t < T; ++t) acc = fma((double)al[sl * T + t], (double)sbh[(sl * T + t) * H + k], acc);
-            } else {
-                for (int t = 0; t < T; ++t)
-                    acc = fma((double)al[sl * T + t], (double)a.bh[((i64)b * T + t) * H + k], acc);
-            }
-            ctx[i] = (float)acc;
+            for (int t = 0; t < T; ++t) acc = fma(ald[sl * T + t], (double)bp[t * H], acc);
+            const float cv = (float)acc;
+            ctx[i] = cv;
+            ctxd[k * S + sl] = (double)cv;
         }
         __syncthreads();
         if (!DECODE) {
@@ -501,13 +539,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
                         j < H ? ctx[sl * H + j] : (j - H == tok[sl] ? 1.0f : 0.0f);
             }
         }
-        // gate pre-activations: (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h
-        for (int i = threadIdx.x; i < S * G4; i += blockDim.x) {
-            const int sl = i / G4, o = i - sl * G4;
-            const double dc = dot2_d(ctx + sl * H, wihT + o, G4, H);
-            const double dh = dot2_d(h + sl * H, whhT + o, G4, H);
-            pre[i] = fadd(fadd(fadd(fadd(a.b_ih[o], a.b_hh[o]), (float)dc), a.w_ih[(i64)o * CV + H + tok[sl]]),
-                          (float)dh);
+        // gate pre-activations: (b_ih + b_hh) + w_ih[:, :H] ctx + w_ih[:, H + tok] + w_hh h.
+        // Lane pair (2o, 2o+1) owns gate row o: the even lane the context dot,
+        // the odd lane the recurrent dot, both for all S samples (two f64
+        // partial sums over even and odd k, added at the end); a shuffle
+        // swaps the halves and each lane finishes S/2 samples.
+        for (int i = threadIdx.x; i < 2 * G4; i += blockDim.x) {
+            const int o = i >> 1, dsel = i & 1;
+            const float *wcol = (dsel ? whhT : wihT) + o;
+            const double *xd = dsel ? hd : ctxd;
+            double a0[S], a1[S];
+#pragma unroll
+            for (int q = 0; q < S; ++q) a0[q] = a1[q] = 0.0;
+            int k = 0;
+            for (; k + 1 < H; k += 2) {
+                const double w0 = (double)wcol[k * G4], w1 = (double)wcol[(k + 1) * G4];
+                const double2 *x0 = reinterpret_cast<const double2 *>(xd + k * S);
+                const double2 *x1 = reinterpret_cast<const double2 *>(xd + (k + 1) * S);
+#pragma unroll
+                for (int q = 0; q < S / 2; ++q) {
+                    const double2 u0 = x0[q], u1 = x1[q];
+                    a0[2 * q] = fma(u0.x, w0, a0[2 * q]);
+                    a0[2 * q + 1] = fma(u0.y, w0, a0[2 * q + 1]);
+                    a1[2 * q] = fma(u1.x, w1, a1[2 * q]);
+                    a1[2 * q + 1] = fma(u1.y, w1, a1[2 * q + 1]);
+                }
+            }
+            if (k < H) {
+                const double w0 = (double)wcol[k * G4];
+#pragma unroll
+                for (int q = 0; q < S; ++q) a0[q] = fma(xd[k * S + q], w0, a0[q]);
+            }
+            const float bsum = fadd(a.b_ih[o], a.b_hh[o]);
+#pragma unroll
+            for (int q = 0; q < S; ++q) {
+                const double mine = a0[q] + a1[q];
+                const double other = __shfl_xor_sync(0xffffffffu, mine, 1);
+                if ((q >= S / 2) == (dsel != 0)) {
+                    const double dc = dsel ? other : mine, dh = dsel ? mine : other;
+                    pre[q * G4 + o] = fadd(fadd(fadd(bsum, (float)dc), a.w_ih[(i64)o * CV + H + tok[q]]), (float)dh);
+                }
+            }
         }
         __syncthreads();
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
@@ -527,6 +599,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
             }
             c[i] = cn;
             h[i] = hn;
+            hd[k * S + sl] = (double)hn;
         }
         __syncthreads();
         if (DECODE) {
@@ -568,19 +641,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(AttnFwd a, int s
     }
 }
 
+__host__ __device__ inline size_t attn_bwd_smem_base(int H, int T) {
+    const int S = kAttnS, G4 = 4 * H;
+    return sizeof(double) * ((size_t)G4 * S + 2 * H * S) +
+           sizeof(float) * ((size_t)9 * H * H + 4 * S * H + 3 * S * T + 2 * S * T * H);
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwd a, int stage) {
-    extern __shared__ float sm[];
-    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V, S = kAttnS;
-    float *wc = sm;                 // [4H][H] context columns of w_ih
-    float *whh = wc + G4 * H;       // [4H][H]
-    float *h2h = whh + G4 * H;      // [H][H]
-    float *dhn = h2h + H * H;       // [S][H]
-    float *dcn = dhn + S * H, *dctx = dcn + S * H, *dhp = dctx + S * H, *dphh = dhp + S * H;  // [S][H]
-    float *dg = dphh + S * H;       // [S][4H]
-    float *da = dg + S * G4, *de = da + S * T, *dot = de + S * T;  // [S][T], [S][T], [S]
-    float *acc_bh = dot + S, *acc_ph = acc_bh + S * T * H;        // [S][T][H]
-    float *als = acc_ph + S * T * H;                              // [S][T] alpha of the step
-    float *sbh = als + S * T;                                     // [S][T][H] when stage != 0
+    extern __shared__ __align__(16) double attn_smd[];
+    const int H = a.H, T = a.T, V = a.V, G4 = 4 * H, CV = H + V;
+    constexpr int S = kAttnS;
+    double *dgd = attn_smd;          // [4H][S] gate gradients as f64
+    double *dctxd = dgd + G4 * S;    // [H][S] d context as f64
+    double *dphhd = dctxd + H * S;   // [H][S] d proj_hh as f64
+    float *wc = reinterpret_cast<float *>(dphhd + H * S);  // [4H][H] context columns of w_ih
+    float *whh = wc + G4 * H;        // [4H][H]
+    float *h2h = whh + G4 * H;       // [H][H]
+    float *dhn = h2h + H * H;        // [S][H]
+    float *dcn = dhn + S * H, *dctx = dcn + S * H, *dhp = dctx + S * H;  // [S][H]
+    float *da = dhp + S * H, *de = da + S * T;                            // [S][T]
+    float *acc_bh = de + S * T, *acc_ph = acc_bh + S * T * H;             // [S][T][H]
+    float *als = acc_ph + S * T * H;                                      // [S][T] alpha of the step
+    float *sbh = als + S * T;                                             // [S][T][H] when stage != 0
     const int b0 = blockIdx.x * S;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int i = threadIdx.x; i < G4 * H; i += blockDim.x) {
@@ -613,46 +695,76 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwd a, int s
             const float cp = st > 0 ? a.cs[(sb - a.B) * H + k] : 0.0f;
             const float dh = fadd(a.d_out_hid[sb * H + k], dhn[i]);
             const float dc = fadd(fmul(fmul(dh, og), fsub(1.0f, fmul(tc, tc))), fmul(dcn[i], fg));
-            float *d = dg + sl * G4;
-            d[k] = fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
-            d[H + k] = fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
-            d[2 * H + k] = fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
-            d[3 * H + k] = fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
+            dgd[k * S + sl] = (double)fmul(fmul(fmul(dc, cg), ig), fsub(1.0f, ig));
+            dgd[(H + k) * S + sl] = (double)fmul(fmul(fmul(dc, cp), fg), fsub(1.0f, fg));
+            dgd[(2 * H + k) * S + sl] = (double)fmul(fmul(dc, ig), fsub(1.0f, fmul(cg, cg)));
+            dgd[(3 * H + k) * S + sl] = (double)fmul(fmul(fmul(dh, tc), og), fsub(1.0f, og));
             dcn[i] = dc;
         }
         __syncthreads();
         for (int i = threadIdx.x; i < S * G4; i += blockDim.x) {
             const int sl = i / G4, o = i - sl * G4, b = b0 + sl;
-            if (b < a.B) a.dgates[((i64)st * a.B + b) * G4 + o] = dg[i];
+            if (b < a.B) a.dgates[((i64)st * a.B + b) * G4 + o] = (float)dgd[o * S + sl];
         }
-        // d ctx = w_ih[:, :H]^T dg, d h_prev (direct) = w_hh^T dg
-        for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
-            const int sl = i / H, k = i - sl * H;
-            const float *d = dg + sl * G4;
-            double s1a = 0.0, s1b = 0.0, s2a = 0.0, s2b = 0.0;
-            for (int o = 0; o < G4; o += 2) {
-                const double d0 = (double)d[o], d1 = (double)d[o + 1];
-                s1a = fma(d0, (double)wc[o * H + k], s1a);
-                s1b = fma(d1, (double)wc[(o + 1) * H + k], s1b);
-                s2a = fma(d0, (double)whh[o * H + k], s2a);
-                s2b = fma(d1, (double)whh[(o + 1) * H + k], s2b);
+        // d ctx = w_ih[:, :H]^T dg, d h_prev (direct) = w_hh^T dg.  Item
+        // ((dot, half, k), parity): the f64 partial sum over the gate rows o
+        // of one parity for the samples of one half; the lane pair adds its
+        // even and odd partial sums.
+        for (int i = threadIdx.x; i < 8 * H; i += blockDim.x) {
+            const int parity = i & 1, r = i >> 1;
+            const int k = r % H, dh2 = r / H, half = dh2 & 1, dsel = dh2 >> 1;
+            const float *wm = (dsel ? whh : wc) + k;
+            double s0 = 0.0, s1 = 0.0;
+            for (int o = parity; o < G4; o += 2) {
+                const double w = (double)wm[o * H];
+                const double2 x = *reinterpret_cast<const double2 *>(dgd + o * S + 2 * half);
+                s0 = fma(x.x, w, s0);
+                s1 = fma(x.y, w, s1);
             }
-            dctx[i] = (float)(s1a + s1b);
-            dhp[i] = (float)(s2a + s2b);
+            const double t0 = s0 + __shfl_xor_sync(0xffffffffu, s0, 1);
+            const double t1 = s1 + __shfl_xor_sync(0xffffffffu, s1, 1);
+            if (parity == 0) {
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int sl = 2 * half + q;
+                    const float v = (float)(q ? t1 : t0);
+                    if (dsel) {
+                        dhp[sl * H + k] = v;
+                    } else {
+                        dctx[sl * H + k] = v;
+                        dctxd[k * S + sl] = (double)v;
+                    }
+                }
+            }
         }
         __syncthreads();
-        // d alpha = d ctx . bh[t], one warp per (sample, t); acc_bh += alpha * d ctx
-        for (int p = warp; p < S * T; p += nwarps) {
-            const int sl = p / T, t = p - sl * T, b = min(b0 + sl, a.B - 1);
-            double acc = 0.0;
-            const float *bht = stage ? sbh + (sl * T + t) * H : a.bh + ((i64)b * T + t) * H;
-            for (int k = lane; k < H; k += 32) acc = fma((double)dctx[sl * H + k], (double)bht[k], acc);
-            acc = warp_sum_d(acc);
-            if (lane == 0) da[p] = (float)acc;
-        }
-        for (int i = threadIdx.x; i < S * T * H; i += blockDim.x) {
-            const int sl = i / (T * H), r = i - sl * T * H, t = r / H, k = r - t * H;
-            acc_bh[i] = fadd(acc_bh[i], fmul(als[sl * T + t], dctx[sl * H + k]));
+        // d alpha = d ctx . bh[t] and acc_bh += alpha * d ctx, one warp per
+        // (sample, t) row, kAttnRows rows' reductions overlapped
+        for (int p0 = warp; p0 < S * T; p0 += nwarps * kAttnRows) {
+            double acc[kAttnRows];
+#pragma unroll
+            for (int u = 0; u < kAttnRows; ++u) {
+                acc[u] = 0.0;
+                const int p = p0 + u * nwarps;
+                if (p < S * T) {
+                    const int sl = p / T, t = p - sl * T, b = min(b0 + sl, a.B - 1);
+                    const float *bht = stage ? sbh + p * H : a.bh + ((i64)b * T + t) * H;
+                    const float alv = als[p];
+                    for (int k = lane; k < H; k += 32) {
+                        acc[u] = fma(dctxd[k * S + sl], (double)bht[k], acc[u]);
+                        acc_bh[p * H + k] = fadd(acc_bh[p * H + k], fmul(alv, dctx[sl * H + k]));
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < kAttnRows; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < kAttnRows; ++u)
+                    if (p0 + u * nwarps < S * T) da[p0 + u * nwarps] = (float)acc[u];
+            }
         }
         __syncthreads();
         // softmax backward, one warp per sample: de = alpha (d alpha - alpha . d alpha)
@@ -684,14 +796,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_bwd_kernel(AttnBwd a, int s
                 if (d != 0.0f) acc_ph[(sl * T + t) * H + k] = fadd(acc_ph[(sl * T + t) * H + k], term);
                 sum += (double)term;
             }
-            dphh[i] = (float)sum;
+            dphhd[k * S + sl] = (double)(float)sum;
             if (b0 + sl < a.B) a.dprojhh[((i64)st * a.B + b) * H + k] = (float)sum;
         }
         __syncthreads();
         // d h_prev += h2h^T d proj_hh
         for (int i = threadIdx.x; i < S * H; i += blockDim.x) {
             const int sl = i / H, j = i - sl * H;
-            dhn[i] = fadd(dhp[i], (float)dot2_d(dphh + sl * H, h2h + j, H, H));
+            double a0 = 0.0, a1 = 0.0;
+            int k = 0;
+            for (; k + 1 < H; k += 2) {
+                a0 = fma(dphhd[k * S + sl], (double)h2h[k * H + j], a0);
+                a1 = fma(dphhd[(k + 1) * S + sl], (double)h2h[(k + 1) * H + j], a1);
+            }
+            if (k < H) a0 = fma(dphhd[k * S + sl], (double)h2h[k * H + j], a0);
+            dhn[i] = fadd(dhp[i], (float)(a0 + a1));
         }
         __syncthreads();
     }
@@ -949,12 +1068,19 @@ void lstm_bwd(const float *dcat, const float *gates, const float *c, const float
     TRBA_LAUNCH_CHECK();
 }
 
+static int attn_fwd_stage(size_t base, size_t block, size_t *total) {
+    int stage = 0;
+    *total = base;
+    if (*total + block <= kAttnMaxSmem) stage |= 1, *total += block;
+    if (*total + block <= kAttnMaxSmem) stage |= 2, *total += block;
+    return stage;
+}
+
 void attn_fwd(const AttnFwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, S = kAttnS;
-    const size_t smem = sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S);
-    const size_t stage_bytes = sizeof(float) * 2 * (size_t)S * T * H;
-    const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
-    const size_t total = smem + (stage ? stage_bytes : 0);
+    TRBA_REQUIRE(H % 4 == 0, "attn_fwd: hidden size must be a multiple of 4 (gate rows fill whole warps)");
+    size_t total = 0;
+    const int stage = attn_fwd_stage(attn_fwd_smem_base(H, T, a.V, false), sizeof(float) * (size_t)S * T * H, &total);
     TRBA_REQUIRE(total <= kAttnMaxSmem, "attn_fwd: hidden / encoder length too large for shared memory");
     set_smem((const void *)attn_fwd_kernel<false>, total);
     attn_fwd_kernel<false><<<(a.B + S - 1) / S, kAttnThreads, total, st>>>(a, stage);
@@ -962,12 +1088,10 @@ void attn_fwd(const AttnFwd &a, cudaStream_t st) {
 }
 
 void attn_decode(const AttnFwd &a, cudaStream_t st) {
-    const int H = a.H, T = a.T, V = a.V, S = kAttnS;
-    const size_t smem =
-        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (4 * H + 4 * H + T * H + 2 * T) + S + (size_t)S * V);
-    const size_t stage_bytes = sizeof(float) * 2 * (size_t)S * T * H;
-    const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
-    const size_t total = smem + (stage ? stage_bytes : 0);
+    const int H = a.H, T = a.T, S = kAttnS;
+    TRBA_REQUIRE(H % 4 == 0, "attn_decode: hidden size must be a multiple of 4 (gate rows fill whole warps)");
+    size_t total = 0;
+    const int stage = attn_fwd_stage(attn_fwd_smem_base(H, T, a.V, true), sizeof(float) * (size_t)S * T * H, &total);
     TRBA_REQUIRE(total <= kAttnMaxSmem, "attn_decode: hidden / encoder length too large for shared memory");
     set_smem((const void *)attn_fwd_kernel<true>, total);
     attn_fwd_kernel<true><<<(a.B + S - 1) / S, kAttnThreads, total, st>>>(a, stage);
@@ -976,8 +1100,8 @@ void attn_decode(const AttnFwd &a, cudaStream_t st) {
 
 void attn_bwd(const AttnBwd &a, cudaStream_t st) {
     const int H = a.H, T = a.T, S = kAttnS;
-    const size_t smem =
-        sizeof(float) * ((size_t)8 * H * H + H * H + (size_t)S * (5 * H + 4 * H + 3 * T + 1 + 2 * T * H));
+    TRBA_REQUIRE(H % 4 == 0, "attn_bwd: hidden size must be a multiple of 4 (gate-gradient items fill whole warps)");
+    const size_t smem = attn_bwd_smem_base(H, T);
     const size_t stage_bytes = sizeof(float) * (size_t)S * T * H;
     const int stage = smem + stage_bytes <= kAttnMaxSmem ? 1 : 0;
     const size_t total = smem + (stage ? stage_bytes : 0);
