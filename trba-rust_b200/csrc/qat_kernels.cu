@@ -272,72 +272,105 @@ __global__ void se_forward_kernel(const float *pool, const float *w1, const floa
 }
 
 // ------------------------------------------------------------ backward --
-__global__ void grad_quant_max_kernel(const float *gv, const float *s_out, i64 n, float *vmax) {
-    __shared__ float smf[32];
-    const float s = *s_out;
-    float mx = 0.0f;
-    GRID_LOOP(i, n) mx = fmaxf(mx, fabsf(fmul(gv[i], s)));
-    const float m = block_max_f(mx, smf);
-    if (threadIdx.x == 0) atomic_max_nonneg(vmax, m);
-}
+// Block-gradient entry and SE backward in one pass over each sample
+// (src/qnet.rs:1684-1708, 1290-1296 and 1298-1330).  One CTA per sample:
+//   dz = q_out > 0 ? rint(clamp(gv * s_out / s_dq)) * s_dq : 0, written out
+//     (the residual and downsample gradients read it later), with
+//     s_dq = max(vmax / 127, 1e-12), vmax = max |gv * s_out| over the batch
+//     (accumulated by the gather that wrote gv);
+//   the squeeze sum over each plane of dz * y2 (f64), one warp per plane,
+//     kSeRows planes' reductions overlapped;
+//   the excitation MLP backward (one warp per hidden unit, then one thread
+//     per channel) and dy2_full = dz * gate + dpooled / HW.
+constexpr int kSeRows = 4;
 
-__global__ void grad_quant_mask_kernel(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out,
-                                       i64 n, float *s_dq_out, float *dz) {
+__global__ void __launch_bounds__(256) se_backward_kernel(
+    const float *__restrict__ gv, const float *__restrict__ s_out, const float *__restrict__ vmax,
+    const int8_t *__restrict__ q_out, float *__restrict__ s_dq_out, float *dz,
+    const float *__restrict__ y2, const float *__restrict__ gate, const float *__restrict__ h1,
+    const float *__restrict__ w1, const float *__restrict__ w2, int C, int HW, int R, float *__restrict__ dpre1,
+    float *__restrict__ dpre2, float *__restrict__ dpooled, float *__restrict__ dy2_full) {
+    extern __shared__ float sm[];
+    float *s_dp2 = sm, *s_dp1 = sm + C, *s_gate = sm + C + R, *s_add = s_gate + C;
+    const int b = blockIdx.x;
+    const i64 base = (i64)b * C * HW;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const float s = *s_out;
     const float sdq = fmaxf(fdiv(*vmax, 127.0f), 1e-12f);
     const float inv = fdiv(1.0f, sdq);
-    if (blockIdx.x == 0 && threadIdx.x == 0 && s_dq_out) *s_dq_out = sdq;
-    GRID_LOOP(i, n) {
-        const float v = fmul(gv[i], s);
-        const int qd = rint_even(fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f));
-        dz[i] = q_out[i] > 0 ? fmul((float)qd, sdq) : 0.0f;
-    }
-}
-
-// One CTA per sample: SE squeeze of dz*y2, the excitation MLP backward and
-// dy2_full = dz*gate + dpooled/HW over the sample's planes.
-__global__ void se_backward_kernel(const float *dz, const float *y2, const float *gate, const float *h1,
-                                   const float *w1, const float *w2, int C, int HW, int R, float *dpre1,
-                                   float *dpre2, float *dpooled, float *dy2_full) {
-    extern __shared__ float sm[];
-    float *s_dp2 = sm, *s_dp1 = sm + C, *s_dpool = sm + C + R;
-    const int b = blockIdx.x;
-    const i64 base = (i64)b * C * HW;
-    // one warp per plane: lane-strided (coalesced) products, f64 warp sum
-    const int lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    for (int c = threadIdx.x >> 5; c < C; c += nwarps) {
-        const float *pz = dz + base + (i64)c * HW, *py = y2 + base + (i64)c * HW;
-        double s = 0.0;
-        for (int j = lane; j < HW; j += 32) s += (double)fmul(pz[j], py[j]);
-        s = warp_sum_d(s);
+    if (b == 0 && threadIdx.x == 0 && s_dq_out) *s_dq_out = sdq;
+    for (int c0 = warp; c0 < C; c0 += nwarps * kSeRows) {
+        double acc[kSeRows];
+#pragma unroll
+        for (int u = 0; u < kSeRows; ++u) {
+            acc[u] = 0.0;
+            const int c = c0 + u * nwarps;
+            if (c < C) {
+                const i64 pb = base + (i64)c * HW;
+                for (int j = lane; j < HW; j += 32) {
+                    const float v = fmul(gv[pb + j], s);
+                    const int qd = rint_even(fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f));
+                    const float d = q_out[pb + j] > 0 ? fmul((float)qd, sdq) : 0.0f;
+                    dz[pb + j] = d;
+                    acc[u] += (double)fmul(d, y2[pb + j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < kSeRows; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
         if (lane == 0) {
-            const float pm = (float)(s / (double)HW);
-            const float dgate = fmul(pm, (float)HW);
-            const float g = gate[(i64)b * C + c];
-            const float d2 = fmul(fmul(dgate, g), fsub(1.0f, g));
-            s_dp2[c] = d2;
-            dpre2[(i64)b * C + c] = d2;
+#pragma unroll
+            for (int u = 0; u < kSeRows; ++u) {
+                const int c = c0 + u * nwarps;
+                if (c >= C) break;
+                const float pm = (float)(acc[u] / (double)HW);
+                const float dgate = fmul(pm, (float)HW);
+                const float g = gate[(i64)b * C + c];
+                const float d2 = fmul(fmul(dgate, g), fsub(1.0f, g));
+                s_dp2[c] = d2;
+                s_gate[c] = g;
+                dpre2[(i64)b * C + c] = d2;
+            }
         }
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < R; j += blockDim.x) {
+    for (int j = warp; j < R; j += nwarps) {
         double acc = 0.0;
-        for (int c = 0; c < C; ++c) acc = fma((double)s_dp2[c], (double)w2[(i64)c * R + j], acc);
-        const float d1 = h1[(i64)b * R + j] > 0.0f ? (float)acc : 0.0f;
-        s_dp1[j] = d1;
-        dpre1[(i64)b * R + j] = d1;
+        for (int c = lane; c < C; c += 32) acc = fma((double)s_dp2[c], (double)w2[(i64)c * R + j], acc);
+        acc = warp_sum_d(acc);
+        if (lane == 0) {
+            const float d1 = h1[(i64)b * R + j] > 0.0f ? (float)acc : 0.0f;
+            s_dp1[j] = d1;
+            dpre1[(i64)b * R + j] = d1;
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < C; i += blockDim.x) {
         double acc = 0.0;
         for (int j = 0; j < R; ++j) acc = fma((double)s_dp1[j], (double)w1[(i64)j * C + i], acc);
-        s_dpool[i] = (float)acc;
-        dpooled[(i64)b * C + i] = (float)acc;
+        const float dp = (float)acc;
+        dpooled[(i64)b * C + i] = dp;
+        s_add[i] = fdiv(dp, (float)HW);
     }
     __syncthreads();
-    for (i64 e = threadIdx.x; e < (i64)C * HW; e += blockDim.x) {
-        const int c = (int)(e / HW);
-        dy2_full[base + e] = fadd(fmul(dz[base + e], gate[(i64)b * C + c]), fdiv(s_dpool[c], (float)HW));
+    if ((HW & 3) == 0) {
+        const int hw4 = HW >> 2;
+        const float4 *z4 = reinterpret_cast<const float4 *>(dz + base);
+        float4 *o4 = reinterpret_cast<float4 *>(dy2_full + base);
+        for (int e = threadIdx.x; e < C * hw4; e += blockDim.x) {
+            const int c = e / hw4;
+            const float g = s_gate[c], ad = s_add[c];
+            const float4 z = z4[e];
+            o4[e] = make_float4(fadd(fmul(z.x, g), ad), fadd(fmul(z.y, g), ad), fadd(fmul(z.z, g), ad),
+                                fadd(fmul(z.w, g), ad));
+        }
+    } else {
+        for (int e = threadIdx.x; e < C * HW; e += blockDim.x) {
+            const int c = e / HW;
+            dy2_full[base + e] = fadd(fmul(dz[base + e], s_gate[c]), s_add[c]);
+        }
     }
 }
 
@@ -890,23 +923,14 @@ void se_forward(const float *pool, const float *w1, const float *w2, int B, int 
     TRBA_LAUNCH_CHECK();
 }
 
-void grad_quant_max(const float *gv, const float *s_out, i64 n, float *vmax, cudaStream_t st) {
-    grad_quant_max_kernel<<<grid_for(n), 256, 0, st>>>(gv, s_out, n, vmax);
-    TRBA_LAUNCH_CHECK();
-}
-
-void grad_quant_mask(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out, i64 n,
-                     float *s_dq_out, float *dz, cudaStream_t st) {
-    grad_quant_mask_kernel<<<grid_for(n), 256, 0, st>>>(gv, s_out, vmax, q_out, n, s_dq_out, dz);
-    TRBA_LAUNCH_CHECK();
-}
-
-void se_backward(const float *dz, const float *y2, const float *gate, const float *h1, const float *pool,
-                 const float *w1, const float *w2, int B, int C, int HW, int R, float *dpre1, float *dpre2,
-                 float *dpooled, float *dy2_full, cudaStream_t st) {
-    (void)pool;
-    se_backward_kernel<<<B, 256, (2 * C + R) * sizeof(float), st>>>(dz, y2, gate, h1, w1, w2, C, HW, R, dpre1, dpre2,
-                                                                   dpooled, dy2_full);
+void se_backward(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out, float *s_dq_out,
+                 float *dz, const float *y2, const float *gate, const float *h1, const float *w1, const float *w2,
+                 int B, int C, int HW, int R, float *dpre1, float *dpre2, float *dpooled, float *dy2_full,
+                 cudaStream_t st) {
+    TRBA_REQUIRE((i64)C * HW < (1ll << 31), "se_backward: sample plane set too large for 32-bit indexing");
+    se_backward_kernel<<<B, 256, (3 * C + R) * sizeof(float), st>>>(gv, s_out, vmax, q_out, s_dq_out, dz, y2, gate,
+                                                                   h1, w1, w2, C, HW, R, dpre1, dpre2, dpooled,
+                                                                   dy2_full);
     TRBA_LAUNCH_CHECK();
 }
 

@@ -50,17 +50,15 @@ void act_quant(const Src &s, int B, const float *vmax, float *s_out, int8_t *q, 
 void se_forward(const float *pool, const float *w1, const float *w2, int B, int C, int R, float *h1, float *gate,
                 cudaStream_t st);
 
-// Block-gradient entry (src/qnet.rs:1684-1708 + 1290-1296): v = gv * s_out;
-// pass A: vmax = max|v|; pass B: s_dq = max(vmax/127,1e-12),
-// dq = rint(clamp(v/s_dq)), dz = q_out > 0 ? dq * s_dq : 0.
-void grad_quant_max(const float *gv, const float *s_out, i64 n, float *vmax, cudaStream_t st);
-void grad_quant_mask(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out, i64 n,
-                     float *s_dq_out, float *dz, cudaStream_t st);
-
-// SE backward (src/qnet.rs:1298-1330).
-void se_backward(const float *dz, const float *y2, const float *gate, const float *h1, const float *pool,
-                 const float *w1, const float *w2, int B, int C, int HW, int R, float *dpre1, float *dpre2,
-                 float *dpooled, float *dy2_full, cudaStream_t st);
+// Block-gradient entry and SE backward (src/qnet.rs:1684-1708, 1290-1296,
+// 1298-1330) in one kernel: v = gv * s_out, s_dq = max(vmax/127, 1e-12),
+// dq = rint(clamp(v/s_dq)), dz = q_out > 0 ? dq * s_dq : 0 (written), then
+// the SE squeeze / excitation backward and dy2_full = dz*gate + dpooled/HW.
+// vmax = max |gv * s_out| over the batch, accumulated by the producer of gv.
+void se_backward(const float *gv, const float *s_out, const float *vmax, const int8_t *q_out, float *s_dq_out,
+                 float *dz, const float *y2, const float *gate, const float *h1, const float *w1, const float *w2,
+                 int B, int C, int HW, int R, float *dpre1, float *dpre2, float *dpooled, float *dy2_full,
+                 cudaStream_t st);
 void se_weight_grads(const float *dpre1, const float *dpre2, const float *h1, const float *pool, int B, int C, int R,
                      float *g_w1, float *g_w2, cudaStream_t st);
 

@@ -986,13 +986,11 @@ void cnn_backward(Ctx &c) {
     for (int bi = nb - 1; bi >= 0; --bi) {
         BlockL &bl = m->blocks[bi];
         ConvL &c1 = cv[bl.c1], &c2 = cv[bl.c2];
-        const i64 n = (i64)c.B * bl.C * bl.Ho * bl.Wo;
         const float *next_scale = bi > 0 ? m->blocks[bi - 1].s_out.get() : nullptr;
         float *next_max = bi > 0 ? m->blocks[bi - 1].gvmax.get() : nullptr;
-        qat::grad_quant_mask(gv, bl.s_out.get(), bl.gvmax.get(), bl.q_out.get(), n, bl.s_dq.get(), bl.dz.get(), c.st);
-        qat::se_backward(bl.dz.get(), c2.y.get(), bl.gate.get(), bl.h1.get(), bl.pool.get(), c.P + bl.w1_off,
-                         c.P + bl.w2_off, c.B, bl.C, bl.Ho * bl.Wo, bl.R, bl.dpre1.get(), bl.dpre2.get(),
-                         bl.dpooled.get(), bl.dy2.get(), c.st);
+        qat::se_backward(gv, bl.s_out.get(), bl.gvmax.get(), bl.q_out.get(), bl.s_dq.get(), bl.dz.get(), c2.y.get(),
+                         bl.gate.get(), bl.h1.get(), c.P + bl.w1_off, c.P + bl.w2_off, c.B, bl.C, bl.Ho * bl.Wo, bl.R,
+                         bl.dpre1.get(), bl.dpre2.get(), bl.dpooled.get(), bl.dy2.get(), c.st);
         qat::se_weight_grads(bl.dpre1.get(), bl.dpre2.get(), bl.h1.get(), bl.pool.get(), c.B, bl.C, bl.R,
                              c.G + bl.w1_off, c.G + bl.w2_off, c.st);
         conv_bwd(c, c2, bl.dy2.get(), c1.q.get(), nullptr, bl.dy1.get());
