@@ -161,6 +161,67 @@ struct EpiConvF32 {
             if (sm[kMaxN + i] != 0.0) atomicAdd(bn_acc + N + i, sm[kMaxN + i]);
         }
     }
+    // Row accumulation (BN = 32, one n block): an epilogue warp drains the
+    // same 16 columns of every tile it takes; each lane adds its rows'
+    // values and squares to f64 partial sums held in registers, and the warp
+    // reduces them across lanes once, at the end.
+    static constexpr bool kRowAccum = true;
+    struct Accum {
+        double s[16], q[16];
+    };
+    __device__ void acc_init(Accum &a) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a.s[j] = a.q[j] = 0.0;
+    }
+    // columns [col, col + 16) of the tile row, taken from v[16 hi + j]
+    __device__ void store_acc(int row, int col, int M, int N, const uint32_t (&v)[32], bool hi, Accum &a) {
+        const float scale = fmul(*s_in, *w_s);
+        if (row >= M) return;
+        const int b = row / HW, p = row - b * HW;
+        float *xp = x + ((i64)b * N + col) * HW + p;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (col + j < N) {
+                const float val = fmul((float)(int32_t)(hi ? v[16 + j] : v[j]), scale);
+                xp[(i64)j * HW] = val;
+                const double d = (double)val;
+                a.s[j] += d;
+                a.q[j] = fma(d, d, a.q[j]);
+            }
+        }
+    }
+    __device__ void acc_flush(Accum &a, int col, int N, int lane, double *sm) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            a.s[j] += __shfl_xor_sync(0xffffffffu, a.s[j], 16);
+            a.q[j] += __shfl_xor_sync(0xffffffffu, a.q[j], 16);
+        }
+        // reduce-scatter over the 16 lanes left: lane l ends with column l & 15
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1) {
+            const bool upper = lane & w;
+#pragma unroll
+            for (int j = 0; j < w; ++j) {
+                const double ss = upper ? a.s[j] : a.s[j + w], ks = upper ? a.s[j + w] : a.s[j];
+                const double sq = upper ? a.q[j] : a.q[j + w], kq = upper ? a.q[j + w] : a.q[j];
+                a.s[j] = ks + __shfl_xor_sync(0xffffffffu, ss, w);
+                a.q[j] = kq + __shfl_xor_sync(0xffffffffu, sq, w);
+            }
+        }
+        if (lane < 16 && col + lane < N) {
+            atomicAdd(sm + col + lane, a.s[0]);
+            atomicAdd(sm + kMaxN + col + lane, a.q[0]);
+        }
+    }
+};
+
+template <class Epi, class = void>
+struct HasRowAccum {
+    static constexpr bool value = false;
+};
+template <class Epi>
+struct HasRowAccum<Epi, decltype(void(Epi::kRowAccum))> {
+    static constexpr bool value = Epi::kRowAccum;
 };
 
 // Fused inference epilogue of the conv path (cuda/kernels.cu:434-466,
@@ -361,7 +422,40 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         // alternate tiles instead (the tiles of accumulator 0, of 1), so two
         // tiles drain at once; the other half only releases the accumulator.
         uint32_t acc = 0, acc_ph = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        bool row_accum = false;
+        if constexpr (HasRowAccum<Epi>::value && BN == 32) row_accum = n_tiles == 1 && sh.splits == 1;
+        if constexpr (HasRowAccum<Epi>::value && BN == 32) {
+            if (row_accum) {
+                // N <= 16: the halves take alternate tiles, columns [0, 16).
+                // N > 16: both halves take every tile, half h columns [16 h, +16).
+                const bool alt = N <= 16;
+                const int c0 = alt ? 0 : 16 * half;
+                typename Epi::Accum st;
+                epi.acc_init(st);
+                for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                    int m0, n0, kb0, kb1;
+                    tile_coords(t, m0, n0, kb0, kb1);
+                    const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort);
+                    __syncwarp();
+                    if (!__all_sync(0xffffffffu, ok)) break;
+                    tc_fence_after();
+                    const bool mine = !alt || (int)acc == half;
+                    if (mine && c0 < N && kb0 < kb1) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + acc * BN, v);
+                        tmem_ld_wait();
+                        epi.store_acc(m0 + q * 32 + lane, c0, M, N, v, c0 != 0, st);
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&ctl->tempty[acc]);
+                    acc ^= 1u;
+                    if (acc == 0) acc_ph ^= 1u;
+                }
+                __syncwarp();
+                epi.acc_flush(st, c0, N, lane, epi_sm);
+            }
+        }
+        for (int t = blockIdx.x; t < tiles && !row_accum; t += gridDim.x) {
             int m0, n0, kb0, kb1;
             tile_coords(t, m0, n0, kb0, kb1);
             const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort);
