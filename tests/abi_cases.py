@@ -47,6 +47,8 @@ def conv_geoms():
         (1, 8, 2, 10, 8, 2, 2, 1, 1, 0, 0),  # conv_out.3 geometry
         (2, 16, 6, 13, 4, 3, 3, 1, 1, 1, 1),  # stem.3 channel count (row-per-thread im2col)
         (2, 3, 7, 9, 4, 3, 3, 2, 2, 1, 1),    # 3 channels, strided
+        (2, 16, 5, 12, 4, 3, 3, 1, 1, 1, 1),  # stem.3 form, W % 4 == 0 (four-pixel im2col)
+        (3, 3, 4, 8, 5, 3, 3, 1, 1, 1, 1),    # stem.0 form, W % 4 == 0
     ]
 
 

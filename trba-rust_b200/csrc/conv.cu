@@ -93,6 +93,90 @@ __global__ void __launch_bounds__(256) im2col_rows_kernel(const int8_t *__restri
     }
 }
 
+// Narrow 3x3 operands with stride 1, padding 1 and W % 4 == 0 (both stem
+// convolutions): one thread per four horizontally adjacent output pixels.
+// For every (channel, kernel row) it reads the 32-bit word of the four input
+// pixels on that input row and its two neighbour words, and forms the
+// windows of kw = 0, 1, 2 with funnel shifts (window byte p = input pixel
+// ow + p + kw - 1; words beyond the plane's left and right edges read as zero
+// padding).  Each group of four K positions becomes one 32-bit word of each
+// of the four output rows by a 4 x 4 byte transpose (byte_perm).  A warp's
+// 128 output rows are one contiguous span of col: they are assembled in
+// shared memory and written with 16-byte stores at consecutive addresses
+// (the rows' own 16-byte pieces, written in place, sit LD * 4 bytes apart
+// across the warp and measured twice as slow).  Rows in [rows, rows_pad) are
+// written as zeros.  Two warps per CTA (a warp stages 128 * LD bytes).
+constexpr int kQuadThreads = 64;
+
+template <int C>
+__global__ void __launch_bounds__(kQuadThreads, 12)
+    im2col_quad_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col, int H, int W, i64 quads,
+                       i64 quads_pad) {
+    constexpr int K = C * 9, LD = (K + 15) / 16 * 16, NCH = LD / 16;
+    constexpr int WB = 32 * 4 * LD;
+    __shared__ __align__(16) uint8_t stage[kQuadThreads / 32][WB];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hw = H * W, plane4 = hw >> 2;
+    for (i64 u0 = (i64)blockIdx.x * blockDim.x + warp * 32; u0 < quads_pad; u0 += (i64)gridDim.x * blockDim.x) {
+        const i64 u = u0 + lane;
+        uint8_t *sw = stage[warp] + lane * 4 * LD;
+        if (u >= quads) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+#pragma unroll
+                for (int m = 0; m < NCH; ++m) *reinterpret_cast<uint4 *>(sw + p * LD + 16 * m) = make_uint4(0, 0, 0, 0);
+        } else {
+            const i64 r = 4 * u;
+            const i64 b = r / hw;
+            const int rem = (int)(r - b * hw), oh = rem / W, ow = rem - oh * W;
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(in + b * C * hw);
+            const uint32_t *rowp[3];
+            bool okh[3];
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh) {
+                const int ih = oh + kh - 1;
+                okh[kh] = (unsigned)ih < (unsigned)H;
+                rowp[kh] = src + (okh[kh] ? (ih * W + ow) >> 2 : 0);
+            }
+            const bool hp = ow > 0, hn = ow + 4 < W;
+            auto win = [&](int k) -> uint32_t {
+                if (k >= K) return 0u;
+                const int c = k / 9, t = k - c * 9, kh = t / 3, kw = t - kh * 3;
+                if (!okh[kh]) return 0u;
+                const uint32_t *p = rowp[kh] + c * plane4;
+                const uint32_t cur = p[0];
+                if (kw == 1) return cur;
+                if (kw == 0) return __funnelshift_r(hp ? p[-1] : 0u, cur, 24);
+                return __funnelshift_r(cur, hn ? p[1] : 0u, 8);
+            };
+#pragma unroll
+            for (int m = 0; m < NCH; ++m) {
+                uint32_t rw[4][4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const int k0 = 16 * m + 4 * g;
+                    const uint32_t a = win(k0), bb = win(k0 + 1), cc = win(k0 + 2), d = win(k0 + 3);
+                    const uint32_t t0 = __byte_perm(a, bb, 0x5140), t1 = __byte_perm(a, bb, 0x7362);
+                    const uint32_t t2 = __byte_perm(cc, d, 0x5140), t3 = __byte_perm(cc, d, 0x7362);
+                    rw[0][g] = __byte_perm(t0, t2, 0x5410);
+                    rw[1][g] = __byte_perm(t0, t2, 0x7632);
+                    rw[2][g] = __byte_perm(t1, t3, 0x5410);
+                    rw[3][g] = __byte_perm(t1, t3, 0x7632);
+                }
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+                    *reinterpret_cast<uint4 *>(sw + p * LD + 16 * m) = make_uint4(rw[p][0], rw[p][1], rw[p][2], rw[p][3]);
+            }
+        }
+        __syncwarp();
+        const i64 nq = quads_pad - u0 < 32 ? quads_pad - u0 : 32;
+        const int pieces = (int)(nq * 4 * LD / 16);
+        uint4 *gdst = reinterpret_cast<uint4 *>(col + 4 * u0 * LD);
+        for (int i = lane; i < pieces; i += 32) gdst[i] = reinterpret_cast<const uint4 *>(stage[warp])[i];
+        __syncwarp();
+    }
+}
+
 template <int KH, int KW>
 __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restrict__ in, int8_t *__restrict__ col,
                                                           int C, int H, int W, int kH_, int kW_, int sH, int sW,
@@ -333,6 +417,19 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
     if (col_ld < cols || (col_ld & 15) || rows <= 0) return;
     const i64 total = ((rows + 15) / 16 * 16) * col_ld;
     const bool aligned = (reinterpret_cast<uintptr_t>(col) & 15) == 0;
+    if (aligned && kH == 3 && kW == 3 && (C == 3 || C == 16) && col_ld == (C * 9 + 15) / 16 * 16 && sH == 1 &&
+        sW == 1 && pH == 1 && pW == 1 && Ho == H && Wo == W && W % 4 == 0 &&
+        (reinterpret_cast<uintptr_t>(input) & 3) == 0) {
+        const i64 rows_pad = (rows + 15) / 16 * 16;
+        const i64 quads = rows / 4, quads_pad = rows_pad / 4;
+        const unsigned grid = (unsigned)((quads_pad + kQuadThreads - 1) / kQuadThreads);
+        if (C == 3)
+            im2col_quad_kernel<3><<<grid, kQuadThreads, 0, as_stream(s)>>>(input, col, H, W, quads, quads_pad);
+        else
+            im2col_quad_kernel<16><<<grid, kQuadThreads, 0, as_stream(s)>>>(input, col, H, W, quads, quads_pad);
+        TRBA_LAUNCH_CHECK();
+        return;
+    }
     if (aligned && kH == 3 && kW == 3 && (C == 3 || C == 16) && col_ld == (C * 9 + 15) / 16 * 16) {
         const i64 rows_pad = (rows + 15) / 16 * 16;
         const i64 want = (rows_pad + 255) / 256, cap = (i64)sm_count() * 16;
