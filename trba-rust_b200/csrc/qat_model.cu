@@ -1027,6 +1027,20 @@ void colsum(trba_model *m, const float *X, int rows, int cols, i64 ld, float *ou
     seq::col_sums(X, rows, cols, ld, m->ones.get(), out, true, m->gemm_ws.get(), m->gemm_ws_elems, st);
 }
 
+// Input projections of both directions, then both recurrences in one launch
+// (independent: the directions share only the layer input).
+void lstm_layer_fwd(Ctx &c, RnnL &r, const float *x) {
+    trba_model *m = c.m;
+    const int B = c.B, T = m->T, H = m->cfg.hidden;
+    seq::LstmFwdDir dirs[2];
+    for (int d = 0; d < 2; ++d) {
+        sgemm(c, gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
+        dirs[d] = seq::LstmFwdDir{r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], r.gates[d].get(),
+                                  r.c[d].get(), r.hprev[d].get(), d, d};
+    }
+    seq::lstm_fwd(dirs, 2, B, T, H, r.cat.get(), c.st);
+}
+
 void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const int32_t *ctc_tgt,
                   const int32_t *ctc_len) {
     trba_model *m = c.m;
@@ -1034,11 +1048,7 @@ void head_forward(Ctx &c, const int32_t *text_in, const int32_t *target, const i
     const int B = c.B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps;
     const float *x = m->feat.get();
     for (auto &r : m->rnn) {  // BiLstmLayer::forward (src/rnn.rs:167-174)
-        for (int d = 0; d < 2; ++d) {
-            sgemm(c, gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
-            seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
-                          r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
-        }
+        lstm_layer_fwd(c, r, x);
         sgemm(c, gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
                    c.st);
         x = r.y.get();
@@ -1086,11 +1096,7 @@ void head_infer(Ctx &c, int32_t *step_tokens) {
     const int B = c.B, T = m->T, H = cf.hidden, V = cf.classes, S = m->steps;
     const float *x = m->feat.get();
     for (auto &r : m->rnn) {
-        for (int d = 0; d < 2; ++d) {
-            sgemm(c, gemm(m, B * T, 4 * H, r.D, x, r.D, 1, c.P + r.wih[d], 1, r.D, r.xg[d].get(), 4 * H), c.st);
-            seq::lstm_fwd(r.xg[d].get(), c.P + r.bih[d], c.P + r.bhh[d], c.P + r.whh[d], B, T, H, d, r.gates[d].get(),
-                          r.c[d].get(), r.hprev[d].get(), r.cat.get(), d, c.st);
-        }
+        lstm_layer_fwd(c, r, x);
         sgemm(c, gemm(m, B * T, H, 2 * H, r.cat.get(), 2 * H, 1, c.P + r.pw, 1, 2 * H, r.y.get(), H, false, c.P + r.pb),
               c.st);
         x = r.y.get();
@@ -1177,9 +1183,11 @@ void head_backward(Ctx &c) {
         colsum(m, dy, B * T, H, H, c.G + r.pb, c.st);
         sgemm(c, gemm(m, B * T, 2 * H, H, dy, H, 1, c.P + r.pw, 2 * H, 1, r.dcat.get(), 2 * H), c.st);
         float *dxout = li == 0 ? m->dfeat.get() : r.dx.get();
+        seq::LstmBwdDir bdirs[2];
+        for (int d = 0; d < 2; ++d)
+            bdirs[d] = seq::LstmBwdDir{r.gates[d].get(), r.c[d].get(), c.P + r.whh[d], r.dg[d].get(), d, d};
+        seq::lstm_bwd(bdirs, 2, r.dcat.get(), B, T, H, c.st);
         for (int d = 0; d < 2; ++d) {
-            seq::lstm_bwd(r.dcat.get(), r.gates[d].get(), r.c[d].get(), c.P + r.whh[d], B, T, H, d, d, r.dg[d].get(),
-                          c.st);
             const float *g = r.dg[d].get();
             sgemm(c, gemm(m, 4 * H, r.D, B * T, g, 1, 4 * H, xin, r.D, 1, c.G + r.wih[d], r.D, true), c.st);
             sgemm(c, gemm(m, 4 * H, H, B * T, g, 1, 4 * H, r.hprev[d].get(), H, 1, c.G + r.whh[d], H, true), c.st);

@@ -158,10 +158,18 @@ __global__ void sgemm_finish_kernel(Gemm g, int splits) {
 // independent chains.  Samples never interact inside a recurrence.
 constexpr int kLstmS = 4, kLstmRows = 2;
 
-__global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const float *b_ih, const float *b_hh,
-                                                       const float *w_hh, int B, int T, int H, int rev,
-                                                       float *gates, float *c_tr, float *h_prev_tr, float *cat,
-                                                       int dir) {
+struct LstmFwdPair {
+    LstmFwdDir d[2];
+};
+struct LstmBwdPair {
+    LstmBwdDir d[2];
+};
+
+__global__ void __launch_bounds__(256) lstm_fwd_kernel(LstmFwdPair dp, int B, int T, int H, float *cat) {
+    const LstmFwdDir D = blockIdx.y ? dp.d[1] : dp.d[0];
+    const float *xg = D.xg, *b_ih = D.b_ih, *b_hh = D.b_hh, *w_hh = D.w_hh;
+    float *gates = D.gates, *c_tr = D.c, *h_prev_tr = D.h_prev;
+    const int rev = D.rev, dir = D.dir;
     constexpr int S = kLstmS;
     extern __shared__ double smd[];
     const int G4 = 4 * H;
@@ -254,9 +262,11 @@ __global__ void __launch_bounds__(256) lstm_fwd_kernel(const float *xg, const fl
     }
 }
 
-__global__ void __launch_bounds__(256) lstm_bwd_kernel(const float *dcat, const float *gates, const float *c_tr,
-                                                       const float *w_hh, int B, int T, int H, int rev, int dir,
-                                                       float *dgates) {
+__global__ void __launch_bounds__(256) lstm_bwd_kernel(LstmBwdPair dp, const float *dcat, int B, int T, int H) {
+    const LstmBwdDir D = blockIdx.y ? dp.d[1] : dp.d[0];
+    const float *gates = D.gates, *c_tr = D.c, *w_hh = D.w_hh;
+    float *dgates = D.dgates;
+    const int rev = D.rev, dir = D.dir;
     constexpr int S = kLstmS;
     extern __shared__ double smd[];
     const int G4 = 4 * H;
@@ -1046,25 +1056,30 @@ static void set_smem(const void *fn, size_t bytes) {
     if (bytes > 48 * 1024) TRBA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
 
-void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H, int rev,
-              float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st) {
+void lstm_fwd(const LstmFwdDir *dirs, int ndir, int B, int T, int H, float *cat, cudaStream_t st) {
+    TRBA_REQUIRE(ndir == 1 || ndir == 2, "lstm_fwd: one or two directions per launch");
     const size_t smem = sizeof(double) * kLstmS * H + sizeof(float) * ((size_t)4 * H * H + kLstmS * H + kLstmS * 4 * H);
     TRBA_REQUIRE(smem <= 200 * 1024, "lstm_fwd: hidden size too large for the shared-memory recurrence");
     TRBA_REQUIRE(4 * H <= kLstmRows * 256, "lstm_fwd: at most 2 gate rows per thread (hidden <= 128)");
     set_smem((const void *)lstm_fwd_kernel, smem);
-    lstm_fwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(xg, b_ih, b_hh, w_hh, B, T, H, rev, gates, c, h_prev,
-                                                                  cat, dir);
+    LstmFwdPair dp{};
+    dp.d[0] = dirs[0];
+    dp.d[1] = dirs[ndir - 1];
+    lstm_fwd_kernel<<<dim3((B + kLstmS - 1) / kLstmS, ndir), 256, smem, st>>>(dp, B, T, H, cat);
     TRBA_LAUNCH_CHECK();
 }
 
-void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H, int rev,
-              int dir, float *dgates, cudaStream_t st) {
+void lstm_bwd(const LstmBwdDir *dirs, int ndir, const float *dcat, int B, int T, int H, cudaStream_t st) {
+    TRBA_REQUIRE(ndir == 1 || ndir == 2, "lstm_bwd: one or two directions per launch");
     TRBA_REQUIRE(H % 8 == 0, "lstm_bwd: hidden size must be a multiple of 8 (4*hidden fills whole warps)");
     const size_t smem = sizeof(double) * kLstmS * 4 * H + sizeof(float) * ((size_t)4 * H * H + 2 * kLstmS * H);
     TRBA_REQUIRE(smem <= 200 * 1024, "lstm_bwd: hidden size too large for the shared-memory recurrence");
     TRBA_REQUIRE(kLstmS * H <= kLstmRows * 256, "lstm_bwd: at most 2 state rows per thread (hidden <= 128)");
     set_smem((const void *)lstm_bwd_kernel, smem);
-    lstm_bwd_kernel<<<(B + kLstmS - 1) / kLstmS, 256, smem, st>>>(dcat, gates, c, w_hh, B, T, H, rev, dir, dgates);
+    LstmBwdPair dp{};
+    dp.d[0] = dirs[0];
+    dp.d[1] = dirs[ndir - 1];
+    lstm_bwd_kernel<<<dim3((B + kLstmS - 1) / kLstmS, ndir), 256, smem, st>>>(dp, dcat, B, T, H);
     TRBA_LAUNCH_CHECK();
 }
 

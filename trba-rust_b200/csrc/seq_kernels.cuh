@@ -31,15 +31,24 @@ struct Gemm {
 };
 void sgemm(const Gemm &g, cudaStream_t st);
 
-// One LSTM direction over all T slots (src/rnn.rs:107-166).  xg = x W_ih^T
-// [B, T, 4H]; writes gates (post-activation) and c [B, T, .], h into
-// cat[b, tt, dir*H + i] (row stride 2H) and h_prev [B, T, H].
-void lstm_fwd(const float *xg, const float *b_ih, const float *b_hh, const float *w_hh, int B, int T, int H,
-              int rev, float *gates, float *c, float *h_prev, float *cat, int dir, cudaStream_t st);
-// Backward through time of one direction (src/rnn.rs:200-288): dh_out from
-// dcat[b, tt, dir*H + i]; writes dgates [B, T, 4H].
-void lstm_bwd(const float *dcat, const float *gates, const float *c, const float *w_hh, int B, int T, int H,
-              int rev, int dir, float *dgates, cudaStream_t st);
+// LSTM recurrences over all T slots (src/rnn.rs:107-166), the directions of
+// a layer in one launch (grid y = entry of `dirs`).  Per direction: xg =
+// x W_ih^T [B, T, 4H]; writes gates (post-activation) and c [B, T, .], h
+// into cat[b, tt, dir*H + i] (row stride 2H) and h_prev [B, T, H].
+struct LstmFwdDir {
+    const float *xg, *b_ih, *b_hh, *w_hh;
+    float *gates, *c, *h_prev;
+    int rev, dir;
+};
+void lstm_fwd(const LstmFwdDir *dirs, int ndir, int B, int T, int H, float *cat, cudaStream_t st);
+// Backward through time (src/rnn.rs:200-288), the directions in one launch:
+// dh_out from dcat[b, tt, dir*H + i]; writes dgates [B, T, 4H].
+struct LstmBwdDir {
+    const float *gates, *c, *w_hh;
+    float *dgates;
+    int rev, dir;
+};
+void lstm_bwd(const LstmBwdDir *dirs, int ndir, const float *dcat, int B, int T, int H, cudaStream_t st);
 
 // Attention decoder, teacher forced (src/attn.rs:119-261).  bh/proj_h [B,T,H];
 // text_in [B, steps]; traces laid out [steps, B, .].
