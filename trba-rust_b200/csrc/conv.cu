@@ -382,6 +382,26 @@ __global__ void maxpool_fwd_i8_kernel(const int8_t *__restrict__ x, int8_t *__re
     }
 }
 
+// W % 8 == 0: one thread per four adjacent outputs.  8-byte loads of the two
+// input rows, per-byte signed max of the rows and then of the horizontal
+// pairs (__vmaxs4), one 4-byte store.
+__global__ void maxpool_fwd_i8_v4_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, int H, int W,
+                                         i64 total4) {
+    const int wq = W >> 3, Ho = H >> 1;  // output quads per output row
+    GRID_LOOP(i, total4) {
+        const i64 row = i / wq;  // bc * Ho + oh
+        const int q = (int)(i - row * wq);
+        const i64 bc = row / Ho;
+        const int oh = (int)(row - bc * Ho);
+        const int8_t *t = x + bc * H * W + (i64)(2 * oh) * W + 8 * q;
+        const uint2 a = *reinterpret_cast<const uint2 *>(t);
+        const uint2 b = *reinterpret_cast<const uint2 *>(t + W);
+        const uint32_t v0 = __vmaxs4(a.x, b.x), v1 = __vmaxs4(a.y, b.y);
+        const uint32_t h0 = __vmaxs4(v0, v0 >> 8), h1 = __vmaxs4(v1, v1 >> 8);
+        reinterpret_cast<uint32_t *>(y)[i] = __byte_perm(h0, h1, 0x6420);
+    }
+}
+
 // Backward recomputes the argmax from x; writes every element of dx.
 __global__ void maxpool_bwd_i8_kernel(const int8_t *__restrict__ x, const float *__restrict__ dy,
                                       float *__restrict__ dx, int H, int W, i64 total) {
@@ -447,7 +467,7 @@ void launch_im2col_pad(const int8_t *input, int8_t *col, int batch, int C, int H
         const i64 rows_pad = (rows + 15) / 16 * 16;
         const size_t smem = (size_t)kTileRows * (col_ld + 4);
         const i64 ntiles = (rows_pad + kTileRows - 1) / kTileRows;
-        const i64 cap = (i64)sm_count() * 4;
+        const i64 cap = (i64)sm_count() * 6;  // six CTAs per SM fit (40 registers, <= 37 KB tiles)
         const unsigned grid = (unsigned)(ntiles < cap ? ntiles : cap);
         auto go = [&](auto kern) {
             static bool attr[64] = {};
@@ -554,7 +574,11 @@ void launch_maxpool2x2_forward_i8(const int8_t *x, int8_t *y, int B, int C, int 
     TRBA_REQUIRE(B > 0 && C > 0 && H >= 2 && W >= 2 && !(H & 1) && !(W & 1),
                  "launch_maxpool2x2_forward_i8: bad shape");
     const i64 total = (i64)B * C * (H / 2) * (W / 2);
-    maxpool_fwd_i8_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(x, y, H, W, total);
+    if (W % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(y) & 3) == 0) {
+        maxpool_fwd_i8_v4_kernel<<<grid_for(total / 4), kThreads, 0, as_stream(s)>>>(x, y, H, W, total / 4);
+    } else {
+        maxpool_fwd_i8_kernel<<<grid_for(total), kThreads, 0, as_stream(s)>>>(x, y, H, W, total);
+    }
     TRBA_LAUNCH_CHECK();
 }
 
