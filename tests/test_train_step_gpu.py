@@ -126,8 +126,9 @@ def test_host_entry_point_equals_device_entry_point(lib, cuda):
 
 
 def test_loss_curve_200_steps_matches_oracle(lib, cuda):
-    """north_star: training loss within 1% of the reference's over 200 steps
-    (TRBA-small 32x64, batch 8, a fresh synthetic batch every step)."""
+    """Training loss within 1% of the reference's over 200 steps (the
+    convergence bar of this port; TRBA-small 32x64, batch 8, a fresh
+    synthetic batch every step)."""
     geom = dict(img_w=64, max_len=4)
     ocfg, params, gm, man = _setup(geom, 8, seed=21)
     orc = so.OracleTrba(ocfg, params, _oracle_backend())
