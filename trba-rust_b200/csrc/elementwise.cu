@@ -208,10 +208,6 @@ __global__ void mask_relu_bwd_kernel(const float *__restrict__ y, const float *_
     GRID_LOOP(i, n) dx[i] = y[i] > 0.0f ? dy[i] : 0.0f;
 }
 
-__global__ void fill_kernel(float *__restrict__ p, i64 n, float v) {
-    GRID_LOOP(i, n) p[i] = v;
-}
-
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, i64 n,
                            float *__restrict__ o) {
     GRID_LOOP(i, n) o[i] = fadd(a[i], b[i]);
