@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm-sweep", action="store_true")
+    ap.add_argument("--aux-out", default=None, help="also write the auxiliary JSON lines to this file")
     ap.add_argument("--eager", action="store_true", help="launch the step kernel by kernel (no CUDA graph)")
     ap.add_argument("--mope", action="store_true",
                     help="MoPE inference serving: 9 length-bucket experts, greedy decoding (not the training metric)")
@@ -118,6 +119,21 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def workload_config(args, world: int) -> dict:
+    """The `config` object both arms print: the workload, never the sample."""
+    return {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}, "
+                        f"batch {args.batch} per GPU",
+            "img": f"3x32x{args.img_w}", "feat_dim": 128, "hidden": 64, "classes": 130,
+            "max_len": args.max_len, "global_batch": args.batch * world, "per_gpu_batch": args.batch,
+            "parallelism": f"dp{world}", "l2": "working set > 126 MB L2 (activations of a step)"}
+
+
+# Lines per step of the CPU samples: the reference's own CPU path takes about
+# 30 ms per 32x160 line on 16 host cores, so 48 lines (the reference's
+# training batch) keep each sampled step near 1.5 s.
+CPU_SAMPLE_LINES = 48
+
+
 # ------------------------------------------------------------ reference --
 def cpu_step_sample(lines: int, steps: int, warmup: int, img_w: int, max_len: int, seed: int):
     """Times the reference's CPU path (oracle/step_oracle.py driving the
@@ -146,18 +162,18 @@ def reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    # bounded sample: about 2 minutes of CPU work in total for the run
-    per_line = 0.12 * args.img_w / 160.0
-    lines = max(2, min(16, int(120.0 / max(1, args.steps + args.warmup) / per_line)))
+    # Bounded sample of the same workload: every step trains CPU_SAMPLE_LINES
+    # lines of it (the full per-GPU batch would take minutes per step on the
+    # host); lines/s is the same metric.
+    lines = CPU_SAMPLE_LINES
     v, cores, kind, lib = cpu_step_sample(lines, args.steps, args.warmup, args.img_w, args.max_len, args.seed)
-    sample = f"{lines} lines/step x {args.steps} timed steps (after {args.warmup} warm-up), {lib}, OMP {cores} threads"
+    sample = (f"{lines} lines of the workload per step x {args.steps} timed steps (after {args.warmup} warm-up), "
+              f"{lib}, OMP {cores} threads")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "lines/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "lines/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * lines / v, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMM / fp32", "data": "synthetic",
-        "config": {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}",
-                   "img": f"3x32x{args.img_w}", "feat_dim": 128, "hidden": 64, "classes": 130,
-                   "lines_per_step": lines},
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (s8xs8->s32) / fp32", "data": "synthetic",
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": v, "unit": "lines/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": v, "unit": "lines/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -386,9 +402,10 @@ def our_arm(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, kind, lib = cpu_step_sample(32, 2, 1, args.img_w, args.max_len, args.seed)
+        lines, steps = CPU_SAMPLE_LINES, 8
+        v, cores, kind, lib = cpu_step_sample(lines, steps, 1, args.img_w, args.max_len, args.seed)
         cpu = {"value": v, "unit": "lines/s", "cores": cores, "kind": kind,
-               "sample": f"32 lines/step x 2 timed steps (1 warm-up) of the same 32x{args.img_w} step, {lib}, "
+               "sample": f"{lines} lines of the workload per step x {steps} timed steps (1 warm-up), {lib}, "
                          f"OMP {cores} threads"}
 
     roofline = None
@@ -401,8 +418,7 @@ def our_arm(args):
             "bound": "fp32",
             "achieved": achieved, "peak": f32_peak.value, "unit": "TFLOP/s",
             "frac": achieved / f32_peak.value,
-            "peak_source": "measured in this run: trba_measure_f32_muladd_peak (separately rounded f32x2 "
-                           "multiply + add chains on every SM)",
+            "peak_source": "measured in this run: separately rounded f32x2 multiply + add chains on every SM",
             "traffic": traffic,
             "algorithmic_bytes_per_launch": dg_bytes / dg_n,
             "hbm_gbs_at_algorithmic_bytes": dg_bytes / dg_n / per_launch_s / 1e9,
@@ -410,8 +426,6 @@ def our_arm(args):
             "launches_per_step": dg_n / dg_steps,
             "ms_per_step": dg_ms / dg_steps,
             "share_of_step": dg_ms / dg_steps / ms,
-            "timed_launches": "CUDA events around every launch of the timed region" if not graphs
-            else "device globaltimer stamps around the launches of the last timed step (replayed CUDA graph)",
         }
     gemm_line = None
     head = gemm.pop("head_sgemm_f64acc")
@@ -423,27 +437,48 @@ def our_arm(args):
                      "peak_source": "measured in this run: torch._int_mm (cuBLAS) int8 8192^3, best of 10",
                      "by_gemm": gemm}
     if rank == 0:
+        # Auxiliary lines first (one JSON object per line, each tagged "aux"),
+        # the headline last and short: the driver parses the final line.
+        aux = []
+        if sweep:
+            for r in sweep.pop("per_shape"):
+                aux.append({"aux": "int8_gemm_sweep_shape", **r})
+            aux.append({"aux": "int8_gemm_sweep_summary", **sweep})
+        if gemm_line:
+            aux.append({"aux": "roofline_int8_gemm", **gemm_line})
+        aux.append({"aux": "head_sgemm", "launches_per_step": head["launches_per_step"],
+                    "ms_per_step": head["ms_per_step"], "tflops": head["tops"]})
+        aux.append({"aux": "step_phases_ms", **phases,
+                    "note": "eager steps, each phase spanned on the step's stream"})
+        aux.append({"aux": "loss_last", "loss": [float(x) for x in loss]})
+        for a in aux:
+            print(json.dumps(a), flush=True)
+        if args.aux_out:
+            Path(args.aux_out).parent.mkdir(parents=True, exist_ok=True)
+            Path(args.aux_out).write_text("\n".join(json.dumps(a) for a in aux) + "\n")
+        summary = None
+        if sweep:
+            summary = {"peak_tops": sweep["peak_tops"],
+                       "best_frac_requant_i8_compute_bound": max(
+                           (c["frac_peak"] for c in sweep["compute_bound_requant_i8"]), default=None)}
         out = {
             "metric": METRIC, "value": value, "unit": "lines/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 (s8xs8->s32 tcgen05) / fp32", "data": "synthetic",
-            "config": {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}",
-                       "img": f"3x32x{args.img_w}", "feat_dim": 128, "hidden": 64, "classes": 130,
-                       "global_batch": args.batch * world, "per_gpu_batch": args.batch,
-                       "parallelism": f"dp{world}", "l2": "working set > 126 MB L2 (activations of a step)",
-                       "loss_last": [float(x) for x in loss]},
+            "vs_baseline": None, "dtype": "int8 (s8xs8->s32) / fp32", "data": "synthetic",
+            "config": workload_config(args, world),
             "gpu_launches": launches,
             "clocks": ck,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "roofline": roofline,
-            "roofline_int8_gemm": gemm_line,
-            "int8_gemm_sweep": sweep,
-            "head_sgemm": {"launches_per_step": head["launches_per_step"], "ms_per_step": head["ms_per_step"],
-                           "tflops": head["tops"]},
-            "step_phases_ms": {**phases, "note": "eager steps, each phase spanned on the step's stream"},
+            "int8_gemm": summary,
         }
-        print(json.dumps(out), flush=True)
+        line = json.dumps(out)
+        if len(line) > 4000:  # keep the headline short whatever the optional parts hold
+            out.pop("int8_gemm")
+            out["roofline"] = {k: roofline[k] for k in ("bound", "achieved", "peak", "unit", "frac", "traffic")}
+            line = json.dumps(out)
+        print(line, flush=True)
     m.close()
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -43,6 +43,8 @@ typedef struct {
     float lr, weight_decay, ctc_weight, muon_cap;
     int clip_warmup;  /* steps with global-norm clipping at 5.0                 */
     int wgrad_mode;   /* 0: reference-compatible operand order, 1: dW = dX^T col */
+    int dgrad_mode;   /* conv input gradient: 0 exact (the reference's f32 order, CUDA cores),
+                         1 tensor cores (implicit GEMM, fp32 dy as three bf16 terms) */
 } trba_model_config;
 
 /* TRBA-small defaults (fd 128, hidden 64, 130 classes, 32x160, max_len 20). */

@@ -36,11 +36,11 @@ def _oracle_backend():
     return so.CpuBackend(REPO / "oracle" / "liboracle.so")
 
 
-def _setup(geom, B, seed, wgrad_mode=0):
+def _setup(geom, B, seed, wgrad_mode=0, dgrad_mode=0):
     import trba_b200.model as tm
     ocfg = so.Config(**geom, wgrad_mode="compat" if wgrad_mode == 0 else "correct")
     params = so.init_params(ocfg, seed)
-    gm = tm.QatModel(tm.Config(**geom, batch=B, wgrad_mode=wgrad_mode))
+    gm = tm.QatModel(tm.Config(**geom, batch=B, wgrad_mode=wgrad_mode, dgrad_mode=dgrad_mode))
     man = gm.manifest()
     onames = [n for n, _, _ in so.manifest(ocfg)]
     assert [e[0] for e in man] == onames, "parameter manifest differs from the reference order"
@@ -91,6 +91,32 @@ def test_train_step_matches_oracle(geom, B, wgrad_mode, lib, cuda):
     for k, v in orc.debug.items():
         g = gm.debug_tensor(k, v.size)
         assert np.array_equal(g, v.ravel().astype(np.float32)), f"{k} differs"
+    _compare(man, gm.get_grads(), orc.g, 1e-6, "gradient")
+    gm.optimizer_step()
+    _compare(man, gm.get_params(), orc.p, 1e-6, "updated parameter")
+    assert lib.trba_tc_error_poll(1) == 0
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()
+
+
+@pytest.mark.parametrize("geom,B,fixed_len", [
+    (dict(img_w=64, max_len=4), 48, 4),      # TRBA-small step: 32x64, batch 48, labels of length 4
+    (dict(img_w=160, max_len=20), 48, None),  # 32x160, max_len 20, batch 48
+    (dict(img_w=256, max_len=40), 48, None),  # 32x256, max_len 40, 48 lines per GPU (T = 32: CTC with L up to 41)
+    (dict(img_w=160, max_len=20), 512, None),  # 32x160, batch 512: the benchmark's per-GPU batch
+], ids=["32x64_L4_b48", "32x160_L20_b48", "32x256_L40_b48", "32x160_L20_b512"])
+def test_benchmark_configurations_match_oracle(geom, B, fixed_len, lib, cuda):
+    """One forward + backward + optimiser step at the benchmark's own
+    configurations, bit for bit against the oracle (exact input gradient)."""
+    ocfg, params, gm, man = _setup(geom, B, seed=2024, dgrad_mode=0)
+    img, ti, tg, ct = so.make_batch(ocfg, B, seed=77, fixed_len=fixed_len)
+    orc = so.OracleTrba(ocfg, params, _oracle_backend())
+    res = orc.train_step(img, ti, tg, ct)
+    gm.forward_backward(*_to_dev(img, ti, tg, ct, ocfg.steps))
+    want = np.array([res["loss"], res["attn"], res["ctc"]])
+    assert np.allclose(gm.loss(), want, rtol=1e-6, atol=0), (gm.loss(), want)
+    for k in ("feat", "logits", "ctc_logits", "dfeat"):
+        v = orc.debug[k]
+        assert np.array_equal(gm.debug_tensor(k, v.size), v.ravel().astype(np.float32)), f"{k} differs"
     _compare(man, gm.get_grads(), orc.g, 1e-6, "gradient")
     gm.optimizer_step()
     _compare(man, gm.get_params(), orc.p, 1e-6, "updated parameter")

@@ -154,10 +154,12 @@ def read(path: str | os.PathLike) -> dict:
 
 
 def load(model, path: str | os.PathLike) -> dict:
-    """Loads a TRBA_V6 / V5 / V4 checkpoint into `model` (same geometry):
-    parameters (by name in V6, by manifest position in V5 / V4), BN running
-    statistics, the optimiser step and — when the geometry matches — the Adam
-    moments.  Returns the file's meta data."""
+    """Loads a TRBA_V6 / V5 / V4 checkpoint into `model`: parameters (by name
+    in V6, by manifest position in V5 / V4), BN running statistics, the
+    optimiser step and the Adam moments of every tensor whose saved moments
+    have the parameter's length.  A V6 file of another geometry is refused;
+    V5 files carry no geometry (their moments load whenever the lengths
+    match) and V4 files no moments.  Returns the file's meta data."""
     ck = read(path)
     man = model.manifest()
     if ck["geometry"] is not None and tuple(ck["geometry"]) != geometry(model):

@@ -1269,12 +1269,14 @@ void trba_model_default_config(trba_model_config *c) {
     c->muon_cap = 10.0f;
     c->clip_warmup = 500;
     c->wgrad_mode = 0;
+    c->dgrad_mode = 0;
 }
 
 trba_model *trba_model_create(const trba_model_config *cfg) {
     if (!cfg || cfg->fd < 16 || cfg->fd % 16 || cfg->fd > 512 || cfg->batch <= 0 || cfg->hidden <= 0 ||
         cfg->hidden > 128 || cfg->hidden % 8 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
-        (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0) {
+        (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0 || cfg->wgrad_mode < 0 ||
+        cfg->wgrad_mode > 1 || cfg->dgrad_mode < 0 || cfg->dgrad_mode > 1) {
         report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
         return nullptr;
     }

@@ -5,6 +5,7 @@
 // shared memory and one CTA per group of samples (samples never interact
 // inside a recurrence); the big batched products (input projections, weight
 // gradients, logits) run as ordinary GEMMs outside the time loop.
+#include <atomic>
 #include "seq_kernels.cuh"
 
 namespace trba {
@@ -1185,7 +1186,12 @@ constexpr long long kNoAllocMaxOut = 1LL << 17;   // M * N
 
 __device__ __align__(256) double g_noalloc_scratch[kNoAllocScratch];
 
-double *g_noalloc_ptr[64] = {};
+// Device address of the scratch array, looked up once per device.  Host
+// threads may call the entry point concurrently, so the cache entries are
+// atomics (a racing first lookup stores the same address twice).  A cached
+// address stays valid for the life of the device's primary context; after a
+// cudaDeviceReset the library must be reloaded.
+std::atomic<double *> g_noalloc_ptr[64];
 
 }  // namespace
 
@@ -1203,21 +1209,23 @@ extern "C" int trba_sgemm_exact_noalloc(const float *a, const float *b, float *c
         report_error(__FILE__, __LINE__, "trba_sgemm_exact_noalloc: no current device", (int)de);
         return de != cudaSuccess ? (int)de : -1;
     }
-    if (!g_noalloc_ptr[dev]) {  // once per device, with that device current
+    double *ws = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (!ws) {  // once per device, with that device current
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
             report_error(__FILE__, __LINE__, "trba_sgemm_exact_noalloc: cudaGetSymbolAddress failed", (int)e);
             return e != cudaSuccess ? (int)e : -1;
         }
-        g_noalloc_ptr[dev] = static_cast<double *>(p);
+        ws = static_cast<double *>(p);
+        g_noalloc_ptr[dev].store(ws, std::memory_order_relaxed);
     }
     seq::Gemm g;
     g.M = m, g.N = n, g.K = k;
     g.A = a, g.sam = k, g.sak = 1;  // A [M, K] row-major
     g.B = b, g.sbk = n, g.sbn = 1;  // B [K, N] row-major
     g.C = c, g.ldc = n;             // C [M, N] compact
-    g.ws = g_noalloc_ptr[dev];
+    g.ws = ws;
     g.ws_elems = kNoAllocScratch;
     seq::sgemm(g, as_stream(stream));
     const cudaError_t le = cudaGetLastError();
