@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-gemm-sweep", action="store_true")
     ap.add_argument("--aux-out", default=None, help="also write the auxiliary JSON lines to this file")
     ap.add_argument("--eager", action="store_true", help="launch the step kernel by kernel (no CUDA graph)")
+    ap.add_argument("--dgrad-mode", type=int, default=1, choices=[0, 1],
+                    help="conv input gradient: 0 exact f32 order (CUDA cores), 1 tensor cores")
     ap.add_argument("--mope", action="store_true",
                     help="MoPE inference serving: 9 length-bucket experts, greedy decoding (not the training metric)")
     ap.add_argument("--mope-lines", type=int, default=65536)
@@ -301,7 +303,7 @@ def our_arm(args):
     from trba_b200 import data, dp
     from trba_b200.model import Config, QatModel
     L = pkg.lib()
-    cfg = Config(img_w=args.img_w, max_len=args.max_len, batch=args.batch)
+    cfg = Config(img_w=args.img_w, max_len=args.max_len, batch=args.batch, dgrad_mode=args.dgrad_mode)
     m = QatModel(cfg)
     m.set_params(data.init_params(m.manifest(), cfg, args.seed))
     if world > 1:

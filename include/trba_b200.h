@@ -62,6 +62,20 @@ long long trba_launch_count(void);
  * counterpart in the reference. */
 int trba_gemm_pair_enable(int enable);
 
+/* launch_conv_backward_grad_input_i8 (reference backend.rs:51, the later
+ * snapshot's cuda/kernels.cu:913-957) on the tensor cores: an implicit GEMM
+ * per stride-phase class of input pixels (tcgen05 kind::f16, the fp32
+ * output gradient as three bf16 terms whose sum is exact, the int8 weights
+ * exact in bf16, fp32 accumulation).  Same arguments and result as the
+ * reference launcher up to the order of the fp32 additions (relative
+ * differences around 1e-6 of the gradient's scale).  Needs Cout % 8 == 0,
+ * at most 4 stride phases and 16 taps per phase.  Keeps a grow-only
+ * per-device buffer for the bf16 weight image.  Returns 0, -1 for an
+ * unsupported conv, or a CUDA error code. */
+int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, int w_ld, float w_scale,
+                               float *grad_input, int b, int cin, int h, int w, int cout, int kh, int kw,
+                               int sh, int sw, int ph, int pw, int ho, int wo, void *stream);
+
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier
  * wait gave up.  Synchronises the device; clears the word if clear != 0. */
 int trba_tc_error_poll(int clear);

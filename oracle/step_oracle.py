@@ -332,6 +332,35 @@ def linear_fwd(x, w, b=None):
     return y
 
 
+# ------------------------------------------------------------ optimiser --
+def adam_vec_step(p, g, m, v, lr, wd, bc1, bc2):
+    """Adam for a vector parameter (src/opt.rs:46-65, f64 intermediates, L2
+    weight decay folded into the gradient), in place on p, m, v."""
+    b1, b2, eps = float(F32(0.9)), float(F32(0.999)), float(F32(1e-8))
+    gi = g.astype(np.float64) + float(wd) * p.astype(np.float64)
+    m[...] = (b1 * m.astype(np.float64) + (1.0 - b1) * gi).astype(F32)
+    v[...] = (b2 * v.astype(np.float64) + (1.0 - b2) * gi * gi).astype(F32)
+    mh, vh = m.astype(np.float64) / bc1, v.astype(np.float64) / bc2
+    p -= (float(lr) * mh / (np.sqrt(vh) + eps)).astype(F32)
+
+
+def muon_host_step(p, g, lr, wd, cap):
+    """Momentum-free Muon for a matrix parameter (later snapshot src/opt.rs
+    muon_step_f32): scale = min(sqrt(min(rows, cols)) / ||g||_F, cap),
+    step = lr * sqrt(max(rows, cols)) * scale, decoupled weight decay; in
+    place on p (non-finite results become 0)."""
+    lr, wd = F32(lr), F32(wd)
+    rows, cols = p.shape
+    sq = F32((g.astype(F32) * g.astype(F32)).astype(np.float64).sum())
+    frob = max(F32(np.sqrt(sq)), F32(1e-8))
+    scale = min(F32(np.sqrt(F32(min(rows, cols)))) / frob, F32(cap))
+    lr_eff = lr * F32(np.sqrt(F32(max(rows, cols))))
+    step = F32(lr_eff * scale)
+    dec = F32(F32(1.0) - lr * wd)
+    u = (p * dec - step * g).astype(F32)
+    p[...] = np.where(np.isfinite(u), u, F32(0))
+
+
 # ---------------------------------------------------------------- oracle --
 @dataclass
 class ConvState:
@@ -638,7 +667,13 @@ class OracleTrba:
         y = linear_fwd(cat.reshape(b * t, 2 * H), self.p[f"rnn{li}.proj.w"], self.p[f"rnn{li}.proj.b"])
         return y.reshape(-1), dict(x=x, f=f, r=r, cat=cat, b=b, t=t)
 
-    def lstm_dir_bwd(self, pre, dh_out, tr, trc, rev):
+    def lstm_dir_bwd(self, pre, dh_out, tr, trc, rev, true_cell_grad=False):
+        """Backward through one direction.  The reference carries the cell
+        gradient into the previous step as dc and multiplies it there by that
+        step's own forget gate (src/rnn.rs:267, later snapshot); the chain
+        rule multiplies by the forget gate of the step the gradient comes
+        from.  true_cell_grad=True computes the latter (for the
+        finite-difference checks); the default keeps the reference's."""
         b, t = tr["b"], tr["t"]
         w_ih, w_hh = self.p[pre + ".w_ih"], self.p[pre + ".w_hh"]
         H, D = w_hh.shape[1], w_ih.shape[1]
@@ -654,10 +689,13 @@ class OracleTrba:
             ig, fg, cg, og = gr[:, :H], gr[:, H:2 * H], gr[:, 2 * H:3 * H], gr[:, 3 * H:]
             tc = tanh32(c)
             dh = (dh_out[step] + dh_next).astype(F32)
-            dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
+            if true_cell_grad:
+                dc = (dh * og * (F32(1) - tc * tc) + dc_next).astype(F32)
+            else:
+                dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
             dg = np.concatenate([dc * cg * ig * (F32(1) - ig), dc * c_prev * fg * (F32(1) - fg),
                                  dc * ig * (F32(1) - cg * cg), dh * tc * og * (F32(1) - og)], axis=1).astype(F32)
-            dc_next = dc
+            dc_next = (dc * fg).astype(F32) if true_cell_grad else dc
             dg_all[:, tt] = dg
             hp_all[:, tt] = trc["hprev"][step]
             dh_next = dot64(dg, w_hh)
@@ -778,7 +816,10 @@ class OracleTrba:
             x, _ = self.bilstm_layer_fwd(li, x, b, t)
         return self.greedy_decode(x.reshape(b, t, self.cfg.hidden), b, t)
 
-    def attn_bwd(self, d_logits, tr):
+    def attn_bwd(self, d_logits, tr, true_cell_grad=False):
+        """Backward through the decoder; true_cell_grad as in lstm_dir_bwd
+        (the reference's decoder cell, src/attn.rs:314 of the later snapshot,
+        carries the cell gradient the same way as its BiLSTM)."""
         cfg, P, G = self.cfg, self.p, self.g
         b, t, steps = tr["b"], tr["t"], tr["steps"]
         H, V = cfg.hidden, cfg.classes
@@ -803,10 +844,13 @@ class OracleTrba:
             ig, fg, cg, og = g[:, :H], g[:, H:2 * H], g[:, 2 * H:3 * H], g[:, 3 * H:]
             tc = tanh32(tr["cs"][st])
             dh = (d_out_hid[st] + dh_next).astype(F32)
-            dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
+            if true_cell_grad:
+                dc = (dh * og * (F32(1) - tc * tc) + dc_next).astype(F32)
+            else:
+                dc = (dh * og * (F32(1) - tc * tc) + dc_next * fg).astype(F32)
             dg = np.concatenate([dc * cg * ig * (F32(1) - ig), dc * c_prev * fg * (F32(1) - fg),
                                  dc * ig * (F32(1) - cg * cg), dh * tc * og * (F32(1) - og)], axis=1).astype(F32)
-            dc_next = dc
+            dc_next = (dc * fg).astype(F32) if true_cell_grad else dc
             dg_all[st] = dg
             dctx = dot64(dg, wc)
             dh_prev = dot64(dg, P["attn.w_hh"])
@@ -981,7 +1025,6 @@ class OracleTrba:
             f = F32(1.0)
         self.t += 1
         bc1, bc2 = bias_corrections(self.t)
-        b1, b2, eps = float(F32(0.9)), float(F32(0.999)), float(F32(1e-8))
         for n, k in kinds.items():
             if k == "conv_w":
                 continue
@@ -990,21 +1033,9 @@ class OracleTrba:
             if k == "vec":
                 m = self.adam_m.setdefault(n, np.zeros_like(p))
                 v = self.adam_v.setdefault(n, np.zeros_like(p))
-                gi = g.astype(np.float64) + float(wd) * p.astype(np.float64)
-                m[...] = (b1 * m.astype(np.float64) + (1.0 - b1) * gi).astype(F32)
-                v[...] = (b2 * v.astype(np.float64) + (1.0 - b2) * gi * gi).astype(F32)
-                mh, vh = m.astype(np.float64) / bc1, v.astype(np.float64) / bc2
-                p -= (float(lr) * mh / (np.sqrt(vh) + eps)).astype(F32)
-            else:  # host Muon, src/opt.rs muon_step_f32
-                rows, cols = p.shape
-                sq = F32((g.astype(F32) * g.astype(F32)).astype(np.float64).sum())
-                frob = max(F32(np.sqrt(sq)), F32(1e-8))
-                scale = min(F32(np.sqrt(F32(min(rows, cols)))) / frob, F32(cfg.muon_cap))
-                lr_eff = lr * F32(np.sqrt(F32(max(rows, cols))))
-                step = F32(lr_eff * scale)
-                dec = F32(F32(1.0) - lr * wd)
-                u = (p * dec - step * g).astype(F32)
-                p[...] = np.where(np.isfinite(u), u, F32(0))
+                adam_vec_step(p, g, m, v, lr, wd, bc1, bc2)
+            else:
+                muon_host_step(p, g, lr, wd, cfg.muon_cap)
         for c in conv_specs(cfg):  # device Muon per conv (src/qnet.rs:559-573)
             w, g = self.p[f"{c.name}.w"], self.g[f"{c.name}.w"]
             gsq = np.zeros(1, np.float64)

@@ -1,0 +1,167 @@
+"""The conv input gradient on the tensor cores (trba_conv_grad_input_i8_tc and
+the training step's dgrad_mode = 1) against the reference's exact gather.
+
+Op level: every conv shape of the model (and odd ones: Cin not a multiple of
+16, a partial last tile, 1x1 stride 2, the 2x2 stride (2, 1) head conv) on
+the same seeded dy and int8 weights, through the C ABI, against the oracle's
+launch_conv_backward_grad_input_i8 (the reference's f32 summation order).
+The tensor-core result is exact up to the order of its fp32 additions, so the
+bar is max |diff| <= 1e-4 x max |gi| (the reference's own bar for gradients
+is 1e-3).
+
+Step level: the forward and the sequence head do not touch the input
+gradient, so the losses and the head's parameter gradients must equal the
+oracle's exactly; every conv gradient must stay within 1e-3 of its scale on
+the convs the input gradient has not yet reached through a re-quantisation.
+Over 200 steps the loss stays within 1% of the oracle's.
+"""
+import ctypes as C
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+sys.path.insert(0, str(REPO / "oracle"))
+import step_oracle as so  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+A16 = lambda x: (x + 15) & ~15  # noqa: E731
+
+# (B, Cin, H, W, Cout, kh, kw, sh, sw, ph, pw): the model's conv shapes at
+# 32x160 (fd 128) with small batches, then odd shapes.
+SHAPES = [
+    (2, 16, 32, 160, 32, 3, 3, 1, 1, 1, 1),    # stem.3
+    (3, 32, 16, 80, 64, 3, 3, 2, 2, 1, 1),     # layer1.0.conv1 (stride 2)
+    (3, 32, 16, 80, 64, 1, 1, 2, 2, 0, 0),     # layer1.0.downsample (1x1 stride 2: three phases without taps)
+    (4, 64, 8, 40, 64, 3, 3, 1, 1, 1, 1),      # layer2.x
+    (4, 64, 8, 40, 128, 3, 3, 2, 2, 1, 1),     # layer3.0.conv1
+    (5, 128, 4, 20, 128, 3, 3, 1, 1, 1, 1),    # layer3/4
+    (5, 128, 4, 20, 128, 2, 2, 2, 1, 0, 1),    # conv_out.0 (2x2, stride (2, 1), pad (0, 1))
+    (5, 128, 2, 21, 128, 2, 2, 1, 1, 0, 0),    # conv_out.3
+    (3, 24, 7, 9, 16, 3, 3, 1, 1, 1, 1),       # Cin 24 (padded N), 7x9 planes, partial tile
+    (2, 8, 5, 6, 8, 3, 3, 2, 2, 1, 1),         # Cout 8, odd planes, stride 2
+    (1, 200, 4, 4, 16, 3, 3, 1, 1, 1, 1),      # Cin > 128: two N tiles
+]
+
+
+def _out_hw(h, w, kh, kw, sh, sw, ph, pw):
+    return (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "b{}_c{}_{}x{}_o{}_k{}x{}_s{}{}".format(*s[:9]))
+def test_tc_input_gradient_matches_exact_gather(shape, lib, cuda, oracle):
+    import torch
+    B, cin, h, w, cout, kh, kw, sh, sw, ph, pw = shape
+    ho, wo = _out_hw(h, w, kh, kw, sh, sw, ph, pw)
+    rng = np.random.default_rng(sum(shape))
+    dy = (rng.standard_normal((B, cout, ho, wo)) * 1e-3).astype(np.float32)
+    dy[rng.random(dy.shape) < 0.3] = 0.0  # masked gradients carry many zeros
+    k = cin * kh * kw
+    wld = A16(k)
+    wq = np.zeros((A16(cout), wld), np.int8)
+    wq[:cout, :k] = rng.integers(-127, 128, (cout, k))
+    w_s = 0.0123
+    want = np.zeros(B * cin * h * w, np.float32)
+    oracle.launch_conv_backward_grad_input_i8(dy.ctypes.data, wq.ctypes.data, wld, w_s, want.ctypes.data, B, cin,
+                                              h, w, cout, kh, kw, sh, sw, ph, pw, ho, wo, None)
+    d_dy = torch.from_numpy(dy).cuda()
+    d_wq = torch.from_numpy(wq).cuda()
+    d_gi = torch.full((B * cin * h * w,), float("nan"), dtype=torch.float32, device="cuda")
+    rc = lib.trba_conv_grad_input_i8_tc(C.c_void_p(d_dy.data_ptr()), C.c_void_p(d_wq.data_ptr()), wld, w_s,
+                                        C.c_void_p(d_gi.data_ptr()), B, cin, h, w, cout, kh, kw, sh, sw, ph, pw,
+                                        ho, wo, None)
+    assert rc == 0, lib.trba_last_error_string()
+    got = d_gi.cpu().numpy()
+    assert np.isfinite(got).all(), "unwritten outputs"
+    scale = float(np.abs(want).max())
+    err = float(np.abs(got - want).max())
+    assert err <= 1e-4 * scale, f"max diff {err:.3g} vs scale {scale:.3g}"
+    assert lib.trba_tc_error_poll(1) == 0
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()
+
+
+def test_tc_input_gradient_repeat_calls_are_identical(lib, cuda):
+    """Same inputs, same result bit for bit (no atomics in the reduction)."""
+    import torch
+    B, cin, h, w, cout = 4, 64, 8, 40, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dy = torch.randn((B, cout, h, w), device="cuda", generator=g) * 1e-3
+    wq = torch.randint(-127, 128, (cout, A16(cin * 9)), dtype=torch.int8, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        gi = torch.empty((B, cin, h, w), device="cuda")
+        assert lib.trba_conv_grad_input_i8_tc(C.c_void_p(dy.data_ptr()), C.c_void_p(wq.data_ptr()), A16(cin * 9),
+                                              0.5, C.c_void_p(gi.data_ptr()), B, cin, h, w, cout, 3, 3, 1, 1, 1,
+                                              1, h, w, None) == 0
+        outs.append(gi.cpu())
+    assert torch.equal(outs[0], outs[1])
+
+
+def _setup(geom, B, seed, dgrad_mode):
+    import trba_b200.model as tm
+    ocfg = so.Config(**geom)
+    params = so.init_params(ocfg, seed)
+    gm = tm.QatModel(tm.Config(**geom, batch=B, dgrad_mode=dgrad_mode))
+    names = [n for n, _, _ in so.manifest(ocfg)]
+    gm.set_params(np.concatenate([params[n].ravel() for n in names]).astype(np.float32))
+    return ocfg, params, gm
+
+
+def _to_dev(img, ti, tg, ct, steps):
+    import torch
+    import trba_b200.model as tm
+    return [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (img, *tm.pack_labels(ti, tg, ct, steps))]
+
+
+HEAD = ("rnn", "attn", "ctc")
+
+
+@pytest.mark.parametrize("geom,B", [(dict(img_w=64, max_len=4), 48), (dict(img_w=160, max_len=20), 48)],
+                         ids=["32x64_b48", "32x160_b48"])
+def test_step_with_tc_input_gradient(geom, B, lib, cuda):
+    ocfg, params, gm = _setup(geom, B, seed=31, dgrad_mode=1)
+    img, ti, tg, ct = so.make_batch(ocfg, B, seed=8)
+    orc = so.OracleTrba(ocfg, params, so.CpuBackend(REPO / "oracle" / "liboracle.so"))
+    res = orc.train_step(img, ti, tg, ct)
+    gm.forward_backward(*_to_dev(img, ti, tg, ct, ocfg.steps))
+    want = np.array([res["loss"], res["attn"], res["ctc"]])
+    assert np.allclose(gm.loss(), want, rtol=1e-6, atol=0)
+    grads = gm.get_grads()
+    rel = {}
+    for name, off, rows, cols, kind in gm.manifest():
+        n = rows * cols if cols else rows
+        g, w = grads[off:off + n], orc.g[name].ravel()
+        rel[name] = float(np.abs(g - w).max() / (np.abs(w).max() + 1e-30))
+    head = {k: v for k, v in rel.items() if k.startswith(HEAD)}
+    assert max(head.values()) <= 1e-6, sorted(head.items(), key=lambda kv: -kv[1])[:3]
+    # the last conv's weight gradient reads dy from the head only
+    assert rel["conv_out.3.w"] <= 1e-6
+    # the conv before it reads the first tensor-core input gradient once
+    assert rel["conv_out.0.w"] <= 1e-3, rel["conv_out.0.w"]
+    assert lib.trba_tc_error_poll(1) == 0
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()
+
+
+def test_loss_curve_200_steps_tc_input_gradient(lib, cuda):
+    """200 training steps with the tensor-core input gradient: the loss stays
+    within 1% of the reference's at every step (TRBA-small 32x64, batch 8, a
+    fresh synthetic batch every step).  The reference side is the oracle's
+    step driving the reference's own CPU backend (oracle/_ref, where it was
+    built; else the oracle's C restatement of it)."""
+    geom = dict(img_w=64, max_len=4)
+    ocfg, params, gm = _setup(geom, 8, seed=21, dgrad_mode=1)
+    ref = REPO / "oracle" / "_ref" / "libtrba_ref_omp.so"
+    orc = so.OracleTrba(ocfg, params, so.CpuBackend(ref if ref.exists() else REPO / "oracle" / "liboracle.so"))
+    lo, lg = [], []
+    for i in range(200):
+        img, ti, tg, ct = so.make_batch(ocfg, 8, seed=1000 + i)
+        lo.append(orc.train_step(img, ti, tg, ct)["loss"])
+        gm.train_step(*_to_dev(img, ti, tg, ct, ocfg.steps))
+        lg.append(float(gm.loss()[0]))
+    lo, lg = np.array(lo), np.array(lg)
+    rel = np.abs(lg - lo) / np.abs(lo)
+    assert rel.max() < 0.01, f"max relative loss gap {rel.max():.3g} at step {int(rel.argmax())}"
+    assert np.mean(lg[-20:]) < np.mean(lg[:20]), "the loss did not decrease"

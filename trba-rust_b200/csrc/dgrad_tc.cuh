@@ -1,0 +1,110 @@
+// Conv input gradient on the tensor cores (tcgen05 kind::f16), as an
+// implicit GEMM over stride-phase classes.
+//
+//   gi[b, ci, y, x] = w_s * sum_{(kh, kw), co} dy[b, co, oy, ox] * Wq[co, ci, kh, kw]
+//   with oy = (y + pH - kh) / sH, ox = (x + pW - kw) / sW on the output grid
+//
+// (the reference's launch_conv_backward_grad_input_i8, later snapshot
+// cuda/kernels.cu:913-957, and src/qnet.rs:1068-1080).
+//
+// Input pixels are split into classes by their stride phase (y mod sH,
+// x mod sW): within a class every pixel uses the same set of kernel taps, so
+// the class is a dense GEMM with M = its pixels, N = Cin and K = taps x Cout
+// (no zero taps in the operand, only the plane border).  The int8 weights
+// are exact in bf16; the fp32 dy is written as the sum of three bf16 terms
+// (hi + mid + lo carry its 24-bit significand), and the three products are
+// accumulated into one fp32 TMEM accumulator.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+namespace trba {
+namespace dgtc {
+
+constexpr int kMaxClasses = 4;
+constexpr int kMaxTaps = 16;
+constexpr int kChunk = 64;  // K values per shared-memory stage row (128 bytes of bf16)
+
+struct Class {
+    int py, px;    // stride phase of the class's input pixels
+    int Hc, Wc;    // class sub-grid (pixels y = py + sH * i, x = px + sW * j)
+    int ntaps;     // kernel taps that reach the output grid from this phase
+    int kchunks;   // ceil(ntaps * Cout / 64): K chunks of the class GEMM
+    int b_off;     // first chunk of this class in the weight image
+    int tile0;     // first tile of this class in the launch (batch dependent)
+    int mtiles;    // 128-pixel tiles of this class (batch dependent)
+    int8_t kh[kMaxTaps], kw[kMaxTaps];
+};
+
+struct Plan {
+    int ncls;
+    int Cin, Cout, H, W, Ho, Wo, kH, kW, sH, sW, pH, pW;
+    int Npad;          // Cin rounded up to the N tile
+    int BN;            // N of one MMA tile: 16, 32, 64 or 128
+    int ntn;           // N tiles (Npad / BN)
+    int total_chunks;  // chunks of the weight image (sum over classes)
+    int B;             // batch of the launch
+    int tiles;         // tiles of the launch (batch dependent)
+    Class cls[kMaxClasses];
+};
+
+// Builds the class plan of a conv, or returns false when the kernel does not
+// serve it (Cout not a multiple of 8, more than 4 stride phases or 16 taps
+// per phase).  Batch-dependent fields are filled by set_batch.
+bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
+               Plan &p);
+void set_batch(Plan &p, int B);
+// Bytes of the bf16 weight image of a plan.
+inline long long weight_image_bytes(const Plan &p) { return (long long)p.total_chunks * p.Npad * 128; }
+
+// Device-side writer of the weight image: element (chunk gc, row n, k of
+// the chunk) of the image of `p` holds bf16(wq[co, n, kh, kw]) for the tap
+// and output channel that k selects, zero past the taps or past Cin; stored
+// in the 128-byte-swizzled K-major layout the MMA reads, so one bulk copy
+// of `BN` rows places a stage's operand.  wq: [a16(Cout), kp] int8 with K
+// order (ci, kh, kw) (the forward GEMM operand).
+__device__ __forceinline__ void image_entry(const Plan &p, long long e, int &gc, int &n, int &kl) {
+    kl = (int)(e & 63);
+    const long long r = e >> 6;
+    n = (int)(r % p.Npad);
+    gc = (int)(r / p.Npad);
+}
+__device__ __forceinline__ long long image_offset(int gc, int n, int kl, int Npad) {
+    return ((long long)gc * Npad + n) * 128 + ((((kl >> 3) ^ (n & 7))) << 4) + (kl & 7) * 2;
+}
+// Source K index (ci * kh*kw + tap) in the forward operand of image element
+// (gc, n, kl), or -1 for a zero entry.
+__device__ __forceinline__ int image_source(const Plan &p, int gc, int n, int kl, int &co) {
+    int c = 0;
+    while (c + 1 < p.ncls && gc >= p.cls[c + 1].b_off) ++c;
+    const Class &C = p.cls[c];
+    const int k = (gc - C.b_off) * kChunk + kl;
+    const int tap = k / p.Cout;
+    co = k - tap * p.Cout;
+    if (tap >= C.ntaps || n >= p.Cin) return -1;
+    return n * p.kH * p.kW + C.kh[tap] * p.kW + C.kw[tap];
+}
+
+// One launch: gi (NCHW f32) from dy (NCHW f32) and the weight image.
+// Epilogue as the exact kernel's: v = acc * w_s (the device scalar w_s, or
+// w_s_val when w_s is null); v = mask_q[i] > 0 ? v : 0 (when mask_q);
+// v += add[i] (when add); gi[i] = v; and, when gmax_out, atomic max of
+// |v * gmax_scale| into gmax_out.  add may alias gi.
+void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
+            const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale, float *gmax_out,
+            cudaStream_t st);
+
+// Writes the weight image of `p` from an int8 weight matrix [Cout rows,
+// w_ld] with K order (ci, kh, kw).
+__global__ void image_from_wq_kernel(const __grid_constant__ Plan P, const int8_t *__restrict__ wq, int w_ld,
+                                     uint8_t *__restrict__ wimg);
+
+// Device error word of this kernel (a bounded wait gave up); clears it when
+// clear.  Synchronises the device.
+int error_poll(bool clear);
+
+}  // namespace dgtc
+}  // namespace trba

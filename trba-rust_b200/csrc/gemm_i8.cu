@@ -32,6 +32,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "dgrad_tc.cuh"
 #include "gemm_i8.cuh"
 #include "trba_backend.h"
 #include "tc_primitives.cuh"
@@ -954,7 +955,8 @@ int trba_tc_error_poll(int clear) {
         const int z = 0;
         TRBA_CHECK(cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)));
     }
-    return v;
+    // the input-gradient kernel keeps its own word (another translation unit)
+    return (v | trba::dgtc::error_poll(clear != 0)) ? 1 : 0;
 }
 
 }  // extern "C"

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "dgrad_tc.cuh"
 #include "gemm_i8.cuh"
 #include "qat_kernels.cuh"
 #include "seq_kernels.cuh"
@@ -104,7 +105,11 @@ struct ConvL {
     i64 w_off, gamma_off, beta_off;
     // persistent
     Ref<int8_t> wq;          // [a16(cout), kp]
-    Ref<float> wT;           // (float) wq in the input-gradient layout (dgrad_weights_index)
+    Ref<float> wT;           // (float) wq in the input-gradient layout (dgrad_weights_index), exact mode
+    dgtc::Plan tc;           // tensor-core input gradient: class plan (tc_ok) and its bf16 weight image
+    bool tc_ok = false;
+    Ref<uint8_t> wimg;
+    Ref<dgtc::Plan> d_tc;
     std::vector<int> cls_perm, cls_start;  // tap-class pixel order of the input gradient (empty: natural)
     Ref<int32_t> d_perm, d_cstart;
     Ref<float> ws, wmax;     // device scalars
@@ -215,8 +220,10 @@ struct trba_model {
         float *ws, *wmax;
         float *mean, *var, *run_mean, *run_var;
         int cout, K, kp;
-        float *wT;
+        float *wT;  // null in tensor-core mode
         int khw;
+        const dgtc::Plan *tc;  // tensor-core mode: the plan (device copy) and the image it writes
+        uint8_t *wimg;
     };
     ConvTab *d_convtab = nullptr;
     long long t = 0;
@@ -445,6 +452,19 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
         const int r = (int)(e / t.kp), c = (int)(e - (i64)r * t.kp);
         t.wq[e] = (r < t.cout && c < t.K) ? quant_w(P[s.off + (i64)r * t.K + c], sc) : (int8_t)0;
     }
+    if (t.wimg) {  // tensor-core input gradient: the bf16 weight image
+        const dgtc::Plan &tp = *t.tc;
+        const i64 n_img = (i64)tp.total_chunks * tp.Npad * dgtc::kChunk;
+        for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < n_img; e += (i64)gridDim.x * blockDim.x) {
+            int gc, n, kl, co;
+            dgtc::image_entry(tp, e, gc, n, kl);
+            const int src = dgtc::image_source(tp, gc, n, kl, co);
+            const float v = src >= 0 ? (float)quant_w(P[s.off + (i64)co * t.K + src], sc) : 0.0f;
+            *reinterpret_cast<__nv_bfloat16 *>(t.wimg + dgtc::image_offset(gc, n, kl, tp.Npad)) =
+                __float2bfloat16_rn(v);
+        }
+    }
+    if (!t.wT) return;
     const int cin = t.K / t.khw;
     const i64 nT = (i64)((cin + 15) >> 4) * t.khw * t.cout * 16;
     for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < nT; e += (i64)gridDim.x * blockDim.x) {
@@ -524,6 +544,8 @@ void plan(trba_model *m) {
         // Input-gradient pixel order: grouped by valid taps (strided convs) or
         // by valid kernel rows (stride 1).
         qat::dgrad_classes(H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, s1 == 1 && s2 == 1, L.cls_perm, L.cls_start);
+        L.tc_ok = m->cfg.dgrad_mode == 1 &&
+                  dgtc::make_plan(cin, cout, H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, L.tc);
         m->convs.push_back(L);
         return (int)m->convs.size() - 1;
     };
@@ -639,8 +661,13 @@ void allocate(trba_model *m) {
         ConvL &L = m->convs[i];
         const i64 rows = L.rows(B), rp = a16l(rows), n = (i64)B * L.cout * L.Ho * L.Wo;
         L.wq = b.p<int8_t>((i64)a16(L.cout) * L.kp);
-        L.wT = b.p<float>(qat::dgrad_weights_size(L.cin, L.cout, L.kh * L.kw));
-        if (!L.cls_perm.empty()) {
+        if (L.tc_ok) {
+            L.wimg = b.p<uint8_t>(dgtc::weight_image_bytes(L.tc));
+            L.d_tc = b.p<dgtc::Plan>(1);
+        } else {
+            L.wT = b.p<float>(qat::dgrad_weights_size(L.cin, L.cout, L.kh * L.kw));
+        }
+        if (!L.tc_ok && !L.cls_perm.empty()) {
             L.d_perm = b.p<int32_t>((i64)L.cls_perm.size());
             L.d_cstart = b.p<int32_t>((i64)L.cls_start.size());
         }
@@ -912,6 +939,12 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
         const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
                              valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
         ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.st);
+        if (L.tc_ok) {
+            dgtc::Plan p = L.tc;
+            dgtc::set_batch(p, B);
+            dgtc::launch(p, L.wimg.get(), dy, L.ws.get(), 1.0f, mask_q, add, gi, gmax_scale, gmax_out, c.st);
+            return;
+        }
         qat::dgrad(dy, L.wT.get(), L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
                    L.Wo, L.cls_perm.empty() ? nullptr : L.d_perm.get(),
                    L.cls_perm.empty() ? nullptr : L.d_cstart.get(), (int)L.cls_start.size() - 1, mask_q, add, gi,
@@ -1299,8 +1332,10 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     std::vector<trba_model::ConvTab> tab;
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
-                       L.run_var.get(), L.cout, L.K, L.kp, L.wT.get(), L.kh * L.kw});
-        if (!L.cls_perm.empty()) {
+                       L.run_var.get(), L.cout, L.K, L.kp, L.tc_ok ? nullptr : L.wT.get(), L.kh * L.kw,
+                       L.tc_ok ? L.d_tc.get() : nullptr, L.tc_ok ? L.wimg.get() : nullptr});
+        if (L.tc_ok) TRBA_CHECK(cudaMemcpy(L.d_tc.get(), &L.tc, sizeof(dgtc::Plan), cudaMemcpyHostToDevice));
+        if (!L.tc_ok && !L.cls_perm.empty()) {
             TRBA_CHECK(cudaMemcpy(L.d_perm.get(), L.cls_perm.data(), sizeof(int) * L.cls_perm.size(),
                                   cudaMemcpyHostToDevice));
             TRBA_CHECK(cudaMemcpy(L.d_cstart.get(), L.cls_start.data(), sizeof(int) * L.cls_start.size(),
