@@ -76,6 +76,15 @@ int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, in
                                float *grad_input, int b, int cin, int h, int w, int cout, int kh, int kw,
                                int sh, int sw, int ph, int pw, int ho, int wo, void *stream);
 
+/* Self-test of the bounded waits of the tensor-core kernels (no
+ * counterpart in the reference): runs one small tensor-core input-gradient
+ * launch whose weight copies are deliberately never issued, so its pipeline
+ * waits give up after limit_ns instead of hanging; the kernel releases its
+ * tensor memory and raises the device error word.  Synchronises the stream;
+ * returns the error word (1: the waits gave up as designed), which it
+ * clears, or a negative value / CUDA error code. */
+int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream);
+
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier
  * wait gave up.  Synchronises the device; clears the word if clear != 0. */
 int trba_tc_error_poll(int clear);

@@ -45,6 +45,8 @@ typedef struct {
     int wgrad_mode;   /* 0: reference-compatible operand order, 1: dW = dX^T col */
     int dgrad_mode;   /* conv input gradient: 0 exact (the reference's f32 order, CUDA cores),
                          1 tensor cores (implicit GEMM, fp32 dy as three bf16 terms) */
+    int wq_per_channel; /* conv weight quantisation: 0 per tensor (the reference, src/qnet.rs:316-331),
+                           1 per output channel (scale max |w[row]| / 127 for each row) */
 } trba_model_config;
 
 /* TRBA-small defaults (fd 128, hidden 64, 130 classes, 32x160, max_len 20). */

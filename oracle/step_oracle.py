@@ -121,6 +121,9 @@ class Config:
     clip_warmup: int = 500
     muon_cap: float = 10.0
     wgrad_mode: str = "compat"
+    # Extension (the reference quantises per tensor, src/qnet.rs:316-331):
+    # one weight scale per output channel, max |w[row]| / 127.
+    wq_per_channel: bool = False
 
     @property
     def widths(self):
@@ -361,6 +364,50 @@ def muon_host_step(p, g, lr, wd, cap):
     p[...] = np.where(np.isfinite(u), u, F32(0))
 
 
+# ------------------------------------------ per-channel weight quantisation --
+def quantize_rows(w, rows_pad, kp):
+    """Per-output-channel quantisation (extension of src/qnet.rs:316-331):
+    s[r] = max |w[r]| / 127 (1 for an all-zero row, division in f64 rounded
+    to f32), q = round-half-away(clamp(f32(w / s[r]), +-127)), padded to the
+    GEMM operand [rows_pad, kp]."""
+    cout, k = w.shape
+    mx = np.abs(w).max(axis=1).astype(np.float64)
+    s = np.where(mx > 0, mx / 127.0, 1.0).astype(F32)
+    v = (w.astype(np.float64) / s.astype(np.float64)[:, None]).astype(F32)
+    v = np.clip(v, F32(-127), F32(127)).astype(np.float64)  # |v| + 0.5 is exact in f64
+    q = np.zeros((rows_pad, kp), np.int8)
+    q[:cout, :k] = (np.sign(v) * np.floor(np.abs(v) + 0.5)).astype(np.int8)
+    return q, s
+
+
+def grad_input_dequant(dy, wq, w_s, c, b, hi, wi, ho, wo):
+    """Input gradient with per-output-channel scales: each input element is
+    one f32 running sum over taps (kh, kw outer) and output channels
+    (inner) of dy * f32(wq * w_s[oc]), every multiply and add rounded (the
+    reference gather's order, cuda/kernels.cu:913-957 of the later snapshot,
+    with the dequantised weight in place of the int8 one and no final
+    scale)."""
+    k = c.cin * c.kh * c.kw
+    wdq = (wq[:c.cout, :k].astype(F32) * w_s[:, None]).astype(F32).reshape(c.cout, c.cin, c.kh, c.kw)
+    d = dy.reshape(b, c.cout, ho, wo)
+    acc = np.zeros((b, c.cin, hi, wi), F32)
+    ys, xs = np.arange(hi), np.arange(wi)
+    for kh in range(c.kh):
+        ny = ys + c.ph - kh
+        oky = (ny >= 0) & (ny % c.sh == 0) & (ny // c.sh < ho)
+        for kw in range(c.kw):
+            nx = xs + c.pw - kw
+            okx = (nx >= 0) & (nx % c.sw == 0) & (nx // c.sw < wo)
+            if not oky.any() or not okx.any():
+                continue
+            sh = np.zeros((b, c.cout, hi, wi), F32)  # dy at the tap's output position, 0 where none
+            yy, xx = np.nonzero(oky)[0], np.nonzero(okx)[0]
+            sh[:, :, yy[:, None], xx[None, :]] = d[:, :, (ny[yy] // c.sh)[:, None], (nx[xx] // c.sw)[None, :]]
+            for oc in range(c.cout):
+                acc = (acc + (sh[:, oc:oc + 1] * wdq[oc, :, kh, kw][None, :, None, None]).astype(F32)).astype(F32)
+    return acc.reshape(-1)
+
+
 # ---------------------------------------------------------------- oracle --
 @dataclass
 class ConvState:
@@ -394,6 +441,9 @@ class OracleTrba:
         ws = np.zeros(1, F32)
         kp = a16(c.k)
         wq = np.zeros((a16(c.cout), kp), np.int8)
+        if self.cfg.wq_per_channel:
+            cs.wq, cs.w_s = quantize_rows(w.reshape(c.cout, c.k), a16(c.cout), kp)
+            return
         self.be("launch_max_abs_f32", w, mx, w.size)
         self.be("launch_quantize_pad_i8", w, mx, ws, wq, c.cout, c.k, kp)
         cs.wq, cs.w_s = wq, F32(ws[0])
@@ -440,7 +490,11 @@ class OracleTrba:
         self.be("launch_gemm_int8", col, cs.wq, acc, rows, c.cout, k)
         n = b * c.cout * ho * wo
         x = np.zeros(n, F32)
-        self.be("launch_epilogue_f32", acc, c.cout, float(F32(s_in) * cs.w_s), x, c.cout, ho, wo, n)
+        if self.cfg.wq_per_channel:  # x = acc * (s_in * w_s[n]), NCHW
+            sc = (F32(s_in) * cs.w_s).astype(F32)
+            x[...] = (acc.reshape(b, ho * wo, c.cout).astype(F32) * sc).astype(F32).transpose(0, 2, 1).reshape(-1)
+        else:
+            self.be("launch_epilogue_f32", acc, c.cout, float(F32(s_in) * cs.w_s), x, c.cout, ho, wo, n)
         mean, var = np.zeros(c.cout, F32), np.zeros(c.cout, F32)
         if train:
             self.be("launch_bn_stats", x, b, c.cout, ho * wo, mean, var)
@@ -490,6 +544,8 @@ class OracleTrba:
         if not need_dx:
             return None
         gi = np.zeros(b * c.cin * hi * wi, F32)
+        if self.cfg.wq_per_channel:
+            return grad_input_dequant(dy, cs.wq, cs.w_s, c, b, hi, wi, ho, wo)
         self.be("launch_conv_backward_grad_input_i8", dy, cs.wq, kp, float(cs.w_s), gi, b, c.cin, hi, wi, c.cout,
                 c.kh, c.kw, c.sh, c.sw, c.ph, c.pw, ho, wo)
         return gi

@@ -35,6 +35,31 @@ def test_exports_match_nm():
     assert ref <= exported
 
 
+def test_static_archive_links_like_the_reference_backend(tmp_path):
+    """libtrba_cuda.a (the archive name the reference's build.rs links) holds
+    every declared function, and a C program calling the reference ABI links
+    against it with the reference's own link line (static cudart, stdc++, m,
+    dl, rt, pthread).  Linking only: nothing runs."""
+    import trba_b200
+    ar = REPO / "trba-rust_b200" / "libtrba_cuda.a"
+    assert ar.exists(), "static archive not built"
+    out = subprocess.run(["nm", "-g", "--defined-only", str(ar)], capture_output=True, text=True).stdout
+    defined = {l.split()[2] for l in out.splitlines() if len(l.split()) == 3 and l.split()[1] == "T"}
+    missing = [n for n in trba_b200.declared_functions() if n not in defined]
+    assert not missing, missing
+    src = tmp_path / "main.c"
+    src.write_text('#include "trba_backend.h"\n#include "trba_qat.h"\n'
+                   "int main(void) { trba_model_config c; trba_model_default_config(&c);\n"
+                   "  launch_gemm_int8(0, 0, 0, 0, 0, 0, 0); return c.fd == 128 ? 0 : 1; }\n")
+    cuda_lib = "/usr/local/cuda/lib64"
+    r = subprocess.run(["g++", "-o", str(tmp_path / "a.out"), "-x", "c", str(src), "-x", "none",
+                        f"-I{REPO / 'include'}", str(ar), f"-L{cuda_lib}", "-lcudart_static", "-lstdc++", "-lm",
+                        "-ldl", "-lrt", "-lpthread"], capture_output=True, text=True)
+    if r.returncode != 0 and "cannot find -lcudart_static" in r.stderr:
+        pytest.skip("CUDA toolkit's static runtime not installed here")
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
 def test_sticky_error_mode_reports_bad_shapes(lib):
     # A shape the reference rejects (odd H for the 2x2 pool) must not launch:
     # with abort disabled it lands in the error word instead.

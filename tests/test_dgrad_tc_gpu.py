@@ -165,3 +165,24 @@ def test_loss_curve_200_steps_tc_input_gradient(lib, cuda):
     rel = np.abs(lg - lo) / np.abs(lo)
     assert rel.max() < 0.01, f"max relative loss gap {rel.max():.3g} at step {int(rel.argmax())}"
     assert np.mean(lg[-20:]) < np.mean(lg[:20]), "the loss did not decrease"
+
+
+def test_bounded_waits_give_up_and_report(lib, cuda):
+    """A launch whose weight copies never come: every pipeline wait gives up
+    after 1 ms, the kernel frees its tensor memory and raises the error word
+    (no fault, no hang), and the next ordinary launch runs normally."""
+    import torch
+    assert lib.trba_tc_error_poll(1) == 0
+    assert lib.trba_tc_wait_selftest(1000000, None) == 1
+    assert lib.trba_tc_error_poll(1) == 0  # the self-test cleared the word
+    B, cin, h, w, cout = 2, 16, 8, 16, 16
+    dy = torch.ones((B, cout, h, w), device="cuda")
+    wq = torch.ones((cout, A16(cin * 9)), dtype=torch.int8, device="cuda")
+    gi = torch.empty((B, cin, h, w), device="cuda")
+    assert lib.trba_conv_grad_input_i8_tc(C.c_void_p(dy.data_ptr()), C.c_void_p(wq.data_ptr()), A16(cin * 9), 1.0,
+                                          C.c_void_p(gi.data_ptr()), B, cin, h, w, cout, 3, 3, 1, 1, 1, 1, h, w,
+                                          None) == 0
+    # interior pixels see all 9 taps x 16 channels of ones
+    assert float(gi[0, 0, 3, 5]) == 144.0
+    assert lib.trba_tc_error_poll(1) == 0
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()

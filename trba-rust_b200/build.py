@@ -2,7 +2,8 @@
 
 Compiles every ``csrc/*.cu`` with nvcc for ``compute_100a``/``sm_100a`` into
 ``_build/`` and links the shared library in-tree next to this file, so it
-travels with the source tree.  Rebuilds only what changed (object newer than
+travels with the source tree; the same objects also go into the static
+archive ``libtrba_cuda.a`` (the archive name the reference's build.rs links).  Rebuilds only what changed (object newer than
 its source and every header).  No PyTorch extension machinery: the library is
 a plain C ABI and is loaded with ctypes.
 """
@@ -19,6 +20,9 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "libtrba_b200.so"
+# The same objects as a static archive under the name the reference's
+# build.rs links (cargo:rustc-link-lib=static=trba_cuda).
+ARCHIVE = HERE / "libtrba_cuda.a"
 REPO = HERE.parent
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -88,6 +92,14 @@ def build(verbose: bool = False, jobs: int = 8) -> Path:
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    if not ARCHIVE.exists() or ARCHIVE.stat().st_mtime < max(o.stat().st_mtime for o in objs):
+        tmp = ARCHIVE.with_suffix(".a.tmp")
+        if tmp.exists():
+            tmp.unlink()
+        r = subprocess.run(["ar", "rcs", str(tmp), *[str(o) for o in objs]], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"ar failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, ARCHIVE)
     return LIB
 
 

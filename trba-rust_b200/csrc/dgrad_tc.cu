@@ -75,6 +75,7 @@ struct Args {
     const uint8_t *wimg;
     const float *w_s;  // device scalar, or null: w_s_val
     float w_s_val;
+    const float *ws_co;  // per-output-channel scales applied to dy, or null
     const int8_t *mask_q;
     const float *add;
     float *gi;
@@ -82,6 +83,8 @@ struct Args {
     float *gmax_out;
     int B;
     int stages;
+    unsigned long long wait_ns;  // limit of every pipeline wait
+    int skip_weights;            // self-test: never issue the weight copies (the waits give up)
 };
 
 __device__ __forceinline__ int tile_class(const Plan &P, int t) {
@@ -179,9 +182,9 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
             for (int kc = 0; kc < C.kchunks; ++kc, ++it) {
                 const int s = it % stages;
                 const uint32_t ph = (it / stages) & 1u;
-                if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort)) break;
+                if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort, a.wait_ns)) break;
                 uint8_t *stage = smem + (size_t)s * G::STAGE;
-                if (r == 0) {
+                if (r == 0 && !a.skip_weights) {
                     mbar_expect_tx(&ctl->bfull[s], G::B_BYTES);
                     bulk_load(stage + 3 * kPartBytes, a.wimg + ((i64)(C.b_off + kc) * P.Npad + n0) * kRowBytes,
                               G::B_BYTES, &ctl->bfull[s]);
@@ -205,6 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                     const float *src = dyb + (i64)co0 * HoWo + oy * P.Wo + ox;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) v[g][j] = ok ? __ldg(src + (i64)j * HoWo) : 0.0f;
+                    if (a.ws_co) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[g][j] = __fmul_rn(v[g][j], __ldg(a.ws_co + co0 + j));
+                    }
                 }
                 uint8_t *rowp = stage + r * kRowBytes;
 #pragma unroll
@@ -231,15 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
             bool ok = true;
             for (int t = blockIdx.x; t < P.tiles && ok; t += gridDim.x) {
                 const Class &C = P.cls[tile_class(P, t)];
-                if (!(ok = mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort))) break;
+                if (!(ok = mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort, a.wait_ns))) break;
                 tc_fence_after();
                 const uint32_t d = tbase + acc * BN;
                 for (int kc = 0; kc < C.kchunks; ++kc, ++it) {
                     const int s = it % stages;
                     const uint32_t ph = (it / stages) & 1u;
-                    if (!(ok = mbar_wait(&ctl->bfull[s], ph, abort))) break;
+                    if (!(ok = mbar_wait(&ctl->bfull[s], ph, abort, a.wait_ns))) break;
                     ctl->b_consumed = it + 1;
-                    if (!(ok = mbar_wait(&ctl->afull[s], ph, abort))) break;
+                    if (!(ok = mbar_wait(&ctl->afull[s], ph, abort, a.wait_ns))) break;
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + (size_t)s * G::STAGE);
                     const uint32_t b0 = st + 3 * kPartBytes;
@@ -272,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
         for (int t = blockIdx.x; t < P.tiles; t += gridDim.x) {
             const Class &C = P.cls[tile_class(P, t)];
             const int local = t - C.tile0, mt = local / P.ntn, n0 = (local - mt * P.ntn) * BN;
-            const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort);
+            const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort, a.wait_ns);
             __syncwarp();  // reconverge before the warp-collective tcgen05.ld
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
@@ -421,16 +428,8 @@ void set_batch(Plan &p, int B) {
     p.tiles = t;
 }
 
-void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
-            const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale, float *gmax_out,
-            cudaStream_t st) {
-    if (p.tiles <= 0) return;
-    Args a{};
-    a.dy = dy, a.wimg = wimg, a.w_s = w_s, a.w_s_val = w_s_val, a.mask_q = mask_q, a.add = add, a.gi = gi;
-    a.gmax_scale = gmax_out ? gmax_scale : nullptr;
-    a.gmax_out = gmax_scale ? gmax_out : nullptr;
-    a.B = p.B;
-    a.stages = stages_for(p.BN);
+namespace {
+void launch_args(const Plan &p, const Args &a, cudaStream_t st) {
     const int grid = std::min(p.tiles, sm_count());
     switch (p.BN) {
         case 16: launch_bn<16>(p, a, grid, st); break;
@@ -438,6 +437,23 @@ void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_
         case 64: launch_bn<64>(p, a, grid, st); break;
         default: launch_bn<128>(p, a, grid, st); break;
     }
+}
+}  // namespace
+
+void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
+            const float *ws_co, const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale,
+            float *gmax_out, cudaStream_t st) {
+    if (p.tiles <= 0) return;
+    Args a{};
+    a.dy = dy, a.wimg = wimg, a.w_s = w_s, a.w_s_val = w_s_val, a.ws_co = ws_co, a.mask_q = mask_q, a.add = add;
+    a.gi = gi;
+    a.gmax_scale = gmax_out ? gmax_scale : nullptr;
+    a.gmax_out = gmax_scale ? gmax_out : nullptr;
+    a.B = p.B;
+    a.stages = stages_for(p.BN);
+    a.wait_ns = 2000000000ull;
+    a.skip_weights = 0;
+    launch_args(p, a, st);
 }
 
 int error_poll(bool clear) {
@@ -500,7 +516,40 @@ extern "C" int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *w
     const long long n = (long long)p.total_chunks * p.Npad * dgtc::kChunk;
     dgtc::image_from_wq_kernel<<<grid_for(n), 256, 0, st>>>(p, weight_q, w_ld, img);
     TRBA_LAUNCH_CHECK();
-    dgtc::launch(p, img, grad_out, nullptr, w_scale, nullptr, nullptr, grad_input, nullptr, nullptr, st);
+    dgtc::launch(p, img, grad_out, nullptr, w_scale, nullptr, nullptr, nullptr, grad_input, nullptr, nullptr, st);
     e = cudaGetLastError();
     return e == cudaSuccess ? 0 : (int)e;
+}
+
+// Bounded-wait self-test: one small input-gradient launch whose weight copies
+// are never issued, so the MMA warp's first wait for them (and then every
+// other role's) gives up after limit_ns; the kernel frees its tensor memory,
+// sets the error word and returns.  Returns the error word (1 expected) and
+// clears it; the context stays usable.
+extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) {
+    using namespace trba;
+    dgtc::Plan p;
+    if (!dgtc::make_plan(16, 16, 8, 16, 3, 3, 1, 1, 1, 1, 8, 16, p)) return -1;
+    dgtc::set_batch(p, 2);
+    float *buf = nullptr;  // dy, gi (2 x 16 x 8 x 16 floats each) and a zero weight image
+    const size_t n = 2 * 16 * 8 * 16;
+    const size_t img = (size_t)dgtc::weight_image_bytes(p);
+    cudaError_t e = cudaMalloc(&buf, 2 * n * sizeof(float) + img);
+    if (e != cudaSuccess) return (int)e;
+    cudaStream_t st = as_stream(stream);
+    TRBA_CHECK(cudaMemsetAsync(buf, 0, 2 * n * sizeof(float) + img, st));
+    dgtc::Args a{};
+    a.dy = buf;
+    a.gi = buf + n;
+    a.wimg = reinterpret_cast<const uint8_t *>(buf + 2 * n);
+    a.w_s_val = 1.0f;
+    a.B = p.B;
+    a.stages = dgtc::stages_for(p.BN);
+    a.wait_ns = limit_ns;
+    a.skip_weights = 1;
+    dgtc::launch_args(p, a, st);
+    TRBA_CHECK(cudaStreamSynchronize(st));
+    const int v = dgtc::error_poll(true);
+    TRBA_CHECK(cudaFree(buf));
+    return v;
 }

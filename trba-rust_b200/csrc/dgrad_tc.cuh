@@ -89,13 +89,15 @@ __device__ __forceinline__ int image_source(const Plan &p, int gc, int n, int kl
 }
 
 // One launch: gi (NCHW f32) from dy (NCHW f32) and the weight image.
-// Epilogue as the exact kernel's: v = acc * w_s (the device scalar w_s, or
-// w_s_val when w_s is null); v = mask_q[i] > 0 ? v : 0 (when mask_q);
-// v += add[i] (when add); gi[i] = v; and, when gmax_out, atomic max of
-// |v * gmax_scale| into gmax_out.  add may alias gi.
+// ws_co (optional, per-output-channel weight scales): dy[b, co] is
+// multiplied by ws_co[co] as it is gathered.  Epilogue as the exact
+// kernel's: v = acc * w_s (the device scalar w_s, or w_s_val when w_s is
+// null); v = mask_q[i] > 0 ? v : 0 (when mask_q); v += add[i] (when add);
+// gi[i] = v; and, when gmax_out, atomic max of |v * gmax_scale| into
+// gmax_out.  add may alias gi.
 void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
-            const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale, float *gmax_out,
-            cudaStream_t st);
+            const float *ws_co, const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale,
+            float *gmax_out, cudaStream_t st);
 
 // Writes the weight image of `p` from an int8 weight matrix [Cout rows,
 // w_ld] with K order (ci, kh, kw).

@@ -130,20 +130,21 @@ struct EpiS32Atomic {
 struct EpiConvF32 {
     float *x;            // NCHW output, row r = b*HW + p, column = channel
     const float *s_in;   // device scalar: activation scale of the conv input
-    const float *w_s;    // device scalar: per-tensor weight scale
+    const float *w_s;    // weight scale: device scalar, or [N] per output channel
+    int per_channel;
     double *bn_acc;      // [2*N]: per-channel sum, then sum of squares (f64)
     int HW;
+    __device__ __forceinline__ float scale_of(int n) const { return fmul(*s_in, per_channel ? w_s[n] : *w_s); }
     __device__ void init(double *sm) {
         for (int i = threadIdx.x - 64; i < 2 * kMaxN; i += blockDim.x - 64) sm[i] = 0.0;
     }
     __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
-        const float scale = fmul(*s_in, *w_s);
         const bool rv = row < M;
         const int b = rv ? row / HW : 0, p = rv ? row - b * HW : 0;
         double s[32], q[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const float val = fmul((float)(int32_t)v[j], scale);
+            const float val = fmul((float)(int32_t)v[j], scale_of(col + j < N ? col + j : N - 1));
             const bool ok = rv && col + j < N;
             if (ok) x[((i64)b * N + col + j) * HW + p] = val;
             s[j] = ok ? (double)val : 0.0;
@@ -176,14 +177,13 @@ struct EpiConvF32 {
     }
     // columns [col, col + 16) of the tile row, taken from v[16 hi + j]
     __device__ void store_acc(int row, int col, int M, int N, const uint32_t (&v)[32], bool hi, Accum &a) {
-        const float scale = fmul(*s_in, *w_s);
         if (row >= M) return;
         const int b = row / HW, p = row - b * HW;
         float *xp = x + ((i64)b * N + col) * HW + p;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             if (col + j < N) {
-                const float val = fmul((float)(int32_t)(hi ? v[16 + j] : v[j]), scale);
+                const float val = fmul((float)(int32_t)(hi ? v[16 + j] : v[j]), scale_of(col + j));
                 xp[(i64)j * HW] = val;
                 const double d = (double)val;
                 a.s[j] += d;
@@ -858,9 +858,10 @@ bool gemm_i8_splitk_atomic(const int8_t *A, int lda, const int8_t *B, int ldb, i
 }
 
 bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, float *x,
-                      const float *s_in, const float *w_s, double *bn_acc, int HW, cudaStream_t st) {
+                      const float *s_in, const float *w_s, bool per_channel, double *bn_acc, int HW, cudaStream_t st) {
     if (N > kMaxN) return false;
-    return run_tc(A, lda, B, ldb, make_shape(M, N, K, 1), EpiConvF32{x, s_in, w_s, bn_acc, HW}, st);
+    return run_tc(A, lda, B, ldb, make_shape(M, N, K, 1), EpiConvF32{x, s_in, w_s, per_channel ? 1 : 0, bn_acc, HW},
+                  st);
 }
 
 bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float *bias, int M, int N, int K, int ld,

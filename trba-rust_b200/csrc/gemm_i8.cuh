@@ -17,9 +17,11 @@ bool gemm_i8_tc(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int 
 bool gemm_i8_splitk_atomic(const int8_t *A, int lda, const int8_t *B, int ldb, int32_t *C, int M, int N, int K,
                            int splits, cudaStream_t st);
 // Conv forward: x[b, n, p] = (float)acc[r = b*HW + p, n] * (s_in * w_s), and
-// bn_acc[n] += sum x, bn_acc[N + n] += sum x^2 (f64).  N <= 512.
+// bn_acc[n] += sum x, bn_acc[N + n] += sum x^2 (f64).  N <= 512.  w_s is a
+// device scalar, or (per_channel) one scale per output channel n.
 bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, float *x,
-                      const float *s_in, const float *w_s, double *bn_acc, int HW, cudaStream_t st);
+                      const float *s_in, const float *w_s, bool per_channel, double *bn_acc, int HW,
+                      cudaStream_t st);
 // Fused epilogues on row-major outputs [M, N]: the conv inference requant
 // (int8) and per-channel dequantisation (f32, optional bias and ReLU).
 bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float *bias, int M, int N, int K, int ld,

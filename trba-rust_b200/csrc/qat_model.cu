@@ -95,6 +95,7 @@ struct Seg {  // a parameter segment for the multi-tensor optimiser kernels
     int n;
     int rows, cols;
     int aux;  // conv: index into conv tables
+    int chan; // conv: offset of its first output channel among all convs' channels
 };
 
 struct ConvL {
@@ -205,7 +206,9 @@ struct trba_model {
     // optimiser scratch (zeroed per step)
     Ref<double> gsq_total;
     Ref<double> conv_gsq;  // per conv
-    Ref<unsigned> wmax_bits;  // per conv: max |w| as f32 bits (atomicMax), cleared before each re-quantisation
+    Ref<unsigned> wmax_bits;  // per conv (per output channel in per-channel mode): max |w| as f32 bits,
+                              // cleared before each re-quantisation
+    int n_chan = 0;           // output channels of all convs
     Ref<float> clip_f, mat_step, conv_step;
     Ref<double> step_state;  // [t, clip active, bc1, bc2]: advanced on the device every step
     // inputs staged for the host-buffer entry point
@@ -224,6 +227,7 @@ struct trba_model {
         int khw;
         const dgtc::Plan *tc;  // tensor-core mode: the plan (device copy) and the image it writes
         uint8_t *wimg;
+        int per_channel;       // per-output-channel weight scales (ws, wmax hold cout values)
     };
     ConvTab *d_convtab = nullptr;
     long long t = 0;
@@ -425,7 +429,22 @@ __global__ void conv_wmax_kernel(const Seg *segs, const float *P, unsigned *wmax
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, sm[w]);
-        atomicMax(wmax_bits + blockIdx.y, __float_as_uint(t));
+        atomicMax(wmax_bits + s.chan, __float_as_uint(t));
+    }
+}
+
+// Per-output-channel max |w| (per-channel weight quantisation): one warp per
+// weight row, rows of every conv in one launch (blockIdx.y = conv).
+__global__ void conv_wmax_rows_kernel(const Seg *segs, const float *P, unsigned *wmax_bits) {
+    const Seg s = segs[blockIdx.y];
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < s.rows; r += gridDim.x * warps) {
+        const float *row = P + s.off + (i64)r * s.cols;
+        float m = 0.0f;
+        for (int j = lane; j < s.cols; j += 32) m = fmaxf(m, fabsf(row[j]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) wmax_bits[s.chan + r] = __float_as_uint(m);
     }
 }
 
@@ -434,23 +453,36 @@ __device__ __forceinline__ int8_t quant_w(float w, float sc) {
     return (int8_t)roundf(fminf(fmaxf(v, -127.0f), 127.0f));
 }
 
-// Writes the padded int8 GEMM operand and, for the input gradient, the same
-// values as f32 in the [Cin / 16][tap][Cout][16] layout.
+__device__ __forceinline__ float wscale_of(unsigned bits) {
+    const double mx = (double)__uint_as_float(bits);
+    return (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
+}
+
+// Writes the padded int8 GEMM operand, the weight scale(s) and the input
+// gradient's weights: per tensor, the same int8 values as f32 in the
+// [Cin / 16][tap][Cout][16] layout (exact gather) or as the bf16 image of
+// the tensor-core kernel.  Per output channel (t.per_channel): row r has
+// scale max |w[r]| / 127; the exact gather's f32 weights are then the
+// dequantised values wq * w_s[r] (its final scale is 1) and the tensor-core
+// image keeps the int8 values (its producer scales dy per channel).
 __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_model::ConvTab *tab,
                                   const unsigned *wmax_bits) {
     const Seg s = segs[blockIdx.y];
     const trba_model::ConvTab t = tab[s.aux];
-    const float wmax = __uint_as_float(wmax_bits[blockIdx.y]);
-    const double mx = (double)wmax;
-    const float sc = (float)(mx > 0.0 ? __ddiv_rn(mx, 127.0) : 1.0);
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        *t.wmax = wmax;
-        *t.ws = sc;
+    const bool pc = t.per_channel;
+    const unsigned *wb = wmax_bits + s.chan;
+    if (blockIdx.x == 0) {
+        for (int r = threadIdx.x; r < (pc ? t.cout : 1); r += blockDim.x) {
+            t.wmax[r] = __uint_as_float(wb[r]);
+            t.ws[r] = wscale_of(wb[r]);
+        }
     }
+    const float sc0 = wscale_of(wb[0]);
     const i64 total = (i64)a16(t.cout) * t.kp;
     for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (i64)gridDim.x * blockDim.x) {
         const int r = (int)(e / t.kp), c = (int)(e - (i64)r * t.kp);
-        t.wq[e] = (r < t.cout && c < t.K) ? quant_w(P[s.off + (i64)r * t.K + c], sc) : (int8_t)0;
+        t.wq[e] = (r < t.cout && c < t.K) ? quant_w(P[s.off + (i64)r * t.K + c], pc ? wscale_of(wb[r]) : sc0)
+                                          : (int8_t)0;
     }
     if (t.wimg) {  // tensor-core input gradient: the bf16 weight image
         const dgtc::Plan &tp = *t.tc;
@@ -459,7 +491,8 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
             int gc, n, kl, co;
             dgtc::image_entry(tp, e, gc, n, kl);
             const int src = dgtc::image_source(tp, gc, n, kl, co);
-            const float v = src >= 0 ? (float)quant_w(P[s.off + (i64)co * t.K + src], sc) : 0.0f;
+            const float v =
+                src >= 0 ? (float)quant_w(P[s.off + (i64)co * t.K + src], pc ? wscale_of(wb[co]) : sc0) : 0.0f;
             *reinterpret_cast<__nv_bfloat16 *>(t.wimg + dgtc::image_offset(gc, n, kl, tp.Npad)) =
                 __float2bfloat16_rn(v);
         }
@@ -473,7 +506,13 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
         const int oc = (int)(r % t.cout);
         const i64 r2 = r / t.cout;
         const int tap = (int)(r2 % t.khw), ci = (int)(r2 / t.khw) * 16 + j;
-        t.wT[e] = ci < cin ? (float)quant_w(P[s.off + (i64)oc * t.K + (i64)ci * t.khw + tap], sc) : 0.0f;
+        float v = 0.0f;
+        if (ci < cin) {
+            const float sc = pc ? wscale_of(wb[oc]) : sc0;
+            v = (float)quant_w(P[s.off + (i64)oc * t.K + (i64)ci * t.khw + tap], sc);
+            if (pc) v = fmul(v, sc);
+        }
+        t.wT[e] = v;
     }
 }
 
@@ -637,13 +676,14 @@ void plan(trba_model *m) {
         m->rnn.push_back(r);
     }
     for (auto &e : m->manifest) {
-        Seg s{e.off, (int)e.size(), e.rows, e.cols, 0};
+        Seg s{e.off, (int)e.size(), e.rows, e.cols, 0, 0};
         if (e.kind == K_VEC) m->vec_segs.push_back(s);
         else if (e.kind == K_MAT) m->mat_segs.push_back(s);
     }
     for (size_t i = 0; i < m->convs.size(); ++i) {
         const ConvL &L = m->convs[i];
-        m->conv_segs.push_back(Seg{L.w_off, L.cout * L.K, L.cout, L.K, (int)i});
+        m->conv_segs.push_back(Seg{L.w_off, L.cout * L.K, L.cout, L.K, (int)i, m->n_chan});
+        m->n_chan += L.cout;
     }
 }
 
@@ -671,8 +711,8 @@ void allocate(trba_model *m) {
             L.d_perm = b.p<int32_t>((i64)L.cls_perm.size());
             L.d_cstart = b.p<int32_t>((i64)L.cls_start.size());
         }
-        L.ws = b.p<float>(1);
-        L.wmax = b.p<float>(1);
+        L.ws = b.p<float>(L.cout);  // per-tensor mode uses ws[0]
+        L.wmax = b.p<float>(L.cout);
         L.run_mean = b.p<float>(L.cout);
         L.run_var = b.p<float>(L.cout);
         L.col = b.p<int8_t>(rp * L.kp);
@@ -772,7 +812,7 @@ void allocate(trba_model *m) {
     m->step_tokens = b.p<int32_t>((i64)S * B);
     m->gsq_total = b.z<double>(1);
     m->conv_gsq = b.z<double>((i64)m->convs.size());
-    m->wmax_bits = b.p<unsigned>((i64)m->convs.size());
+    m->wmax_bits = b.p<unsigned>((i64)m->n_chan);
     m->clip_f = b.p<float>(1);
     m->step_state = b.p<double>(4);
     m->mat_step = b.p<float>((i64)m->mat_segs.size());
@@ -854,7 +894,7 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
         ProbeScope ps(c.m, TRBA_PROBE_CONV_GEMM, 2.0 * rows * L.cout * L.K,
                       (double)rows * L.kp + (double)L.cout * L.kp + 4.0 * rows * L.cout, c.st);
         if (!gemm_i8_conv_f32(L.col.get(), L.kp, L.wq.get(), L.kp, (int)rows, L.cout, L.K, L.x.get(), s_in,
-                              L.ws.get(), L.bn_acc.get(), L.Ho * L.Wo, c.st))
+                              L.ws.get(), c.m->cfg.wq_per_channel != 0, L.bn_acc.get(), L.Ho * L.Wo, c.st))
             report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
     }
     if (c.m->cfg.wgrad_mode == 1)
@@ -939,13 +979,17 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
         const double terms = (double)B * L.cin * L.cout * valid_taps(L.H, L.kh, L.sh, L.ph, L.Ho) *
                              valid_taps(L.W, L.kw, L.sw, L.pw, L.Wo);
         ProbeScope ps(c.m, TRBA_PROBE_DGRAD, 2.0 * terms, bytes, c.st);
+        // per-channel scales are folded into the operands (dy per output
+        // channel, or the exact gather's dequantised weights): final scale 1
+        const bool pc = c.m->cfg.wq_per_channel != 0;
         if (L.tc_ok) {
             dgtc::Plan p = L.tc;
             dgtc::set_batch(p, B);
-            dgtc::launch(p, L.wimg.get(), dy, L.ws.get(), 1.0f, mask_q, add, gi, gmax_scale, gmax_out, c.st);
+            dgtc::launch(p, L.wimg.get(), dy, pc ? c.m->ones.get() : L.ws.get(), 1.0f, pc ? L.ws.get() : nullptr,
+                         mask_q, add, gi, gmax_scale, gmax_out, c.st);
             return;
         }
-        qat::dgrad(dy, L.wT.get(), L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
+        qat::dgrad(dy, L.wT.get(), pc ? c.m->ones.get() : L.ws.get(), B, L.cin, L.H, L.W, L.cout, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
                    L.Wo, L.cls_perm.empty() ? nullptr : L.d_perm.get(),
                    L.cls_perm.empty() ? nullptr : L.d_cstart.get(), (int)L.cls_start.size() - 1, mask_q, add, gi,
                    c.st, gmax_scale, gmax_out);
@@ -1233,6 +1277,18 @@ void head_backward(Ctx &c) {
     }
 }
 
+// max |w| per conv, or per output channel, into m->wmax_bits.
+void launch_wmax(trba_model *m, const float *P, cudaStream_t st) {
+    const int ncv = (int)m->conv_segs.size();
+    if (m->cfg.wq_per_channel) {
+        conv_wmax_rows_kernel<<<dim3(4, ncv), 256, 0, st>>>(m->d_conv, P, m->wmax_bits.get());
+    } else {
+        TRBA_CHECK(cudaMemsetAsync(m->wmax_bits.get(), 0, sizeof(unsigned) * m->n_chan, st));
+        conv_wmax_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->wmax_bits.get());
+    }
+    TRBA_LAUNCH_CHECK();
+}
+
 void optimizer(trba_model *m, cudaStream_t st) {
     const auto &cf = m->cfg;
     float *P = m->P.get(), *G = m->G.get();
@@ -1251,16 +1307,14 @@ void optimizer(trba_model *m, cudaStream_t st) {
     conv_gsq_kernel<<<dim3(8, ncv), 256, 0, st>>>(m->d_conv, G, m->conv_gsq.get());
     conv_muon_apply_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, G, m->conv_gsq.get(), m->clip_f.get(), lr, wd,
                                                           (double)cf.muon_cap);
-    TRBA_CHECK(cudaMemsetAsync(m->wmax_bits.get(), 0, sizeof(unsigned) * ncv, st));
-    conv_wmax_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->wmax_bits.get());
+    launch_wmax(m, P, st);
     conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, P, m->d_convtab, m->wmax_bits.get());
     TRBA_LAUNCH_CHECK();
 }
 
 void requantize(trba_model *m, cudaStream_t st) {
     const int ncv = (int)m->conv_segs.size();
-    TRBA_CHECK(cudaMemsetAsync(m->wmax_bits.get(), 0, sizeof(unsigned) * ncv, st));
-    conv_wmax_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->wmax_bits.get());
+    launch_wmax(m, m->P.get(), st);
     conv_quant_kernel<<<dim3(16, ncv), 256, 0, st>>>(m->d_conv, m->P.get(), m->d_convtab, m->wmax_bits.get());
     TRBA_LAUNCH_CHECK();
 }
@@ -1303,13 +1357,15 @@ void trba_model_default_config(trba_model_config *c) {
     c->clip_warmup = 500;
     c->wgrad_mode = 0;
     c->dgrad_mode = 0;
+    c->wq_per_channel = 0;
 }
 
 trba_model *trba_model_create(const trba_model_config *cfg) {
     if (!cfg || cfg->fd < 16 || cfg->fd % 16 || cfg->fd > 512 || cfg->batch <= 0 || cfg->hidden <= 0 ||
         cfg->hidden > 128 || cfg->hidden % 8 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
         (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0 || cfg->wgrad_mode < 0 ||
-        cfg->wgrad_mode > 1 || cfg->dgrad_mode < 0 || cfg->dgrad_mode > 1) {
+        cfg->wgrad_mode > 1 || cfg->dgrad_mode < 0 || cfg->dgrad_mode > 1 ||
+        cfg->wq_per_channel < 0 || cfg->wq_per_channel > 1) {
         report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
         return nullptr;
     }
@@ -1333,7 +1389,7 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
                        L.run_var.get(), L.cout, L.K, L.kp, L.tc_ok ? nullptr : L.wT.get(), L.kh * L.kw,
-                       L.tc_ok ? L.d_tc.get() : nullptr, L.tc_ok ? L.wimg.get() : nullptr});
+                       L.tc_ok ? L.d_tc.get() : nullptr, L.tc_ok ? L.wimg.get() : nullptr, m->cfg.wq_per_channel});
         if (L.tc_ok) TRBA_CHECK(cudaMemcpy(L.d_tc.get(), &L.tc, sizeof(dgtc::Plan), cudaMemcpyHostToDevice));
         if (!L.tc_ok && !L.cls_perm.empty()) {
             TRBA_CHECK(cudaMemcpy(L.d_perm.get(), L.cls_perm.data(), sizeof(int) * L.cls_perm.size(),

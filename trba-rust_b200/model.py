@@ -21,7 +21,8 @@ class _Cfg(C.Structure):
                 ("img_w", C.c_int), ("max_len", C.c_int), ("rnn_layers", C.c_int), ("batch", C.c_int),
                 ("sos", C.c_int), ("eos", C.c_int), ("pad", C.c_int), ("lr", C.c_float),
                 ("weight_decay", C.c_float), ("ctc_weight", C.c_float), ("muon_cap", C.c_float),
-                ("clip_warmup", C.c_int), ("wgrad_mode", C.c_int), ("dgrad_mode", C.c_int)]
+                ("clip_warmup", C.c_int), ("wgrad_mode", C.c_int), ("dgrad_mode", C.c_int),
+                ("wq_per_channel", C.c_int)]
 
 
 @dataclass
@@ -44,6 +45,7 @@ class Config:
     clip_warmup: int = 500
     wgrad_mode: int = 0  # 0: the reference's operand order, 1: dW = dX^T col
     dgrad_mode: int = 0  # conv input gradient: 0 exact f32 order, 1 tensor cores (bf16 x3 split)
+    wq_per_channel: int = 0  # conv weight scales: 0 per tensor (the reference), 1 per output channel
 
     def to_c(self) -> _Cfg:
         return _Cfg(**{f.name: getattr(self, f.name) for f in fields(self)})
