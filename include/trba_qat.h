@@ -47,6 +47,8 @@ typedef struct {
                          1 tensor cores (implicit GEMM, fp32 dy as three bf16 terms) */
     int wq_per_channel; /* conv weight quantisation: 0 per tensor (the reference, src/qnet.rs:316-331),
                            1 per output channel (scale max |w[row]| / 127 for each row) */
+    int inference_only; /* 1: allocate the forward path only (no gradients, optimiser state or
+                           backward traces); training entry points then return -3 */
 } trba_model_config;
 
 /* TRBA-small defaults (fd 128, hidden 64, 130 classes, 32x160, max_len 20). */
@@ -174,6 +176,23 @@ int trba_dp_unique_id(void *id128);
  * the gradient buffer before the optimizer step. */
 int trba_dp_init(trba_model *m, const void *id128, int rank, int world);
 int trba_dp_finalize(trba_model *m);
+/* Failure detection for data-parallel steps (no counterpart in the
+ * reference, which has no multi-GPU path): waits until the work queued on
+ * `stream` (a step and its all-reduce) has finished, polling the stream and
+ * ncclCommGetAsyncError every 100 us.  An asynchronous NCCL error (a peer
+ * that failed) or more than timeout_ms without completion aborts the
+ * communicator (ncclCommAbort, which also ends an all-reduce stuck waiting
+ * for a peer) and leaves the model single-rank.  Returns 0 when the work
+ * finished, 1 after an NCCL error, 2 after a timeout, negative on a CUDA
+ * error of the stream. */
+int trba_dp_wait(trba_model *m, void *stream, double timeout_ms);
+/* The decision loop of trba_dp_wait over caller-supplied probes:
+ * stream_done(ctx) returns 1 when the work finished, 0 while pending,
+ * negative on error (returned as is); async_error(ctx) returns non-zero for
+ * a communicator error; abort_comm(ctx) is called once before returning 1
+ * (error) or 2 (timeout_ms passed); poll_us between polls. */
+int trba_dp_watch(int (*stream_done)(void *), int (*async_error)(void *), void (*abort_comm)(void *), void *ctx,
+                  double timeout_ms, double poll_us);
 
 #ifdef __cplusplus
 }

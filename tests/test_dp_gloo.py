@@ -109,3 +109,49 @@ def test_rank_leaving_between_steps_ends_the_peer_collective_with_an_error():
     assert r0[0] == "error", f"rank 0 expected an error, got {r0}"
     assert r0[2] < 60.0
     assert out[1][0] == "left"
+
+
+# ------------------------------------------------ NCCL failure detection --
+def _watch(lib, done_after=None, error_after=None, timeout_ms=1e9):
+    """Runs trba_dp_watch over fake probes: the 'stream' finishes at poll
+    done_after, the 'communicator' reports an error at poll error_after."""
+    import ctypes as C
+    polls, aborts = [0], [0]
+    probe = C.CFUNCTYPE(C.c_int, C.c_void_p)
+    hook = C.CFUNCTYPE(None, C.c_void_p)
+
+    def done(_):
+        polls[0] += 1
+        return 1 if done_after is not None and polls[0] >= done_after else 0
+
+    def err(_):
+        return 5 if error_after is not None and polls[0] >= error_after else 0
+
+    def abort(_):
+        aborts[0] += 1
+
+    cbs = (probe(done), probe(err), hook(abort))  # kept alive for the call
+    rc = lib.trba_dp_watch(*(C.cast(c, C.c_void_p) for c in cbs), None, float(timeout_ms), 50.0)
+    return rc, polls[0], aborts[0]
+
+
+def test_watchdog_returns_when_the_step_finishes(lib):
+    rc, polls, aborts = _watch(lib, done_after=4)
+    assert (rc, polls, aborts) == (0, 4, 0)
+
+
+def test_watchdog_aborts_on_a_communicator_error(lib):
+    """A peer's failure surfaces as ncclCommGetAsyncError != ncclSuccess: the
+    communicator is aborted once and the wait returns 1."""
+    rc, polls, aborts = _watch(lib, error_after=3)
+    assert (rc, aborts) == (1, 1) and polls == 3
+
+
+def test_watchdog_aborts_a_step_that_never_finishes(lib):
+    """A rank that never joins leaves the all-reduce waiting: after the
+    timeout the communicator is aborted once and the wait returns 2."""
+    import time
+    t0 = time.perf_counter()
+    rc, polls, aborts = _watch(lib, timeout_ms=30.0)
+    assert (rc, aborts) == (2, 1) and polls > 1
+    assert time.perf_counter() - t0 < 5.0

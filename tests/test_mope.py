@@ -71,8 +71,8 @@ def test_expert_serving_equals_model_inference_and_oracle(lib, cuda):
     import torch
     import trba_b200.mope as mp
     e = mp.Expert("bucket_04_04", 4, 4, 64, 4)
-    run = mp.ExpertRunner(e, batch=8, seed=11)
-    ocfg = so.Config(img_w=64, max_len=4)
+    run = mp.ExpertRunner(e, batch=8, seed=11)  # inference-only, per-channel int8 weights
+    ocfg = so.Config(img_w=64, max_len=4, wq_per_channel=True)
     imgs = [so.make_batch(ocfg, 8, seed=70 + i)[0] for i in range(2)]
     dev = torch.from_numpy(np.ascontiguousarray(np.concatenate(imgs))).cuda()
     served = run.decode(dev)
@@ -91,3 +91,30 @@ def test_expert_serving_equals_model_inference_and_oracle(lib, cuda):
     want = orc.infer(imgs[0])[0] + orc.infer(imgs[1])[0]
     assert served == want
     run.close()
+
+
+@pytest.mark.gpu
+def test_inference_only_expert_refuses_training_and_is_smaller(lib, cuda):
+    """An inference-only expert holds the forward path only: no gradients,
+    optimiser state or backward traces, and every training entry point
+    returns -3 instead of touching them."""
+    import trba_b200.model as tm
+    from trba_b200.data import init_params
+    cfg = tm.Config(img_w=256, max_len=40, batch=64, wq_per_channel=1, inference_only=1)
+    inf = tm.QatModel(cfg)
+    tr = tm.QatModel(tm.Config(img_w=256, max_len=40, batch=64, wq_per_channel=1))
+    bi, bt = int(lib.trba_model_device_bytes(inf.h)), int(lib.trba_model_device_bytes(tr.h))
+    assert bi < 0.75 * bt, (bi, bt)
+    inf.set_params(init_params(inf.manifest(), cfg, 3))
+    lib.trba_set_abort_on_error(0)
+    assert lib.trba_model_optimizer_step(inf.h, None) == -3
+    g = np.empty(inf.n_params, np.float32)
+    assert lib.trba_model_get_grads(inf.h, g.ctypes.data, g.size) == -3
+    lib.trba_clear_error()
+    import torch
+    img = torch.zeros((4, 3, 32, 256), dtype=torch.int8, device="cuda")
+    tok = inf.infer(img)
+    assert tok.shape == (41, 4)
+    assert lib.trba_last_error() == 0, lib.trba_last_error_string()
+    inf.close()
+    tr.close()

@@ -10,8 +10,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstring>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -37,6 +39,8 @@ struct Nccl {
                               cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     bool ok = false;
 };
 
@@ -54,7 +58,10 @@ const Nccl &nccl() {
     n.AllReduce = (decltype(n.AllReduce))dlsym(h, "ncclAllReduce");
     n.CommDestroy = (decltype(n.CommDestroy))dlsym(h, "ncclCommDestroy");
     n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
-    n.ok = n.GetUniqueId && n.CommInitRank && n.AllReduce && n.CommDestroy && n.GetErrorString;
+    n.CommGetAsyncError = (decltype(n.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+    n.CommAbort = (decltype(n.CommAbort))dlsym(h, "ncclCommAbort");
+    n.ok = n.GetUniqueId && n.CommInitRank && n.AllReduce && n.CommDestroy && n.GetErrorString &&
+           n.CommGetAsyncError && n.CommAbort;
     return n;
 }
 
@@ -75,10 +82,10 @@ struct Arena {
 };
 
 template <typename T>
-struct Ref {  // arena-relative pointer, resolved after the single cudaMalloc
+struct Ref {  // arena-relative pointer, resolved after the single cudaMalloc (null: never allocated)
     size_t off = 0;
     Arena *a = nullptr;
-    T *get() const { return reinterpret_cast<T *>(a->base + off); }
+    T *get() const { return a ? reinterpret_cast<T *>(a->base + off) : nullptr; }
 };
 
 enum Kind { K_CONV = 0, K_MAT = 1, K_VEC = 2 };
@@ -543,6 +550,12 @@ struct Builder {
     Ref<T> p(i64 n) { return take<T>(A, n); }
     template <typename T>
     Ref<T> z(i64 n) { return take<T>(Z, n); }
+    // training-only buffers (gradients, optimiser state, backward traces):
+    // not allocated for an inference-only model
+    template <typename T>
+    Ref<T> tp(i64 n) { return m->cfg.inference_only ? Ref<T>{} : take<T>(A, n); }
+    template <typename T>
+    Ref<T> tz(i64 n) { return m->cfg.inference_only ? Ref<T>{} : take<T>(Z, n); }
 };
 
 void add_entry(trba_model *m, const std::string &name, int rows, int cols, int kind) {
@@ -692,9 +705,9 @@ void allocate(trba_model *m) {
     const int B = m->B;
     Builder b{m, &m->arena, &m->zarena};
     m->P = b.p<float>(m->n_params);
-    m->G = b.p<float>(m->n_params);
-    m->Mm = b.p<float>(m->n_params);
-    m->Vv = b.p<float>(m->n_params);
+    m->G = b.tp<float>(m->n_params);
+    m->Mm = b.tp<float>(m->n_params);
+    m->Vv = b.tp<float>(m->n_params);
     m->s_img = b.p<float>(1);
     const bool correct = c.wgrad_mode == 1;
     for (size_t i = 0; i < m->convs.size(); ++i) {
@@ -702,31 +715,31 @@ void allocate(trba_model *m) {
         const i64 rows = L.rows(B), rp = a16l(rows), n = (i64)B * L.cout * L.Ho * L.Wo;
         L.wq = b.p<int8_t>((i64)a16(L.cout) * L.kp);
         if (L.tc_ok) {
-            L.wimg = b.p<uint8_t>(dgtc::weight_image_bytes(L.tc));
-            L.d_tc = b.p<dgtc::Plan>(1);
+            L.wimg = b.tp<uint8_t>(dgtc::weight_image_bytes(L.tc));
+            L.d_tc = b.tp<dgtc::Plan>(1);
         } else {
-            L.wT = b.p<float>(qat::dgrad_weights_size(L.cin, L.cout, L.kh * L.kw));
+            L.wT = b.tp<float>(qat::dgrad_weights_size(L.cin, L.cout, L.kh * L.kw));
         }
         if (!L.tc_ok && !L.cls_perm.empty()) {
-            L.d_perm = b.p<int32_t>((i64)L.cls_perm.size());
-            L.d_cstart = b.p<int32_t>((i64)L.cls_start.size());
+            L.d_perm = b.tp<int32_t>((i64)L.cls_perm.size());
+            L.d_cstart = b.tp<int32_t>((i64)L.cls_start.size());
         }
         L.ws = b.p<float>(L.cout);  // per-tensor mode uses ws[0]
         L.wmax = b.p<float>(L.cout);
         L.run_mean = b.p<float>(L.cout);
         L.run_var = b.p<float>(L.cout);
         L.col = b.p<int8_t>(rp * L.kp);
-        if (correct) L.colT = b.p<int8_t>((i64)a16(L.K) * rp);
+        if (correct) L.colT = b.tp<int8_t>((i64)a16(L.K) * rp);
         L.x = b.p<float>(n);
         L.mean = b.p<float>(L.cout);
         L.var = b.p<float>(L.cout);
-        L.A = b.p<int8_t>((i64)a16(L.cout) * rp);
+        L.A = b.tp<int8_t>((i64)a16(L.cout) * rp);
         L.bn_acc = b.z<double>(2 * L.cout);
-        L.bwd_acc = b.z<double>(2 * L.cout);
+        L.bwd_acc = b.tz<double>(2 * L.cout);
         L.ymax = b.z<float>(1);
-        L.dxmax = b.z<float>(1);
-        L.s_dx = b.z<float>(1);
-        L.gw = b.z<int32_t>((i64)L.cout * L.K);
+        L.dxmax = b.tz<float>(1);
+        L.s_dx = b.tz<float>(1);
+        L.gw = b.tz<int32_t>((i64)L.cout * L.K);
     }
     // which convs store y / produce a quantised output
     for (auto &bl : m->blocks) {
@@ -755,36 +768,36 @@ void allocate(trba_model *m) {
         bl.s_dq = b.p<float>(1);
         bl.q_out = b.p<int8_t>(n);
         bl.zmax = b.z<float>(1);
-        bl.gvmax = b.z<float>(1);
-        bl.dz = b.p<float>(n);
-        bl.dy2 = b.p<float>(n);
-        bl.dy1 = b.p<float>(n);
-        bl.gin = b.p<float>(nin);
-        bl.dpre1 = b.p<float>((i64)B * bl.R);
-        bl.dpre2 = b.p<float>((i64)B * bl.C);
-        bl.dpooled = b.p<float>((i64)B * bl.C);
+        bl.gvmax = b.tz<float>(1);
+        bl.dz = b.tp<float>(n);
+        bl.dy2 = b.tp<float>(n);
+        bl.dy1 = b.tp<float>(n);
+        bl.gin = b.tp<float>(nin);
+        bl.dpre1 = b.tp<float>((i64)B * bl.R);
+        bl.dpre2 = b.tp<float>((i64)B * bl.C);
+        bl.dpooled = b.tp<float>((i64)B * bl.C);
     }
     const ConvL &o0 = m->convs[nc - 2], &o1 = m->convs[nc - 1];
-    m->dy_o1 = b.p<float>((i64)B * o1.cout * o1.Ho * o1.Wo);
-    m->dy_o0 = b.p<float>((i64)B * o0.cout * o0.Ho * o0.Wo);
-    m->gv_last = b.p<float>((i64)B * o0.cin * o0.H * o0.W);
-    m->dy_c1 = b.p<float>((i64)B * s1.cout * s1.Ho * s1.Wo);
-    m->dy_c0 = b.p<float>((i64)B * m->convs[0].cout * m->convs[0].Ho * m->convs[0].Wo);
+    m->dy_o1 = b.tp<float>((i64)B * o1.cout * o1.Ho * o1.Wo);
+    m->dy_o0 = b.tp<float>((i64)B * o0.cout * o0.Ho * o0.Wo);
+    m->gv_last = b.tp<float>((i64)B * o0.cin * o0.H * o0.W);
+    m->dy_c1 = b.tp<float>((i64)B * s1.cout * s1.Ho * s1.Wo);
+    m->dy_c0 = b.tp<float>((i64)B * m->convs[0].cout * m->convs[0].Ho * m->convs[0].Wo);
     const int T = m->T, Hh = c.hidden, V = c.classes, S = m->steps, fd = c.fd;
     m->feat = b.p<float>((i64)B * T * fd);
-    m->dfeat = b.p<float>((i64)B * T * fd);
+    m->dfeat = b.tp<float>((i64)B * T * fd);
     for (auto &r : m->rnn) {
         for (int d = 0; d < 2; ++d) {
             r.xg[d] = b.p<float>((i64)B * T * 4 * Hh);
             r.gates[d] = b.p<float>((i64)B * T * 4 * Hh);
             r.c[d] = b.p<float>((i64)B * T * Hh);
             r.hprev[d] = b.p<float>((i64)B * T * Hh);
-            r.dg[d] = b.p<float>((i64)B * T * 4 * Hh);
+            r.dg[d] = b.tp<float>((i64)B * T * 4 * Hh);
         }
         r.cat = b.p<float>((i64)B * T * 2 * Hh);
-        r.dcat = b.p<float>((i64)B * T * 2 * Hh);
+        r.dcat = b.tp<float>((i64)B * T * 2 * Hh);
         r.y = b.p<float>((i64)B * T * Hh);
-        r.dx = b.p<float>((i64)B * T * r.D);
+        r.dx = b.tp<float>((i64)B * T * r.D);
     }
     m->proj_h = b.p<float>((i64)B * T * Hh);
     m->tanh_tr = b.p<float>((i64)S * B * T * Hh);
@@ -794,16 +807,16 @@ void allocate(trba_model *m) {
     m->hs = b.p<float>((i64)S * B * Hh);
     m->cs = b.p<float>((i64)S * B * Hh);
     m->logits = b.p<float>((i64)S * B * V);
-    m->dlogits = b.p<float>((i64)S * B * V);
+    m->dlogits = b.tp<float>((i64)S * B * V);
     m->row_loss = b.p<float>((i64)S * B);
     m->ctc_logits = b.p<float>((i64)B * T * V);
-    m->dctc = b.p<float>((i64)B * T * V);
-    m->d_out_hid = b.p<float>((i64)S * B * Hh);
-    m->adg = b.p<float>((i64)S * B * 4 * Hh);
-    m->ade = b.p<float>((i64)S * B * T);
-    m->adprojhh = b.p<float>((i64)S * B * Hh);
-    m->d_proj_h = b.p<float>((i64)B * T * Hh);
-    m->d_bh = b.p<float>((i64)B * T * Hh);
+    m->dctc = b.tp<float>((i64)B * T * V);
+    m->d_out_hid = b.tp<float>((i64)S * B * Hh);
+    m->adg = b.tp<float>((i64)S * B * 4 * Hh);
+    m->ade = b.tp<float>((i64)S * B * T);
+    m->adprojhh = b.tp<float>((i64)S * B * Hh);
+    m->d_proj_h = b.tp<float>((i64)B * T * Hh);
+    m->d_bh = b.tp<float>((i64)B * T * Hh);
     m->ctc_sample_loss = b.p<double>(B);
     m->gemm_ws_elems = (i64)8 << 20;
     m->gemm_ws = b.p<double>(m->gemm_ws_elems);
@@ -897,7 +910,7 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
                               L.ws.get(), c.m->cfg.wq_per_channel != 0, L.bn_acc.get(), L.Ho * L.Wo, c.st))
             report_error(__FILE__, __LINE__, "conv forward GEMM: operands not TMA-describable", -1);
     }
-    if (c.m->cfg.wgrad_mode == 1)
+    if (c.m->cfg.wgrad_mode == 1 && !c.eval)  // the weight gradient's operand: training only
         qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
                       (int)a16l(rows), c.st);
 }
@@ -1328,6 +1341,11 @@ T *upload_table(const std::vector<T> &v) {
     return d;
 }
 
+int training_refused(trba_model *) {
+    report_error(__FILE__, __LINE__, "inference-only model: training entry points are not available", -1);
+    return -3;
+}
+
 int cuda_status() {
     const int e = trba_last_error();
     return e > 0 ? e : (e < 0 ? -e : 0);
@@ -1358,6 +1376,7 @@ void trba_model_default_config(trba_model_config *c) {
     c->wgrad_mode = 0;
     c->dgrad_mode = 0;
     c->wq_per_channel = 0;
+    c->inference_only = 0;
 }
 
 trba_model *trba_model_create(const trba_model_config *cfg) {
@@ -1365,7 +1384,7 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
         cfg->hidden > 128 || cfg->hidden % 8 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
         (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0 || cfg->wgrad_mode < 0 ||
         cfg->wgrad_mode > 1 || cfg->dgrad_mode < 0 || cfg->dgrad_mode > 1 ||
-        cfg->wq_per_channel < 0 || cfg->wq_per_channel > 1) {
+        cfg->wq_per_channel < 0 || cfg->wq_per_channel > 1 || cfg->inference_only < 0 || cfg->inference_only > 1) {
         report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
         return nullptr;
     }
@@ -1462,8 +1481,10 @@ int trba_model_param_entry(const trba_model *m, int i, char *name, int name_cap,
 int trba_model_set_params(trba_model *m, const float *host, long long n) {
     if (!m || !host || n != m->n_params) return -1;
     TRBA_CHECK(cudaMemcpy(m->P.get(), host, n * 4, cudaMemcpyHostToDevice));
-    TRBA_CHECK(cudaMemset(m->Mm.get(), 0, n * 4));
-    TRBA_CHECK(cudaMemset(m->Vv.get(), 0, n * 4));
+    if (!m->cfg.inference_only) {
+        TRBA_CHECK(cudaMemset(m->Mm.get(), 0, n * 4));
+        TRBA_CHECK(cudaMemset(m->Vv.get(), 0, n * 4));
+    }
     m->t = 0;
     TRBA_CHECK(cudaMemset(m->step_state.get(), 0, 4 * sizeof(double)));
     requantize(m, 0);
@@ -1479,6 +1500,7 @@ int trba_model_get_params(trba_model *m, float *host, long long n) {
 }
 
 int trba_model_get_grads(trba_model *m, float *host, long long n) {
+    if (m && m->cfg.inference_only) return training_refused(m);
     if (!m || !host || n != m->n_params) return -1;
     TRBA_CHECK(cudaDeviceSynchronize());
     TRBA_CHECK(cudaMemcpy(host, m->G.get(), n * 4, cudaMemcpyDeviceToHost));
@@ -1515,6 +1537,7 @@ int trba_model_get_running_stats(trba_model *m, float *host, long long n) {
 int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
                                 const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
     if (!m || !img || !text_in || !target || !ctc_tgt || !ctc_len || batch <= 0 || batch > m->B) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     cudaStream_t st = as_stream(stream);
     Ctx c{m, st, batch, m->P.get(), m->G.get()};
     m->last_B = batch;
@@ -1592,6 +1615,7 @@ int trba_model_infer_host(trba_model *m, const int8_t *img, int batch, int32_t *
 
 int trba_model_optimizer_step(trba_model *m, void *stream) {
     if (!m) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     optimizer(m, as_stream(stream));
     return cuda_status();
 }
@@ -1673,6 +1697,7 @@ extern "C" {
 int trba_model_train_step(trba_model *m, const int8_t *img, const int32_t *text_in, const int32_t *target,
                           const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, void *stream) {
     if (!m || !img || !text_in || !target || !ctc_tgt || !ctc_len || batch <= 0 || batch > m->B) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     if (m->use_graphs)
         return graph_step(m, img, text_in, target, ctc_tgt, ctc_len, batch, as_stream(stream));
     return step_body(m, img, text_in, target, ctc_tgt, ctc_len, batch, as_stream(stream));
@@ -1692,6 +1717,7 @@ int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *
                                const int32_t *ctc_tgt, const int32_t *ctc_len, int batch, float *loss_host,
                                void *stream) {
     if (!m || batch <= 0 || batch > m->B || !loss_host) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     cudaStream_t st = as_stream(stream);
     const auto &cf = m->cfg;
     const size_t S = (size_t)m->steps;
@@ -1714,6 +1740,7 @@ int trba_model_train_step_host(trba_model *m, const int8_t *img, const int32_t *
 // Optimiser state and running statistics in and out (checkpoints).
 int trba_model_get_moments(trba_model *m, float *m_host, float *v_host, long long n) {
     if (!m || n != m->n_params) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     TRBA_CHECK(cudaDeviceSynchronize());
     if (m_host) TRBA_CHECK(cudaMemcpy(m_host, m->Mm.get(), n * 4, cudaMemcpyDeviceToHost));
     if (v_host) TRBA_CHECK(cudaMemcpy(v_host, m->Vv.get(), n * 4, cudaMemcpyDeviceToHost));
@@ -1721,6 +1748,7 @@ int trba_model_get_moments(trba_model *m, float *m_host, float *v_host, long lon
 }
 
 int trba_model_set_moments(trba_model *m, const float *m_host, const float *v_host, long long n) {
+    if (m && m->cfg.inference_only) return training_refused(m);
     if (!m || n != m->n_params) return -1;
     TRBA_CHECK(cudaDeviceSynchronize());
     if (m_host) TRBA_CHECK(cudaMemcpy(m->Mm.get(), m_host, n * 4, cudaMemcpyHostToDevice));
@@ -1772,7 +1800,7 @@ int trba_model_debug_tensor(trba_model *m, const char *name, float *host, long l
             else if (nm == L.name + ".var") src = L.var.get(), cnt = L.cout;
         }
     }
-    if (!src || cnt != n) return -2;
+    if (!src || cnt != n) return -2;  // also: a training buffer of an inference-only model
     TRBA_CHECK(cudaDeviceSynchronize());
     TRBA_CHECK(cudaMemcpy(host, src, n * 4, cudaMemcpyDeviceToHost));
     return cuda_status();
@@ -1837,6 +1865,7 @@ int trba_dp_unique_id(void *id128) {
 
 int trba_dp_init(trba_model *m, const void *id128, int rank, int world) {
     if (!m || !id128 || world < 1 || rank < 0 || rank >= world) return -1;
+    if (m->cfg.inference_only) return training_refused(m);
     if (world == 1) return 0;
     if (!nccl().ok) {
         report_error(__FILE__, __LINE__, "libnccl.so.2 not found", -1);
@@ -1852,6 +1881,61 @@ int trba_dp_init(trba_model *m, const void *id128, int rank, int world) {
     }
     m->world = world;
     return 0;
+}
+
+// Watchdog over one step's completion (see include/trba_qat.h).
+int trba_dp_watch(int (*stream_done)(void *), int (*async_error)(void *), void (*abort_comm)(void *), void *ctx,
+                  double timeout_ms, double poll_us) {
+    if (!stream_done || !async_error || !abort_comm) return -1;
+    const auto t0 = std::chrono::steady_clock::now();
+    const auto nap = std::chrono::microseconds((long long)(poll_us > 0 ? poll_us : 100.0));
+    while (true) {
+        const int d = stream_done(ctx);
+        if (d < 0) return d;  // the stream reported an error of its own
+        if (d > 0) return 0;
+        const int e = async_error(ctx);
+        if (e != 0) {
+            abort_comm(ctx);
+            return 1;
+        }
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (ms > timeout_ms) {
+            abort_comm(ctx);
+            return 2;
+        }
+        std::this_thread::sleep_for(nap);
+    }
+}
+
+int trba_dp_wait(trba_model *m, void *stream, double timeout_ms) {
+    if (!m) return -1;
+    struct Ctx {
+        trba_model *m;
+        cudaStream_t st;
+    } c{m, as_stream(stream)};
+    auto done = [](void *p) -> int {
+        const cudaError_t e = cudaStreamQuery(static_cast<Ctx *>(p)->st);
+        if (e == cudaSuccess) return 1;
+        if (e == cudaErrorNotReady) return 0;
+        return -(int)e;
+    };
+    auto async_err = [](void *p) -> int {
+        trba_model *mm = static_cast<Ctx *>(p)->m;
+        if (!mm->comm) return 0;
+        ncclResult_t r = ncclSuccess;
+        if (nccl().CommGetAsyncError(mm->comm, &r) != ncclSuccess) return -1;
+        return r == ncclSuccess || r == ncclInProgress ? 0 : (int)r;
+    };
+    auto abort_comm = [](void *p) {
+        trba_model *mm = static_cast<Ctx *>(p)->m;
+        if (mm->comm) nccl().CommAbort(mm->comm);
+        mm->comm = nullptr;
+        mm->world = 1;
+    };
+    const int r = trba_dp_watch(done, async_err, abort_comm, &c, timeout_ms, 100.0);
+    if (r == 1) report_error(__FILE__, __LINE__, "trba_dp_wait: NCCL reported an asynchronous error; aborted", -1);
+    if (r == 2) report_error(__FILE__, __LINE__, "trba_dp_wait: step did not finish in time; NCCL aborted", -1);
+    return r;
 }
 
 int trba_dp_finalize(trba_model *m) {

@@ -60,6 +60,9 @@ def parse_header(text: str) -> dict[str, tuple]:
         if args and args != "void":
             for a in args.split(","):
                 a = a.strip()
+                if "(*" in a:  # function pointer (one parameter each in these headers): passed as an address
+                    argtypes.append(C.c_void_p)
+                    continue
                 am = re.match(r"^(.*?[\s\*])([A-Za-z_]\w*)$", a)
                 argtypes.append(_ctype(am.group(1) if am else a))
         out[name] = (_ctype(ret.strip()), argtypes)

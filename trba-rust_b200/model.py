@@ -22,7 +22,7 @@ class _Cfg(C.Structure):
                 ("sos", C.c_int), ("eos", C.c_int), ("pad", C.c_int), ("lr", C.c_float),
                 ("weight_decay", C.c_float), ("ctc_weight", C.c_float), ("muon_cap", C.c_float),
                 ("clip_warmup", C.c_int), ("wgrad_mode", C.c_int), ("dgrad_mode", C.c_int),
-                ("wq_per_channel", C.c_int)]
+                ("wq_per_channel", C.c_int), ("inference_only", C.c_int)]
 
 
 @dataclass
@@ -46,6 +46,7 @@ class Config:
     wgrad_mode: int = 0  # 0: the reference's operand order, 1: dW = dX^T col
     dgrad_mode: int = 0  # conv input gradient: 0 exact f32 order, 1 tensor cores (bf16 x3 split)
     wq_per_channel: int = 0  # conv weight scales: 0 per tensor (the reference), 1 per output channel
+    inference_only: int = 0  # 1: forward buffers only (serving); training calls are refused
 
     def to_c(self) -> _Cfg:
         return _Cfg(**{f.name: getattr(self, f.name) for f in fields(self)})
@@ -228,6 +229,15 @@ class QatModel:
 
     def dp_finalize(self):
         self.L.trba_dp_finalize(self.h)
+
+    def dp_wait(self, stream=None, timeout_s: float = 60.0) -> int:
+        """Wait for the queued step(s) on `stream`; a peer's NCCL failure or
+        a step that does not finish within timeout_s aborts the communicator
+        (trba_dp_wait).  Returns 0 (finished), 1 (NCCL error) or 2 (timeout)."""
+        rc = self.L.trba_dp_wait(self.h, stream, float(timeout_s) * 1000.0)
+        if rc < 0:
+            raise RuntimeError("trba_dp_wait: " + self.L.trba_last_error_string().decode())
+        return rc
 
     @staticmethod
     def dp_unique_id() -> bytes:

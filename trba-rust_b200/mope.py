@@ -90,14 +90,17 @@ def synthetic_lengths(n: int, seed: int, max_len: int = 32) -> list[int]:
 
 
 class ExpertRunner:
-    """One expert on the current GPU: a QatModel sized for `batch` lines per
-    decoding call; greedy decoding of device image batches."""
+    """One expert on the current GPU: an inference-only int8 model (weights
+    quantised per output channel, no gradient or optimiser buffers) sized
+    for `batch` lines per decoding call; greedy decoding of device image
+    batches.  per_channel=False gives the reference's per-tensor scales."""
 
-    def __init__(self, expert: Expert, batch: int, seed: int):
+    def __init__(self, expert: Expert, batch: int, seed: int, per_channel: bool = True):
         from .data import init_params
         from .model import Config, QatModel
         self.expert, self.batch = expert, batch
-        self.cfg = Config(img_w=expert.img_w, max_len=expert.max_len, batch=batch)
+        self.cfg = Config(img_w=expert.img_w, max_len=expert.max_len, batch=batch,
+                          wq_per_channel=int(per_channel), inference_only=1)
         self.model = QatModel(self.cfg)
         self.model.set_params(init_params(self.model.manifest(), self.cfg, seed))
 
