@@ -2,28 +2,36 @@
 // class, tcgen05.mma kind::f16 with bf16 operands and an fp32 TMEM
 // accumulator (the plan and the operand contract are in dgrad_tc.cuh).
 //
-// CTA (one per SM, persistent over 128-pixel tiles), 9 warps:
-//   warps 0..3  producers.  Thread r owns row r of the tile (one input
-//               pixel): for each 64-wide K chunk (tap-major, output channel
-//               minor) it gathers the 64 dy values its pixel needs straight
-//               from the NCHW gradient (coalesced across the warp: adjacent
-//               pixels read adjacent dy), writes them as three bf16 terms
-//               into the hi / mid / lo A operands of a shared-memory stage
-//               (128-byte rows, 16-byte chunks XOR-swizzled by row, the
-//               layout TMA's SWIZZLE_128B produces), and thread 0 bulk-copies
-//               the stage's weight chunk, pre-swizzled in global memory.
-//   warp 4      MMA issuer (lane 0): per stage, 3 terms x 4 MMAs of
-//               M = 128, N = BN, K = 16 into one of two TMEM accumulators,
-//               so the epilogue of a tile overlaps the MMAs of the next.
-//   warps 5..8  epilogue: tcgen05.ld of the accumulator (one pixel row per
-//               thread), times w_s, STE mask, residual add, NCHW store and
-//               the max |gi * scale| of the next re-quantisation.
-//
-// The split is exact: hi = v with the low 16 significand bits cleared,
-// mid = (v - hi) likewise, lo = v - hi - mid; each subtraction is exact and
-// lo has at most 8 significant bits, so hi + mid + lo == v and every
-// product with an int8 weight is exact in fp32.  The only rounding is the
-// tensor core's fp32 accumulation.
+// Two launches per input gradient:
+//   split_nhwc_kernel   dy (NCHW f32, optionally times a per-output-channel
+//                       weight scale) -> three bf16 planes hi / mid / lo in
+//                       NHWC order, so that the 64 values of one K chunk of
+//                       one pixel (one tap, 64 output channels) are 128
+//                       contiguous bytes of each plane.  The split is exact:
+//                       hi = v with the low 16 significand bits cleared,
+//                       mid = (v - hi) likewise, lo = v - hi - mid; each
+//                       subtraction is exact and lo has at most 8 significant
+//                       bits, so hi + mid + lo == v and every product with an
+//                       int8 weight is exact in fp32.  The only rounding is
+//                       the tensor core's fp32 accumulation.
+//   dgrad_tc_kernel     one CTA per SM, persistent over 128-pixel tiles,
+//                       9 warps:
+//     warps 0..3  producers: 16-byte cp.async copies of the three planes'
+//                 rows of the tile's pixels at the chunk's tap into the
+//                 A operands of a shared-memory stage (128-byte rows,
+//                 16-byte pieces XOR-swizzled by row, the layout TMA's
+//                 SWIZZLE_128B produces; zero-filled where the tap leaves
+//                 the output grid), one copy group in flight per thread
+//                 while the next is issued; thread 0 bulk-copies the
+//                 stage's weight chunk, pre-swizzled in global memory.
+//     warp 4      MMA issuer (lane 0): per stage, 3 terms x 4 MMAs of
+//                 M = 128, N = BN, K = 16 into one of two TMEM
+//                 accumulators, so the epilogue of a tile overlaps the MMAs
+//                 of the next.
+//     warps 5..8  epilogue: tcgen05.ld of the accumulator (one pixel row
+//                 per thread), times w_s, STE mask, residual add, NCHW
+//                 store and the max |gi * scale| of the next
+//                 re-quantisation.
 //
 // Every mbarrier wait is bounded (2 s): on a timeout the CTA raises an
 // abort flag, every role leaves its loop, issued weight copies are drained,
@@ -37,6 +45,7 @@
 #include "dgrad_tc.cuh"
 #include "tc_primitives.cuh"
 #include "trba_b200.h"
+#include "trba_backend.h"
 
 using namespace trba;
 using namespace trba::tc;
@@ -56,7 +65,7 @@ constexpr int kMmaWarp = kProdWarps;
 constexpr int kEpiWarps = 4;                    // one per TMEM lane quarter
 constexpr int kThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kMaxStages = 4;
-constexpr size_t kSmemBudget = 200 * 1024;
+constexpr size_t kSmemBudget = 224 * 1024;
 
 struct Ctl {
     uint64_t afull[kMaxStages];  // producer arrivals (128)
@@ -71,11 +80,11 @@ struct Ctl {
 };
 
 struct Args {
-    const float *dy;
+    const uint16_t *planes;  // hi, mid, lo bf16 planes of dy, NHWC, plane_elems apart
+    long long plane_elems;
     const uint8_t *wimg;
     const float *w_s;  // device scalar, or null: w_s_val
     float w_s_val;
-    const float *ws_co;  // per-output-channel scales applied to dy, or null
     const int8_t *mask_q;
     const float *add;
     float *gi;
@@ -168,67 +177,66 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
 
     if (warp < kProdWarps) {
         // ------------------------------------------------ producers
-        const int r = threadIdx.x;
-        const int sw = r & 7;
+        // Thread (rs, l8): 16-byte piece l8 of the 128-byte rows rs + 16 i
+        // (i < 8) of every A operand; the piece's 8 K values belong to one
+        // tap (Cout is a power of two >= 8).
+        const int l8 = threadIdx.x & 7, rs = threadIdx.x >> 3;
+        const int lgC = P.lgCout;
         uint32_t it = 0;
+        int pend = -1;  // stage of the copy group issued but not yet handed to the MMA warp
         for (int t = blockIdx.x; t < P.tiles && !*abort; t += gridDim.x) {
             const Class &C = P.cls[tile_class(P, t)];
+            if (C.kchunks == 0) continue;  // a phase without taps: the epilogue alone writes it
             const int local = t - C.tile0, mt = local / P.ntn, n0 = (local - mt * P.ntn) * BN;
-            const int m = mt * kRows + r;
-            const bool rv = m < a.B * C.Hc * C.Wc;
-            int b = 0, y = 0, x = 0;
-            if (rv) class_pixel(P, C, m, b, y, x);
-            const float *dyb = a.dy + (i64)b * P.Cout * HoWo;
+            int py[8], px[8], pb[8];  // rows' pixels: input row, column, b * Ho * Wo (-1: past the end)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int m = mt * kRows + rs + 16 * i;
+                int b = 0, y = 0, x = 0;
+                const bool rv = m < a.B * C.Hc * C.Wc;
+                if (rv) class_pixel(P, C, m, b, y, x);
+                py[i] = y, px[i] = x, pb[i] = rv ? b * HoWo : -1;
+            }
             for (int kc = 0; kc < C.kchunks; ++kc, ++it) {
                 const int s = it % stages;
                 const uint32_t ph = (it / stages) & 1u;
                 if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort, a.wait_ns)) break;
                 uint8_t *stage = smem + (size_t)s * G::STAGE;
-                if (r == 0 && !a.skip_weights) {
+                if (threadIdx.x == 0 && !a.skip_weights) {
                     mbar_expect_tx(&ctl->bfull[s], G::B_BYTES);
                     bulk_load(stage + 3 * kPartBytes, a.wimg + ((i64)(C.b_off + kc) * P.Npad + n0) * kRowBytes,
                               G::B_BYTES, &ctl->bfull[s]);
                     ctl->b_issued = it + 1;
                 }
-                // gather the 64 values of this pixel's K chunk (8 groups of 8
-                // output channels of one tap), all loads in flight at once
-                float v[8][8];
+                const int k0 = kc * kChunk + l8 * 8;
+                const int tap = k0 >> lgC, co = k0 & (P.Cout - 1);
+                const bool tok = tap < C.ntaps;
+                const int dh = tok ? P.pH - C.kh[tap] : 0, dw = tok ? P.pW - C.kw[tap] : 0;
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    const int k0 = kc * kChunk + g * 8;
-                    const int tap = k0 / P.Cout, co0 = k0 - tap * P.Cout;
-                    bool ok = rv && tap < C.ntaps;
-                    int oy = 0, ox = 0;
-                    if (ok) {
-                        const int ny = y + P.pH - C.kh[tap], nx = x + P.pW - C.kw[tap];
-                        oy = ny / P.sH;
-                        ox = nx / P.sW;
-                        ok = ny >= 0 && nx >= 0 && oy < P.Ho && ox < P.Wo;
-                    }
-                    const float *src = dyb + (i64)co0 * HoWo + oy * P.Wo + ox;
+                for (int i = 0; i < 8; ++i) {
+                    const int r = rs + 16 * i;
+                    const int ny = py[i] + dh, nx = px[i] + dw;
+                    const int oy = ny >> P.lgSH, ox = nx >> P.lgSW;  // exact: the class fixes the phase
+                    const bool ok = tok && pb[i] >= 0 && ny >= 0 && nx >= 0 && oy < P.Ho && ox < P.Wo;
+                    const i64 e = ok ? ((i64)(pb[i] + oy * P.Wo + ox) << lgC) + co : 0;
+                    uint8_t *dst = stage + r * kRowBytes + ((l8 ^ (r & 7)) << 4);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[g][j] = ok ? __ldg(src + (i64)j * HoWo) : 0.0f;
-                    if (a.ws_co) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) v[g][j] = __fmul_rn(v[g][j], __ldg(a.ws_co + co0 + j));
-                    }
+                    for (int p = 0; p < 3; ++p)
+                        cp_async16(dst + p * kPartBytes, a.planes + p * a.plane_elems + e, ok ? 16u : 0u);
                 }
-                uint8_t *rowp = stage + r * kRowBytes;
-#pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    uint4 h, mm, l;
-                    split_pair(v[g][0], v[g][1], h.x, mm.x, l.x);
-                    split_pair(v[g][2], v[g][3], h.y, mm.y, l.y);
-                    split_pair(v[g][4], v[g][5], h.z, mm.z, l.z);
-                    split_pair(v[g][6], v[g][7], h.w, mm.w, l.w);
-                    const int off = (g ^ sw) << 4;
-                    *reinterpret_cast<uint4 *>(rowp + off) = h;
-                    *reinterpret_cast<uint4 *>(rowp + kPartBytes + off) = mm;
-                    *reinterpret_cast<uint4 *>(rowp + 2 * kPartBytes + off) = l;
+                cp_async_commit();
+                if (pend >= 0) {  // the previous chunk's copies have landed: hand its stage over
+                    cp_async_wait<1>();
+                    fence_proxy_async_smem();
+                    mbar_arrive(&ctl->afull[pend]);
                 }
-                fence_proxy_async_smem();
-                mbar_arrive(&ctl->afull[s]);
+                pend = s;
             }
+        }
+        cp_async_wait<0>();
+        if (pend >= 0) {
+            fence_proxy_async_smem();
+            mbar_arrive(&ctl->afull[pend]);
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
@@ -279,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
         for (int t = blockIdx.x; t < P.tiles; t += gridDim.x) {
             const Class &C = P.cls[tile_class(P, t)];
             const int local = t - C.tile0, mt = local / P.ntn, n0 = (local - mt * P.ntn) * BN;
-            const bool ok = mbar_wait(&ctl->tfull[acc], acc_ph, abort, a.wait_ns);
+            const bool ok = mbar_wait_sleep(&ctl->tfull[acc], acc_ph, abort, a.wait_ns, 256);
             __syncwarp();  // reconverge before the warp-collective tcgen05.ld
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
@@ -340,6 +348,41 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
 
 }  // namespace
 
+// dy (NCHW f32) -> hi / mid / lo bf16 planes (NHWC), optionally scaled per
+// output channel first.  Block: 32 pixels of one image; 32 channels at a time
+// pass through a shared-memory transpose (reads coalesced along pixels,
+// writes along channels).  C is a power of two >= 8.
+__global__ void __launch_bounds__(256) split_nhwc_kernel(const float *__restrict__ dy,
+                                                         const float *__restrict__ ws_co, int C, int HW,
+                                                         uint16_t *__restrict__ planes, long long plane_elems) {
+    __shared__ float tile[32][33];
+    const int b = blockIdx.y, p0 = blockIdx.x * 32;
+    const float *src = dy + (i64)b * C * HW;
+    uint16_t *hi = planes + (i64)b * HW * C, *mid = hi + plane_elems, *lo = mid + plane_elems;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pl = threadIdx.x >> 3, cq = (threadIdx.x & 7) * 4;
+    for (int c0 = 0; c0 < C; c0 += 32) {
+        for (int cc = w; cc < 32; cc += 8) {
+            const int c = c0 + cc, p = p0 + lane;
+            float v = (c < C && p < HW) ? __ldg(src + (i64)c * HW + p) : 0.0f;
+            if (ws_co && c < C) v = __fmul_rn(v, __ldg(ws_co + c));
+            tile[cc][lane] = v;
+        }
+        __syncthreads();
+        const int p = p0 + pl;
+        if (p < HW && c0 + cq < C) {
+            uint32_t h0, m0, l0, h1, m1, l1;
+            split_pair(tile[cq][pl], tile[cq + 1][pl], h0, m0, l0);
+            split_pair(tile[cq + 2][pl], tile[cq + 3][pl], h1, m1, l1);
+            const i64 o = (i64)p * C + c0 + cq;
+            *reinterpret_cast<uint2 *>(hi + o) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2 *>(mid + o) = make_uint2(m0, m1);
+            *reinterpret_cast<uint2 *>(lo + o) = make_uint2(l0, l1);
+        }
+        __syncthreads();
+    }
+}
+
 // Weight image from an int8 weight matrix [cout rows, w_ld] with K order
 // (ci, kh, kw) (the ABI entry point's operand).
 __global__ void image_from_wq_kernel(const __grid_constant__ Plan P, const int8_t *__restrict__ wq, int w_ld,
@@ -380,10 +423,16 @@ int stages_for(int BN) {
 
 bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
                Plan &p) {
-    if (Cin <= 0 || Cout <= 0 || Cout % 8 || sH <= 0 || sW <= 0 || sH * sW > kMaxClasses || H <= 0 || W <= 0 ||
-        Ho <= 0 || Wo <= 0)
+    auto lg2 = [](int v) {
+        int l = 0;
+        while ((1 << l) < v) ++l;
+        return (1 << l) == v ? l : -1;
+    };
+    if (Cin <= 0 || Cout < 8 || lg2(Cout) < 0 || sH <= 0 || sW <= 0 || lg2(sH) < 0 || lg2(sW) < 0 ||
+        sH * sW > kMaxClasses || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0)
         return false;
     p = Plan{};
+    p.lgCout = lg2(Cout), p.lgSH = lg2(sH), p.lgSW = lg2(sW);
     p.Cin = Cin, p.Cout = Cout, p.H = H, p.W = W, p.Ho = Ho, p.Wo = Wo, p.kH = kH, p.kW = kW;
     p.sH = sH, p.sW = sW, p.pH = pH, p.pW = pW;
     if (Cin <= 16) p.BN = 16;
@@ -440,13 +489,18 @@ void launch_args(const Plan &p, const Args &a, cudaStream_t st) {
 }
 }  // namespace
 
-void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
+void launch(const Plan &p, const uint8_t *wimg, uint16_t *planes, const float *dy, const float *w_s, float w_s_val,
             const float *ws_co, const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale,
             float *gmax_out, cudaStream_t st) {
     if (p.tiles <= 0) return;
+    const int HoWo = p.Ho * p.Wo;
+    const long long plane_elems = plane_elements(p);
+    split_nhwc_kernel<<<dim3((unsigned)((HoWo + 31) / 32), (unsigned)p.B), 256, 0, st>>>(dy, ws_co, p.Cout, HoWo,
+                                                                                      planes, plane_elems);
+    TRBA_LAUNCH_CHECK();
     Args a{};
-    a.dy = dy, a.wimg = wimg, a.w_s = w_s, a.w_s_val = w_s_val, a.ws_co = ws_co, a.mask_q = mask_q, a.add = add;
-    a.gi = gi;
+    a.planes = planes, a.plane_elems = plane_elems, a.wimg = wimg, a.w_s = w_s, a.w_s_val = w_s_val;
+    a.mask_q = mask_q, a.add = add, a.gi = gi;
     a.gmax_scale = gmax_out ? gmax_scale : nullptr;
     a.gmax_out = gmax_scale ? gmax_out : nullptr;
     a.B = p.B;
@@ -472,8 +526,8 @@ int error_poll(bool clear) {
 
 // -------------------------------------------------------------- C ABI --
 namespace {
-// Grow-only per-device buffer for the weight image of the ABI entry point
-// (the fused training step keeps its images in the model's arena).
+// Grow-only per-device buffer for the weight image and the dy planes of the
+// ABI entry point (the fused training step keeps both in the model's arena).
 std::mutex g_img_mu;
 uint8_t *g_img[64] = {};
 size_t g_img_bytes[64] = {};
@@ -487,16 +541,17 @@ extern "C" int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *w
     dgtc::Plan p;
     if (!dgtc::make_plan(cin, cout, h, w, kh, kw, sh, sw, ph, pw, ho, wo, p)) {
         report_error(__FILE__, __LINE__,
-                     "trba_conv_grad_input_i8_tc: unsupported conv (Cout % 8, at most 4 stride phases and 16 taps "
-                     "per phase)", -1);
+                     "trba_conv_grad_input_i8_tc: unsupported conv (Cout and strides powers of two, Cout >= 8, at "
+                     "most 4 stride phases and 16 taps per phase)", -1);
         return -1;
     }
     dgtc::set_batch(p, b);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= 64) return e != cudaSuccess ? (int)e : -1;
-    const size_t need = (size_t)dgtc::weight_image_bytes(p);
-    uint8_t *img = nullptr;
+    const size_t img_bytes = ((size_t)dgtc::weight_image_bytes(p) + 255) & ~size_t(255);
+    const size_t need = img_bytes + 3 * sizeof(uint16_t) * (size_t)dgtc::plane_elements(p);
+    uint8_t *buf = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_img_mu);
         if (g_img_bytes[dev] < need) {
@@ -505,20 +560,24 @@ extern "C" int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *w
             g_img_bytes[dev] = 0;
             e = cudaMalloc(&g_img[dev], need);
             if (e != cudaSuccess) {
-                report_error(__FILE__, __LINE__, "trba_conv_grad_input_i8_tc: weight image allocation", (int)e);
+                report_error(__FILE__, __LINE__, "trba_conv_grad_input_i8_tc: scratch allocation", (int)e);
                 return (int)e;
             }
             g_img_bytes[dev] = need;
         }
-        img = g_img[dev];
+        buf = g_img[dev];
     }
     cudaStream_t st = as_stream(stream);
     const long long n = (long long)p.total_chunks * p.Npad * dgtc::kChunk;
-    dgtc::image_from_wq_kernel<<<grid_for(n), 256, 0, st>>>(p, weight_q, w_ld, img);
+    dgtc::image_from_wq_kernel<<<grid_for(n), 256, 0, st>>>(p, weight_q, w_ld, buf);
     TRBA_LAUNCH_CHECK();
-    dgtc::launch(p, img, grad_out, nullptr, w_scale, nullptr, nullptr, nullptr, grad_input, nullptr, nullptr, st);
+    const int before = trba_last_error();
+    dgtc::launch(p, buf, reinterpret_cast<uint16_t *>(buf + img_bytes), grad_out, nullptr, w_scale, nullptr, nullptr,
+                 nullptr, grad_input, nullptr, nullptr, st);
     e = cudaGetLastError();
-    return e == cudaSuccess ? 0 : (int)e;
+    if (e != cudaSuccess) return (int)e;
+    const int after = trba_last_error();  // a launch error already reported in the sticky error mode
+    return after != before ? (after ? after : -1) : 0;
 }
 
 // Bounded-wait self-test: one small input-gradient launch whose weight copies
@@ -531,17 +590,20 @@ extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) 
     dgtc::Plan p;
     if (!dgtc::make_plan(16, 16, 8, 16, 3, 3, 1, 1, 1, 1, 8, 16, p)) return -1;
     dgtc::set_batch(p, 2);
-    float *buf = nullptr;  // dy, gi (2 x 16 x 8 x 16 floats each) and a zero weight image
+    // gi (2 x 16 x 8 x 16 floats), a zero weight image and zero dy planes
     const size_t n = 2 * 16 * 8 * 16;
-    const size_t img = (size_t)dgtc::weight_image_bytes(p);
-    cudaError_t e = cudaMalloc(&buf, 2 * n * sizeof(float) + img);
+    const size_t img = ((size_t)dgtc::weight_image_bytes(p) + 255) & ~size_t(255);
+    const size_t planes = 3 * sizeof(uint16_t) * (size_t)dgtc::plane_elements(p);
+    uint8_t *buf = nullptr;
+    cudaError_t e = cudaMalloc(&buf, n * sizeof(float) + img + planes);
     if (e != cudaSuccess) return (int)e;
     cudaStream_t st = as_stream(stream);
-    TRBA_CHECK(cudaMemsetAsync(buf, 0, 2 * n * sizeof(float) + img, st));
+    TRBA_CHECK(cudaMemsetAsync(buf, 0, n * sizeof(float) + img + planes, st));
     dgtc::Args a{};
-    a.dy = buf;
-    a.gi = buf + n;
-    a.wimg = reinterpret_cast<const uint8_t *>(buf + 2 * n);
+    a.gi = reinterpret_cast<float *>(buf);
+    a.wimg = buf + n * sizeof(float);
+    a.planes = reinterpret_cast<const uint16_t *>(buf + n * sizeof(float) + img);
+    a.plane_elems = dgtc::plane_elements(p);
     a.w_s_val = 1.0f;
     a.B = p.B;
     a.stages = dgtc::stages_for(p.BN);

@@ -42,6 +42,7 @@ struct Class {
 struct Plan {
     int ncls;
     int Cin, Cout, H, W, Ho, Wo, kH, kW, sH, sW, pH, pW;
+    int lgCout, lgSH, lgSW;  // log2 of Cout and of the strides (all powers of two)
     int Npad;          // Cin rounded up to the N tile
     int BN;            // N of one MMA tile: 16, 32, 64 or 128
     int ntn;           // N tiles (Npad / BN)
@@ -52,8 +53,8 @@ struct Plan {
 };
 
 // Builds the class plan of a conv, or returns false when the kernel does not
-// serve it (Cout not a multiple of 8, more than 4 stride phases or 16 taps
-// per phase).  Batch-dependent fields are filled by set_batch.
+// serve it (Cout or a stride not a power of two, Cout < 8, more than 4
+// stride phases or 16 taps per phase).  Batch-dependent fields are filled by set_batch.
 bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
                Plan &p);
 void set_batch(Plan &p, int B);
@@ -88,14 +89,19 @@ __device__ __forceinline__ int image_source(const Plan &p, int gc, int n, int kl
     return n * p.kH * p.kW + C.kh[tap] * p.kW + C.kw[tap];
 }
 
-// One launch: gi (NCHW f32) from dy (NCHW f32) and the weight image.
-// ws_co (optional, per-output-channel weight scales): dy[b, co] is
-// multiplied by ws_co[co] as it is gathered.  Epilogue as the exact
+// Elements of one bf16 plane of dy (NHWC, B x Ho x Wo x Cout); the launch
+// needs a scratch of 3 planes (6 bytes per dy element).
+inline long long plane_elements(const Plan &p) { return (long long)p.B * p.Ho * p.Wo * p.Cout; }
+
+// gi (NCHW f32) from dy (NCHW f32) and the weight image: two launches (the
+// split of dy into three bf16 planes, in `planes`, then the tensor-core
+// GEMM).  ws_co (optional, per-output-channel weight scales): dy[b, co] is
+// multiplied by ws_co[co] before the split.  Epilogue as the exact
 // kernel's: v = acc * w_s (the device scalar w_s, or w_s_val when w_s is
 // null); v = mask_q[i] > 0 ? v : 0 (when mask_q); v += add[i] (when add);
 // gi[i] = v; and, when gmax_out, atomic max of |v * gmax_scale| into
 // gmax_out.  add may alias gi.
-void launch(const Plan &p, const uint8_t *wimg, const float *dy, const float *w_s, float w_s_val,
+void launch(const Plan &p, const uint8_t *wimg, uint16_t *planes, const float *dy, const float *w_s, float w_s_val,
             const float *ws_co, const int8_t *mask_q, const float *add, float *gi, const float *gmax_scale,
             float *gmax_out, cudaStream_t st);
 

@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -206,6 +207,7 @@ struct trba_model {
     Ref<float> d_out_hid, adg, ade, adprojhh, d_proj_h, d_bh;
     Ref<double> ctc_sample_loss;
     Ref<double> gemm_ws;   // split-K partial sums of the fp32 GEMMs
+    Ref<uint16_t> dg_planes;  // tensor-core input gradient: dy as three bf16 planes (largest conv's dy)
     i64 gemm_ws_elems = 0;
     Ref<float> ones;       // column-sum helper
     Ref<float> loss;  // 4 floats
@@ -818,6 +820,12 @@ void allocate(trba_model *m) {
     m->d_proj_h = b.tp<float>((i64)B * T * Hh);
     m->d_bh = b.tp<float>((i64)B * T * Hh);
     m->ctc_sample_loss = b.p<double>(B);
+    {
+        i64 planes = 0;  // scratch of the tensor-core input gradients, reused conv after conv (one stream)
+        for (auto &L : m->convs)
+            if (L.tc_ok) planes = std::max(planes, 3 * (i64)B * L.cout * L.Ho * L.Wo);
+        if (planes) m->dg_planes = b.tp<uint16_t>(planes);
+    }
     m->gemm_ws_elems = (i64)8 << 20;
     m->gemm_ws = b.p<double>(m->gemm_ws_elems);
     m->ones = b.p<float>((i64)B * (S > T ? S : T) * 1);
@@ -998,7 +1006,8 @@ void conv_bwd(Ctx &c, ConvL &L, const float *dy, const int8_t *mask_q, const flo
         if (L.tc_ok) {
             dgtc::Plan p = L.tc;
             dgtc::set_batch(p, B);
-            dgtc::launch(p, L.wimg.get(), dy, pc ? c.m->ones.get() : L.ws.get(), 1.0f, pc ? L.ws.get() : nullptr,
+            dgtc::launch(p, L.wimg.get(), c.m->dg_planes.get(), dy, pc ? c.m->ones.get() : L.ws.get(), 1.0f,
+                         pc ? L.ws.get() : nullptr,
                          mask_q, add, gi, gmax_scale, gmax_out, c.st);
             return;
         }

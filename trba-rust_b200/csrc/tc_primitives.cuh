@@ -65,6 +65,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+// The same for a role with little to do between waits (an epilogue waiting
+// for a whole tile): backs off with __nanosleep between polls so it does not
+// take issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                                uint64_t limit_ns, unsigned sleep_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        __nanosleep(sleep_ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > limit_ns) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -98,6 +116,20 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // proxy (the tensor cores read operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (L2 only); src_bytes 0 fills
+// the 16 bytes with zeros without reading src.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ---------------------------------------------------------------- TMEM
