@@ -183,7 +183,13 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
         const int l8 = threadIdx.x & 7, rs = threadIdx.x >> 3;
         const int lgC = P.lgCout;
         uint32_t it = 0;
-        int pend = -1;  // stage of the copy group issued but not yet handed to the MMA warp
+        // Copy groups issued but not yet handed to the MMA warp (their
+        // stages, oldest first): one chunk's copies stay in flight while the
+        // next chunk's are issued.  (Deeper, stages - 1 groups in flight,
+        // measured slower: the MMA warp then waits on fewer landed stages.)
+        const int depth = 1;
+        int pend[kMaxStages];
+        int npend = 0;
         for (int t = blockIdx.x; t < P.tiles && !*abort; t += gridDim.x) {
             const Class &C = P.cls[tile_class(P, t)];
             if (C.kchunks == 0) continue;  // a phase without taps: the epilogue alone writes it
@@ -225,19 +231,22 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                         cp_async16(dst + p * kPartBytes, a.planes + p * a.plane_elems + e, ok ? 16u : 0u);
                 }
                 cp_async_commit();
-                if (pend >= 0) {  // the previous chunk's copies have landed: hand its stage over
-                    cp_async_wait<1>();
+                pend[npend++] = s;
+                if (npend > depth) {
+                    // the oldest group has landed once at most `depth` newer ones are pending
+                    if (depth >= 3) cp_async_wait<3>();
+                    else if (depth == 2) cp_async_wait<2>();
+                    else cp_async_wait<1>();
                     fence_proxy_async_smem();
-                    mbar_arrive(&ctl->afull[pend]);
+                    mbar_arrive(&ctl->afull[pend[0]]);
+                    for (int j = 1; j < npend; ++j) pend[j - 1] = pend[j];
+                    --npend;
                 }
-                pend = s;
             }
         }
         cp_async_wait<0>();
-        if (pend >= 0) {
-            fence_proxy_async_smem();
-            mbar_arrive(&ctl->afull[pend]);
-        }
+        fence_proxy_async_smem();
+        for (int j = 0; j < npend; ++j) mbar_arrive(&ctl->afull[pend[j]]);
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {

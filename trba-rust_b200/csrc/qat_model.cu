@@ -1417,9 +1417,10 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
                        L.run_var.get(), L.cout, L.K, L.kp, L.tc_ok ? nullptr : L.wT.get(), L.kh * L.kw,
-                       L.tc_ok ? L.d_tc.get() : nullptr, L.tc_ok ? L.wimg.get() : nullptr, m->cfg.wq_per_channel});
-        if (L.tc_ok) TRBA_CHECK(cudaMemcpy(L.d_tc.get(), &L.tc, sizeof(dgtc::Plan), cudaMemcpyHostToDevice));
-        if (!L.tc_ok && !L.cls_perm.empty()) {
+                       L.d_tc.get(), L.wimg.get(), m->cfg.wq_per_channel});
+        // (the input-gradient tables are training buffers: absent in an inference-only model)
+        if (L.d_tc.get()) TRBA_CHECK(cudaMemcpy(L.d_tc.get(), &L.tc, sizeof(dgtc::Plan), cudaMemcpyHostToDevice));
+        if (L.d_perm.get() && !L.cls_perm.empty()) {
             TRBA_CHECK(cudaMemcpy(L.d_perm.get(), L.cls_perm.data(), sizeof(int) * L.cls_perm.size(),
                                   cudaMemcpyHostToDevice));
             TRBA_CHECK(cudaMemcpy(L.d_cstart.get(), L.cls_start.data(), sizeof(int) * L.cls_start.size(),
