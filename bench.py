@@ -68,6 +68,9 @@ def parse():
     ap.add_argument("--mope-batch", type=int, default=512)
     ap.add_argument("--gemm-shape", default=None,
                     help="M,N,K: time only the int8 GEMM (s32 and fused int8 epilogue) at this shape")
+    ap.add_argument("--dgrad-shape", default=None,
+                    help="B,Cin,H,W,Cout,kh,kw,sh,sw,ph,pw: time only the tensor-core conv input gradient "
+                         "(trba_conv_grad_input_i8_tc) at this shape")
     return ap.parse_args()
 
 
@@ -413,22 +416,39 @@ def our_arm(args):
     roofline = None
     if dg_n > 0 and dg_ms > 0:
         per_launch_s = dg_ms * 1e-3 / dg_n
-        achieved = dg_ops / dg_n / per_launch_s / 1e12
-        traffic = profiled_traffic("dgrad_kernel", args.batch)
-        roofline = {
-            "kernel": "dgrad_kernel: conv input gradient, f32 in the reference's summation order",
-            "bound": "fp32",
-            "achieved": achieved, "peak": f32_peak.value, "unit": "TFLOP/s",
-            "frac": achieved / f32_peak.value,
-            "peak_source": "measured in this run: separately rounded f32x2 multiply + add chains on every SM",
+        useful = dg_ops / dg_n / per_launch_s / 1e12  # fp32-equivalent multiply-adds of the gather terms
+        hbm = measured_peaks().get("hbm_gbs")
+        if args.dgrad_mode == 1:
+            # tensor cores: dy enters as three bf16 terms, so the MMA work of
+            # the exact product is three times the useful multiply-adds
+            peak = measured_peaks().get("bf16_tflops_sustained")
+            achieved = 3.0 * useful
+            traffic = profiled_traffic("dgrad_tc_kernel", args.batch)
+            roofline = {
+                "kernel": "dgrad_tc_kernel + split_nhwc_kernel: conv input gradient, implicit GEMM on tcgen05 "
+                          "(kind::f16, dy as three exact bf16 terms)",
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if peak else None,
+                "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (the kernel runs inside a long step)",
+                "useful_fp32_equiv_tflops": useful,
+            }
+        else:
+            traffic = profiled_traffic("dgrad_kernel", args.batch)
+            roofline = {
+                "kernel": "dgrad_kernel: conv input gradient, f32 in the reference's summation order",
+                "bound": "fp32", "achieved": useful, "peak": f32_peak.value, "unit": "TFLOP/s",
+                "frac": useful / f32_peak.value,
+                "peak_source": "measured in this run: separately rounded f32x2 multiply + add chains on every SM",
+            }
+        roofline.update({
             "traffic": traffic,
             "algorithmic_bytes_per_launch": dg_bytes / dg_n,
             "hbm_gbs_at_algorithmic_bytes": dg_bytes / dg_n / per_launch_s / 1e9,
-            "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
+            "hbm_peak_gbs": hbm,
             "launches_per_step": dg_n / dg_steps,
             "ms_per_step": dg_ms / dg_steps,
             "share_of_step": dg_ms / dg_steps / ms,
-        }
+        })
     gemm_line = None
     head = gemm.pop("head_sgemm_f64acc")
     if int8_peak:
@@ -543,6 +563,44 @@ def gemm_only(args):
     if L.trba_tc_error_poll(1) != 0:
         raise RuntimeError("tensor-core GEMM reported a timed-out wait")
     print(json.dumps(out), flush=True)
+
+
+def dgrad_only(args):
+    """One conv input-gradient shape through trba_conv_grad_input_i8_tc (for
+    timing and profiling one kernel): per-call device time with CUDA events
+    (weight image, dy split and the tensor-core GEMM), after 3 warm-up calls."""
+    import torch
+    B, cin, h, w, cout, kh, kw, sh, sw, ph, pw = (int(x) for x in args.dgrad_shape.split(","))
+    ho, wo = (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
+    pkg = load_package()
+    L = pkg.lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    kp = (cin * kh * kw + 15) & ~15
+    dy = torch.randn((B, cout, ho, wo), device=dev, generator=g) * 1e-3
+    wq = torch.randint(-127, 128, ((cout + 15) & ~15, kp), dtype=torch.int8, device=dev, generator=g)
+    gi = torch.empty((B, cin, h, w), device=dev)
+    a = (C.c_void_p(dy.data_ptr()), C.c_void_p(wq.data_ptr()), kp, 0.01, C.c_void_p(gi.data_ptr()), B, cin, h, w,
+         cout, kh, kw, sh, sw, ph, pw, ho, wo, None)
+    for _ in range(3):
+        if L.trba_conv_grad_input_i8_tc(*a) != 0:
+            raise RuntimeError(L.trba_last_error_string().decode())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(1, args.steps)
+    e0.record()
+    for _ in range(n):
+        L.trba_conv_grad_input_i8_tc(*a)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    vy = sum(1 for y in range(h) for t in range(kh) if (y + ph - t) >= 0 and (y + ph - t) % sh == 0 and (y + ph - t) // sh < ho)
+    vx = sum(1 for x in range(w) for t in range(kw) if (x + pw - t) >= 0 and (x + pw - t) % sw == 0 and (x + pw - t) // sw < wo)
+    flops = 2.0 * B * cin * cout * vy * vx
+    if L.trba_tc_error_poll(1) != 0 or L.trba_last_error() != 0:
+        raise RuntimeError("input-gradient kernel reported an error")
+    print(json.dumps({"dgrad": [B, cin, h, w, cout, kh, kw, sh, sw, ph, pw], "us_per_call": us,
+                      "useful_tflops": flops / (us * 1e-6) / 1e12,
+                      "bf16_mma_tflops_three_terms": 3 * flops / (us * 1e-6) / 1e12}), flush=True)
 
 
 def mope_arm(args):
@@ -700,6 +758,9 @@ def main():
         return
     if args.gemm_shape:
         gemm_only(args)
+        return
+    if args.dgrad_shape:
+        dgrad_only(args)
         return
     if args.impl == "reference":
         reference_arm(args)

@@ -21,8 +21,9 @@
 //                 A operands of a shared-memory stage (128-byte rows,
 //                 16-byte pieces XOR-swizzled by row, the layout TMA's
 //                 SWIZZLE_128B produces; zero-filled where the tap leaves
-//                 the output grid), one copy group in flight per thread
-//                 while the next is issued; thread 0 bulk-copies the
+//                 the output grid); each thread's copies of a stage arrive
+//                 on the stage's barrier when they land, so producers run
+//                 ahead over every free stage; thread 0 bulk-copies the
 //                 stage's weight chunk, pre-swizzled in global memory.
 //     warp 4      MMA issuer (lane 0): per stage, 3 terms x 4 MMAs of
 //                 M = 128, N = BN, K = 16 into one of two TMEM
@@ -183,13 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
         const int l8 = threadIdx.x & 7, rs = threadIdx.x >> 3;
         const int lgC = P.lgCout;
         uint32_t it = 0;
-        // Copy groups issued but not yet handed to the MMA warp (their
-        // stages, oldest first): one chunk's copies stay in flight while the
-        // next chunk's are issued.  (Deeper, stages - 1 groups in flight,
-        // measured slower: the MMA warp then waits on fewer landed stages.)
-        const int depth = 1;
-        int pend[kMaxStages];
-        int npend = 0;
         for (int t = blockIdx.x; t < P.tiles && !*abort; t += gridDim.x) {
             const Class &C = P.cls[tile_class(P, t)];
             if (C.kchunks == 0) continue;  // a phase without taps: the epilogue alone writes it
@@ -230,23 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                     for (int p = 0; p < 3; ++p)
                         cp_async16(dst + p * kPartBytes, a.planes + p * a.plane_elems + e, ok ? 16u : 0u);
                 }
-                cp_async_commit();
-                pend[npend++] = s;
-                if (npend > depth) {
-                    // the oldest group has landed once at most `depth` newer ones are pending
-                    if (depth >= 3) cp_async_wait<3>();
-                    else if (depth == 2) cp_async_wait<2>();
-                    else cp_async_wait<1>();
-                    fence_proxy_async_smem();
-                    mbar_arrive(&ctl->afull[pend[0]]);
-                    for (int j = 1; j < npend; ++j) pend[j - 1] = pend[j];
-                    --npend;
-                }
+                // the stage's barrier receives this thread's arrival when its
+                // copies have landed: no waiting here, the next chunk's copies
+                // go out at once (the MMA warp fences the async proxy)
+                cp_async_arrive_noinc(&ctl->afull[s]);
             }
         }
-        cp_async_wait<0>();
-        fence_proxy_async_smem();
-        for (int j = 0; j < npend; ++j) mbar_arrive(&ctl->afull[pend[j]]);
+        cp_async_wait<0>();  // nothing may land after the CTA is gone
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
@@ -264,6 +248,9 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                     if (!(ok = mbar_wait(&ctl->bfull[s], ph, abort, a.wait_ns))) break;
                     ctl->b_consumed = it + 1;
                     if (!(ok = mbar_wait(&ctl->afull[s], ph, abort, a.wait_ns))) break;
+                    // the stage's A rows were written by the producers' cp.async (generic
+                    // proxy); order them before the tensor cores' reads (async proxy)
+                    fence_proxy_async_smem();
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + (size_t)s * G::STAGE);
                     const uint32_t b0 = st + 3 * kPartBytes;

@@ -126,6 +126,11 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t 
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// One arrival on `bar` once every cp.async this thread issued so far has
+// completed (the barrier's expected count includes it: noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 // Wait until at most N of this thread's committed copy groups are pending.
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
