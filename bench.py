@@ -352,6 +352,10 @@ def our_arm(args):
     for _ in range(args.steps):
         m.train_step(*devb, stream=sptr)
     e1.record(stream)
+    # NCCL failure detection: a rank whose peer failed (or never joined) aborts
+    # its communicator instead of hanging in the next synchronisation
+    if world > 1 and m.dp_wait(sptr, timeout_s=120.0) != 0:
+        raise RuntimeError("data-parallel step failed: the NCCL communicator was aborted")
     barrier()
     ck = clocks.stop()
     launches = (L.trba_launch_count() - l0) / args.steps
