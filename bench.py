@@ -124,6 +124,10 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def metric_name(args) -> str:
+    return METRIC if args.img_w == 160 else f"QAT train lines/s (TRBA 32x{args.img_w})"
+
+
 def workload_config(args, world: int) -> dict:
     """The `config` object both arms print: the workload, never the sample."""
     return {"workload": f"TRBA-small QAT train step 32x{args.img_w}, max_len {args.max_len}, "
@@ -175,7 +179,7 @@ def reference_arm(args):
     sample = (f"{lines} lines of the workload per step x {args.steps} timed steps (after {args.warmup} warm-up), "
               f"{lib}, OMP {cores} threads")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "lines/s", "n_gpus": world,
+        "impl": "reference", "metric": metric_name(args), "value": v, "unit": "lines/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * lines / v, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 (s8xs8->s32) / fp32", "data": "synthetic",
         "config": workload_config(args, world),
@@ -488,7 +492,7 @@ def our_arm(args):
                        "best_frac_requant_i8_compute_bound": max(
                            (c["frac_peak"] for c in sweep["compute_bound_requant_i8"]), default=None)}
         out = {
-            "metric": METRIC, "value": value, "unit": "lines/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args), "value": value, "unit": "lines/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 (s8xs8->s32) / fp32", "data": "synthetic",
             "config": workload_config(args, world),
