@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--dgrad-shape", default=None,
                     help="B,Cin,H,W,Cout,kh,kw,sh,sw,ph,pw: time only the tensor-core conv input gradient "
                          "(trba_conv_grad_input_i8_tc) at this shape")
+    ap.add_argument("--dgrad-tiling", default="0,0",
+                    help="mb,kc of the tensor-core input gradient (trba_tc_dgrad_tiling): -1,0 class tiling "
+                         "for every conv, 0,0 automatic, else a forced halo tile")
     return ap.parse_args()
 
 
@@ -310,6 +313,7 @@ def our_arm(args):
     from trba_b200 import data, dp
     from trba_b200.model import Config, QatModel
     L = pkg.lib()
+    L.trba_tc_dgrad_tiling(*(int(x) for x in args.dgrad_tiling.split(",")))
     cfg = Config(img_w=args.img_w, max_len=args.max_len, batch=args.batch, dgrad_mode=args.dgrad_mode)
     m = QatModel(cfg)
     m.set_params(data.init_params(m.manifest(), cfg, args.seed))
@@ -582,6 +586,11 @@ def dgrad_only(args):
     ho, wo = (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
     pkg = load_package()
     L = pkg.lib()
+    L.trba_tc_dgrad_tiling(*(int(x) for x in args.dgrad_tiling.split(",")))
+    plan = (C.c_longlong * 80)()
+    nf = L.trba_tc_dgrad_plan(B, cin, h, w, cout, kh, kw, sh, sw, ph, pw, ho, wo, plan, 80)
+    names = "halo BN Npad ntn tiles ntaps KC nchunks mb R sa sb Hq Wq dmin mpos rows".split()
+    plan_info = dict(zip(names, list(plan[:min(nf, len(names))])))
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(3)
     kp = (cin * kh * kw + 15) & ~15
@@ -606,7 +615,7 @@ def dgrad_only(args):
     flops = 2.0 * B * cin * cout * vy * vx
     if L.trba_tc_error_poll(1) != 0 or L.trba_last_error() != 0:
         raise RuntimeError("input-gradient kernel reported an error")
-    print(json.dumps({"dgrad": [B, cin, h, w, cout, kh, kw, sh, sw, ph, pw], "us_per_call": us,
+    print(json.dumps({"dgrad": [B, cin, h, w, cout, kh, kw, sh, sw, ph, pw], "plan": plan_info, "us_per_call": us,
                       "useful_tflops": flops / (us * 1e-6) / 1e12,
                       "bf16_mma_tflops_three_terms": 3 * flops / (us * 1e-6) / 1e12}), flush=True)
 

@@ -66,11 +66,14 @@ int trba_gemm_pair_enable(int enable);
  * snapshot's cuda/kernels.cu:913-957) on the tensor cores: an implicit GEMM
  * per stride-phase class of input pixels (tcgen05 kind::f16, the fp32
  * output gradient as three bf16 terms whose sum is exact, the int8 weights
- * exact in bf16, fp32 accumulation).  Same arguments and result as the
- * reference launcher up to the order of the fp32 additions (relative
- * differences around 1e-6 of the gradient's scale).  Needs Cout % 8 == 0,
- * at most 4 stride phases and 16 taps per phase.  Keeps a grow-only
- * per-device buffer for the bf16 weight image.  Returns 0, -1 for an
+ * exact in bf16, fp32 accumulation).  Stride-1 convs (Cout % 16 == 0,
+ * padding below the kernel size) use the halo tiling instead: dy on a
+ * zero-padded grid, one shared-memory halo per tile serving every tap as a
+ * shifted window.  Same arguments and result as the reference launcher up
+ * to the order of the fp32 additions (relative differences around 1e-6 of
+ * the gradient's scale).  Needs Cout a power of two >= 8, at most 4 stride
+ * phases and 16 taps per phase.  Keeps a grow-only per-device buffer for
+ * the bf16 weight image and the dy planes.  Returns 0, -1 for an
  * unsupported conv, or a CUDA error code. */
 int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, int w_ld, float w_scale,
                                float *grad_input, int b, int cin, int h, int w, int cout, int kh, int kw,
@@ -78,12 +81,29 @@ int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, in
 
 /* Self-test of the bounded waits of the tensor-core kernels (no
  * counterpart in the reference): runs one small tensor-core input-gradient
- * launch whose weight copies are deliberately never issued, so its pipeline
- * waits give up after limit_ns instead of hanging; the kernel releases its
- * tensor memory and raises the device error word.  Synchronises the stream;
- * returns the error word (1: the waits gave up as designed), which it
- * clears, or a negative value / CUDA error code. */
+ * launch of each tiling (class and halo) whose weight copies are
+ * deliberately never issued, so its pipeline waits give up after limit_ns
+ * instead of hanging; each kernel releases its tensor memory and raises the
+ * device error word.  Synchronises the stream; returns 1 when both launches
+ * gave up as designed (the word is cleared after each), or the other
+ * launch's error word / a negative value / a CUDA error code. */
 int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream);
+
+/* Tiling of the tensor-core input gradient for plans made after the call
+ * (process wide; no counterpart in the reference, for tests and tuning):
+ * mb < 0 keeps every conv on the class tiling, mb == 0 (the default) lets a
+ * cost model pick the halo tile of stride-1 convs, mb = 1, 2 or 4 forces
+ * 128 * mb positions per halo tile, and kc = 16, 32 or 64 forces the output
+ * channels per halo stage (0: chosen). */
+void trba_tc_dgrad_tiling(int mb, int kc);
+
+/* Host-side plan of the tensor-core input gradient of a conv at batch b (no
+ * counterpart in the reference; no GPU work): fills up to n_out fields of
+ * out (tiling, tile counts, halo geometry, scratch and shared-memory sizes,
+ * per-tap offsets; the order is documented at the definition) and returns
+ * how many the plan has, or -1 when the conv is not served. */
+int trba_tc_dgrad_plan(int b, int cin, int h, int w, int cout, int kh, int kw, int sh, int sw, int ph, int pw,
+                       int ho, int wo, long long *out, int n_out);
 
 /* Device error word of the tensor-core kernels: 1 when a bounded mbarrier
  * wait gave up.  Synchronises the device; clears the word if clear != 0. */

@@ -4,7 +4,10 @@ the training step's dgrad_mode = 1) against the reference's exact gather.
 Op level: every conv shape of the model (and odd ones: Cin not a multiple of
 16, a partial last tile, 1x1 stride 2, the 2x2 stride (2, 1) head conv) on
 the same seeded dy and int8 weights, through the C ABI, against the oracle's
-launch_conv_backward_grad_input_i8 (the reference's f32 summation order).
+launch_conv_backward_grad_input_i8 (the reference's f32 summation order),
+under the default tiling (the halo tiling for stride-1 convs), with every conv
+forced onto the class tiling, and with forced halo tiles (128, 256 or 512
+positions; 16, 32 or 64 output channels per halo stage).
 The tensor-core result is exact up to the order of its fp32 additions, so the
 bar is max |diff| <= 1e-4 x max |gi| (the reference's own bar for gradients
 is 1e-3).
@@ -48,6 +51,9 @@ SHAPES = [
     (3, 24, 7, 9, 16, 3, 3, 1, 1, 1, 1),       # Cin 24 (padded N), 7x9 planes, partial tile
     (2, 8, 5, 6, 8, 3, 3, 2, 2, 1, 1),         # Cout 8, odd planes, stride 2
     (1, 200, 4, 4, 16, 3, 3, 1, 1, 1, 1),      # Cin > 128: two N tiles
+    (2, 16, 5, 7, 32, 1, 1, 1, 1, 0, 0),       # 1x1 stride 1
+    (2, 8, 6, 5, 16, 3, 2, 1, 1, 1, 0),        # asymmetric kernel and padding
+    (2, 8, 6, 9, 16, 3, 3, 1, 1, 0, 2),        # padding 0 on one axis, 2 on the other
 ]
 
 
@@ -55,10 +61,25 @@ def _out_hw(h, w, kh, kw, sh, sw, ph, pw):
     return (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
 
 
+# Tilings: (0, 0) the default (halo tiling for stride-1 convs, chosen tile),
+# (-1, 0) every conv on the class tiling, then forced halo tiles.
+TILINGS = [(0, 0), (-1, 0), (1, 16), (2, 32), (4, 16), (1, 64)]
+
+
+@pytest.fixture
+def tiling(request, lib):
+    lib.trba_tc_dgrad_tiling(*request.param)
+    yield request.param
+    lib.trba_tc_dgrad_tiling(0, 0)
+
+
+@pytest.mark.parametrize("tiling", TILINGS, ids=lambda t: "mb{}_kc{}".format(*t), indirect=True)
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "b{}_c{}_{}x{}_o{}_k{}x{}_s{}{}".format(*s[:9]))
-def test_tc_input_gradient_matches_exact_gather(shape, lib, cuda, oracle):
+def test_tc_input_gradient_matches_exact_gather(shape, tiling, lib, cuda, oracle):
     import torch
     B, cin, h, w, cout, kh, kw, sh, sw, ph, pw = shape
+    if tiling not in ((0, 0), (-1, 0)) and (sh, sw) != (1, 1):
+        pytest.skip("forced halo tiles apply to stride-1 convs only")
     ho, wo = _out_hw(h, w, kh, kw, sh, sw, ph, pw)
     rng = np.random.default_rng(sum(shape))
     dy = (rng.standard_normal((B, cout, ho, wo)) * 1e-3).astype(np.float32)

@@ -40,6 +40,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -138,6 +139,38 @@ template <int CW>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[CW]) {
     if constexpr (CW == 16) tmem_ld_32x32b_x16(taddr, v);
     else tmem_ld_32x32b_x32(taddr, v);
+}
+
+// Epilogue of CW accumulator columns of one output pixel (row of the tile):
+// every STE-mask and residual value of the columns is loaded first, so the
+// loads are in flight together (`add` may alias `gi`, but each element is
+// read before it is written), then the values are scaled, masked, added and
+// stored, and |v * gsc| goes into the running max.  Columns j < nvalid are
+// real input channels; rv: the row is a real pixel; base: its element of
+// column 0 (NCHW, channel stride HW).
+template <int CW>
+__device__ __forceinline__ void epilogue_cols(const uint32_t (&v)[CW], bool any, float ws, const Args &a, i64 base,
+                                              i64 HW, int nvalid, bool rv, float gsc, float &gm) {
+    float av[CW];
+    bool keep[CW];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        const bool ok = rv && j < nvalid;
+        const i64 e = base + (i64)j * HW;
+        av[j] = (ok && a.add) ? a.add[e] : 0.0f;
+        keep[j] = (ok && a.mask_q) ? a.mask_q[e] > 0 : true;
+    }
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+        if (rv && j < nvalid) {
+            const i64 e = base + (i64)j * HW;
+            float val = any ? fmul(__uint_as_float(v[j]), ws) : 0.0f;
+            if (a.mask_q) val = keep[j] ? val : 0.0f;
+            if (a.add) val = fadd(val, av[j]);
+            a.gi[e] = val;
+            gm = fmaxf(gm, fabsf(fmul(val, gsc)));
+        }
+    }
 }
 
 template <int BN>
@@ -252,14 +285,15 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                     // proxy); order them before the tensor cores' reads (async proxy)
                     fence_proxy_async_smem();
                     tc_fence_after();
-                    const uint32_t st = smem_u32(smem + (size_t)s * G::STAGE);
-                    const uint32_t b0 = st + 3 * kPartBytes;
+                    // the stage's base descriptors once, then compile-time offsets
+                    const uint64_t da = desc_k_sw128(smem_u32(smem + (size_t)s * G::STAGE));
+                    const uint64_t db = da + (uint64_t)((3 * kPartBytes) >> 4);
 #pragma unroll
                     for (int p = 0; p < 3; ++p)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            mma_bf16(d, desc_k_sw128(st + p * kPartBytes + k * 32), desc_k_sw128(b0 + k * 32), idesc,
-                                     (kc | p | k) ? 1u : 0u);
+                            mma_bf16(d, da + (uint64_t)((p * kPartBytes + k * 32) >> 4), db + (uint64_t)((k * 32) >> 4),
+                                     idesc, (kc | p | k) ? 1u : 0u);
                     mma_commit(&ctl->empty[s]);
                 }
                 if (!ok) break;
@@ -300,17 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                     tmem_ld_cols<CW>(tbase + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
                     tmem_ld_wait();
                 }
-#pragma unroll
-                for (int j = 0; j < CW; ++j) {
-                    if (rv && n0 + c0 + j < P.Cin) {
-                        const i64 i = base + (i64)(c0 + j) * HW;
-                        float val = any ? fmul(__uint_as_float(v[j]), ws) : 0.0f;
-                        if (a.mask_q) val = a.mask_q[i] > 0 ? val : 0.0f;
-                        if (a.add) val = fadd(val, a.add[i]);
-                        a.gi[i] = val;
-                        gm = fmaxf(gm, fabsf(fmul(val, gsc)));
-                    }
-                }
+                epilogue_cols<CW>(v, any, ws, a, base + (i64)c0 * HW, HW, P.Cin - n0 - c0, rv, gsc, gm);
             }
             tc_fence_before();
             mbar_arrive(&ctl->tempty[acc]);
@@ -342,6 +366,280 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
     }
 }
 
+
+// ------------------------------------------------------------ halo tiling
+// Stride-1 convs (plan.halo).  7 warps:
+//   warp 0      halo producer: per (tile, chunk of KC output channels), one
+//               bulk copy per (plane, 8-channel slab) of the tile's R
+//               consecutive plane rows into an A stage laid out
+//               [plane][slab][R rows][16 bytes] (no swizzle: a window of 128
+//               rows starting at any row is a valid K-major operand with
+//               SBO = 128 and LBO = R * 16).
+//   warp 1      weight producer (lane 0): one bulk copy per (chunk, tap) of
+//               the pre-laid-out weight block [KC / 8][BN][8].
+//   warp 2      MMA issuer (lane 0): per (chunk, tap), 3 terms x KC / 16
+//               K steps x mb row blocks of M = 128, N = BN, K = 16, the A
+//               window shifted by the tap's offset; double-buffered TMEM
+//               accumulators of mb x BN columns.
+//   warps 3..6  epilogue, as the class kernel's, over the tile's positions
+//               (gap positions are skipped).
+constexpr int kHWarps = 7;
+constexpr int kHThreads = 32 * kHWarps;
+constexpr int kHEpi0 = 3;
+constexpr int kMaxBStages = 16;
+
+struct HCtl {
+    uint64_t afull[2], aempty[2];
+    uint64_t bfull[kMaxBStages], bempty[kMaxBStages];
+    uint64_t tfull[2], tempty[2];
+    uint64_t drained;
+    uint32_t tmem_base;
+    int abort;
+    uint32_t a_issued, a_consumed, b_issued, b_consumed;
+};
+
+__host__ __device__ inline uint32_t halo_a_stage(const Halo &h) { return (3u * (h.KC >> 3) * h.R * 16 + 127) & ~127u; }
+__host__ __device__ inline uint32_t halo_b_stage(const Plan &p) { return (uint32_t)p.BN * p.h.KC * 2; }
+__host__ __device__ inline uint32_t halo_tmem_cols(const Plan &p) {
+    uint32_t c = 32;
+    while (c < 2u * p.h.mb * p.BN) c <<= 1;
+    return c;
+}
+
+// The MMAs of one (channel chunk, tap) of a halo tile: 3 split terms x
+// KC / 16 K steps x MB row blocks, every descriptor the stage's base plus a
+// compile-time offset (the per-term slab offsets are multiples of the run-time
+// halo height R, loop-invariant).  Issued by one elected lane of the calling
+// warp, which must be converged.  a_lo / b_lo: low descriptor words of the
+// tap's A window and of the weight block; first: the tile's first MMAs
+// (overwrite the accumulators).
+template <int BN, int KC, int MB>
+__device__ __forceinline__ void halo_tap_mmas(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t R,
+                                              uint32_t idesc, bool first) {
+    if (!elect_one()) return;
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int kk = 0; kk < KC / 16; ++kk) {
+            const uint64_t bd = desc_join(b_lo + kk * 2 * BN, hi);  // two slabs of BN rows x 16 bytes per K step
+#pragma unroll
+            for (int i = 0; i < MB; ++i)
+                mma_bf16(d + i * BN, desc_join(a_lo + (p * (KC / 8) + 2 * kk) * R + i * 128, hi), bd, idesc,
+                         (first && p == 0 && kk == 0) ? 0u : 1u);
+        }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_constant__ Plan P, const Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const Halo &h = P.h;
+    const int nsl = h.KC >> 3, ntaps = P.cls[0].ntaps, MT = 128 * h.mb;
+    const uint32_t slab = (uint32_t)h.R * 16, a_stage = halo_a_stage(h), b_stage = halo_b_stage(P);
+    uint8_t *As = smem;
+    uint8_t *Bs = smem + (size_t)h.sa * a_stage;
+    HCtl *ctl = reinterpret_cast<HCtl *>(Bs + (size_t)h.sb * b_stage);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tcols = halo_tmem_cols(P);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&ctl->afull[s], 1);
+            mbar_init(&ctl->aempty[s], 1);
+            mbar_init(&ctl->tfull[s], 1);
+            mbar_init(&ctl->tempty[s], 4 * 32);
+        }
+        for (int s = 0; s < h.sb; ++s) {
+            mbar_init(&ctl->bfull[s], 1);
+            mbar_init(&ctl->bempty[s], 1);
+        }
+        mbar_init(&ctl->drained, 1);
+        ctl->abort = 0;
+        ctl->a_issued = ctl->a_consumed = ctl->b_issued = ctl->b_consumed = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(&ctl->tmem_base, tcols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = ctl->tmem_base;
+    volatile int *abort = &ctl->abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------ halo producer
+        uint32_t ia = 0;
+        bool run = true;
+        for (int t = blockIdx.x; t < P.tiles && run; t += gridDim.x) {
+            const i64 row0 = (i64)(t / P.ntn) * MT;  // plane row of the halo's first row
+            for (int c = 0; c < h.nchunks; ++c, ++ia) {
+                const int s = ia % h.sa;
+                const uint32_t ph = (ia / h.sa) & 1u;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&ctl->aempty[s], ph ^ 1u, abort, a.wait_ns);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    run = false;
+                    break;
+                }
+                if (lane == 0) mbar_expect_tx(&ctl->afull[s], 3u * nsl * slab);
+                __syncwarp();
+                uint8_t *st = As + (size_t)s * a_stage;
+                for (int idx = lane; idx < 3 * nsl; idx += 32) {
+                    const int p = idx / nsl, sl = idx - p * nsl;
+                    bulk_load(st + (size_t)idx * slab,
+                              a.planes + p * a.plane_elems + ((i64)(c * nsl + sl) * h.rows + row0) * 8, slab,
+                              &ctl->afull[s]);
+                }
+                __syncwarp();
+                if (lane == 0) ctl->a_issued = ia + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ weight producer
+        if (lane == 0) {
+            uint32_t ib = 0;
+            bool run = true;
+            for (int t = blockIdx.x; t < P.tiles && run; t += gridDim.x) {
+                const int nt = t % P.ntn;
+                for (int c = 0; c < h.nchunks && run; ++c)
+                    for (int tap = 0; tap < ntaps; ++tap, ++ib) {
+                        const int s = ib % h.sb;
+                        const uint32_t ph = (ib / h.sb) & 1u;
+                        if (!mbar_wait(&ctl->bempty[s], ph ^ 1u, abort, a.wait_ns)) {
+                            run = false;
+                            break;
+                        }
+                        if (a.skip_weights) continue;
+                        mbar_expect_tx(&ctl->bfull[s], b_stage);
+                        bulk_load(Bs + (size_t)s * b_stage,
+                                  a.wimg + ((i64)(nt * h.nchunks + c) * ntaps + tap) * b_stage, b_stage,
+                                  &ctl->bfull[s]);
+                        ctl->b_issued = ib + 1;
+                    }
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ MMA issuer
+        // The whole warp runs the loop (its descriptor arithmetic stays
+        // warp-uniform); one elected lane issues the tcgen05 instructions.
+        constexpr uint32_t idesc = idesc_bf16(128, BN);
+        const uint32_t a_lo0 = ((smem_u32(As) >> 4) & 0x3FFFu) | desc_interleave_lo(slab);
+        const uint32_t b_lo0 = ((smem_u32(Bs) >> 4) & 0x3FFFu) | desc_interleave_lo(BN * 16);
+        const uint32_t hi = desc_interleave_hi(128);
+        const uint32_t a_step = a_stage >> 4, b_step = b_stage >> 4, R = (uint32_t)h.R;
+        const int kind = h.KC * 8 + h.mb;
+        uint32_t ia = 0, ib = 0, acc = 0, acc_ph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < P.tiles && ok; t += gridDim.x) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort, a.wait_ns));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t d = tbase + acc * h.mb * BN;
+            for (int c = 0; c < h.nchunks && ok; ++c, ++ia) {
+                const int sa = ia % h.sa;
+                ok = __all_sync(0xffffffffu, mbar_wait(&ctl->afull[sa], (ia / h.sa) & 1u, abort, a.wait_ns));
+                if (!ok) break;
+                ctl->a_consumed = ia + 1;  // every lane stores the same value: the warp stays converged
+                tc_fence_after();
+                const uint32_t a_lo = a_lo0 + sa * a_step;
+                for (int tap = 0; tap < ntaps; ++tap, ++ib) {
+                    const int sb = ib % h.sb;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&ctl->bfull[sb], (ib / h.sb) & 1u, abort, a.wait_ns));
+                    if (!ok) break;
+                    ctl->b_consumed = ib + 1;
+                    tc_fence_after();
+                    const uint32_t al = a_lo + (uint32_t)h.off[tap], bl = b_lo0 + sb * b_step;
+                    const bool first = (c | tap) == 0;
+                    switch (kind) {
+#define TRBA_HALO_TAP(KC_, MB_)                                                          \
+    case KC_ * 8 + MB_:                                                                  \
+        if constexpr (2 * MB_ * BN <= 512) halo_tap_mmas<BN, KC_, MB_>(d, al, bl, hi, R, idesc, first); \
+        break;
+                        TRBA_HALO_TAP(16, 1) TRBA_HALO_TAP(16, 2) TRBA_HALO_TAP(16, 4)
+                        TRBA_HALO_TAP(32, 1) TRBA_HALO_TAP(32, 2) TRBA_HALO_TAP(32, 4)
+                        TRBA_HALO_TAP(64, 1) TRBA_HALO_TAP(64, 2) TRBA_HALO_TAP(64, 4)
+#undef TRBA_HALO_TAP
+                        default: break;
+                    }
+                    __syncwarp();  // the issuing lane rejoins before the next elect
+                    if (elect_one()) mma_commit(&ctl->bempty[sb]);
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (elect_one()) mma_commit(&ctl->aempty[sa]);
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&ctl->tfull[acc]);
+            __syncwarp();
+            acc ^= 1u;
+            if (acc == 0) acc_ph ^= 1u;
+        }
+        if (elect_one()) mma_commit(&ctl->drained);
+        __syncwarp();
+        volatile int never = 0;
+        mbar_wait(&ctl->drained, 0, &never, 200000000ull);
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue
+        constexpr int CW = BN < 32 ? BN : 32;
+        const int q = warp & 3;  // TMEM lane quarter this warp may read
+        const float ws = a.w_s ? *a.w_s : a.w_s_val;
+        const float gsc = a.gmax_out ? *a.gmax_scale : 0.0f;
+        const int HW = P.H * P.W, HqWq = h.Hq * h.Wq;
+        float gm = 0.0f;
+        uint32_t acc = 0, acc_ph = 0;
+        for (int t = blockIdx.x; t < P.tiles; t += gridDim.x) {
+            const int mt = t / P.ntn, n0 = (t - mt * P.ntn) * BN;
+            const bool ok = mbar_wait_sleep(&ctl->tfull[acc], acc_ph, abort, a.wait_ns, 256);
+            __syncwarp();  // reconverge before the warp-collective tcgen05.ld
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            for (int i = 0; i < h.mb; ++i) {
+                const i64 pos = (i64)mt * MT + i * 128 + q * 32 + lane;
+                const int b = (int)(pos / HqWq), rem = (int)(pos - (i64)b * HqWq);
+                const int y = rem / h.Wq, x = rem - y * h.Wq;
+                const bool rv = pos < h.mpos && y < P.H && x < P.W;
+                const i64 base = ((i64)b * P.Cin + n0) * HW + (i64)y * P.W + x;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN && n0 + c0 < P.Cin; c0 += CW) {
+                    uint32_t v[CW];
+                    tmem_ld_cols<CW>(tbase + ((uint32_t)(q * 32) << 16) + (acc * h.mb + i) * BN + c0, v);
+                    tmem_ld_wait();
+                    epilogue_cols<CW>(v, true, ws, a, base + (i64)c0 * HW, HW, P.Cin - n0 - c0, rv, gsc, gm);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&ctl->tempty[acc]);
+            acc ^= 1u;
+            if (acc == 0) acc_ph ^= 1u;
+        }
+        if (a.gmax_out) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+            if (lane == 0 && gm > 0.0f) atomicMax(reinterpret_cast<int *>(a.gmax_out), __float_as_int(gm));
+        }
+    }
+
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort) {
+        // copies issued but never waited for must land before exit
+        volatile int never = 0;
+        for (uint32_t i = ctl->a_consumed; i < ctl->a_issued; ++i)
+            mbar_wait(&ctl->afull[i % h.sa], (i / h.sa) & 1u, &never, 200000000ull);
+        for (uint32_t i = ctl->b_consumed; i < ctl->b_issued; ++i)
+            mbar_wait(&ctl->bfull[i % h.sb], (i / h.sb) & 1u, &never, 200000000ull);
+        atomicExch(&g_dgtc_error, 1);
+    }
+    __syncthreads();
+    if (warp == 2) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tbase, tcols);
+    }
+}
 }  // namespace
 
 // dy (NCHW f32) -> hi / mid / lo bf16 planes (NHWC), optionally scaled per
@@ -379,40 +677,178 @@ __global__ void __launch_bounds__(256) split_nhwc_kernel(const float *__restrict
     }
 }
 
+// dy (NCHW f32) -> hi / mid / lo bf16 planes in the halo layout
+// [C / 8][rows][8]: plane row r holds position r + dmin of the padded grid
+// (Hq x Wq per image), dy where the position is a real output pixel, zero in
+// the gaps and guards (every row is written: the scratch is shared by convs
+// of different geometry).  Thread: one row x one 8-channel slab; a warp reads
+// 32 consecutive positions per channel and writes 512 contiguous bytes per
+// plane.
+__global__ void __launch_bounds__(256) split_halo_kernel(const float *__restrict__ dy,
+                                                         const float *__restrict__ ws_co, int C, int Ho, int Wo,
+                                                         int Hq, int Wq, int mpos, int dmin, int rows,
+                                                         uint16_t *__restrict__ planes, long long plane_elems) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x, sl = blockIdx.y;
+    if (r >= rows) return;
+    const int pos = r + dmin;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+    if (pos >= 0 && pos < mpos) {
+        const int HqWq = Hq * Wq, b = pos / HqWq, rem = pos - b * HqWq, yy = rem / Wq, xx = rem - yy * Wq;
+        if (yy < Ho && xx < Wo) {
+            const i64 HW = (i64)Ho * Wo;
+            const float *src = dy + ((i64)b * C + sl * 8) * HW + (i64)yy * Wo + xx;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                v[e] = __ldg(src + e * HW);
+                if (ws_co) v[e] = __fmul_rn(v[e], __ldg(ws_co + sl * 8 + e));
+            }
+        }
+    }
+    uint32_t hi[4], mid[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) split_pair(v[2 * e], v[2 * e + 1], hi[e], mid[e], lo[e]);
+    uint16_t *o = planes + ((i64)sl * rows + r) * 8;
+    *reinterpret_cast<uint4 *>(o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(o + plane_elems) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
+    *reinterpret_cast<uint4 *>(o + 2 * plane_elems) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
 // Weight image from an int8 weight matrix [cout rows, w_ld] with K order
 // (ci, kh, kw) (the ABI entry point's operand).
 __global__ void image_from_wq_kernel(const __grid_constant__ Plan P, const int8_t *__restrict__ wq, int w_ld,
                                      uint8_t *__restrict__ wimg) {
-    const i64 n = (i64)P.total_chunks * P.Npad * kChunk;
+    const i64 n = image_elements(P);
     GRID_LOOP(e, n) {
-        int gc, row, kl, co;
-        image_entry(P, e, gc, row, kl);
-        const int src = image_source(P, gc, row, kl, co);
+        int co;
+        i64 dst;
+        const int src = image_element(P, e, co, dst);
         const float v = src >= 0 ? (float)wq[(i64)co * w_ld + src] : 0.0f;
-        *reinterpret_cast<__nv_bfloat16 *>(wimg + image_offset(gc, row, kl, P.Npad)) = __float2bfloat16_rn(v);
+        *reinterpret_cast<__nv_bfloat16 *>(wimg + dst) = __float2bfloat16_rn(v);
     }
 }
 
 namespace {
 
+// Raises a kernel's dynamic shared-memory limit to `smem` on the current
+// device when the last value set there was lower.
+template <typename K>
+void ensure_smem(K kernel, size_t smem, int (&set)[64]) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || set[dev] >= (int)smem) return;
+    TRBA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    set[dev] = (int)smem;
+}
+
 template <int BN>
 void launch_bn(const Plan &p, const Args &a, int grid, cudaStream_t st) {
     using G = Geo<BN>;
     const size_t smem = 1024 + (size_t)a.stages * G::STAGE + sizeof(Ctl);
-    static bool attr[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        TRBA_CHECK(cudaFuncSetAttribute(dgrad_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr[dev] = true;
-    }
+    static int set[64] = {};
+    ensure_smem(dgrad_tc_kernel<BN>, smem, set);
     dgrad_tc_kernel<BN><<<grid, kThreads, smem, st>>>(p, a);
+    TRBA_LAUNCH_CHECK();
+}
+
+size_t halo_smem(const Plan &p) {
+    return 1024 + (size_t)p.h.sa * halo_a_stage(p.h) + (size_t)p.h.sb * halo_b_stage(p) + sizeof(HCtl);
+}
+
+template <int BN>
+void launch_halo(const Plan &p, const Args &a, int grid, cudaStream_t st) {
+    const size_t smem = halo_smem(p);
+    static int set[64] = {};
+    ensure_smem(dgrad_halo_kernel<BN>, smem, set);
+    dgrad_halo_kernel<BN><<<grid, kHThreads, smem, st>>>(p, a);
     TRBA_LAUNCH_CHECK();
 }
 
 int stages_for(int BN) {
     const size_t stage = 3 * kPartBytes + (size_t)BN * kRowBytes;
     return (int)std::min<size_t>(kMaxStages, kSmemBudget / stage);
+}
+
+}  // namespace
+
+namespace {
+
+std::atomic<int> g_tiling_mb{0}, g_tiling_kc{0};
+
+int halo_sms() {
+    const int n = sm_count();
+    return n > 0 ? n : 148;
+}
+
+// Cost model of one halo tile on one SM: tensor-core time at the sustained
+// bf16 rate (9.46 TFLOP/s per SM: 1.4 PFLOP/s over 148 SMs) against the
+// L2 -> shared-memory bytes of its halos and weight blocks at 45 bytes/ns
+// per SM; with two halo stages the two overlap, with one they add.
+struct HaloCost {
+    bool ok;
+    int R, sa, sb;
+    double tile_ns;
+};
+
+HaloCost halo_cost(const Plan &p, int mb, int KC) {
+    HaloCost c{};
+    const Halo &h = p.h;
+    const int ntaps = p.cls[0].ntaps;
+    const int dmax = p.pH * h.Wq + p.pW;
+    c.R = 128 * mb + dmax - h.dmin;
+    Halo t = h;
+    t.KC = KC, t.R = c.R;
+    const size_t a = halo_a_stage(t), b = (size_t)p.BN * KC * 2;
+    const size_t budget = kSmemBudget - sizeof(HCtl);
+    if (2u * mb * p.BN > 512 || (size_t)c.R * 16 >= (1u << 18)) return c;
+    if (2 * a + 3 * b <= budget) c.sa = 2;
+    else if (a + 3 * b <= budget) c.sa = 1;
+    else return c;
+    c.sb = (int)std::min<size_t>(kMaxBStages, (budget - c.sa * a) / b);
+    const int nchunks = p.Cout / KC;
+    const double mma = 3.0 * ntaps * p.Cout * 128.0 * mb * p.BN * 2.0 / 9460.0;
+    const double load = (double)nchunks * (a + (double)ntaps * b) / 45.0;
+    c.tile_ns = (c.sa == 2 ? std::max(mma, load) : mma + load) + 300.0;
+    c.ok = true;
+    return c;
+}
+
+// Halo geometry of a stride-1 plan (one class holding every tap) and its
+// channel chunk KC (fixed here: the weight image depends on it; the tile
+// height mb is chosen per batch).  Leaves p.halo = 0 when the conv does not
+// fit the tiling (Cout not a multiple of 16, padding >= kernel size, no KC
+// whose stages fit shared memory).
+void make_halo(Plan &p) {
+    if (p.Cout % 16 || p.pH < 0 || p.pW < 0 || p.pH >= p.kH || p.pW >= p.kW || p.ncls != 1) return;
+    Halo &h = p.h;
+    // gaps shared by neighbouring images / rows: reads above or left of the
+    // grid land in the previous slot's gap, reads below or right in this one's
+    h.Hq = p.Ho + std::max(0, std::max(p.kH - 1 - p.pH, p.H - p.Ho + p.pH));
+    h.Wq = p.Wo + std::max(0, std::max(p.kW - 1 - p.pW, p.W - p.Wo + p.pW));
+    h.dmin = (p.pH - p.kH + 1) * h.Wq + (p.pW - p.kW + 1);
+    const Class &C = p.cls[0];
+    for (int t = 0; t < C.ntaps; ++t) h.off[t] = (p.pH - C.kh[t]) * h.Wq + (p.pW - C.kw[t]) - h.dmin;
+    const int forced_mb = g_tiling_mb.load(), forced_kc = g_tiling_kc.load();
+    // largest KC first (fewer, larger stages); a smaller one must be clearly
+    // cheaper per position to win
+    int best_kc = 0;
+    double best = 0.0;
+    for (int KC = 64; KC >= 16; KC /= 2) {
+        if (p.Cout % KC || (forced_kc && KC != forced_kc)) continue;
+        if (!halo_cost(p, forced_mb > 0 ? forced_mb : 1, KC).ok) continue;
+        for (int mb = 1; mb <= 4; mb *= 2) {
+            if (forced_mb > 0 && mb != forced_mb) continue;
+            const HaloCost c = halo_cost(p, mb, KC);
+            if (!c.ok) continue;
+            const double per_pos = c.tile_ns / (128.0 * mb);
+            if (!best_kc || per_pos < 0.97 * best) best_kc = KC, best = per_pos;
+        }
+    }
+    if (!best_kc) return;
+    h.KC = best_kc;
+    h.nchunks = p.Cout / best_kc;
+    p.halo = 1;
 }
 
 }  // namespace
@@ -458,11 +894,42 @@ bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, 
             p.cls[p.ncls++] = C;
         }
     p.total_chunks = chunks;
-    return p.ncls > 0;
+    if (p.ncls == 0) return false;
+    if (sH == 1 && sW == 1 && g_tiling_mb.load() >= 0) make_halo(p);
+    return true;
+}
+
+void set_tiling_override(int mb, int kc) {
+    g_tiling_mb.store(mb == 1 || mb == 2 || mb == 4 || mb < 0 ? mb : 0);
+    g_tiling_kc.store(kc == 16 || kc == 32 || kc == 64 ? kc : 0);
 }
 
 void set_batch(Plan &p, int B) {
     p.B = B;
+    if (p.halo) {
+        Halo &h = p.h;
+        h.mpos = (i64)B * h.Hq * h.Wq;
+        const int forced = g_tiling_mb.load();
+        int best = 0;
+        double best_ns = 0.0;
+        for (int mb = 1; mb <= 4; mb *= 2) {
+            if (forced > 0 && mb != forced) continue;
+            const HaloCost c = halo_cost(p, mb, h.KC);
+            if (!c.ok) continue;
+            const i64 tiles = (h.mpos + 128 * mb - 1) / (128 * mb) * p.ntn;
+            const double ns = (double)((tiles + halo_sms() - 1) / halo_sms()) * c.tile_ns;
+            if (!best || ns < best_ns) best = mb, best_ns = ns;
+        }
+        if (!best) best = 1;  // make_plan checked that KC fits with one 128-row block
+        const HaloCost c = halo_cost(p, best, h.KC);
+        h.mb = best, h.R = c.R, h.sa = c.sa, h.sb = c.sb;
+        const i64 mtiles = (h.mpos + 128 * best - 1) / (128 * best);
+        p.cls[0].tile0 = 0;
+        p.cls[0].mtiles = (int)mtiles;
+        p.tiles = (int)(mtiles * p.ntn);
+        h.rows = (mtiles - 1) * 128 * best + h.R;
+        return;
+    }
     int t = 0;
     for (int c = 0; c < p.ncls; ++c) {
         Class &C = p.cls[c];
@@ -476,6 +943,15 @@ void set_batch(Plan &p, int B) {
 namespace {
 void launch_args(const Plan &p, const Args &a, cudaStream_t st) {
     const int grid = std::min(p.tiles, sm_count());
+    if (p.halo) {
+        switch (p.BN) {
+            case 16: launch_halo<16>(p, a, grid, st); break;
+            case 32: launch_halo<32>(p, a, grid, st); break;
+            case 64: launch_halo<64>(p, a, grid, st); break;
+            default: launch_halo<128>(p, a, grid, st); break;
+        }
+        return;
+    }
     switch (p.BN) {
         case 16: launch_bn<16>(p, a, grid, st); break;
         case 32: launch_bn<32>(p, a, grid, st); break;
@@ -491,8 +967,14 @@ void launch(const Plan &p, const uint8_t *wimg, uint16_t *planes, const float *d
     if (p.tiles <= 0) return;
     const int HoWo = p.Ho * p.Wo;
     const long long plane_elems = plane_elements(p);
-    split_nhwc_kernel<<<dim3((unsigned)((HoWo + 31) / 32), (unsigned)p.B), 256, 0, st>>>(dy, ws_co, p.Cout, HoWo,
-                                                                                      planes, plane_elems);
+    if (p.halo) {
+        const Halo &h = p.h;
+        split_halo_kernel<<<dim3((unsigned)((h.rows + 255) / 256), (unsigned)(p.Cout / 8)), 256, 0, st>>>(
+            dy, ws_co, p.Cout, p.Ho, p.Wo, h.Hq, h.Wq, (int)h.mpos, h.dmin, (int)h.rows, planes, plane_elems);
+    } else {
+        split_nhwc_kernel<<<dim3((unsigned)((HoWo + 31) / 32), (unsigned)p.B), 256, 0, st>>>(dy, ws_co, p.Cout,
+                                                                                          HoWo, planes, plane_elems);
+    }
     TRBA_LAUNCH_CHECK();
     Args a{};
     a.planes = planes, a.plane_elems = plane_elems, a.wimg = wimg, a.w_s = w_s, a.w_s_val = w_s_val;
@@ -564,7 +1046,7 @@ extern "C" int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *w
         buf = g_img[dev];
     }
     cudaStream_t st = as_stream(stream);
-    const long long n = (long long)p.total_chunks * p.Npad * dgtc::kChunk;
+    const long long n = dgtc::image_elements(p);
     dgtc::image_from_wq_kernel<<<grid_for(n), 256, 0, st>>>(p, weight_q, w_ld, buf);
     TRBA_LAUNCH_CHECK();
     const int before = trba_last_error();
@@ -576,15 +1058,19 @@ extern "C" int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *w
     return after != before ? (after ? after : -1) : 0;
 }
 
-// Bounded-wait self-test: one small input-gradient launch whose weight copies
-// are never issued, so the MMA warp's first wait for them (and then every
-// other role's) gives up after limit_ns; the kernel frees its tensor memory,
-// sets the error word and returns.  Returns the error word (1 expected) and
-// clears it; the context stays usable.
-extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) {
+// Bounded-wait self-test: small input-gradient launches of both tilings
+// (a stride-2 conv on the class tiling, a stride-1 conv on the halo tiling)
+// whose weight copies are never issued, so the MMA warp's first wait for them
+// (and then every other role's) gives up after limit_ns; each kernel frees
+// its tensor memory, sets the error word and returns.  Returns 1 when both
+// kernels reported the give-up (and clears the word); the context stays
+// usable.
+namespace {
+int wait_selftest_one(int stride, unsigned long long limit_ns, cudaStream_t st) {
     using namespace trba;
     dgtc::Plan p;
-    if (!dgtc::make_plan(16, 16, 8, 16, 3, 3, 1, 1, 1, 1, 8, 16, p)) return -1;
+    const int ho = stride == 1 ? 8 : 4, wo = stride == 1 ? 16 : 8;
+    if (!dgtc::make_plan(16, 16, 8, 16, 3, 3, stride, stride, 1, 1, ho, wo, p)) return -1;
     dgtc::set_batch(p, 2);
     // gi (2 x 16 x 8 x 16 floats), a zero weight image and zero dy planes
     const size_t n = 2 * 16 * 8 * 16;
@@ -593,7 +1079,6 @@ extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) 
     uint8_t *buf = nullptr;
     cudaError_t e = cudaMalloc(&buf, n * sizeof(float) + img + planes);
     if (e != cudaSuccess) return (int)e;
-    cudaStream_t st = as_stream(stream);
     TRBA_CHECK(cudaMemsetAsync(buf, 0, n * sizeof(float) + img + planes, st));
     dgtc::Args a{};
     a.gi = reinterpret_cast<float *>(buf);
@@ -610,4 +1095,45 @@ extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) 
     const int v = dgtc::error_poll(true);
     TRBA_CHECK(cudaFree(buf));
     return v;
+}
+}  // namespace
+
+extern "C" int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream) {
+    cudaStream_t st = trba::as_stream(stream);
+    const int a = wait_selftest_one(2, limit_ns, st);
+    const int b = wait_selftest_one(1, limit_ns, st);
+    return a == 1 && b == 1 ? 1 : (a != 1 ? a : b);
+}
+
+extern "C" void trba_tc_dgrad_tiling(int mb, int kc) { trba::dgtc::set_tiling_override(mb, kc); }
+
+// Host-side plan of the tensor-core input gradient for a conv at batch b,
+// for tests and tuning (no GPU work).  Writes up to n_out fields into out:
+//   [0] halo  [1] BN  [2] Npad  [3] ntn  [4] tiles  [5] ntaps
+//   halo plans only:
+//   [6] KC  [7] nchunks  [8] mb  [9] R  [10] sa  [11] sb  [12] Hq  [13] Wq
+//   [14] dmin  [15] mpos  [16] rows  [17] plane elements  [18] image bytes
+//   [19] shared-memory bytes  [20] TMEM columns
+//   [21 + 3 t .. 23 + 3 t] tap t: kh, kw, offset from the halo's first row
+// Returns the number of fields the plan has, or -1 when the conv is not served.
+extern "C" int trba_tc_dgrad_plan(int b, int cin, int h, int w, int cout, int kh, int kw, int sh, int sw, int ph,
+                                  int pw, int ho, int wo, long long *out, int n_out) {
+    using namespace trba::dgtc;
+    Plan p;
+    if (b <= 0 || !make_plan(cin, cout, h, w, kh, kw, sh, sw, ph, pw, ho, wo, p)) return -1;
+    set_batch(p, b);
+    const Class &C = p.cls[0];
+    long long f[21 + 3 * kMaxTaps] = {p.halo, p.BN, p.Npad, p.ntn, p.tiles, p.halo ? C.ntaps : 0};
+    int n = 6;
+    if (p.halo) {
+        const Halo &hh = p.h;
+        const long long v[] = {hh.KC,   hh.nchunks, hh.mb,          hh.R,
+                               hh.sa,   hh.sb,      hh.Hq,          hh.Wq,
+                               hh.dmin, hh.mpos,    hh.rows,        plane_elements(p),
+                               weight_image_bytes(p), (long long)halo_smem(p), (long long)halo_tmem_cols(p)};
+        for (long long x : v) f[n++] = x;
+        for (int t = 0; t < C.ntaps; ++t) f[n++] = C.kh[t], f[n++] = C.kw[t], f[n++] = hh.off[t];
+    }
+    for (int i = 0; i < n && i < n_out; ++i) out[i] = f[i];
+    return n;
 }

@@ -39,6 +39,28 @@ struct Class {
     int8_t kh[kMaxTaps], kw[kMaxTaps];
 };
 
+// Stride-1 convs use the halo tiling instead of the class tiling: the three
+// dy planes hold dy on a padded grid of Hq x Wq positions per image (real
+// values at rows < Ho and columns < Wo of each image's slot, zeros in the
+// gap rows and columns, which the neighbouring image and row share), so the
+// rows a kernel tap reads for a run of consecutive positions are the same
+// run shifted by the tap's offset (dh * Wq + dw).  A tile is 128 * mb
+// consecutive positions; one copy of its halo (128 * mb + dmax - dmin rows)
+// per KC output channels serves every tap.  Positions outside the input
+// grid (gap rows and columns) are computed and not stored.
+struct Halo {
+    int Hq, Wq;         // padded slot of one image
+    int mb;             // 128-row MMA blocks per tile (the tile has 128 * mb positions)
+    int KC;             // output channels (K) per halo stage: 16, 32 or 64
+    int nchunks;        // Cout / KC
+    int dmin;           // smallest tap offset (<= 0)
+    int R;              // halo rows per tile
+    int sa, sb;         // shared-memory stages of halos and of weight blocks
+    int off[kMaxTaps];  // tap offset from the halo's first row
+    long long mpos;     // B * Hq * Wq (batch dependent)
+    long long rows;     // rows of one plane slab, guards included (batch dependent)
+};
+
 struct Plan {
     int ncls;
     int Cin, Cout, H, W, Ho, Wo, kH, kW, sH, sW, pH, pW;
@@ -50,16 +72,29 @@ struct Plan {
     int B;             // batch of the launch
     int tiles;         // tiles of the launch (batch dependent)
     Class cls[kMaxClasses];
+    int halo;  // 1: halo tiling (stride 1, one class holding every tap)
+    Halo h;
 };
 
-// Builds the class plan of a conv, or returns false when the kernel does not
+// Builds the plan of a conv, or returns false when the kernel does not
 // serve it (Cout or a stride not a power of two, Cout < 8, more than 4
-// stride phases or 16 taps per phase).  Batch-dependent fields are filled by set_batch.
+// stride phases or 16 taps per phase).  Stride-1 convs with Cout a multiple
+// of 16 and padding below the kernel size get the halo tiling.
+// Batch-dependent fields are filled by set_batch.
 bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
                Plan &p);
 void set_batch(Plan &p, int B);
+// Tiling override for tests and tuning (process wide, read by make_plan):
+// mb < 0 keeps every conv on the class tiling; mb == 0 chooses the halo
+// tile by the cost model; mb in {1, 2, 4} forces 128 * mb positions per tile
+// and, when kc is 16, 32 or 64, KC output channels per halo stage.
+void set_tiling_override(int mb, int kc);
+// Elements (bf16) of the weight image of a plan.
+__host__ __device__ inline long long image_elements(const Plan &p) {
+    return p.halo ? (long long)p.Npad * p.Cout * p.cls[0].ntaps : (long long)p.total_chunks * p.Npad * kChunk;
+}
 // Bytes of the bf16 weight image of a plan.
-inline long long weight_image_bytes(const Plan &p) { return (long long)p.total_chunks * p.Npad * 128; }
+inline long long weight_image_bytes(const Plan &p) { return 2 * image_elements(p); }
 
 // Device-side writer of the weight image: element (chunk gc, row n, k of
 // the chunk) of the image of `p` holds bf16(wq[co, n, kh, kw]) for the tap
@@ -89,9 +124,43 @@ __device__ __forceinline__ int image_source(const Plan &p, int gc, int n, int kl
     return n * p.kH * p.kW + C.kh[tap] * p.kW + C.kw[tap];
 }
 
-// Elements of one bf16 plane of dy (NHWC, B x Ho x Wo x Cout); the launch
-// needs a scratch of 3 planes (6 bytes per dy element).
-inline long long plane_elements(const Plan &p) { return (long long)p.B * p.Ho * p.Wo * p.Cout; }
+// Element e (0 <= e < image_elements) of the weight image of either tiling:
+// its byte offset in the image (*dst), its output channel (*co) and its
+// source K index in the forward operand, or -1 for a zero entry.  The halo
+// image is blocks of [KC / 8][BN rows][8] bf16, one per (N tile, channel
+// chunk, tap) in that order: the no-swizzle K-major layout one bulk copy
+// places as a weight stage.
+__device__ __forceinline__ int image_element(const Plan &p, long long e, int &co, long long &dst) {
+    if (!p.halo) {
+        int gc, n, kl;
+        image_entry(p, e, gc, n, kl);
+        dst = image_offset(gc, n, kl, p.Npad);
+        return image_source(p, gc, n, kl, co);
+    }
+    dst = 2 * e;
+    const int j = (int)(e & 7);
+    long long q = e >> 3;
+    const int r = (int)(q % p.BN);
+    q /= p.BN;
+    const int nsl = p.h.KC >> 3;
+    const int s = (int)(q % nsl);
+    q /= nsl;
+    const Class &C = p.cls[0];
+    const int t = (int)(q % C.ntaps);
+    q /= C.ntaps;
+    const int c = (int)(q % p.h.nchunks);
+    const int nt = (int)(q / p.h.nchunks);
+    co = c * p.h.KC + s * 8 + j;
+    const int ci = nt * p.BN + r;
+    return ci < p.Cin ? ci * p.kH * p.kW + C.kh[t] * p.kW + C.kw[t] : -1;
+}
+
+// Elements of one bf16 plane of dy: NHWC, B x Ho x Wo x Cout for the class
+// tiling; [Cout / 8][h.rows][8] for the halo tiling.  The launch needs a
+// scratch of 3 planes.
+inline long long plane_elements(const Plan &p) {
+    return p.halo ? (long long)p.Cout * p.h.rows : (long long)p.B * p.Ho * p.Wo * p.Cout;
+}
 
 // gi (NCHW f32) from dy (NCHW f32) and the weight image: two launches (the
 // split of dy into three bf16 planes, in `planes`, then the tensor-core

@@ -396,10 +396,13 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                     if (!(ok = mbar_wait(&ctl->full[s], ph, abort))) break;
                     ctl->consumed = it + 1;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * G::A_BYTES), b0 = smem_u32(sB + s * G::B_BYTES);
+                    // the stage's base descriptors once, then compile-time K offsets
+                    // (one add per MMA: a descriptor rebuilt per MMA halves the issue rate)
+                    const uint64_t da = desc_k_sw128(smem_u32(sA + s * G::A_BYTES));
+                    const uint64_t db = desc_k_sw128(smem_u32(sB + s * G::B_BYTES));
 #pragma unroll
                     for (int k = 0; k < BK / UK; ++k)
-                        mma_i8(d, desc_k_sw128(a0 + k * UK), desc_k_sw128(b0 + k * UK), idesc,
+                        mma_i8(d, da + (uint64_t)((k * UK) >> 4), db + (uint64_t)((k * UK) >> 4), idesc,
                                (kb != kb0 || k != 0) ? 1u : 0u);
                     mma_commit(&ctl->empty[s]);
                 }
@@ -622,10 +625,11 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     if (!(ok = mbar_wait(&ctl->full[s], ph, abort))) break;
                     ctl->consumed = it + 1;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * G::A_BYTES), b0 = smem_u32(sB + s * G::B_BYTES);
+                    const uint64_t da = desc_k_sw128(smem_u32(sA + s * G::A_BYTES));
+                    const uint64_t db = desc_k_sw128(smem_u32(sB + s * G::B_BYTES));
 #pragma unroll
                     for (int k = 0; k < BK / UK; ++k)
-                        mma_i8_pair(d, desc_k_sw128(a0 + k * UK), desc_k_sw128(b0 + k * UK), idesc,
+                        mma_i8_pair(d, da + (uint64_t)((k * UK) >> 4), db + (uint64_t)((k * UK) >> 4), idesc,
                                     (kb != 0 || k != 0) ? 1u : 0u);
                     const uint32_t e_loc = smem_u32(&ctl->empty[s]);
                     mma_commit_pair(e_loc);

@@ -495,15 +495,14 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
     }
     if (t.wimg) {  // tensor-core input gradient: the bf16 weight image
         const dgtc::Plan &tp = *t.tc;
-        const i64 n_img = (i64)tp.total_chunks * tp.Npad * dgtc::kChunk;
+        const i64 n_img = dgtc::image_elements(tp);
         for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < n_img; e += (i64)gridDim.x * blockDim.x) {
-            int gc, n, kl, co;
-            dgtc::image_entry(tp, e, gc, n, kl);
-            const int src = dgtc::image_source(tp, gc, n, kl, co);
+            int co;
+            i64 dst;
+            const int src = dgtc::image_element(tp, e, co, dst);
             const float v =
                 src >= 0 ? (float)quant_w(P[s.off + (i64)co * t.K + src], pc ? wscale_of(wb[co]) : sc0) : 0.0f;
-            *reinterpret_cast<__nv_bfloat16 *>(t.wimg + dgtc::image_offset(gc, n, kl, tp.Npad)) =
-                __float2bfloat16_rn(v);
+            *reinterpret_cast<__nv_bfloat16 *>(t.wimg + dst) = __float2bfloat16_rn(v);
         }
     }
     if (!t.wT) return;
@@ -823,7 +822,11 @@ void allocate(trba_model *m) {
     {
         i64 planes = 0;  // scratch of the tensor-core input gradients, reused conv after conv (one stream)
         for (auto &L : m->convs)
-            if (L.tc_ok) planes = std::max(planes, 3 * (i64)B * L.cout * L.Ho * L.Wo);
+            if (L.tc_ok) {
+                dgtc::Plan p = L.tc;
+                dgtc::set_batch(p, B);
+                planes = std::max(planes, 3 * (i64)dgtc::plane_elements(p));
+            }
         if (planes) m->dg_planes = b.tp<uint16_t>(planes);
     }
     m->gemm_ws_elems = (i64)8 << 20;

@@ -170,6 +170,41 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory descriptor of a K-major operand without swizzle: 8 x 16-byte
+// core matrices, rows `sbo` bytes apart per group of 8 (128 when every row
+// follows the previous one at 16 bytes), the two 8-element K halves of one
+// K = 16 step `lbo` bytes apart.  The start needs 16-byte alignment only, so
+// a window may begin at any row.
+__device__ __forceinline__ uint64_t desc_k_interleave(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // descriptor version (sm_100); layout type 0: no swizzle
+    return d;
+}
+
+// The two 32-bit halves of a no-swizzle K-major descriptor (start address
+// 0): an MMA loop keeps `lo` of a stage's base and adds (byte offset >> 4)
+// for each K step or row block, a single integer add per instruction (the
+// start field has 14 bits: every shared-memory address fits, so the add
+// never carries into the LBO field).
+__host__ __device__ constexpr uint32_t desc_interleave_lo(uint32_t lbo) { return ((lbo >> 4) & 0x3FFFu) << 16; }
+__host__ __device__ constexpr uint32_t desc_interleave_hi(uint32_t sbo) { return ((sbo >> 4) & 0x3FFFu) | (1u << 14); }
+__device__ __forceinline__ uint64_t desc_join(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+
+// One lane of a converged warp (the lowest active), as CUTLASS's
+// elect_one_sync: the MMA warp runs its loop warp-wide (its descriptor
+// arithmetic stays warp-uniform) and the elected lane issues the
+// tcgen05 instructions.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\telect.sync rx|px, %1;\n\t@px mov.s32 %0, 1;\n\t}"
+                 : "+r"(pred)
+                 : "r"(0xffffffffu));
+    return pred != 0;
+}
+
 // Instruction descriptor: dense, K-major A and B, M x N tile.
 //   kind::i8 : D s32 (2), A/B signed int8 (1)
 //   kind::f16: D f32 (1), A/B bf16 (1)
