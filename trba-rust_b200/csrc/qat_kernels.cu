@@ -279,10 +279,12 @@ __global__ void se_forward_kernel(const float *pool, const float *w1, const floa
 //     s_dq = max(vmax / 127, 1e-12), vmax = max |gv * s_out| over the batch
 //     (accumulated by the gather that wrote gv);
 //   the squeeze sum over each plane of dz * y2 (f64), one warp per plane,
-//     kSeRows planes' reductions overlapped;
+//     kSeRows planes' reductions overlapped, kSeCols positions per lane
+//     loaded ahead;
 //   the excitation MLP backward (one warp per hidden unit, then one thread
 //     per channel) and dy2_full = dz * gate + dpooled / HW.
 constexpr int kSeRows = 4;
+constexpr int kSeCols = 4;
 
 __global__ void __launch_bounds__(256) se_backward_kernel(
     const float *__restrict__ gv, const float *__restrict__ s_out, const float *__restrict__ vmax,
@@ -302,19 +304,38 @@ __global__ void __launch_bounds__(256) se_backward_kernel(
     for (int c0 = warp; c0 < C; c0 += nwarps * kSeRows) {
         double acc[kSeRows];
 #pragma unroll
-        for (int u = 0; u < kSeRows; ++u) {
-            acc[u] = 0.0;
-            const int c = c0 + u * nwarps;
-            if (c < C) {
-                const i64 pb = base + (i64)c * HW;
-                for (int j = lane; j < HW; j += 32) {
-                    const float v = fmul(gv[pb + j], s);
-                    const int qd = rint_even(fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f));
-                    const float d = q_out[pb + j] > 0 ? fmul((float)qd, sdq) : 0.0f;
-                    dz[pb + j] = d;
-                    acc[u] += (double)fmul(d, y2[pb + j]);
+        for (int u = 0; u < kSeRows; ++u) acc[u] = 0.0;
+        // kSeRows planes x kSeCols positions per lane per pass: every load of
+        // the pass is issued before the first use, so the planes' loads are in
+        // flight together; each lane still adds its positions j = lane,
+        // lane + 32, ... in increasing order (the f64 sums are unchanged).
+        for (int j0 = lane; j0 < HW; j0 += 32 * kSeCols) {
+            float gvv[kSeRows][kSeCols], y2v[kSeRows][kSeCols];
+            int8_t qv[kSeRows][kSeCols];
+#pragma unroll
+            for (int u = 0; u < kSeRows; ++u)
+#pragma unroll
+                for (int t = 0; t < kSeCols; ++t) {
+                    const int c = c0 + u * nwarps, j = j0 + 32 * t;
+                    const bool ok = c < C && j < HW;
+                    const i64 e = base + (i64)c * HW + j;
+                    gvv[u][t] = ok ? gv[e] : 0.0f;
+                    y2v[u][t] = ok ? y2[e] : 0.0f;
+                    qv[u][t] = ok ? q_out[e] : (int8_t)0;
                 }
-            }
+#pragma unroll
+            for (int u = 0; u < kSeRows; ++u)
+#pragma unroll
+                for (int t = 0; t < kSeCols; ++t) {
+                    const int c = c0 + u * nwarps, j = j0 + 32 * t;
+                    if (c < C && j < HW) {
+                        const float v = fmul(gvv[u][t], s);
+                        const int qd = rint_even(fminf(fmaxf(fmul(v, inv), -127.0f), 127.0f));
+                        const float d = qv[u][t] > 0 ? fmul((float)qd, sdq) : 0.0f;
+                        dz[base + (i64)c * HW + j] = d;
+                        acc[u] += (double)fmul(d, y2v[u][t]);
+                    }
+                }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
@@ -356,15 +377,28 @@ __global__ void __launch_bounds__(256) se_backward_kernel(
     }
     __syncthreads();
     if ((HW & 3) == 0) {
-        const int hw4 = HW >> 2;
+        // four float4 per thread per pass, loaded before any is stored (dz and
+        // dy2_full are distinct buffers)
+        const int hw4 = HW >> 2, n4 = C * hw4;
         const float4 *z4 = reinterpret_cast<const float4 *>(dz + base);
         float4 *o4 = reinterpret_cast<float4 *>(dy2_full + base);
-        for (int e = threadIdx.x; e < C * hw4; e += blockDim.x) {
-            const int c = e / hw4;
-            const float g = s_gate[c], ad = s_add[c];
-            const float4 z = z4[e];
-            o4[e] = make_float4(fadd(fmul(z.x, g), ad), fadd(fmul(z.y, g), ad), fadd(fmul(z.z, g), ad),
-                                fadd(fmul(z.w, g), ad));
+        for (int e0 = threadIdx.x; e0 < n4; e0 += 4 * blockDim.x) {
+            float4 z[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int e = e0 + t * blockDim.x;
+                z[t] = e < n4 ? z4[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int e = e0 + t * blockDim.x;
+                if (e < n4) {
+                    const int c = e / hw4;
+                    const float g = s_gate[c], ad = s_add[c];
+                    o4[e] = make_float4(fadd(fmul(z[t].x, g), ad), fadd(fmul(z[t].y, g), ad),
+                                        fadd(fmul(z[t].z, g), ad), fadd(fmul(z[t].w, g), ad));
+                }
+            }
         }
     } else {
         for (int e = threadIdx.x; e < C * HW; e += blockDim.x) {
@@ -399,11 +433,100 @@ __global__ void se_wgrad_kernel(const float *dpre1, const float *dpre2, const fl
     }
 }
 
+// Warp-per-channel-group form of the per-plane BN backward passes (planes
+// of at most kWarpPlaneMaxHW elements): a warp takes the planes of channel c
+// of images b0 .. b0 + G - 1 (G = bn_group(HW)), walks their elements as one
+// list with kBnAhead loads of dy and x per lane in flight, and reduces once
+// for the whole group (one shuffle tree and one pair of atomics per G planes
+// instead of per plane).
+constexpr int kBnAhead = 4;
+__host__ __device__ inline int bn_group(int HW) {
+    const int g = (640 + HW - 1) / HW;
+    return g < 1 ? 1 : (g > 16 ? 16 : g);
+}
+struct BnGroup {
+    int c, b0, n;  // channel, first image, images in the group (0: idle warp)
+};
+__device__ __forceinline__ BnGroup bn_group_of(int B, int C, int G) {
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int per_c = (B + G - 1) / G;
+    BnGroup g;
+    g.c = gw % C;
+    g.b0 = (gw / C) * G;
+    g.n = gw < C * per_c ? min(G, B - g.b0) : 0;
+    return g;
+}
+// f(dy, x) over the group's elements, kBnAhead float4 (or scalars when HW is
+// not a multiple of 4) per lane loaded before any is used.
+template <typename F>
+__device__ __forceinline__ void bn_group_walk(const float *dy, const float *x, int C, int HW, const BnGroup &g,
+                                              int lane, F &&f) {
+    if (vec4_ok(HW)) {
+        const int n4 = HW >> 2, total = g.n * n4;
+        for (int e0 = lane; e0 < total; e0 += 32 * kBnAhead) {
+            float4 d[kBnAhead], xv[kBnAhead];
+#pragma unroll
+            for (int u = 0; u < kBnAhead; ++u) {
+                const int e = e0 + 32 * u;
+                if (e < total) {
+                    const int gi = e / n4, j4 = e - gi * n4;
+                    const i64 i = ((i64)(g.b0 + gi) * C + g.c) * HW + 4 * j4;
+                    d[u] = *reinterpret_cast<const float4 *>(dy + i);
+                    xv[u] = *reinterpret_cast<const float4 *>(x + i);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kBnAhead; ++u)
+                if (e0 + 32 * u < total) {
+                    f(d[u].x, xv[u].x);
+                    f(d[u].y, xv[u].y);
+                    f(d[u].z, xv[u].z);
+                    f(d[u].w, xv[u].w);
+                }
+        }
+    } else {
+        const int total = g.n * HW;
+        for (int e0 = lane; e0 < total; e0 += 32 * kBnAhead) {
+            float d[kBnAhead], xv[kBnAhead];
+#pragma unroll
+            for (int u = 0; u < kBnAhead; ++u) {
+                const int e = e0 + 32 * u;
+                if (e < total) {
+                    const int gi = e / HW, j = e - gi * HW;
+                    const i64 i = ((i64)(g.b0 + gi) * C + g.c) * HW + j;
+                    d[u] = dy[i];
+                    xv[u] = x[i];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kBnAhead; ++u)
+                if (e0 + 32 * u < total) f(d[u], xv[u]);
+        }
+    }
+}
+
 // later snapshot cpu_backend.cpp:782-802, one CTA per (b, c) plane, f64
 // partials added into acc[c] (sum dy) and acc[C + c] (sum dy*xhat).
 __global__ void bn_bwd_sums_kernel(const float *dy, const float *x, const float *mean, const float *var, int C,
                                    int HW, int nplanes, int warp_mode, double *acc) {
     __shared__ double smd[32];
+    if (warp_mode) {
+        const BnGroup g = bn_group_of(nplanes / C, C, bn_group(HW));
+        if (g.n == 0) return;
+        const float m = mean[g.c], r = bn_rstd(var[g.c]);
+        double s = 0.0, sx = 0.0;
+        bn_group_walk(dy, x, C, HW, g, threadIdx.x & 31, [&](float d, float xv) {
+            s += (double)d;
+            sx += (double)fmul(d, fmul(fsub(xv, m), r));
+        });
+        s = warp_sum_d(s);
+        sx = warp_sum_d(sx);
+        if ((threadIdx.x & 31) == 0) {
+            atomicAdd(acc + g.c, s);
+            atomicAdd(acc + C + g.c, sx);
+        }
+        return;
+    }
     const PlaneIdx q = plane_idx(nplanes, warp_mode);
     const int c = q.plane % C;
     const float m = mean[c], r = bn_rstd(var[c]);
@@ -459,6 +582,22 @@ __global__ void bn_dx_max_kernel(const float *dy, const float *x, const float *m
                                  const float *gamma, const double *acc, int B, int C, int HW, int nplanes,
                                  int warp_mode, float *g_gamma, float *g_beta, float *vmax) {
     __shared__ float smf[32];
+    if (warp_mode) {
+        const BnGroup g = bn_group_of(B, C, bn_group(HW));
+        float mx = 0.0f;
+        if (g.n > 0) {
+            const DxPlane p = dx_plane(mean, var, gamma, acc, C, g.c, (i64)B * HW);
+            if (g.b0 == 0 && (threadIdx.x & 31) == 0) {  // src/qnet.rs:974-982
+                g_beta[g.c] = fadd(g_beta[g.c], p.sdy);
+                g_gamma[g.c] = fadd(g_gamma[g.c], p.sdxh);
+            }
+            bn_group_walk(dy, x, C, HW, g, threadIdx.x & 31,
+                          [&](float d, float xv) { mx = fmaxf(mx, fabsf(dx_at(p, d, xv))); });
+        }
+        const float t = block_max_f(mx, smf);
+        if (threadIdx.x == 0) atomic_max_nonneg(vmax, t);
+        return;
+    }
     const PlaneIdx q = plane_idx(nplanes, warp_mode);
     const int b = q.plane / C, c = q.plane - b * C;
     const DxPlane p = dx_plane(mean, var, gamma, acc, C, c, (i64)B * HW);
@@ -941,10 +1080,21 @@ void se_weight_grads(const float *dpre1, const float *dpre2, const float *h1, co
     TRBA_LAUNCH_CHECK();
 }
 
+// Grid of the BN backward passes: warp mode launches one warp per (channel,
+// group of bn_group(HW) images).
+PlaneLaunch bn_launch(int B, int C, int HW) {
+    PlaneLaunch L = plane_launch((i64)B * C, HW);
+    if (L.warp_mode) {
+        const i64 warps = (i64)C * ((B + bn_group(HW) - 1) / bn_group(HW));
+        L.grid = (int)((warps + 7) / 8);
+    }
+    return L;
+}
+
 void bn_bwd_sums(const float *dy, const float *x, const float *mean, const float *var, int B, int C, int HW,
                  double *acc, cudaStream_t st) {
     const int np = B * C;
-    const PlaneLaunch L = plane_launch(np, HW);
+    const PlaneLaunch L = bn_launch(B, C, HW);
     bn_bwd_sums_kernel<<<L.grid, L.threads, 0, st>>>(dy, x, mean, var, C, HW, np, L.warp_mode, acc);
     TRBA_LAUNCH_CHECK();
 }
@@ -952,7 +1102,7 @@ void bn_bwd_sums(const float *dy, const float *x, const float *mean, const float
 void bn_dx_max(const float *dy, const float *x, const float *mean, const float *var, const float *gamma,
                const double *acc, int B, int C, int HW, float *g_gamma, float *g_beta, float *vmax, cudaStream_t st) {
     const int np = B * C;
-    const PlaneLaunch L = plane_launch(np, HW);
+    const PlaneLaunch L = bn_launch(B, C, HW);
     bn_dx_max_kernel<<<L.grid, L.threads, 0, st>>>(dy, x, mean, var, gamma, acc, B, C, HW, np, L.warp_mode, g_gamma,
                                                    g_beta, vmax);
     TRBA_LAUNCH_CHECK();

@@ -1440,8 +1440,16 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
         fill_f32_kernel<<<grid_for(n1), 256>>>(m->ones.get(), n1, 1.0f);
     }
     TRBA_CHECK(cudaEventCreateWithFlags(&m->ev, cudaEventDisableTiming));
-    TRBA_CHECK(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking));
-    TRBA_CHECK(cudaStreamCreateWithFlags(&m->gstream, cudaStreamNonBlocking));
+    {
+        // The replayed step's stream (the chain of input gradients is its
+        // critical path) at the highest priority, the weight-gradient stream
+        // at the lowest: when both have CTAs waiting, the critical chain's are
+        // placed first and the weight gradients fill the SMs it leaves free.
+        int least = 0, greatest = 0;
+        TRBA_CHECK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        TRBA_CHECK(cudaStreamCreateWithPriority(&m->side, cudaStreamNonBlocking, least));
+        TRBA_CHECK(cudaStreamCreateWithPriority(&m->gstream, cudaStreamNonBlocking, greatest));
+    }
     TRBA_CHECK(cudaMalloc(&m->probe.stamps, 2 * kProbeStamps * sizeof(unsigned long long)));
     TRBA_CHECK(cudaEventCreateWithFlags(&m->gfork, cudaEventDisableTiming));
     TRBA_CHECK(cudaEventCreateWithFlags(&m->gjoin, cudaEventDisableTiming));
