@@ -208,6 +208,9 @@ __global__ void __launch_bounds__(256) im2col_tile_kernel(const int8_t *__restri
             for (int i = 0; i < KH; ++i) okh[i] = (unsigned)(ih0 + i) < (unsigned)H;
 #pragma unroll
             for (int j = 0; j < KW; ++j) okw[j] = (unsigned)(iw0 + j) < (unsigned)W;
+            // four channels' gathers in flight per lane (the loop body's loads
+            // do not depend on the previous channel's shared-memory stores)
+#pragma unroll 4
             for (int c = warp; c < C; c += nwarps) {
                 const int8_t *src = in + base + c * hw;
                 uint8_t v[KH * KW];

@@ -284,9 +284,9 @@ __global__ void se_forward_kernel(const float *pool, const float *w1, const floa
 //   the excitation MLP backward (one warp per hidden unit, then one thread
 //     per channel) and dy2_full = dz * gate + dpooled / HW.
 constexpr int kSeRows = 4;
-constexpr int kSeCols = 4;
+constexpr int kSeCols = 2;
 
-__global__ void __launch_bounds__(256) se_backward_kernel(
+__global__ void __launch_bounds__(256, 4) se_backward_kernel(
     const float *__restrict__ gv, const float *__restrict__ s_out, const float *__restrict__ vmax,
     const int8_t *__restrict__ q_out, float *__restrict__ s_dq_out, float *dz,
     const float *__restrict__ y2, const float *__restrict__ gate, const float *__restrict__ h1,
@@ -768,27 +768,48 @@ __global__ void __launch_bounds__(256) bn_dx_quant_tr_kernel(const float *dy, co
     const i64 r0 = (i64)blockIdx.x * R;
     const int nrows = (int)min((i64)R, rows - r0);
     const int quads = (nrows + 3) >> 2;
-    for (int k = threadIdx.x; k < C * quads; k += blockDim.x) {
-        const int q4 = k / C, o = k - q4 * C;
-        uint32_t word = 0;
+    // two quads (eight rows) of one column per thread per pass: the sixteen
+    // loads of dy and x are issued before any is used
+    for (int k0 = threadIdx.x; k0 < C * quads; k0 += 2 * blockDim.x) {
+        float dv[2][4], xv[2][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int r = 4 * q4 + j;
-            if (r < nrows) {
-                const uint32_t i = (uint32_t)((r0 + r) * C + o);
-                const uint32_t plane = div_hw.div(i);
-                const int c = (int)(plane - div_c.div(plane) * (uint32_t)C);
-                DxPlane p;
-                p.m = chs[c];
-                p.r = chs[C + c];
-                p.a = chs[2 * C + c];
-                p.sdy = chs[3 * C + c];
-                p.sdxh = chs[4 * C + c];
-                p.cnt = cnt;
-                word |= (uint32_t)(uint8_t)quant_dx(dx_at(p, dy[i], x[i]), inv) << (8 * j);
+        for (int h = 0; h < 2; ++h) {
+            const int k = k0 + h * blockDim.x;
+            const int q4 = k / C, o = k - q4 * C;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = 4 * q4 + j;
+                const bool ok = k < C * quads && r < nrows;
+                const uint32_t i = ok ? (uint32_t)((r0 + r) * C + o) : 0u;
+                dv[h][j] = ok ? dy[i] : 0.0f;
+                xv[h][j] = ok ? x[i] : 0.0f;
             }
         }
-        tile[o * RW + q4] = word;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int k = k0 + h * blockDim.x;
+            if (k >= C * quads) break;
+            const int q4 = k / C, o = k - q4 * C;
+            uint32_t word = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = 4 * q4 + j;
+                if (r < nrows) {
+                    const uint32_t i = (uint32_t)((r0 + r) * C + o);
+                    const uint32_t plane = div_hw.div(i);
+                    const int c = (int)(plane - div_c.div(plane) * (uint32_t)C);
+                    DxPlane p;
+                    p.m = chs[c];
+                    p.r = chs[C + c];
+                    p.a = chs[2 * C + c];
+                    p.sdy = chs[3 * C + c];
+                    p.sdxh = chs[4 * C + c];
+                    p.cnt = cnt;
+                    word |= (uint32_t)(uint8_t)quant_dx(dx_at(p, dv[h][j], xv[h][j]), inv) << (8 * j);
+                }
+            }
+            tile[o * RW + q4] = word;
+        }
     }
     __syncthreads();
     if (nrows == R) {
