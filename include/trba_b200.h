@@ -92,7 +92,7 @@ int trba_tc_wait_selftest(unsigned long long limit_ns, void *stream);
 /* Tiling of the tensor-core input gradient for plans made after the call
  * (process wide; no counterpart in the reference, for tests and tuning):
  * mb < 0 keeps every conv on the class tiling, mb == 0 (the default) lets a
- * cost model pick the halo tile of stride-1 convs, mb = 1, 2 or 4 forces
+ * cost model pick the halo tile of stride-1 convs, mb = 1 .. 4 forces
  * 128 * mb positions per halo tile, and kc = 16, 32 or 64 forces the output
  * channels per halo stage (0: chosen). */
 void trba_tc_dgrad_tiling(int mb, int kc);

@@ -121,8 +121,8 @@ SHAPES = [
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "b{}_c{}_{}x{}_o{}_k{}x{}_p{}{}".format(*s))
-@pytest.mark.parametrize("tiling", [(0, 0), (1, 16), (2, 32), (4, 16), (1, 64)],
-                         ids=["auto", "mb1_kc16", "mb2_kc32", "mb4_kc16", "mb1_kc64"])
+@pytest.mark.parametrize("tiling", [(0, 0), (1, 16), (2, 32), (3, 32), (4, 16), (1, 64)],
+                         ids=["auto", "mb1_kc16", "mb2_kc32", "mb3_kc32", "mb4_kc16", "mb1_kc64"])
 def test_halo_plan_matches_oracle(shape, tiling, lib, oracle):
     B, cin, h, w, cout, kh, kw, ph, pw = shape
     ho, wo = h + 2 * ph - kh + 1, w + 2 * pw - kw + 1

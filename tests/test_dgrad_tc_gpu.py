@@ -63,7 +63,7 @@ def _out_hw(h, w, kh, kw, sh, sw, ph, pw):
 
 # Tilings: (0, 0) the default (halo tiling for stride-1 convs, chosen tile),
 # (-1, 0) every conv on the class tiling, then forced halo tiles.
-TILINGS = [(0, 0), (-1, 0), (1, 16), (2, 32), (4, 16), (1, 64)]
+TILINGS = [(0, 0), (-1, 0), (1, 16), (2, 32), (3, 32), (4, 16), (1, 64)]
 
 
 @pytest.fixture

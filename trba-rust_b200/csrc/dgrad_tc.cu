@@ -132,7 +132,7 @@ struct Geo {
     static constexpr int B_BYTES = BN * kRowBytes;
     static constexpr int STAGE = 3 * kPartBytes + B_BYTES;  // multiple of 1024
     static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr int CW = BN < 32 ? BN : 32;  // accumulator columns per tcgen05.ld
+    static constexpr int CW = 16;  // accumulator columns per tcgen05.ld (BN >= 16)
 };
 
 template <int CW>
@@ -150,25 +150,33 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[CW]) 
 // column 0 (NCHW, channel stride HW).
 template <int CW>
 __device__ __forceinline__ void epilogue_cols(const uint32_t (&v)[CW], bool any, float ws, const Args &a, i64 base,
-                                              i64 HW, int nvalid, bool rv, float gsc, float &gm) {
-    float av[CW];
-    bool keep[CW];
+                                              int HW, int nvalid, bool rv, float gsc, float &gm) {
+    // 16 columns per batch, addressed by 32-bit offsets from the row's base
+    // pointers (CW planes of one image fit an int offset)
+    float *gi = a.gi + base;
+    const float *add = a.add ? a.add + base : nullptr;
+    const int8_t *mq = a.mask_q ? a.mask_q + base : nullptr;
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-        const bool ok = rv && j < nvalid;
-        const i64 e = base + (i64)j * HW;
-        av[j] = (ok && a.add) ? a.add[e] : 0.0f;
-        keep[j] = (ok && a.mask_q) ? a.mask_q[e] > 0 : true;
-    }
+    for (int h = 0; h < CW; h += 16) {
+        constexpr int NB = CW < 16 ? CW : 16;
+        float av[NB];
+        bool keep[NB];
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-        if (rv && j < nvalid) {
-            const i64 e = base + (i64)j * HW;
-            float val = any ? fmul(__uint_as_float(v[j]), ws) : 0.0f;
-            if (a.mask_q) val = keep[j] ? val : 0.0f;
-            if (a.add) val = fadd(val, av[j]);
-            a.gi[e] = val;
-            gm = fmaxf(gm, fabsf(fmul(val, gsc)));
+        for (int j = 0; j < NB; ++j) {
+            const bool ok = rv && h + j < nvalid;
+            const int o = (h + j) * HW;
+            av[j] = (ok && add) ? add[o] : 0.0f;
+            keep[j] = (ok && mq) ? mq[o] > 0 : true;
+        }
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+            if (rv && h + j < nvalid) {
+                float val = any ? fmul(__uint_as_float(v[h + j]), ws) : 0.0f;
+                if (mq) val = keep[j] ? val : 0.0f;
+                if (add) val = fadd(val, av[j]);
+                gi[(h + j) * HW] = val;
+                gm = fmaxf(gm, fabsf(fmul(val, gsc)));
+            }
         }
     }
 }
@@ -402,7 +410,7 @@ __host__ __device__ inline uint32_t halo_a_stage(const Halo &h) { return (3u * (
 __host__ __device__ inline uint32_t halo_b_stage(const Plan &p) { return (uint32_t)p.BN * p.h.KC * 2; }
 __host__ __device__ inline uint32_t halo_tmem_cols(const Plan &p) {
     uint32_t c = 32;
-    while (c < 2u * p.h.mb * p.BN) c <<= 1;
+    while (c < (uint32_t)(p.h.nacc * p.h.mb * p.BN)) c <<= 1;
     return c;
 }
 
@@ -555,11 +563,11 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
                     switch (kind) {
 #define TRBA_HALO_TAP(KC_, MB_)                                                          \
     case KC_ * 8 + MB_:                                                                  \
-        if constexpr (2 * MB_ * BN <= 512) halo_tap_mmas<BN, KC_, MB_>(d, al, bl, hi, R, idesc, first); \
+        if constexpr (MB_ * BN <= 384) halo_tap_mmas<BN, KC_, MB_>(d, al, bl, hi, R, idesc, first); \
         break;
-                        TRBA_HALO_TAP(16, 1) TRBA_HALO_TAP(16, 2) TRBA_HALO_TAP(16, 4)
-                        TRBA_HALO_TAP(32, 1) TRBA_HALO_TAP(32, 2) TRBA_HALO_TAP(32, 4)
-                        TRBA_HALO_TAP(64, 1) TRBA_HALO_TAP(64, 2) TRBA_HALO_TAP(64, 4)
+                        TRBA_HALO_TAP(16, 1) TRBA_HALO_TAP(16, 2) TRBA_HALO_TAP(16, 3) TRBA_HALO_TAP(16, 4)
+                        TRBA_HALO_TAP(32, 1) TRBA_HALO_TAP(32, 2) TRBA_HALO_TAP(32, 3) TRBA_HALO_TAP(32, 4)
+                        TRBA_HALO_TAP(64, 1) TRBA_HALO_TAP(64, 2) TRBA_HALO_TAP(64, 3) TRBA_HALO_TAP(64, 4)
 #undef TRBA_HALO_TAP
                         default: break;
                     }
@@ -574,8 +582,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             if (!ok) break;
             if (elect_one()) mma_commit(&ctl->tfull[acc]);
             __syncwarp();
-            acc ^= 1u;
-            if (acc == 0) acc_ph ^= 1u;
+            if (++acc == (uint32_t)h.nacc) acc = 0, acc_ph ^= 1u;
         }
         if (elect_one()) mma_commit(&ctl->drained);
         __syncwarp();
@@ -584,7 +591,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
         __syncwarp();
     } else {
         // ------------------------------------------------ epilogue
-        constexpr int CW = BN < 32 ? BN : 32;
+        constexpr int CW = 16;  // accumulator columns per tcgen05.ld (BN >= 16)
         const int q = warp & 3;  // TMEM lane quarter this warp may read
         const float ws = a.w_s ? *a.w_s : a.w_s_val;
         const float gsc = a.gmax_out ? *a.gmax_scale : 0.0f;
@@ -613,8 +620,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             }
             tc_fence_before();
             mbar_arrive(&ctl->tempty[acc]);
-            acc ^= 1u;
-            if (acc == 0) acc_ph ^= 1u;
+            if (++acc == (uint32_t)h.nacc) acc = 0, acc_ph ^= 1u;
         }
         if (a.gmax_out) {
 #pragma unroll
@@ -781,44 +787,53 @@ int halo_sms() {
     return n > 0 ? n : 148;
 }
 
-// Cost model of one halo tile on one SM: tensor-core time at the sustained
-// bf16 rate (9.46 TFLOP/s per SM: 1.4 PFLOP/s over 148 SMs) against the
-// L2 -> shared-memory bytes of its halos and weight blocks at 45 bytes/ns
-// per SM; with two halo stages the two overlap, with one they add.
-struct HaloCost {
+// Shared-memory and TMEM fit of a halo tile of 128 * mb positions with KC
+// channels per halo stage: halo rows R, stages (two halo stages when they
+// fit with at least three weight stages, else one), accumulators (two when
+// 2 x mb x BN columns fit TMEM).
+struct HaloFit {
     bool ok;
-    int R, sa, sb;
-    double tile_ns;
+    int R, sa, sb, nacc;
 };
 
-HaloCost halo_cost(const Plan &p, int mb, int KC) {
-    HaloCost c{};
+HaloFit halo_fit(const Plan &p, int mb, int KC) {
+    HaloFit c{};
     const Halo &h = p.h;
-    const int ntaps = p.cls[0].ntaps;
     const int dmax = p.pH * h.Wq + p.pW;
     c.R = 128 * mb + dmax - h.dmin;
     Halo t = h;
     t.KC = KC, t.R = c.R;
     const size_t a = halo_a_stage(t), b = (size_t)p.BN * KC * 2;
     const size_t budget = kSmemBudget - sizeof(HCtl);
-    if (2u * mb * p.BN > 512 || (size_t)c.R * 16 >= (1u << 18)) return c;
+    c.nacc = 2 * mb * p.BN <= 512 ? 2 : 1;
+    if (mb * p.BN > 384 || (size_t)c.R * 16 >= (1u << 18)) return c;
     if (2 * a + 3 * b <= budget) c.sa = 2;
     else if (a + 3 * b <= budget) c.sa = 1;
     else return c;
     c.sb = (int)std::min<size_t>(kMaxBStages, (budget - c.sa * a) / b);
-    const int nchunks = p.Cout / KC;
-    const double mma = 3.0 * ntaps * p.Cout * 128.0 * mb * p.BN * 2.0 / 9460.0;
-    const double load = (double)nchunks * (a + (double)ntaps * b) / 45.0;
-    c.tile_ns = (c.sa == 2 ? std::max(mma, load) : mma + load) + 300.0;
     c.ok = true;
     return c;
 }
 
+// Preferred tile height: the smallest mb whose halo adds at most half a tile
+// of rows (dmax - dmin <= 64 mb), else 4 (wide planes: the stem).  Measured
+// on the model's convs at batch 512, taller tiles only pay where the halo
+// is large: they halve the tile count (wave quantisation) without saving
+// weight traffic that limits the kernel.
+int halo_mb_pref(const Plan &p) {
+    const int extra = p.pH * p.h.Wq + p.pW - p.h.dmin;
+    for (int mb = 1; mb < 4; ++mb)
+        if (extra <= 64 * mb) return mb;
+    return 4;
+}
+
 // Halo geometry of a stride-1 plan (one class holding every tap) and its
 // channel chunk KC (fixed here: the weight image depends on it; the tile
-// height mb is chosen per batch).  Leaves p.halo = 0 when the conv does not
-// fit the tiling (Cout not a multiple of 16, padding >= kernel size, no KC
-// whose stages fit shared memory).
+// height is set per batch): the largest KC (fewer, larger stages) whose
+// stages fit two halo buffers at the preferred height, else the largest that
+// fits at all, trying lower heights last.  Leaves p.halo = 0 when the conv
+// does not fit the tiling (Cout not a multiple of 16, padding >= kernel
+// size, no fitting KC).
 void make_halo(Plan &p) {
     if (p.Cout % 16 || p.pH < 0 || p.pW < 0 || p.pH >= p.kH || p.pW >= p.kW || p.ncls != 1) return;
     Halo &h = p.h;
@@ -830,24 +845,18 @@ void make_halo(Plan &p) {
     const Class &C = p.cls[0];
     for (int t = 0; t < C.ntaps; ++t) h.off[t] = (p.pH - C.kh[t]) * h.Wq + (p.pW - C.kw[t]) - h.dmin;
     const int forced_mb = g_tiling_mb.load(), forced_kc = g_tiling_kc.load();
-    // largest KC first (fewer, larger stages); a smaller one must be clearly
-    // cheaper per position to win
-    int best_kc = 0;
-    double best = 0.0;
-    for (int KC = 64; KC >= 16; KC /= 2) {
-        if (p.Cout % KC || (forced_kc && KC != forced_kc)) continue;
-        if (!halo_cost(p, forced_mb > 0 ? forced_mb : 1, KC).ok) continue;
-        for (int mb = 1; mb <= 4; mb *= 2) {
-            if (forced_mb > 0 && mb != forced_mb) continue;
-            const HaloCost c = halo_cost(p, mb, KC);
-            if (!c.ok) continue;
-            const double per_pos = c.tile_ns / (128.0 * mb);
-            if (!best_kc || per_pos < 0.97 * best) best_kc = KC, best = per_pos;
-        }
-    }
-    if (!best_kc) return;
-    h.KC = best_kc;
-    h.nchunks = p.Cout / best_kc;
+    const int mb0 = forced_mb > 0 ? forced_mb : halo_mb_pref(p);
+    int kc = 0;
+    for (int pass = 0; pass < 2 && !kc; ++pass)  // pass 0: two halo stages; pass 1: any fit
+        for (int mb = mb0; mb >= (forced_mb > 0 ? mb0 : 1) && !kc; --mb)
+            for (int KC = 64; KC >= 16 && !kc; KC /= 2) {
+                if (p.Cout % KC || (forced_kc && KC != forced_kc)) continue;
+                const HaloFit f = halo_fit(p, mb, KC);
+                if (f.ok && (pass == 1 || f.sa == 2)) kc = KC;
+            }
+    if (!kc) return;
+    h.KC = kc;
+    h.nchunks = p.Cout / kc;
     p.halo = 1;
 }
 
@@ -900,7 +909,7 @@ bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, 
 }
 
 void set_tiling_override(int mb, int kc) {
-    g_tiling_mb.store(mb == 1 || mb == 2 || mb == 4 || mb < 0 ? mb : 0);
+    g_tiling_mb.store((mb >= 1 && mb <= 4) || mb < 0 ? mb : 0);
     g_tiling_kc.store(kc == 16 || kc == 32 || kc == 64 ? kc : 0);
 }
 
@@ -910,19 +919,14 @@ void set_batch(Plan &p, int B) {
         Halo &h = p.h;
         h.mpos = (i64)B * h.Hq * h.Wq;
         const int forced = g_tiling_mb.load();
-        int best = 0;
-        double best_ns = 0.0;
-        for (int mb = 1; mb <= 4; mb *= 2) {
-            if (forced > 0 && mb != forced) continue;
-            const HaloCost c = halo_cost(p, mb, h.KC);
-            if (!c.ok) continue;
-            const i64 tiles = (h.mpos + 128 * mb - 1) / (128 * mb) * p.ntn;
-            const double ns = (double)((tiles + halo_sms() - 1) / halo_sms()) * c.tile_ns;
-            if (!best || ns < best_ns) best = mb, best_ns = ns;
-        }
-        if (!best) best = 1;  // make_plan checked that KC fits with one 128-row block
-        const HaloCost c = halo_cost(p, best, h.KC);
-        h.mb = best, h.R = c.R, h.sa = c.sa, h.sb = c.sb;
+        // the preferred height (or the forced one), lowered while the KC of the
+        // plan does not fit it or while it would leave SMs without a tile
+        int best = forced > 0 ? forced : halo_mb_pref(p);
+        while (best > 1 && (!halo_fit(p, best, h.KC).ok ||
+                            (forced <= 0 && (h.mpos + 128 * best - 1) / (128 * best) * p.ntn < halo_sms())))
+            --best;
+        const HaloFit c = halo_fit(p, best, h.KC);
+        h.mb = best, h.R = c.R, h.sa = c.sa, h.sb = c.sb, h.nacc = c.nacc;
         const i64 mtiles = (h.mpos + 128 * best - 1) / (128 * best);
         p.cls[0].tile0 = 0;
         p.cls[0].mtiles = (int)mtiles;

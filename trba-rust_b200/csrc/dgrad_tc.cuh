@@ -56,6 +56,7 @@ struct Halo {
     int dmin;           // smallest tap offset (<= 0)
     int R;              // halo rows per tile
     int sa, sb;         // shared-memory stages of halos and of weight blocks
+    int nacc;           // TMEM accumulators (2: double-buffered, 1 when 2 x mb x BN columns do not fit)
     int off[kMaxTaps];  // tap offset from the halo's first row
     long long mpos;     // B * Hq * Wq (batch dependent)
     long long rows;     // rows of one plane slab, guards included (batch dependent)
@@ -86,7 +87,7 @@ bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, 
 void set_batch(Plan &p, int B);
 // Tiling override for tests and tuning (process wide, read by make_plan):
 // mb < 0 keeps every conv on the class tiling; mb == 0 chooses the halo
-// tile by the cost model; mb in {1, 2, 4} forces 128 * mb positions per tile
+// tile by the cost model; mb in 1..4 forces 128 * mb positions per tile
 // and, when kc is 16, 32 or 64, KC output channels per halo stage.
 void set_tiling_override(int mb, int kc);
 // Elements (bf16) of the weight image of a plan.
