@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const Halo &h = P.h;
-    const int nsl = h.KC >> 3, ntaps = P.cls[0].ntaps, MT = 128 * h.mb;
+    const int nsl = h.KC >> 3, MT = 128 * h.mb;
     const uint32_t slab = (uint32_t)h.R * 16, a_stage = halo_a_stage(h), b_stage = halo_b_stage(P);
     uint8_t *As = smem;
     uint8_t *Bs = smem + (size_t)h.sa * a_stage;
@@ -481,7 +481,9 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
         uint32_t ia = 0;
         bool run = true;
         for (int t = blockIdx.x; t < P.tiles && run; t += gridDim.x) {
-            const i64 row0 = (i64)(t / P.ntn) * MT;  // plane row of the halo's first row
+            const Class &C = P.cls[tile_class(P, t)];
+            if (C.ntaps == 0) continue;  // a phase without taps: the epilogue alone writes it
+            const i64 row0 = (i64)((t - C.tile0) / P.ntn) * MT;  // plane row of the halo's first row
             for (int c = 0; c < h.nchunks; ++c, ++ia) {
                 const int s = ia % h.sa;
                 const uint32_t ph = (ia / h.sa) & 1u;
@@ -510,7 +512,8 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             uint32_t ib = 0;
             bool run = true;
             for (int t = blockIdx.x; t < P.tiles && run; t += gridDim.x) {
-                const int nt = t % P.ntn;
+                const Class &C = P.cls[tile_class(P, t)];
+                const int nt = (t - C.tile0) % P.ntn, ntaps = C.ntaps;
                 for (int c = 0; c < h.nchunks && run; ++c)
                     for (int tap = 0; tap < ntaps; ++tap, ++ib) {
                         const int s = ib % h.sb;
@@ -522,8 +525,8 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
                         if (a.skip_weights) continue;
                         mbar_expect_tx(&ctl->bfull[s], b_stage);
                         bulk_load(Bs + (size_t)s * b_stage,
-                                  a.wimg + ((i64)(nt * h.nchunks + c) * ntaps + tap) * b_stage, b_stage,
-                                  &ctl->bfull[s]);
+                                  a.wimg + ((i64)C.b_off + (i64)(nt * h.nchunks + c) * ntaps + tap) * b_stage,
+                                  b_stage, &ctl->bfull[s]);
                         ctl->b_issued = ib + 1;
                     }
             }
@@ -544,8 +547,10 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             ok = __all_sync(0xffffffffu, mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort, a.wait_ns));
             if (!ok) break;
             tc_fence_after();
+            const int k = tile_class(P, t);
+            const int ntaps = P.cls[k].ntaps;
             const uint32_t d = tbase + acc * h.mb * BN;
-            for (int c = 0; c < h.nchunks && ok; ++c, ++ia) {
+            for (int c = 0; c < h.nchunks && ntaps > 0 && ok; ++c, ++ia) {
                 const int sa = ia % h.sa;
                 ok = __all_sync(0xffffffffu, mbar_wait(&ctl->afull[sa], (ia / h.sa) & 1u, abort, a.wait_ns));
                 if (!ok) break;
@@ -558,7 +563,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
                     if (!ok) break;
                     ctl->b_consumed = ib + 1;
                     tc_fence_after();
-                    const uint32_t al = a_lo + (uint32_t)h.off[tap], bl = b_lo0 + sb * b_step;
+                    const uint32_t al = a_lo + (uint32_t)h.off[k][tap], bl = b_lo0 + sb * b_step;
                     const bool first = (c | tap) == 0;
                     switch (kind) {
 #define TRBA_HALO_TAP(KC_, MB_)                                                          \
@@ -599,23 +604,29 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
         float gm = 0.0f;
         uint32_t acc = 0, acc_ph = 0;
         for (int t = blockIdx.x; t < P.tiles; t += gridDim.x) {
-            const int mt = t / P.ntn, n0 = (t - mt * P.ntn) * BN;
+            const Class &C = P.cls[tile_class(P, t)];
+            const int local = t - C.tile0, mt = local / P.ntn, n0 = (local - mt * P.ntn) * BN;
+            const bool any = C.ntaps > 0;
             const bool ok = mbar_wait_sleep(&ctl->tfull[acc], acc_ph, abort, a.wait_ns, 256);
             __syncwarp();  // reconverge before the warp-collective tcgen05.ld
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
             for (int i = 0; i < h.mb; ++i) {
+                // position (b, i, j) of the class grid -> pixel (py + sH i, px + sW j)
                 const i64 pos = (i64)mt * MT + i * 128 + q * 32 + lane;
                 const int b = (int)(pos / HqWq), rem = (int)(pos - (i64)b * HqWq);
-                const int y = rem / h.Wq, x = rem - y * h.Wq;
-                const bool rv = pos < h.mpos && y < P.H && x < P.W;
+                const int ci = rem / h.Wq, cj = rem - ci * h.Wq;
+                const bool rv = pos < h.mpos && ci < C.Hc && cj < C.Wc;
+                const int y = C.py + (ci << P.lgSH), x = C.px + (cj << P.lgSW);
                 const i64 base = ((i64)b * P.Cin + n0) * HW + (i64)y * P.W + x;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN && n0 + c0 < P.Cin; c0 += CW) {
                     uint32_t v[CW];
-                    tmem_ld_cols<CW>(tbase + ((uint32_t)(q * 32) << 16) + (acc * h.mb + i) * BN + c0, v);
-                    tmem_ld_wait();
-                    epilogue_cols<CW>(v, true, ws, a, base + (i64)c0 * HW, HW, P.Cin - n0 - c0, rv, gsc, gm);
+                    if (any) {
+                        tmem_ld_cols<CW>(tbase + ((uint32_t)(q * 32) << 16) + (acc * h.mb + i) * BN + c0, v);
+                        tmem_ld_wait();
+                    }
+                    epilogue_cols<CW>(v, any, ws, a, base + (i64)c0 * HW, HW, P.Cin - n0 - c0, rv, gsc, gm);
                 }
             }
             tc_fence_before();
@@ -799,8 +810,7 @@ struct HaloFit {
 HaloFit halo_fit(const Plan &p, int mb, int KC) {
     HaloFit c{};
     const Halo &h = p.h;
-    const int dmax = p.pH * h.Wq + p.pW;
-    c.R = 128 * mb + dmax - h.dmin;
+    c.R = 128 * mb + h.dmax - h.dmin;
     Halo t = h;
     t.KC = KC, t.R = c.R;
     const size_t a = halo_a_stage(t), b = (size_t)p.BN * KC * 2;
@@ -821,29 +831,51 @@ HaloFit halo_fit(const Plan &p, int mb, int KC) {
 // is large: they halve the tile count (wave quantisation) without saving
 // weight traffic that limits the kernel.
 int halo_mb_pref(const Plan &p) {
-    const int extra = p.pH * p.h.Wq + p.pW - p.h.dmin;
+    const int extra = p.h.dmax - p.h.dmin;
     for (int mb = 1; mb < 4; ++mb)
         if (extra <= 64 * mb) return mb;
     return 4;
 }
 
-// Halo geometry of a stride-1 plan (one class holding every tap) and its
-// channel chunk KC (fixed here: the weight image depends on it; the tile
-// height is set per batch): the largest KC (fewer, larger stages) whose
-// stages fit two halo buffers at the preferred height, else the largest that
-// fits at all, trying lower heights last.  Leaves p.halo = 0 when the conv
-// does not fit the tiling (Cout not a multiple of 16, padding >= kernel
-// size, no fitting KC).
+// Halo geometry of a plan and its channel chunk KC (fixed here: the weight
+// image depends on it; the tile height is set per batch): the largest KC
+// (fewer, larger stages) whose stages fit two halo buffers at the preferred
+// height, else the largest that fits at all, trying lower heights last.
+// The padded slot (Hq, Wq) holds every row and column a class reads: reads
+// above / left of the grid land in the previous slot's gap, reads below /
+// right in this one's.  Leaves p.halo = 0 when the conv does not fit the
+// tiling (Cout not a multiple of 16, padding >= kernel size, no fitting KC).
 void make_halo(Plan &p) {
-    if (p.Cout % 16 || p.pH < 0 || p.pW < 0 || p.pH >= p.kH || p.pW >= p.kW || p.ncls != 1) return;
+    if (p.Cout % 16 || p.pH < 0 || p.pW < 0 || p.pH >= p.kH || p.pW >= p.kW) return;
     Halo &h = p.h;
-    // gaps shared by neighbouring images / rows: reads above or left of the
-    // grid land in the previous slot's gap, reads below or right in this one's
-    h.Hq = p.Ho + std::max(0, std::max(p.kH - 1 - p.pH, p.H - p.Ho + p.pH));
-    h.Wq = p.Wo + std::max(0, std::max(p.kW - 1 - p.pW, p.W - p.Wo + p.pW));
-    h.dmin = (p.pH - p.kH + 1) * h.Wq + (p.pW - p.kW + 1);
-    const Class &C = p.cls[0];
-    for (int t = 0; t < C.ntaps; ++t) h.off[t] = (p.pH - C.kh[t]) * h.Wq + (p.pW - C.kw[t]) - h.dmin;
+    int dh_lo = 0, dw_lo = 0, hq = p.Ho, wq = p.Wo;
+    for (int k = 0; k < p.ncls; ++k) {
+        const Class &C = p.cls[k];
+        hq = std::max(hq, C.Hc);
+        wq = std::max(wq, C.Wc);
+        for (int t = 0; t < C.ntaps; ++t) {
+            const int dh = (C.py + p.pH - C.kh[t]) / p.sH, dw = (C.px + p.pW - C.kw[t]) / p.sW;  // exact
+            dh_lo = std::min(dh_lo, dh), dw_lo = std::min(dw_lo, dw);
+            hq = std::max(hq, C.Hc + dh), wq = std::max(wq, C.Wc + dw);
+        }
+    }
+    h.Hq = std::max(hq, p.Ho - dh_lo);
+    h.Wq = std::max(wq, p.Wo - dw_lo);
+    h.dmin = h.dmax = 0;
+    h.taps = 0;
+    for (int k = 0; k < p.ncls; ++k) {
+        const Class &C = p.cls[k];
+        for (int t = 0; t < C.ntaps; ++t) {
+            const int o = (C.py + p.pH - C.kh[t]) / p.sH * h.Wq + (C.px + p.pW - C.kw[t]) / p.sW;
+            h.dmin = std::min(h.dmin, o), h.dmax = std::max(h.dmax, o);
+        }
+        h.taps += C.ntaps;
+    }
+    for (int k = 0; k < p.ncls; ++k) {
+        const Class &C = p.cls[k];
+        for (int t = 0; t < C.ntaps; ++t)
+            h.off[k][t] = (C.py + p.pH - C.kh[t]) / p.sH * h.Wq + (C.px + p.pW - C.kw[t]) / p.sW - h.dmin;
+    }
     const int forced_mb = g_tiling_mb.load(), forced_kc = g_tiling_kc.load();
     const int mb0 = forced_mb > 0 ? forced_mb : halo_mb_pref(p);
     int kc = 0;
@@ -857,6 +889,11 @@ void make_halo(Plan &p) {
     if (!kc) return;
     h.KC = kc;
     h.nchunks = p.Cout / kc;
+    int blocks = 0;  // weight blocks: (class, N tile, chunk, tap)
+    for (int k = 0; k < p.ncls; ++k) {
+        p.cls[k].b_off = blocks;
+        blocks += p.ntn * h.nchunks * p.cls[k].ntaps;
+    }
     p.halo = 1;
 }
 
@@ -904,7 +941,7 @@ bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, 
         }
     p.total_chunks = chunks;
     if (p.ncls == 0) return false;
-    if (sH == 1 && sW == 1 && g_tiling_mb.load() >= 0) make_halo(p);
+    if (g_tiling_mb.load() >= 0) make_halo(p);
     return true;
 }
 
@@ -922,15 +959,18 @@ void set_batch(Plan &p, int B) {
         // the preferred height (or the forced one), lowered while the KC of the
         // plan does not fit it or while it would leave SMs without a tile
         int best = forced > 0 ? forced : halo_mb_pref(p);
-        while (best > 1 && (!halo_fit(p, best, h.KC).ok ||
-                            (forced <= 0 && (h.mpos + 128 * best - 1) / (128 * best) * p.ntn < halo_sms())))
+        while (best > 1 &&
+               (!halo_fit(p, best, h.KC).ok ||
+                (forced <= 0 && (h.mpos + 128 * best - 1) / (128 * best) * p.ntn * p.ncls < halo_sms())))
             --best;
         const HaloFit c = halo_fit(p, best, h.KC);
         h.mb = best, h.R = c.R, h.sa = c.sa, h.sb = c.sb, h.nacc = c.nacc;
         const i64 mtiles = (h.mpos + 128 * best - 1) / (128 * best);
-        p.cls[0].tile0 = 0;
-        p.cls[0].mtiles = (int)mtiles;
-        p.tiles = (int)(mtiles * p.ntn);
+        for (int k = 0; k < p.ncls; ++k) {  // every class covers the whole padded grid
+            p.cls[k].tile0 = (int)(k * mtiles * p.ntn);
+            p.cls[k].mtiles = (int)mtiles;
+        }
+        p.tiles = (int)(p.ncls * mtiles * p.ntn);
         h.rows = (mtiles - 1) * 128 * best + h.R;
         return;
     }
@@ -1113,12 +1153,13 @@ extern "C" void trba_tc_dgrad_tiling(int mb, int kc) { trba::dgtc::set_tiling_ov
 
 // Host-side plan of the tensor-core input gradient for a conv at batch b,
 // for tests and tuning (no GPU work).  Writes up to n_out fields into out:
-//   [0] halo  [1] BN  [2] Npad  [3] ntn  [4] tiles  [5] ntaps
+//   [0] halo  [1] BN  [2] Npad  [3] ntn  [4] tiles  [5] taps of all classes
 //   halo plans only:
 //   [6] KC  [7] nchunks  [8] mb  [9] R  [10] sa  [11] sb  [12] Hq  [13] Wq
 //   [14] dmin  [15] mpos  [16] rows  [17] plane elements  [18] image bytes
-//   [19] shared-memory bytes  [20] TMEM columns
-//   [21 + 3 t .. 23 + 3 t] tap t: kh, kw, offset from the halo's first row
+//   [19] shared-memory bytes  [20] TMEM columns  [21] classes, then per
+//   class: py, px, Hc, Wc, ntaps, tile0, mtiles, first weight block, and
+//   per tap kh, kw, offset from the halo's first row
 // Returns the number of fields the plan has, or -1 when the conv is not served.
 extern "C" int trba_tc_dgrad_plan(int b, int cin, int h, int w, int cout, int kh, int kw, int sh, int sw, int ph,
                                   int pw, int ho, int wo, long long *out, int n_out) {
@@ -1126,18 +1167,24 @@ extern "C" int trba_tc_dgrad_plan(int b, int cin, int h, int w, int cout, int kh
     Plan p;
     if (b <= 0 || !make_plan(cin, cout, h, w, kh, kw, sh, sw, ph, pw, ho, wo, p)) return -1;
     set_batch(p, b);
-    const Class &C = p.cls[0];
-    long long f[21 + 3 * kMaxTaps] = {p.halo, p.BN, p.Npad, p.ntn, p.tiles, p.halo ? C.ntaps : 0};
-    int n = 6;
+    std::vector<long long> f = {p.halo, p.BN, p.Npad, p.ntn, p.tiles, p.halo ? p.h.taps : 0};
     if (p.halo) {
         const Halo &hh = p.h;
-        const long long v[] = {hh.KC,   hh.nchunks, hh.mb,          hh.R,
-                               hh.sa,   hh.sb,      hh.Hq,          hh.Wq,
-                               hh.dmin, hh.mpos,    hh.rows,        plane_elements(p),
-                               weight_image_bytes(p), (long long)halo_smem(p), (long long)halo_tmem_cols(p)};
-        for (long long x : v) f[n++] = x;
-        for (int t = 0; t < C.ntaps; ++t) f[n++] = C.kh[t], f[n++] = C.kw[t], f[n++] = hh.off[t];
+        for (long long x : {(long long)hh.KC, (long long)hh.nchunks, (long long)hh.mb, (long long)hh.R,
+                            (long long)hh.sa, (long long)hh.sb, (long long)hh.Hq, (long long)hh.Wq,
+                            (long long)hh.dmin, hh.mpos, hh.rows, plane_elements(p), weight_image_bytes(p),
+                            (long long)halo_smem(p), (long long)halo_tmem_cols(p), (long long)p.ncls})
+            f.push_back(x);
+        for (int k = 0; k < p.ncls; ++k) {
+            const Class &C = p.cls[k];
+            for (long long x : {C.py, C.px, C.Hc, C.Wc, C.ntaps, C.tile0, C.mtiles, C.b_off}) f.push_back(x);
+            for (int t = 0; t < C.ntaps; ++t) {
+                f.push_back(C.kh[t]);
+                f.push_back(C.kw[t]);
+                f.push_back(hh.off[k][t]);
+            }
+        }
     }
-    for (int i = 0; i < n && i < n_out; ++i) out[i] = f[i];
-    return n;
+    for (int i = 0; i < (int)f.size() && i < n_out; ++i) out[i] = f[i];
+    return (int)f.size();
 }

@@ -33,31 +33,35 @@ struct Class {
     int Hc, Wc;    // class sub-grid (pixels y = py + sH * i, x = px + sW * j)
     int ntaps;     // kernel taps that reach the output grid from this phase
     int kchunks;   // ceil(ntaps * Cout / 64): K chunks of the class GEMM
-    int b_off;     // first chunk of this class in the weight image
+    int b_off;     // first chunk (halo tiling: first weight block) of this class in the weight image
     int tile0;     // first tile of this class in the launch (batch dependent)
-    int mtiles;    // 128-pixel tiles of this class (batch dependent)
+    int mtiles;    // M tiles of this class (batch dependent)
     int8_t kh[kMaxTaps], kw[kMaxTaps];
 };
 
-// Stride-1 convs use the halo tiling instead of the class tiling: the three
-// dy planes hold dy on a padded grid of Hq x Wq positions per image (real
-// values at rows < Ho and columns < Wo of each image's slot, zeros in the
-// gap rows and columns, which the neighbouring image and row share), so the
-// rows a kernel tap reads for a run of consecutive positions are the same
-// run shifted by the tap's offset (dh * Wq + dw).  A tile is 128 * mb
-// consecutive positions; one copy of its halo (128 * mb + dmax - dmin rows)
-// per KC output channels serves every tap.  Positions outside the input
-// grid (gap rows and columns) are computed and not stored.
+// The halo tiling (Cout a multiple of 16): the three dy planes hold dy on a
+// padded grid of Hq x Wq positions per image (real values at rows < Ho and
+// columns < Wo of each image's slot, zeros in the gap rows and columns,
+// which the neighbouring image and row share).  Class pixel (i, j) of a
+// stride phase (y = py + sH i, x = px + sW j) reads dy at (i + dh, j + dw)
+// for each of its taps, dh = (py + pH - kh) / sH (exact within the class),
+// so on the padded grid the rows a tap reads for a run of consecutive
+// positions (b, i, j) are that run shifted by the tap's offset dh * Wq + dw:
+// every class is a stride-1 problem over the same planes.  A tile is 128 * mb
+// consecutive positions of one class; one copy of its halo (128 * mb +
+// dmax - dmin rows) per KC output channels serves every tap of the class.
+// Positions outside the class grid are computed and not stored.
 struct Halo {
     int Hq, Wq;         // padded slot of one image
     int mb;             // 128-row MMA blocks per tile (the tile has 128 * mb positions)
     int KC;             // output channels (K) per halo stage: 16, 32 or 64
     int nchunks;        // Cout / KC
-    int dmin;           // smallest tap offset (<= 0)
+    int dmin, dmax;     // smallest (<= 0) and largest (>= 0) tap offset over all classes
     int R;              // halo rows per tile
     int sa, sb;         // shared-memory stages of halos and of weight blocks
     int nacc;           // TMEM accumulators (2: double-buffered, 1 when 2 x mb x BN columns do not fit)
-    int off[kMaxTaps];  // tap offset from the halo's first row
+    int taps;           // taps of all classes (weight blocks per N tile and chunk)
+    int off[kMaxClasses][kMaxTaps];  // tap offset from the halo's first row
     long long mpos;     // B * Hq * Wq (batch dependent)
     long long rows;     // rows of one plane slab, guards included (batch dependent)
 };
@@ -73,14 +77,15 @@ struct Plan {
     int B;             // batch of the launch
     int tiles;         // tiles of the launch (batch dependent)
     Class cls[kMaxClasses];
-    int halo;  // 1: halo tiling (stride 1, one class holding every tap)
+    int halo;  // 1: halo tiling
     Halo h;
 };
 
 // Builds the plan of a conv, or returns false when the kernel does not
 // serve it (Cout or a stride not a power of two, Cout < 8, more than 4
 // stride phases or 16 taps per phase).  Stride-1 convs with Cout a multiple
-// of 16 and padding below the kernel size get the halo tiling.
+// of 16 and padding below the kernel size get the halo tiling, as do
+// strided convs whose phase classes fit it.
 // Batch-dependent fields are filled by set_batch.
 bool make_plan(int Cin, int Cout, int H, int W, int kH, int kW, int sH, int sW, int pH, int pW, int Ho, int Wo,
                Plan &p);
@@ -92,7 +97,7 @@ void set_batch(Plan &p, int B);
 void set_tiling_override(int mb, int kc);
 // Elements (bf16) of the weight image of a plan.
 __host__ __device__ inline long long image_elements(const Plan &p) {
-    return p.halo ? (long long)p.Npad * p.Cout * p.cls[0].ntaps : (long long)p.total_chunks * p.Npad * kChunk;
+    return p.halo ? (long long)p.Npad * p.Cout * p.h.taps : (long long)p.total_chunks * p.Npad * kChunk;
 }
 // Bytes of the bf16 weight image of a plan.
 inline long long weight_image_bytes(const Plan &p) { return 2 * image_elements(p); }
@@ -128,9 +133,10 @@ __device__ __forceinline__ int image_source(const Plan &p, int gc, int n, int kl
 // Element e (0 <= e < image_elements) of the weight image of either tiling:
 // its byte offset in the image (*dst), its output channel (*co) and its
 // source K index in the forward operand, or -1 for a zero entry.  The halo
-// image is blocks of [KC / 8][BN rows][8] bf16, one per (N tile, channel
-// chunk, tap) in that order: the no-swizzle K-major layout one bulk copy
-// places as a weight stage.
+// image is blocks of [KC / 8][BN rows][8] bf16, one per (class, N tile,
+// channel chunk, tap of the class) in that order (class c's first block is
+// cls[c].b_off): the no-swizzle K-major layout one bulk copy places as a
+// weight stage.
 __device__ __forceinline__ int image_element(const Plan &p, long long e, int &co, long long &dst) {
     if (!p.halo) {
         int gc, n, kl;
@@ -145,8 +151,11 @@ __device__ __forceinline__ int image_element(const Plan &p, long long e, int &co
     q /= p.BN;
     const int nsl = p.h.KC >> 3;
     const int s = (int)(q % nsl);
-    q /= nsl;
-    const Class &C = p.cls[0];
+    q /= nsl;  // weight block
+    int k = 0;
+    while (k + 1 < p.ncls && q >= p.cls[k + 1].b_off) ++k;
+    const Class &C = p.cls[k];
+    q -= C.b_off;
     const int t = (int)(q % C.ntaps);
     q /= C.ntaps;
     const int c = (int)(q % p.h.nchunks);
