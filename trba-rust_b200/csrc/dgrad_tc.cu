@@ -414,27 +414,72 @@ __host__ __device__ inline uint32_t halo_tmem_cols(const Plan &p) {
     return c;
 }
 
-// The MMAs of one (channel chunk, tap) of a halo tile: 3 split terms x
-// KC / 16 K steps x MB row blocks, every descriptor the stage's base plus a
-// compile-time offset (the per-term slab offsets are multiples of the run-time
-// halo height R, loop-invariant).  Issued by one elected lane of the calling
-// warp, which must be converged.  a_lo / b_lo: low descriptor words of the
-// tap's A window and of the weight block; first: the tile's first MMAs
-// (overwrite the accumulators).
+// The MMA issuer of the halo kernel (one thread), for a compile-time channel
+// chunk KC and tile height MB: per tile, per channel chunk (one halo stage),
+// per tap of the tile's class (one weight stage), 3 split terms x KC / 16 K
+// steps x MB row blocks of M = 128, N = BN, K = 16.  Every descriptor is a
+// stage base plus offsets fixed before the loop (the per-term slab offsets
+// are multiples of the run-time halo height R), so an MMA costs one add
+// per operand.
 template <int BN, int KC, int MB>
-__device__ __forceinline__ void halo_tap_mmas(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t R,
-                                              uint32_t idesc, bool first) {
-    if (!elect_one()) return;
+__device__ __forceinline__ void halo_mma_loop(const Plan &P, const Args &a, HCtl *ctl, uint32_t as0, uint32_t bs0,
+                                              uint32_t tbase, uint32_t slab, uint32_t a_stage, uint32_t b_stage,
+                                              volatile int *abort) {
+    const Halo &h = P.h;
+    constexpr uint32_t idesc = idesc_bf16(128, BN);
+    constexpr int NSL = KC / 8, NK = KC / 16;
+    const uint32_t a_lo0 = ((as0 >> 4) & 0x3FFFu) | desc_interleave_lo(slab);
+    const uint32_t b_lo0 = ((bs0 >> 4) & 0x3FFFu) | desc_interleave_lo(BN * 16);
+    const uint32_t hi = desc_interleave_hi(128);
+    const uint32_t a_step = a_stage >> 4, b_step = b_stage >> 4, R = (uint32_t)h.R;
+    uint32_t roff[3][NK];  // slab offset of (term, K step), in 16-byte units
 #pragma unroll
     for (int p = 0; p < 3; ++p)
 #pragma unroll
-        for (int kk = 0; kk < KC / 16; ++kk) {
-            const uint64_t bd = desc_join(b_lo + kk * 2 * BN, hi);  // two slabs of BN rows x 16 bytes per K step
+        for (int kk = 0; kk < NK; ++kk) roff[p][kk] = (uint32_t)(p * NSL + 2 * kk) * R;
+    uint32_t ia = 0, ib = 0, acc = 0, acc_ph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < P.tiles && ok; t += gridDim.x) {
+        if (!(ok = mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort, a.wait_ns))) break;
+        tc_fence_after();
+        const int k = tile_class(P, t);
+        const int ntaps = P.cls[k].ntaps;
+        const uint32_t d = tbase + acc * MB * BN;
+        for (int c = 0; c < h.nchunks && ntaps > 0 && ok; ++c, ++ia) {
+            const int sa = ia % h.sa;
+            if (!(ok = mbar_wait(&ctl->afull[sa], (ia / h.sa) & 1u, abort, a.wait_ns))) break;
+            ctl->a_consumed = ia + 1;
+            tc_fence_after();
+            const uint32_t a_lo = a_lo0 + sa * a_step;
+            for (int tap = 0; tap < ntaps; ++tap, ++ib) {
+                const int sb = ib % h.sb;
+                if (!(ok = mbar_wait(&ctl->bfull[sb], (ib / h.sb) & 1u, abort, a.wait_ns))) break;
+                ctl->b_consumed = ib + 1;
+                tc_fence_after();
+                const uint32_t al = a_lo + (uint32_t)h.off[k][tap], bl = b_lo0 + sb * b_step;
+                const bool first = (c | tap) == 0;
 #pragma unroll
-            for (int i = 0; i < MB; ++i)
-                mma_bf16(d + i * BN, desc_join(a_lo + (p * (KC / 8) + 2 * kk) * R + i * 128, hi), bd, idesc,
-                         (first && p == 0 && kk == 0) ? 0u : 1u);
+                for (int p = 0; p < 3; ++p)
+#pragma unroll
+                    for (int kk = 0; kk < NK; ++kk) {
+                        const uint64_t bd = desc_join(bl + kk * 2 * BN, hi);  // two slabs of BN rows x 16 bytes
+#pragma unroll
+                        for (int i = 0; i < MB; ++i)
+                            mma_bf16(d + i * BN, desc_join(al + roff[p][kk] + i * 128, hi), bd, idesc,
+                                     (first && p == 0 && kk == 0) ? 0u : 1u);
+                    }
+                mma_commit(&ctl->bempty[sb]);
+            }
+            if (!ok) break;
+            mma_commit(&ctl->aempty[sa]);
         }
+        if (!ok) break;
+        mma_commit(&ctl->tfull[acc]);
+        if (++acc == (uint32_t)h.nacc) acc = 0, acc_ph ^= 1u;
+    }
+    mma_commit(&ctl->drained);
+    volatile int never = 0;
+    mbar_wait(&ctl->drained, 0, &never, 200000000ull);
 }
 
 template <int BN>
@@ -532,68 +577,22 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             }
         }
     } else if (warp == 2) {
-        // ------------------------------------------------ MMA issuer
-        // The whole warp runs the loop (its descriptor arithmetic stays
-        // warp-uniform); one elected lane issues the tcgen05 instructions.
-        constexpr uint32_t idesc = idesc_bf16(128, BN);
-        const uint32_t a_lo0 = ((smem_u32(As) >> 4) & 0x3FFFu) | desc_interleave_lo(slab);
-        const uint32_t b_lo0 = ((smem_u32(Bs) >> 4) & 0x3FFFu) | desc_interleave_lo(BN * 16);
-        const uint32_t hi = desc_interleave_hi(128);
-        const uint32_t a_step = a_stage >> 4, b_step = b_stage >> 4, R = (uint32_t)h.R;
-        const int kind = h.KC * 8 + h.mb;
-        uint32_t ia = 0, ib = 0, acc = 0, acc_ph = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < P.tiles && ok; t += gridDim.x) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&ctl->tempty[acc], acc_ph ^ 1u, abort, a.wait_ns));
-            if (!ok) break;
-            tc_fence_after();
-            const int k = tile_class(P, t);
-            const int ntaps = P.cls[k].ntaps;
-            const uint32_t d = tbase + acc * h.mb * BN;
-            for (int c = 0; c < h.nchunks && ntaps > 0 && ok; ++c, ++ia) {
-                const int sa = ia % h.sa;
-                ok = __all_sync(0xffffffffu, mbar_wait(&ctl->afull[sa], (ia / h.sa) & 1u, abort, a.wait_ns));
-                if (!ok) break;
-                ctl->a_consumed = ia + 1;  // every lane stores the same value: the warp stays converged
-                tc_fence_after();
-                const uint32_t a_lo = a_lo0 + sa * a_step;
-                for (int tap = 0; tap < ntaps; ++tap, ++ib) {
-                    const int sb = ib % h.sb;
-                    ok = __all_sync(0xffffffffu, mbar_wait(&ctl->bfull[sb], (ib / h.sb) & 1u, abort, a.wait_ns));
-                    if (!ok) break;
-                    ctl->b_consumed = ib + 1;
-                    tc_fence_after();
-                    const uint32_t al = a_lo + (uint32_t)h.off[k][tap], bl = b_lo0 + sb * b_step;
-                    const bool first = (c | tap) == 0;
-                    switch (kind) {
-#define TRBA_HALO_TAP(KC_, MB_)                                                          \
-    case KC_ * 8 + MB_:                                                                  \
-        if constexpr (MB_ * BN <= 384) halo_tap_mmas<BN, KC_, MB_>(d, al, bl, hi, R, idesc, first); \
+        // ------------------------------------------------ MMA issuer (lane 0)
+        if (lane == 0) {
+            const uint32_t as0 = smem_u32(As), bs0 = smem_u32(Bs);
+            switch (h.KC * 8 + h.mb) {
+#define TRBA_HALO_LOOP(KC_, MB_)                                                                         \
+    case KC_ * 8 + MB_:                                                                                  \
+        if constexpr (MB_ * BN <= 384)                                                                   \
+            halo_mma_loop<BN, KC_, MB_>(P, a, ctl, as0, bs0, tbase, slab, a_stage, b_stage, abort); \
         break;
-                        TRBA_HALO_TAP(16, 1) TRBA_HALO_TAP(16, 2) TRBA_HALO_TAP(16, 3) TRBA_HALO_TAP(16, 4)
-                        TRBA_HALO_TAP(32, 1) TRBA_HALO_TAP(32, 2) TRBA_HALO_TAP(32, 3) TRBA_HALO_TAP(32, 4)
-                        TRBA_HALO_TAP(64, 1) TRBA_HALO_TAP(64, 2) TRBA_HALO_TAP(64, 3) TRBA_HALO_TAP(64, 4)
-#undef TRBA_HALO_TAP
-                        default: break;
-                    }
-                    __syncwarp();  // the issuing lane rejoins before the next elect
-                    if (elect_one()) mma_commit(&ctl->bempty[sb]);
-                    __syncwarp();
-                }
-                if (!ok) break;
-                if (elect_one()) mma_commit(&ctl->aempty[sa]);
-                __syncwarp();
+                TRBA_HALO_LOOP(16, 1) TRBA_HALO_LOOP(16, 2) TRBA_HALO_LOOP(16, 3) TRBA_HALO_LOOP(16, 4)
+                TRBA_HALO_LOOP(32, 1) TRBA_HALO_LOOP(32, 2) TRBA_HALO_LOOP(32, 3) TRBA_HALO_LOOP(32, 4)
+                TRBA_HALO_LOOP(64, 1) TRBA_HALO_LOOP(64, 2) TRBA_HALO_LOOP(64, 3) TRBA_HALO_LOOP(64, 4)
+#undef TRBA_HALO_LOOP
+                default: *abort = 1; break;  // a tile the planner never makes
             }
-            if (!ok) break;
-            if (elect_one()) mma_commit(&ctl->tfull[acc]);
-            __syncwarp();
-            if (++acc == (uint32_t)h.nacc) acc = 0, acc_ph ^= 1u;
         }
-        if (elect_one()) mma_commit(&ctl->drained);
-        __syncwarp();
-        volatile int never = 0;
-        mbar_wait(&ctl->drained, 0, &never, 200000000ull);
-        __syncwarp();
     } else {
         // ------------------------------------------------ epilogue
         constexpr int CW = 16;  // accumulator columns per tcgen05.ld (BN >= 16)

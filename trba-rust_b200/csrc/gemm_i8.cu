@@ -141,10 +141,16 @@ struct EpiConvF32 {
     __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
         const bool rv = row < M;
         const int b = rv ? row / HW : 0, p = rv ? row - b * HW : 0;
+        // the scales are read before any store (a store to x could alias
+        // them as far as the compiler knows, which would make every column
+        // wait for the previous column's store)
+        float sc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] = scale_of(col + j < N ? col + j : N - 1);
         double s[32], q[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const float val = fmul((float)(int32_t)v[j], scale_of(col + j < N ? col + j : N - 1));
+            const float val = fmul((float)(int32_t)v[j], sc[j]);
             const bool ok = rv && col + j < N;
             if (ok) x[((i64)b * N + col + j) * HW + p] = val;
             s[j] = ok ? (double)val : 0.0;
@@ -180,10 +186,13 @@ struct EpiConvF32 {
         if (row >= M) return;
         const int b = row / HW, p = row - b * HW;
         float *xp = x + ((i64)b * N + col) * HW + p;
+        float sc[16];  // read before any store, as in store()
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sc[j] = scale_of(col + j < N ? col + j : N - 1);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             if (col + j < N) {
-                const float val = fmul((float)(int32_t)(hi ? v[16 + j] : v[j]), scale_of(col + j));
+                const float val = fmul((float)(int32_t)(hi ? v[16 + j] : v[j]), sc[j]);
                 xp[(i64)j * HW] = val;
                 const double d = (double)val;
                 a.s[j] += d;
