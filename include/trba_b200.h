@@ -79,6 +79,22 @@ int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, in
                                float *grad_input, int b, int cin, int h, int w, int cout, int kh, int kw,
                                int sh, int sw, int ph, int pw, int ho, int wo, void *stream);
 
+/* launch_im2col_pad followed by launch_gemm_int8 (reference backend.rs,
+ * cuda/kernels.cu:476-541 and :227-250: the QAT conv forward's GEMM,
+ * src/qnet.rs:338-458) as one implicit GEMM on the tensor cores (tcgen05
+ * kind::i8): the receptive field of each output pixel is gathered into the
+ * GEMM's shared-memory stages straight from the activations, so the im2col
+ * matrix is never written.  acc = s32 [b*ho*wo, cout] compact, bit for bit
+ * what im2col + GEMM give (integer sums do not depend on the K order).
+ * input: int8 NCHW [b, cin, h, w]; weight_q: [cout, w_ld] in the reference's
+ * (ci, ky, kx) K order, w_ld >= cin*kh*kw.  Needs cin a power of two in
+ * [16, 1024].  Keeps a grow-only per-device buffer for the channel-innermost
+ * copy of the input and the re-ordered weights.  Returns 0, -1 for an
+ * unsupported conv, or a CUDA error code. */
+int trba_conv_gemm_int8_implicit(const int8_t *input, const int8_t *weight_q, int w_ld, int32_t *acc, int b,
+                                 int cin, int h, int w, int cout, int kh, int kw, int sh, int sw, int ph, int pw,
+                                 int ho, int wo, void *stream);
+
 /* Self-test of the bounded waits of the tensor-core kernels (no
  * counterpart in the reference): runs one small tensor-core input-gradient
  * launch of each tiling (class and halo) whose weight copies are

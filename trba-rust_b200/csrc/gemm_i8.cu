@@ -65,6 +65,7 @@ struct Cfg {
 struct Ctl {  // lives after the stage ring in shared memory
     uint64_t full[8];
     uint64_t empty[8];
+    uint64_t afull[8];  // implicit-GEMM conv: the gathered A rows of a stage have landed
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drained;
@@ -313,10 +314,34 @@ struct Shape {
     int kb_per_split;  // K blocks of 128 per split
 };
 
-template <int BN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+// Where the A operand comes from.
+//   TmaA       a row-major int8 matrix read through the A tensor map.
+//   ConvGather the implicit-GEMM conv forward: A[r, k] for output pixel
+//              r = (b, oy, ox) and k = (ky * kw + kx) * Cin + ci is read
+//              straight from NHWC int8 activations by kGatherWarps extra
+//              warps with 16-byte cp.async (zero-filled where the tap falls
+//              on the conv's zero padding), written into the stage in the
+//              layout TMA's 128-byte swizzle gives, so the im2col matrix is
+//              never materialised.  Integer accumulation makes the K order
+//              irrelevant: the s32 results equal im2col + GEMM exactly.
+struct TmaA {
+    static constexpr bool kGather = false;
+};
+struct ConvGather {
+    static constexpr bool kGather = true;
+    const int8_t *x;  // [B, H, W, Cin], 16-byte aligned; Cin = 1 << lgC >= 16
+    int H, W, lgC, kh, kw, sh, sw, ph, pw, Wo, HoWo;
+};
+constexpr int kGatherWarps = 2;
+template <class Src>
+constexpr int threads_for() {
+    return kThreads + (Src::kGather ? 32 * kGatherWarps : 0);
+}
+
+template <int BN, class Epi, class Src = TmaA>
+__global__ void __launch_bounds__(threads_for<Src>(), 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
-                  Epi epi) {
+                  Epi epi, Src src = Src()) {
     using G = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -334,6 +359,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         for (int s = 0; s < G::STAGES; ++s) {
             mbar_init(&ctl->full[s], 1);
             mbar_init(&ctl->empty[s], 1);
+            if constexpr (Src::kGather) mbar_init(&ctl->afull[s], 32 * kGatherWarps);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&ctl->tfull[a], 1);
@@ -344,7 +370,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         ctl->issued = 0;
         ctl->consumed = 0;
         fence_barrier_init();
-        tma_prefetch_desc(&tmA);
+        if constexpr (!Src::kGather) tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
     if (warp >= 2) epi.init(epi_sm);
@@ -380,8 +406,12 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                     const int s = it % G::STAGES;
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort)) break;
-                    mbar_expect_tx(&ctl->full[s], G::STAGE_BYTES);
-                    tma_load_2d(sA + s * G::A_BYTES, &tmA, &ctl->full[s], kb * BK, m0);
+                    if constexpr (Src::kGather) {  // A comes from the gather warps
+                        mbar_expect_tx(&ctl->full[s], G::B_BYTES);
+                    } else {
+                        mbar_expect_tx(&ctl->full[s], G::STAGE_BYTES);
+                        tma_load_2d(sA + s * G::A_BYTES, &tmA, &ctl->full[s], kb * BK, m0);
+                    }
                     tma_load_2d(sB + s * G::B_BYTES, &tmB, &ctl->full[s], kb * BK, n0);
                     ctl->issued = it + 1;
                 }
@@ -404,6 +434,12 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                     const uint32_t ph = (it / G::STAGES) & 1u;
                     if (!(ok = mbar_wait(&ctl->full[s], ph, abort))) break;
                     ctl->consumed = it + 1;
+                    if constexpr (Src::kGather) {
+                        if (!(ok = mbar_wait(&ctl->afull[s], ph, abort))) break;
+                        // the gathered rows were written by cp.async (generic proxy):
+                        // order them before the tensor cores' reads (async proxy)
+                        fence_proxy_async_smem();
+                    }
                     tc_fence_after();
                     // the stage's base descriptors once, then compile-time K offsets
                     // (one add per MMA: a descriptor rebuilt per MMA halves the issue rate)
@@ -427,7 +463,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             volatile int never = 0;
             mbar_wait(&ctl->drained, 0, &never, 200000000ull);
         }
-    } else {
+    } else if (warp < 2 + kEpiWarps) {
         // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int half = (warp - 2) >> 2;       // which 32-column blocks of the tile it takes
@@ -491,6 +527,49 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             acc ^= 1u;
             if (acc == 0) acc_ph ^= 1u;
         }
+    } else if constexpr (Src::kGather) {
+        // ---------------- implicit-GEMM producers (warps 10..) ----------------
+        // Thread g copies 16-byte piece (g & 7) of rows (g >> 3) + kRowStep i
+        // of every stage: eight consecutive threads fill one 128-byte row.
+        constexpr int kRowStep = 32 * kGatherWarps / 8, kRowsPer = BM / kRowStep;
+        const int g = threadIdx.x - 32 * (2 + kEpiWarps);
+        const int l8 = g & 7, rs = g >> 3;
+        const int cmask = (1 << src.lgC) - 1, ntaps = src.kh * src.kw;
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < tiles && !*abort; t += gridDim.x) {
+            int m0, n0, kb0, kb1;
+            tile_coords(t, m0, n0, kb0, kb1);
+            int iy0[kRowsPer], ix0[kRowsPer], pb[kRowsPer];  // the rows' top-left input tap, b * H (-1: no row)
+#pragma unroll
+            for (int i = 0; i < kRowsPer; ++i) {
+                const int m = m0 + rs + kRowStep * i;
+                const int b = m / src.HoWo, p = m - b * src.HoWo, oy = p / src.Wo, ox = p - oy * src.Wo;
+                iy0[i] = oy * src.sh - src.ph;
+                ix0[i] = ox * src.sw - src.pw;
+                pb[i] = m < M ? b * src.H : -1;
+            }
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                const int s = it % G::STAGES;
+                const uint32_t ph = (it / G::STAGES) & 1u;
+                if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort)) break;
+                const int koff = kb * BK + l8 * 16;
+                const int tap = koff >> src.lgC, ci0 = koff & cmask;
+                const bool tok = tap < ntaps;
+                const int ky = tok ? tap / src.kw : 0, kx = tok ? tap - ky * src.kw : 0;
+                uint8_t *stage = sA + s * G::A_BYTES;
+#pragma unroll
+                for (int i = 0; i < kRowsPer; ++i) {
+                    const int r = rs + kRowStep * i;
+                    const int iy = iy0[i] + ky, ix = ix0[i] + kx;
+                    const bool ok = tok && pb[i] >= 0 && (unsigned)iy < (unsigned)src.H && (unsigned)ix < (unsigned)src.W;
+                    const int8_t *gp = ok ? src.x + ((((i64)(pb[i] + iy) * src.W + ix) << src.lgC) + ci0) : src.x;
+                    cp_async16(stage + r * BK + ((l8 ^ (r & 7)) << 4), gp, ok ? 16u : 0u);
+                }
+                // arrives on the stage's A barrier once these copies have landed
+                cp_async_arrive_noinc(&ctl->afull[s]);
+            }
+        }
+        cp_async_wait<0>();  // nothing may land after the CTA is gone
     }
 
     __syncthreads();
@@ -755,20 +834,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int BN, class Epi>
-void launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const Epi &epi, cudaStream_t st) {
+template <int BN, class Epi, class Src = TmaA>
+void launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, Shape sh, const Epi &epi, cudaStream_t st,
+               const Src &src = Src()) {
     using G = Cfg<BN>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        TRBA_CHECK(cudaFuncSetAttribute(gemm_i8_tc_kernel<BN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        G::SMEM));
+        TRBA_CHECK(cudaFuncSetAttribute(gemm_i8_tc_kernel<BN, Epi, Src>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
         attr_set[dev] = true;
     }
     const int tiles = ((sh.M + BM - 1) / BM) * ((sh.N + BN - 1) / BN) * sh.splits;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_i8_tc_kernel<BN, Epi><<<grid, kThreads, G::SMEM, st>>>(ta, tb, sh, epi);
+    gemm_i8_tc_kernel<BN, Epi, Src><<<grid, threads_for<Src>(), G::SMEM, st>>>(ta, tb, sh, epi, src);
     TRBA_LAUNCH_CHECK();
 }
 
@@ -832,6 +912,29 @@ bool run_tc(const int8_t *A, int lda, const int8_t *B, int ldb, Shape sh, const 
     return true;
 }
 
+// The implicit-GEMM conv forward (ConvGather): B = the weights in the
+// gather's K order, [N, kh*kw*Cin] with leading dimension ldw.
+template <class Epi>
+bool run_conv_gather(const ConvGeo &g, const int8_t *Wh, int ldw, int N, const Epi &epi, cudaStream_t st) {
+    if (!conv_implicit_ok(g)) return false;
+    const int K = g.kh * g.kw * g.Cin, M = g.B * g.Ho * g.Wo;
+    const int bn = pick_bn(N);
+    CUtensorMap tb;
+    if (!make_tmap_i8(&tb, Wh, N, K, ldw, bn)) return false;
+    int lg = 0;
+    while ((1 << lg) < g.Cin) ++lg;
+    const ConvGather src{g.x, g.H, g.W, lg, g.kh, g.kw, g.sh, g.sw, g.ph, g.pw, g.Wo, g.Ho * g.Wo};
+    const int kblocks = (K + BK - 1) / BK;
+    const Shape sh{M, N, K, 1, kblocks};
+    switch (bn) {
+        case 32: launch_tc<32>(tb, tb, sh, epi, st, src); break;
+        case 64: launch_tc<64>(tb, tb, sh, epi, st, src); break;
+        case 128: launch_tc<128>(tb, tb, sh, epi, st, src); break;
+        default: launch_tc<256>(tb, tb, sh, epi, st, src); break;
+    }
+    return true;
+}
+
 Shape make_shape(int M, int N, int K, int splits) {
     const int kblocks = (K + BK - 1) / BK;
     if (splits < 1) splits = 1;
@@ -888,6 +991,23 @@ bool gemm_i8_dequant(const int8_t *A, const int8_t *B, float *out, const float *
     EpiDequantF32 e{out, N, w_scale, bias, a_scale, relu,
                     ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (N & 3) == 0};
     return run_tc(A, ld, B, ld, make_shape(M, N, K, 1), e, st);
+}
+
+bool conv_implicit_ok(const ConvGeo &g) {
+    const bool pow2 = g.Cin >= 16 && g.Cin <= 1024 && (g.Cin & (g.Cin - 1)) == 0;
+    return pow2 && (reinterpret_cast<uintptr_t>(g.x) & 15) == 0 && g.B > 0 && g.Ho > 0 && g.Wo > 0 &&
+           (i64)g.B * g.Ho * g.Wo < (1ll << 31) && (i64)g.B * g.H * g.W * g.Cin < (1ll << 40);
+}
+
+bool gemm_i8_conv_implicit_f32(const ConvGeo &g, const int8_t *Wh, int ldw, int N, float *x, const float *s_in,
+                               const float *w_s, bool per_channel, double *bn_acc, cudaStream_t st) {
+    if (N > kMaxN) return false;
+    return run_conv_gather(g, Wh, ldw, N, EpiConvF32{x, s_in, w_s, per_channel ? 1 : 0, bn_acc, g.Ho * g.Wo}, st);
+}
+
+bool gemm_i8_conv_implicit_s32(const ConvGeo &g, const int8_t *Wh, int ldw, int N, int32_t *C, cudaStream_t st) {
+    EpiS32 e{C, N, ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && (N & 3) == 0};
+    return run_conv_gather(g, Wh, ldw, N, e, st);
 }
 
 int splitk_for(int M, int N, int K) {

@@ -28,6 +28,21 @@ bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float 
                      float div, float mul, cudaStream_t st);
 bool gemm_i8_dequant(const int8_t *A, const int8_t *B, float *out, const float *w_scale, float a_scale,
                      const float *bias, int relu, int M, int N, int K, int ld, cudaStream_t st);
+// Implicit-GEMM conv forward: the GEMM's A rows gathered from NHWC int8
+// activations x [B, H, W, Cin] (Cin a power of two >= 16, x 16-byte aligned)
+// in K order (ky, kx, ci); Wh = the int8 weights in that K order,
+// [N, kh*kw*Cin] with leading dimension ldw (a multiple of 16).  Row r of the
+// result is output pixel (b, oy, ox), as with im2col.
+struct ConvGeo {
+    const int8_t *x;
+    int B, H, W, Cin, kh, kw, sh, sw, ph, pw, Ho, Wo;
+};
+bool conv_implicit_ok(const ConvGeo &g);
+// The conv forward epilogue of gemm_i8_conv_f32 over the gathered operand.
+bool gemm_i8_conv_implicit_f32(const ConvGeo &g, const int8_t *Wh, int ldw, int N, float *x, const float *s_in,
+                               const float *w_s, bool per_channel, double *bn_acc, cudaStream_t st);
+// s32 accumulators, compact C [B*Ho*Wo, N].
+bool gemm_i8_conv_implicit_s32(const ConvGeo &g, const int8_t *Wh, int ldw, int N, int32_t *C, cudaStream_t st);
 int splitk_for(int M, int N, int K);
 void gemm_i8_simt(const int8_t *A, const int8_t *B, int32_t *C, int M, int N, int K, int ld, cudaStream_t st);
 

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "conv_implicit.cuh"
 #include "dgrad_tc.cuh"
 #include "gemm_i8.cuh"
 #include "qat_kernels.cuh"
@@ -114,6 +115,10 @@ struct ConvL {
     i64 w_off, gamma_off, beta_off;
     // persistent
     Ref<int8_t> wq;          // [a16(cout), kp]
+    // Implicit-GEMM forward (Cin a power of two >= 16): the operand is gathered
+    // from the NHWC copy of the input; wqh = the weights in (ky, kx, ci) K order
+    bool implicit = false;
+    Ref<int8_t> wqh;         // [cout, K]
     Ref<float> wT;           // (float) wq in the input-gradient layout (dgrad_weights_index), exact mode
     dgtc::Plan tc;           // tensor-core input gradient: class plan (tc_ok) and its bf16 weight image
     bool tc_ok = false;
@@ -124,7 +129,7 @@ struct ConvL {
     Ref<float> ws, wmax;     // device scalars
     Ref<float> run_mean, run_var;
     // forward traces
-    Ref<int8_t> col, colT;   // [a16(rows), kp] / [a16(K), a16(rows)]
+    Ref<int8_t> col, colT;   // [a16(rows), kp] / [a16(K), a16(rows)]; implicit convs: training only
     Ref<float> x, mean, var, y;
     Ref<int8_t> q;           // quantised output (when the conv is followed by relu_quant)
     Ref<float> s_q;          // its scale
@@ -199,6 +204,7 @@ struct trba_model {
     Ref<float> P, G, Mm, Vv;
     // stem
     Ref<int8_t> qpool;
+    Ref<int8_t> qh;          // NHWC copy of the current implicit conv's input
     Ref<float> s_img;
     Ref<float> dy_c1, dy_c0, gv_last, dy_o1, dy_o0;
     // features and sequence head
@@ -237,6 +243,7 @@ struct trba_model {
         const dgtc::Plan *tc;  // tensor-core mode: the plan (device copy) and the image it writes
         uint8_t *wimg;
         int per_channel;       // per-output-channel weight scales (ws, wmax hold cout values)
+        int8_t *wqh;           // implicit-GEMM forward: [cout, K] in (ky, kx, ci) order, or null
     };
     ConvTab *d_convtab = nullptr;
     long long t = 0;
@@ -493,6 +500,15 @@ __global__ void conv_quant_kernel(const Seg *segs, const float *P, const trba_mo
         t.wq[e] = (r < t.cout && c < t.K) ? quant_w(P[s.off + (i64)r * t.K + c], pc ? wscale_of(wb[r]) : sc0)
                                           : (int8_t)0;
     }
+    if (t.wqh) {  // implicit-GEMM forward: K order (ky, kx, ci)
+        const int cin = t.K / t.khw;
+        const i64 nh = (i64)t.cout * t.K;
+        for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < nh; e += (i64)gridDim.x * blockDim.x) {
+            const int r = (int)(e / t.K), k = (int)(e - (i64)r * t.K);
+            const int tap = k / cin, ci = k - tap * cin;
+            t.wqh[e] = quant_w(P[s.off + (i64)r * t.K + (i64)ci * t.khw + tap], pc ? wscale_of(wb[r]) : sc0);
+        }
+    }
     if (t.wimg) {  // tensor-core input gradient: the bf16 weight image
         const dgtc::Plan &tp = *t.tc;
         const i64 n_img = dgtc::image_elements(tp);
@@ -599,6 +615,7 @@ void plan(trba_model *m) {
         qat::dgrad_classes(H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, s1 == 1 && s2 == 1, L.cls_perm, L.cls_start);
         L.tc_ok = m->cfg.dgrad_mode == 1 &&
                   dgtc::make_plan(cin, cout, H, W, k1, k2, s1, s2, p1, p2, L.Ho, L.Wo, L.tc);
+        L.implicit = m->cfg.conv_fwd_mode == 1 && cin >= 16 && cin <= 1024 && (cin & (cin - 1)) == 0;
         m->convs.push_back(L);
         return (int)m->convs.size() - 1;
     };
@@ -711,6 +728,7 @@ void allocate(trba_model *m) {
     m->Vv = b.tp<float>(m->n_params);
     m->s_img = b.p<float>(1);
     const bool correct = c.wgrad_mode == 1;
+    i64 qh_bytes = 0;
     for (size_t i = 0; i < m->convs.size(); ++i) {
         ConvL &L = m->convs[i];
         const i64 rows = L.rows(B), rp = a16l(rows), n = (i64)B * L.cout * L.Ho * L.Wo;
@@ -729,7 +747,15 @@ void allocate(trba_model *m) {
         L.wmax = b.p<float>(L.cout);
         L.run_mean = b.p<float>(L.cout);
         L.run_var = b.p<float>(L.cout);
-        L.col = b.p<int8_t>(rp * L.kp);
+        if (L.implicit) {
+            L.wqh = b.p<int8_t>((i64)L.cout * L.K);
+            // the im2col matrix: training in the reference-compatible
+            // weight-gradient mode only (its GEMM reads it)
+            if (!correct) L.col = b.tp<int8_t>(rp * L.kp);
+            qh_bytes = std::max(qh_bytes, (i64)B * L.cin * L.H * L.W);
+        } else {
+            L.col = b.p<int8_t>(rp * L.kp);
+        }
         if (correct) L.colT = b.tp<int8_t>((i64)a16(L.K) * rp);
         L.x = b.p<float>(n);
         L.mean = b.p<float>(L.cout);
@@ -760,6 +786,7 @@ void allocate(trba_model *m) {
     }
     const ConvL &s1 = m->convs[1];
     m->qpool = b.p<int8_t>((i64)B * s1.cout * (s1.Ho / 2) * (s1.Wo / 2));
+    if (qh_bytes) m->qh = b.p<int8_t>(qh_bytes);
     for (auto &bl : m->blocks) {
         const i64 n = (i64)B * bl.C * bl.Ho * bl.Wo, nin = (i64)B * bl.Cin * bl.H * bl.W;
         bl.pool = b.p<float>((i64)B * bl.C);
@@ -855,6 +882,7 @@ struct Ctx {
     int B;
     float *P, *G;
     bool eval = false;  // inference: BN with the running statistics, no running-stat update
+    const int8_t *nhwc_src = nullptr;  // the activations m->qh holds in NHWC order
 };
 
 struct ProbeScope {
@@ -911,6 +939,29 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     const i64 rows = L.rows(B);
     L.q_in = q_in;
     L.s_in = s_in;
+    // The implicit GEMM serves every forward that does not need the im2col
+    // matrix anyway: inference, and training in the corrected weight-gradient
+    // mode (whose operand is the transposed matrix).  The reference-compatible
+    // weight gradient (wgrad_mode 0) reads the im2col matrix itself, so there
+    // the forward GEMM reads that matrix too (gathering it a second time
+    // measured no faster).
+    if (L.implicit && (c.eval || c.m->cfg.wgrad_mode == 1)) {
+        if (c.nhwc_src != q_in) {  // a downsample conv and conv1 share their input
+            nhwc_from_nchw_i8(q_in, c.m->qh.get(), B, L.cin, L.H * L.W, c.st);
+            c.nhwc_src = q_in;
+        }
+        // bytes: the int8 input + weights read, x (f32) written
+        ProbeScope ps(c.m, TRBA_PROBE_CONV_GEMM, 2.0 * rows * L.cout * L.K,
+                      (double)B * L.cin * L.H * L.W + (double)L.cout * L.K + 4.0 * rows * L.cout, c.st);
+        const ConvGeo g{c.m->qh.get(), B, L.H, L.W, L.cin, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo};
+        if (!gemm_i8_conv_implicit_f32(g, L.wqh.get(), L.K, L.cout, L.x.get(), s_in, L.ws.get(),
+                                       c.m->cfg.wq_per_channel != 0, L.bn_acc.get(), c.st))
+            report_error(__FILE__, __LINE__, "conv forward implicit GEMM: unsupported operands", -1);
+        if (!c.eval)  // the weight gradient's operand
+            qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
+                          (int)a16l(rows), c.st);
+        return;
+    }
     launch_im2col_pad(q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo, L.kp,
                       c.st);
     {
@@ -1389,6 +1440,7 @@ void trba_model_default_config(trba_model_config *c) {
     c->dgrad_mode = 0;
     c->wq_per_channel = 0;
     c->inference_only = 0;
+    c->conv_fwd_mode = 1;
 }
 
 trba_model *trba_model_create(const trba_model_config *cfg) {
@@ -1396,7 +1448,8 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
         cfg->hidden > 128 || cfg->hidden % 8 || cfg->classes <= 3 || cfg->img_h < 8 || cfg->img_w < 8 || (cfg->img_h & 1) ||
         (cfg->img_w & 1) || cfg->max_len <= 0 || cfg->rnn_layers <= 0 || cfg->wgrad_mode < 0 ||
         cfg->wgrad_mode > 1 || cfg->dgrad_mode < 0 || cfg->dgrad_mode > 1 ||
-        cfg->wq_per_channel < 0 || cfg->wq_per_channel > 1 || cfg->inference_only < 0 || cfg->inference_only > 1) {
+        cfg->wq_per_channel < 0 || cfg->wq_per_channel > 1 || cfg->inference_only < 0 || cfg->inference_only > 1 ||
+        cfg->conv_fwd_mode < 0 || cfg->conv_fwd_mode > 1) {
         report_error(__FILE__, __LINE__, "trba_model_create: unsupported configuration", -1);
         return nullptr;
     }
@@ -1420,7 +1473,7 @@ trba_model *trba_model_create(const trba_model_config *cfg) {
     for (auto &L : m->convs) {
         tab.push_back({L.wq.get(), L.ws.get(), L.wmax.get(), L.mean.get(), L.var.get(), L.run_mean.get(),
                        L.run_var.get(), L.cout, L.K, L.kp, L.tc_ok ? nullptr : L.wT.get(), L.kh * L.kw,
-                       L.d_tc.get(), L.wimg.get(), m->cfg.wq_per_channel});
+                       L.d_tc.get(), L.wimg.get(), m->cfg.wq_per_channel, L.implicit ? L.wqh.get() : nullptr});
         // (the input-gradient tables are training buffers: absent in an inference-only model)
         if (L.d_tc.get()) TRBA_CHECK(cudaMemcpy(L.d_tc.get(), &L.tc, sizeof(dgtc::Plan), cudaMemcpyHostToDevice));
         if (L.d_perm.get() && !L.cls_perm.empty()) {

@@ -22,7 +22,7 @@ class _Cfg(C.Structure):
                 ("sos", C.c_int), ("eos", C.c_int), ("pad", C.c_int), ("lr", C.c_float),
                 ("weight_decay", C.c_float), ("ctc_weight", C.c_float), ("muon_cap", C.c_float),
                 ("clip_warmup", C.c_int), ("wgrad_mode", C.c_int), ("dgrad_mode", C.c_int),
-                ("wq_per_channel", C.c_int), ("inference_only", C.c_int)]
+                ("wq_per_channel", C.c_int), ("inference_only", C.c_int), ("conv_fwd_mode", C.c_int)]
 
 
 @dataclass
@@ -47,6 +47,7 @@ class Config:
     dgrad_mode: int = 0  # conv input gradient: 0 exact f32 order, 1 tensor cores (bf16 x3 split)
     wq_per_channel: int = 0  # conv weight scales: 0 per tensor (the reference), 1 per output channel
     inference_only: int = 0  # 1: forward buffers only (serving); training calls are refused
+    conv_fwd_mode: int = 1  # conv forward GEMM: 0 im2col + GEMM, 1 implicit GEMM (same accumulators)
 
     def to_c(self) -> _Cfg:
         return _Cfg(**{f.name: getattr(self, f.name) for f in fields(self)})
