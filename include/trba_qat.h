@@ -50,10 +50,10 @@ typedef struct {
     int inference_only; /* 1: allocate the forward path only (no gradients, optimiser state or
                            backward traces); training entry points then return -3 */
     int conv_fwd_mode;  /* conv forward GEMM: 0 im2col matrix + GEMM (the reference's two launches),
-                           1 (default) implicit GEMM, the operand gathered from the activations,
-                           wherever the weight gradient does not read the im2col matrix itself
-                           (inference, wgrad_mode 1; Cin a power of two >= 16).  Same s32
-                           accumulators either way. */
+                           1 (default) implicit GEMM for Cin a power of two >= 16: the operand is
+                           gathered from the activations, and in training the weight gradient's
+                           im2col operand is built off the forward path, beside the sequence
+                           head.  Same s32 accumulators either way. */
 } trba_model_config;
 
 /* TRBA-small defaults (fd 128, hidden 64, 130 classes, 32x160, max_len 20). */

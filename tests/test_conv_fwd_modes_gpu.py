@@ -2,10 +2,11 @@
 default) against the im2col matrix + GEMM (conv_fwd_mode = 0) on identical
 weights and inputs.
 
-The implicit GEMM serves inference and training in the corrected
-weight-gradient mode (wgrad_mode = 1); with the reference-compatible weight
-gradient (wgrad_mode = 0) the forward reads the im2col matrix that the weight
-gradient needs anyway.  The s32 accumulators are equal either way, so losses,
+In training the implicit GEMM's forward writes no im2col matrix; the weight
+gradient's operand (the matrix for the reference-compatible weight gradient,
+wgrad_mode = 0, its transpose for wgrad_mode = 1) is built on the
+weight-gradient stream while the sequence head runs.  The s32 accumulators
+and the operands are equal either way, so losses,
 every parameter gradient, parameters after an optimiser step, and the greedy
 tokens must be bit-identical between the two modes."""
 import sys

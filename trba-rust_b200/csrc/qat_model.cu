@@ -749,8 +749,8 @@ void allocate(trba_model *m) {
         L.run_var = b.p<float>(L.cout);
         if (L.implicit) {
             L.wqh = b.p<int8_t>((i64)L.cout * L.K);
-            // the im2col matrix: training in the reference-compatible
-            // weight-gradient mode only (its GEMM reads it)
+            // the im2col matrix: the reference-compatible weight gradient's
+            // operand (training only)
             if (!correct) L.col = b.tp<int8_t>(rp * L.kp);
             qh_bytes = std::max(qh_bytes, (i64)B * L.cin * L.H * L.W);
         } else {
@@ -939,13 +939,11 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     const i64 rows = L.rows(B);
     L.q_in = q_in;
     L.s_in = s_in;
-    // The implicit GEMM serves every forward that does not need the im2col
-    // matrix anyway: inference, and training in the corrected weight-gradient
-    // mode (whose operand is the transposed matrix).  The reference-compatible
-    // weight gradient (wgrad_mode 0) reads the im2col matrix itself, so there
-    // the forward GEMM reads that matrix too (gathering it a second time
-    // measured no faster).
-    if (L.implicit && (c.eval || c.m->cfg.wgrad_mode == 1)) {
+    // Implicit GEMM: the forward writes no im2col matrix.  The weight
+    // gradient's operand (the matrix itself for the reference-compatible
+    // weight gradient, its transpose in the corrected mode) is built later,
+    // off the forward path (wgrad_operands).
+    if (L.implicit) {
         if (c.nhwc_src != q_in) {  // a downsample conv and conv1 share their input
             nhwc_from_nchw_i8(q_in, c.m->qh.get(), B, L.cin, L.H * L.W, c.st);
             c.nhwc_src = q_in;
@@ -957,9 +955,6 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
         if (!gemm_i8_conv_implicit_f32(g, L.wqh.get(), L.K, L.cout, L.x.get(), s_in, L.ws.get(),
                                        c.m->cfg.wq_per_channel != 0, L.bn_acc.get(), c.st))
             report_error(__FILE__, __LINE__, "conv forward implicit GEMM: unsupported operands", -1);
-        if (!c.eval)  // the weight gradient's operand
-            qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
-                          (int)a16l(rows), c.st);
         return;
     }
     launch_im2col_pad(q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo, L.kp,
@@ -975,6 +970,34 @@ void conv_fwd(Ctx &c, ConvL &L, const int8_t *q_in, const float *s_in) {
     if (c.m->cfg.wgrad_mode == 1 && !c.eval)  // the weight gradient's operand: training only
         qat::im2col_t(q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
                       (int)a16l(rows), c.st);
+}
+
+// The weight-gradient operands of the implicit-GEMM convs (training), built
+// from the inputs the forward kept (L.q_in) on the weight-gradient stream
+// once the forward is done: they overlap the sequence head, whose
+// recurrences leave most SMs idle, instead of the forward.  Last conv first,
+// the order the backward needs them in; the weight-gradient stream runs them
+// before the backward's weight-gradient work it queues behind them.
+void wgrad_operands(Ctx &c) {
+    trba_model *m = c.m;
+    const bool correct = m->cfg.wgrad_mode == 1;
+    bool forked = false;
+    for (int i = (int)m->convs.size() - 1; i >= 0; --i) {
+        ConvL &L = m->convs[i];
+        if (!L.implicit) continue;
+        if (!forked) {
+            TRBA_CHECK(cudaEventRecord(m->fork_ev, c.st));
+            TRBA_CHECK(cudaStreamWaitEvent(m->side, m->fork_ev, 0));
+            forked = true;
+        }
+        const int B = c.B;
+        if (correct)
+            qat::im2col_t(L.q_in, L.colT.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho, L.Wo,
+                          (int)a16l(L.rows(B)), m->side);
+        else
+            launch_im2col_pad(L.q_in, L.col.get(), B, L.cin, L.H, L.W, L.kh, L.kw, L.sh, L.sw, L.ph, L.pw, L.Ho,
+                              L.Wo, L.kp, m->side);
+    }
 }
 
 qat::Src bn_src(Ctx &c, ConvL &L) {
@@ -1622,6 +1645,7 @@ int trba_model_forward_backward(trba_model *m, const int8_t *img, const int32_t 
         ProbeScope ps(m, TRBA_PROBE_PHASE_CNN_FWD, 0.0, 0.0, st);
         cnn_forward(c, img);
     }
+    wgrad_operands(c);
     {
         ProbeScope ps(m, TRBA_PROBE_PHASE_HEAD_FWD, 0.0, 0.0, st);
         head_forward(c, text_in, target, ctc_tgt, ctc_len);
