@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--dgrad-shape", default=None,
                     help="B,Cin,H,W,Cout,kh,kw,sh,sw,ph,pw: time only the tensor-core conv input gradient "
                          "(trba_conv_grad_input_i8_tc) at this shape")
+    ap.add_argument("--conv-shape", default=None,
+                    help="B,Cin,H,W,Cout,kh,kw,sh,sw,ph,pw: time only the implicit-GEMM conv forward "
+                         "(trba_conv_gemm_int8_implicit) against im2col + GEMM at this shape")
     ap.add_argument("--dgrad-tiling", default="0,0",
                     help="mb,kc of the tensor-core input gradient (trba_tc_dgrad_tiling): -1,0 class tiling "
                          "for every conv, 0,0 automatic, else a forced halo tile")
@@ -435,10 +438,10 @@ def our_arm(args):
             # the exact product is three times the useful multiply-adds
             peak = measured_peaks().get("bf16_tflops_sustained")
             achieved = 3.0 * useful
-            traffic = profiled_traffic("dgrad_tc_kernel", args.batch)
+            traffic = profiled_traffic("dgrad_halo_kernel", args.batch)
             roofline = {
-                "kernel": "dgrad_tc_kernel + split_nhwc_kernel: conv input gradient, implicit GEMM on tcgen05 "
-                          "(kind::f16, dy as three exact bf16 terms)",
+                "kernel": "dgrad_halo_kernel + split_halo_kernel: conv input gradient, implicit GEMM on tcgen05 "
+                          "(kind::f16, dy as three exact bf16 terms, one shared-memory halo per tile)",
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if peak else None,
                 "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (the kernel runs inside a long step)",
@@ -620,6 +623,58 @@ def dgrad_only(args):
                       "bf16_mma_tflops_three_terms": 3 * flops / (us * 1e-6) / 1e12}), flush=True)
 
 
+def conv_only(args):
+    """One conv forward shape: im2col + GEMM (launch_im2col_pad,
+    launch_gemm_int8) against the implicit GEMM (trba_conv_gemm_int8_implicit:
+    NHWC copy of the input, weight re-order, gathered-operand GEMM), per-call
+    device time with CUDA events after 3 warm-up calls, s32 results compared."""
+    import torch
+    B, cin, h, w, cout, kh, kw, sh, sw, ph, pw = (int(x) for x in args.conv_shape.split(","))
+    ho, wo = (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
+    L = load_package().lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4)
+    k = cin * kh * kw
+    kp, rows = (k + 15) & ~15, B * ho * wo
+    x = torch.randint(-127, 128, (B, cin, h, w), dtype=torch.int8, device=dev, generator=g)
+    wq = torch.randint(-127, 128, ((cout + 15) & ~15, kp), dtype=torch.int8, device=dev, generator=g)
+    col = torch.zeros(((rows + 15) & ~15, kp), dtype=torch.int8, device=dev)
+    acc0 = torch.empty((rows, cout), dtype=torch.int32, device=dev)
+    acc1 = torch.empty((rows, cout), dtype=torch.int32, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def two_launch():
+        L.launch_im2col_pad(p(x), p(col), B, cin, h, w, kh, kw, sh, sw, ph, pw, ho, wo, kp, None)
+        L.launch_gemm_int8(p(col), p(wq), p(acc0), rows, cout, k, None)
+
+    def implicit():
+        if L.trba_conv_gemm_int8_implicit(p(x), p(wq), kp, p(acc1), B, cin, h, w, cout, kh, kw, sh, sw, ph, pw, ho,
+                                          wo, None) != 0:
+            raise RuntimeError(L.trba_last_error_string().decode())
+
+    out = {"conv": [B, cin, h, w, cout, kh, kw, sh, sw, ph, pw]}
+    n = max(1, args.steps)
+    for name, fn in (("im2col_gemm_us", two_launch), ("implicit_us", implicit)):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        e1.synchronize()
+        out[name] = e0.elapsed_time(e1) * 1e3 / n
+    if not torch.equal(acc0, acc1):
+        raise RuntimeError("implicit conv GEMM differs from im2col + GEMM")
+    if L.trba_tc_error_poll(1) != 0 or L.trba_last_error() != 0:
+        raise RuntimeError("conv kernels reported an error")
+    ops = 2.0 * rows * cout * k
+    out["implicit_tops"] = ops / (out["implicit_us"] * 1e-6) / 1e12
+    # algorithmic bytes of the implicit conv: int8 input + weights + s32 output
+    out["implicit_gbs_algorithmic"] = (B * cin * h * w + cout * k + 4.0 * rows * cout) / (out["implicit_us"] * 1e-6) / 1e9
+    print(json.dumps(out), flush=True)
+
+
 def mope_arm(args):
     """MoPE inference serving: synthetic lines with the documented length
     histogram, routed to 9 length-bucket experts placed on the ranks by
@@ -778,6 +833,9 @@ def main():
         return
     if args.dgrad_shape:
         dgrad_only(args)
+        return
+    if args.conv_shape:
+        conv_only(args)
         return
     if args.impl == "reference":
         reference_arm(args)
