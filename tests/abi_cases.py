@@ -49,6 +49,10 @@ def conv_geoms():
         (2, 3, 7, 9, 4, 3, 3, 2, 2, 1, 1),    # 3 channels, strided
         (2, 16, 5, 12, 4, 3, 3, 1, 1, 1, 1),  # stem.3 form, W % 4 == 0 (four-pixel im2col)
         (3, 3, 4, 8, 5, 3, 3, 1, 1, 1, 1),    # stem.0 form, W % 4 == 0
+        (2, 32, 5, 9, 8, 3, 3, 1, 1, 1, 1),   # C % 16 == 0: row-segment im2col
+        (2, 64, 6, 7, 16, 3, 3, 2, 2, 1, 1),  # the same, strided
+        (1, 32, 4, 9, 8, 2, 2, 2, 1, 0, 1),   # the same, conv_out.0 geometry
+        (2, 48, 5, 6, 8, 1, 1, 2, 2, 0, 0),   # the same, 1x1 stride 2
     ]
 
 
