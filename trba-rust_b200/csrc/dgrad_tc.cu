@@ -74,7 +74,7 @@ struct Ctl {
     uint64_t bfull[kMaxStages];  // weight chunk bulk copy (transaction bytes)
     uint64_t empty[kMaxStages];  // MMA commit: the stage may be refilled
     uint64_t tfull[2];           // accumulator ready for the epilogue
-    uint64_t tempty[2];          // accumulator drained (128 epilogue arrivals)
+    uint64_t tempty[2];          // accumulator drained (one arrival per epilogue warp)
     uint64_t drained;
     uint32_t tmem_base;
     int abort;
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&ctl->tfull[i], 1);
-            mbar_init(&ctl->tempty[i], kEpiWarps * 32);
+            mbar_init(&ctl->tempty[i], kEpiWarps);
         }
         mbar_init(&ctl->drained, 1);
         ctl->abort = 0;
@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
                 epilogue_cols<CW>(v, any, ws, a, base + (i64)c0 * HW, HW, P.Cin - n0 - c0, rv, gsc, gm);
             }
             tc_fence_before();
-            mbar_arrive(&ctl->tempty[acc]);
+            __syncwarp();  // every lane's TMEM reads are done: one arrival per warp
+            if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
             acc ^= 1u;
             if (acc == 0) acc_ph ^= 1u;
         }
@@ -500,7 +501,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             mbar_init(&ctl->afull[s], 1);
             mbar_init(&ctl->aempty[s], 1);
             mbar_init(&ctl->tfull[s], 1);
-            mbar_init(&ctl->tempty[s], 4 * 32);
+            mbar_init(&ctl->tempty[s], 4);  // one arrival per epilogue warp
         }
         for (int s = 0; s < h.sb; ++s) {
             mbar_init(&ctl->bfull[s], 1);
@@ -629,7 +630,8 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
                 }
             }
             tc_fence_before();
-            mbar_arrive(&ctl->tempty[acc]);
+            __syncwarp();  // every lane's TMEM reads are done: one arrival per warp
+            if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
             if (++acc == (uint32_t)h.nacc) acc = 0, acc_ph ^= 1u;
         }
         if (a.gmax_out) {

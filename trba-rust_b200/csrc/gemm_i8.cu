@@ -363,7 +363,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&ctl->tfull[a], 1);
-            mbar_init(&ctl->tempty[a], kEpiWarps * 32);
+            mbar_init(&ctl->tempty[a], kEpiWarps);  // one arrival per epilogue warp
         }
         mbar_init(&ctl->drained, 1);
         ctl->abort = 0;
@@ -496,7 +496,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                         epi.store_acc(m0 + q * 32 + lane, c0, M, N, v, c0 != 0, st);
                     }
                     tc_fence_before();
-                    mbar_arrive(&ctl->tempty[acc]);
+                    __syncwarp();  // every lane's TMEM reads are done: one arrival per warp
+                    if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
                     acc ^= 1u;
                     if (acc == 0) acc_ph ^= 1u;
                 }
@@ -523,7 +524,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                 epi.store(row, n0 + c0, M, N, v, lane, epi_sm);
             }
             tc_fence_before();
-            mbar_arrive(&ctl->tempty[acc]);
+            __syncwarp();  // every lane's TMEM reads are done: one arrival per warp
+            if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
             acc ^= 1u;
             if (acc == 0) acc_ph ^= 1u;
         }
@@ -603,7 +605,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 //             the TMA loads of both CTAs.
 //   empty[s]  (each CTA): released by CTA 0's MMA commit (one commit per CTA).
 //   tfull[a]  (each CTA): accumulator a is ready (commits as above).
-//   tempty[a] (CTA 0): released by the epilogue threads of both CTAs.
+//   tempty[a] (CTA 0): released by the epilogue warps of both CTAs (one
+//             arrival per warp, after the warp's TMEM reads).
 // All waits are bounded as in the single-CTA kernel; the CTAs meet at a
 // cluster barrier before TMEM is freed.
 constexpr int kPairBN = 256;   // N of one pair MMA; each CTA holds 128 rows of B
@@ -651,7 +654,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&ctl->tfull[a], 1);
-            mbar_init(&ctl->tempty[a], 2 * EW * 32);
+            mbar_init(&ctl->tempty[a], 2 * EW);  // one arrival per epilogue warp of either CTA
         }
         mbar_init(&ctl->drained, 1);
         ctl->abort = 0;
@@ -755,7 +758,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 epi.store(row, n0 + c0, M, N, v, lane, epi_sm);
             }
             tc_fence_before();
-            mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
+            __syncwarp();  // every lane's TMEM reads are done: one (remote) arrival per warp
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->tempty[acc]), 0));
             acc ^= 1u;
             if (acc == 0) acc_ph ^= 1u;
         }
