@@ -79,6 +79,16 @@ int trba_conv_grad_input_i8_tc(const float *grad_out, const int8_t *weight_q, in
                                float *grad_input, int b, int cin, int h, int w, int cout, int kh, int kw,
                                int sh, int sw, int ph, int pw, int ho, int wo, void *stream);
 
+/* Check of the division in the fused requant epilogue of
+ * trba_gemm_int8_requant (no counterpart in the reference): for 2^-90 <=
+ * |div| <= 2^90 the epilogue divides each s32 accumulator by div with an
+ * FMA-based correctly rounded division against a host-computed reciprocal
+ * (outside that range it uses the IEEE division).  Runs all 2^32 s32
+ * accumulator values through both divisions on the device and returns how
+ * many results differ in any bit (0 expected), or -1 when div is outside the
+ * FMA path's range.  Synchronises the stream. */
+long long trba_requant_division_check(float div, void *stream);
+
 /* launch_im2col_pad followed by launch_gemm_int8 (reference backend.rs,
  * cuda/kernels.cu:476-541 and :227-250: the QAT conv forward's GEMM,
  * src/qnet.rs:338-458) as one implicit GEMM on the tensor cores (tcgen05

@@ -28,6 +28,7 @@
 // freed and the device error word g_tc_error is set for the host to read.
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <mutex>
 #include <type_traits>
 
@@ -235,6 +236,21 @@ struct HasRowAccum<Epi, decltype(void(Epi::kRowAccum))> {
     static constexpr bool value = Epi::kRowAccum;
 };
 
+// Division by a per-call divisor b with r = RN(1/b) precomputed on the
+// host: Markstein's FMA division (q = RN(a r), e = a - b q exact by FMA,
+// RN(q + e r)), which gives RN(a / b) for normal a and b whenever q is a
+// faithful quotient and r approximates 1/b within a relative 2^-24, with no
+// underflow or overflow (Handbook of Floating-Point Arithmetic, Muller et
+// al., the theorem on Markstein's division).  The host takes this path only
+// for 2^-90 <= |b| <= 2^90, where every quotient of an s32 accumulator by b
+// is a normal float; trba_requant_division_check compares it with the
+// IEEE division for every s32 accumulator value.
+__device__ __forceinline__ float div_by(float a, float b, float r) {
+    const float q = __fmul_rn(a, r);
+    const float e = __fmaf_rn(-q, b, a);
+    return __fmaf_rn(e, r, q);
+}
+
 // Fused inference epilogue of the conv path (cuda/kernels.cu:434-466,
 // launch_conv_epilogue): out[r, n] = rint(clamp(max(acc/div + bias[n], 0) *
 // mul, +-127)) as int8, row-major [M, ldo].
@@ -243,16 +259,30 @@ struct EpiRequantI8 {
     int ldo;
     const float *bias;
     float div, mul;
-    bool vec;  // out rows 16-byte aligned and N % 16 == 0
+    bool vec;     // out rows 16-byte aligned and N % 16 == 0
+    float rdiv;   // RN(1 / div) when fast_div
+    bool fast_div;
     __device__ void init(double *) {}
     __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
         if (row >= M) return;
         int8_t *orow = out + (i64)row * ldo;
+        // the 32 columns' biases (the same for every lane: broadcast loads)
+        float bv[32];
+        if (col + 32 <= N && (reinterpret_cast<uintptr_t>(bias + col) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 b4 = reinterpret_cast<const float4 *>(bias + col)[j];
+                bv[4 * j] = b4.x, bv[4 * j + 1] = b4.y, bv[4 * j + 2] = b4.z, bv[4 * j + 3] = b4.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) bv[j] = bias[col + j < N ? col + j : N - 1];
+        }
         uint32_t packed[8];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const int n = col + j < N ? col + j : N - 1;
-            float t = fadd(fdiv((float)(int32_t)v[j], div), bias[n]);
+            const float a = (float)(int32_t)v[j];
+            float t = fadd(fast_div ? div_by(a, div, rdiv) : fdiv(a, div), bv[j]);
             t = fmul(fmaxf(t, 0.0f), mul);
             t = fminf(fmaxf(t, -127.0f), 127.0f);
             const uint32_t q = (uint32_t)(uint8_t)(int8_t)rint_even(t);
@@ -786,6 +816,19 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 }
 
 
+// Every s32 accumulator value a (as the float the epilogue converts it to)
+// through the FMA division and the IEEE division by b: counts the results
+// that differ in any bit.
+__global__ void division_check_kernel(float b, float r, unsigned long long *bad) {
+    unsigned long long local = 0;
+    const long long n = 1ll << 32, stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float a = (float)(int32_t)(uint32_t)i;
+        if (__float_as_uint(div_by(a, b, r)) != __float_as_uint(__fdiv_rn(a, b))) ++local;
+    }
+    if (local) atomicAdd(bad, local);
+}
+
 // CUDA-core fallback for operands TMA cannot describe (base address not
 // 16-byte aligned): 64x64 tile per CTA, K in 32-byte slices, dp4a.
 __global__ void gemm_i8_simt_kernel(const int8_t *__restrict__ A, const int8_t *__restrict__ B,
@@ -984,9 +1027,31 @@ bool gemm_i8_conv_f32(const int8_t *A, int lda, const int8_t *B, int ldb, int M,
                   st);
 }
 
+// RN(1 / d) (the float nearest 1/d: no ties exist) when d is in the range of
+// the FMA division path (2^-90 <= |d| <= 2^90), else false.
+bool division_reciprocal(float d, float &r) {
+    if (!std::isfinite(d)) return false;
+    const float ad = std::fabs(d);
+    if (!(ad >= 0x1p-90f && ad <= 0x1p90f)) return false;
+    // (float)(1.0 / d) may round twice (to double, then to float): keep the
+    // float among it and its two neighbours with the smallest |f d - 1|,
+    // which double evaluates exactly (24 + 24 significand bits).
+    const float c = (float)(1.0 / (double)d);
+    float best = c;
+    double err = std::fabs((double)c * (double)d - 1.0);
+    for (const float f : {std::nextafter(c, -INFINITY), std::nextafter(c, INFINITY)}) {
+        const double e = std::fabs((double)f * (double)d - 1.0);
+        if (e < err) best = f, err = e;
+    }
+    r = best;
+    return true;
+}
+
 bool gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, const float *bias, int M, int N, int K, int ld,
                      float div, float mul, cudaStream_t st) {
-    EpiRequantI8 e{out, N, bias, div, mul, ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (N & 15) == 0};
+    EpiRequantI8 e{out, N, bias, div, mul, ((reinterpret_cast<uintptr_t>(out) & 15) == 0) && (N & 15) == 0, 0.0f,
+                   false};
+    e.fast_div = division_reciprocal(div, e.rdiv);
     return run_tc(A, ld, B, ld, make_shape(M, N, K, 1), e, st);
 }
 
@@ -1081,6 +1146,26 @@ void trba_gemm_int8_dequant_f32(const int8_t *a, const int8_t *b, const float *w
     const int ld = (k + 15) & ~15;
     if (gemm_i8_dequant(a, b, out, w_scale, a_scale, bias, relu, m, n, k, ld, as_stream(stream))) return;
     report_error(__FILE__, __LINE__, "trba_gemm_int8_dequant_f32: operands not 16-byte aligned", -1);
+}
+
+// The requant epilogue's division against the IEEE division for all 2^32
+// s32 accumulator values and one divisor (synchronous): the number of
+// results that differ, or -1 when the divisor is outside the FMA path's
+// range (the epilogue then divides with the IEEE division itself).
+long long trba_requant_division_check(float div, void *stream) {
+    float r = 0.0f;
+    if (!division_reciprocal(div, r)) return -1;
+    cudaStream_t st = as_stream(stream);
+    unsigned long long *bad = nullptr, h = 0;
+    TRBA_CHECK(cudaMallocAsync((void **)&bad, sizeof(unsigned long long), st));
+    if (!bad) return -2;
+    TRBA_CHECK(cudaMemsetAsync(bad, 0, sizeof(unsigned long long), st));
+    division_check_kernel<<<sm_count() * 8, 256, 0, st>>>(div, r, bad);
+    TRBA_LAUNCH_CHECK();
+    TRBA_CHECK(cudaMemcpyAsync(&h, bad, sizeof(h), cudaMemcpyDeviceToHost, st));
+    TRBA_CHECK(cudaStreamSynchronize(st));
+    TRBA_CHECK(cudaFreeAsync(bad, st));
+    return (long long)h;
 }
 
 // Device-side error word of the tensor-core kernels (1 = a bounded wait
