@@ -61,6 +61,7 @@ struct Cfg {
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two >= 64)
     static constexpr int EPI_SMEM = 2 * kMaxN * 8;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512 + EPI_SMEM;
+    static_assert(kEpiWarps * 1024 <= EPI_SMEM, "EpiS32 stages 1 KB per epilogue warp");
 };
 
 struct Ctl {  // lives after the stage ring in shared memory
@@ -98,18 +99,39 @@ struct EpiS32 {
     int ldc;
     bool vec4;  // C rows are 16-byte aligned and N % 4 == 0
     __device__ void init(double *) {}
-    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
-        if (row >= M) return;
-        int32_t *crow = C + (i64)row * ldc;
-        if (vec4 && col + 32 <= N) {
-            int4 *dst = reinterpret_cast<int4 *>(crow + col);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                dst[j] = make_int4((int)v[4 * j], (int)v[4 * j + 1], (int)v[4 * j + 2], (int)v[4 * j + 3]);
-        } else {
+    // Each lane holds 32 consecutive columns of its own row.  Written as they
+    // are, one 16-byte store per lane touches 32 rows: every 32-byte sector
+    // is written in two halves by two instructions.  Instead the warp's 32
+    // rows pass 8 columns at a time through its own 1 KB of shared memory
+    // (the epilogue's scratch, unused by this policy): two lanes then write
+    // one row's 8 columns, so every store instruction writes 16 whole
+    // sectors.  Pieces are XOR-swizzled by row so neither side conflicts.
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
+        if (!(vec4 && col + 32 <= N)) {  // warp-uniform (col and N are)
+            if (row >= M) return;
+            int32_t *crow = C + (i64)row * ldc;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (col + j < N) crow[col + j] = (int32_t)v[j];
+            return;
+        }
+        uint8_t *buf = reinterpret_cast<uint8_t *>(sm) + (size_t)((threadIdx.x >> 5) - 2) * 1024;
+        const int row0 = row - lane;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                *reinterpret_cast<uint4 *>(buf + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+                    make_uint4(v[8 * p + 4 * h], v[8 * p + 4 * h + 1], v[8 * p + 4 * h + 2], v[8 * p + 4 * h + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int k = lane + 32 * t, r = k >> 1, half = k & 1;
+                const uint4 w = *reinterpret_cast<const uint4 *>(buf + r * 32 + ((half ^ ((r >> 2) & 1)) << 4));
+                if (row0 + r < M)
+                    *reinterpret_cast<uint4 *>(C + (i64)(row0 + r) * ldc + col + 8 * p + 4 * half) = w;
+            }
+            __syncwarp();
         }
     }
     __device__ void finish(double *, int) {}
@@ -663,6 +685,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
                     Epi epi) {
     using G = PairCfg;
+    static_assert(!std::is_same<Epi, EpiS32>::value || EW * 1024 <= G::EPI_SMEM,
+                  "EpiS32 stages 1 KB per epilogue warp");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
