@@ -141,12 +141,30 @@ struct EpiS32Atomic {
     int32_t *C;
     int ldc;
     __device__ void init(double *) {}
-    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
-        if (row >= M) return;
-        int32_t *crow = C + (i64)row * ldc;
+    // Integer atomics, exact in any order.  As in EpiS32, the warp's 32 rows
+    // pass 8 columns at a time through its 1 KB of shared memory, so that one
+    // atomic instruction covers 8 consecutive columns of 4 rows (4 sectors)
+    // instead of one column of 32 rows (32 lines).
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
+        uint8_t *buf = reinterpret_cast<uint8_t *>(sm) + (size_t)((threadIdx.x >> 5) - 2) * 1024;
+        const int row0 = row - lane, c = lane & 7;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (col + j < N && v[j] != 0u) atomicAdd(crow + col + j, (int32_t)v[j]);
+        for (int p = 0; p < 4; ++p) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                *reinterpret_cast<uint4 *>(buf + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+                    make_uint4(v[8 * p + 4 * h], v[8 * p + 4 * h + 1], v[8 * p + 4 * h + 2], v[8 * p + 4 * h + 3]);
+            __syncwarp();
+            const int n = col + 8 * p + c;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = 4 * i + (lane >> 3);  // r >> 2 == i
+                const uint32_t val =
+                    *reinterpret_cast<const uint32_t *>(buf + r * 32 + ((((c >> 2) ^ (i & 1))) << 4) + (c & 3) * 4);
+                if (row0 + r < M && n < N && val != 0u) atomicAdd(C + (i64)(row0 + r) * ldc + n, (int32_t)val);
+            }
+            __syncwarp();
+        }
     }
     __device__ void finish(double *, int) {}
 };
@@ -664,11 +682,12 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 constexpr int kPairBN = 256;   // N of one pair MMA; each CTA holds 128 rows of B
 constexpr int kPairStages = 6;
 // Epilogue warps of the pair kernel: 16 (four per TMEM lane quarter) for the
-// arithmetic epilogues, 8 for the plain s32 store, which is bound by its
-// stores (more warps measured slower there).
+// arithmetic epilogues, 8 for the plain s32 store and the s32 atomics, which
+// are bound by their stores (more warps measured slower there) and stage
+// 1 KB per warp in the epilogue scratch.
 template <class Epi>
 constexpr int pair_epi_warps() {
-    return std::is_same<Epi, EpiS32>::value ? 8 : 16;
+    return std::is_same<Epi, EpiS32>::value || std::is_same<Epi, EpiS32Atomic>::value ? 8 : 16;
 }
 
 struct PairCfg {
@@ -685,8 +704,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
                     Epi epi) {
     using G = PairCfg;
-    static_assert(!std::is_same<Epi, EpiS32>::value || EW * 1024 <= G::EPI_SMEM,
-                  "EpiS32 stages 1 KB per epilogue warp");
+    static_assert((!std::is_same<Epi, EpiS32>::value && !std::is_same<Epi, EpiS32Atomic>::value) ||
+                      EW * 1024 <= G::EPI_SMEM,
+                  "EpiS32 / EpiS32Atomic stage 1 KB per epilogue warp");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
