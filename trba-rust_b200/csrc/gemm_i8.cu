@@ -303,9 +303,8 @@ struct EpiRequantI8 {
     float rdiv;   // RN(1 / div) when fast_div
     bool fast_div;
     __device__ void init(double *) {}
-    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
-        if (row >= M) return;
-        int8_t *orow = out + (i64)row * ldo;
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
+        int8_t *orow = out + (i64)row * ldo;  // rows >= M compute but never store
         // the 32 columns' biases (the same for every lane: broadcast loads)
         float bv[32];
         if (col + 32 <= N && (reinterpret_cast<uintptr_t>(bias + col) & 15) == 0) {
@@ -330,10 +329,25 @@ struct EpiRequantI8 {
             packed[j >> 2] |= q << (8 * (j & 3));
         }
         if (vec && col + 32 <= N) {
-            uint4 *dst = reinterpret_cast<uint4 *>(orow + col);
-            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            // the row's 32 bytes are one sector: the warp's 32 rows pass
+            // through its 1 KB of shared memory so that two lanes write one
+            // row and every store instruction writes 16 whole sectors
+            uint8_t *buf = reinterpret_cast<uint8_t *>(sm) + (size_t)((threadIdx.x >> 5) - 2) * 1024;
+            const int row0 = row - lane;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                *reinterpret_cast<uint4 *>(buf + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+                    make_uint4(packed[4 * h], packed[4 * h + 1], packed[4 * h + 2], packed[4 * h + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int k = lane + 32 * t, r = k >> 1, half = k & 1;
+                const uint4 w = *reinterpret_cast<const uint4 *>(buf + r * 32 + ((half ^ ((r >> 2) & 1)) << 4));
+                if (row0 + r < M) *reinterpret_cast<uint4 *>(out + (i64)(row0 + r) * ldo + col + 16 * half) = w;
+            }
+            __syncwarp();
         } else {
+            if (row >= M) return;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (col + j < N) orow[col + j] = (int8_t)((packed[j >> 2] >> (8 * (j & 3))) & 0xffu);
@@ -695,7 +709,9 @@ struct PairCfg {
     static constexpr int B_BYTES = (kPairBN / 2) * BK;    // 16 KB
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * kPairBN;         // two accumulators: the whole TMEM
-    static constexpr int EPI_SMEM = 2 * kMaxN * 8;
+    // per-column sums (2 x kMaxN doubles), or 1 KB of store staging per
+    // epilogue warp (16 warps)
+    static constexpr int EPI_SMEM = 2 * kMaxN * 8 > 16 * 1024 ? 2 * kMaxN * 8 : 16 * 1024;
     static constexpr int SMEM = 1024 + kPairStages * STAGE_BYTES + 512 + EPI_SMEM;
 };
 
@@ -704,9 +720,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Shape sh,
                     Epi epi) {
     using G = PairCfg;
-    static_assert((!std::is_same<Epi, EpiS32>::value && !std::is_same<Epi, EpiS32Atomic>::value) ||
-                      EW * 1024 <= G::EPI_SMEM,
-                  "EpiS32 / EpiS32Atomic stage 1 KB per epilogue warp");
+    static_assert(EW * 1024 <= G::EPI_SMEM, "the store epilogues stage 1 KB per epilogue warp");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
