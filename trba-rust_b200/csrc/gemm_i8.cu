@@ -368,9 +368,7 @@ struct EpiDequantF32 {
     int relu;
     bool vec;  // out rows 16-byte aligned and N % 4 == 0
     __device__ void init(double *) {}
-    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int, double *) {
-        if (row >= M) return;
-        float *orow = out + (i64)row * ldo;
+    __device__ void store(int row, int col, int M, int N, const uint32_t (&v)[32], int lane, double *sm) {
         float r[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -379,11 +377,27 @@ struct EpiDequantF32 {
             if (bias) t = fadd(t, bias[n]);
             r[j] = relu ? fmaxf(t, 0.0f) : t;
         }
-        if (vec && col + 32 <= N) {
-            float4 *dst = reinterpret_cast<float4 *>(orow + col);
+        if (vec && col + 32 <= N) {  // warp-uniform: whole sectors per store, as in EpiS32
+            uint8_t *buf = reinterpret_cast<uint8_t *>(sm) + (size_t)((threadIdx.x >> 5) - 2) * 1024;
+            const int row0 = row - lane;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            for (int p = 0; p < 4; ++p) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    *reinterpret_cast<float4 *>(buf + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+                        make_float4(r[8 * p + 4 * h], r[8 * p + 4 * h + 1], r[8 * p + 4 * h + 2], r[8 * p + 4 * h + 3]);
+                __syncwarp();
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    const int k = lane + 32 * t, rr = k >> 1, half = k & 1;
+                    const float4 w = *reinterpret_cast<const float4 *>(buf + rr * 32 + ((half ^ ((rr >> 2) & 1)) << 4));
+                    if (row0 + rr < M) *reinterpret_cast<float4 *>(out + (i64)(row0 + rr) * ldo + col + 8 * p + 4 * half) = w;
+                }
+                __syncwarp();
+            }
         } else {
+            if (row >= M) return;
+            float *orow = out + (i64)row * ldo;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (col + j < N) orow[col + j] = r[j];
