@@ -390,9 +390,10 @@ __global__ void __launch_bounds__(kThreads, 1) dgrad_tc_kernel(const __grid_cons
 //               K steps x mb row blocks of M = 128, N = BN, K = 16, the A
 //               window shifted by the tap's offset; double-buffered TMEM
 //               accumulators of mb x BN columns.
-//   warps 3..6  epilogue, as the class kernel's, over the tile's positions
-//               (gap positions are skipped).
-constexpr int kHWarps = 7;
+//   warps 3..10 epilogue, as the class kernel's, over the tile's positions
+//               (gap positions are skipped): two warps per TMEM lane
+//               quarter, each draining half of the tile's columns (BN >= 32).
+constexpr int kHWarps = 11;
 constexpr int kHThreads = 32 * kHWarps;
 constexpr int kHEpi0 = 3;
 constexpr int kMaxBStages = 16;
@@ -501,7 +502,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
             mbar_init(&ctl->afull[s], 1);
             mbar_init(&ctl->aempty[s], 1);
             mbar_init(&ctl->tfull[s], 1);
-            mbar_init(&ctl->tempty[s], 4);  // one arrival per epilogue warp
+            mbar_init(&ctl->tempty[s], kHWarps - kHEpi0);  // one arrival per epilogue warp
         }
         for (int s = 0; s < h.sb; ++s) {
             mbar_init(&ctl->bfull[s], 1);
@@ -598,6 +599,11 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
         // ------------------------------------------------ epilogue
         constexpr int CW = 16;  // accumulator columns per tcgen05.ld (BN >= 16)
         const int q = warp & 3;  // TMEM lane quarter this warp may read
+        // columns of this warp: half of the tile's for BN >= 32, all of them
+        // (first half) or none (second half) for BN = 16
+        const int half = (warp - kHEpi0) >> 2;
+        constexpr int HC = BN >= 32 ? BN / 2 : BN;
+        const int cb = half * HC, ce = BN >= 32 ? cb + HC : (half ? 0 : BN);
         const float ws = a.w_s ? *a.w_s : a.w_s_val;
         const float gsc = a.gmax_out ? *a.gmax_scale : 0.0f;
         const int HW = P.H * P.W, HqWq = h.Hq * h.Wq;
@@ -620,7 +626,7 @@ __global__ void __launch_bounds__(kHThreads, 1) dgrad_halo_kernel(const __grid_c
                 const int y = C.py + (ci << P.lgSH), x = C.px + (cj << P.lgSW);
                 const i64 base = ((i64)b * P.Cin + n0) * HW + (i64)y * P.W + x;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN && n0 + c0 < P.Cin; c0 += CW) {
+                for (int c0 = cb; c0 < ce && n0 + c0 < P.Cin; c0 += CW) {
                     uint32_t v[CW];
                     if (any) {
                         tmem_ld_cols<CW>(tbase + ((uint32_t)(q * 32) << 16) + (acc * h.mb + i) * BN + c0, v);
