@@ -102,7 +102,9 @@ class LinearInt8:
 
 
 def _exp32(x):
-    return np.exp(np.asarray(x, F32).astype(np.float64)).astype(F32)
+    # exp beyond the f32 range rounds to inf, as f32::exp overflows
+    with np.errstate(over="ignore"):
+        return np.exp(np.asarray(x, F32).astype(np.float64)).astype(F32)
 
 
 def _tanh32(x):
